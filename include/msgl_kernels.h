@@ -1,0 +1,180 @@
+/*
+ * msgl_kernels.h -- C ABI of libmsgl, the sm_100a (B200) kernels of the mini-sglang-cpp
+ * per-layer Qwen3 / Qwen3-MoE forward path.
+ *
+ * Conventions (all entry points):
+ *  - plain pointers and sizes; every device pointer is a CUDA device address on the current
+ *    device; the caller owns every buffer (inputs, outputs, workspaces) -- no entry point
+ *    allocates device memory;
+ *  - each call is asynchronous on the given stream and returns an msgl_status; on failure
+ *    msgl_last_error() returns a message (thread-local);
+ *  - kernel-side failures (a bounded wait that ran out, an index outside a pool) never trap:
+ *    they are recorded in a per-device error word read by msgl_device_error();
+ *  - activations and weights are bf16 unless a dtype argument says otherwise; accumulation is
+ *    fp32; the residual stream is fp32.
+ *
+ * The four reference launchers (include/minisgl/kernel/kernels.h:13-21 of mini-sglang-cpp) keep
+ * their names (prefixed msgl_), argument order and meaning, plus a dtype tag and a status.
+ */
+#ifndef MSGL_KERNELS_H
+#define MSGL_KERNELS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __CUDACC__
+#include <cuda_runtime.h>
+typedef cudaStream_t msgl_stream_t;
+#else
+typedef void* msgl_stream_t; /* a cudaStream_t */
+#endif
+
+#if defined(__GNUC__)
+#define MSGL_API __attribute__((visibility("default")))
+#else
+#define MSGL_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    MSGL_OK = 0,
+    MSGL_ERR_INVALID_ARG = 1,
+    MSGL_ERR_UNSUPPORTED_SHAPE = 2,
+    MSGL_ERR_CUDA = 3,
+    MSGL_ERR_NCCL = 4,
+    MSGL_ERR_TIMEOUT = 5,
+    MSGL_ERR_BOUNDS = 6,
+    MSGL_ERR_WORKSPACE = 7
+} msgl_status;
+
+typedef enum { MSGL_F32 = 0, MSGL_BF16 = 1 } msgl_dtype;
+
+/* ---------------------------------------------------------------- library */
+MSGL_API const char* msgl_version(void);
+/* Message of the last failing call on this host thread ("" if none). */
+MSGL_API const char* msgl_last_error(void);
+/* Synchronises `stream`, then reads the device error word of the current device (code and an
+ * info word naming the failing site); reset != 0 clears it. */
+MSGL_API int msgl_device_error(int* code, int* info, int reset, msgl_stream_t stream);
+
+/* ---------------------------------------------------------------- reference launchers */
+/* launch_rmsnorm (kernels.h:13-14; kernels/cuda/rmsnorm.cu:37-43; semantics of
+ * RMSNorm::forward, src/layer/layer.cpp:48-77). input/weight/output share `dtype`. */
+MSGL_API int msgl_launch_rmsnorm(const void* input, const void* weight, void* output, int num_tokens,
+                        int hidden_size, float eps, int dtype, msgl_stream_t stream);
+
+/* launch_rope (kernels.h:15-16; kernels/cuda/rotary.cu:43-51). Rotate-half RoPE in place on
+ * query [T, num_q_heads, D] and key [T, num_kv_heads, D] (key may be NULL) with the fp32 table
+ * cos_sin_cache [max_pos, D] (RotaryEmbedding ctor, layer.cpp:163-176) and per-token positions.
+ * The reference passes one head count for both tensors; K has its own here. */
+MSGL_API int msgl_launch_rope(void* query, void* key, const int* positions, const float* cos_sin_cache,
+                     int num_tokens, int num_q_heads, int num_kv_heads, int head_dim, int dtype,
+                     msgl_stream_t stream);
+
+/* launch_index_gather (kernels.h:17-18; kernels/cuda/index.cu:21-28): out[i,:] = in[idx[i],:].
+ * Ids outside [0, num_rows) give a zero row, as Embedding::forward does (layer.cpp:26-31). */
+MSGL_API int msgl_launch_index_gather(const void* input, const int* indices, void* output,
+                             int hidden_size, int num_indices, int num_rows, int dtype,
+                             msgl_stream_t stream);
+
+/* launch_store_kv_page (kernels.h:19-21; kernels/cuda/radix.cu:28-36): token t of k/v
+ * [T, heads*D] goes to pool row page_table[t / page_size] * page_size + t % page_size. */
+MSGL_API int msgl_launch_store_kv_page(const void* k, const void* v, void* k_cache, void* v_cache,
+                              const int* page_table, int page_size, int num_heads, int head_dim,
+                              int num_tokens, int dtype, msgl_stream_t stream);
+
+/* ---------------------------------------------------------------- fused norm / RoPE / KV */
+/* RMSNorm::forward_fused_add (layer.cpp:79-112): residual += x; x = rmsnorm(residual) * w.
+ * x bf16 [T,H] in/out, residual fp32 [T,H] in/out, weight bf16 [H].
+ * first != 0 is the aliasing first call (layer.cpp:80-84): residual = x; x = rmsnorm(x). */
+MSGL_API int msgl_add_rmsnorm(void* x, float* residual, const void* weight, int num_tokens, int hidden,
+                     float eps, int first, msgl_stream_t stream);
+
+/* Embedding::forward (layer.cpp:15-42) fused with the first layer's input norm:
+ * residual = embed[ids]; x = rmsnorm(residual) * w. Out-of-range ids give zero rows. */
+MSGL_API int msgl_embed_rmsnorm(const void* embed, const int* ids, int num_tokens, int vocab, int hidden,
+                       const void* weight, float eps, void* x_out, float* residual_out,
+                       msgl_stream_t stream);
+
+/* QK-norm + RoPE + KV page store, one pass over the QKV projection output (split of
+ * src/model/qwen3.cpp:28-45, RoPE of :48, store of kernels/cuda/radix.cu:19-22):
+ *   qkv [T, (Hq + 2 Hkv) D] bf16, rows q | k | v per token;
+ *   q_out [T, Hq, D] = rope(rmsnorm_D(q) * q_norm);
+ *   k_pool[slot_mapping[t], :] = rope(rmsnorm_D(k) * k_norm);  v_pool[slot_mapping[t], :] = v.
+ * Pools are [num_slots, Hkv * D] bf16; a negative slot skips the store (padding token), a slot
+ * >= num_slots is skipped and recorded as MSGL_ERR_BOUNDS in the device error word.
+ * head_dim must be 128. */
+MSGL_API int msgl_qknorm_rope_store_kv(const void* qkv, void* q_out, void* k_pool, void* v_pool,
+                              int64_t num_slots, const int* positions, const int* slot_mapping,
+                              const float* cos_sin_cache, const void* q_norm_w,
+                              const void* k_norm_w, int num_tokens, int num_q_heads,
+                              int num_kv_heads, int head_dim, float eps, msgl_stream_t stream);
+
+/* ---------------------------------------------------------------- paged attention */
+/* Replaces Attention::forward (src/layer/layer.cpp:214-262) with attention over the paged KV
+ * pool. Pools: [num_slots, Hkv * D] bf16, slot = page * page_size + offset (radix.cu:19-22).
+ * page_table [num_reqs, max_pages] int32; seq_lens [num_reqs] = context length including this
+ * step's tokens (already stored). head_dim 128, page_size 16, num_q_heads / num_kv_heads <= 8.
+ *
+ * Decode: one query token per request, q/out [num_reqs, Hq, D] bf16. max_seq_len bounds
+ * seq_lens (it sizes the grid and the workspace). The workspace must be zero-filled once before
+ * its first use; every call leaves it zero-filled again. */
+MSGL_API size_t msgl_paged_attention_workspace_size(int num_reqs, int max_seq_len, int num_q_heads,
+                                           int num_kv_heads, int head_dim);
+MSGL_API int msgl_paged_attention_decode(const void* q, const void* k_pool, const void* v_pool,
+                                int64_t num_slots, const int* page_table, int max_pages,
+                                const int* seq_lens, int num_reqs, int max_seq_len,
+                                int num_q_heads, int num_kv_heads, int head_dim, int page_size,
+                                float scale, void* out, void* workspace,
+                                size_t workspace_bytes, msgl_stream_t stream);
+
+/* Extend / prefill: request r owns query rows [q_indptr[r], q_indptr[r+1]) of q/out
+ * [total_q, Hq, D]; row i of an n-row request sits at position seq_lens[r] - n + i and attends
+ * causally to context tokens 0..that position. max_q_len bounds the per-request row count. */
+MSGL_API int msgl_paged_attention_extend(const void* q, const void* k_pool, const void* v_pool,
+                                int64_t num_slots, const int* page_table, int max_pages,
+                                const int* seq_lens, const int* q_indptr, int num_reqs,
+                                int max_q_len, int num_q_heads, int num_kv_heads, int head_dim,
+                                int page_size, float scale, void* out, msgl_stream_t stream);
+
+/* ---------------------------------------------------------------- tcgen05 GEMMs */
+/* Linear::forward (layer.cpp:122-143): y[M,N] = x[M,K] * W[N,K]^T, W in the reference's
+ * [out, in] row-major layout. x, W bf16; y bf16 (out_dtype MSGL_BF16) or fp32 (MSGL_F32).
+ * K % 64 == 0, N % 128 == 0, x/W/y 16-byte aligned. Split-K partial sums go through `workspace`
+ * (msgl_gemm_workspace_size bytes; zero-filled once before first use, left zero-filled). */
+MSGL_API size_t msgl_gemm_workspace_size(int M, int N, int K);
+MSGL_API int msgl_gemm_bf16(const void* x, const void* w, void* y, int M, int N, int K, int out_dtype,
+                   void* workspace, size_t workspace_bytes, msgl_stream_t stream);
+
+/* gate_up projection + split + SwiGLU (qwen3.cpp:60-79, layer.cpp:145-161) in one GEMM:
+ * y[M, I] = silu(x W_gate^T) * (x W_up^T), with w_packed the gate_up weight re-laid out by
+ * msgl_pack_gate_up. I % 16 == 0 and 2I % 128 == 0. */
+MSGL_API int msgl_pack_gate_up(const void* w_gate_up, void* w_packed, int inter, int hidden,
+                      msgl_stream_t stream);
+MSGL_API int msgl_gemm_gate_up_silu(const void* x, const void* w_packed, void* y, int M, int inter, int K,
+                           void* workspace, size_t workspace_bytes, msgl_stream_t stream);
+
+/* lm_head (qwen3.cpp:178) fused with greedy sampling (scheduler.cpp:117-124): ids[m] = argmax_n
+ * of the fp32 logits x[m] . W[n]; ties to the lowest id. `packed` is [M] uint64 scratch. */
+MSGL_API int msgl_lm_head_argmax(const void* x, const void* w, int M, int vocab, int K,
+                        unsigned long long* packed, int* ids, void* workspace,
+                        size_t workspace_bytes, msgl_stream_t stream);
+
+/* ---------------------------------------------------------------- sampling / utilities */
+/* Greedy argmax over logits [num_rows, vocab] (scheduler.cpp:117-124): first maximum wins. */
+MSGL_API int msgl_argmax(const void* logits, int num_rows, int vocab, int dtype, int* out,
+                msgl_stream_t stream);
+
+/* Fill a bf16 buffer with N(mean, std) values from a counter-based generator
+ * (Philox4x32-10 keyed by (seed, stream_id), Box-Muller). Used for random-init weights and
+ * synthetic KV contents. */
+MSGL_API int msgl_fill_normal_bf16(void* out, int64_t n, uint64_t seed, uint64_t stream_id, float mean,
+                          float std, msgl_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MSGL_KERNELS_H */

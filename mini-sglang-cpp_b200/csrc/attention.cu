@@ -1,0 +1,590 @@
+// attention.cu -- paged-KV decode and extend attention over the page pool.
+//
+// Replaces Attention::forward (src/layer/layer.cpp:214-262). Same math -- scale 1/sqrt(D),
+// softmax with max subtraction, fp32 accumulation -- evaluated online (flash style) per request
+// over the paged pool [num_slots, Hkv * 128] (slot = page * 16 + offset, the layout of
+// kernels/cuda/radix.cu:19-22), with GQA (query head h reads kv head h / (Hq / Hkv)).
+//
+// Data movement: a producer warp walks the request's page-table row and stages each page's K and
+// V rows (16 tokens x 128 dims of one kv head, 4 KB each) into shared memory with 2-D TMA loads
+// (SWIZZLE_128B, no multicast) on an mbarrier ring. Four consumer warps compute
+// S = Q K^T and O += P V with warp-level bf16 MMA (m16n8k16, fp32 accumulate; fragments read
+// with ldmatrix from the swizzled tiles, conflict-free) and a warp-shuffle online softmax.
+// The query group of one kv head (Hq / Hkv <= 8 heads) fills the MMA rows; in decode the pages
+// of one request are split over the four warps and over `chunks` CTAs (split-KV), whose partial
+// (m, l, O) are merged by the last CTA to finish (a self-resetting arrival counter).
+//
+// Bound: HBM. Per (request, kv head, token) the kernel reads 512 B of K/V; the tensor work per
+// byte is ~4 FLOP, far below the MMA rate.
+#include <algorithm>
+
+#include "common.cuh"
+#include "tmap.h"
+
+namespace msgl {
+namespace {
+
+constexpr int kPage = 16;
+constexpr int kHd = 128;
+constexpr int kPageSlotBytes = 4 * 2048;  // K lo, K hi, V lo, V hi halves of one page
+constexpr int kConsumerWarps = 4;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kDecodeStages = 3;          // x 4 pages per stage
+constexpr int kExtendStages = 8;          // x 1 page per stage
+constexpr float kNegInf = -__builtin_huge_valf();
+
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// One page (16 tokens) for one warp: S = Q K^T (2 x 8 MMAs), masked online softmax, O += P V
+// (16 MMAs). Rows g (lane >> 2) and g + 8 of the MMA tile are query rows; TWO selects whether
+// rows g + 8 carry data. lim0 / lim1: last kv token index visible to row g / g + 8.
+template <bool TWO>
+__device__ __forceinline__ void attend_page(uint32_t k_base, uint32_t v_base,
+                                            const uint32_t (&qa)[8][4], float (&o)[16][4],
+                                            float (&m)[2], float (&l)[2], int tok0, int lim0,
+                                            int lim1, float sl2e, int lane) {
+    float s[2][4];
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) s[n][e] = 0.f;
+
+    const int mi = lane >> 3;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+        const int row = ((mi >> 1) << 3) + (lane & 7);
+        const int chunk = ((kk & 3) << 1) + (mi & 1);
+        uint32_t addr = k_base + ((kk >> 2) << 11) + row * 128 + ((chunk ^ (row & 7)) << 4);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(addr, b0, b1, b2, b3);
+        mma_bf16_16816(s[0], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b0, b1);
+        mma_bf16_16816(s[1], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b2, b3);
+    }
+
+    const int c = lane & 3;
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            int tk = tok0 + n * 8 + 2 * c + e;
+            s[n][e] = tk <= lim0 ? s[n][e] * sl2e : kNegInf;
+            if (TWO) s[n][2 + e] = tk <= lim1 ? s[n][2 + e] * sl2e : kNegInf;
+        }
+
+    float p[2][4];
+#pragma unroll
+    for (int r = 0; r < (TWO ? 2 : 1); ++r) {
+        float mx = fmaxf(fmaxf(s[0][2 * r], s[0][2 * r + 1]), fmaxf(s[1][2 * r], s[1][2 * r + 1]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        float m_new = fmaxf(m[r], mx);
+        float alpha = 1.f, base = 0.f;
+        if (m_new != kNegInf) {
+            alpha = exp2f(m[r] - m_new);
+            base = m_new;
+        }
+        float ps = 0.f;
+#pragma unroll
+        for (int n = 0; n < 2; ++n)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                float v = exp2f(s[n][2 * r + e] - base);
+                p[n][2 * r + e] = v;
+                ps += v;
+            }
+        l[r] = l[r] * alpha + ps;
+        m[r] = m_new;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            o[j][2 * r] *= alpha;
+            o[j][2 * r + 1] *= alpha;
+        }
+    }
+    const uint32_t pa0 = pack_bf16x2(p[0][0], p[0][1]);
+    const uint32_t pa2 = pack_bf16x2(p[1][0], p[1][1]);
+    const uint32_t pa1 = TWO ? pack_bf16x2(p[0][2], p[0][3]) : 0u;
+    const uint32_t pa3 = TWO ? pack_bf16x2(p[1][2], p[1][3]) : 0u;
+
+#pragma unroll
+    for (int j2 = 0; j2 < 8; ++j2) {
+        const int row = ((mi & 1) << 3) + (lane & 7);
+        const int chunk = ((j2 & 3) << 1) + (mi >> 1);
+        uint32_t addr = v_base + ((j2 >> 2) << 11) + row * 128 + ((chunk ^ (row & 7)) << 4);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(addr, b0, b1, b2, b3);
+        mma_bf16_16816(o[2 * j2], pa0, pa1, pa2, pa3, b0, b1);
+        mma_bf16_16816(o[2 * j2 + 1], pa0, pa1, pa2, pa3, b2, b3);
+    }
+}
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+    return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+__device__ __forceinline__ void issue_page(uint8_t* dst, const CUtensorMap* tk,
+                                           const CUtensorMap* tv, uint64_t* bar, int kvh, int page) {
+    const int x = kvh * kHd, y = page * kPage;
+    tma_load_2d(dst, tk, bar, x, y);
+    tma_load_2d(dst + 2048, tk, bar, x + 64, y);
+    tma_load_2d(dst + 4096, tv, bar, x, y);
+    tma_load_2d(dst + 6144, tv, bar, x + 64, y);
+}
+
+__device__ __forceinline__ void store_bf16x8(__nv_bfloat16* dst, const float (&v)[8]) {
+    uint4 u;
+    u.x = pack_bf16x2(v[0], v[1]);
+    u.y = pack_bf16x2(v[2], v[3]);
+    u.z = pack_bf16x2(v[4], v[5]);
+    u.w = pack_bf16x2(v[6], v[7]);
+    *reinterpret_cast<uint4*>(dst) = u;
+}
+
+// ------------------------------------------------------------------------------ decode
+// grid (max_chunks, Hkv, B); block 160 = 4 consumer warps + 1 TMA producer warp.
+__global__ void __launch_bounds__(kThreads)
+paged_decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+                    const __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ out,
+                    const int* __restrict__ page_table, int max_pages,
+                    const int* __restrict__ seq_lens, int pool_pages, int hq, int hkv,
+                    int chunk_pages, int max_chunks, float sl2e, float* __restrict__ ws_o,
+                    float* __restrict__ ws_ml, int* __restrict__ ws_cnt, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = align1024(smem_raw);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDecodeStages * 4 * kPageSlotBytes);
+    uint64_t* empty = full + kDecodeStages;
+    int* flag = reinterpret_cast<int*>(empty + kDecodeStages);
+
+    const int b = blockIdx.z, kvh = blockIdx.y, chunk = blockIdx.x;
+    const int group = hq / hkv;
+    int L = seq_lens[b];
+    if (L < 0 || L > max_pages * kPage) {  // context longer than the page-table row
+        if (threadIdx.x == 0 && chunk == 0) record_error(err, MSGL_ERR_BOUNDS, 202);
+        L = L < 0 ? 0 : max_pages * kPage;
+    }
+    const int npages = (L + kPage - 1) / kPage;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (npages == 0) {  // empty context: output zeros (chunk 0 only)
+        if (chunk == 0 && threadIdx.x < group * 16) {
+            float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            int row = threadIdx.x >> 4, d0 = (threadIdx.x & 15) * 8;
+            store_bf16x8(out + (static_cast<int64_t>(b) * hq + kvh * group + row) * kHd + d0, z);
+        }
+        return;
+    }
+    const int p0 = chunk * chunk_pages;
+    if (p0 >= npages) return;
+    const int np = min(npages - p0, chunk_pages);
+    const int nchunks = (npages + chunk_pages - 1) / chunk_pages;
+    const int nsteps = (np + 3) / 4;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kDecodeStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    if (warp == kConsumerWarps) {
+        // ---------------- TMA producer
+        if (lane == 0) {
+            tma_prefetch_desc(&tk);
+            tma_prefetch_desc(&tv);
+            const int* pt = page_table + static_cast<int64_t>(b) * max_pages;
+            for (int it = 0; it < nsteps; ++it) {
+                const int s = it % kDecodeStages;
+                if (it >= kDecodeStages &&
+                    !mbar_wait(&empty[s], ((it / kDecodeStages) - 1) & 1, err, 200))
+                    break;
+                const int cnt = min(4, np - it * 4);
+                mbar_arrive_expect_tx(&full[s], cnt * kPageSlotBytes);
+                for (int p = 0; p < cnt; ++p) {
+                    int page = pt[p0 + it * 4 + p];
+                    if (static_cast<unsigned>(page) >= static_cast<unsigned>(pool_pages)) {
+                        record_error(err, MSGL_ERR_BOUNDS, 201);
+                        page = 0;
+                    }
+                    issue_page(smem + (s * 4 + p) * kPageSlotBytes, &tk, &tv, &full[s], kvh, page);
+                }
+            }
+        }
+        return;
+    }
+
+    // ---------------- consumers
+    const int g = lane >> 2, c = lane & 3;
+    uint32_t qa[8][4];
+    {
+        const bool real = g < group;
+        const __nv_bfloat16* qr = q + (static_cast<int64_t>(b) * hq + kvh * group + (real ? g : 0)) * kHd;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+            qa[kk][0] = real ? *reinterpret_cast<const uint32_t*>(qr + 16 * kk + 2 * c) : 0u;
+            qa[kk][2] = real ? *reinterpret_cast<const uint32_t*>(qr + 16 * kk + 8 + 2 * c) : 0u;
+            qa[kk][1] = 0u;
+            qa[kk][3] = 0u;
+        }
+    }
+    float o[16][4];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    float m[2] = {kNegInf, kNegInf}, l[2] = {0.f, 0.f};
+
+    for (int it = 0; it < nsteps; ++it) {
+        const int s = it % kDecodeStages;
+        if (!mbar_wait(&full[s], (it / kDecodeStages) & 1, err, 210)) break;
+        const int pidx = it * 4 + warp;
+        if (pidx < np) {
+            uint32_t base = smem_u32(smem + (s * 4 + warp) * kPageSlotBytes);
+            attend_page<false>(base, base + 4096, qa, o, m, l, (p0 + pidx) * kPage, L - 1, -1,
+                               sl2e, lane);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+
+    // ---------------- merge the four warps (shared memory aliases the drained stage ring)
+    float lsum = l[0];
+    lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
+    lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);
+    named_bar_sync(1, kConsumerWarps * 32);
+    float* mo = reinterpret_cast<float*>(smem);      // [4][8][128]
+    float* mm = mo + kConsumerWarps * 8 * kHd;        // [4][8]
+    float* ml = mm + kConsumerWarps * 8;              // [4][8]
+    if (g < group) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            mo[(warp * 8 + g) * kHd + 8 * j + 2 * c] = o[j][0];
+            mo[(warp * 8 + g) * kHd + 8 * j + 2 * c + 1] = o[j][1];
+        }
+        if (c == 0) {
+            mm[warp * 8 + g] = m[0];
+            ml[warp * 8 + g] = lsum;
+        }
+    }
+    named_bar_sync(1, kConsumerWarps * 32);
+
+    const int row = threadIdx.x >> 4, d0 = (threadIdx.x & 15) * 8;
+    const int head = kvh * group + row;
+    if (row < group) {
+        float M = kNegInf;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, mm[w * 8 + row]);
+        float O[8] = {0, 0, 0, 0, 0, 0, 0, 0}, Ls = 0.f;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) {
+            float mw = mm[w * 8 + row];
+            float sc = (mw == kNegInf) ? 0.f : exp2f(mw - M);
+            Ls += ml[w * 8 + row] * sc;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) O[e] += mo[(w * 8 + row) * kHd + d0 + e] * sc;
+        }
+        if (nchunks == 1) {
+            float inv = Ls > 0.f ? 1.f / Ls : 0.f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) O[e] *= inv;
+            store_bf16x8(out + (static_cast<int64_t>(b) * hq + head) * kHd + d0, O);
+        } else {
+            int64_t pi = (static_cast<int64_t>(b) * max_chunks + chunk) * hq + head;
+            float4* dst = reinterpret_cast<float4*>(ws_o + pi * kHd + d0);
+            dst[0] = make_float4(O[0], O[1], O[2], O[3]);
+            dst[1] = make_float4(O[4], O[5], O[6], O[7]);
+            if ((threadIdx.x & 15) == 0) {
+                ws_ml[pi * 2] = M;
+                ws_ml[pi * 2 + 1] = Ls;
+            }
+        }
+    }
+    if (nchunks == 1) return;
+
+    // ---------------- split-KV: the last chunk CTA of (b, kvh) merges all chunks
+    __threadfence();
+    named_bar_sync(1, kConsumerWarps * 32);
+    if (threadIdx.x == 0) {
+        int old = atomicAdd(&ws_cnt[b * hkv + kvh], 1);
+        *flag = (old == nchunks - 1);
+    }
+    named_bar_sync(1, kConsumerWarps * 32);
+    if (!*flag) return;
+    __threadfence();
+    if (row < group) {
+        float M = kNegInf;
+        for (int ch = 0; ch < nchunks; ++ch) {
+            int64_t pi = (static_cast<int64_t>(b) * max_chunks + ch) * hq + head;
+            M = fmaxf(M, __ldcg(ws_ml + pi * 2));
+        }
+        float O[8] = {0, 0, 0, 0, 0, 0, 0, 0}, Ls = 0.f;
+        for (int ch = 0; ch < nchunks; ++ch) {
+            int64_t pi = (static_cast<int64_t>(b) * max_chunks + ch) * hq + head;
+            float mc = __ldcg(ws_ml + pi * 2);
+            float sc = (mc == kNegInf) ? 0.f : exp2f(mc - M);
+            Ls += __ldcg(ws_ml + pi * 2 + 1) * sc;
+            const float4* src = reinterpret_cast<const float4*>(ws_o + pi * kHd + d0);
+            float4 a = __ldcg(src), bq = __ldcg(src + 1);
+            O[0] += a.x * sc; O[1] += a.y * sc; O[2] += a.z * sc; O[3] += a.w * sc;
+            O[4] += bq.x * sc; O[5] += bq.y * sc; O[6] += bq.z * sc; O[7] += bq.w * sc;
+        }
+        float inv = Ls > 0.f ? 1.f / Ls : 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) O[e] *= inv;
+        store_bf16x8(out + (static_cast<int64_t>(b) * hq + head) * kHd + d0, O);
+    }
+    if (threadIdx.x == 0) ws_cnt[b * hkv + kvh] = 0;
+}
+
+// ------------------------------------------------------------------------------ extend
+// grid (q tiles, Hkv, B); each warp owns 16 MMA rows = (16 / group) query tokens x group heads;
+// all four warps walk the same pages 0..(last visible page of the tile).
+__global__ void __launch_bounds__(kThreads)
+paged_extend_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+                    const __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ out,
+                    const int* __restrict__ page_table, int max_pages,
+                    const int* __restrict__ seq_lens, const int* __restrict__ q_indptr,
+                    int pool_pages, int hq, int hkv, float sl2e, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = align1024(smem_raw);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kExtendStages * kPageSlotBytes);
+    uint64_t* empty = full + kExtendStages;
+
+    const int b = blockIdx.z, kvh = blockIdx.y;
+    const int group = hq / hkv;
+    const int tpw = 16 / group;  // query tokens per warp
+    const int qbeg = q_indptr[b];
+    const int nq = q_indptr[b + 1] - qbeg;
+    const int tile0 = blockIdx.x * kConsumerWarps * tpw;
+    if (tile0 >= nq) return;
+    const int L = seq_lens[b];
+    const int last_tok = min(nq, tile0 + kConsumerWarps * tpw) - 1;
+    const int last_pos = L - nq + last_tok;  // visible kv tokens 0..last_pos
+    if (last_pos < 0) return;
+    int npages = last_pos / kPage + 1;
+    if (npages > max_pages) {  // context longer than the page-table row
+        if (threadIdx.x == 0) record_error(err, MSGL_ERR_BOUNDS, 222);
+        npages = max_pages;
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kExtendStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    if (warp == kConsumerWarps) {
+        if (lane == 0) {
+            tma_prefetch_desc(&tk);
+            tma_prefetch_desc(&tv);
+            const int* pt = page_table + static_cast<int64_t>(b) * max_pages;
+            for (int it = 0; it < npages; ++it) {
+                const int s = it % kExtendStages;
+                if (it >= kExtendStages &&
+                    !mbar_wait(&empty[s], ((it / kExtendStages) - 1) & 1, err, 220))
+                    break;
+                mbar_arrive_expect_tx(&full[s], kPageSlotBytes);
+                int page = pt[it];
+                if (static_cast<unsigned>(page) >= static_cast<unsigned>(pool_pages)) {
+                    record_error(err, MSGL_ERR_BOUNDS, 221);
+                    page = 0;
+                }
+                issue_page(smem + s * kPageSlotBytes, &tk, &tv, &full[s], kvh, page);
+            }
+        }
+        return;
+    }
+
+    const int g = lane >> 2, c = lane & 3;
+    // rows g and g + 8 of this warp: local token r / group, head r % group
+    const int r0 = g, r1 = g + 8;
+    const int i0 = tile0 + warp * tpw + r0 / group, i1 = tile0 + warp * tpw + r1 / group;
+    const bool v0 = i0 < nq, v1 = i1 < nq;
+    const int h0 = kvh * group + r0 % group, h1 = kvh * group + r1 % group;
+    const int lim0 = v0 ? L - nq + i0 : -1, lim1 = v1 ? L - nq + i1 : -1;
+    uint32_t qa[8][4];
+    {
+        const __nv_bfloat16* q0 = q + (static_cast<int64_t>(qbeg + (v0 ? i0 : 0)) * hq + h0) * kHd;
+        const __nv_bfloat16* q1 = q + (static_cast<int64_t>(qbeg + (v1 ? i1 : 0)) * hq + h1) * kHd;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+            qa[kk][0] = v0 ? *reinterpret_cast<const uint32_t*>(q0 + 16 * kk + 2 * c) : 0u;
+            qa[kk][2] = v0 ? *reinterpret_cast<const uint32_t*>(q0 + 16 * kk + 8 + 2 * c) : 0u;
+            qa[kk][1] = v1 ? *reinterpret_cast<const uint32_t*>(q1 + 16 * kk + 2 * c) : 0u;
+            qa[kk][3] = v1 ? *reinterpret_cast<const uint32_t*>(q1 + 16 * kk + 8 + 2 * c) : 0u;
+        }
+    }
+    float o[16][4];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    float m[2] = {kNegInf, kNegInf}, l[2] = {0.f, 0.f};
+    const int warp_last = max(lim0, lim1);
+
+    for (int it = 0; it < npages; ++it) {
+        const int s = it % kExtendStages;
+        if (!mbar_wait(&full[s], (it / kExtendStages) & 1, err, 230)) break;
+        if (it * kPage <= warp_last) {
+            uint32_t base = smem_u32(smem + s * kPageSlotBytes);
+            attend_page<true>(base, base + 4096, qa, o, m, l, it * kPage, lim0, lim1, sl2e, lane);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        float ls = l[r];
+        ls += __shfl_xor_sync(0xffffffffu, ls, 1);
+        ls += __shfl_xor_sync(0xffffffffu, ls, 2);
+        const bool valid = r == 0 ? v0 : v1;
+        if (!valid) continue;
+        const float inv = ls > 0.f ? 1.f / ls : 0.f;
+        const int i = r == 0 ? i0 : i1;
+        const int h = r == 0 ? h0 : h1;
+        __nv_bfloat16* dst = out + (static_cast<int64_t>(qbeg + i) * hq + h) * kHd;
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            *reinterpret_cast<uint32_t*>(dst + 8 * j + 2 * c) =
+                pack_bf16x2(o[j][2 * r] * inv, o[j][2 * r + 1] * inv);
+    }
+}
+
+// ------------------------------------------------------------------------------ host side
+struct DecodePlan {
+    int chunk_pages, max_chunks;
+    size_t off_ml, off_cnt, bytes;
+};
+
+DecodePlan plan_decode(int B, int max_seq_len, int hq, int hkv) {
+    DecodePlan p{};
+    const int max_pages_seq = std::max(1, (max_seq_len + kPage - 1) / kPage);
+    // Enough CTAs for ~8 per SM, chunks of at least 16 pages (256 tokens).
+    const int pairs = std::max(1, B * hkv);
+    int chunks = (8 * 148 + pairs - 1) / pairs;
+    chunks = std::max(1, std::min(chunks, (max_pages_seq + 15) / 16));
+    p.chunk_pages = (max_pages_seq + chunks - 1) / chunks;
+    p.max_chunks = (max_pages_seq + p.chunk_pages - 1) / p.chunk_pages;
+    auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+    size_t o_bytes = up(static_cast<size_t>(B) * p.max_chunks * hq * kHd * sizeof(float));
+    size_t ml_bytes = up(static_cast<size_t>(B) * p.max_chunks * hq * 2 * sizeof(float));
+    size_t cnt_bytes = up(static_cast<size_t>(B) * hkv * sizeof(int));
+    p.off_ml = o_bytes;
+    p.off_cnt = o_bytes + ml_bytes;
+    p.bytes = p.max_chunks > 1 ? o_bytes + ml_bytes + cnt_bytes : 0;
+    return p;
+}
+
+int check_common(int hq, int hkv, int head_dim, int page_size, int64_t num_slots) {
+    if (head_dim != kHd) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "attention: head_dim must be 128");
+    if (page_size != kPage) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "attention: page_size must be 16");
+    if (hkv <= 0 || hq <= 0 || hq % hkv) return set_error(MSGL_ERR_INVALID_ARG, "attention: Hq % Hkv != 0");
+    int group = hq / hkv;
+    if (group > 8 || (16 % group)) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "attention: Hq/Hkv must be 1,2,4 or 8");
+    if (num_slots <= 0 || num_slots % kPage || num_slots / kPage > INT32_MAX)
+        return set_error(MSGL_ERR_INVALID_ARG, "attention: num_slots must be a positive multiple of 16");
+    return MSGL_OK;
+}
+
+int make_pool_maps(CUtensorMap* tk, CUtensorMap* tv, const void* k_pool, const void* v_pool,
+                   int64_t num_slots, int hkv) {
+    const uint64_t row = static_cast<uint64_t>(hkv) * kHd;
+    int rc = make_tmap_2d_bf16(tk, k_pool, row, num_slots, row * 2, 64, kPage, true);
+    if (rc) return rc;
+    return make_tmap_2d_bf16(tv, v_pool, row, num_slots, row * 2, 64, kPage, true);
+}
+
+}  // namespace
+}  // namespace msgl
+
+using namespace msgl;
+
+extern "C" {
+
+size_t msgl_paged_attention_workspace_size(int num_reqs, int max_seq_len, int num_q_heads,
+                                           int num_kv_heads, int head_dim) {
+    if (num_reqs <= 0 || num_kv_heads <= 0 || head_dim != kHd) return 0;
+    return plan_decode(num_reqs, max_seq_len, num_q_heads, num_kv_heads).bytes;
+}
+
+int msgl_paged_attention_decode(const void* q, const void* k_pool, const void* v_pool,
+                                int64_t num_slots, const int* page_table, int max_pages,
+                                const int* seq_lens, int num_reqs, int max_seq_len,
+                                int num_q_heads, int num_kv_heads, int head_dim, int page_size,
+                                float scale, void* out, void* workspace,
+                                size_t workspace_bytes, msgl_stream_t stream) {
+    int rc = check_common(num_q_heads, num_kv_heads, head_dim, page_size, num_slots);
+    if (rc) return rc;
+    if (num_reqs < 0 || max_seq_len < 0 || max_pages <= 0)
+        return set_error(MSGL_ERR_INVALID_ARG, "decode: bad sizes");
+    if (num_reqs == 0) return MSGL_OK;
+    if ((max_seq_len + kPage - 1) / kPage > max_pages)
+        return set_error(MSGL_ERR_INVALID_ARG, "decode: max_seq_len exceeds page-table width");
+    DecodePlan p = plan_decode(num_reqs, max_seq_len, num_q_heads, num_kv_heads);
+    if (p.bytes > 0 && (!workspace || workspace_bytes < p.bytes))
+        return set_error(MSGL_ERR_WORKSPACE, "decode: workspace too small");
+    if (num_reqs > 65535) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "decode: num_reqs > 65535");
+    CUtensorMap tk, tv;
+    rc = make_pool_maps(&tk, &tv, k_pool, v_pool, num_slots, num_kv_heads);
+    if (rc) return rc;
+    int* err = device_error_word();
+    if (!err) return set_error(MSGL_ERR_CUDA, "device error word unavailable");
+    const size_t smem = kDecodeStages * 4 * kPageSlotBytes + 2 * kDecodeStages * 8 + 16 + 1024;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaFuncSetAttribute(paged_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem));
+        attr_set = true;
+    }
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    dim3 grid(p.max_chunks, num_kv_heads, num_reqs);
+    const float sl2e = scale * 1.4426950408889634f;
+    paged_decode_kernel<<<grid, kThreads, smem, stream>>>(
+        tk, tv, static_cast<const __nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(out), page_table,
+        max_pages, seq_lens, static_cast<int>(num_slots / kPage), num_q_heads, num_kv_heads,
+        p.chunk_pages, p.max_chunks, sl2e, p.bytes ? reinterpret_cast<float*>(ws) : nullptr,
+        p.bytes ? reinterpret_cast<float*>(ws + p.off_ml) : nullptr,
+        p.bytes ? reinterpret_cast<int*>(ws + p.off_cnt) : nullptr, err);
+    MSGL_LAUNCH_CHECK();
+    return MSGL_OK;
+}
+
+int msgl_paged_attention_extend(const void* q, const void* k_pool, const void* v_pool,
+                                int64_t num_slots, const int* page_table, int max_pages,
+                                const int* seq_lens, const int* q_indptr, int num_reqs,
+                                int max_q_len, int num_q_heads, int num_kv_heads, int head_dim,
+                                int page_size, float scale, void* out, msgl_stream_t stream) {
+    int rc = check_common(num_q_heads, num_kv_heads, head_dim, page_size, num_slots);
+    if (rc) return rc;
+    if (num_reqs < 0 || max_q_len < 0 || max_pages <= 0)
+        return set_error(MSGL_ERR_INVALID_ARG, "extend: bad sizes");
+    if (num_reqs == 0 || max_q_len == 0) return MSGL_OK;
+    if (num_reqs > 65535) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "extend: num_reqs > 65535");
+    CUtensorMap tk, tv;
+    rc = make_pool_maps(&tk, &tv, k_pool, v_pool, num_slots, num_kv_heads);
+    if (rc) return rc;
+    int* err = device_error_word();
+    if (!err) return set_error(MSGL_ERR_CUDA, "device error word unavailable");
+    const size_t smem = kExtendStages * kPageSlotBytes + 2 * kExtendStages * 8 + 1024;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaFuncSetAttribute(paged_extend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem));
+        attr_set = true;
+    }
+    const int group = num_q_heads / num_kv_heads;
+    const int tile_tokens = kConsumerWarps * (16 / group);
+    dim3 grid((max_q_len + tile_tokens - 1) / tile_tokens, num_kv_heads, num_reqs);
+    const float sl2e = scale * 1.4426950408889634f;
+    paged_extend_kernel<<<grid, kThreads, smem, stream>>>(
+        tk, tv, static_cast<const __nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(out), page_table,
+        max_pages, seq_lens, q_indptr, static_cast<int>(num_slots / kPage), num_q_heads,
+        num_kv_heads, sl2e, err);
+    MSGL_LAUNCH_CHECK();
+    return MSGL_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,431 @@
+// gemm.cu -- tcgen05 / TMEM bf16 GEMMs for the dense projections.
+//
+// Linear::forward (src/layer/layer.cpp:122-143): y[M,N] = x[M,K] W[N,K]^T with W in the
+// reference's [out, in] layout. Each CTA computes one 128 x BN tile of y^T = W x^T: the 128
+// weight rows are the UMMA M dimension and up to 256 tokens the N dimension, so a decode step
+// (M = batch tokens) is a single weight-streaming pass in which every weight byte crosses HBM
+// once. Roles (192 threads):
+//   warp 0      TMA producer: 128 x 64 weight tile + BN x 64 token tile per k-block (SW128)
+//   warp 1      TMEM allocator and single-thread tcgen05.mma issuer (M=128, N=BN, K=16)
+//   warps 2-5   epilogue: tcgen05.ld of the fp32 accumulator (one TMEM lane = one weight row)
+// Small grids split K across CTAs; partial tiles go to a workspace and the last CTA to arrive
+// (self-resetting counter) sums them in split order (deterministic) and runs the epilogue.
+// Epilogues: bf16 store, fp32 store, SwiGLU (gate/up rows interleaved by msgl_pack_gate_up;
+// split of qwen3.cpp:62-77 + SwiGLU of layer.cpp:155-158), argmax (scheduler.cpp:117-124).
+#include <algorithm>
+
+#include "common.cuh"
+#include "tmap.h"
+
+namespace msgl {
+namespace {
+
+constexpr int kBM = 128;       // weight rows per tile (UMMA M)
+constexpr int kBK = 64;        // K per stage: one 128-byte swizzle row
+constexpr int kGemmThreads = 192;
+constexpr int kTileA = kBM * kBK * 2;  // 16 KB
+
+enum Epi { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3 };
+
+template <int BN>
+struct GemmCfg {
+    static constexpr int kTileB = BN * kBK * 2;
+    static constexpr int kStageBytes = kTileA + kTileB;
+    static constexpr int kStages = BN >= 256 ? 4 : (96 * 1024) / kStageBytes;
+    static constexpr int kTmemCols = BN < 32 ? 32 : BN;
+    static constexpr size_t kSmem = static_cast<size_t>(kStages) * kStageBytes + 1024 + 256;
+};
+
+__device__ __forceinline__ void named_bar(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long argmax_key(float v, int n) {
+    uint32_t u = __float_as_uint(v);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return (static_cast<unsigned long long>(u) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(n));
+}
+
+// Epilogue on one 16-column chunk of the accumulator held by this thread (row `row` of the
+// tile = weight row n). vals[j] is column col0 + j (token m0 + col0 + j).
+template <int EPI>
+__device__ __forceinline__ void epilogue_chunk(const float (&vals)[16], int n, int N, int m_base,
+                                               int M, void* y, unsigned long long* amax,
+                                               int lane, int warp_q, int n_tile) {
+    if (EPI == EPI_BF16 || EPI == EPI_F32) {
+        if (n >= N) return;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            int m = m_base + j;
+            if (m < M) {
+                if (EPI == EPI_BF16)
+                    static_cast<__nv_bfloat16*>(y)[static_cast<int64_t>(m) * N + n] =
+                        __float2bfloat16_rn(vals[j]);
+                else
+                    static_cast<float*>(y)[static_cast<int64_t>(m) * N + n] = vals[j];
+            }
+        }
+    } else if (EPI == EPI_SWIGLU) {
+        // rows of each 32-row group: 16 gate rows then the 16 matching up rows
+        const int inter = N >> 1;
+        const int f = n_tile * (kBM / 2) + warp_q * 16 + (lane & 15);
+        const bool lo = lane < 16;
+#pragma unroll
+        for (int j = 0; j < 16; j += 2) {
+            float send = lo ? vals[j + 1] : vals[j];
+            float recv = __shfl_xor_sync(0xffffffffu, send, 16);
+            float g = lo ? vals[j] : recv;
+            float u = lo ? recv : vals[j + 1];
+            int m = m_base + j + (lo ? 0 : 1);
+            if (m < M && f < inter)
+                static_cast<__nv_bfloat16*>(y)[static_cast<int64_t>(m) * inter + f] =
+                    __float2bfloat16_rn(g / (1.0f + expf(-g)) * u);
+        }
+    } else {  // EPI_ARGMAX
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            unsigned long long key = n < N ? argmax_key(vals[j], n) : 0ull;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+                key = other > key ? other : key;
+            }
+            int m = m_base + j;
+            if (lane == 0 && m < M) atomicMax(amax + m, key);
+        }
+    }
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+            void* __restrict__ y, unsigned long long* __restrict__ amax, int M, int N, int K,
+            int kb_per_split, int splits, float* __restrict__ ws, int* __restrict__ ws_cnt,
+            int* err) {
+    using Cfg = GemmCfg<BN>;
+    constexpr int ST = Cfg::kStages;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + ST * kTileA;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + ST * Cfg::kStageBytes);
+    uint64_t* empty = full + ST;
+    uint64_t* accum_full = empty + ST;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum_full + 1);
+    int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m_tile = blockIdx.x, n_tile = blockIdx.y, split = blockIdx.z;
+    const int m0 = m_tile * BN, n0 = n_tile * kBM;
+    const int kbs = (K + kBK - 1) / kBK;
+    const int kb0 = split * kb_per_split;
+    const int kb1 = min(kbs, kb0 + kb_per_split);
+    const int nkb = kb1 - kb0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < ST; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accum_full, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, Cfg::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            tma_prefetch_desc(&tmap_w);
+            tma_prefetch_desc(&tmap_x);
+            const uint64_t pol_w = policy_evict_first();
+            const uint64_t pol_x = policy_evict_last();
+            for (int i = 0; i < nkb; ++i) {
+                const int s = i % ST;
+                if (i >= ST && !mbar_wait(&empty[s], ((i / ST) - 1) & 1, err, 300)) break;
+                mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
+                const int kx = (kb0 + i) * kBK;
+                tma_load_2d_hint(sA + s * kTileA, &tmap_w, &full[s], kx, n0, pol_w);
+                tma_load_2d_hint(sB + s * Cfg::kTileB, &tmap_x, &full[s], kx, m0, pol_x);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_bf16(kBM, BN);
+            for (int i = 0; i < nkb; ++i) {
+                const int s = i % ST;
+                if (!mbar_wait(&full[s], (i / ST) & 1, err, 310)) break;
+                tc_fence_after();
+                const uint32_t a_addr = smem_u32(sA + s * kTileA);
+                const uint32_t b_addr = smem_u32(sB + s * Cfg::kTileB);
+#pragma unroll
+                for (int k = 0; k < kBK / 16; ++k) {
+                    umma_bf16(tmem, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32),
+                              idesc, (i > 0 || k > 0) ? 1u : 0u);
+                }
+                umma_commit(&empty[s]);
+            }
+            umma_commit(accum_full);
+        }
+    } else {
+        // ---------------- epilogue warps 2..5
+        const int warp_q = warp & 3;  // TMEM lane quarter this warp may access
+        const int row = warp_q * 32 + lane;
+        const int n = n0 + row;
+        const int et = threadIdx.x - 64;  // 0..127
+        const bool have = nkb > 0 && mbar_wait(accum_full, 0, err, 320);
+        tc_fence_after();
+        const uint32_t taddr = tmem + (static_cast<uint32_t>(warp_q * 32) << 16);
+        if (splits == 1) {
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 16) {
+                uint32_t r[16];
+                float v[16];
+                tmem_ld16(taddr + c0, r);
+                tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = have ? __uint_as_float(r[j]) : 0.f;
+                epilogue_chunk<EPI>(v, n, N, m0 + c0, M, y, amax, lane, warp_q, n_tile);
+            }
+        } else {
+            const int64_t tile_id = static_cast<int64_t>(n_tile) * gridDim.x + m_tile;
+            float* part = ws + (tile_id * splits + split) * (static_cast<int64_t>(BN) * kBM);
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 16) {
+                uint32_t r[16];
+                tmem_ld16(taddr + c0, r);
+                tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    __stcg(part + (c0 + j) * kBM + row, have ? __uint_as_float(r[j]) : 0.f);
+            }
+            __threadfence();
+            named_bar(1, 128);
+            if (et == 0) {
+                int old = atomicAdd(ws_cnt + tile_id, 1);
+                *last_flag = (old == splits - 1);
+            }
+            named_bar(1, 128);
+            if (*last_flag) {
+                __threadfence();
+                const float* base = ws + tile_id * splits * (static_cast<int64_t>(BN) * kBM);
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 16) {
+                    float v[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] = 0.f;
+                    for (int sp = 0; sp < splits; ++sp) {
+                        const float* p = base + static_cast<int64_t>(sp) * BN * kBM;
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) v[j] += __ldcg(p + (c0 + j) * kBM + row);
+                    }
+                    epilogue_chunk<EPI>(v, n, N, m0 + c0, M, y, amax, lane, warp_q, n_tile);
+                }
+                if (et == 0) ws_cnt[tile_id] = 0;
+            }
+        }
+        tc_fence_before();
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, Cfg::kTmemCols);
+    }
+}
+
+struct GemmPlan {
+    int bn, m_tiles, n_tiles, splits, kb_per_split;
+    size_t ws_part_bytes, ws_cnt_off, ws_bytes;
+};
+
+int pick_bn(int M) {
+    if (M <= 16) return 16;
+    if (M <= 32) return 32;
+    if (M <= 64) return 64;
+    if (M <= 128) return 128;
+    return 256;
+}
+
+GemmPlan plan_gemm(int M, int N, int K) {
+    GemmPlan p{};
+    p.bn = pick_bn(M);
+    p.m_tiles = (M + p.bn - 1) / p.bn;
+    p.n_tiles = (N + kBM - 1) / kBM;
+    const int kbs = (K + kBK - 1) / kBK;
+    const int tiles = p.m_tiles * p.n_tiles;
+    const int slots = p.bn >= 256 ? 148 : 2 * 148;  // resident CTAs (smem-bound)
+    int splits = 1;
+    if (tiles < slots) splits = std::max(1, std::min(slots / tiles, std::max(1, kbs / 4)));
+    splits = std::min(splits, 32);
+    p.kb_per_split = (kbs + splits - 1) / splits;
+    p.splits = (kbs + p.kb_per_split - 1) / p.kb_per_split;
+    auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+    if (p.splits > 1) {
+        p.ws_part_bytes = up(static_cast<size_t>(tiles) * p.splits * p.bn * kBM * sizeof(float));
+        p.ws_cnt_off = p.ws_part_bytes;
+        p.ws_bytes = p.ws_part_bytes + up(static_cast<size_t>(tiles) * sizeof(int));
+    }
+    return p;
+}
+
+template <int BN, int EPI>
+int launch_bn(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& tx, void* y,
+              unsigned long long* amax, int M, int N, int K, void* ws, cudaStream_t stream) {
+    using Cfg = GemmCfg<BN>;
+    int* err = device_error_word();
+    if (!err) return set_error(MSGL_ERR_CUDA, "device error word unavailable");
+    cudaFuncSetAttribute(gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(Cfg::kSmem));
+    dim3 grid(p.m_tiles, p.n_tiles, p.splits);
+    uint8_t* w8 = static_cast<uint8_t*>(ws);
+    gemm_kernel<BN, EPI><<<grid, kGemmThreads, Cfg::kSmem, stream>>>(
+        tw, tx, y, amax, M, N, K, p.kb_per_split, p.splits,
+        p.splits > 1 ? reinterpret_cast<float*>(w8) : nullptr,
+        p.splits > 1 ? reinterpret_cast<int*>(w8 + p.ws_cnt_off) : nullptr, err);
+    MSGL_LAUNCH_CHECK();
+    return MSGL_OK;
+}
+
+template <int EPI>
+int run_gemm(const void* x, const void* w, void* y, unsigned long long* amax, int M, int N, int K,
+             void* ws, size_t ws_bytes, cudaStream_t stream) {
+    if (M < 0 || N <= 0 || K <= 0) return set_error(MSGL_ERR_INVALID_ARG, "gemm: bad sizes");
+    if (K % 8) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "gemm: K must be a multiple of 8");
+    if (M == 0) return MSGL_OK;
+    if (M > 65535 * 256) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "gemm: M too large");
+    GemmPlan p = plan_gemm(M, N, K);
+    if (p.ws_bytes > 0 && (!ws || ws_bytes < p.ws_bytes))
+        return set_error(MSGL_ERR_WORKSPACE, "gemm: workspace too small");
+    CUtensorMap tw, tx;
+    int rc = make_tmap_2d_bf16(&tw, w, K, N, static_cast<uint64_t>(K) * 2, kBK, kBM, true);
+    if (rc) return rc;
+    rc = make_tmap_2d_bf16(&tx, x, K, M, static_cast<uint64_t>(K) * 2, kBK, p.bn, true);
+    if (rc) return rc;
+    switch (p.bn) {
+        case 16: return launch_bn<16, EPI>(p, tw, tx, y, amax, M, N, K, ws, stream);
+        case 32: return launch_bn<32, EPI>(p, tw, tx, y, amax, M, N, K, ws, stream);
+        case 64: return launch_bn<64, EPI>(p, tw, tx, y, amax, M, N, K, ws, stream);
+        case 128: return launch_bn<128, EPI>(p, tw, tx, y, amax, M, N, K, ws, stream);
+        default: return launch_bn<256, EPI>(p, tw, tx, y, amax, M, N, K, ws, stream);
+    }
+}
+
+__global__ void pack_gate_up_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst,
+                                    int inter, int row_vecs) {
+    const int r = blockIdx.x;  // packed row
+    const int grp = r >> 5, within = r & 31;
+    const int srow = within < 16 ? grp * 16 + within : inter + grp * 16 + within - 16;
+    for (int v = threadIdx.x; v < row_vecs; v += blockDim.x)
+        dst[static_cast<int64_t>(r) * row_vecs + v] = src[static_cast<int64_t>(srow) * row_vecs + v];
+}
+
+__global__ void unpack_argmax_kernel(unsigned long long* __restrict__ packed, int* __restrict__ ids,
+                                     int M) {
+    int m = blockIdx.x * blockDim.x + threadIdx.x;
+    if (m < M) ids[m] = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(packed[m] & 0xFFFFFFFFull));
+}
+
+template <typename T>
+__global__ void argmax_rows_kernel(const T* __restrict__ logits, int vocab, int* __restrict__ out) {
+    __shared__ unsigned long long red[8];
+    const T* r = logits + static_cast<int64_t>(blockIdx.x) * vocab;
+    unsigned long long best = 0ull;
+    for (int v = threadIdx.x; v < vocab; v += blockDim.x) {
+        float x;
+        if constexpr (sizeof(T) == 4) x = r[v];
+        else x = __bfloat162float(r[v]);
+        unsigned long long k = argmax_key(x, v);
+        best = k > best ? k : best;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+        best = other > best ? other : best;
+    }
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) best = red[w] > best ? red[w] : best;
+        best = red[0] > best ? red[0] : best;
+        out[blockIdx.x] = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(best & 0xFFFFFFFFull));
+    }
+}
+
+}  // namespace
+}  // namespace msgl
+
+using namespace msgl;
+
+extern "C" {
+
+size_t msgl_gemm_workspace_size(int M, int N, int K) {
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    return plan_gemm(M, N, K).ws_bytes;
+}
+
+int msgl_gemm_bf16(const void* x, const void* w, void* y, int M, int N, int K, int out_dtype,
+                   void* workspace, size_t workspace_bytes, msgl_stream_t stream) {
+    if (out_dtype == MSGL_BF16)
+        return run_gemm<EPI_BF16>(x, w, y, nullptr, M, N, K, workspace, workspace_bytes, stream);
+    if (out_dtype == MSGL_F32)
+        return run_gemm<EPI_F32>(x, w, y, nullptr, M, N, K, workspace, workspace_bytes, stream);
+    return set_error(MSGL_ERR_INVALID_ARG, "gemm: unknown out_dtype");
+}
+
+int msgl_pack_gate_up(const void* w_gate_up, void* w_packed, int inter, int hidden,
+                      msgl_stream_t stream) {
+    if (inter <= 0 || inter % 16 || hidden <= 0 || hidden % 8)
+        return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "pack_gate_up: inter % 16, hidden % 8");
+    if (w_gate_up == w_packed) return set_error(MSGL_ERR_INVALID_ARG, "pack_gate_up: in place");
+    pack_gate_up_kernel<<<2 * inter, 128, 0, stream>>>(static_cast<const uint4*>(w_gate_up),
+                                                       static_cast<uint4*>(w_packed), inter,
+                                                       hidden / 8);
+    MSGL_LAUNCH_CHECK();
+    return MSGL_OK;
+}
+
+int msgl_gemm_gate_up_silu(const void* x, const void* w_packed, void* y, int M, int inter, int K,
+                           void* workspace, size_t workspace_bytes, msgl_stream_t stream) {
+    if (inter <= 0 || inter % 16) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "gate_up: inter % 16");
+    return run_gemm<EPI_SWIGLU>(x, w_packed, y, nullptr, M, 2 * inter, K, workspace,
+                                workspace_bytes, stream);
+}
+
+int msgl_lm_head_argmax(const void* x, const void* w, int M, int vocab, int K,
+                        unsigned long long* packed, int* ids, void* workspace,
+                        size_t workspace_bytes, msgl_stream_t stream) {
+    if (M <= 0) return M == 0 ? MSGL_OK : set_error(MSGL_ERR_INVALID_ARG, "lm_head: M < 0");
+    if (cudaMemsetAsync(packed, 0, static_cast<size_t>(M) * sizeof(unsigned long long), stream) !=
+        cudaSuccess)
+        return set_error(MSGL_ERR_CUDA, "lm_head: memset failed");
+    int rc = run_gemm<EPI_ARGMAX>(x, w, nullptr, packed, M, vocab, K, workspace, workspace_bytes,
+                                  stream);
+    if (rc) return rc;
+    unpack_argmax_kernel<<<(M + 255) / 256, 256, 0, stream>>>(packed, ids, M);
+    MSGL_LAUNCH_CHECK();
+    return MSGL_OK;
+}
+
+int msgl_argmax(const void* logits, int num_rows, int vocab, int dtype, int* out,
+                msgl_stream_t stream) {
+    if (num_rows < 0 || vocab <= 0) return set_error(MSGL_ERR_INVALID_ARG, "argmax: bad sizes");
+    if (num_rows == 0) return MSGL_OK;
+    if (dtype == MSGL_F32)
+        argmax_rows_kernel<float><<<num_rows, 256, 0, stream>>>(static_cast<const float*>(logits),
+                                                                vocab, out);
+    else if (dtype == MSGL_BF16)
+        argmax_rows_kernel<__nv_bfloat16><<<num_rows, 256, 0, stream>>>(
+            static_cast<const __nv_bfloat16*>(logits), vocab, out);
+    else
+        return set_error(MSGL_ERR_INVALID_ARG, "argmax: unknown dtype");
+    MSGL_LAUNCH_CHECK();
+    return MSGL_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,77 @@
+"""ctypes loader for libmsgl.so with the argument types of include/msgl_kernels.h."""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+PKG = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+ROOT = os.path.dirname(PKG)
+LIB_PATH = os.path.join(PKG, "libmsgl.so")
+HEADERS = [os.path.join(ROOT, "include", f) for f in ("msgl_kernels.h", "msgl_engine.h")]
+
+P, I, I64, F, SZ, U64 = C.c_void_p, C.c_int, C.c_int64, C.c_float, C.c_size_t, C.c_uint64
+
+# entry point -> (restype, argtypes)
+SIGNATURES = {
+    "msgl_version": (C.c_char_p, []),
+    "msgl_last_error": (C.c_char_p, []),
+    "msgl_device_error": (I, [P, P, I, P]),
+    "msgl_launch_rmsnorm": (I, [P, P, P, I, I, F, I, P]),
+    "msgl_launch_rope": (I, [P, P, P, P, I, I, I, I, I, P]),
+    "msgl_launch_index_gather": (I, [P, P, P, I, I, I, I, P]),
+    "msgl_launch_store_kv_page": (I, [P, P, P, P, P, I, I, I, I, I, P]),
+    "msgl_add_rmsnorm": (I, [P, P, P, I, I, F, I, P]),
+    "msgl_embed_rmsnorm": (I, [P, P, I, I, I, P, F, P, P, P]),
+    "msgl_qknorm_rope_store_kv": (I, [P, P, P, P, I64, P, P, P, P, P, I, I, I, I, F, P]),
+    "msgl_paged_attention_workspace_size": (SZ, [I, I, I, I, I]),
+    "msgl_paged_attention_decode": (I, [P, P, P, I64, P, I, P, I, I, I, I, I, I, F, P, P, SZ, P]),
+    "msgl_paged_attention_extend": (I, [P, P, P, I64, P, I, P, P, I, I, I, I, I, I, F, P, P]),
+    "msgl_gemm_workspace_size": (SZ, [I, I, I]),
+    "msgl_gemm_bf16": (I, [P, P, P, I, I, I, I, P, SZ, P]),
+    "msgl_pack_gate_up": (I, [P, P, I, I, P]),
+    "msgl_gemm_gate_up_silu": (I, [P, P, P, I, I, I, P, SZ, P]),
+    "msgl_lm_head_argmax": (I, [P, P, I, I, I, P, P, P, SZ, P]),
+    "msgl_argmax": (I, [P, I, I, I, P, P]),
+    "msgl_fill_normal_bf16": (I, [P, I64, U64, U64, F, F, P]),
+}
+
+_LIB = None
+
+
+class MsglError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"msgl error {code}: {msg}")
+        self.code = code
+
+
+def header_symbols() -> list[str]:
+    """Names of every entry point declared with MSGL_API in include/*.h."""
+    names = []
+    for h in HEADERS:
+        if os.path.exists(h):
+            names += re.findall(r"^MSGL_API[^(]*?\b(msgl_\w+)\s*\(", open(h).read(), flags=re.M)
+    return names
+
+
+def lib():
+    """The loaded libmsgl (ctypes.CDLL). Raises if the in-tree library has not been built."""
+    global _LIB
+    if _LIB is None:
+        if not os.path.exists(LIB_PATH):
+            raise FileNotFoundError(
+                f"{LIB_PATH} not built: run `python mini-sglang-cpp_b200/build.py`")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name, None)
+            if fn is None:
+                continue
+            fn.restype = res
+            fn.argtypes = args
+        _LIB = L
+    return _LIB
+
+
+def check(rc: int) -> None:
+    if rc != 0:
+        raise MsglError(rc, lib().msgl_last_error().decode())
