@@ -1,0 +1,460 @@
+"""Qwen3-8B decode throughput on B200 (the reference's headline metric).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (one step = one decode step of the executor): Qwen3-8B architecture (36 layers,
+hidden 4096, 32 q / 8 kv heads, head_dim 128, intermediate 12288, vocab 151936), random-init
+bf16 weights N(0, 0.02) (norm gains 1), batch 128, context 2048 per request = a 1024-token
+prefix held once in the pool (64 pages referenced by every page table, as a radix-cache match
+would) + 1024 unique tokens, page size 16, page placement shuffled over the pool (seed 3).
+KV contents are synthetic N(0, 1) bf16 (no prefill is timed). Every step reads ~35 GB
+(weights 16.4 GB + unique KV 19.5 GB), far above the 126 MB L2, so no flush is needed.
+
+value  : 128 tokens / step time, the step replayed as a CUDA graph on device-resident inputs
+         (CUDA events on the launching stream, max over ranks).
+e2e    : the same steps through msgl_model_step_host: pinned host batch -> H2D -> graph ->
+         D2H of the 128 next tokens -> stream sync, all inside the timed region.
+roofline: the paged decode-attention kernel (the largest share of the step) timed alone on the
+         same stream over all 36 layers' pools: unique KV bytes per launch / mean duration,
+         against MEASURED_PEAKS.json hbm_gbs.
+cpu_baseline: the reference's own CPU code (oracle/_ref: Linear::forward of the 4 layer
+         projections + lm_head; attention from the C restatement, as the reference has no
+         paged/GQA attention) on a bounded token sample, extrapolated to the full step.
+N > 1: independent replicas, one per GPU (weak scaling); tensor parallelism is not timed here.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "mini-sglang-cpp_b200"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+import numpy as np  # noqa: E402
+
+METRIC = "Qwen3-8B decode tok/s (batch 128, ctx 2048, 1024-token shared prefix)"
+UNIT = "tokens/s"
+CFG8B = dict(num_layers=36, hidden=4096, num_q_heads=32, num_kv_heads=8, head_dim=128,
+             inter=12288, vocab=151936, eps=1e-6, rope_base=1e6, max_position=4096)
+BATCH, CTX, PREFIX, PAGE = 128, 2048, 1024, 16
+
+
+def workload_config(n_gpus):
+    return {"workload": "qwen3-8b-decode", "model_arch": "Qwen3-8B", "global_batch": BATCH * n_gpus,
+            "batch_per_gpu": BATCH, "seq_len": CTX, "shared_prefix": PREFIX, "page_size": PAGE,
+            "parallelism": f"replicas{n_gpus}" if n_gpus > 1 else "single",
+            "l2": "inputs larger than L2 (35 GB read per step)"}
+
+
+# ------------------------------------------------------------------------------ page tables
+def build_pages(seed=3):
+    """Page tables for the 128 requests: 64 shared prefix pages + 64 unique pages each,
+    drawn LIFO (KVCachePool order) from a free list shuffled with `seed`."""
+    from msgl.model import PagePool
+    n_prefix, n_own = PREFIX // PAGE, (CTX - PREFIX) // PAGE
+    num_pages = n_prefix + BATCH * n_own + 16
+    pool = PagePool(num_pages)
+    rng = np.random.default_rng(seed)
+    rng.shuffle(pool.free)
+    prefix = [pool.allocate() for _ in range(n_prefix)]
+    pt = np.zeros((BATCH, n_prefix + n_own), np.int32)
+    for r in range(BATCH):
+        pt[r] = prefix + [pool.allocate() for _ in range(n_own)]
+    return num_pages, pt
+
+
+def decode_batch_host(pt, vocab, seed=1):
+    rng = np.random.default_rng(seed)
+    pos = np.full(BATCH, CTX - 1, np.int32)
+    slots = (pt[:, (CTX - 1) // PAGE] * PAGE + (CTX - 1) % PAGE).astype(np.int32)
+    return dict(input_ids=rng.integers(0, vocab, BATCH).astype(np.int32), positions=pos,
+                slot_mapping=slots, page_table=np.ascontiguousarray(pt),
+                seq_lens=np.full(BATCH, CTX, np.int32),
+                q_indptr=np.arange(BATCH + 1, dtype=np.int32),
+                last_idx=np.arange(BATCH, dtype=np.int32))
+
+
+# ------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples of this rank's GPU during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu, self.p, self.out = str(gpu_index), None, ""
+        try:  # nvidia-smi numbers GPUs independently of CUDA_VISIBLE_DEVICES: use the PCI id
+            import torch
+            pr = torch.cuda.get_device_properties(gpu_index)
+            self.gpu = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+        except Exception:
+            pass
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "100"],
+                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.p = None
+        return self
+
+    def __exit__(self, *a):
+        if self.p:
+            self.p.terminate()
+            try:
+                self.out, _ = self.p.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+                self.out = ""
+
+    def summary(self):
+        sm, mx, reasons = [], 0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------ CPU reference
+class CpuReference:
+    """The decode step on the reference CPU code, timed on a bounded sample.
+
+    Each worker thread carries one token through one layer's four projections (the reference's
+    Linear::forward, weights held in persistent Linear objects as in a loaded model) and one
+    request's attention over the 2048-token context (the C restatement: the reference has no
+    paged / GQA attention), then one token through lm_head. `threads` tokens therefore advance
+    one layer per sample; the full step (128 tokens x 36 layers + lm_head) extrapolates
+    linearly."""
+
+    def __init__(self, threads=None):
+        from oracle import Oracle, RefLib
+        self.ref, self.orc = RefLib(), Oracle()
+        t = threads or os.cpu_count() or 1
+        self.threads = max(1, min(t, 64))
+        H, I, V, D = CFG8B["hidden"], CFG8B["inter"], CFG8B["vocab"], 128
+        hq, hkv = CFG8B["num_q_heads"], CFG8B["num_kv_heads"]
+        self.dims = (H, V, D, hq, hkv)
+        L = self.ref.lib
+        self.handles = []
+        for n, k in [((hq + 2 * hkv) * D, H), (H, hq * D), (2 * I, H), (H, I)]:
+            w = np.full((n, k), 0.01, np.float32)  # values do not change fp32 loop timing
+            self.handles.append((L.ref_linear_create(w.ctypes.data, k, n), n, k))
+        wl = np.full((V, H), 0.01, np.float32)
+        self.lm = L.ref_linear_create(wl.ctypes.data, H, V)
+        ctx_pages = CTX // PAGE
+        rng = np.random.default_rng(0)
+        self.kp = rng.standard_normal((ctx_pages * PAGE, hkv * D)).astype(np.float32)
+        self.vp = rng.standard_normal((ctx_pages * PAGE, hkv * D)).astype(np.float32)
+        self.pt = np.arange(ctx_pages, dtype=np.int32)[None, :]
+
+    def close(self):
+        L = self.ref.lib
+        for h, _, _ in self.handles:
+            L.ref_linear_destroy(h)
+        L.ref_linear_destroy(self.lm)
+        self.handles = []
+
+    def _timed(self, fn):
+        ts = [threading.Thread(target=fn) for _ in range(self.threads)]
+        t0 = time.perf_counter()
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join()
+        return time.perf_counter() - t0
+
+    def sample(self, layers=36):
+        H, V, D, hq, hkv = self.dims
+        L = self.ref.lib
+
+        def layer_worker():
+            for h, n, k in self.handles:
+                xin = np.full((1, k), 0.1, np.float32)
+                out = np.empty((1, n), np.float32)
+                L.ref_linear_run(h, xin.ctypes.data, 1, out.ctypes.data)
+            q = np.full((1, hq * D), 0.01, np.float32)
+            self.orc.paged_attention(q, self.kp, self.vp, self.pt, [CTX], [0, 1], hq, hkv, D, PAGE)
+
+        def lm_worker():
+            xin = np.full((1, H), 0.1, np.float32)
+            out = np.empty((1, V), np.float32)
+            L.ref_linear_run(self.lm, xin.ctypes.data, 1, out.ctypes.data)
+
+        w_layer = self._timed(layer_worker)
+        w_lm = self._timed(lm_worker)
+        step_s = BATCH / self.threads * (layers * w_layer + w_lm)
+        desc = (f"{self.threads} tokens x 1 of 36 layers (4 projections, reference "
+                f"Linear::forward; attention over 2048 tokens, C restatement) + {self.threads} "
+                f"tokens x lm_head, extrapolated to 128 tokens x 36 layers; fp32")
+        return BATCH / step_s, desc
+
+
+def run_reference_arm(args, rank):
+    if rank != 0:
+        return 0
+    cpu = CpuReference()
+    vals = []
+    for i in range(args.warmup + args.steps):
+        v, sample = cpu.sample()
+        if i >= args.warmup:
+            vals.append(v)
+    cpu.close()
+    cores = cpu.threads
+    value = float(np.median(vals))
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000.0 * BATCH / value, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": workload_config(args.gpus),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "reference",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------------------ our arm
+def run_ours(args, rank, world, local_rank):
+    import ctypes as C
+
+    import torch
+    import torch.distributed as dist
+
+    import msgl
+    from msgl import ops
+    from msgl.model import BatchT, Qwen3Model, device_view, make_step
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    msgl.lib()
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+
+    num_pages, pt = build_pages()
+    model = Qwen3Model(CFG8B, max_tokens=BATCH, max_reqs=BATCH)
+    model.random_init(seed=0, std=0.02)
+    model.alloc_kv(num_pages)
+    L = CFG8B["num_layers"]
+    pools = [model.kv_pool(l) for l in range(L)]
+    for l, (k, v, n) in enumerate(pools):  # synthetic KV contents, N(0,1)
+        for j, p in enumerate((k, v)):
+            t = device_view(p, (n * CFG8B["num_kv_heads"] * 128,), torch.bfloat16)
+            ops.fill_normal_(t, seed=4, stream_id=2 * l + j, std=1.0)
+    host = decode_batch_host(pt, CFG8B["vocab"])
+    sb = make_step(host, True, dev, CTX, 1)
+    nxt = torch.empty(BATCH, dtype=torch.int32, device=dev)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- value: device-resident inputs, graph replay
+    for _ in range(max(args.warmup, 3)):
+        model.forward(sb, out=nxt, graph=True)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            model.forward(sb, out=nxt, graph=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    err = ops.device_error()
+    assert err == (0, 0), f"device error word {err}"
+
+    # ---- e2e: host buffers through msgl_model_step_host
+    pinned = {k: torch.from_numpy(v).pin_memory() for k, v in host.items()}
+    hb = BatchT(BATCH, BATCH, 1, pt.shape[1], CTX, 1,
+                *[pinned[k].data_ptr() for k in ("input_ids", "positions", "slot_mapping",
+                                                  "page_table", "seq_lens", "q_indptr",
+                                                  "last_idx")])
+    out_host = torch.empty(BATCH, dtype=torch.int32).pin_memory()
+    lib = msgl.lib()
+    sp = stream.cuda_stream
+    for _ in range(max(args.warmup, 3)):
+        msgl.check(lib.msgl_model_step_host(model.h, C.addressof(hb), out_host.data_ptr(), 1, sp))
+    barrier()
+    torch.cuda.synchronize()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for _ in range(args.steps):
+        msgl.check(lib.msgl_model_step_host(model.h, C.addressof(hb), out_host.data_ptr(), 1, sp))
+    e3.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms_e2e = max_over_ranks(e2.elapsed_time(e3) / args.steps)
+    h2d = sum(v.nbytes for v in host.values())
+    d2h = BATCH * 4
+    assert torch.equal(out_host.to(dev), nxt), "host step and device step disagree"
+
+    # ---- roofline: paged decode attention alone, every layer's pool
+    hq, hkv = CFG8B["num_q_heads"], CFG8B["num_kv_heads"]
+    q = torch.empty(BATCH, hq, 128, dtype=torch.bfloat16, device=dev)
+    ops.fill_normal_(q, seed=5, std=1.0)
+    aout = torch.empty_like(q)
+    ws = ops.attention_workspace(BATCH, CTX, hq, hkv, dev)
+    pt_d, seq_d = sb.tensors["page_table"], sb.tensors["seq_lens"]
+
+    def attn(l):
+        k, v, n = pools[l]
+        msgl.check(lib.msgl_paged_attention_decode(
+            q.data_ptr(), k, v, n, pt_d.data_ptr(), pt_d.shape[1], seq_d.data_ptr(), BATCH, CTX,
+            hq, hkv, 128, PAGE, 1.0 / 128 ** 0.5, aout.data_ptr(), ws.data_ptr(), ws.numel(), sp))
+
+    for l in range(L):
+        attn(l)
+    torch.cuda.synchronize()
+    reps = 3
+    e4, e5 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e4.record(stream)
+    for _ in range(reps):
+        for l in range(L):
+            attn(l)
+    e5.record(stream)
+    torch.cuda.synchronize()
+    attn_ms = e4.elapsed_time(e5) / (reps * L)
+    kv_row = hkv * 128 * 2 * 2  # K and V bytes per token
+    unique_bytes = (PREFIX + BATCH * (CTX - PREFIX)) * kv_row
+    per_request_bytes = BATCH * CTX * kv_row
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        pass
+    peak = peaks.get("hbm_gbs", 6650.0)
+    achieved = unique_bytes / (attn_ms * 1e-3) / 1e9
+
+    launches_per_step = 1 + L * 8 - 1 + 1 + 2
+    if rank == 0:
+        cpu = CpuReference()
+        cpu.sample()
+        cpu_val, sample = cpu.sample()
+        cpu.close()
+        cores = cpu.threads
+        line = {
+            "metric": METRIC, "value": world * BATCH / (ms * 1e-3), "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random-init weights, N(0,1) KV, random token ids)",
+            "config": workload_config(world),
+            "e2e": {"value": world * BATCH / (ms_e2e * 1e-3), "unit": UNIT,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": ms_e2e},
+            "roofline": {"kernel": "paged_decode_kernel", "bound": "hbm",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None,
+                         "algorithmic_bytes_per_launch": unique_bytes,
+                         "per_request_bytes_per_launch": per_request_bytes,
+                         "launch_ms": attn_ms,
+                         "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback"},
+            "cpu_baseline": {"value": cpu_val, "unit": UNIT, "cores": cores, "kind": "reference",
+                             "sample": sample},
+            "clocks": clk.summary(),
+            "gpu_launches": launches_per_step * args.steps,
+            "weights_gb": model.weight_bytes() / 1e9,
+        }
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_case(args):
+    """Small single-kernel cases at the bench's shapes, for profiling (one layer, < 1 GB):
+    `attention`: paged decode attention, 128 requests x 2048 context (shared 1024 prefix);
+    `gemm`: the gate_up + SwiGLU projection of one layer at 128 tokens (201 MB of weights)."""
+    import torch
+
+    import msgl
+    from msgl import ops
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    hq, hkv, H, I = CFG8B["num_q_heads"], CFG8B["num_kv_heads"], CFG8B["hidden"], CFG8B["inter"]
+    if args.case == "attention":
+        num_pages, pt = build_pages()
+        kp = torch.empty(num_pages * PAGE, hkv * 128, dtype=torch.bfloat16, device=dev)
+        vp = torch.empty_like(kp)
+        ops.fill_normal_(kp, seed=4, stream_id=0)
+        ops.fill_normal_(vp, seed=4, stream_id=1)
+        q = ops.fill_normal_(torch.empty(BATCH, hq, 128, dtype=torch.bfloat16, device=dev), seed=5)
+        ptd = torch.from_numpy(pt).to(dev)
+        seq = torch.full((BATCH,), CTX, dtype=torch.int32, device=dev)
+        ws = ops.attention_workspace(BATCH, CTX, hq, hkv, dev)
+        run = lambda: ops.paged_attention_decode(q, kp, vp, ptd, seq, CTX, hq, hkv, workspace=ws)
+    else:
+        x = ops.fill_normal_(torch.empty(BATCH, H, dtype=torch.bfloat16, device=dev), seed=6)
+        w = ops.fill_normal_(torch.empty(2 * I, H, dtype=torch.bfloat16, device=dev), seed=7,
+                             std=0.02)
+        ws = ops.gemm_workspace(BATCH, 2 * I, H, dev)
+        run = lambda: ops.gate_up_silu(x, w, workspace=ws)
+    for _ in range(args.steps):
+        run()
+    torch.cuda.synchronize()
+    assert ops.device_error() == (0, 0)
+    print(f"case {args.case}: {args.steps} launches ok", flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--case", choices=["attention", "gemm"], default=None,
+                    help="run one kernel of the step on a small single-layer case (profiling)")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.case:
+        return run_case(args)
+    if args.impl == "reference":
+        return run_reference_arm(args, rank)
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    try:
+        return run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

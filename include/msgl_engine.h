@@ -1,0 +1,102 @@
+/*
+ * msgl_engine.h -- C ABI of the device-side Qwen3 executor in libmsgl.
+ *
+ * The executor is the B200 counterpart of Qwen3ForCausalLM / Qwen3MoEForCausalLM
+ * (include/minisgl/model/qwen3.h:34-50, qwen3_moe.h:35-51 of mini-sglang-cpp): it owns bf16
+ * weights, one paged K/V pool per layer (layout of src/cache/kvcache.cpp:8-19, bf16, token-major
+ * [num_pages * page_size, Hkv * D]) and a preallocated workspace, and runs the per-layer forward
+ * (src/model/qwen3.cpp:16-83, 168-180) entirely through the kernels of msgl_kernels.h.
+ *
+ * A step is described by msgl_batch: the flattened token ids / positions of the scheduled
+ * requests (Scheduler::step, src/scheduler/scheduler.cpp:83-106) plus the paged-KV metadata
+ * the reference never passes down (page table, context lengths, query offsets, pool slots).
+ * The executor allocates all of its device memory at create / alloc_kv time; forward() itself
+ * allocates nothing and is capturable into a CUDA graph.
+ */
+#ifndef MSGL_ENGINE_H
+#define MSGL_ENGINE_H
+
+#include "msgl_kernels.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct msgl_model msgl_model;
+
+/* Model shape (fields of ModelConfig, include/minisgl/model/config.h:18-36) plus capacity. */
+typedef struct {
+    int num_layers, hidden, num_q_heads, num_kv_heads, head_dim, inter, vocab;
+    int num_experts, top_k, moe_inter, norm_topk; /* num_experts == 0: dense */
+    float eps, rope_base;
+    int max_position;      /* RoPE table rows; bounds every position */
+    int max_tokens;        /* capacity: tokens per step */
+    int max_reqs;          /* capacity: requests per step */
+    int tp_rank, tp_size;  /* tensor parallel shard of this process (1 GPU each) */
+} msgl_model_config;
+
+/* One scheduler step. All pointers are device int32 arrays. */
+typedef struct {
+    int num_tokens;          /* T */
+    int num_reqs;            /* B */
+    int is_decode;           /* 1: every request contributes exactly one token */
+    int max_pages;           /* page_table row width */
+    int max_seq_len;         /* bound on seq_lens */
+    int max_q_len;           /* bound on per-request query rows */
+    const int* input_ids;    /* [T] */
+    const int* positions;    /* [T] */
+    const int* slot_mapping; /* [T] pool slot of each token (page * page_size + offset), <0 skip */
+    const int* page_table;   /* [B, max_pages] */
+    const int* seq_lens;     /* [B] context length including this step's tokens */
+    const int* q_indptr;     /* [B+1] */
+    const int* last_idx;     /* [B] row of each request's last token (q_indptr[r+1]-1) */
+} msgl_batch;
+
+MSGL_API int msgl_model_create(const msgl_model_config* cfg, msgl_model** out);
+MSGL_API int msgl_model_destroy(msgl_model* m);
+
+/* Weights. random_init: every matrix N(0, std) from the counter-based generator keyed by
+ * (seed, tensor index), every norm gain 1.0. set_weight: host bf16 bit patterns of the FULL
+ * (unsharded) tensor named as in the reference's loader (qwen3.cpp:94-166) shortened:
+ *   embed, norm, lm_head, layers.<l>.{input_ln, qkv, q_norm, k_norm, o, post_ln, gate_up, down,
+ *   router}, layers.<l>.experts.<e>.{gate_up, down}
+ * (gate_up rows gate | up; qkv rows q | k | v). The executor keeps its tensor-parallel shard. */
+MSGL_API int msgl_model_random_init(msgl_model* m, uint64_t seed, float std, msgl_stream_t stream);
+MSGL_API int msgl_model_set_weight(msgl_model* m, const char* name, const uint16_t* host_bf16,
+                                   int64_t numel, msgl_stream_t stream);
+/* Device bytes held by weights / KV pools / workspace. */
+MSGL_API int64_t msgl_model_weight_bytes(const msgl_model* m);
+
+/* KV pools: num_pages pages of page_size (16) tokens per layer, zero-filled. */
+MSGL_API int msgl_model_alloc_kv(msgl_model* m, int num_pages, int page_size, msgl_stream_t stream);
+MSGL_API int msgl_model_kv_pool(msgl_model* m, int layer, void** k_pool, void** v_pool,
+                                int64_t* num_slots);
+
+/* One forward step: next_tokens [B] (device) = greedy tokens of each request's last row
+ * (scheduler.cpp:117-124 on the last token, fixing D10); logits (optional, device fp32
+ * [B, vocab]) receives the final logits of those rows.
+ * flags & MSGL_FWD_GRAPH: run the step as a CUDA graph, captured on first use and replayed
+ * while the batch's pointers and shape fields are unchanged (stream must not be the legacy
+ * default stream). */
+#define MSGL_FWD_GRAPH 1
+MSGL_API int msgl_model_forward(msgl_model* m, const msgl_batch* batch, int* next_tokens,
+                                float* logits, int flags, msgl_stream_t stream);
+
+/* The scheduler-facing step (Scheduler::step -> model_->forward, scheduler.cpp:108-124):
+ * `host_batch` holds HOST pointers (pinned for asynchronous copies); the executor copies them
+ * into its own device buffers, runs the step (as a CUDA graph when flags & MSGL_FWD_GRAPH and
+ * the step is a decode), copies the greedy tokens back into host_next_tokens [B] and
+ * synchronises the stream. */
+MSGL_API int msgl_model_step_host(msgl_model* m, const msgl_batch* host_batch,
+                                  int* host_next_tokens, int flags, msgl_stream_t stream);
+
+/* Debug: device pointer to the hidden state [max_tokens, hidden] bf16 after the most recent
+ * forward (the last layer's output before the final norm) -- used by per-layer parity tests
+ * together with num_layers_override. */
+MSGL_API int msgl_model_debug_hidden(msgl_model* m, void** x, float** residual);
+MSGL_API int msgl_model_set_num_layers_run(msgl_model* m, int n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MSGL_ENGINE_H */

@@ -22,7 +22,7 @@
 #include <stddef.h>
 #include <stdint.h>
 
-#ifdef __CUDACC__
+#if defined(__CUDACC__) || defined(CUDART_VERSION)
 #include <cuda_runtime.h>
 typedef cudaStream_t msgl_stream_t;
 #else
@@ -162,6 +162,44 @@ MSGL_API int msgl_gemm_gate_up_silu(const void* x, const void* w_packed, void* y
 MSGL_API int msgl_lm_head_argmax(const void* x, const void* w, int M, int vocab, int K,
                         unsigned long long* packed, int* ids, void* workspace,
                         size_t workspace_bytes, msgl_stream_t stream);
+
+/* ---------------------------------------------------------------- MoE */
+/* MoERouter::route (layer.cpp:270-309) after the router logits GEMM (msgl_gemm_bf16 with
+ * out_dtype MSGL_F32): per token the top_k experts by logit, equal logits resolved to the larger
+ * expert id (std::greater on pair<float,int>, layer.cpp:291-292); weight exp(logit), divided by
+ * the top-k sum when norm_topk (layer.cpp:294-305). num_experts <= 256, top_k <= 32. */
+MSGL_API int msgl_moe_route_topk(const float* router_logits, int num_tokens, int num_experts,
+                                 int top_k, int norm_topk, int* topk_ids, float* topk_weights,
+                                 msgl_stream_t stream);
+
+/* Counting sort of the num_tokens * top_k (token, k) pairs by expert, stable in pair order:
+ * expert_offsets [E+1] (rows of each expert in the sorted matrix), sorted_token [T*k] (token of
+ * each sorted row; gather x with msgl_launch_index_gather), pair_pos [T*k] (sorted row of pair
+ * t*k+j). Replaces the per-token expert loop of src/model/qwen3_moe.cpp:74-108. */
+MSGL_API int msgl_moe_permute(const int* topk_ids, int num_tokens, int top_k, int num_experts,
+                              int* expert_offsets, int* sorted_token, int* pair_pos,
+                              msgl_stream_t stream);
+
+/* Grouped tcgen05 GEMM over the expert-sorted rows: for expert e, rows
+ * [offsets[e], offsets[e+1]) of x_sorted [max_rows, K] times W_e^T, W = [E, N, K] (each expert
+ * in Linear's [out, in] layout), into y [max_rows, N]. The gate_up form takes per-expert weights
+ * packed by msgl_pack_gate_up and writes silu(gate) * up [max_rows, inter]. The workspace
+ * (msgl_grouped_gemm_workspace_size) holds the device-built tile list. */
+MSGL_API size_t msgl_grouped_gemm_workspace_size(int max_rows, int num_experts);
+MSGL_API int msgl_grouped_gemm_bf16(const void* x_sorted, const void* w, void* y,
+                                    const int* expert_offsets, int num_experts, int N, int K,
+                                    int max_rows, void* workspace, size_t workspace_bytes,
+                                    msgl_stream_t stream);
+MSGL_API int msgl_grouped_gemm_gate_up_silu(const void* x_sorted, const void* w_packed, void* y,
+                                            const int* expert_offsets, int num_experts, int inter,
+                                            int K, int max_rows, void* workspace,
+                                            size_t workspace_bytes, msgl_stream_t stream);
+
+/* out[t] = sum_j topk_weights[t,j] * y_sorted[pair_pos[t*k+j]], j in order, fp32 accumulation
+ * (qwen3_moe.cpp:102-106). out [T, hidden] bf16. */
+MSGL_API int msgl_moe_combine(const void* y_sorted, const int* pair_pos, const float* topk_weights,
+                              int num_tokens, int top_k, int hidden, void* out,
+                              msgl_stream_t stream);
 
 /* ---------------------------------------------------------------- sampling / utilities */
 /* Greedy argmax over logits [num_rows, vocab] (scheduler.cpp:117-124): first maximum wins. */

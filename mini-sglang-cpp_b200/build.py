@@ -50,7 +50,7 @@ def _compile(src, verbose):
         if verbose:
             cmd += ["-Xptxas", "-v"]
     else:
-        cmd = [NVCC, *COMMON, "-x", "cu", *ARCH, "-c", src, "-o", obj]
+        cmd = [NVCC, *ARCH, *COMMON, "-c", src, "-o", obj]
     r = subprocess.run(cmd, capture_output=True, text=True)
     return src, obj, r
 

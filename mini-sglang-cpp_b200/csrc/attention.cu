@@ -422,7 +422,10 @@ paged_extend_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
 #pragma unroll
     for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
     float m[2] = {kNegInf, kNegInf}, l[2] = {0.f, 0.f};
-    const int warp_last = max(lim0, lim1);
+    // Last visible kv token of any row of this warp. Warp-uniform on purpose: attend_page is
+    // made of warp-collective instructions (ldmatrix, mma.sync, full-mask shuffles), so the
+    // whole warp must take the same branch even when only some of its rows are valid.
+    const int warp_last = __reduce_max_sync(0xffffffffu, max(lim0, lim1));
 
     for (int it = 0; it < npages; ++it) {
         const int s = it % kExtendStages;

@@ -96,12 +96,21 @@ __device__ __forceinline__ void epilogue_chunk(const float (&vals)[16], int n, i
     }
 }
 
-template <int BN, int EPI>
+// Grouped (MoE) mode: CTA x of the grid takes tile `tiles[x]` = (expert, first row) of the
+// expert-sorted token matrix; rows past the expert's end are masked, weight rows are offset by
+// expert * N. CTAs beyond *num_tiles exit at once.
+struct GroupArgs {
+    const int2* tiles = nullptr;
+    const int* num_tiles = nullptr;
+    const int* offsets = nullptr;  // [E + 1] row offsets of each expert
+};
+
+template <int BN, int EPI, bool GROUPED>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
             void* __restrict__ y, unsigned long long* __restrict__ amax, int M, int N, int K,
             int kb_per_split, int splits, float* __restrict__ ws, int* __restrict__ ws_cnt,
-            int* err) {
+            GroupArgs grp, int* err) {
     using Cfg = GemmCfg<BN>;
     constexpr int ST = Cfg::kStages;
     extern __shared__ uint8_t smem_raw[];
@@ -117,7 +126,16 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m_tile = blockIdx.x, n_tile = blockIdx.y, split = blockIdx.z;
-    const int m0 = m_tile * BN, n0 = n_tile * kBM;
+    int m0 = m_tile * BN;
+    const int n0 = n_tile * kBM;
+    int w_row0 = 0;
+    if (GROUPED) {
+        if (m_tile >= *grp.num_tiles) return;  // uniform: before any barrier or TMEM use
+        const int2 t = grp.tiles[m_tile];
+        m0 = t.y;
+        M = grp.offsets[t.x + 1];
+        w_row0 = t.x * N;
+    }
     const int kbs = (K + kBK - 1) / kBK;
     const int kb0 = split * kb_per_split;
     const int kb1 = min(kbs, kb0 + kb_per_split);
@@ -151,7 +169,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
                 if (i >= ST && !mbar_wait(&empty[s], ((i / ST) - 1) & 1, err, 300)) break;
                 mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
                 const int kx = (kb0 + i) * kBK;
-                tma_load_2d_hint(sA + s * kTileA, &tmap_w, &full[s], kx, n0, pol_w);
+                tma_load_2d_hint(sA + s * kTileA, &tmap_w, &full[s], kx, w_row0 + n0, pol_w);
                 tma_load_2d_hint(sB + s * Cfg::kTileB, &tmap_x, &full[s], kx, m0, pol_x);
             }
         }
@@ -274,20 +292,21 @@ GemmPlan plan_gemm(int M, int N, int K) {
     return p;
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool GROUPED = false>
 int launch_bn(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& tx, void* y,
-              unsigned long long* amax, int M, int N, int K, void* ws, cudaStream_t stream) {
+              unsigned long long* amax, int M, int N, int K, void* ws, cudaStream_t stream,
+              GroupArgs grp = GroupArgs{}) {
     using Cfg = GemmCfg<BN>;
     int* err = device_error_word();
     if (!err) return set_error(MSGL_ERR_CUDA, "device error word unavailable");
-    cudaFuncSetAttribute(gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(gemm_kernel<BN, EPI, GROUPED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(Cfg::kSmem));
     dim3 grid(p.m_tiles, p.n_tiles, p.splits);
     uint8_t* w8 = static_cast<uint8_t*>(ws);
-    gemm_kernel<BN, EPI><<<grid, kGemmThreads, Cfg::kSmem, stream>>>(
+    gemm_kernel<BN, EPI, GROUPED><<<grid, kGemmThreads, Cfg::kSmem, stream>>>(
         tw, tx, y, amax, M, N, K, p.kb_per_split, p.splits,
         p.splits > 1 ? reinterpret_cast<float*>(w8) : nullptr,
-        p.splits > 1 ? reinterpret_cast<int*>(w8 + p.ws_cnt_off) : nullptr, err);
+        p.splits > 1 ? reinterpret_cast<int*>(w8 + p.ws_cnt_off) : nullptr, grp, err);
     MSGL_LAUNCH_CHECK();
     return MSGL_OK;
 }
@@ -313,6 +332,66 @@ int run_gemm(const void* x, const void* w, void* y, unsigned long long* amax, in
         case 64: return launch_bn<64, EPI>(p, tw, tx, y, amax, M, N, K, ws, stream);
         case 128: return launch_bn<128, EPI>(p, tw, tx, y, amax, M, N, K, ws, stream);
         default: return launch_bn<256, EPI>(p, tw, tx, y, amax, M, N, K, ws, stream);
+    }
+}
+
+// One thread per expert: the expert's row tiles of height bn, as (expert, first row) pairs.
+__global__ void group_tiles_kernel(const int* __restrict__ offsets, int E, int bn,
+                                   int2* __restrict__ tiles, int* __restrict__ num_tiles) {
+    __shared__ int pre[1025];
+    const int e = threadIdx.x;
+    int cnt = 0, beg = 0;
+    if (e < E) {
+        beg = offsets[e];
+        cnt = (offsets[e + 1] - beg + bn - 1) / bn;
+    }
+    pre[e + 1] = cnt;
+    if (e == 0) pre[0] = 0;
+    __syncthreads();
+    if (e == 0) {
+        for (int i = 1; i <= static_cast<int>(blockDim.x); ++i) pre[i] += pre[i - 1];
+        *num_tiles = pre[blockDim.x];
+    }
+    __syncthreads();
+    for (int i = 0; i < cnt; ++i) tiles[pre[e] + i] = make_int2(e, beg + i * bn);
+}
+
+template <int EPI>
+int run_grouped(const void* x, const void* w, void* y, const int* offsets, int E, int N, int K,
+                int max_rows, void* ws, size_t ws_bytes, cudaStream_t stream) {
+    if (E <= 0 || E > 1024 || N <= 0 || K <= 0 || max_rows < 0)
+        return set_error(MSGL_ERR_INVALID_ARG, "grouped gemm: bad sizes");
+    if (K % 8) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "grouped gemm: K % 8");
+    if (max_rows == 0) return MSGL_OK;
+    const int avg = (max_rows + E - 1) / E;
+    const int bn = pick_bn(avg);
+    const int max_tiles = (max_rows + bn - 1) / bn + E;
+    const size_t need = static_cast<size_t>(max_tiles) * sizeof(int2) + 256;
+    if (!ws || ws_bytes < need) return set_error(MSGL_ERR_WORKSPACE, "grouped gemm: workspace too small");
+    if (max_tiles > 65535 * 8) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "grouped gemm: too many tiles");
+    int* num_tiles = static_cast<int*>(ws);
+    int2* tiles = reinterpret_cast<int2*>(static_cast<uint8_t*>(ws) + 256);
+    group_tiles_kernel<<<1, E, 0, stream>>>(offsets, E, bn, tiles, num_tiles);
+    MSGL_LAUNCH_CHECK();
+    CUtensorMap tw, tx;
+    int rc = make_tmap_2d_bf16(&tw, w, K, static_cast<uint64_t>(E) * N, static_cast<uint64_t>(K) * 2,
+                               kBK, kBM, true);
+    if (rc) return rc;
+    rc = make_tmap_2d_bf16(&tx, x, K, max_rows, static_cast<uint64_t>(K) * 2, kBK, bn, true);
+    if (rc) return rc;
+    GemmPlan p{};
+    p.bn = bn;
+    p.m_tiles = max_tiles;
+    p.n_tiles = (N + kBM - 1) / kBM;
+    p.splits = 1;
+    p.kb_per_split = (K + kBK - 1) / kBK;
+    GroupArgs g{tiles, num_tiles, offsets};
+    switch (bn) {
+        case 16: return launch_bn<16, EPI, true>(p, tw, tx, y, nullptr, max_rows, N, K, nullptr, stream, g);
+        case 32: return launch_bn<32, EPI, true>(p, tw, tx, y, nullptr, max_rows, N, K, nullptr, stream, g);
+        case 64: return launch_bn<64, EPI, true>(p, tw, tx, y, nullptr, max_rows, N, K, nullptr, stream, g);
+        case 128: return launch_bn<128, EPI, true>(p, tw, tx, y, nullptr, max_rows, N, K, nullptr, stream, g);
+        default: return launch_bn<256, EPI, true>(p, tw, tx, y, nullptr, max_rows, N, K, nullptr, stream, g);
     }
 }
 
@@ -395,6 +474,28 @@ int msgl_gemm_gate_up_silu(const void* x, const void* w_packed, void* y, int M, 
     if (inter <= 0 || inter % 16) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "gate_up: inter % 16");
     return run_gemm<EPI_SWIGLU>(x, w_packed, y, nullptr, M, 2 * inter, K, workspace,
                                 workspace_bytes, stream);
+}
+
+size_t msgl_grouped_gemm_workspace_size(int max_rows, int num_experts) {
+    if (max_rows < 0 || num_experts <= 0) return 0;
+    const int bn = pick_bn((max_rows + num_experts - 1) / num_experts);
+    return static_cast<size_t>((max_rows + bn - 1) / bn + num_experts) * sizeof(int2) + 256;
+}
+
+int msgl_grouped_gemm_bf16(const void* x_sorted, const void* w, void* y,
+                           const int* expert_offsets, int num_experts, int N, int K, int max_rows,
+                           void* workspace, size_t workspace_bytes, msgl_stream_t stream) {
+    return run_grouped<EPI_BF16>(x_sorted, w, y, expert_offsets, num_experts, N, K, max_rows,
+                                 workspace, workspace_bytes, stream);
+}
+
+int msgl_grouped_gemm_gate_up_silu(const void* x_sorted, const void* w_packed, void* y,
+                                   const int* expert_offsets, int num_experts, int inter, int K,
+                                   int max_rows, void* workspace, size_t workspace_bytes,
+                                   msgl_stream_t stream) {
+    if (inter <= 0 || inter % 16) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "grouped gate_up: inter % 16");
+    return run_grouped<EPI_SWIGLU>(x_sorted, w_packed, y, expert_offsets, num_experts, 2 * inter,
+                                   K, max_rows, workspace, workspace_bytes, stream);
 }
 
 int msgl_lm_head_argmax(const void* x, const void* w, int M, int vocab, int K,

@@ -1,0 +1,187 @@
+// layers.h -- device-side layer classes of the executor.
+//
+// Same class and method names as the reference's layer ops (include/minisgl/layer/layer.h:11-96),
+// with the bodies dispatching to the libmsgl C ABI. Differences, all deliberate:
+//  * the caller owns every buffer (the reference allocates a fresh Tensor per call,
+//    src/layer/layer.cpp:17,50,124,147,218,273);
+//  * activations are bf16, accumulation fp32, the residual stream fp32;
+//  * Attention reads the paged per-layer KV pool (the reference attends over the flattened batch,
+//    layer.cpp:226-257) and RotaryEmbedding rotates q and k (layer.cpp:186-199 rotates q only);
+//  * gate_up and SwiGLU are one GEMM (GateUpSwiGLU) and QK-norm + RoPE + KV store one kernel.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "msgl_engine.h"
+
+namespace msgl {
+namespace engine {
+
+using bf16_t = uint16_t;  // bf16 storage
+
+struct Fail : std::runtime_error {
+    int code;
+    Fail(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+inline void ck(int rc, const char* what) {
+    if (rc != MSGL_OK) throw Fail(rc, std::string(what) + ": " + msgl_last_error());
+}
+inline void ckc(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) throw Fail(MSGL_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// Device buffer owned by the executor.
+struct DevBuf {
+    void* p = nullptr;
+    size_t bytes = 0;
+    DevBuf() = default;
+    DevBuf(const DevBuf&) = delete;
+    DevBuf& operator=(const DevBuf&) = delete;
+    DevBuf(DevBuf&& o) noexcept : p(o.p), bytes(o.bytes) { o.p = nullptr; o.bytes = 0; }
+    DevBuf& operator=(DevBuf&& o) noexcept {
+        if (this != &o) {
+            reset();
+            p = o.p; bytes = o.bytes;
+            o.p = nullptr; o.bytes = 0;
+        }
+        return *this;
+    }
+    ~DevBuf() { reset(); }
+    void alloc(size_t n) {
+        reset();
+        if (n == 0) return;
+        ckc(cudaMalloc(&p, n), "cudaMalloc");
+        bytes = n;
+    }
+    void reset() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        bytes = 0;
+    }
+    template <typename T>
+    T* as() const { return static_cast<T*>(p); }
+};
+
+// Workspace shared by the GEMMs / attention of one executor (they run in stream order).
+struct Scratch {
+    void* gemm_ws = nullptr;
+    size_t gemm_ws_bytes = 0;
+    void* attn_ws = nullptr;
+    size_t attn_ws_bytes = 0;
+};
+
+class RMSNorm {  // layer.h:23-34
+  public:
+    RMSNorm() = default;
+    RMSNorm(int size, float eps) : size_(size), eps_(eps) {}
+    void forward_fused_add(bf16_t* x, float* residual, int num_tokens, bool first,
+                           cudaStream_t s) const {
+        ck(msgl_add_rmsnorm(x, residual, weight.p, num_tokens, size_, eps_, first ? 1 : 0, s),
+           "RMSNorm::forward_fused_add");
+    }
+    DevBuf weight;  // bf16 [size]
+    int size() const { return size_; }
+    float eps() const { return eps_; }
+
+  private:
+    int size_ = 0;
+    float eps_ = 1e-6f;
+};
+
+class Linear {  // layer.h:36-48; y = x W^T, W [out, in]
+  public:
+    Linear() = default;
+    Linear(int in_features, int out_features) : in_(in_features), out_(out_features) {}
+    void forward(const bf16_t* x, bf16_t* y, int num_tokens, const Scratch& ws,
+                 cudaStream_t s) const {
+        ck(msgl_gemm_bf16(x, weight.p, y, num_tokens, out_, in_, MSGL_BF16, ws.gemm_ws,
+                          ws.gemm_ws_bytes, s),
+           "Linear::forward");
+    }
+    size_t workspace(int max_tokens) const { return msgl_gemm_workspace_size(max_tokens, out_, in_); }
+    DevBuf weight;  // bf16 [out, in]
+    int in_features() const { return in_; }
+    int out_features() const { return out_; }
+
+  private:
+    int in_ = 0, out_ = 0;
+};
+
+// gate_up_proj + split + SwiGLU (qwen3.cpp:60-79) as one GEMM on the packed gate/up weight.
+class GateUpSwiGLU {
+  public:
+    GateUpSwiGLU() = default;
+    GateUpSwiGLU(int in_features, int inter) : in_(in_features), inter_(inter) {}
+    void forward(const bf16_t* x, bf16_t* act, int num_tokens, const Scratch& ws,
+                 cudaStream_t s) const {
+        ck(msgl_gemm_gate_up_silu(x, weight_packed.p, act, num_tokens, inter_, in_, ws.gemm_ws,
+                                  ws.gemm_ws_bytes, s),
+           "GateUpSwiGLU::forward");
+    }
+    size_t workspace(int max_tokens) const {
+        return msgl_gemm_workspace_size(max_tokens, 2 * inter_, in_);
+    }
+    DevBuf weight_packed;  // bf16 [2 * inter, in], rows packed by msgl_pack_gate_up
+    int inter() const { return inter_; }
+    int in_features() const { return in_; }
+
+  private:
+    int in_ = 0, inter_ = 0;
+};
+
+// RotaryEmbedding (layer.h:57-68): one fp32 [max_position, D] table for all layers (the
+// reference builds one per layer, D18), computed on the host with the reference formula
+// (layer.cpp:168-175) and uploaded.
+class RotaryEmbedding {
+  public:
+    void init(int head_dim, int max_position, float base, cudaStream_t s);
+    DevBuf cos_sin_cache;
+    int head_dim = 128, max_position = 0;
+};
+
+// QK-norm + RoPE + KV-page store, then paged attention (replaces Attention, layer.h:70-81).
+class Attention {
+  public:
+    Attention() = default;
+    Attention(int hq, int hkv, int head_dim, float eps)
+        : hq_(hq), hkv_(hkv), head_dim_(head_dim), eps_(eps) {}
+    // qkv [T, (hq + 2 hkv) D] -> q [T, hq, D] (normed, rotated); k / v stored in the pools.
+    void prepare(const bf16_t* qkv, bf16_t* q, void* k_pool, void* v_pool, int64_t num_slots,
+                 const int* positions, const int* slot_mapping, const RotaryEmbedding& rope,
+                 const void* q_norm_w, const void* k_norm_w, int num_tokens, cudaStream_t s) const {
+        ck(msgl_qknorm_rope_store_kv(qkv, q, k_pool, v_pool, num_slots, positions, slot_mapping,
+                                     rope.cos_sin_cache.as<float>(), q_norm_w, k_norm_w,
+                                     num_tokens, hq_, hkv_, head_dim_, eps_, s),
+           "Attention::prepare");
+    }
+    void forward(const bf16_t* q, const void* k_pool, const void* v_pool, int64_t num_slots,
+                 const msgl_batch& b, bf16_t* out, const Scratch& ws, cudaStream_t s) const {
+        const float scale = 1.0f / sqrtf(static_cast<float>(head_dim_));  // layer.cpp:212
+        if (b.is_decode)
+            ck(msgl_paged_attention_decode(q, k_pool, v_pool, num_slots, b.page_table, b.max_pages,
+                                           b.seq_lens, b.num_reqs, b.max_seq_len, hq_, hkv_,
+                                           head_dim_, 16, scale, out, ws.attn_ws, ws.attn_ws_bytes,
+                                           s),
+               "Attention::forward(decode)");
+        else
+            ck(msgl_paged_attention_extend(q, k_pool, v_pool, num_slots, b.page_table, b.max_pages,
+                                           b.seq_lens, b.q_indptr, b.num_reqs, b.max_q_len, hq_,
+                                           hkv_, head_dim_, 16, scale, out, s),
+               "Attention::forward(extend)");
+    }
+    int hq() const { return hq_; }
+    int hkv() const { return hkv_; }
+
+  private:
+    int hq_ = 0, hkv_ = 0, head_dim_ = 128;
+    float eps_ = 1e-6f;
+};
+
+}  // namespace engine
+}  // namespace msgl

@@ -1,0 +1,501 @@
+// qwen3.cpp -- the device-side Qwen3 executor (Qwen3DecoderLayer / Qwen3ForCausalLM of
+// src/model/qwen3.cpp:16-83, 85-92, 168-180) and its C ABI (include/msgl_engine.h).
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "layers.h"
+#include "msgl_engine.h"
+
+namespace msgl {
+namespace engine {
+
+void RotaryEmbedding::init(int d, int max_pos, float base, cudaStream_t s) {
+    head_dim = d;
+    max_position = max_pos;
+    std::vector<float> t(static_cast<size_t>(max_pos) * d);
+    for (int p = 0; p < max_pos; ++p)  // layer.cpp:168-175
+        for (int i = 0; i < d / 2; ++i) {
+            float freq = 1.0f / std::pow(base, (2.0f * i) / d);
+            float val = p * freq;
+            t[static_cast<size_t>(p) * d + i] = std::cos(val);
+            t[static_cast<size_t>(p) * d + d / 2 + i] = std::sin(val);
+        }
+    cos_sin_cache.alloc(t.size() * sizeof(float));
+    ckc(cudaMemcpyAsync(cos_sin_cache.p, t.data(), t.size() * sizeof(float),
+                        cudaMemcpyHostToDevice, s),
+        "rope table upload");
+    ckc(cudaStreamSynchronize(s), "rope table upload");
+}
+
+struct Qwen3DecoderLayer {  // qwen3.h:11-30
+    RMSNorm input_layernorm, post_attention_layernorm;
+    Linear qkv_proj, o_proj, down_proj;
+    GateUpSwiGLU gate_up_proj;  // gate_up_proj + swiglu
+    Attention attn;
+    DevBuf q_norm, k_norm;      // Qwen3 per-head norms (absent in the reference, D14)
+    DevBuf k_pool, v_pool;      // [num_slots, hkv * D] bf16
+};
+
+struct Model {
+    msgl_model_config cfg{};
+    int hq = 0, hkv = 0, inter = 0, vocab_l = 0;  // this rank's shard
+    int kv_head0 = 0;                              // first global kv head held by this rank
+    std::vector<Qwen3DecoderLayer> layers;
+    DevBuf embed;        // [V, H]
+    RMSNorm norm;        // final norm
+    Linear lm_head;      // [V_l, H]
+    RotaryEmbedding rope;
+    int64_t num_slots = 0;
+    int page_size = 16;
+    int layers_run = -1;  // debug: run only the first n layers
+
+    // workspace (allocated once)
+    DevBuf x, residual, qkv, q, attn_out, act, x_last, res_last, packed, gemm_ws, attn_ws;
+    Scratch scratch;
+    // device copies of a host batch (msgl_model_step_host)
+    DevBuf st_ids, st_pos, st_slots, st_pt, st_seq, st_indptr, st_last, st_next;
+    int st_max_pages = 0;
+    // captured decode graphs, keyed by every pointer and shape field of the step
+    struct GraphEntry {
+        std::vector<int64_t> key;
+        cudaGraphExec_t exec = nullptr;
+    };
+    std::vector<GraphEntry> graphs;
+
+    ~Model() {
+        for (auto& g : graphs)
+            if (g.exec) cudaGraphExecDestroy(g.exec);
+    }
+
+    int64_t weight_bytes() const {
+        int64_t b = embed.bytes + norm.weight.bytes + lm_head.weight.bytes;
+        for (auto& L : layers)
+            b += L.input_layernorm.weight.bytes + L.post_attention_layernorm.weight.bytes +
+                 L.qkv_proj.weight.bytes + L.o_proj.weight.bytes + L.down_proj.weight.bytes +
+                 L.gate_up_proj.weight_packed.bytes + L.q_norm.bytes + L.k_norm.bytes;
+        return b;
+    }
+};
+
+static void validate(const msgl_model_config& c) {
+    auto bad = [](const char* m) { throw Fail(MSGL_ERR_INVALID_ARG, m); };
+    if (c.num_layers <= 0 || c.hidden <= 0 || c.vocab <= 0 || c.max_tokens <= 0 || c.max_reqs <= 0)
+        bad("model: non-positive size");
+    if (c.head_dim != 128) throw Fail(MSGL_ERR_UNSUPPORTED_SHAPE, "model: head_dim must be 128");
+    if (c.num_kv_heads <= 0 || c.num_q_heads % c.num_kv_heads) bad("model: Hq % Hkv");
+    if (c.tp_size < 1 || c.tp_rank < 0 || c.tp_rank >= c.tp_size) bad("model: tp rank/size");
+    if (c.num_q_heads % c.tp_size) bad("model: Hq % tp");
+    if (c.num_experts > 0) throw Fail(MSGL_ERR_UNSUPPORTED_SHAPE, "model: MoE layers not built in this executor");
+    if (c.inter % c.tp_size || (c.inter / c.tp_size) % 16) bad("model: inter / tp must be a multiple of 16");
+    if (c.tp_size > 1) throw Fail(MSGL_ERR_UNSUPPORTED_SHAPE, "model: tensor parallel needs msgl_tp (not built yet)");
+}
+
+static void create(Model& m, const msgl_model_config& c) {
+    validate(c);
+    m.cfg = c;
+    const int tp = c.tp_size, D = c.head_dim, H = c.hidden;
+    m.hq = c.num_q_heads / tp;
+    m.hkv = c.num_kv_heads >= tp ? c.num_kv_heads / tp : 1;
+    m.kv_head0 = c.num_kv_heads >= tp ? c.tp_rank * m.hkv
+                                      : (c.tp_rank * m.hq) / (c.num_q_heads / c.num_kv_heads);
+    m.inter = c.inter / tp;
+    m.vocab_l = c.vocab;  // vocab-parallel lm_head arrives with TP
+    m.layers.resize(c.num_layers);
+    cudaStream_t s = nullptr;
+    for (auto& L : m.layers) {
+        L.input_layernorm = RMSNorm(H, c.eps);
+        L.post_attention_layernorm = RMSNorm(H, c.eps);
+        L.qkv_proj = Linear(H, (m.hq + 2 * m.hkv) * D);
+        L.o_proj = Linear(m.hq * D, H);
+        L.gate_up_proj = GateUpSwiGLU(H, m.inter);
+        L.down_proj = Linear(m.inter, H);
+        L.attn = Attention(m.hq, m.hkv, D, c.eps);
+        L.input_layernorm.weight.alloc(H * 2);
+        L.post_attention_layernorm.weight.alloc(H * 2);
+        L.qkv_proj.weight.alloc(static_cast<size_t>(L.qkv_proj.out_features()) * H * 2);
+        L.o_proj.weight.alloc(static_cast<size_t>(H) * m.hq * D * 2);
+        L.gate_up_proj.weight_packed.alloc(static_cast<size_t>(2 * m.inter) * H * 2);
+        L.down_proj.weight.alloc(static_cast<size_t>(H) * m.inter * 2);
+        L.q_norm.alloc(D * 2);
+        L.k_norm.alloc(D * 2);
+    }
+    m.embed.alloc(static_cast<size_t>(c.vocab) * H * 2);
+    m.norm = RMSNorm(H, c.eps);
+    m.norm.weight.alloc(H * 2);
+    m.lm_head = Linear(H, m.vocab_l);
+    m.lm_head.weight.alloc(static_cast<size_t>(m.vocab_l) * H * 2);
+    m.rope.init(D, c.max_position, c.rope_base, s);
+
+    // workspace
+    const size_t T = c.max_tokens, B = c.max_reqs;
+    m.x.alloc(T * H * 2);
+    m.residual.alloc(T * H * 4);
+    m.qkv.alloc(T * (m.hq + 2 * m.hkv) * D * 2);
+    m.q.alloc(T * m.hq * D * 2);
+    m.attn_out.alloc(T * m.hq * D * 2);
+    m.act.alloc(T * std::max(m.inter, H) * 2);
+    m.x_last.alloc(B * H * 2);
+    m.res_last.alloc(B * H * 4);
+    m.packed.alloc(B * 8);
+    // split-K workspaces: the largest any step size up to capacity can ask for
+    size_t gws = 0;
+    const auto& L0 = m.layers[0];
+    for (int t = 1; t <= static_cast<int>(T); ++t) {
+        gws = std::max(gws, L0.qkv_proj.workspace(t));
+        gws = std::max(gws, L0.o_proj.workspace(t));
+        gws = std::max(gws, L0.gate_up_proj.workspace(t));
+        gws = std::max(gws, L0.down_proj.workspace(t));
+        if (t <= static_cast<int>(B)) gws = std::max(gws, m.lm_head.workspace(t));
+    }
+    m.gemm_ws.alloc(std::max<size_t>(gws, 256));
+    ckc(cudaMemset(m.gemm_ws.p, 0, m.gemm_ws.bytes), "gemm workspace");
+    size_t aws = 0;
+    for (int b = 1; b <= static_cast<int>(B); ++b)
+        aws = std::max(aws, msgl_paged_attention_workspace_size(b, c.max_position, m.hq, m.hkv, D));
+    m.attn_ws.alloc(std::max<size_t>(aws, 256));
+    ckc(cudaMemset(m.attn_ws.p, 0, m.attn_ws.bytes), "attention workspace");
+    m.scratch = Scratch{m.gemm_ws.p, m.gemm_ws.bytes, m.attn_ws.p, m.attn_ws.bytes};
+    m.st_max_pages = (c.max_position + 15) / 16;
+    m.st_ids.alloc(T * 4);
+    m.st_pos.alloc(T * 4);
+    m.st_slots.alloc(T * 4);
+    m.st_pt.alloc(B * m.st_max_pages * 4);
+    m.st_seq.alloc(B * 4);
+    m.st_indptr.alloc((B + 1) * 4);
+    m.st_last.alloc(B * 4);
+    m.st_next.alloc(B * 4);
+}
+
+// ----------------------------------------------------------------------------- weights
+static void fill(DevBuf& b, uint64_t seed, uint64_t id, float mean, float std, cudaStream_t s) {
+    ck(msgl_fill_normal_bf16(b.p, static_cast<int64_t>(b.bytes / 2), seed, id, mean, std, s),
+       "random_init");
+}
+
+static void random_init(Model& m, uint64_t seed, float std, cudaStream_t s) {
+    uint64_t id = static_cast<uint64_t>(m.cfg.tp_rank) << 40;
+    fill(m.embed, seed, id++, 0.f, std, s);
+    for (auto& L : m.layers) {
+        fill(L.input_layernorm.weight, seed, id++, 1.f, 0.f, s);
+        fill(L.qkv_proj.weight, seed, id++, 0.f, std, s);
+        fill(L.q_norm, seed, id++, 1.f, 0.f, s);
+        fill(L.k_norm, seed, id++, 1.f, 0.f, s);
+        fill(L.o_proj.weight, seed, id++, 0.f, std, s);
+        fill(L.post_attention_layernorm.weight, seed, id++, 1.f, 0.f, s);
+        fill(L.gate_up_proj.weight_packed, seed, id++, 0.f, std, s);  // i.i.d.: packing is moot
+        fill(L.down_proj.weight, seed, id++, 0.f, std, s);
+    }
+    fill(m.norm.weight, seed, id++, 1.f, 0.f, s);
+    fill(m.lm_head.weight, seed, id++, 0.f, std, s);
+    ckc(cudaStreamSynchronize(s), "random_init");
+}
+
+// Copy rows [r0, r0 + nrows) x cols [c0, c0 + ncols) of a host [rows, cols] bf16 matrix.
+static void upload_block(void* dst, const bf16_t* src, int64_t cols, int64_t r0, int64_t nrows,
+                         int64_t c0, int64_t ncols, cudaStream_t s) {
+    ckc(cudaMemcpy2DAsync(dst, ncols * 2, src + r0 * cols + c0, cols * 2, ncols * 2, nrows,
+                          cudaMemcpyHostToDevice, s),
+        "set_weight upload");
+}
+
+static void set_weight(Model& m, const std::string& name, const bf16_t* h, int64_t numel,
+                       cudaStream_t s) {
+    const auto& c = m.cfg;
+    const int64_t H = c.hidden, D = c.head_dim, tp = c.tp_size, r = c.tp_rank;
+    auto need = [&](int64_t n) {
+        if (numel != n) throw Fail(MSGL_ERR_INVALID_ARG, "set_weight " + name + ": numel mismatch");
+    };
+    if (name == "embed") { need(c.vocab * H); upload_block(m.embed.p, h, H, 0, c.vocab, 0, H, s); }
+    else if (name == "norm") { need(H); upload_block(m.norm.weight.p, h, H, 0, 1, 0, H, s); }
+    else if (name == "lm_head") { need(c.vocab * H); upload_block(m.lm_head.weight.p, h, H, 0, m.vocab_l, 0, H, s); }
+    else if (name.rfind("layers.", 0) == 0) {
+        size_t dot = name.find('.', 7);
+        int l = std::stoi(name.substr(7, dot - 7));
+        if (l < 0 || l >= c.num_layers) throw Fail(MSGL_ERR_INVALID_ARG, "set_weight: layer");
+        std::string f = name.substr(dot + 1);
+        auto& L = m.layers[l];
+        const int64_t hq_g = c.num_q_heads, hkv_g = c.num_kv_heads, I = c.inter;
+        if (f == "input_ln") { need(H); upload_block(L.input_layernorm.weight.p, h, H, 0, 1, 0, H, s); }
+        else if (f == "post_ln") { need(H); upload_block(L.post_attention_layernorm.weight.p, h, H, 0, 1, 0, H, s); }
+        else if (f == "q_norm") { need(D); upload_block(L.q_norm.p, h, D, 0, 1, 0, D, s); }
+        else if (f == "k_norm") { need(D); upload_block(L.k_norm.p, h, D, 0, 1, 0, D, s); }
+        else if (f == "qkv") {  // rows q | k | v; keep this rank's q heads and kv heads
+            need((hq_g + 2 * hkv_g) * D * H);
+            char* dst = static_cast<char*>(L.qkv_proj.weight.p);
+            upload_block(dst, h, H, r * m.hq * D, m.hq * D, 0, H, s);
+            dst += m.hq * D * H * 2;
+            upload_block(dst, h, H, (hq_g + m.kv_head0) * D, m.hkv * D, 0, H, s);
+            dst += m.hkv * D * H * 2;
+            upload_block(dst, h, H, (hq_g + hkv_g + m.kv_head0) * D, m.hkv * D, 0, H, s);
+        } else if (f == "o") {  // [H, Hq D]: column shard
+            need(H * hq_g * D);
+            upload_block(L.o_proj.weight.p, h, hq_g * D, 0, H, r * m.hq * D, m.hq * D, s);
+        } else if (f == "gate_up") {  // rows gate | up: this rank's I/tp of each, then pack
+            need(2 * I * H);
+            DevBuf tmp;
+            tmp.alloc(static_cast<size_t>(2 * m.inter) * H * 2);
+            upload_block(tmp.p, h, H, r * m.inter, m.inter, 0, H, s);
+            upload_block(static_cast<char*>(tmp.p) + static_cast<size_t>(m.inter) * H * 2, h, H,
+                         I + r * m.inter, m.inter, 0, H, s);
+            ck(msgl_pack_gate_up(tmp.p, L.gate_up_proj.weight_packed.p, m.inter, H, s), "pack_gate_up");
+            ckc(cudaStreamSynchronize(s), "set_weight");
+        } else if (f == "down") {  // [H, I]: column shard
+            need(H * I);
+            upload_block(L.down_proj.weight.p, h, I, 0, H, r * m.inter, m.inter, s);
+        } else {
+            throw Fail(MSGL_ERR_INVALID_ARG, "set_weight: unknown tensor " + name);
+        }
+    } else {
+        throw Fail(MSGL_ERR_INVALID_ARG, "set_weight: unknown tensor " + name);
+    }
+    ckc(cudaStreamSynchronize(s), "set_weight");
+}
+
+static void alloc_kv(Model& m, int num_pages, int page_size, cudaStream_t s) {
+    if (page_size != 16) throw Fail(MSGL_ERR_UNSUPPORTED_SHAPE, "alloc_kv: page_size must be 16");
+    if (num_pages <= 0) throw Fail(MSGL_ERR_INVALID_ARG, "alloc_kv: num_pages");
+    m.page_size = page_size;
+    m.num_slots = static_cast<int64_t>(num_pages) * page_size;
+    const size_t bytes = static_cast<size_t>(m.num_slots) * m.hkv * m.cfg.head_dim * 2;
+    for (auto& L : m.layers) {
+        L.k_pool.alloc(bytes);
+        L.v_pool.alloc(bytes);
+        ckc(cudaMemsetAsync(L.k_pool.p, 0, bytes, s), "alloc_kv");
+        ckc(cudaMemsetAsync(L.v_pool.p, 0, bytes, s), "alloc_kv");
+    }
+    ckc(cudaStreamSynchronize(s), "alloc_kv");
+}
+
+// ----------------------------------------------------------------------------- forward
+// Qwen3ForCausalLM::forward (qwen3.cpp:168-180) with Qwen3DecoderLayer::forward (:16-83) inlined.
+static void forward(Model& m, const msgl_batch& b, int* next_tokens, float* logits,
+                    cudaStream_t s) {
+    const auto& c = m.cfg;
+    if (b.num_tokens <= 0 || b.num_tokens > c.max_tokens || b.num_reqs <= 0 ||
+        b.num_reqs > c.max_reqs)
+        throw Fail(MSGL_ERR_INVALID_ARG, "forward: batch exceeds the executor's capacity");
+    if (b.is_decode && b.num_tokens != b.num_reqs)
+        throw Fail(MSGL_ERR_INVALID_ARG, "forward: decode needs one token per request");
+    if (b.max_seq_len > c.max_position)
+        throw Fail(MSGL_ERR_INVALID_ARG, "forward: max_seq_len exceeds max_position");
+    if (m.num_slots == 0) throw Fail(MSGL_ERR_INVALID_ARG, "forward: KV pools not allocated");
+    const int T = b.num_tokens, H = c.hidden;
+    auto* x = m.x.as<bf16_t>();
+    float* res = m.residual.as<float>();
+    const int nl = m.layers_run >= 0 ? std::min(m.layers_run, c.num_layers) : c.num_layers;
+
+    // embed_tokens + layer 0's input_layernorm (residual aliasing first call, layer.cpp:80-84)
+    ck(msgl_embed_rmsnorm(m.embed.p, b.input_ids, T, c.vocab, H, m.layers[0].input_layernorm.weight.p,
+                          c.eps, x, res, s),
+       "embed_tokens");
+    for (int l = 0; l < nl; ++l) {
+        auto& L = m.layers[l];
+        if (l > 0) L.input_layernorm.forward_fused_add(x, res, T, false, s);  // qwen3.cpp:19
+        L.qkv_proj.forward(x, m.qkv.as<bf16_t>(), T, m.scratch, s);          // :22
+        L.attn.prepare(m.qkv.as<bf16_t>(), m.q.as<bf16_t>(), L.k_pool.p, L.v_pool.p, m.num_slots,
+                       b.positions, b.slot_mapping, m.rope, L.q_norm.p, L.k_norm.p, T, s);  // :28-48
+        L.attn.forward(m.q.as<bf16_t>(), L.k_pool.p, L.v_pool.p, m.num_slots, b,
+                       m.attn_out.as<bf16_t>(), m.scratch, s);                // :51-52
+        L.o_proj.forward(m.attn_out.as<bf16_t>(), x, T, m.scratch, s);       // :55
+        L.post_attention_layernorm.forward_fused_add(x, res, T, false, s);   // :57
+        L.gate_up_proj.forward(x, m.act.as<bf16_t>(), T, m.scratch, s);      // :60-79
+        L.down_proj.forward(m.act.as<bf16_t>(), x, T, m.scratch, s);         // :80
+    }
+    // final norm on each request's last row (qwen3.cpp:177, sampling row of D10), lm_head +
+    // greedy argmax (scheduler.cpp:117-124)
+    const int B = b.num_reqs;
+    bf16_t* xl = x;
+    float* rl = res;
+    if (!b.is_decode) {
+        ck(msgl_launch_index_gather(x, b.last_idx, m.x_last.p, H, B, T, MSGL_BF16, s), "gather x");
+        ck(msgl_launch_index_gather(res, b.last_idx, m.res_last.p, H, B, T, MSGL_F32, s), "gather res");
+        xl = m.x_last.as<bf16_t>();
+        rl = m.res_last.as<float>();
+    }
+    m.norm.forward_fused_add(xl, rl, B, false, s);
+    ck(msgl_lm_head_argmax(xl, m.lm_head.weight.p, B, m.vocab_l, H,
+                           m.packed.as<unsigned long long>(), next_tokens, m.scratch.gemm_ws,
+                           m.scratch.gemm_ws_bytes, s),
+       "lm_head");
+    if (logits)
+        ck(msgl_gemm_bf16(xl, m.lm_head.weight.p, logits, B, m.vocab_l, H, MSGL_F32,
+                          m.scratch.gemm_ws, m.scratch.gemm_ws_bytes, s),
+           "lm_head logits");
+}
+
+static std::vector<int64_t> graph_key(const msgl_batch& b, const int* next, const float* logits) {
+    return {b.num_tokens, b.num_reqs, b.is_decode, b.max_pages, b.max_seq_len, b.max_q_len,
+            reinterpret_cast<int64_t>(b.input_ids), reinterpret_cast<int64_t>(b.positions),
+            reinterpret_cast<int64_t>(b.slot_mapping), reinterpret_cast<int64_t>(b.page_table),
+            reinterpret_cast<int64_t>(b.seq_lens), reinterpret_cast<int64_t>(b.q_indptr),
+            reinterpret_cast<int64_t>(b.last_idx), reinterpret_cast<int64_t>(next),
+            reinterpret_cast<int64_t>(logits)};
+}
+
+static void run(Model& m, const msgl_batch& b, int* next, float* logits, int flags,
+                cudaStream_t s) {
+    if (!(flags & MSGL_FWD_GRAPH)) {
+        forward(m, b, next, logits, s);
+        return;
+    }
+    if (s == nullptr) throw Fail(MSGL_ERR_INVALID_ARG, "graph step needs a non-default stream");
+    auto key = graph_key(b, next, logits);
+    for (auto& g : m.graphs)
+        if (g.key == key) {
+            ckc(cudaGraphLaunch(g.exec, s), "cudaGraphLaunch");
+            return;
+        }
+    // one eager pass first: first-use work (module loading, attribute setting) stays out of
+    // the capture
+    forward(m, b, next, logits, s);
+    cudaGraph_t graph = nullptr;
+    ckc(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "begin capture");
+    try {
+        forward(m, b, next, logits, s);
+    } catch (...) {
+        cudaStreamEndCapture(s, &graph);
+        if (graph) cudaGraphDestroy(graph);
+        throw;
+    }
+    ckc(cudaStreamEndCapture(s, &graph), "end capture");
+    cudaGraphExec_t exec = nullptr;
+    cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    ckc(e, "cudaGraphInstantiate");
+    m.graphs.push_back({key, exec});
+    ckc(cudaGraphLaunch(exec, s), "cudaGraphLaunch");
+}
+
+static void step_host(Model& m, const msgl_batch& hb, int* host_next, int flags, cudaStream_t s) {
+    const int T = hb.num_tokens, B = hb.num_reqs;
+    if (T <= 0 || T > m.cfg.max_tokens || B <= 0 || B > m.cfg.max_reqs)
+        throw Fail(MSGL_ERR_INVALID_ARG, "step_host: batch exceeds the executor's capacity");
+    if (hb.max_pages <= 0 || hb.max_pages > m.st_max_pages)
+        throw Fail(MSGL_ERR_INVALID_ARG, "step_host: page-table width exceeds max_position / 16");
+    auto h2d = [&](DevBuf& d, const int* h, size_t n) {
+        if (!h) throw Fail(MSGL_ERR_INVALID_ARG, "step_host: null host array");
+        ckc(cudaMemcpyAsync(d.p, h, n * 4, cudaMemcpyHostToDevice, s), "step_host H2D");
+    };
+    h2d(m.st_ids, hb.input_ids, T);
+    h2d(m.st_pos, hb.positions, T);
+    h2d(m.st_slots, hb.slot_mapping, T);
+    h2d(m.st_pt, hb.page_table, static_cast<size_t>(B) * hb.max_pages);
+    h2d(m.st_seq, hb.seq_lens, B);
+    h2d(m.st_indptr, hb.q_indptr, B + 1);
+    h2d(m.st_last, hb.last_idx, B);
+    msgl_batch db = hb;
+    db.input_ids = m.st_ids.as<int>();
+    db.positions = m.st_pos.as<int>();
+    db.slot_mapping = m.st_slots.as<int>();
+    db.page_table = m.st_pt.as<int>();
+    db.seq_lens = m.st_seq.as<int>();
+    db.q_indptr = m.st_indptr.as<int>();
+    db.last_idx = m.st_last.as<int>();
+    run(m, db, m.st_next.as<int>(), nullptr, hb.is_decode ? flags : 0, s);
+    ckc(cudaMemcpyAsync(host_next, m.st_next.p, B * 4, cudaMemcpyDeviceToHost, s), "step_host D2H");
+    ckc(cudaStreamSynchronize(s), "step_host sync");
+}
+
+}  // namespace engine
+}  // namespace msgl
+
+using namespace msgl::engine;
+
+struct msgl_model {
+    Model m;
+};
+
+namespace msgl {
+int set_error(int code, const char* msg);
+}
+
+template <typename F>
+static int guarded(F&& f) {
+    try {
+        f();
+        return MSGL_OK;
+    } catch (const Fail& e) {
+        return msgl::set_error(e.code, e.what());
+    } catch (const std::exception& e) {
+        return msgl::set_error(MSGL_ERR_INVALID_ARG, e.what());
+    }
+}
+
+extern "C" {
+
+int msgl_model_create(const msgl_model_config* cfg, msgl_model** out) {
+    if (!cfg || !out) return msgl::set_error(MSGL_ERR_INVALID_ARG, "model_create: null");
+    *out = nullptr;
+    auto* mm = new msgl_model();
+    int rc = guarded([&] { create(mm->m, *cfg); });
+    if (rc) {
+        delete mm;
+        return rc;
+    }
+    *out = mm;
+    return MSGL_OK;
+}
+
+int msgl_model_destroy(msgl_model* m) {
+    delete m;
+    return MSGL_OK;
+}
+
+int msgl_model_random_init(msgl_model* m, uint64_t seed, float std, msgl_stream_t stream) {
+    if (!m) return msgl::set_error(MSGL_ERR_INVALID_ARG, "null model");
+    return guarded([&] { random_init(m->m, seed, std, stream); });
+}
+
+int msgl_model_set_weight(msgl_model* m, const char* name, const uint16_t* host_bf16,
+                          int64_t numel, msgl_stream_t stream) {
+    if (!m || !name || !host_bf16) return msgl::set_error(MSGL_ERR_INVALID_ARG, "set_weight: null");
+    return guarded([&] { set_weight(m->m, name, host_bf16, numel, stream); });
+}
+
+int64_t msgl_model_weight_bytes(const msgl_model* m) { return m ? m->m.weight_bytes() : 0; }
+
+int msgl_model_alloc_kv(msgl_model* m, int num_pages, int page_size, msgl_stream_t stream) {
+    if (!m) return msgl::set_error(MSGL_ERR_INVALID_ARG, "null model");
+    return guarded([&] { alloc_kv(m->m, num_pages, page_size, stream); });
+}
+
+int msgl_model_kv_pool(msgl_model* m, int layer, void** k_pool, void** v_pool, int64_t* num_slots) {
+    if (!m || layer < 0 || layer >= m->m.cfg.num_layers)
+        return msgl::set_error(MSGL_ERR_INVALID_ARG, "kv_pool: layer");
+    if (k_pool) *k_pool = m->m.layers[layer].k_pool.p;
+    if (v_pool) *v_pool = m->m.layers[layer].v_pool.p;
+    if (num_slots) *num_slots = m->m.num_slots;
+    return MSGL_OK;
+}
+
+int msgl_model_forward(msgl_model* m, const msgl_batch* batch, int* next_tokens, float* logits,
+                       int flags, msgl_stream_t stream) {
+    if (!m || !batch || !next_tokens) return msgl::set_error(MSGL_ERR_INVALID_ARG, "forward: null");
+    return guarded([&] { run(m->m, *batch, next_tokens, logits, flags, stream); });
+}
+
+int msgl_model_step_host(msgl_model* m, const msgl_batch* host_batch, int* host_next_tokens,
+                         int flags, msgl_stream_t stream) {
+    if (!m || !host_batch || !host_next_tokens)
+        return msgl::set_error(MSGL_ERR_INVALID_ARG, "step_host: null");
+    return guarded([&] { step_host(m->m, *host_batch, host_next_tokens, flags, stream); });
+}
+
+int msgl_model_debug_hidden(msgl_model* m, void** x, float** residual) {
+    if (!m) return msgl::set_error(MSGL_ERR_INVALID_ARG, "null model");
+    if (x) *x = m->m.x.p;
+    if (residual) *residual = m->m.residual.as<float>();
+    return MSGL_OK;
+}
+
+int msgl_model_set_num_layers_run(msgl_model* m, int n) {
+    if (!m) return msgl::set_error(MSGL_ERR_INVALID_ARG, "null model");
+    m->m.layers_run = n;
+    return MSGL_OK;
+}
+
+}  // extern "C"

@@ -34,6 +34,24 @@ SIGNATURES = {
     "msgl_lm_head_argmax": (I, [P, P, I, I, I, P, P, P, SZ, P]),
     "msgl_argmax": (I, [P, I, I, I, P, P]),
     "msgl_fill_normal_bf16": (I, [P, I64, U64, U64, F, F, P]),
+    "msgl_moe_route_topk": (I, [P, I, I, I, I, P, P, P]),
+    "msgl_moe_permute": (I, [P, I, I, I, P, P, P, P]),
+    "msgl_grouped_gemm_workspace_size": (SZ, [I, I]),
+    "msgl_grouped_gemm_bf16": (I, [P, P, P, P, I, I, I, I, P, SZ, P]),
+    "msgl_grouped_gemm_gate_up_silu": (I, [P, P, P, P, I, I, I, I, P, SZ, P]),
+    "msgl_moe_combine": (I, [P, P, P, I, I, I, P, P]),
+    # executor (msgl_engine.h)
+    "msgl_model_create": (I, [P, P]),
+    "msgl_model_destroy": (I, [P]),
+    "msgl_model_random_init": (I, [P, U64, F, P]),
+    "msgl_model_set_weight": (I, [P, C.c_char_p, P, I64, P]),
+    "msgl_model_weight_bytes": (I64, [P]),
+    "msgl_model_alloc_kv": (I, [P, I, I, P]),
+    "msgl_model_kv_pool": (I, [P, I, P, P, P]),
+    "msgl_model_forward": (I, [P, P, P, P, I, P]),
+    "msgl_model_step_host": (I, [P, P, P, I, P]),
+    "msgl_model_debug_hidden": (I, [P, P, P]),
+    "msgl_model_set_num_layers_run": (I, [P, I]),
 }
 
 _LIB = None

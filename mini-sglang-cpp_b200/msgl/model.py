@@ -1,0 +1,208 @@
+"""Python handle on the C++ executor (include/msgl_engine.h) and host-side batch building.
+
+``PagePool`` mirrors KVCachePool's free list (src/cache/kvcache.cpp:16-32: pages handed out
+LIFO from [0..N-1], so N-1 first); ``BatchBuilder`` turns per-request state into the step
+metadata of Scheduler::step (src/scheduler/scheduler.cpp:83-106: prefill positions
+cached_len..device_len-1, decode position device_len-1), allocating ceil(len / page_size)
+pages per request (the reference allocates one page per token, D12).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from ._lib import check, lib
+
+P, I, I64, F, U64 = C.c_void_p, C.c_int, C.c_int64, C.c_float, C.c_uint64
+
+
+class ModelConfig(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("num_layers", "hidden", "num_q_heads", "num_kv_heads",
+                                        "head_dim", "inter", "vocab", "num_experts", "top_k",
+                                        "moe_inter", "norm_topk")] + \
+               [("eps", C.c_float), ("rope_base", C.c_float)] + \
+               [(n, C.c_int) for n in ("max_position", "max_tokens", "max_reqs", "tp_rank", "tp_size")]
+
+
+class BatchT(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("num_tokens", "num_reqs", "is_decode", "max_pages",
+                                        "max_seq_len", "max_q_len")] + \
+               [(n, C.c_void_p) for n in ("input_ids", "positions", "slot_mapping", "page_table",
+                                           "seq_lens", "q_indptr", "last_idx")]
+
+
+def _engine():
+    return lib()
+
+
+def _s():
+    return torch.cuda.current_stream().cuda_stream
+
+
+class _CudaArray:
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"data": (ptr, False), "shape": tuple(shape),
+                                         "typestr": typestr, "version": 3}
+
+
+def device_view(ptr: int, shape, dtype) -> torch.Tensor:
+    """A torch view (no copy) of executor-owned device memory."""
+    if dtype == torch.bfloat16:
+        return torch.as_tensor(_CudaArray(ptr, shape, "<i2"), device="cuda").view(torch.bfloat16)
+    ts = {torch.float32: "<f4", torch.int32: "<i4"}[dtype]
+    return torch.as_tensor(_CudaArray(ptr, shape, ts), device="cuda")
+
+
+# ---------------------------------------------------------------------------- host metadata
+class PagePool:
+    """KVCachePool free list (kvcache.cpp:16-32): LIFO from [0..N-1]."""
+
+    def __init__(self, num_pages: int):
+        self.free = list(range(num_pages))
+
+    def allocate(self) -> int:
+        if not self.free:
+            raise RuntimeError("KV Cache OOM: No free pages available")
+        return self.free.pop()
+
+    def release(self, page: int) -> None:
+        self.free.append(page)
+
+    def num_free(self) -> int:
+        return len(self.free)
+
+
+@dataclass
+class Request:
+    """The Req fields the step needs (include/minisgl/core/types.h:29-60)."""
+    input_ids: list
+    cached_len: int = 0
+    pages: list = field(default_factory=list)
+
+    @property
+    def device_len(self) -> int:
+        return len(self.input_ids)
+
+
+@dataclass
+class StepBatch:
+    """Device tensors of one step plus the msgl_batch struct pointing at them."""
+    tensors: dict
+    struct: BatchT
+    num_reqs: int
+
+
+class BatchBuilder:
+    def __init__(self, pool: PagePool, page_size: int = 16):
+        self.pool, self.P = pool, page_size
+
+    def _ensure_pages(self, req: Request, upto_len: int):
+        need = (upto_len + self.P - 1) // self.P
+        while len(req.pages) < need:
+            req.pages.append(self.pool.allocate())
+
+    def build(self, reqs: list, decode: bool, device="cuda", max_pages: int | None = None) -> StepBatch:
+        ids, pos, slots, seq, qlens = [], [], [], [], []
+        for r in reqs:
+            if decode:  # scheduler.cpp:93-95
+                toks = [(r.input_ids[-1], r.device_len - 1)]
+            else:       # scheduler.cpp:88-92
+                toks = [(r.input_ids[i], i) for i in range(r.cached_len, r.device_len)]
+            self._ensure_pages(r, r.device_len)
+            for t, p in toks:
+                ids.append(t)
+                pos.append(p)
+                slots.append(r.pages[p // self.P] * self.P + p % self.P)
+            seq.append(r.device_len)
+            qlens.append(len(toks))
+        width = max_pages or max(len(r.pages) for r in reqs)
+        pt = np.zeros((len(reqs), width), np.int32)
+        for i, r in enumerate(reqs):
+            pt[i, : len(r.pages)] = r.pages
+        indptr = np.concatenate([[0], np.cumsum(qlens)]).astype(np.int32)
+        host = dict(input_ids=np.array(ids, np.int32), positions=np.array(pos, np.int32),
+                    slot_mapping=np.array(slots, np.int32), page_table=pt,
+                    seq_lens=np.array(seq, np.int32), q_indptr=indptr,
+                    last_idx=(indptr[1:] - 1).astype(np.int32))
+        return make_step(host, decode, device, max(seq), max(qlens))
+
+
+def make_step(host: dict, decode: bool, device, max_seq_len: int, max_q_len: int) -> StepBatch:
+    t = {k: torch.from_numpy(np.ascontiguousarray(v)).to(device) for k, v in host.items()}
+    B = t["seq_lens"].numel()
+    st = BatchT(t["input_ids"].numel(), B, int(decode), t["page_table"].shape[1], max_seq_len,
+                max_q_len, *[t[k].data_ptr() for k in ("input_ids", "positions", "slot_mapping",
+                                                        "page_table", "seq_lens", "q_indptr",
+                                                        "last_idx")])
+    return StepBatch(t, st, B)
+
+
+# ---------------------------------------------------------------------------- executor
+def to_bf16_bits(a: np.ndarray) -> np.ndarray:
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    u = a.view(np.uint32).astype(np.uint64)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16).reshape(a.shape)
+
+
+class Qwen3Model:
+    def __init__(self, cfg: dict, max_tokens: int, max_reqs: int, tp_rank: int = 0,
+                 tp_size: int = 1):
+        self.L = _engine()
+        self.cfg = cfg
+        c = ModelConfig(cfg["num_layers"], cfg["hidden"], cfg["num_q_heads"], cfg["num_kv_heads"],
+                        cfg.get("head_dim", 128), cfg.get("inter", 0), cfg["vocab"],
+                        cfg.get("num_experts", 0), cfg.get("top_k", 0), cfg.get("moe_inter", 0),
+                        int(cfg.get("norm_topk", True)), cfg.get("eps", 1e-6),
+                        cfg.get("rope_base", 1e6), cfg["max_position"], max_tokens, max_reqs,
+                        tp_rank, tp_size)
+        h = C.c_void_p()
+        check(self.L.msgl_model_create(C.addressof(c), C.addressof(h)))
+        self.h = h
+
+    def __del__(self):
+        h = getattr(self, "h", None)
+        if h is not None and h.value:
+            self.L.msgl_model_destroy(h)
+            self.h = None
+
+    def random_init(self, seed: int = 0, std: float = 0.02):
+        check(self.L.msgl_model_random_init(self.h, seed, std, _s()))
+
+    def set_weight(self, name: str, arr: np.ndarray):
+        bits = to_bf16_bits(arr)
+        check(self.L.msgl_model_set_weight(self.h, name.encode(), bits.ctypes.data, bits.size, _s()))
+
+    def set_weights(self, named: dict):
+        for k, v in named.items():
+            self.set_weight(k, v)
+
+    def weight_bytes(self) -> int:
+        return self.L.msgl_model_weight_bytes(self.h)
+
+    def alloc_kv(self, num_pages: int, page_size: int = 16):
+        check(self.L.msgl_model_alloc_kv(self.h, num_pages, page_size, _s()))
+
+    def kv_pool(self, layer: int):
+        k, v, n = C.c_void_p(), C.c_void_p(), C.c_int64()
+        check(self.L.msgl_model_kv_pool(self.h, layer, C.addressof(k), C.addressof(v), C.addressof(n)))
+        return k.value, v.value, n.value
+
+    def forward(self, step: StepBatch, logits: bool = False, out=None, graph: bool = False):
+        B = step.num_reqs
+        dev = step.tensors["input_ids"].device
+        nxt = out if out is not None else torch.empty(B, dtype=torch.int32, device=dev)
+        lg = torch.empty(B, self.cfg["vocab"], dtype=torch.float32, device=dev) if logits else None
+        check(self.L.msgl_model_forward(self.h, C.addressof(step.struct), nxt.data_ptr(),
+                                        None if lg is None else lg.data_ptr(), int(graph), _s()))
+        return (nxt, lg) if logits else nxt
+
+    def set_num_layers_run(self, n: int):
+        check(self.L.msgl_model_set_num_layers_run(self.h, n))
+
+    def hidden(self, T: int):
+        x, r = C.c_void_p(), C.c_void_p()
+        check(self.L.msgl_model_debug_hidden(self.h, C.addressof(x), C.addressof(r)))
+        return x.value, r.value

@@ -211,6 +211,10 @@ class RefLib:
         L.ref_radix_match.argtypes = [VP, i32p, I32, i32p, I32, C.POINTER(C.c_int)]
         L.ref_model_forward.argtypes = [I32] * 7 + [F32, F32] + [I32] * 5 + [VP, i32p, i32p, I32,
                                                                             f32p]
+        L.ref_linear_create.argtypes = [VP, I32, I32]
+        L.ref_linear_create.restype = VP
+        L.ref_linear_run.argtypes = [VP, VP, I32, VP]
+        L.ref_linear_destroy.argtypes = [VP]
 
     def embedding(self, w, ids):
         w, ids = _f(w), _i(ids)

@@ -70,6 +70,23 @@ void ref_linear(const float* x, const float* w, int num_tokens, int in_f, int ou
     copy_out(lin.forward(make_f32({num_tokens, in_f}, x)), out);
 }
 
+// A persistent Linear (weights set once, as in a loaded model) for timing Linear::forward.
+struct RefLinearHandle {
+    Linear lin;
+    int in_f;
+    RefLinearHandle(int i, int o) : lin(i, o), in_f(i) {}
+};
+void* ref_linear_create(const float* w, int in_f, int out_f) {
+    auto* h = new RefLinearHandle(in_f, out_f);
+    h->lin.weight = make_f32({out_f, in_f}, w);
+    return h;
+}
+void ref_linear_run(void* handle, const float* x, int num_tokens, float* out) {
+    auto* h = static_cast<RefLinearHandle*>(handle);
+    copy_out(h->lin.forward(make_f32({num_tokens, h->in_f}, x)), out);
+}
+void ref_linear_destroy(void* handle) { delete static_cast<RefLinearHandle*>(handle); }
+
 // SwiGLU::forward (src/layer/layer.cpp:145-161)
 void ref_swiglu(const float* g, const float* u, int n, float* out) {
     SwiGLU s;

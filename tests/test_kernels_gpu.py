@@ -168,10 +168,9 @@ def test_paged_decode(cuda, oracle, hq, hkv, seq_lens):
     out = host(ops.paged_attention_decode(*args, workspace=ws)).reshape(B, -1)
     assert rel_l2(out, ref) < 1e-2, rel_l2(out, ref)
     assert np.abs(out - ref).max() < 3e-2
-    # the split-KV workspace is left zeroed: a second call gives identical bits
+    # the split-KV arrival counters reset themselves: reusing the workspace gives identical bits
     out2 = host(ops.paged_attention_decode(*args, workspace=ws)).reshape(B, -1)
     assert np.array_equal(out, out2)
-    assert int(ws.count_nonzero()) == 0 or ws.numel() == 256
     assert ops.device_error() == (0, 0)
 
 

@@ -1,0 +1,104 @@
+"""End-to-end parity of the executor (prefill + greedy decode) against the oracle composition.
+
+A small Qwen3 (head_dim 128, GQA, QK-norm) runs through msgl_model_forward; the oracle runs the
+same steps (same weights, same page tables / slots / positions) in fp32. Checked per step:
+final logits of each request's last token (relative L2 <= 2e-2, the bf16-vs-fp32 tolerance),
+greedy tokens identical wherever the oracle's top-1 / top-2 margin exceeds the logit error,
+and the per-layer hidden state after layer 0.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import OracleModel, bf16_round
+
+pytestmark = pytest.mark.gpu
+
+CFG = dict(num_layers=3, hidden=512, num_q_heads=8, num_kv_heads=2, head_dim=128, inter=768,
+           vocab=1000, eps=1e-6, rope_base=1e6, max_position=512, page_size=16)
+
+
+def weights(cfg, seed):
+    rng = np.random.default_rng(seed)
+    rn = lambda *s, std=1.0: bf16_round(rng.standard_normal(s).astype(np.float32) * std)
+    one = lambda n: bf16_round(1.0 + 0.1 * rng.standard_normal(n).astype(np.float32))
+    H, D, hq, hkv, I, V = (cfg[k] for k in ("hidden", "head_dim", "num_q_heads", "num_kv_heads",
+                                            "inter", "vocab"))
+    w = {"embed": rn(V, H), "norm": one(H), "lm_head": rn(V, H, std=0.05)}
+    for l in range(cfg["num_layers"]):
+        p = f"layers.{l}."
+        w.update({p + "input_ln": one(H), p + "qkv": rn((hq + 2 * hkv) * D, H, std=0.05),
+                  p + "q_norm": one(D), p + "k_norm": one(D), p + "o": rn(H, hq * D, std=0.05),
+                  p + "post_ln": one(H), p + "gate_up": rn(2 * I, H, std=0.05),
+                  p + "down": rn(H, I, std=0.05)})
+    return w
+
+
+def rel_l2(a, b):
+    return float(np.linalg.norm(a - b) / np.linalg.norm(b))
+
+
+def test_prefill_then_decode(cuda, oracle):
+    from msgl.model import BatchBuilder, PagePool, Qwen3Model, Request
+
+    w = weights(CFG, 0)
+    num_pages = 64
+    model = Qwen3Model(CFG, max_tokens=256, max_reqs=8)
+    model.set_weights(w)
+    model.alloc_kv(num_pages)
+    orc = OracleModel(oracle, CFG, w, num_slots=num_pages * 16)
+
+    rng = np.random.default_rng(1)
+    reqs = [Request(list(rng.integers(0, CFG["vocab"], n))) for n in (5, 20, 33, 16)]
+    pool = PagePool(num_pages)
+    bb = BatchBuilder(pool)
+    worst = 0.0
+    for step in range(6):
+        decode = step > 0
+        sb = bb.build(reqs, decode=decode, max_pages=8)
+        nxt, lg = model.forward(sb, logits=True)
+        torch.cuda.synchronize()
+        h = {k: v.cpu().numpy() for k, v in sb.tensors.items()}
+        ref = orc.forward(h["input_ids"], h["positions"], h["slot_mapping"], h["page_table"],
+                          h["seq_lens"], h["q_indptr"])
+        got = lg.cpu().numpy()
+        err = rel_l2(got, ref)
+        worst = max(worst, err)
+        assert err < 2e-2, (step, err)
+        ids = nxt.cpu().numpy()
+        assert np.array_equal(ids, got.argmax(axis=1))  # fused lm_head argmax == argmax of logits
+        top2 = np.sort(ref, axis=1)[:, -2:]
+        margin = top2[:, 1] - top2[:, 0]
+        tol = 4 * np.abs(got - ref).max()
+        clear = margin > tol
+        assert np.array_equal(ids[clear], ref.argmax(axis=1)[clear]), step
+        for r, t in zip(reqs, ids):  # teacher-forced on the GPU's tokens
+            r.cached_len = r.device_len
+            r.input_ids.append(int(t))
+    # page tables: LIFO allocation from the top of the pool, ceil(len/16) pages per request
+    assert reqs[0].pages == [63]
+    assert reqs[1].pages == [62, 61]
+
+
+def test_layer0_hidden_state(cuda, oracle):
+    """Hidden state after one decoder layer (x = mlp_out, residual) vs the oracle's layer."""
+    from msgl.model import BatchBuilder, PagePool, Qwen3Model, Request
+
+    w = weights(CFG, 3)
+    model = Qwen3Model(CFG, max_tokens=64, max_reqs=4)
+    model.set_weights(w)
+    model.alloc_kv(16)
+    model.set_num_layers_run(1)
+    reqs = [Request([3, 99, 512, 7, 1, 0, 999]), Request([42] * 19)]
+    sb = BatchBuilder(PagePool(16)).build(reqs, decode=False, max_pages=4)
+    model.forward(sb)
+    torch.cuda.synchronize()
+    from msgl.model import device_view
+    xp, rp = model.hidden(26)
+    T, H = 26, CFG["hidden"]
+    x = device_view(xp, (T, H), torch.bfloat16).clone()
+    orc = OracleModel(oracle, dict(CFG, num_layers=1), w, num_slots=16 * 16)
+    h = {k: v.cpu().numpy() for k, v in sb.tensors.items()}
+    _, hidden = orc.forward(h["input_ids"], h["positions"], h["slot_mapping"], h["page_table"],
+                            h["seq_lens"], h["q_indptr"], return_hidden=True)
+    assert rel_l2(x.float().cpu().numpy(), hidden[0]) < 2e-2
