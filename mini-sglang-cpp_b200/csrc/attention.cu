@@ -457,9 +457,11 @@ paged_extend_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
 }
 
 // ------------------------------------------------------------------------------ host side
+constexpr size_t kDecodeCounterBytes = 262144;  // one int per (request, kv head): 65536
+
 struct DecodePlan {
     int chunk_pages, max_chunks;
-    size_t off_ml, off_cnt, bytes;
+    size_t off_o, off_ml, off_cnt, bytes;
 };
 
 DecodePlan plan_decode(int B, int max_seq_len, int hq, int hkv) {
@@ -472,12 +474,15 @@ DecodePlan plan_decode(int B, int max_seq_len, int hq, int hkv) {
     p.chunk_pages = (max_pages_seq + chunks - 1) / chunks;
     p.max_chunks = (max_pages_seq + p.chunk_pages - 1) / p.chunk_pages;
     auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+    // Layout: arrival counters at a fixed offset (0) whatever the batch shape -- they persist
+    // (self-resetting) between calls, so no other call's partials may land on them -- then
+    // the partial O and (m, l) of every chunk.
     size_t o_bytes = up(static_cast<size_t>(B) * p.max_chunks * hq * kHd * sizeof(float));
     size_t ml_bytes = up(static_cast<size_t>(B) * p.max_chunks * hq * 2 * sizeof(float));
-    size_t cnt_bytes = up(static_cast<size_t>(B) * hkv * sizeof(int));
-    p.off_ml = o_bytes;
-    p.off_cnt = o_bytes + ml_bytes;
-    p.bytes = p.max_chunks > 1 ? o_bytes + ml_bytes + cnt_bytes : 0;
+    p.off_cnt = 0;
+    p.off_o = kDecodeCounterBytes;
+    p.off_ml = kDecodeCounterBytes + o_bytes;
+    p.bytes = p.max_chunks > 1 ? kDecodeCounterBytes + o_bytes + ml_bytes : 0;
     return p;
 }
 
@@ -529,6 +534,8 @@ int msgl_paged_attention_decode(const void* q, const void* k_pool, const void* v
     DecodePlan p = plan_decode(num_reqs, max_seq_len, num_q_heads, num_kv_heads);
     if (p.bytes > 0 && (!workspace || workspace_bytes < p.bytes))
         return set_error(MSGL_ERR_WORKSPACE, "decode: workspace too small");
+    if (p.bytes > 0 && static_cast<size_t>(num_reqs) * num_kv_heads * sizeof(int) > kDecodeCounterBytes)
+        return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "decode: num_reqs * num_kv_heads > 65536");
     if (num_reqs > 65535) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "decode: num_reqs > 65535");
     CUtensorMap tk, tv;
     rc = make_pool_maps(&tk, &tv, k_pool, v_pool, num_slots, num_kv_heads);
@@ -548,7 +555,7 @@ int msgl_paged_attention_decode(const void* q, const void* k_pool, const void* v
     paged_decode_kernel<<<grid, kThreads, smem, stream>>>(
         tk, tv, static_cast<const __nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(out), page_table,
         max_pages, seq_lens, static_cast<int>(num_slots / kPage), num_q_heads, num_kv_heads,
-        p.chunk_pages, p.max_chunks, sl2e, p.bytes ? reinterpret_cast<float*>(ws) : nullptr,
+        p.chunk_pages, p.max_chunks, sl2e, p.bytes ? reinterpret_cast<float*>(ws + p.off_o) : nullptr,
         p.bytes ? reinterpret_cast<float*>(ws + p.off_ml) : nullptr,
         p.bytes ? reinterpret_cast<int*>(ws + p.off_cnt) : nullptr, err);
     MSGL_LAUNCH_CHECK();

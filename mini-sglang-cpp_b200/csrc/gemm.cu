@@ -24,6 +24,7 @@ constexpr int kBM = 128;       // weight rows per tile (UMMA M)
 constexpr int kBK = 64;        // K per stage: one 128-byte swizzle row
 constexpr int kGemmThreads = 192;
 constexpr int kTileA = kBM * kBK * 2;  // 16 KB
+constexpr size_t kCounterBytes = 16384;  // split-K arrival counters: up to 4096 tiles
 
 enum Epi { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3 };
 
@@ -284,10 +285,14 @@ GemmPlan plan_gemm(int M, int N, int K) {
     p.kb_per_split = (kbs + splits - 1) / splits;
     p.splits = (kbs + p.kb_per_split - 1) / p.kb_per_split;
     auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+    // Workspace layout: arrival counters at a FIXED offset (0) for every GEMM shape, partial
+    // tiles after them. One workspace serves GEMMs of different shapes in stream order; a
+    // shape-dependent counter offset would let one GEMM's partials overwrite another's
+    // (self-resetting, hence persistent) counters.
     if (p.splits > 1) {
+        p.ws_cnt_off = 0;
         p.ws_part_bytes = up(static_cast<size_t>(tiles) * p.splits * p.bn * kBM * sizeof(float));
-        p.ws_cnt_off = p.ws_part_bytes;
-        p.ws_bytes = p.ws_part_bytes + up(static_cast<size_t>(tiles) * sizeof(int));
+        p.ws_bytes = kCounterBytes + p.ws_part_bytes;
     }
     return p;
 }
@@ -305,7 +310,7 @@ int launch_bn(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& tx, v
     uint8_t* w8 = static_cast<uint8_t*>(ws);
     gemm_kernel<BN, EPI, GROUPED><<<grid, kGemmThreads, Cfg::kSmem, stream>>>(
         tw, tx, y, amax, M, N, K, p.kb_per_split, p.splits,
-        p.splits > 1 ? reinterpret_cast<float*>(w8) : nullptr,
+        p.splits > 1 ? reinterpret_cast<float*>(w8 + kCounterBytes) : nullptr,
         p.splits > 1 ? reinterpret_cast<int*>(w8 + p.ws_cnt_off) : nullptr, grp, err);
     MSGL_LAUNCH_CHECK();
     return MSGL_OK;

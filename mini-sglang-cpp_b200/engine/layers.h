@@ -183,5 +183,58 @@ class Attention {
     float eps_ = 1e-6f;
 };
 
+// MoERouter (layer.h:83-96) + the expert loop of Qwen3MoEDecoderLayer::forward
+// (src/model/qwen3_moe.cpp:62-111): router logits GEMM (fp32 out) -> top-k -> stable
+// permutation by expert -> gather -> grouped gate_up+SwiGLU -> grouped down -> weighted combine.
+struct MoEScratch {
+    float* logits = nullptr;      // [T, E]
+    int* topk_ids = nullptr;      // [T, k]
+    float* topk_w = nullptr;      // [T, k]
+    int* offsets = nullptr;       // [E + 1]
+    int* sorted_token = nullptr;  // [T k]
+    int* pair_pos = nullptr;      // [T k]
+    bf16_t* xs = nullptr;         // [T k, H]
+    bf16_t* act = nullptr;        // [T k, inter]
+    bf16_t* ys = nullptr;         // [T k, H]
+    void* grouped_ws = nullptr;
+    size_t grouped_ws_bytes = 0;
+};
+
+class MoEExperts {
+  public:
+    MoEExperts() = default;
+    MoEExperts(int hidden, int num_experts, int top_k, int inter, bool norm_topk)
+        : hidden_(hidden), E_(num_experts), k_(top_k), inter_(inter), norm_topk_(norm_topk) {}
+    // x [T, H] (post-attention normed) -> out [T, H] (may alias x: x is consumed first)
+    void forward(const bf16_t* x, bf16_t* out, int T, const MoEScratch& ms, const Scratch& ws,
+                 cudaStream_t s) const {
+        ck(msgl_gemm_bf16(x, router.p, ms.logits, T, E_, hidden_, MSGL_F32, ws.gemm_ws,
+                          ws.gemm_ws_bytes, s), "MoERouter logits");
+        ck(msgl_moe_route_topk(ms.logits, T, E_, k_, norm_topk_ ? 1 : 0, ms.topk_ids, ms.topk_w, s),
+           "MoERouter::route");
+        ck(msgl_moe_permute(ms.topk_ids, T, k_, E_, ms.offsets, ms.sorted_token, ms.pair_pos, s),
+           "moe permute");
+        ck(msgl_launch_index_gather(x, ms.sorted_token, ms.xs, hidden_, T * k_, T, MSGL_BF16, s),
+           "moe gather");
+        ck(msgl_grouped_gemm_gate_up_silu(ms.xs, gate_up_packed.p, ms.act, ms.offsets, E_, inter_,
+                                          hidden_, T * k_, ms.grouped_ws, ms.grouped_ws_bytes, s),
+           "experts gate_up");
+        ck(msgl_grouped_gemm_bf16(ms.act, down.p, ms.ys, ms.offsets, E_, hidden_, inter_, T * k_,
+                                  ms.grouped_ws, ms.grouped_ws_bytes, s),
+           "experts down");
+        ck(msgl_moe_combine(ms.ys, ms.pair_pos, ms.topk_w, T, k_, hidden_, out, s), "moe combine");
+    }
+    DevBuf router;          // bf16 [E, H]
+    DevBuf gate_up_packed;  // bf16 [E, 2 inter, H], each expert packed by msgl_pack_gate_up
+    DevBuf down;            // bf16 [E, H, inter]
+    int num_experts() const { return E_; }
+    int top_k() const { return k_; }
+    int inter() const { return inter_; }
+
+  private:
+    int hidden_ = 0, E_ = 0, k_ = 0, inter_ = 0;
+    bool norm_topk_ = true;
+};
+
 }  // namespace engine
 }  // namespace msgl

@@ -36,6 +36,7 @@ struct Qwen3DecoderLayer {  // qwen3.h:11-30
     Linear qkv_proj, o_proj, down_proj;
     GateUpSwiGLU gate_up_proj;  // gate_up_proj + swiglu
     Attention attn;
+    MoEExperts moe;             // Qwen3MoEDecoderLayer: router + experts (qwen3_moe.h:13-30)
     DevBuf q_norm, k_norm;      // Qwen3 per-head norms (absent in the reference, D14)
     DevBuf k_pool, v_pool;      // [num_slots, hkv * D] bf16
 };
@@ -56,6 +57,9 @@ struct Model {
     // workspace (allocated once)
     DevBuf x, residual, qkv, q, attn_out, act, x_last, res_last, packed, gemm_ws, attn_ws;
     Scratch scratch;
+    DevBuf moe_logits, moe_ids, moe_w, moe_off, moe_tok, moe_pos, moe_xs, moe_act, moe_ys, moe_ws;
+    MoEScratch moe_scratch;
+    int moe_inter = 0;  // this rank's expert intermediate size
     // device copies of a host batch (msgl_model_step_host)
     DevBuf st_ids, st_pos, st_slots, st_pt, st_seq, st_indptr, st_last, st_next;
     int st_max_pages = 0;
@@ -76,7 +80,8 @@ struct Model {
         for (auto& L : layers)
             b += L.input_layernorm.weight.bytes + L.post_attention_layernorm.weight.bytes +
                  L.qkv_proj.weight.bytes + L.o_proj.weight.bytes + L.down_proj.weight.bytes +
-                 L.gate_up_proj.weight_packed.bytes + L.q_norm.bytes + L.k_norm.bytes;
+                 L.gate_up_proj.weight_packed.bytes + L.q_norm.bytes + L.k_norm.bytes +
+                 L.moe.router.bytes + L.moe.gate_up_packed.bytes + L.moe.down.bytes;
         return b;
     }
 };
@@ -89,8 +94,14 @@ static void validate(const msgl_model_config& c) {
     if (c.num_kv_heads <= 0 || c.num_q_heads % c.num_kv_heads) bad("model: Hq % Hkv");
     if (c.tp_size < 1 || c.tp_rank < 0 || c.tp_rank >= c.tp_size) bad("model: tp rank/size");
     if (c.num_q_heads % c.tp_size) bad("model: Hq % tp");
-    if (c.num_experts > 0) throw Fail(MSGL_ERR_UNSUPPORTED_SHAPE, "model: MoE layers not built in this executor");
-    if (c.inter % c.tp_size || (c.inter / c.tp_size) % 16) bad("model: inter / tp must be a multiple of 16");
+    if (c.num_experts > 0) {
+        if (c.num_experts > 256 || c.top_k <= 0 || c.top_k > 32 || c.top_k > c.num_experts)
+            throw Fail(MSGL_ERR_UNSUPPORTED_SHAPE, "model: MoE needs <= 256 experts, top_k <= 32");
+        if (c.moe_inter % c.tp_size || (c.moe_inter / c.tp_size) % 16)
+            bad("model: moe_inter / tp must be a multiple of 16");
+    } else if (c.inter % c.tp_size || (c.inter / c.tp_size) % 16) {
+        bad("model: inter / tp must be a multiple of 16");
+    }
     if (c.tp_size > 1) throw Fail(MSGL_ERR_UNSUPPORTED_SHAPE, "model: tensor parallel needs msgl_tp (not built yet)");
 }
 
@@ -102,7 +113,8 @@ static void create(Model& m, const msgl_model_config& c) {
     m.hkv = c.num_kv_heads >= tp ? c.num_kv_heads / tp : 1;
     m.kv_head0 = c.num_kv_heads >= tp ? c.tp_rank * m.hkv
                                       : (c.tp_rank * m.hq) / (c.num_q_heads / c.num_kv_heads);
-    m.inter = c.inter / tp;
+    m.inter = c.num_experts > 0 ? 0 : c.inter / tp;
+    m.moe_inter = c.num_experts > 0 ? c.moe_inter / tp : 0;
     m.vocab_l = c.vocab;  // vocab-parallel lm_head arrives with TP
     m.layers.resize(c.num_layers);
     cudaStream_t s = nullptr;
@@ -118,8 +130,16 @@ static void create(Model& m, const msgl_model_config& c) {
         L.post_attention_layernorm.weight.alloc(H * 2);
         L.qkv_proj.weight.alloc(static_cast<size_t>(L.qkv_proj.out_features()) * H * 2);
         L.o_proj.weight.alloc(static_cast<size_t>(H) * m.hq * D * 2);
-        L.gate_up_proj.weight_packed.alloc(static_cast<size_t>(2 * m.inter) * H * 2);
-        L.down_proj.weight.alloc(static_cast<size_t>(H) * m.inter * 2);
+        if (c.num_experts > 0) {
+            const size_t E = c.num_experts, Im = m.moe_inter;
+            L.moe = MoEExperts(H, c.num_experts, c.top_k, m.moe_inter, c.norm_topk != 0);
+            L.moe.router.alloc(E * H * 2);
+            L.moe.gate_up_packed.alloc(E * 2 * Im * H * 2);
+            L.moe.down.alloc(E * H * Im * 2);
+        } else {
+            L.gate_up_proj.weight_packed.alloc(static_cast<size_t>(2 * m.inter) * H * 2);
+            L.down_proj.weight.alloc(static_cast<size_t>(H) * m.inter * 2);
+        }
         L.q_norm.alloc(D * 2);
         L.k_norm.alloc(D * 2);
     }
@@ -147,8 +167,12 @@ static void create(Model& m, const msgl_model_config& c) {
     for (int t = 1; t <= static_cast<int>(T); ++t) {
         gws = std::max(gws, L0.qkv_proj.workspace(t));
         gws = std::max(gws, L0.o_proj.workspace(t));
-        gws = std::max(gws, L0.gate_up_proj.workspace(t));
-        gws = std::max(gws, L0.down_proj.workspace(t));
+        if (c.num_experts > 0) {
+            gws = std::max(gws, msgl_gemm_workspace_size(t, c.num_experts, H));
+        } else {
+            gws = std::max(gws, L0.gate_up_proj.workspace(t));
+            gws = std::max(gws, L0.down_proj.workspace(t));
+        }
         if (t <= static_cast<int>(B)) gws = std::max(gws, m.lm_head.workspace(t));
     }
     m.gemm_ws.alloc(std::max<size_t>(gws, 256));
@@ -159,6 +183,26 @@ static void create(Model& m, const msgl_model_config& c) {
     m.attn_ws.alloc(std::max<size_t>(aws, 256));
     ckc(cudaMemset(m.attn_ws.p, 0, m.attn_ws.bytes), "attention workspace");
     m.scratch = Scratch{m.gemm_ws.p, m.gemm_ws.bytes, m.attn_ws.p, m.attn_ws.bytes};
+    if (c.num_experts > 0) {
+        const size_t E = c.num_experts, k = c.top_k, R = T * k;
+        m.moe_logits.alloc(T * E * 4);
+        m.moe_ids.alloc(T * k * 4);
+        m.moe_w.alloc(T * k * 4);
+        m.moe_off.alloc((E + 1) * 4);
+        m.moe_tok.alloc(R * 4);
+        m.moe_pos.alloc(R * 4);
+        m.moe_xs.alloc(R * H * 2);
+        m.moe_act.alloc(R * m.moe_inter * 2);
+        m.moe_ys.alloc(R * H * 2);
+        size_t gw = 0;
+        for (size_t r = k; r <= R; r += k)
+            gw = std::max(gw, msgl_grouped_gemm_workspace_size(static_cast<int>(r), c.num_experts));
+        m.moe_ws.alloc(std::max<size_t>(gw, 256));
+        m.moe_scratch = MoEScratch{m.moe_logits.as<float>(), m.moe_ids.as<int>(), m.moe_w.as<float>(),
+                                   m.moe_off.as<int>(), m.moe_tok.as<int>(), m.moe_pos.as<int>(),
+                                   m.moe_xs.as<bf16_t>(), m.moe_act.as<bf16_t>(), m.moe_ys.as<bf16_t>(),
+                                   m.moe_ws.p, m.moe_ws.bytes};
+    }
     m.st_max_pages = (c.max_position + 15) / 16;
     m.st_ids.alloc(T * 4);
     m.st_pos.alloc(T * 4);
@@ -186,8 +230,14 @@ static void random_init(Model& m, uint64_t seed, float std, cudaStream_t s) {
         fill(L.k_norm, seed, id++, 1.f, 0.f, s);
         fill(L.o_proj.weight, seed, id++, 0.f, std, s);
         fill(L.post_attention_layernorm.weight, seed, id++, 1.f, 0.f, s);
-        fill(L.gate_up_proj.weight_packed, seed, id++, 0.f, std, s);  // i.i.d.: packing is moot
-        fill(L.down_proj.weight, seed, id++, 0.f, std, s);
+        if (m.cfg.num_experts > 0) {
+            fill(L.moe.router, seed, id++, 0.f, std, s);
+            fill(L.moe.gate_up_packed, seed, id++, 0.f, std, s);
+            fill(L.moe.down, seed, id++, 0.f, std, s);
+        } else {
+            fill(L.gate_up_proj.weight_packed, seed, id++, 0.f, std, s);  // i.i.d.: packing is moot
+            fill(L.down_proj.weight, seed, id++, 0.f, std, s);
+        }
     }
     fill(m.norm.weight, seed, id++, 1.f, 0.f, s);
     fill(m.lm_head.weight, seed, id++, 0.f, std, s);
@@ -243,6 +293,33 @@ static void set_weight(Model& m, const std::string& name, const bf16_t* h, int64
                          I + r * m.inter, m.inter, 0, H, s);
             ck(msgl_pack_gate_up(tmp.p, L.gate_up_proj.weight_packed.p, m.inter, H, s), "pack_gate_up");
             ckc(cudaStreamSynchronize(s), "set_weight");
+        } else if (f == "router") {  // [E, H], replicated on every rank
+            need(static_cast<int64_t>(c.num_experts) * H);
+            upload_block(L.moe.router.p, h, H, 0, c.num_experts, 0, H, s);
+        } else if (f.rfind("experts.", 0) == 0) {
+            size_t d2 = f.find('.', 8);
+            const int e = std::stoi(f.substr(8, d2 - 8));
+            const std::string part = f.substr(d2 + 1);
+            if (e < 0 || e >= c.num_experts) throw Fail(MSGL_ERR_INVALID_ARG, "set_weight: expert");
+            const int64_t Im = c.moe_inter, Iml = m.moe_inter;
+            if (part == "gate_up") {  // [2 Im, H] rows gate | up: this rank's Im/tp of each, packed
+                need(2 * Im * H);
+                DevBuf tmp;
+                tmp.alloc(static_cast<size_t>(2 * Iml) * H * 2);
+                upload_block(tmp.p, h, H, r * Iml, Iml, 0, H, s);
+                upload_block(static_cast<char*>(tmp.p) + static_cast<size_t>(Iml) * H * 2, h, H,
+                             Im + r * Iml, Iml, 0, H, s);
+                char* dst = static_cast<char*>(L.moe.gate_up_packed.p) +
+                            static_cast<size_t>(e) * 2 * Iml * H * 2;
+                ck(msgl_pack_gate_up(tmp.p, dst, static_cast<int>(Iml), H, s), "pack_gate_up");
+                ckc(cudaStreamSynchronize(s), "set_weight");
+            } else if (part == "down") {  // [H, Im]: column shard
+                need(H * Im);
+                char* dst = static_cast<char*>(L.moe.down.p) + static_cast<size_t>(e) * H * Iml * 2;
+                upload_block(dst, h, Im, 0, H, r * Iml, Iml, s);
+            } else {
+                throw Fail(MSGL_ERR_INVALID_ARG, "set_weight: unknown tensor " + name);
+            }
         } else if (f == "down") {  // [H, I]: column shard
             need(H * I);
             upload_block(L.down_proj.weight.p, h, I, 0, H, r * m.inter, m.inter, s);
@@ -302,8 +379,12 @@ static void forward(Model& m, const msgl_batch& b, int* next_tokens, float* logi
                        m.attn_out.as<bf16_t>(), m.scratch, s);                // :51-52
         L.o_proj.forward(m.attn_out.as<bf16_t>(), x, T, m.scratch, s);       // :55
         L.post_attention_layernorm.forward_fused_add(x, res, T, false, s);   // :57
-        L.gate_up_proj.forward(x, m.act.as<bf16_t>(), T, m.scratch, s);      // :60-79
-        L.down_proj.forward(m.act.as<bf16_t>(), x, T, m.scratch, s);         // :80
+        if (c.num_experts > 0) {
+            L.moe.forward(x, x, T, m.moe_scratch, m.scratch, s);              // qwen3_moe.cpp:62-111
+        } else {
+            L.gate_up_proj.forward(x, m.act.as<bf16_t>(), T, m.scratch, s);  // :60-79
+            L.down_proj.forward(m.act.as<bf16_t>(), x, T, m.scratch, s);     // :80
+        }
     }
     // final norm on each request's last row (qwen3.cpp:177, sampling row of D10), lm_head +
     // greedy argmax (scheduler.cpp:117-124)

@@ -232,6 +232,44 @@ def test_gemm_bf16(cuda, M, N, K):
     assert ops.device_error() == (0, 0)
 
 
+def test_gemm_workspace_shared_across_shapes(cuda):
+    """One workspace reused, in stream order, by split-K GEMMs of different shapes (as the
+    executor does across a layer): every result stays correct."""
+    from msgl import ops
+    rng = np.random.default_rng(12)
+    shapes = [(128, 6144, 4096), (128, 4096, 4096), (128, 4096, 12288), (4, 1000, 512)]
+    ws = torch.zeros(max(ops.gemm_workspace(*s).numel() for s in shapes), dtype=torch.uint8,
+                     device="cuda")
+    data = [(rn(rng, M, K), rn(rng, N, K, std=0.02)) for M, N, K in shapes]
+    for rep in range(2):
+        for (x, w) in data:
+            ref = (torch.from_numpy(x).double() @ torch.from_numpy(w).double().T).numpy()
+            y = host(ops.linear(dev(x), dev(w), out_dtype=torch.float32, workspace=ws))
+            assert rel_l2(y, ref) < 1e-5, (rep, x.shape, w.shape)
+    assert ops.device_error() == (0, 0)
+
+
+def test_decode_workspace_shared_across_shapes(cuda, oracle):
+    from msgl import ops
+    rng = np.random.default_rng(13)
+    cases = [[2048, 1000, 77, 3000], [513, 4096], [100] * 9]
+    ws = torch.zeros(max(ops.attention_workspace(len(c), max(c), 32, 8).numel() for c in cases),
+                     dtype=torch.uint8, device="cuda")
+    for rep in range(2):
+        for seq_lens in cases:
+            B = len(seq_lens)
+            kp, vp, pt = make_paged(rng, seq_lens, 8, sum((s + 15) // 16 for s in seq_lens) + 1)
+            q = rn(rng, B, 32 * 128)
+            seq = np.array(seq_lens, np.int32)
+            ref = oracle.paged_attention(q, kp, vp, pt, seq, np.arange(B + 1, dtype=np.int32),
+                                         32, 8, 128, 16)
+            out = ops.paged_attention_decode(dev(q), dev(kp), dev(vp), dev(pt, torch.int32),
+                                             dev(seq, torch.int32), max(seq_lens), 32, 8,
+                                             workspace=ws)
+            assert rel_l2(host(out).reshape(B, -1), ref) < 1e-2, (rep, seq_lens)
+    assert ops.device_error() == (0, 0)
+
+
 def test_gemm_matches_oracle_linear(cuda, oracle):
     from msgl import ops
     rng = np.random.default_rng(1)

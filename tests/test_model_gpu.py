@@ -102,3 +102,53 @@ def test_layer0_hidden_state(cuda, oracle):
     _, hidden = orc.forward(h["input_ids"], h["positions"], h["slot_mapping"], h["page_table"],
                             h["seq_lens"], h["q_indptr"], return_hidden=True)
     assert rel_l2(x.float().cpu().numpy(), hidden[0]) < 2e-2
+
+
+MOE_CFG = dict(num_layers=2, hidden=512, num_q_heads=8, num_kv_heads=2, head_dim=128, inter=0,
+               vocab=1000, eps=1e-6, rope_base=1e6, max_position=512, page_size=16,
+               num_experts=8, top_k=8, moe_inter=96, norm_topk=True)
+
+
+def moe_weights(cfg, seed):
+    rng = np.random.default_rng(seed)
+    rn = lambda *s, std=1.0: bf16_round(rng.standard_normal(s).astype(np.float32) * std)
+    one = lambda n: bf16_round(1.0 + 0.1 * rng.standard_normal(n).astype(np.float32))
+    H, D, hq, hkv, V = (cfg[k] for k in ("hidden", "head_dim", "num_q_heads", "num_kv_heads", "vocab"))
+    E, Im = cfg["num_experts"], cfg["moe_inter"]
+    w = {"embed": rn(V, H), "norm": one(H), "lm_head": rn(V, H, std=0.05)}
+    for l in range(cfg["num_layers"]):
+        p = f"layers.{l}."
+        w.update({p + "input_ln": one(H), p + "qkv": rn((hq + 2 * hkv) * D, H, std=0.05),
+                  p + "q_norm": one(D), p + "k_norm": one(D), p + "o": rn(H, hq * D, std=0.05),
+                  p + "post_ln": one(H), p + "router": rn(E, H, std=0.05)})
+        for e in range(E):
+            w[p + f"experts.{e}.gate_up"] = rn(2 * Im, H, std=0.05)
+            w[p + f"experts.{e}.down"] = rn(H, Im, std=0.05)
+    return w
+
+
+def test_moe_model_prefill_then_decode(cuda, oracle):
+    """Qwen3-MoE layers (router, softmax top-k weights, grouped experts) end to end; top_k equals
+    the expert count so routing has no discrete near-ties (top-k selection is pinned at op level)."""
+    from msgl.model import BatchBuilder, PagePool, Qwen3Model, Request
+
+    w = moe_weights(MOE_CFG, 5)
+    model = Qwen3Model(MOE_CFG, max_tokens=128, max_reqs=4)
+    model.set_weights(w)
+    model.alloc_kv(32)
+    orc = OracleModel(oracle, MOE_CFG, w, num_slots=32 * 16)
+    rng = np.random.default_rng(2)
+    reqs = [Request(list(rng.integers(0, MOE_CFG["vocab"], n))) for n in (9, 30)]
+    bb = BatchBuilder(PagePool(32))
+    for step in range(3):
+        sb = bb.build(reqs, decode=step > 0, max_pages=4)
+        nxt, lg = model.forward(sb, logits=True)
+        torch.cuda.synchronize()
+        h = {k: v.cpu().numpy() for k, v in sb.tensors.items()}
+        ref = orc.forward(h["input_ids"], h["positions"], h["slot_mapping"], h["page_table"],
+                          h["seq_lens"], h["q_indptr"])
+        err = rel_l2(lg.cpu().numpy(), ref)
+        assert err < 2e-2, (step, err)
+        for r, t in zip(reqs, nxt.cpu().numpy()):
+            r.cached_len = r.device_len
+            r.input_ids.append(int(t))

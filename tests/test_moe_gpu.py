@@ -52,7 +52,8 @@ def test_route_topk(cuda, oracle, T, E, k):
     rng = np.random.default_rng(T + E)
     logits = rng.standard_normal((T, E)).astype(np.float32)
     logits[0, [3, E - 1]] = 10.0            # exact tie at the top: larger id first
-    logits[-1, :] = 0.5                     # all equal: ids E-1, E-2, ...
+    if T > 1:
+        logits[-1, :] = 0.5                 # all equal: ids E-1, E-2, ...
     for norm in (True, False):
         ids, w = route(dev(logits, torch.float32), k, norm)
         eid, ew = oracle.router_topk(logits, k, norm)
