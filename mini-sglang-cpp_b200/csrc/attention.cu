@@ -31,6 +31,8 @@ constexpr int kConsumerWarps = 4;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kDecodeStages = 3;          // x 4 pages per stage
 constexpr int kExtendStages = 8;          // x 1 page per stage
+constexpr int kMaxChunkPages = 512;       // decode split-KV chunk bound (page ids in smem)
+constexpr int kExtendPageBatch = 1024;    // extend: page ids staged per batch
 constexpr float kNegInf = -__builtin_huge_valf();
 
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
@@ -191,10 +193,22 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
 
     if (warp == kConsumerWarps) {
         // ---------------- TMA producer
+        // The chunk's page ids come into shared memory in one coalesced warp load, so no TMA
+        // issue waits on a dependent global read of the page table.
+        int* pages = flag + 4;  // [chunk_pages <= kMaxChunkPages]
+        const int* pt = page_table + static_cast<int64_t>(b) * max_pages + p0;
+        for (int i = lane; i < np; i += 32) {
+            int page = pt[i];
+            if (static_cast<unsigned>(page) >= static_cast<unsigned>(pool_pages)) {
+                record_error(err, MSGL_ERR_BOUNDS, 201);
+                page = 0;
+            }
+            pages[i] = page;
+        }
+        __syncwarp();
         if (lane == 0) {
             tma_prefetch_desc(&tk);
             tma_prefetch_desc(&tv);
-            const int* pt = page_table + static_cast<int64_t>(b) * max_pages;
             for (int it = 0; it < nsteps; ++it) {
                 const int s = it % kDecodeStages;
                 if (it >= kDecodeStages &&
@@ -202,14 +216,9 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
                     break;
                 const int cnt = min(4, np - it * 4);
                 mbar_arrive_expect_tx(&full[s], cnt * kPageSlotBytes);
-                for (int p = 0; p < cnt; ++p) {
-                    int page = pt[p0 + it * 4 + p];
-                    if (static_cast<unsigned>(page) >= static_cast<unsigned>(pool_pages)) {
-                        record_error(err, MSGL_ERR_BOUNDS, 201);
-                        page = 0;
-                    }
-                    issue_page(smem + (s * 4 + p) * kPageSlotBytes, &tk, &tv, &full[s], kvh, page);
-                }
+                for (int p = 0; p < cnt; ++p)
+                    issue_page(smem + (s * 4 + p) * kPageSlotBytes, &tk, &tv, &full[s], kvh,
+                               pages[it * 4 + p]);
             }
         }
         return;
@@ -381,20 +390,38 @@ paged_extend_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
         if (lane == 0) {
             tma_prefetch_desc(&tk);
             tma_prefetch_desc(&tv);
-            const int* pt = page_table + static_cast<int64_t>(b) * max_pages;
-            for (int it = 0; it < npages; ++it) {
+        }
+        // Page ids staged in shared memory, kExtendPageBatch at a time (one coalesced warp load
+        // per batch); lane 0 issues the TMA loads.
+        int* pages = reinterpret_cast<int*>(empty + kExtendStages);
+        const int* pt = page_table + static_cast<int64_t>(b) * max_pages;
+        bool ok = true;
+        for (int it = 0; it < npages && ok; ++it) {
+            if (it % kExtendPageBatch == 0) {
+                __syncwarp();
+                const int n = min(kExtendPageBatch, npages - it);
+                for (int i = lane; i < n; i += 32) {
+                    int page = pt[it + i];
+                    if (static_cast<unsigned>(page) >= static_cast<unsigned>(pool_pages)) {
+                        record_error(err, MSGL_ERR_BOUNDS, 221);
+                        page = 0;
+                    }
+                    pages[i] = page;
+                }
+                __syncwarp();
+            }
+            if (lane == 0) {
                 const int s = it % kExtendStages;
                 if (it >= kExtendStages &&
-                    !mbar_wait(&empty[s], ((it / kExtendStages) - 1) & 1, err, 220))
-                    break;
-                mbar_arrive_expect_tx(&full[s], kPageSlotBytes);
-                int page = pt[it];
-                if (static_cast<unsigned>(page) >= static_cast<unsigned>(pool_pages)) {
-                    record_error(err, MSGL_ERR_BOUNDS, 221);
-                    page = 0;
+                    !mbar_wait(&empty[s], ((it / kExtendStages) - 1) & 1, err, 220)) {
+                    ok = false;
+                } else {
+                    mbar_arrive_expect_tx(&full[s], kPageSlotBytes);
+                    issue_page(smem + s * kPageSlotBytes, &tk, &tv, &full[s], kvh,
+                               pages[it % kExtendPageBatch]);
                 }
-                issue_page(smem + s * kPageSlotBytes, &tk, &tv, &full[s], kvh, page);
             }
+            ok = __shfl_sync(0xffffffffu, ok, 0);
         }
         return;
     }
@@ -471,6 +498,7 @@ DecodePlan plan_decode(int B, int max_seq_len, int hq, int hkv) {
     const int pairs = std::max(1, B * hkv);
     int chunks = (8 * 148 + pairs - 1) / pairs;
     chunks = std::max(1, std::min(chunks, (max_pages_seq + 15) / 16));
+    chunks = std::max(chunks, (max_pages_seq + kMaxChunkPages - 1) / kMaxChunkPages);
     p.chunk_pages = (max_pages_seq + chunks - 1) / chunks;
     p.max_chunks = (max_pages_seq + p.chunk_pages - 1) / p.chunk_pages;
     auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
@@ -542,7 +570,8 @@ int msgl_paged_attention_decode(const void* q, const void* k_pool, const void* v
     if (rc) return rc;
     int* err = device_error_word();
     if (!err) return set_error(MSGL_ERR_CUDA, "device error word unavailable");
-    const size_t smem = kDecodeStages * 4 * kPageSlotBytes + 2 * kDecodeStages * 8 + 16 + 1024;
+    const size_t smem = kDecodeStages * 4 * kPageSlotBytes + 2 * kDecodeStages * 8 + 16 +
+                        kMaxChunkPages * sizeof(int) + 1024;
     static bool attr_set = false;
     if (!attr_set) {
         cudaFuncSetAttribute(paged_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -578,7 +607,8 @@ int msgl_paged_attention_extend(const void* q, const void* k_pool, const void* v
     if (rc) return rc;
     int* err = device_error_word();
     if (!err) return set_error(MSGL_ERR_CUDA, "device error word unavailable");
-    const size_t smem = kExtendStages * kPageSlotBytes + 2 * kExtendStages * 8 + 1024;
+    const size_t smem = kExtendStages * kPageSlotBytes + 2 * kExtendStages * 8 +
+                        kExtendPageBatch * sizeof(int) + 1024;
     static bool attr_set = false;
     if (!attr_set) {
         cudaFuncSetAttribute(paged_extend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

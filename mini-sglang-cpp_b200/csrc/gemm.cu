@@ -258,6 +258,224 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
     }
 }
 
+// ============================================================================ stream-K kernel
+// Persistent: one CTA per SM. The (tile, k-block) units of the whole GEMM are cut into G equal
+// contiguous ranges, one per CTA, so every SM streams the same number of weight bytes whatever
+// the tile count. A CTA's range covers one or more tile segments; each segment accumulates into
+// one of two TMEM buffers (the epilogue of segment j overlaps the mainloop of segment j+1).
+// A segment that is a whole tile runs the epilogue directly; a partial segment stores its fp32
+// tile into the CTA's workspace slot, and the last contributor of the tile (arrival counter)
+// sums the contributors' slots in CTA order -- deterministic -- and runs the epilogue.
+template <int BN>
+struct SkCfg {
+    static constexpr int kTileB = BN * kBK * 2;
+    static constexpr int kStageBytes = kTileA + kTileB;
+    static constexpr int kStages = BN >= 256 ? 4 : (BN >= 128 ? 6 : 8);
+    static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+    static constexpr size_t kSmem = static_cast<size_t>(kStages) * kStageBytes + 1024 + 256;
+};
+
+__device__ __forceinline__ int sk_cta_of(int64_t u, int64_t U, int G) {
+    return static_cast<int>(((u + 1) * G + U - 1) / U - 1);
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+gemm_sk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+               void* __restrict__ y, unsigned long long* __restrict__ amax, int M, int N, int K,
+               int m_tiles, float* __restrict__ ws_part, int* __restrict__ ws_cnt, int* err) {
+    using Cfg = SkCfg<BN>;
+    constexpr int ST = Cfg::kStages;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + ST * kTileA;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + ST * Cfg::kStageBytes);
+    uint64_t* empty = full + ST;
+    uint64_t* tfull = empty + ST;   // [2] accumulator ready
+    uint64_t* tempty = tfull + 2;   // [2] accumulator drained
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = gridDim.x, c = blockIdx.x;
+    const int KB = (K + kBK - 1) / kBK;
+    const int64_t U = static_cast<int64_t>(m_tiles) * ((N + kBM - 1) / kBM) * KB;
+    const int64_t u0 = static_cast<int64_t>(c) * U / G, u1 = static_cast<int64_t>(c + 1) * U / G;
+    const int t_first = static_cast<int>(u0 / KB), t_last = static_cast<int>((u1 - 1) / KB);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < ST; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 4);
+        }
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, Cfg::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            tma_prefetch_desc(&tmap_w);
+            tma_prefetch_desc(&tmap_x);
+            const uint64_t pol_w = policy_evict_first();
+            const uint64_t pol_x = policy_evict_last();
+            int i = 0;
+            for (int64_t u = u0; u < u1; ++u, ++i) {
+                const int s = i % ST;
+                if (i >= ST && !mbar_wait(&empty[s], ((i / ST) - 1) & 1, err, 330)) break;
+                const int t = static_cast<int>(u / KB), kb = static_cast<int>(u % KB);
+                mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
+                tma_load_2d_hint(sA + s * kTileA, &tmap_w, &full[s], kb * kBK, (t / m_tiles) * kBM, pol_w);
+                tma_load_2d_hint(sB + s * Cfg::kTileB, &tmap_x, &full[s], kb * kBK, (t % m_tiles) * BN, pol_x);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_bf16(kBM, BN);
+            int i = 0;
+            bool ok = true;
+            for (int t = t_first, j = 0; t <= t_last && ok; ++t, ++j) {
+                const int a = j & 1;
+                const int kb_s = static_cast<int>(max(u0, static_cast<int64_t>(t) * KB) - static_cast<int64_t>(t) * KB);
+                const int kb_e = static_cast<int>(min(u1, static_cast<int64_t>(t + 1) * KB) - static_cast<int64_t>(t) * KB);
+                if (j >= 2 && !mbar_wait(&tempty[a], ((j >> 1) - 1) & 1, err, 340)) break;
+                tc_fence_after();
+                const uint32_t acc = tmem + a * BN;
+                for (int kb = kb_s; kb < kb_e; ++kb, ++i) {
+                    const int s = i % ST;
+                    if (!mbar_wait(&full[s], (i / ST) & 1, err, 341)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(sA + s * kTileA);
+                    const uint32_t b_addr = smem_u32(sB + s * Cfg::kTileB);
+#pragma unroll
+                    for (int k = 0; k < kBK / 16; ++k)
+                        umma_bf16(acc, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32),
+                                  idesc, (kb > kb_s || k > 0) ? 1u : 0u);
+                    umma_commit(&empty[s]);
+                }
+                umma_commit(&tfull[a]);
+            }
+        }
+    } else {
+        // ---------------- epilogue warps 2..5
+        const int warp_q = warp & 3;
+        const int row = warp_q * 32 + lane;
+        const int et = threadIdx.x - 64;
+        for (int t = t_first, j = 0; t <= t_last; ++t, ++j) {
+            const int a = j & 1;
+            const int64_t tb = static_cast<int64_t>(t) * KB;
+            const int kb_s = static_cast<int>(max(u0, tb) - tb);
+            const int kb_e = static_cast<int>(min(u1, tb + KB) - tb);
+            const bool have = mbar_wait(&tfull[a], (j >> 1) & 1, err, 350);
+            tc_fence_after();
+            const int n_tile = t / m_tiles, m_tile = t % m_tiles;
+            const int n = n_tile * kBM + row, m0 = m_tile * BN;
+            const uint32_t taddr = tmem + a * BN + (static_cast<uint32_t>(warp_q * 32) << 16);
+            if (kb_s == 0 && kb_e == KB) {
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 16) {
+                    uint32_t r[16];
+                    float v[16];
+                    tmem_ld16(taddr + c0, r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int q = 0; q < 16; ++q) v[q] = have ? __uint_as_float(r[q]) : 0.f;
+                    epilogue_chunk<EPI>(v, n, N, m0 + c0, M, y, amax, lane, warp_q, n_tile);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[a]);
+                continue;
+            }
+            // partial tile -> this CTA's slot (0: its first segment, 1: any later one)
+            float* part = ws_part + ((static_cast<int64_t>(c) * 2 + (t == t_first ? 0 : 1)) * kBM + row) * BN;
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 16) {
+                uint32_t r[16];
+                tmem_ld16(taddr + c0, r);
+                tmem_ld_wait();
+                float4* dst = reinterpret_cast<float4*>(part + c0);
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    __stcg(dst + q, have ? make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                                       __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]))
+                                         : make_float4(0.f, 0.f, 0.f, 0.f));
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[a]);  // TMEM buffer free for segment j + 2
+            const int first = sk_cta_of(tb, U, G), last = sk_cta_of(tb + KB - 1, U, G);
+            __threadfence();
+            named_bar(1, 128);
+            if (et == 0) {
+                int old = atomicAdd(ws_cnt + t, 1);
+                *last_flag = (old == last - first);
+            }
+            named_bar(1, 128);
+            if (*last_flag) {
+                __threadfence();
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 16) {
+                    float v[16];
+#pragma unroll
+                    for (int q = 0; q < 16; ++q) v[q] = 0.f;
+                    for (int cc = first; cc <= last; ++cc) {
+                        // contributor cc stored tile t in slot 0 if t is the first tile of its
+                        // range, else in slot 1 (same rule as the writer above)
+                        const int64_t cu0 = static_cast<int64_t>(cc) * U / G;
+                        const int slot = (cu0 / KB == t) ? 0 : 1;
+                        const float4* src = reinterpret_cast<const float4*>(
+                            ws_part + ((static_cast<int64_t>(cc) * 2 + slot) * kBM + row) * BN + c0);
+                        float4 x0 = __ldcg(src), x1 = __ldcg(src + 1), x2 = __ldcg(src + 2), x3 = __ldcg(src + 3);
+                        v[0] += x0.x; v[1] += x0.y; v[2] += x0.z; v[3] += x0.w;
+                        v[4] += x1.x; v[5] += x1.y; v[6] += x1.z; v[7] += x1.w;
+                        v[8] += x2.x; v[9] += x2.y; v[10] += x2.z; v[11] += x2.w;
+                        v[12] += x3.x; v[13] += x3.y; v[14] += x3.z; v[15] += x3.w;
+                    }
+                    epilogue_chunk<EPI>(v, n, N, m0 + c0, M, y, amax, lane, warp_q, n_tile);
+                }
+                if (et == 0) ws_cnt[t] = 0;
+            }
+        }
+        tc_fence_before();
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, Cfg::kTmemCols);
+    }
+}
+
+int num_sms() {
+    static int n[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return 148;
+    if (!n[dev]) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+        n[dev] = v;
+    }
+    return n[dev];
+}
+
+// Stream-K workspace: counters at a fixed offset, then 2 fp32 tile slots per CTA.
+size_t sk_workspace_bytes(int bn, int sms) {
+    return kCounterBytes + static_cast<size_t>(sms) * 2 * kBM * bn * sizeof(float);
+}
+
 struct GemmPlan {
     int bn, m_tiles, n_tiles, splits, kb_per_split;
     size_t ws_part_bytes, ws_cnt_off, ws_bytes;
@@ -316,6 +534,25 @@ int launch_bn(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& tx, v
     return MSGL_OK;
 }
 
+template <int BN, int EPI>
+int launch_sk(const CUtensorMap& tw, const CUtensorMap& tx, void* y, unsigned long long* amax,
+              int M, int N, int K, void* ws, int sms, cudaStream_t stream) {
+    using Cfg = SkCfg<BN>;
+    int* err = device_error_word();
+    if (!err) return set_error(MSGL_ERR_CUDA, "device error word unavailable");
+    cudaFuncSetAttribute(gemm_sk_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(Cfg::kSmem));
+    const int m_tiles = (M + BN - 1) / BN;
+    const int64_t units = static_cast<int64_t>(m_tiles) * ((N + kBM - 1) / kBM) * ((K + kBK - 1) / kBK);
+    const int G = static_cast<int>(std::min<int64_t>(sms, units));
+    uint8_t* w8 = static_cast<uint8_t*>(ws);
+    gemm_sk_kernel<BN, EPI><<<G, kGemmThreads, Cfg::kSmem, stream>>>(
+        tw, tx, y, amax, M, N, K, m_tiles, reinterpret_cast<float*>(w8 + kCounterBytes),
+        reinterpret_cast<int*>(w8), err);
+    MSGL_LAUNCH_CHECK();
+    return MSGL_OK;
+}
+
 template <int EPI>
 int run_gemm(const void* x, const void* w, void* y, unsigned long long* amax, int M, int N, int K,
              void* ws, size_t ws_bytes, cudaStream_t stream) {
@@ -323,14 +560,29 @@ int run_gemm(const void* x, const void* w, void* y, unsigned long long* amax, in
     if (K % 8) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "gemm: K must be a multiple of 8");
     if (M == 0) return MSGL_OK;
     if (M > 65535 * 256) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "gemm: M too large");
-    GemmPlan p = plan_gemm(M, N, K);
-    if (p.ws_bytes > 0 && (!ws || ws_bytes < p.ws_bytes))
-        return set_error(MSGL_ERR_WORKSPACE, "gemm: workspace too small");
+    const int bn = pick_bn(M);
+    const int64_t tiles = static_cast<int64_t>((M + bn - 1) / bn) * ((N + kBM - 1) / kBM);
     CUtensorMap tw, tx;
     int rc = make_tmap_2d_bf16(&tw, w, K, N, static_cast<uint64_t>(K) * 2, kBK, kBM, true);
     if (rc) return rc;
-    rc = make_tmap_2d_bf16(&tx, x, K, M, static_cast<uint64_t>(K) * 2, kBK, p.bn, true);
+    rc = make_tmap_2d_bf16(&tx, x, K, M, static_cast<uint64_t>(K) * 2, kBK, bn, true);
     if (rc) return rc;
+    if (tiles <= static_cast<int64_t>(kCounterBytes / sizeof(int))) {
+        const int sms = num_sms();
+        if (!ws || ws_bytes < sk_workspace_bytes(bn, sms))
+            return set_error(MSGL_ERR_WORKSPACE, "gemm: workspace too small");
+        switch (bn) {
+            case 16: return launch_sk<16, EPI>(tw, tx, y, amax, M, N, K, ws, sms, stream);
+            case 32: return launch_sk<32, EPI>(tw, tx, y, amax, M, N, K, ws, sms, stream);
+            case 64: return launch_sk<64, EPI>(tw, tx, y, amax, M, N, K, ws, sms, stream);
+            case 128: return launch_sk<128, EPI>(tw, tx, y, amax, M, N, K, ws, sms, stream);
+            default: return launch_sk<256, EPI>(tw, tx, y, amax, M, N, K, ws, sms, stream);
+        }
+    }
+    // very large grids: one CTA per tile, no K split, no workspace
+    GemmPlan p = plan_gemm(M, N, K);
+    p.splits = 1;
+    p.kb_per_split = (K + kBK - 1) / kBK;
     switch (p.bn) {
         case 16: return launch_bn<16, EPI>(p, tw, tx, y, amax, M, N, K, ws, stream);
         case 32: return launch_bn<32, EPI>(p, tw, tx, y, amax, M, N, K, ws, stream);
@@ -450,7 +702,17 @@ extern "C" {
 
 size_t msgl_gemm_workspace_size(int M, int N, int K) {
     if (M <= 0 || N <= 0 || K <= 0) return 0;
-    return plan_gemm(M, N, K).ws_bytes;
+    const int bn = pick_bn(M);
+    const int64_t tiles = static_cast<int64_t>((M + bn - 1) / bn) * ((N + kBM - 1) / kBM);
+    if (tiles > static_cast<int64_t>(kCounterBytes / sizeof(int))) return 0;
+    int sms = 148;
+    int dev = 0, v = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0)
+        sms = v;
+    else
+        cudaGetLastError();  // no device (host-only query): size for a 148-SM B200
+    return sk_workspace_bytes(bn, sms);
 }
 
 int msgl_gemm_bf16(const void* x, const void* w, void* y, int M, int N, int K, int out_dtype,
