@@ -20,7 +20,8 @@ roofline: the paged decode-attention kernel (the largest share of the step) time
 cpu_baseline: the reference's own CPU code (oracle/_ref: Linear::forward of the 4 layer
          projections + lm_head; attention from the C restatement, as the reference has no
          paged/GQA attention) on a bounded token sample, extrapolated to the full step.
-N > 1: independent replicas, one per GPU (weak scaling); tensor parallelism is not timed here.
+N > 1: tensor parallelism over the N GPUs (one process each, NCCL over NVLink): the same
+         128-request step, heads / FFN columns / vocab rows sharded (strong scaling).
 """
 from __future__ import annotations
 
@@ -46,9 +47,9 @@ BATCH, CTX, PREFIX, PAGE = 128, 2048, 1024, 16
 
 
 def workload_config(n_gpus):
-    return {"workload": "qwen3-8b-decode", "model_arch": "Qwen3-8B", "global_batch": BATCH * n_gpus,
+    return {"workload": "qwen3-8b-decode", "model_arch": "Qwen3-8B", "global_batch": BATCH,
             "batch_per_gpu": BATCH, "seq_len": CTX, "shared_prefix": PREFIX, "page_size": PAGE,
-            "parallelism": f"replicas{n_gpus}" if n_gpus > 1 else "single",
+            "parallelism": f"tp{n_gpus}" if n_gpus > 1 else "tp1",
             "l2": "inputs larger than L2 (35 GB read per step)"}
 
 
@@ -242,7 +243,7 @@ def run_ours(args, rank, world, local_rank):
 
     import msgl
     from msgl import ops
-    from msgl.model import BatchT, Qwen3Model, device_view, make_step
+    from msgl.model import BatchT, Qwen3Model, TPComm, device_view, make_step, shard_plan
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -250,15 +251,28 @@ def run_ours(args, rank, world, local_rank):
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
 
+    # tensor parallel over the `world` GPUs: every rank runs the same 128-request step on its
+    # shard (heads / FFN columns / vocab rows); NCCL id from rank 0 through the process group
+    comm = None
+    if world > 1:
+        uid = [TPComm.new_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = TPComm(rank, world, uid[0])
+    plan = shard_plan(CFG8B["num_q_heads"], CFG8B["num_kv_heads"], CFG8B["inter"],
+                      CFG8B["vocab"], rank, world)
+    hq_l, hkv_l = plan["q_heads"], plan["kv_heads"]
+
     num_pages, pt = build_pages()
-    model = Qwen3Model(CFG8B, max_tokens=BATCH, max_reqs=BATCH)
+    model = Qwen3Model(CFG8B, max_tokens=BATCH, max_reqs=BATCH, tp_rank=rank, tp_size=world)
+    if comm is not None:
+        model.set_tp(comm)
     model.random_init(seed=0, std=0.02)
     model.alloc_kv(num_pages)
     L = CFG8B["num_layers"]
     pools = [model.kv_pool(l) for l in range(L)]
     for l, (k, v, n) in enumerate(pools):  # synthetic KV contents, N(0,1)
         for j, p in enumerate((k, v)):
-            t = device_view(p, (n * CFG8B["num_kv_heads"] * 128,), torch.bfloat16)
+            t = device_view(p, (n * hkv_l * 128,), torch.bfloat16)
             ops.fill_normal_(t, seed=4, stream_id=2 * l + j, std=1.0)
     host = decode_batch_host(pt, CFG8B["vocab"])
     sb = make_step(host, True, dev, CTX, 1)
@@ -320,7 +334,7 @@ def run_ours(args, rank, world, local_rank):
     assert torch.equal(out_host.to(dev), nxt), "host step and device step disagree"
 
     # ---- roofline: paged decode attention alone, every layer's pool
-    hq, hkv = CFG8B["num_q_heads"], CFG8B["num_kv_heads"]
+    hq, hkv = hq_l, hkv_l  # this rank's heads
     q = torch.empty(BATCH, hq, 128, dtype=torch.bfloat16, device=dev)
     ops.fill_normal_(q, seed=5, std=1.0)
     aout = torch.empty_like(q)
@@ -364,12 +378,13 @@ def run_ours(args, rank, world, local_rank):
         cpu.close()
         cores = cpu.threads
         line = {
-            "metric": METRIC, "value": world * BATCH / (ms * 1e-3), "unit": UNIT,
+            "metric": METRIC, "value": BATCH / (ms * 1e-3), "unit": UNIT,
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+            "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (random-init weights, N(0,1) KV, random token ids)",
             "config": workload_config(world),
-            "e2e": {"value": world * BATCH / (ms_e2e * 1e-3), "unit": UNIT,
+            "e2e": {"value": BATCH / (ms_e2e * 1e-3), "unit": UNIT,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": ms_e2e},
             "roofline": {"kernel": "paged_decode_kernel", "bound": "hbm",
@@ -386,6 +401,10 @@ def run_ours(args, rank, world, local_rank):
             "weights_gb": model.weight_bytes() / 1e9,
         }
         print(json.dumps(line), flush=True)
+    # graphs holding NCCL calls and the communicator go before the process group
+    del model
+    if comm is not None:
+        comm.close()
     return 0
 
 

@@ -94,6 +94,12 @@ MSGL_API int msgl_model_step_host(msgl_model* m, const msgl_batch* host_batch,
  * forward (the last layer's output before the final norm) -- used by per-layer parity tests
  * together with num_layers_override. */
 MSGL_API int msgl_model_debug_hidden(msgl_model* m, void** x, float** residual);
+
+/* Attach the tensor-parallel communicator of this rank (required when cfg.tp_size > 1; its rank
+ * and world must match the config). The executor then all-reduces the row-parallel o_proj /
+ * down_proj outputs (fused with the following add + RMSNorm) and combines the vocab-parallel
+ * lm_head argmax over the ranks. */
+MSGL_API int msgl_model_set_tp(msgl_model* m, msgl_tp* tp);
 MSGL_API int msgl_model_set_num_layers_run(msgl_model* m, int n);
 
 #ifdef __cplusplus

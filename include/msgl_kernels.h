@@ -201,6 +201,42 @@ MSGL_API int msgl_moe_combine(const void* y_sorted, const int* pair_pos, const f
                               int num_tokens, int top_k, int hidden, void* out,
                               msgl_stream_t stream);
 
+/* Vocab-parallel lm_head: this rank's rows W [vocab_local, K] cover token ids
+ * [vocab_offset, vocab_offset + vocab_local). packed[m] receives the rank's best
+ * (logit, id) key, ties to the lowest id; combine the ranks with msgl_tp_argmax_combine. */
+MSGL_API int msgl_lm_head_argmax_partial(const void* x, const void* w, int M, int vocab_local,
+                                         int K, int vocab_offset, unsigned long long* packed,
+                                         void* workspace, size_t workspace_bytes,
+                                         msgl_stream_t stream);
+
+/* ---------------------------------------------------------------- tensor parallelism */
+/* TPCommunicator (include/minisgl/distributed/tp.h:9-25; a stub in the reference,
+ * src/distributed/tp.cpp:13-47) over NCCL, one process per GPU. Rank 0 creates the id
+ * (msgl_tp_unique_id_size() bytes) and the launcher broadcasts it to every rank. */
+typedef struct msgl_tp msgl_tp;
+MSGL_API size_t msgl_tp_unique_id_size(void);
+MSGL_API int msgl_tp_get_unique_id(void* out);
+MSGL_API int msgl_tp_init(int rank, int world, const void* unique_id, msgl_tp** out);
+MSGL_API int msgl_tp_destroy(msgl_tp* tp);
+MSGL_API int msgl_tp_rank(const msgl_tp* tp);
+MSGL_API int msgl_tp_world(const msgl_tp* tp);
+/* TPCommunicator::all_reduce_sum (tp.cpp:18-31): in-place sum of bf16 x [n] over the ranks. */
+MSGL_API int msgl_tp_all_reduce_sum(msgl_tp* tp, void* x, int64_t n, msgl_stream_t stream);
+/* Row-parallel projection output x [T, H] (this rank's partial sum) all-reduced, then
+ * msgl_add_rmsnorm (residual += x; x = rmsnorm(residual) * w; first as in msgl_add_rmsnorm). */
+MSGL_API int msgl_tp_allreduce_add_rmsnorm(msgl_tp* tp, void* x, float* residual,
+                                           const void* weight, int num_tokens, int hidden,
+                                           float eps, int first, msgl_stream_t stream);
+/* packed [num_rows] uint64 keys (msgl_lm_head_argmax_partial) max-reduced over the ranks and
+ * unpacked to ids [num_rows]: greedy sampling over the full vocabulary. */
+MSGL_API int msgl_tp_argmax_combine(msgl_tp* tp, unsigned long long* packed, int* ids,
+                                    int num_rows, msgl_stream_t stream);
+/* Host only: the shard of `rank` as 8 ints {q_head0, q_heads, kv_head0, kv_heads, inter0,
+ * inter_cols, vocab0, vocab_rows} (column-parallel qkv / gate_up, row-parallel o / down,
+ * vocab-parallel lm_head; kv heads replicated when world > num_kv_heads). */
+MSGL_API int msgl_tp_shard_plan(int num_q_heads, int num_kv_heads, int inter, int vocab,
+                                int rank, int world, int* out8);
+
 /* ---------------------------------------------------------------- sampling / utilities */
 /* Greedy argmax over logits [num_rows, vocab] (scheduler.cpp:117-124): first maximum wins. */
 MSGL_API int msgl_argmax(const void* logits, int num_rows, int vocab, int dtype, int* out,

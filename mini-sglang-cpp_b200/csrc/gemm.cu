@@ -52,7 +52,7 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int n) {
 template <int EPI>
 __device__ __forceinline__ void epilogue_chunk(const float (&vals)[16], int n, int N, int m_base,
                                                int M, void* y, unsigned long long* amax,
-                                               int lane, int warp_q, int n_tile) {
+                                               int lane, int warp_q, int n_tile, int id_off) {
     if (EPI == EPI_BF16 || EPI == EPI_F32) {
         if (n >= N) return;
 #pragma unroll
@@ -85,7 +85,7 @@ __device__ __forceinline__ void epilogue_chunk(const float (&vals)[16], int n, i
     } else {  // EPI_ARGMAX
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-            unsigned long long key = n < N ? argmax_key(vals[j], n) : 0ull;
+            unsigned long long key = n < N ? argmax_key(vals[j], n + id_off) : 0ull;
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) {
                 unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
@@ -111,7 +111,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
             void* __restrict__ y, unsigned long long* __restrict__ amax, int M, int N, int K,
             int kb_per_split, int splits, float* __restrict__ ws, int* __restrict__ ws_cnt,
-            GroupArgs grp, int* err) {
+            GroupArgs grp, int id_off, int* err) {
     using Cfg = GemmCfg<BN>;
     constexpr int ST = Cfg::kStages;
     extern __shared__ uint8_t smem_raw[];
@@ -210,7 +210,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
                 tmem_ld_wait();
 #pragma unroll
                 for (int j = 0; j < 16; ++j) v[j] = have ? __uint_as_float(r[j]) : 0.f;
-                epilogue_chunk<EPI>(v, n, N, m0 + c0, M, y, amax, lane, warp_q, n_tile);
+                epilogue_chunk<EPI>(v, n, N, m0 + c0, M, y, amax, lane, warp_q, n_tile, id_off);
             }
         } else {
             const int64_t tile_id = static_cast<int64_t>(n_tile) * gridDim.x + m_tile;
@@ -244,7 +244,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
 #pragma unroll
                         for (int j = 0; j < 16; ++j) v[j] += __ldcg(p + (c0 + j) * kBM + row);
                     }
-                    epilogue_chunk<EPI>(v, n, N, m0 + c0, M, y, amax, lane, warp_q, n_tile);
+                    epilogue_chunk<EPI>(v, n, N, m0 + c0, M, y, amax, lane, warp_q, n_tile, id_off);
                 }
                 if (et == 0) ws_cnt[tile_id] = 0;
             }
@@ -279,11 +279,40 @@ __device__ __forceinline__ int sk_cta_of(int64_t u, int64_t U, int G) {
     return static_cast<int>(((u + 1) * G + U - 1) / U - 1);
 }
 
+// A CTA's work is a list of tile segments (tile t, k-blocks [kb_s, kb_e)):
+//  * data-parallel mode (tiles >= CTAs): whole tiles c, c + G, c + 2G, ... -- no partials;
+//  * stream-K mode (tiles < CTAs): the CTA's contiguous range of (tile, k-block) units, cut at
+//    tile boundaries.
+struct SkWork {
+    int64_t U, u0, u1;
+    int T, KB, G, c;
+    bool dp;
+    __device__ __forceinline__ int num_segs() const {
+        if (dp) return c < T ? (T - c + G - 1) / G : 0;
+        return static_cast<int>((u1 - 1) / KB - u0 / KB + 1);
+    }
+    __device__ __forceinline__ void seg(int j, int& t, int& kb_s, int& kb_e) const {
+        if (dp) {
+            t = c + j * G;
+            kb_s = 0;
+            kb_e = KB;
+            return;
+        }
+        t = static_cast<int>(u0 / KB) + j;
+        const int64_t tb = static_cast<int64_t>(t) * KB;
+        kb_s = static_cast<int>(max(u0, tb) - tb);
+        kb_e = static_cast<int>(min(u1, tb + KB) - tb);
+    }
+};
+
+constexpr int kMaxContrib = 8;  // partial tiles loaded at once by the reducing CTA
+
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_sk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                void* __restrict__ y, unsigned long long* __restrict__ amax, int M, int N, int K,
-               int m_tiles, float* __restrict__ ws_part, int* __restrict__ ws_cnt, int* err) {
+               int m_tiles, float* __restrict__ ws_part, int* __restrict__ ws_cnt, int id_off,
+               int* err) {
     using Cfg = SkCfg<BN>;
     constexpr int ST = Cfg::kStages;
     extern __shared__ uint8_t smem_raw[];
@@ -299,11 +328,16 @@ gemm_sk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int G = gridDim.x, c = blockIdx.x;
-    const int KB = (K + kBK - 1) / kBK;
-    const int64_t U = static_cast<int64_t>(m_tiles) * ((N + kBM - 1) / kBM) * KB;
-    const int64_t u0 = static_cast<int64_t>(c) * U / G, u1 = static_cast<int64_t>(c + 1) * U / G;
-    const int t_first = static_cast<int>(u0 / KB), t_last = static_cast<int>((u1 - 1) / KB);
+    SkWork wk;
+    wk.G = gridDim.x;
+    wk.c = blockIdx.x;
+    wk.KB = (K + kBK - 1) / kBK;
+    wk.T = m_tiles * ((N + kBM - 1) / kBM);
+    wk.dp = wk.T >= wk.G;
+    wk.U = static_cast<int64_t>(wk.T) * wk.KB;
+    wk.u0 = static_cast<int64_t>(wk.c) * wk.U / wk.G;
+    wk.u1 = static_cast<int64_t>(wk.c + 1) * wk.U / wk.G;
+    const int nseg = wk.num_segs();
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < ST; ++s) {
@@ -332,13 +366,18 @@ gemm_sk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
             const uint64_t pol_w = policy_evict_first();
             const uint64_t pol_x = policy_evict_last();
             int i = 0;
-            for (int64_t u = u0; u < u1; ++u, ++i) {
-                const int s = i % ST;
-                if (i >= ST && !mbar_wait(&empty[s], ((i / ST) - 1) & 1, err, 330)) break;
-                const int t = static_cast<int>(u / KB), kb = static_cast<int>(u % KB);
-                mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
-                tma_load_2d_hint(sA + s * kTileA, &tmap_w, &full[s], kb * kBK, (t / m_tiles) * kBM, pol_w);
-                tma_load_2d_hint(sB + s * Cfg::kTileB, &tmap_x, &full[s], kb * kBK, (t % m_tiles) * BN, pol_x);
+            bool ok = true;
+            for (int j = 0; j < nseg && ok; ++j) {
+                int t, kb_s, kb_e;
+                wk.seg(j, t, kb_s, kb_e);
+                const int wrow = (t / m_tiles) * kBM, xrow = (t % m_tiles) * BN;
+                for (int kb = kb_s; kb < kb_e; ++kb, ++i) {
+                    const int s = i % ST;
+                    if (i >= ST && !mbar_wait(&empty[s], ((i / ST) - 1) & 1, err, 330)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
+                    tma_load_2d_hint(sA + s * kTileA, &tmap_w, &full[s], kb * kBK, wrow, pol_w);
+                    tma_load_2d_hint(sB + s * Cfg::kTileB, &tmap_x, &full[s], kb * kBK, xrow, pol_x);
+                }
             }
         }
     } else if (warp == 1) {
@@ -346,10 +385,10 @@ gemm_sk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
             constexpr uint32_t idesc = umma_idesc_bf16(kBM, BN);
             int i = 0;
             bool ok = true;
-            for (int t = t_first, j = 0; t <= t_last && ok; ++t, ++j) {
+            for (int j = 0; j < nseg && ok; ++j) {
+                int t, kb_s, kb_e;
+                wk.seg(j, t, kb_s, kb_e);
                 const int a = j & 1;
-                const int kb_s = static_cast<int>(max(u0, static_cast<int64_t>(t) * KB) - static_cast<int64_t>(t) * KB);
-                const int kb_e = static_cast<int>(min(u1, static_cast<int64_t>(t + 1) * KB) - static_cast<int64_t>(t) * KB);
                 if (j >= 2 && !mbar_wait(&tempty[a], ((j >> 1) - 1) & 1, err, 340)) break;
                 tc_fence_after();
                 const uint32_t acc = tmem + a * BN;
@@ -373,17 +412,16 @@ gemm_sk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         const int warp_q = warp & 3;
         const int row = warp_q * 32 + lane;
         const int et = threadIdx.x - 64;
-        for (int t = t_first, j = 0; t <= t_last; ++t, ++j) {
+        for (int j = 0; j < nseg; ++j) {
+            int t, kb_s, kb_e;
+            wk.seg(j, t, kb_s, kb_e);
             const int a = j & 1;
-            const int64_t tb = static_cast<int64_t>(t) * KB;
-            const int kb_s = static_cast<int>(max(u0, tb) - tb);
-            const int kb_e = static_cast<int>(min(u1, tb + KB) - tb);
             const bool have = mbar_wait(&tfull[a], (j >> 1) & 1, err, 350);
             tc_fence_after();
             const int n_tile = t / m_tiles, m_tile = t % m_tiles;
             const int n = n_tile * kBM + row, m0 = m_tile * BN;
             const uint32_t taddr = tmem + a * BN + (static_cast<uint32_t>(warp_q * 32) << 16);
-            if (kb_s == 0 && kb_e == KB) {
+            if (kb_s == 0 && kb_e == wk.KB) {
 #pragma unroll 1
                 for (int c0 = 0; c0 < BN; c0 += 16) {
                     uint32_t r[16];
@@ -392,15 +430,17 @@ gemm_sk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
                     tmem_ld_wait();
 #pragma unroll
                     for (int q = 0; q < 16; ++q) v[q] = have ? __uint_as_float(r[q]) : 0.f;
-                    epilogue_chunk<EPI>(v, n, N, m0 + c0, M, y, amax, lane, warp_q, n_tile);
+                    epilogue_chunk<EPI>(v, n, N, m0 + c0, M, y, amax, lane, warp_q, n_tile, id_off);
                 }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[a]);
                 continue;
             }
-            // partial tile -> this CTA's slot (0: its first segment, 1: any later one)
-            float* part = ws_part + ((static_cast<int64_t>(c) * 2 + (t == t_first ? 0 : 1)) * kBM + row) * BN;
+            // ---- stream-K partial tile: publish this CTA's part (slot 0: its first segment,
+            // slot 1: its last), count arrivals; the last contributor sums all parts in CTA order
+            const int my_slot = (j == 0) ? 0 : 1;
+            float* part = ws_part + ((static_cast<int64_t>(wk.c) * 2 + my_slot) * kBM + row) * BN;
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 16) {
                 uint32_t r[16];
@@ -413,10 +453,8 @@ gemm_sk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
                                                        __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]))
                                          : make_float4(0.f, 0.f, 0.f, 0.f));
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[a]);  // TMEM buffer free for segment j + 2
-            const int first = sk_cta_of(tb, U, G), last = sk_cta_of(tb + KB - 1, U, G);
+            const int64_t tb = static_cast<int64_t>(t) * wk.KB;
+            const int first = sk_cta_of(tb, wk.U, wk.G), last = sk_cta_of(tb + wk.KB - 1, wk.U, wk.G);
             __threadfence();
             named_bar(1, 128);
             if (et == 0) {
@@ -429,25 +467,54 @@ gemm_sk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
 #pragma unroll 1
                 for (int c0 = 0; c0 < BN; c0 += 16) {
                     float v[16];
+                    {  // own part straight from TMEM
+                        uint32_t r[16];
+                        tmem_ld16(taddr + c0, r);
+                        tmem_ld_wait();
 #pragma unroll
-                    for (int q = 0; q < 16; ++q) v[q] = 0.f;
-                    for (int cc = first; cc <= last; ++cc) {
-                        // contributor cc stored tile t in slot 0 if t is the first tile of its
-                        // range, else in slot 1 (same rule as the writer above)
-                        const int64_t cu0 = static_cast<int64_t>(cc) * U / G;
-                        const int slot = (cu0 / KB == t) ? 0 : 1;
-                        const float4* src = reinterpret_cast<const float4*>(
-                            ws_part + ((static_cast<int64_t>(cc) * 2 + slot) * kBM + row) * BN + c0);
-                        float4 x0 = __ldcg(src), x1 = __ldcg(src + 1), x2 = __ldcg(src + 2), x3 = __ldcg(src + 3);
-                        v[0] += x0.x; v[1] += x0.y; v[2] += x0.z; v[3] += x0.w;
-                        v[4] += x1.x; v[5] += x1.y; v[6] += x1.z; v[7] += x1.w;
-                        v[8] += x2.x; v[9] += x2.y; v[10] += x2.z; v[11] += x2.w;
-                        v[12] += x3.x; v[13] += x3.y; v[14] += x3.z; v[15] += x3.w;
+                        for (int q = 0; q < 16; ++q) v[q] = have ? __uint_as_float(r[q]) : 0.f;
                     }
-                    epilogue_chunk<EPI>(v, n, N, m0 + c0, M, y, amax, lane, warp_q, n_tile);
+                    float acc[16];
+#pragma unroll
+                    for (int q = 0; q < 16; ++q) acc[q] = 0.f;
+                    for (int g0 = first; g0 <= last; g0 += kMaxContrib) {
+                        float4 buf[kMaxContrib][4];
+#pragma unroll
+                        for (int k = 0; k < kMaxContrib; ++k) {  // every load in flight at once
+                            const int cc = g0 + k;
+                            if (cc <= last && cc != wk.c) {
+                                const int slot = (static_cast<int64_t>(cc) * wk.U / wk.G) / wk.KB == t ? 0 : 1;
+                                const float4* src = reinterpret_cast<const float4*>(
+                                    ws_part + ((static_cast<int64_t>(cc) * 2 + slot) * kBM + row) * BN + c0);
+#pragma unroll
+                                for (int q = 0; q < 4; ++q) buf[k][q] = __ldcg(src + q);
+                            }
+                        }
+#pragma unroll
+                        for (int k = 0; k < kMaxContrib; ++k) {  // sum in CTA order
+                            const int cc = g0 + k;
+                            if (cc > last) break;
+                            if (cc == wk.c) {
+#pragma unroll
+                                for (int q = 0; q < 16; ++q) acc[q] += v[q];
+                            } else {
+#pragma unroll
+                                for (int q = 0; q < 4; ++q) {
+                                    acc[4 * q] += buf[k][q].x;
+                                    acc[4 * q + 1] += buf[k][q].y;
+                                    acc[4 * q + 2] += buf[k][q].z;
+                                    acc[4 * q + 3] += buf[k][q].w;
+                                }
+                            }
+                        }
+                    }
+                    epilogue_chunk<EPI>(acc, n, N, m0 + c0, M, y, amax, lane, warp_q, n_tile, id_off);
                 }
                 if (et == 0) ws_cnt[t] = 0;
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[a]);  // TMEM buffer free for segment j + 2
         }
         tc_fence_before();
     }
@@ -518,7 +585,7 @@ GemmPlan plan_gemm(int M, int N, int K) {
 template <int BN, int EPI, bool GROUPED = false>
 int launch_bn(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& tx, void* y,
               unsigned long long* amax, int M, int N, int K, void* ws, cudaStream_t stream,
-              GroupArgs grp = GroupArgs{}) {
+              GroupArgs grp = GroupArgs{}, int id_off = 0) {
     using Cfg = GemmCfg<BN>;
     int* err = device_error_word();
     if (!err) return set_error(MSGL_ERR_CUDA, "device error word unavailable");
@@ -529,14 +596,14 @@ int launch_bn(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& tx, v
     gemm_kernel<BN, EPI, GROUPED><<<grid, kGemmThreads, Cfg::kSmem, stream>>>(
         tw, tx, y, amax, M, N, K, p.kb_per_split, p.splits,
         p.splits > 1 ? reinterpret_cast<float*>(w8 + kCounterBytes) : nullptr,
-        p.splits > 1 ? reinterpret_cast<int*>(w8 + p.ws_cnt_off) : nullptr, grp, err);
+        p.splits > 1 ? reinterpret_cast<int*>(w8 + p.ws_cnt_off) : nullptr, grp, id_off, err);
     MSGL_LAUNCH_CHECK();
     return MSGL_OK;
 }
 
 template <int BN, int EPI>
 int launch_sk(const CUtensorMap& tw, const CUtensorMap& tx, void* y, unsigned long long* amax,
-              int M, int N, int K, void* ws, int sms, cudaStream_t stream) {
+              int M, int N, int K, void* ws, int sms, cudaStream_t stream, int id_off = 0) {
     using Cfg = SkCfg<BN>;
     int* err = device_error_word();
     if (!err) return set_error(MSGL_ERR_CUDA, "device error word unavailable");
@@ -548,14 +615,14 @@ int launch_sk(const CUtensorMap& tw, const CUtensorMap& tx, void* y, unsigned lo
     uint8_t* w8 = static_cast<uint8_t*>(ws);
     gemm_sk_kernel<BN, EPI><<<G, kGemmThreads, Cfg::kSmem, stream>>>(
         tw, tx, y, amax, M, N, K, m_tiles, reinterpret_cast<float*>(w8 + kCounterBytes),
-        reinterpret_cast<int*>(w8), err);
+        reinterpret_cast<int*>(w8), id_off, err);
     MSGL_LAUNCH_CHECK();
     return MSGL_OK;
 }
 
 template <int EPI>
 int run_gemm(const void* x, const void* w, void* y, unsigned long long* amax, int M, int N, int K,
-             void* ws, size_t ws_bytes, cudaStream_t stream) {
+             void* ws, size_t ws_bytes, cudaStream_t stream, int id_off = 0) {
     if (M < 0 || N <= 0 || K <= 0) return set_error(MSGL_ERR_INVALID_ARG, "gemm: bad sizes");
     if (K % 8) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "gemm: K must be a multiple of 8");
     if (M == 0) return MSGL_OK;
@@ -572,11 +639,11 @@ int run_gemm(const void* x, const void* w, void* y, unsigned long long* amax, in
         if (!ws || ws_bytes < sk_workspace_bytes(bn, sms))
             return set_error(MSGL_ERR_WORKSPACE, "gemm: workspace too small");
         switch (bn) {
-            case 16: return launch_sk<16, EPI>(tw, tx, y, amax, M, N, K, ws, sms, stream);
-            case 32: return launch_sk<32, EPI>(tw, tx, y, amax, M, N, K, ws, sms, stream);
-            case 64: return launch_sk<64, EPI>(tw, tx, y, amax, M, N, K, ws, sms, stream);
-            case 128: return launch_sk<128, EPI>(tw, tx, y, amax, M, N, K, ws, sms, stream);
-            default: return launch_sk<256, EPI>(tw, tx, y, amax, M, N, K, ws, sms, stream);
+            case 16: return launch_sk<16, EPI>(tw, tx, y, amax, M, N, K, ws, sms, stream, id_off);
+            case 32: return launch_sk<32, EPI>(tw, tx, y, amax, M, N, K, ws, sms, stream, id_off);
+            case 64: return launch_sk<64, EPI>(tw, tx, y, amax, M, N, K, ws, sms, stream, id_off);
+            case 128: return launch_sk<128, EPI>(tw, tx, y, amax, M, N, K, ws, sms, stream, id_off);
+            default: return launch_sk<256, EPI>(tw, tx, y, amax, M, N, K, ws, sms, stream, id_off);
         }
     }
     // very large grids: one CTA per tile, no K split, no workspace
@@ -584,11 +651,11 @@ int run_gemm(const void* x, const void* w, void* y, unsigned long long* amax, in
     p.splits = 1;
     p.kb_per_split = (K + kBK - 1) / kBK;
     switch (p.bn) {
-        case 16: return launch_bn<16, EPI>(p, tw, tx, y, amax, M, N, K, ws, stream);
-        case 32: return launch_bn<32, EPI>(p, tw, tx, y, amax, M, N, K, ws, stream);
-        case 64: return launch_bn<64, EPI>(p, tw, tx, y, amax, M, N, K, ws, stream);
-        case 128: return launch_bn<128, EPI>(p, tw, tx, y, amax, M, N, K, ws, stream);
-        default: return launch_bn<256, EPI>(p, tw, tx, y, amax, M, N, K, ws, stream);
+        case 16: return launch_bn<16, EPI>(p, tw, tx, y, amax, M, N, K, ws, stream, GroupArgs{}, id_off);
+        case 32: return launch_bn<32, EPI>(p, tw, tx, y, amax, M, N, K, ws, stream, GroupArgs{}, id_off);
+        case 64: return launch_bn<64, EPI>(p, tw, tx, y, amax, M, N, K, ws, stream, GroupArgs{}, id_off);
+        case 128: return launch_bn<128, EPI>(p, tw, tx, y, amax, M, N, K, ws, stream, GroupArgs{}, id_off);
+        default: return launch_bn<256, EPI>(p, tw, tx, y, amax, M, N, K, ws, stream, GroupArgs{}, id_off);
     }
 }
 
@@ -778,6 +845,18 @@ int msgl_lm_head_argmax(const void* x, const void* w, int M, int vocab, int K,
     unpack_argmax_kernel<<<(M + 255) / 256, 256, 0, stream>>>(packed, ids, M);
     MSGL_LAUNCH_CHECK();
     return MSGL_OK;
+}
+
+int msgl_lm_head_argmax_partial(const void* x, const void* w, int M, int vocab_local, int K,
+                                int vocab_offset, unsigned long long* packed, void* workspace,
+                                size_t workspace_bytes, msgl_stream_t stream) {
+    if (M <= 0) return M == 0 ? MSGL_OK : set_error(MSGL_ERR_INVALID_ARG, "lm_head: M < 0");
+    if (vocab_offset < 0) return set_error(MSGL_ERR_INVALID_ARG, "lm_head: vocab_offset < 0");
+    if (cudaMemsetAsync(packed, 0, static_cast<size_t>(M) * sizeof(unsigned long long), stream) !=
+        cudaSuccess)
+        return set_error(MSGL_ERR_CUDA, "lm_head: memset failed");
+    return run_gemm<EPI_ARGMAX>(x, w, nullptr, packed, M, vocab_local, K, workspace,
+                                workspace_bytes, stream, vocab_offset);
 }
 
 int msgl_argmax(const void* logits, int num_rows, int vocab, int dtype, int* out,

@@ -45,6 +45,8 @@ struct Model {
     msgl_model_config cfg{};
     int hq = 0, hkv = 0, inter = 0, vocab_l = 0;  // this rank's shard
     int kv_head0 = 0;                              // first global kv head held by this rank
+    int vocab0 = 0;                                // first lm_head row (token id) of this rank
+    msgl_tp* tp = nullptr;                         // communicator (tp_size > 1), not owned
     std::vector<Qwen3DecoderLayer> layers;
     DevBuf embed;        // [V, H]
     RMSNorm norm;        // final norm
@@ -102,20 +104,24 @@ static void validate(const msgl_model_config& c) {
     } else if (c.inter % c.tp_size || (c.inter / c.tp_size) % 16) {
         bad("model: inter / tp must be a multiple of 16");
     }
-    if (c.tp_size > 1) throw Fail(MSGL_ERR_UNSUPPORTED_SHAPE, "model: tensor parallel needs msgl_tp (not built yet)");
 }
 
 static void create(Model& m, const msgl_model_config& c) {
     validate(c);
     m.cfg = c;
     const int tp = c.tp_size, D = c.head_dim, H = c.hidden;
-    m.hq = c.num_q_heads / tp;
-    m.hkv = c.num_kv_heads >= tp ? c.num_kv_heads / tp : 1;
-    m.kv_head0 = c.num_kv_heads >= tp ? c.tp_rank * m.hkv
-                                      : (c.tp_rank * m.hq) / (c.num_q_heads / c.num_kv_heads);
+    int plan[8];
+    ck(msgl_tp_shard_plan(c.num_q_heads, c.num_kv_heads,
+                          c.num_experts > 0 ? c.moe_inter : c.inter, c.vocab, c.tp_rank, tp, plan),
+       "model: tensor-parallel shard");
+    m.hq = plan[1];
+    m.kv_head0 = plan[2];
+    m.hkv = plan[3];
     m.inter = c.num_experts > 0 ? 0 : c.inter / tp;
     m.moe_inter = c.num_experts > 0 ? c.moe_inter / tp : 0;
-    m.vocab_l = c.vocab;  // vocab-parallel lm_head arrives with TP
+    m.vocab0 = plan[6];
+    m.vocab_l = plan[7];
+    if (m.vocab_l <= 0) throw Fail(MSGL_ERR_INVALID_ARG, "model: empty vocab shard");
     m.layers.resize(c.num_layers);
     cudaStream_t s = nullptr;
     for (auto& L : m.layers) {
@@ -261,7 +267,7 @@ static void set_weight(Model& m, const std::string& name, const bf16_t* h, int64
     };
     if (name == "embed") { need(c.vocab * H); upload_block(m.embed.p, h, H, 0, c.vocab, 0, H, s); }
     else if (name == "norm") { need(H); upload_block(m.norm.weight.p, h, H, 0, 1, 0, H, s); }
-    else if (name == "lm_head") { need(c.vocab * H); upload_block(m.lm_head.weight.p, h, H, 0, m.vocab_l, 0, H, s); }
+    else if (name == "lm_head") { need(c.vocab * H); upload_block(m.lm_head.weight.p, h, H, m.vocab0, m.vocab_l, 0, H, s); }
     else if (name.rfind("layers.", 0) == 0) {
         size_t dot = name.find('.', 7);
         int l = std::stoi(name.substr(7, dot - 7));
@@ -360,6 +366,7 @@ static void forward(Model& m, const msgl_batch& b, int* next_tokens, float* logi
     if (b.max_seq_len > c.max_position)
         throw Fail(MSGL_ERR_INVALID_ARG, "forward: max_seq_len exceeds max_position");
     if (m.num_slots == 0) throw Fail(MSGL_ERR_INVALID_ARG, "forward: KV pools not allocated");
+    if (c.tp_size > 1 && !m.tp) throw Fail(MSGL_ERR_INVALID_ARG, "forward: tp_size > 1 needs msgl_model_set_tp");
     const int T = b.num_tokens, H = c.hidden;
     auto* x = m.x.as<bf16_t>();
     float* res = m.residual.as<float>();
@@ -378,13 +385,19 @@ static void forward(Model& m, const msgl_batch& b, int* next_tokens, float* logi
         L.attn.forward(m.q.as<bf16_t>(), L.k_pool.p, L.v_pool.p, m.num_slots, b,
                        m.attn_out.as<bf16_t>(), m.scratch, s);                // :51-52
         L.o_proj.forward(m.attn_out.as<bf16_t>(), x, T, m.scratch, s);       // :55
-        L.post_attention_layernorm.forward_fused_add(x, res, T, false, s);   // :57
+        if (m.tp)  // row-parallel o_proj: all-reduce fused with the add + norm of :57
+            ck(msgl_tp_allreduce_add_rmsnorm(m.tp, x, res, L.post_attention_layernorm.weight.p, T, H,
+                                             c.eps, 0, s), "o_proj all-reduce");
+        else
+            L.post_attention_layernorm.forward_fused_add(x, res, T, false, s);  // :57
         if (c.num_experts > 0) {
             L.moe.forward(x, x, T, m.moe_scratch, m.scratch, s);              // qwen3_moe.cpp:62-111
         } else {
             L.gate_up_proj.forward(x, m.act.as<bf16_t>(), T, m.scratch, s);  // :60-79
             L.down_proj.forward(m.act.as<bf16_t>(), x, T, m.scratch, s);     // :80
         }
+        if (m.tp)  // row-parallel down_proj / expert combine: partial sums over the ranks
+            ck(msgl_tp_all_reduce_sum(m.tp, x, static_cast<int64_t>(T) * H, s), "mlp all-reduce");
     }
     // final norm on each request's last row (qwen3.cpp:177, sampling row of D10), lm_head +
     // greedy argmax (scheduler.cpp:117-124)
@@ -398,6 +411,15 @@ static void forward(Model& m, const msgl_batch& b, int* next_tokens, float* logi
         rl = m.res_last.as<float>();
     }
     m.norm.forward_fused_add(xl, rl, B, false, s);
+    if (m.tp) {  // vocab-parallel lm_head: local best (logit, id), max over the ranks
+        if (logits) throw Fail(MSGL_ERR_UNSUPPORTED_SHAPE, "forward: logits output needs tp_size 1");
+        ck(msgl_lm_head_argmax_partial(xl, m.lm_head.weight.p, B, m.vocab_l, H, m.vocab0,
+                                       m.packed.as<unsigned long long>(), m.scratch.gemm_ws,
+                                       m.scratch.gemm_ws_bytes, s), "lm_head");
+        ck(msgl_tp_argmax_combine(m.tp, m.packed.as<unsigned long long>(), next_tokens, B, s),
+           "argmax over ranks");
+        return;
+    }
     ck(msgl_lm_head_argmax(xl, m.lm_head.weight.p, B, m.vocab_l, H,
                            m.packed.as<unsigned long long>(), next_tokens, m.scratch.gemm_ws,
                            m.scratch.gemm_ws_bytes, s),
@@ -570,6 +592,15 @@ int msgl_model_debug_hidden(msgl_model* m, void** x, float** residual) {
     if (!m) return msgl::set_error(MSGL_ERR_INVALID_ARG, "null model");
     if (x) *x = m->m.x.p;
     if (residual) *residual = m->m.residual.as<float>();
+    return MSGL_OK;
+}
+
+int msgl_model_set_tp(msgl_model* m, msgl_tp* tp) {
+    if (!m) return msgl::set_error(MSGL_ERR_INVALID_ARG, "null model");
+    const int world = tp ? msgl_tp_world(tp) : 1;
+    if (world != m->m.cfg.tp_size || (tp && msgl_tp_rank(tp) != m->m.cfg.tp_rank))
+        return msgl::set_error(MSGL_ERR_INVALID_ARG, "set_tp: communicator rank/world differ from the config");
+    m->m.tp = world > 1 ? tp : nullptr;
     return MSGL_OK;
 }
 

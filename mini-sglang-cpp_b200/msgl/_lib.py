@@ -40,6 +40,17 @@ SIGNATURES = {
     "msgl_grouped_gemm_bf16": (I, [P, P, P, P, I, I, I, I, P, SZ, P]),
     "msgl_grouped_gemm_gate_up_silu": (I, [P, P, P, P, I, I, I, I, P, SZ, P]),
     "msgl_moe_combine": (I, [P, P, P, I, I, I, P, P]),
+    "msgl_lm_head_argmax_partial": (I, [P, P, I, I, I, I, P, P, SZ, P]),
+    "msgl_tp_unique_id_size": (SZ, []),
+    "msgl_tp_get_unique_id": (I, [P]),
+    "msgl_tp_init": (I, [I, I, P, P]),
+    "msgl_tp_destroy": (I, [P]),
+    "msgl_tp_rank": (I, [P]),
+    "msgl_tp_world": (I, [P]),
+    "msgl_tp_all_reduce_sum": (I, [P, P, I64, P]),
+    "msgl_tp_allreduce_add_rmsnorm": (I, [P, P, P, P, I, I, F, I, P]),
+    "msgl_tp_argmax_combine": (I, [P, P, P, I, P]),
+    "msgl_tp_shard_plan": (I, [I, I, I, I, I, I, P]),
     # executor (msgl_engine.h)
     "msgl_model_create": (I, [P, P]),
     "msgl_model_destroy": (I, [P]),
@@ -52,6 +63,7 @@ SIGNATURES = {
     "msgl_model_step_host": (I, [P, P, P, I, P]),
     "msgl_model_debug_hidden": (I, [P, P, P]),
     "msgl_model_set_num_layers_run": (I, [P, I]),
+    "msgl_model_set_tp": (I, [P, P]),
 }
 
 _LIB = None

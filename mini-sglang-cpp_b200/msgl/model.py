@@ -199,6 +199,10 @@ class Qwen3Model:
                                         None if lg is None else lg.data_ptr(), int(graph), _s()))
         return (nxt, lg) if logits else nxt
 
+    def set_tp(self, comm):
+        self.tp = comm
+        check(self.L.msgl_model_set_tp(self.h, comm.h if comm is not None else None))
+
     def set_num_layers_run(self, n: int):
         check(self.L.msgl_model_set_num_layers_run(self.h, n))
 
@@ -206,3 +210,37 @@ class Qwen3Model:
         x, r = C.c_void_p(), C.c_void_p()
         check(self.L.msgl_model_debug_hidden(self.h, C.addressof(x), C.addressof(r)))
         return x.value, r.value
+
+
+# ---------------------------------------------------------------------------- tensor parallel
+class TPComm:
+    """msgl_tp (NCCL) of this rank. `unique_id` comes from rank 0's `TPComm.new_unique_id()` and
+    reaches the other ranks through the launcher (torch.distributed broadcast in the bench)."""
+
+    def __init__(self, rank: int, world: int, unique_id: bytes):
+        self.L = lib()
+        buf = C.create_string_buffer(unique_id, len(unique_id))
+        h = C.c_void_p()
+        check(self.L.msgl_tp_init(rank, world, buf, C.addressof(h)))
+        self.h, self.rank, self.world = h, rank, world
+
+    @staticmethod
+    def new_unique_id() -> bytes:
+        L = lib()
+        n = L.msgl_tp_unique_id_size()
+        buf = C.create_string_buffer(n)
+        check(L.msgl_tp_get_unique_id(buf))
+        return buf.raw
+
+    def close(self):
+        if getattr(self, "h", None) is not None and self.h.value:
+            self.L.msgl_tp_destroy(self.h)
+            self.h = None
+
+
+def shard_plan(num_q_heads, num_kv_heads, inter, vocab, rank, world):
+    """msgl_tp_shard_plan as a dict (host only)."""
+    out = (C.c_int * 8)()
+    check(lib().msgl_tp_shard_plan(num_q_heads, num_kv_heads, inter, vocab, rank, world, out))
+    keys = ("q_head0", "q_heads", "kv_head0", "kv_heads", "inter0", "inter_cols", "vocab0", "vocab_rows")
+    return dict(zip(keys, list(out)))
