@@ -419,6 +419,8 @@ def run_case(args):
     torch.cuda.set_device(0)
     dev = torch.device("cuda", 0)
     hq, hkv, H, I = CFG8B["num_q_heads"], CFG8B["num_kv_heads"], CFG8B["hidden"], CFG8B["inter"]
+    if args.case == "breakdown":
+        return run_breakdown(args, dev)
     if args.case == "attention":
         num_pages, pt = build_pages()
         kp = torch.empty(num_pages * PAGE, hkv * 128, dtype=torch.bfloat16, device=dev)
@@ -444,13 +446,81 @@ def run_case(args):
     return 0
 
 
+def run_breakdown(args, dev):
+    """Each kernel of the decode step timed alone with CUDA events at the bench's shapes (one
+    layer; weight copies rotated so every launch streams its weights from HBM, as in the step).
+    Prints one JSON line: per kernel the mean launch time and achieved GB/s."""
+    import torch
+
+    from msgl import ops
+    hq, hkv, H, I, V = (CFG8B[k] for k in ("num_q_heads", "num_kv_heads", "hidden", "inter", "vocab"))
+    res = {}
+
+    def timed(name, fns, nbytes, reps=None):
+        reps = reps or max(args.steps, 10)
+        for f in fns:
+            f()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(reps):
+            fns[i % len(fns)]()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1000 / reps
+        res[name] = {"us": round(us, 2), "GB/s": round(nbytes / (us * 1e-6) / 1e9, 1)}
+
+    x = ops.fill_normal_(torch.empty(BATCH, H, dtype=torch.bfloat16, device=dev), seed=1)
+    act = ops.fill_normal_(torch.empty(BATCH, I, dtype=torch.bfloat16, device=dev), seed=2)
+    attn_in = ops.fill_normal_(torch.empty(BATCH, hq * 128, dtype=torch.bfloat16, device=dev), seed=3)
+    for name, (n, k, inp, kind) in {"qkv": ((hq + 2 * hkv) * 128, H, x, "bf16"),
+                                    "o_proj": (H, hq * 128, attn_in, "bf16"),
+                                    "gate_up_silu": (2 * I, H, x, "silu"),
+                                    "down": (H, I, act, "bf16")}.items():
+        copies = max(1, -(-400_000_000 // (n * k * 2)))  # > 3x the 126 MB L2 in total
+        ws = [ops.fill_normal_(torch.empty(n, k, dtype=torch.bfloat16, device=dev), seed=10 + i,
+                               std=0.02) for i in range(copies)]
+        gws = ops.gemm_workspace(BATCH, n, k, dev)
+        if kind == "silu":
+            fns = [lambda w=w: ops.gate_up_silu(inp, w, workspace=gws) for w in ws]
+        else:
+            fns = [lambda w=w: ops.linear(inp, w, workspace=gws) for w in ws]
+        timed(name, fns, n * k * 2)
+        del ws
+    wl = ops.fill_normal_(torch.empty(V, H, dtype=torch.bfloat16, device=dev), seed=20, std=0.02)
+    lws = ops.gemm_workspace(BATCH, V, H, dev)
+    timed("lm_head_argmax", [lambda: ops.lm_head_argmax(x, wl, workspace=lws)], V * H * 2)
+    del wl
+    num_pages, pt = build_pages()
+    kp = torch.empty(num_pages * PAGE, hkv * 128, dtype=torch.bfloat16, device=dev)
+    vp = torch.empty_like(kp)
+    ops.fill_normal_(kp, seed=4, stream_id=0)
+    ops.fill_normal_(vp, seed=4, stream_id=1)
+    q = ops.fill_normal_(torch.empty(BATCH, hq, 128, dtype=torch.bfloat16, device=dev), seed=5)
+    ptd = torch.from_numpy(pt).to(dev)
+    seq = torch.full((BATCH,), CTX, dtype=torch.int32, device=dev)
+    aws = ops.attention_workspace(BATCH, CTX, hq, hkv, dev)
+    unique = (PREFIX + BATCH * (CTX - PREFIX)) * hkv * 128 * 4
+    timed("paged_decode", [lambda: ops.paged_attention_decode(q, kp, vp, ptd, seq, CTX, hq, hkv,
+                                                               workspace=aws)], unique)
+    r = torch.zeros(BATCH, H, dtype=torch.float32, device=dev)
+    nw = torch.ones(H, dtype=torch.bfloat16, device=dev)
+    timed("add_rmsnorm", [lambda: ops.add_rmsnorm_(x, r, nw, 1e-6)], BATCH * H * 12)
+    peak = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))).get("hbm_gbs", 6650.0) \
+        if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else 6650.0
+    for v in res.values():
+        v["frac_hbm"] = round(v["GB/s"] / peak, 3)
+    print(json.dumps({"case": "breakdown", "kernels": res}), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--case", choices=["attention", "gemm"], default=None,
+    ap.add_argument("--case", choices=["attention", "gemm", "breakdown"], default=None,
                     help="run one kernel of the step on a small single-layer case (profiling)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))

@@ -144,8 +144,16 @@ __device__ __forceinline__ void store_bf16x8(__nv_bfloat16* dst, const float (&v
 }
 
 // ------------------------------------------------------------------------------ decode
-// grid (max_chunks, Hkv, B); block 160 = 4 consumer warps + 1 TMA producer warp.
-__global__ void __launch_bounds__(kThreads)
+// grid (max_chunks, B); block 288 = 8 consumer warps + 1 TMA producer warp. One CTA covers a
+// request's chunk of pages for ALL kv heads, so each page is fetched as whole token rows
+// (16 rows x Hkv * 256 B, contiguous in the token-major pool) rather than one kv head's 256 B
+// slice of each row. A stage holds kDecPPS = 8 / Hkv pages; warp w attends kv head w % Hkv on
+// page w / Hkv of the stage, so every consumer warp does one (page, head) per stage.
+constexpr int kDecWarps = 8;
+constexpr int kDecThreads = (kDecWarps + 1) * 32;
+constexpr int kDecStageBytes = kDecWarps * kPageSlotBytes;  // 64 KB: 8 (page, head) slots
+
+__global__ void __launch_bounds__(kDecThreads, 1)
 paged_decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                     const __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ out,
                     const int* __restrict__ page_table, int max_pages,
@@ -154,12 +162,14 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
                     float* __restrict__ ws_ml, int* __restrict__ ws_cnt, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = align1024(smem_raw);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDecodeStages * 4 * kPageSlotBytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDecodeStages * kDecStageBytes);
     uint64_t* empty = full + kDecodeStages;
     int* flag = reinterpret_cast<int*>(empty + kDecodeStages);
+    int* pages = flag + 4;  // [chunk_pages <= kMaxChunkPages]
 
-    const int b = blockIdx.z, kvh = blockIdx.y, chunk = blockIdx.x;
+    const int b = blockIdx.y, chunk = blockIdx.x;
     const int group = hq / hkv;
+    const int pps = kDecWarps / hkv;  // pages per stage
     int L = seq_lens[b];
     if (L < 0 || L > max_pages * kPage) {  // context longer than the page-table row
         if (threadIdx.x == 0 && chunk == 0) record_error(err, MSGL_ERR_BOUNDS, 202);
@@ -169,33 +179,30 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (npages == 0) {  // empty context: output zeros (chunk 0 only)
-        if (chunk == 0 && threadIdx.x < group * 16) {
-            float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-            int row = threadIdx.x >> 4, d0 = (threadIdx.x & 15) * 8;
-            store_bf16x8(out + (static_cast<int64_t>(b) * hq + kvh * group + row) * kHd + d0, z);
-        }
+        if (chunk == 0)
+            for (int i = threadIdx.x; i < hq * 16; i += blockDim.x) {
+                float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                store_bf16x8(out + (static_cast<int64_t>(b) * hq + (i >> 4)) * kHd + (i & 15) * 8, z);
+            }
         return;
     }
     const int p0 = chunk * chunk_pages;
     if (p0 >= npages) return;
     const int np = min(npages - p0, chunk_pages);
     const int nchunks = (npages + chunk_pages - 1) / chunk_pages;
-    const int nsteps = (np + 3) / 4;
+    const int nsteps = (np + pps - 1) / pps;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kDecodeStages; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kConsumerWarps);
+            mbar_init(&empty[s], kDecWarps);
         }
         fence_barrier_init();
     }
     __syncthreads();
 
-    if (warp == kConsumerWarps) {
-        // ---------------- TMA producer
-        // The chunk's page ids come into shared memory in one coalesced warp load, so no TMA
-        // issue waits on a dependent global read of the page table.
-        int* pages = flag + 4;  // [chunk_pages <= kMaxChunkPages]
+    if (warp == kDecWarps) {
+        // ---------------- TMA producer: page ids staged in shared memory first
         const int* pt = page_table + static_cast<int64_t>(b) * max_pages + p0;
         for (int i = lane; i < np; i += 32) {
             int page = pt[i];
@@ -214,22 +221,26 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
                 if (it >= kDecodeStages &&
                     !mbar_wait(&empty[s], ((it / kDecodeStages) - 1) & 1, err, 200))
                     break;
-                const int cnt = min(4, np - it * 4);
-                mbar_arrive_expect_tx(&full[s], cnt * kPageSlotBytes);
-                for (int p = 0; p < cnt; ++p)
-                    issue_page(smem + (s * 4 + p) * kPageSlotBytes, &tk, &tv, &full[s], kvh,
-                               pages[it * 4 + p]);
+                const int cnt = min(pps, np - it * pps);
+                mbar_arrive_expect_tx(&full[s], cnt * hkv * kPageSlotBytes);
+                for (int p = 0; p < cnt; ++p) {
+                    const int page = pages[it * pps + p];
+                    for (int h = 0; h < hkv; ++h)  // all heads of the page back to back
+                        issue_page(smem + s * kDecStageBytes + (p * hkv + h) * kPageSlotBytes, &tk,
+                                   &tv, &full[s], h, page);
+                }
             }
         }
         return;
     }
 
-    // ---------------- consumers
+    // ---------------- consumers: kv head `head`, page `psub` of every stage
+    const int head = warp % hkv, psub = warp / hkv;
     const int g = lane >> 2, c = lane & 3;
     uint32_t qa[8][4];
     {
         const bool real = g < group;
-        const __nv_bfloat16* qr = q + (static_cast<int64_t>(b) * hq + kvh * group + (real ? g : 0)) * kHd;
+        const __nv_bfloat16* qr = q + (static_cast<int64_t>(b) * hq + head * group + (real ? g : 0)) * kHd;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
             qa[kk][0] = real ? *reinterpret_cast<const uint32_t*>(qr + 16 * kk + 2 * c) : 0u;
@@ -246,9 +257,10 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
     for (int it = 0; it < nsteps; ++it) {
         const int s = it % kDecodeStages;
         if (!mbar_wait(&full[s], (it / kDecodeStages) & 1, err, 210)) break;
-        const int pidx = it * 4 + warp;
+        const int pidx = it * pps + psub;
         if (pidx < np) {
-            uint32_t base = smem_u32(smem + (s * 4 + warp) * kPageSlotBytes);
+            const uint32_t base =
+                smem_u32(smem + s * kDecStageBytes + (psub * hkv + head) * kPageSlotBytes);
             attend_page<false>(base, base + 4096, qa, o, m, l, (p0 + pidx) * kPage, L - 1, -1,
                                sl2e, lane);
         }
@@ -256,14 +268,14 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
         if (lane == 0) mbar_arrive(&empty[s]);
     }
 
-    // ---------------- merge the four warps (shared memory aliases the drained stage ring)
+    // ---------------- combine the pps warps of each head (shared memory over the drained ring)
     float lsum = l[0];
     lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
     lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);
-    named_bar_sync(1, kConsumerWarps * 32);
-    float* mo = reinterpret_cast<float*>(smem);      // [4][8][128]
-    float* mm = mo + kConsumerWarps * 8 * kHd;        // [4][8]
-    float* ml = mm + kConsumerWarps * 8;              // [4][8]
+    named_bar_sync(1, kDecWarps * 32);
+    float* mo = reinterpret_cast<float*>(smem);      // [8 warps][8 rows][128]
+    float* mm = mo + kDecWarps * 8 * kHd;             // [8][8]
+    float* ml = mm + kDecWarps * 8;                   // [8][8]
     if (g < group) {
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -275,34 +287,34 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
             ml[warp * 8 + g] = lsum;
         }
     }
-    named_bar_sync(1, kConsumerWarps * 32);
+    named_bar_sync(1, kDecWarps * 32);
 
-    const int row = threadIdx.x >> 4, d0 = (threadIdx.x & 15) * 8;
-    const int head = kvh * group + row;
-    if (row < group) {
+    // items: (q head qh in [0, hq), 8-wide d chunk) over the 256 consumer threads
+    for (int item = threadIdx.x; item < hq * 16; item += kDecWarps * 32) {
+        const int qh = item >> 4, d0 = (item & 15) * 8;
+        const int h = qh / group, r = qh % group;
         float M = kNegInf;
-#pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, mm[w * 8 + row]);
+        for (int ps = 0; ps < pps; ++ps) M = fmaxf(M, mm[(ps * hkv + h) * 8 + r]);
         float O[8] = {0, 0, 0, 0, 0, 0, 0, 0}, Ls = 0.f;
+        for (int ps = 0; ps < pps; ++ps) {
+            const int w = ps * hkv + h;
+            const float mw = mm[w * 8 + r];
+            const float sc = (mw == kNegInf) ? 0.f : exp2f(mw - M);
+            Ls += ml[w * 8 + r] * sc;
 #pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) {
-            float mw = mm[w * 8 + row];
-            float sc = (mw == kNegInf) ? 0.f : exp2f(mw - M);
-            Ls += ml[w * 8 + row] * sc;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) O[e] += mo[(w * 8 + row) * kHd + d0 + e] * sc;
+            for (int e = 0; e < 8; ++e) O[e] += mo[(w * 8 + r) * kHd + d0 + e] * sc;
         }
         if (nchunks == 1) {
-            float inv = Ls > 0.f ? 1.f / Ls : 0.f;
+            const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
 #pragma unroll
             for (int e = 0; e < 8; ++e) O[e] *= inv;
-            store_bf16x8(out + (static_cast<int64_t>(b) * hq + head) * kHd + d0, O);
+            store_bf16x8(out + (static_cast<int64_t>(b) * hq + qh) * kHd + d0, O);
         } else {
-            int64_t pi = (static_cast<int64_t>(b) * max_chunks + chunk) * hq + head;
+            const int64_t pi = (static_cast<int64_t>(b) * max_chunks + chunk) * hq + qh;
             float4* dst = reinterpret_cast<float4*>(ws_o + pi * kHd + d0);
             dst[0] = make_float4(O[0], O[1], O[2], O[3]);
             dst[1] = make_float4(O[4], O[5], O[6], O[7]);
-            if ((threadIdx.x & 15) == 0) {
+            if ((item & 15) == 0) {
                 ws_ml[pi * 2] = M;
                 ws_ml[pi * 2 + 1] = Ls;
             }
@@ -310,39 +322,38 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
     }
     if (nchunks == 1) return;
 
-    // ---------------- split-KV: the last chunk CTA of (b, kvh) merges all chunks
+    // ---------------- split-KV: the last chunk CTA of request b merges all chunks
     __threadfence();
-    named_bar_sync(1, kConsumerWarps * 32);
+    named_bar_sync(1, kDecWarps * 32);
     if (threadIdx.x == 0) {
-        int old = atomicAdd(&ws_cnt[b * hkv + kvh], 1);
+        const int old = atomicAdd(&ws_cnt[b], 1);
         *flag = (old == nchunks - 1);
     }
-    named_bar_sync(1, kConsumerWarps * 32);
+    named_bar_sync(1, kDecWarps * 32);
     if (!*flag) return;
     __threadfence();
-    if (row < group) {
+    for (int item = threadIdx.x; item < hq * 16; item += kDecWarps * 32) {
+        const int qh = item >> 4, d0 = (item & 15) * 8;
         float M = kNegInf;
-        for (int ch = 0; ch < nchunks; ++ch) {
-            int64_t pi = (static_cast<int64_t>(b) * max_chunks + ch) * hq + head;
-            M = fmaxf(M, __ldcg(ws_ml + pi * 2));
-        }
+        for (int ch = 0; ch < nchunks; ++ch)
+            M = fmaxf(M, __ldcg(ws_ml + ((static_cast<int64_t>(b) * max_chunks + ch) * hq + qh) * 2));
         float O[8] = {0, 0, 0, 0, 0, 0, 0, 0}, Ls = 0.f;
         for (int ch = 0; ch < nchunks; ++ch) {
-            int64_t pi = (static_cast<int64_t>(b) * max_chunks + ch) * hq + head;
-            float mc = __ldcg(ws_ml + pi * 2);
-            float sc = (mc == kNegInf) ? 0.f : exp2f(mc - M);
+            const int64_t pi = (static_cast<int64_t>(b) * max_chunks + ch) * hq + qh;
+            const float mc = __ldcg(ws_ml + pi * 2);
+            const float sc = (mc == kNegInf) ? 0.f : exp2f(mc - M);
             Ls += __ldcg(ws_ml + pi * 2 + 1) * sc;
             const float4* src = reinterpret_cast<const float4*>(ws_o + pi * kHd + d0);
-            float4 a = __ldcg(src), bq = __ldcg(src + 1);
-            O[0] += a.x * sc; O[1] += a.y * sc; O[2] += a.z * sc; O[3] += a.w * sc;
-            O[4] += bq.x * sc; O[5] += bq.y * sc; O[6] += bq.z * sc; O[7] += bq.w * sc;
+            const float4 x0 = __ldcg(src), x1 = __ldcg(src + 1);
+            O[0] += x0.x * sc; O[1] += x0.y * sc; O[2] += x0.z * sc; O[3] += x0.w * sc;
+            O[4] += x1.x * sc; O[5] += x1.y * sc; O[6] += x1.z * sc; O[7] += x1.w * sc;
         }
-        float inv = Ls > 0.f ? 1.f / Ls : 0.f;
+        const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
 #pragma unroll
         for (int e = 0; e < 8; ++e) O[e] *= inv;
-        store_bf16x8(out + (static_cast<int64_t>(b) * hq + head) * kHd + d0, O);
+        store_bf16x8(out + (static_cast<int64_t>(b) * hq + qh) * kHd + d0, O);
     }
-    if (threadIdx.x == 0) ws_cnt[b * hkv + kvh] = 0;
+    if (threadIdx.x == 0) ws_cnt[b] = 0;
 }
 
 // ------------------------------------------------------------------------------ extend
@@ -484,7 +495,7 @@ paged_extend_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
 }
 
 // ------------------------------------------------------------------------------ host side
-constexpr size_t kDecodeCounterBytes = 262144;  // one int per (request, kv head): 65536
+constexpr size_t kDecodeCounterBytes = 262144;  // one int per request: up to 65536
 
 struct DecodePlan {
     int chunk_pages, max_chunks;
@@ -494,17 +505,17 @@ struct DecodePlan {
 DecodePlan plan_decode(int B, int max_seq_len, int hq, int hkv) {
     DecodePlan p{};
     const int max_pages_seq = std::max(1, (max_seq_len + kPage - 1) / kPage);
-    // Enough CTAs for ~8 per SM, chunks of at least 16 pages (256 tokens).
-    const int pairs = std::max(1, B * hkv);
-    int chunks = (8 * 148 + pairs - 1) / pairs;
-    chunks = std::max(1, std::min(chunks, (max_pages_seq + 15) / 16));
+    // One CTA per SM (192 KB ring): aim at >= 3 CTAs per SM over (chunk, request), chunks of
+    // at least 8 pages, at most kMaxChunkPages.
+    int chunks = (3 * 148 + B - 1) / std::max(1, B);
+    chunks = std::max(1, std::min(chunks, (max_pages_seq + 7) / 8));
     chunks = std::max(chunks, (max_pages_seq + kMaxChunkPages - 1) / kMaxChunkPages);
     p.chunk_pages = (max_pages_seq + chunks - 1) / chunks;
     p.max_chunks = (max_pages_seq + p.chunk_pages - 1) / p.chunk_pages;
     auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
-    // Layout: arrival counters at a fixed offset (0) whatever the batch shape -- they persist
-    // (self-resetting) between calls, so no other call's partials may land on them -- then
-    // the partial O and (m, l) of every chunk.
+    // Layout: arrival counters (one per request) at a fixed offset (0) whatever the batch
+    // shape -- they persist (self-resetting) between calls, so no other call's partials may
+    // land on them -- then the partial O and (m, l) of every chunk.
     size_t o_bytes = up(static_cast<size_t>(B) * p.max_chunks * hq * kHd * sizeof(float));
     size_t ml_bytes = up(static_cast<size_t>(B) * p.max_chunks * hq * 2 * sizeof(float));
     p.off_cnt = 0;
@@ -562,15 +573,15 @@ int msgl_paged_attention_decode(const void* q, const void* k_pool, const void* v
     DecodePlan p = plan_decode(num_reqs, max_seq_len, num_q_heads, num_kv_heads);
     if (p.bytes > 0 && (!workspace || workspace_bytes < p.bytes))
         return set_error(MSGL_ERR_WORKSPACE, "decode: workspace too small");
-    if (p.bytes > 0 && static_cast<size_t>(num_reqs) * num_kv_heads * sizeof(int) > kDecodeCounterBytes)
-        return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "decode: num_reqs * num_kv_heads > 65536");
+    if (kDecWarps % num_kv_heads)
+        return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "decode: num_kv_heads must be 1, 2, 4 or 8");
     if (num_reqs > 65535) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "decode: num_reqs > 65535");
     CUtensorMap tk, tv;
     rc = make_pool_maps(&tk, &tv, k_pool, v_pool, num_slots, num_kv_heads);
     if (rc) return rc;
     int* err = device_error_word();
     if (!err) return set_error(MSGL_ERR_CUDA, "device error word unavailable");
-    const size_t smem = kDecodeStages * 4 * kPageSlotBytes + 2 * kDecodeStages * 8 + 16 +
+    const size_t smem = kDecodeStages * kDecStageBytes + 2 * kDecodeStages * 8 + 16 +
                         kMaxChunkPages * sizeof(int) + 1024;
     static bool attr_set = false;
     if (!attr_set) {
@@ -579,9 +590,9 @@ int msgl_paged_attention_decode(const void* q, const void* k_pool, const void* v
         attr_set = true;
     }
     uint8_t* ws = static_cast<uint8_t*>(workspace);
-    dim3 grid(p.max_chunks, num_kv_heads, num_reqs);
+    dim3 grid(p.max_chunks, num_reqs);
     const float sl2e = scale * 1.4426950408889634f;
-    paged_decode_kernel<<<grid, kThreads, smem, stream>>>(
+    paged_decode_kernel<<<grid, kDecThreads, smem, stream>>>(
         tk, tv, static_cast<const __nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(out), page_table,
         max_pages, seq_lens, static_cast<int>(num_slots / kPage), num_q_heads, num_kv_heads,
         p.chunk_pages, p.max_chunks, sl2e, p.bytes ? reinterpret_cast<float*>(ws + p.off_o) : nullptr,

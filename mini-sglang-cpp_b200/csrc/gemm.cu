@@ -284,24 +284,46 @@ __device__ __forceinline__ int sk_cta_of(int64_t u, int64_t U, int G) {
 //  * stream-K mode (tiles < CTAs): the CTA's contiguous range of (tile, k-block) units, cut at
 //    tile boundaries.
 struct SkWork {
-    int64_t U, u0, u1;
+    // Hybrid schedule: the T tiles split into full waves of G whole tiles (data-parallel, no
+    // partials) and a remainder of T_rem tiles whose (tile, k-block) units are cut into G_sk
+    // equal contiguous ranges (stream-K). A CTA does its stream-K range first -- so the
+    // reduction of split tiles overlaps its whole tiles -- then its whole tiles c, c + G, ...
     int T, KB, G, c;
-    bool dp;
-    __device__ __forceinline__ int num_segs() const {
-        if (dp) return c < T ? (T - c + G - 1) / G : 0;
-        return static_cast<int>((u1 - 1) / KB - u0 / KB + 1);
+    int T_dp, T_rem, G_sk;
+    int64_t U_sk, u0, u1;  // this CTA's stream-K units (relative to tile T_dp)
+    int n_sk;              // stream-K segments of this CTA
+    __device__ __forceinline__ void init(int T_, int KB_, int G_, int c_) {
+        T = T_; KB = KB_; G = G_; c = c_;
+        T_dp = T >= G ? (T / G) * G : 0;
+        T_rem = T - T_dp;
+        U_sk = static_cast<int64_t>(T_rem) * KB;
+        const int64_t min_units = max(1, KB / 8);
+        G_sk = T_rem > 0 ? static_cast<int>(min(static_cast<int64_t>(G), max(static_cast<int64_t>(1), U_sk / min_units))) : 0;
+        if (c < G_sk) {
+            u0 = static_cast<int64_t>(c) * U_sk / G_sk;
+            u1 = static_cast<int64_t>(c + 1) * U_sk / G_sk;
+            n_sk = static_cast<int>((u1 - 1) / KB - u0 / KB + 1);
+        } else {
+            u0 = u1 = 0;
+            n_sk = 0;
+        }
     }
+    __device__ __forceinline__ int num_segs() const {
+        return n_sk + (c < T_dp ? (T_dp - c + G - 1) / G : 0);
+    }
+    // segment j: tile t, k-blocks [kb_s, kb_e); `partial` when the tile is shared (stream-K)
     __device__ __forceinline__ void seg(int j, int& t, int& kb_s, int& kb_e) const {
-        if (dp) {
-            t = c + j * G;
-            kb_s = 0;
-            kb_e = KB;
+        if (j < n_sk) {
+            const int tr = static_cast<int>(u0 / KB) + j;
+            const int64_t tb = static_cast<int64_t>(tr) * KB;
+            kb_s = static_cast<int>(max(u0, tb) - tb);
+            kb_e = static_cast<int>(min(u1, tb + KB) - tb);
+            t = T_dp + tr;
             return;
         }
-        t = static_cast<int>(u0 / KB) + j;
-        const int64_t tb = static_cast<int64_t>(t) * KB;
-        kb_s = static_cast<int>(max(u0, tb) - tb);
-        kb_e = static_cast<int>(min(u1, tb + KB) - tb);
+        t = c + (j - n_sk) * G;
+        kb_s = 0;
+        kb_e = KB;
     }
 };
 
@@ -329,14 +351,7 @@ gemm_sk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     SkWork wk;
-    wk.G = gridDim.x;
-    wk.c = blockIdx.x;
-    wk.KB = (K + kBK - 1) / kBK;
-    wk.T = m_tiles * ((N + kBM - 1) / kBM);
-    wk.dp = wk.T >= wk.G;
-    wk.U = static_cast<int64_t>(wk.T) * wk.KB;
-    wk.u0 = static_cast<int64_t>(wk.c) * wk.U / wk.G;
-    wk.u1 = static_cast<int64_t>(wk.c + 1) * wk.U / wk.G;
+    wk.init(m_tiles * ((N + kBM - 1) / kBM), (K + kBK - 1) / kBK, gridDim.x, blockIdx.x);
     const int nseg = wk.num_segs();
 
     if (threadIdx.x == 0) {
@@ -421,7 +436,7 @@ gemm_sk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
             const int n_tile = t / m_tiles, m_tile = t % m_tiles;
             const int n = n_tile * kBM + row, m0 = m_tile * BN;
             const uint32_t taddr = tmem + a * BN + (static_cast<uint32_t>(warp_q * 32) << 16);
-            if (kb_s == 0 && kb_e == wk.KB) {
+            if (j >= wk.n_sk || (kb_s == 0 && kb_e == wk.KB)) {
 #pragma unroll 1
                 for (int c0 = 0; c0 < BN; c0 += 16) {
                     uint32_t r[16];
@@ -453,8 +468,9 @@ gemm_sk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
                                                        __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]))
                                          : make_float4(0.f, 0.f, 0.f, 0.f));
             }
-            const int64_t tb = static_cast<int64_t>(t) * wk.KB;
-            const int first = sk_cta_of(tb, wk.U, wk.G), last = sk_cta_of(tb + wk.KB - 1, wk.U, wk.G);
+            const int64_t tb = static_cast<int64_t>(t - wk.T_dp) * wk.KB;
+            const int first = sk_cta_of(tb, wk.U_sk, wk.G_sk);
+            const int last = sk_cta_of(tb + wk.KB - 1, wk.U_sk, wk.G_sk);
             __threadfence();
             named_bar(1, 128);
             if (et == 0) {
@@ -483,7 +499,7 @@ gemm_sk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
                         for (int k = 0; k < kMaxContrib; ++k) {  // every load in flight at once
                             const int cc = g0 + k;
                             if (cc <= last && cc != wk.c) {
-                                const int slot = (static_cast<int64_t>(cc) * wk.U / wk.G) / wk.KB == t ? 0 : 1;
+                                const int slot = (static_cast<int64_t>(cc) * wk.U_sk / wk.G_sk) / wk.KB == t - wk.T_dp ? 0 : 1;
                                 const float4* src = reinterpret_cast<const float4*>(
                                     ws_part + ((static_cast<int64_t>(cc) * 2 + slot) * kBM + row) * BN + c0);
 #pragma unroll
