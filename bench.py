@@ -432,12 +432,18 @@ def run_case(args):
         seq = torch.full((BATCH,), CTX, dtype=torch.int32, device=dev)
         ws = ops.attention_workspace(BATCH, CTX, hq, hkv, dev)
         run = lambda: ops.paged_attention_decode(q, kp, vp, ptd, seq, CTX, hq, hkv, workspace=ws)
-    else:
+    elif args.case == "gemm":
         x = ops.fill_normal_(torch.empty(BATCH, H, dtype=torch.bfloat16, device=dev), seed=6)
         w = ops.fill_normal_(torch.empty(2 * I, H, dtype=torch.bfloat16, device=dev), seed=7,
                              std=0.02)
         ws = ops.gemm_workspace(BATCH, 2 * I, H, dev)
         run = lambda: ops.gate_up_silu(x, w, workspace=ws)
+    else:  # gemm_qkv: the qkv projection, a small-N (stream-K) GEMM
+        n = (hq + 2 * hkv) * 128
+        x = ops.fill_normal_(torch.empty(BATCH, H, dtype=torch.bfloat16, device=dev), seed=6)
+        w = ops.fill_normal_(torch.empty(n, H, dtype=torch.bfloat16, device=dev), seed=7, std=0.02)
+        ws = ops.gemm_workspace(BATCH, n, H, dev)
+        run = lambda: ops.linear(x, w, workspace=ws)
     for _ in range(args.steps):
         run()
     torch.cuda.synchronize()
@@ -457,16 +463,26 @@ def run_breakdown(args, dev):
     res = {}
 
     def timed(name, fns, nbytes, reps=None):
+        # the launches are captured in a CUDA graph, so only device time is measured
         reps = reps or max(args.steps, 10)
-        for f in fns:
-            f()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for f in fns:
+                f()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for i in range(reps):
+                fns[i % len(fns)]()
+        g.replay()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for i in range(reps):
-            fns[i % len(fns)]()
+        g.replay()
         e1.record()
         torch.cuda.synchronize()
+        del g
         us = e0.elapsed_time(e1) * 1000 / reps
         res[name] = {"us": round(us, 2), "GB/s": round(nbytes / (us * 1e-6) / 1e9, 1)}
 
@@ -520,7 +536,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--case", choices=["attention", "gemm", "breakdown"], default=None,
+    ap.add_argument("--case", choices=["attention", "gemm", "gemm_qkv", "breakdown"], default=None,
                     help="run one kernel of the step on a small single-layer case (profiling)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
