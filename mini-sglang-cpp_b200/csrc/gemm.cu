@@ -452,8 +452,8 @@ gemm_sk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
                 if (lane == 0) mbar_arrive(&tempty[a]);
                 continue;
             }
-            // ---- stream-K partial tile: publish this CTA's part (slot 0: its first segment,
-            // slot 1: its last), count arrivals; the last contributor sums all parts in CTA order
+            // ---- stream-K partial tile: publish this CTA's fp32 part (slot 0: its first
+            // segment, slot 1: a later one); sk_fixup_kernel sums the parts of each split tile
             const int my_slot = (j == 0) ? 0 : 1;
             float* part = ws_part + ((static_cast<int64_t>(wk.c) * 2 + my_slot) * kBM + row) * BN;
 #pragma unroll 1
@@ -468,66 +468,6 @@ gemm_sk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
                                                        __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]))
                                          : make_float4(0.f, 0.f, 0.f, 0.f));
             }
-            const int64_t tb = static_cast<int64_t>(t - wk.T_dp) * wk.KB;
-            const int first = sk_cta_of(tb, wk.U_sk, wk.G_sk);
-            const int last = sk_cta_of(tb + wk.KB - 1, wk.U_sk, wk.G_sk);
-            __threadfence();
-            named_bar(1, 128);
-            if (et == 0) {
-                int old = atomicAdd(ws_cnt + t, 1);
-                *last_flag = (old == last - first);
-            }
-            named_bar(1, 128);
-            if (*last_flag) {
-                __threadfence();
-#pragma unroll 1
-                for (int c0 = 0; c0 < BN; c0 += 16) {
-                    float v[16];
-                    {  // own part straight from TMEM
-                        uint32_t r[16];
-                        tmem_ld16(taddr + c0, r);
-                        tmem_ld_wait();
-#pragma unroll
-                        for (int q = 0; q < 16; ++q) v[q] = have ? __uint_as_float(r[q]) : 0.f;
-                    }
-                    float acc[16];
-#pragma unroll
-                    for (int q = 0; q < 16; ++q) acc[q] = 0.f;
-                    for (int g0 = first; g0 <= last; g0 += kMaxContrib) {
-                        float4 buf[kMaxContrib][4];
-#pragma unroll
-                        for (int k = 0; k < kMaxContrib; ++k) {  // every load in flight at once
-                            const int cc = g0 + k;
-                            if (cc <= last && cc != wk.c) {
-                                const int slot = (static_cast<int64_t>(cc) * wk.U_sk / wk.G_sk) / wk.KB == t - wk.T_dp ? 0 : 1;
-                                const float4* src = reinterpret_cast<const float4*>(
-                                    ws_part + ((static_cast<int64_t>(cc) * 2 + slot) * kBM + row) * BN + c0);
-#pragma unroll
-                                for (int q = 0; q < 4; ++q) buf[k][q] = __ldcg(src + q);
-                            }
-                        }
-#pragma unroll
-                        for (int k = 0; k < kMaxContrib; ++k) {  // sum in CTA order
-                            const int cc = g0 + k;
-                            if (cc > last) break;
-                            if (cc == wk.c) {
-#pragma unroll
-                                for (int q = 0; q < 16; ++q) acc[q] += v[q];
-                            } else {
-#pragma unroll
-                                for (int q = 0; q < 4; ++q) {
-                                    acc[4 * q] += buf[k][q].x;
-                                    acc[4 * q + 1] += buf[k][q].y;
-                                    acc[4 * q + 2] += buf[k][q].z;
-                                    acc[4 * q + 3] += buf[k][q].w;
-                                }
-                            }
-                        }
-                    }
-                    epilogue_chunk<EPI>(acc, n, N, m0 + c0, M, y, amax, lane, warp_q, n_tile, id_off);
-                }
-                if (et == 0) ws_cnt[t] = 0;
-            }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[a]);  // TMEM buffer free for segment j + 2
@@ -539,6 +479,55 @@ gemm_sk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         tc_fence_after();
         tmem_dealloc(tmem, Cfg::kTmemCols);
     }
+}
+
+// Sums the contributors' fp32 parts of every split (stream-K) tile in CTA order --
+// deterministic -- and runs the epilogue. grid (split tiles, BN / 16 column chunks), 128
+// threads = the tile's 128 weight rows; every contributor's load of a chunk is in flight at once.
+template <int BN, int EPI>
+__global__ void __launch_bounds__(128)
+sk_fixup_kernel(const float* __restrict__ ws_part, void* __restrict__ y,
+                unsigned long long* __restrict__ amax, int M, int N, int K, int m_tiles,
+                int G, int id_off) {
+    SkWork wk;
+    wk.init(m_tiles * ((N + kBM - 1) / kBM), (K + kBK - 1) / kBK, G, 0);
+    const int t_rel = blockIdx.x, c0 = blockIdx.y * 16;
+    const int t = wk.T_dp + t_rel;
+    const int row = threadIdx.x, lane = threadIdx.x & 31, warp_q = threadIdx.x >> 5;
+    const int64_t tb = static_cast<int64_t>(t_rel) * wk.KB;
+    const int first = sk_cta_of(tb, wk.U_sk, wk.G_sk);
+    const int last = sk_cta_of(tb + wk.KB - 1, wk.U_sk, wk.G_sk);
+    float acc[16];
+#pragma unroll
+    for (int q = 0; q < 16; ++q) acc[q] = 0.f;
+    for (int g0 = first; g0 <= last; g0 += kMaxContrib) {
+        float4 buf[kMaxContrib][4];
+#pragma unroll
+        for (int k = 0; k < kMaxContrib; ++k) {
+            const int cc = g0 + k;
+            if (cc <= last) {
+                const int slot = (static_cast<int64_t>(cc) * wk.U_sk / wk.G_sk) / wk.KB == t_rel ? 0 : 1;
+                const float4* src = reinterpret_cast<const float4*>(
+                    ws_part + ((static_cast<int64_t>(cc) * 2 + slot) * kBM + row) * BN + c0);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) buf[k][q] = __ldcg(src + q);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kMaxContrib; ++k) {
+            if (g0 + k > last) break;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                acc[4 * q] += buf[k][q].x;
+                acc[4 * q + 1] += buf[k][q].y;
+                acc[4 * q + 2] += buf[k][q].z;
+                acc[4 * q + 3] += buf[k][q].w;
+            }
+        }
+    }
+    const int n_tile = t / m_tiles, m_tile = t % m_tiles;
+    epilogue_chunk<EPI>(acc, n_tile * kBM + row, N, m_tile * BN + c0, M, y, amax, lane, warp_q,
+                        n_tile, id_off);
 }
 
 int num_sms() {
@@ -554,9 +543,9 @@ int num_sms() {
     return n[dev];
 }
 
-// Stream-K workspace: counters at a fixed offset, then 2 fp32 tile slots per CTA.
+// Stream-K workspace: 2 fp32 tile slots per CTA (no persistent state between calls).
 size_t sk_workspace_bytes(int bn, int sms) {
-    return kCounterBytes + static_cast<size_t>(sms) * 2 * kBM * bn * sizeof(float);
+    return static_cast<size_t>(sms) * 2 * kBM * bn * sizeof(float);
 }
 
 struct GemmPlan {
@@ -628,11 +617,18 @@ int launch_sk(const CUtensorMap& tw, const CUtensorMap& tx, void* y, unsigned lo
     const int m_tiles = (M + BN - 1) / BN;
     const int64_t units = static_cast<int64_t>(m_tiles) * ((N + kBM - 1) / kBM) * ((K + kBK - 1) / kBK);
     const int G = static_cast<int>(std::min<int64_t>(sms, units));
-    uint8_t* w8 = static_cast<uint8_t*>(ws);
+    float* part = static_cast<float*>(ws);
     gemm_sk_kernel<BN, EPI><<<G, kGemmThreads, Cfg::kSmem, stream>>>(
-        tw, tx, y, amax, M, N, K, m_tiles, reinterpret_cast<float*>(w8 + kCounterBytes),
-        reinterpret_cast<int*>(w8), id_off, err);
+        tw, tx, y, amax, M, N, K, m_tiles, part, nullptr, id_off, err);
     MSGL_LAUNCH_CHECK();
+    // split tiles of the stream-K remainder: same schedule arithmetic as SkWork::init
+    const int T = m_tiles * ((N + kBM - 1) / kBM);
+    const int T_rem = T - (T >= G ? (T / G) * G : 0);
+    if (T_rem > 0) {
+        sk_fixup_kernel<BN, EPI><<<dim3(T_rem, BN / 16), 128, 0, stream>>>(
+            part, y, amax, M, N, K, m_tiles, G, id_off);
+        MSGL_LAUNCH_CHECK();
+    }
     return MSGL_OK;
 }
 
