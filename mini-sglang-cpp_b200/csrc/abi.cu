@@ -78,6 +78,31 @@ int make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64
     return MSGL_OK;
 }
 
+int make_tmap_3d_bf16(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                      uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2) {
+    EncodeTiledFn fn = get_encode_fn();
+    if (!fn) return set_error(MSGL_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (s1 & 15) || (s2 & 15))
+        return set_error(MSGL_ERR_INVALID_ARG, "TMA base / strides not 16-byte aligned");
+    cuuint64_t dims[3] = {d0, d1, d2};
+    cuuint64_t strides[2] = {s1, s2};
+    cuuint32_t box[3] = {b0, b1, b2};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
+                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        char buf[200];
+        snprintf(buf, sizeof(buf),
+                 "cuTensorMapEncodeTiled (3-D) failed (%d): dims %llu x %llu x %llu strides %llu %llu "
+                 "box %u x %u x %u",
+                 (int)r, (unsigned long long)d0, (unsigned long long)d1, (unsigned long long)d2,
+                 (unsigned long long)s1, (unsigned long long)s2, b0, b1, b2);
+        return set_error(MSGL_ERR_CUDA, buf);
+    }
+    return MSGL_OK;
+}
+
 // ------------------------------------------------------------------ Philox4x32-10
 // Salmon, Moraes, Dror, Shaw, "Parallel random numbers: as easy as 1, 2, 3" (SC'11).
 struct U4 { uint32_t x, y, z, w; };

@@ -5,14 +5,16 @@
 // over the paged pool [num_slots, Hkv * 128] (slot = page * 16 + offset, the layout of
 // kernels/cuda/radix.cu:19-22), with GQA (query head h reads kv head h / (Hq / Hkv)).
 //
-// Data movement: a producer warp walks the request's page-table row and stages each page's K and
-// V rows (16 tokens x 128 dims of one kv head, 4 KB each) into shared memory with 2-D TMA loads
-// (SWIZZLE_128B, no multicast) on an mbarrier ring. Four consumer warps compute
-// S = Q K^T and O += P V with warp-level bf16 MMA (m16n8k16, fp32 accumulate; fragments read
-// with ldmatrix from the swizzled tiles, conflict-free) and a warp-shuffle online softmax.
-// The query group of one kv head (Hq / Hkv <= 8 heads) fills the MMA rows; in decode the pages
-// of one request are split over the four warps and over `chunks` CTAs (split-KV), whose partial
-// (m, l, O) are merged by the last CTA to finish (a self-resetting arrival counter).
+// Data movement: a producer warp walks the request's page-table row and stages pages of K and
+// V into shared memory with TMA loads (SWIZZLE_128B, no multicast) on an mbarrier ring; four
+// consumer warps compute S = Q K^T and O += P V with warp-level bf16 MMA (m16n8k16, fp32
+// accumulate; fragments read with ldmatrix from the swizzled tiles, conflict-free) and a
+// warp-shuffle online softmax. The query group of one kv head (Hq / Hkv <= 8 heads) fills the MMA
+// rows. Decode: one 3-D TMA per pool brings a whole page of up to four kv heads (16 KB) -- TMA
+// throughput per CTA is set by the number of boxes in flight, not their size -- and the pages of
+// a request are split over `chunks` CTAs (split-KV) whose partial (m, l, O) the last CTA to
+// finish merges (a self-resetting arrival counter). Extend: one CTA per (query tile, kv head),
+// one page (2-D TMA, 4 x 2 KB) per stage.
 //
 // Bound: HBM. Per (request, kv head, token) the kernel reads 512 B of K/V; the tensor work per
 // byte is ~4 FLOP, far below the MMA rate.
@@ -29,7 +31,6 @@ constexpr int kHd = 128;
 constexpr int kPageSlotBytes = 4 * 2048;  // K lo, K hi, V lo, V hi halves of one page
 constexpr int kConsumerWarps = 4;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
-constexpr int kDecodeStages = 3;          // x 4 pages per stage
 constexpr int kExtendStages = 8;          // x 1 page per stage
 constexpr int kMaxChunkPages = 512;       // decode split-KV chunk bound (page ids in smem)
 constexpr int kExtendPageBatch = 1024;    // extend: page ids staged per batch
@@ -144,35 +145,41 @@ __device__ __forceinline__ void store_bf16x8(__nv_bfloat16* dst, const float (&v
 }
 
 // ------------------------------------------------------------------------------ decode
-// grid (max_chunks, B); block 288 = 8 consumer warps + 1 TMA producer warp. One CTA covers a
-// request's chunk of pages for ALL kv heads, so each page is fetched as whole token rows
-// (16 rows x Hkv * 256 B, contiguous in the token-major pool) rather than one kv head's 256 B
-// slice of each row. A stage holds kDecPPS = 8 / Hkv pages; warp w attends kv head w % Hkv on
-// page w / Hkv of the stage, so every consumer warp does one (page, head) per stage.
-constexpr int kDecWarps = 8;
+// grid (max_chunks, Hkv / hc, B); block 160 = 4 consumer warps + 1 TMA producer warp. One CTA
+// covers a chunk of one request's pages for a group of hc = min(Hkv, 4) kv heads. A page of the
+// group is ONE 3-D TMA box per pool -- {64 dims, 16 token rows, 2 hc head halves}, token rows
+// 2 * Hkv * 128 B apart, head halves 128 B apart -- landing head-major ([hh][token][64], the
+// same 2 KB swizzled tiles the MMA fragments read), so the ring moves 16 KB per TMA instead of
+// 2 KB. A stage holds pps = 4 / hc pages; warp w attends local kv head w % hc on page w / hc.
+constexpr int kDecWarps = 4;
 constexpr int kDecThreads = (kDecWarps + 1) * 32;
-constexpr int kDecStageBytes = kDecWarps * kPageSlotBytes;  // 64 KB: 8 (page, head) slots
+constexpr int kDecHeads = 4;                                 // kv heads per CTA (max)
+constexpr int kDecHalfStage = kDecHeads * 2 * 2048;          // 16 KB of K (or of V) per stage
+constexpr int kDecStageBytes = 2 * kDecHalfStage;            // 32 KB: K then V
+constexpr int kDecStages = 3;                                // 96 KB ring: 2 CTAs per SM
 
-__global__ void __launch_bounds__(kDecThreads, 1)
+__global__ void __launch_bounds__(kDecThreads, 2)
 paged_decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                     const __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ out,
                     const int* __restrict__ page_table, int max_pages,
-                    const int* __restrict__ seq_lens, int pool_pages, int hq, int hkv,
+                    const int* __restrict__ seq_lens, int pool_pages, int hq, int hkv, int hc,
                     int chunk_pages, int max_chunks, float sl2e, float* __restrict__ ws_o,
                     float* __restrict__ ws_ml, int* __restrict__ ws_cnt, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = align1024(smem_raw);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDecodeStages * kDecStageBytes);
-    uint64_t* empty = full + kDecodeStages;
-    int* flag = reinterpret_cast<int*>(empty + kDecodeStages);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDecStages * kDecStageBytes);
+    uint64_t* empty = full + kDecStages;
+    int* flag = reinterpret_cast<int*>(empty + kDecStages);
     int* pages = flag + 4;  // [chunk_pages <= kMaxChunkPages]
 
-    const int b = blockIdx.y, chunk = blockIdx.x;
+    const int b = blockIdx.z, hg = blockIdx.y, chunk = blockIdx.x;
     const int group = hq / hkv;
-    const int pps = kDecWarps / hkv;  // pages per stage
+    const int pps = kDecWarps / hc;   // pages per stage
+    const int nq = hc * group;        // query heads of this CTA
+    const int qh0 = hg * nq;          // first of them
     int L = seq_lens[b];
     if (L < 0 || L > max_pages * kPage) {  // context longer than the page-table row
-        if (threadIdx.x == 0 && chunk == 0) record_error(err, MSGL_ERR_BOUNDS, 202);
+        if (threadIdx.x == 0 && chunk == 0 && hg == 0) record_error(err, MSGL_ERR_BOUNDS, 202);
         L = L < 0 ? 0 : max_pages * kPage;
     }
     const int npages = (L + kPage - 1) / kPage;
@@ -180,9 +187,9 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
 
     if (npages == 0) {  // empty context: output zeros (chunk 0 only)
         if (chunk == 0)
-            for (int i = threadIdx.x; i < hq * 16; i += blockDim.x) {
+            for (int i = threadIdx.x; i < nq * 16; i += blockDim.x) {
                 float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-                store_bf16x8(out + (static_cast<int64_t>(b) * hq + (i >> 4)) * kHd + (i & 15) * 8, z);
+                store_bf16x8(out + (static_cast<int64_t>(b) * hq + qh0 + (i >> 4)) * kHd + (i & 15) * 8, z);
             }
         return;
     }
@@ -193,7 +200,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
     const int nsteps = (np + pps - 1) / pps;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kDecodeStages; ++s) {
+        for (int s = 0; s < kDecStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kDecWarps);
         }
@@ -216,31 +223,32 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
         if (lane == 0) {
             tma_prefetch_desc(&tk);
             tma_prefetch_desc(&tv);
+            const int page_half = hc * 4096;  // K (or V) bytes of one page of the head group
             for (int it = 0; it < nsteps; ++it) {
-                const int s = it % kDecodeStages;
-                if (it >= kDecodeStages &&
-                    !mbar_wait(&empty[s], ((it / kDecodeStages) - 1) & 1, err, 200))
+                const int s = it % kDecStages;
+                if (it >= kDecStages && !mbar_wait(&empty[s], ((it / kDecStages) - 1) & 1, err, 200))
                     break;
                 const int cnt = min(pps, np - it * pps);
-                mbar_arrive_expect_tx(&full[s], cnt * hkv * kPageSlotBytes);
+                mbar_arrive_expect_tx(&full[s], cnt * 2 * page_half);
+                uint8_t* st = smem + s * kDecStageBytes;
                 for (int p = 0; p < cnt; ++p) {
-                    const int page = pages[it * pps + p];
-                    for (int h = 0; h < hkv; ++h)  // all heads of the page back to back
-                        issue_page(smem + s * kDecStageBytes + (p * hkv + h) * kPageSlotBytes, &tk,
-                                   &tv, &full[s], h, page);
+                    const int y = pages[it * pps + p] * kPage;
+                    tma_load_3d(st + p * page_half, &tk, &full[s], 0, y, 2 * hc * hg);
+                    tma_load_3d(st + kDecHalfStage + p * page_half, &tv, &full[s], 0, y, 2 * hc * hg);
                 }
             }
         }
         return;
     }
 
-    // ---------------- consumers: kv head `head`, page `psub` of every stage
-    const int head = warp % hkv, psub = warp / hkv;
+    // ---------------- consumers: local kv head `head`, page `psub` of every stage
+    const int head = warp % hc, psub = warp / hc;
     const int g = lane >> 2, c = lane & 3;
     uint32_t qa[8][4];
     {
         const bool real = g < group;
-        const __nv_bfloat16* qr = q + (static_cast<int64_t>(b) * hq + head * group + (real ? g : 0)) * kHd;
+        const __nv_bfloat16* qr =
+            q + (static_cast<int64_t>(b) * hq + qh0 + head * group + (real ? g : 0)) * kHd;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
             qa[kk][0] = real ? *reinterpret_cast<const uint32_t*>(qr + 16 * kk + 2 * c) : 0u;
@@ -254,15 +262,15 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
     for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
     float m[2] = {kNegInf, kNegInf}, l[2] = {0.f, 0.f};
 
+    const uint32_t my_off = (psub * hc + head) * 4096;
     for (int it = 0; it < nsteps; ++it) {
-        const int s = it % kDecodeStages;
-        if (!mbar_wait(&full[s], (it / kDecodeStages) & 1, err, 210)) break;
+        const int s = it % kDecStages;
+        if (!mbar_wait(&full[s], (it / kDecStages) & 1, err, 210)) break;
         const int pidx = it * pps + psub;
         if (pidx < np) {
-            const uint32_t base =
-                smem_u32(smem + s * kDecStageBytes + (psub * hkv + head) * kPageSlotBytes);
-            attend_page<false>(base, base + 4096, qa, o, m, l, (p0 + pidx) * kPage, L - 1, -1,
-                               sl2e, lane);
+            const uint32_t base = smem_u32(smem + s * kDecStageBytes) + my_off;
+            attend_page<false>(base, base + kDecHalfStage, qa, o, m, l, (p0 + pidx) * kPage, L - 1,
+                               -1, sl2e, lane);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
@@ -273,9 +281,9 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
     lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
     lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);
     named_bar_sync(1, kDecWarps * 32);
-    float* mo = reinterpret_cast<float*>(smem);      // [8 warps][8 rows][128]
-    float* mm = mo + kDecWarps * 8 * kHd;             // [8][8]
-    float* ml = mm + kDecWarps * 8;                   // [8][8]
+    float* mo = reinterpret_cast<float*>(smem);      // [4 warps][8 rows][128]
+    float* mm = mo + kDecWarps * 8 * kHd;             // [4][8]
+    float* ml = mm + kDecWarps * 8;                   // [4][8]
     if (g < group) {
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -289,15 +297,16 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
     }
     named_bar_sync(1, kDecWarps * 32);
 
-    // items: (q head qh in [0, hq), 8-wide d chunk) over the 256 consumer threads
-    for (int item = threadIdx.x; item < hq * 16; item += kDecWarps * 32) {
-        const int qh = item >> 4, d0 = (item & 15) * 8;
-        const int h = qh / group, r = qh % group;
+    // items: (local query head, 8-wide d chunk) over the 128 consumer threads
+    for (int item = threadIdx.x; item < nq * 16; item += kDecWarps * 32) {
+        const int lq = item >> 4, d0 = (item & 15) * 8;
+        const int h = lq / group, r = lq % group;
+        const int qh = qh0 + lq;
         float M = kNegInf;
-        for (int ps = 0; ps < pps; ++ps) M = fmaxf(M, mm[(ps * hkv + h) * 8 + r]);
+        for (int ps = 0; ps < pps; ++ps) M = fmaxf(M, mm[(ps * hc + h) * 8 + r]);
         float O[8] = {0, 0, 0, 0, 0, 0, 0, 0}, Ls = 0.f;
         for (int ps = 0; ps < pps; ++ps) {
-            const int w = ps * hkv + h;
+            const int w = ps * hc + h;
             const float mw = mm[w * 8 + r];
             const float sc = (mw == kNegInf) ? 0.f : exp2f(mw - M);
             Ls += ml[w * 8 + r] * sc;
@@ -322,18 +331,19 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
     }
     if (nchunks == 1) return;
 
-    // ---------------- split-KV: the last chunk CTA of request b merges all chunks
+    // ---------------- split-KV: the last chunk CTA of (request, head group) merges all chunks
     __threadfence();
     named_bar_sync(1, kDecWarps * 32);
+    int* cnt = ws_cnt + static_cast<int64_t>(b) * gridDim.y + hg;
     if (threadIdx.x == 0) {
-        const int old = atomicAdd(&ws_cnt[b], 1);
+        const int old = atomicAdd(cnt, 1);
         *flag = (old == nchunks - 1);
     }
     named_bar_sync(1, kDecWarps * 32);
     if (!*flag) return;
     __threadfence();
-    for (int item = threadIdx.x; item < hq * 16; item += kDecWarps * 32) {
-        const int qh = item >> 4, d0 = (item & 15) * 8;
+    for (int item = threadIdx.x; item < nq * 16; item += kDecWarps * 32) {
+        const int qh = qh0 + (item >> 4), d0 = (item & 15) * 8;
         float M = kNegInf;
         for (int ch = 0; ch < nchunks; ++ch)
             M = fmaxf(M, __ldcg(ws_ml + ((static_cast<int64_t>(b) * max_chunks + ch) * hq + qh) * 2));
@@ -353,7 +363,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
         for (int e = 0; e < 8; ++e) O[e] *= inv;
         store_bf16x8(out + (static_cast<int64_t>(b) * hq + qh) * kHd + d0, O);
     }
-    if (threadIdx.x == 0) ws_cnt[b] = 0;
+    if (threadIdx.x == 0) *cnt = 0;
 }
 
 // ------------------------------------------------------------------------------ extend
@@ -502,20 +512,27 @@ struct DecodePlan {
     size_t off_o, off_ml, off_cnt, bytes;
 };
 
+// kv heads per decode CTA: the largest of 4, 2, 1 that divides Hkv.
+int decode_heads_per_cta(int hkv) { return hkv % 4 == 0 ? 4 : (hkv % 2 == 0 ? 2 : 1); }
+
 DecodePlan plan_decode(int B, int max_seq_len, int hq, int hkv) {
     DecodePlan p{};
     const int max_pages_seq = std::max(1, (max_seq_len + kPage - 1) / kPage);
-    // One CTA per SM (192 KB ring): aim at >= 3 CTAs per SM over (chunk, request), chunks of
-    // at least 8 pages, at most kMaxChunkPages.
-    int chunks = (3 * 148 + B - 1) / std::max(1, B);
-    chunks = std::max(1, std::min(chunks, (max_pages_seq + 7) / 8));
+    const int n_hg = hkv / decode_heads_per_cta(hkv);
+    // Two CTAs per SM (96 KB ring each): split each request's pages into chunks so that
+    // (chunk, head group, request) gives about four waves of CTAs, chunks of at least 16 pages
+    // (so the pipeline fill is amortised) and at most kMaxChunkPages.
+    const int slots = 2 * 148;
+    const long long rows = static_cast<long long>(std::max(1, B)) * n_hg;
+    int chunks = static_cast<int>(std::min<long long>((4LL * slots + rows - 1) / rows, 1 << 20));
+    chunks = std::max(1, std::min(chunks, (max_pages_seq + 15) / 16));
     chunks = std::max(chunks, (max_pages_seq + kMaxChunkPages - 1) / kMaxChunkPages);
     p.chunk_pages = (max_pages_seq + chunks - 1) / chunks;
     p.max_chunks = (max_pages_seq + p.chunk_pages - 1) / p.chunk_pages;
     auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
-    // Layout: arrival counters (one per request) at a fixed offset (0) whatever the batch
-    // shape -- they persist (self-resetting) between calls, so no other call's partials may
-    // land on them -- then the partial O and (m, l) of every chunk.
+    // Layout: arrival counters (one per request and head group) at a fixed offset (0) whatever
+    // the batch shape -- they persist (self-resetting) between calls, so no other call's
+    // partials may land on them -- then the partial O and (m, l) of every chunk.
     size_t o_bytes = up(static_cast<size_t>(B) * p.max_chunks * hq * kHd * sizeof(float));
     size_t ml_bytes = up(static_cast<size_t>(B) * p.max_chunks * hq * 2 * sizeof(float));
     p.off_cnt = 0;
@@ -542,6 +559,16 @@ int make_pool_maps(CUtensorMap* tk, CUtensorMap* tv, const void* k_pool, const v
     int rc = make_tmap_2d_bf16(tk, k_pool, row, num_slots, row * 2, 64, kPage, true);
     if (rc) return rc;
     return make_tmap_2d_bf16(tv, v_pool, row, num_slots, row * 2, 64, kPage, true);
+}
+
+// Decode view of a pool: {64 dims, num_slots token rows (Hkv * 256 B apart), 2 Hkv head halves
+// (128 B apart)}, box {64, 16, 2 hc}: one page of hc kv heads, head-major in shared memory.
+int make_decode_maps(CUtensorMap* tk, CUtensorMap* tv, const void* k_pool, const void* v_pool,
+                     int64_t num_slots, int hkv, int hc) {
+    const uint64_t row_bytes = static_cast<uint64_t>(hkv) * kHd * 2;
+    int rc = make_tmap_3d_bf16(tk, k_pool, 64, num_slots, 2 * hkv, row_bytes, 128, 64, kPage, 2 * hc);
+    if (rc) return rc;
+    return make_tmap_3d_bf16(tv, v_pool, 64, num_slots, 2 * hkv, row_bytes, 128, 64, kPage, 2 * hc);
 }
 
 }  // namespace
@@ -573,15 +600,18 @@ int msgl_paged_attention_decode(const void* q, const void* k_pool, const void* v
     DecodePlan p = plan_decode(num_reqs, max_seq_len, num_q_heads, num_kv_heads);
     if (p.bytes > 0 && (!workspace || workspace_bytes < p.bytes))
         return set_error(MSGL_ERR_WORKSPACE, "decode: workspace too small");
-    if (kDecWarps % num_kv_heads)
-        return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "decode: num_kv_heads must be 1, 2, 4 or 8");
-    if (num_reqs > 65535) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "decode: num_reqs > 65535");
+    const int hc = decode_heads_per_cta(num_kv_heads);
+    const int n_hg = num_kv_heads / hc;
+    if (num_reqs > 65535 || n_hg > 65535)
+        return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "decode: num_reqs or Hkv too large");
+    if (p.bytes > 0 && static_cast<size_t>(num_reqs) * n_hg * sizeof(int) > kDecodeCounterBytes)
+        return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "decode: num_reqs * Hkv / 4 > 65536");
     CUtensorMap tk, tv;
-    rc = make_pool_maps(&tk, &tv, k_pool, v_pool, num_slots, num_kv_heads);
+    rc = make_decode_maps(&tk, &tv, k_pool, v_pool, num_slots, num_kv_heads, hc);
     if (rc) return rc;
     int* err = device_error_word();
     if (!err) return set_error(MSGL_ERR_CUDA, "device error word unavailable");
-    const size_t smem = kDecodeStages * kDecStageBytes + 2 * kDecodeStages * 8 + 16 +
+    const size_t smem = kDecStages * kDecStageBytes + 2 * kDecStages * 8 + 16 +
                         kMaxChunkPages * sizeof(int) + 1024;
     static bool attr_set = false;
     if (!attr_set) {
@@ -590,11 +620,11 @@ int msgl_paged_attention_decode(const void* q, const void* k_pool, const void* v
         attr_set = true;
     }
     uint8_t* ws = static_cast<uint8_t*>(workspace);
-    dim3 grid(p.max_chunks, num_reqs);
+    dim3 grid(p.max_chunks, n_hg, num_reqs);
     const float sl2e = scale * 1.4426950408889634f;
     paged_decode_kernel<<<grid, kDecThreads, smem, stream>>>(
         tk, tv, static_cast<const __nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(out), page_table,
-        max_pages, seq_lens, static_cast<int>(num_slots / kPage), num_q_heads, num_kv_heads,
+        max_pages, seq_lens, static_cast<int>(num_slots / kPage), num_q_heads, num_kv_heads, hc,
         p.chunk_pages, p.max_chunks, sl2e, p.bytes ? reinterpret_cast<float*>(ws + p.off_o) : nullptr,
         p.bytes ? reinterpret_cast<float*>(ws + p.off_ml) : nullptr,
         p.bytes ? reinterpret_cast<int*>(ws + p.off_cnt) : nullptr, err);

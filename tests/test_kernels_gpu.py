@@ -153,6 +153,9 @@ def make_paged(rng, seq_lens, hkv, num_pages, P=16, D=128):
     (32, 4, [300, 33, 2500]),
     (8, 8, [64, 5]),
     (16, 2, [1000]),
+    (4, 1, [200, 17, 1]),     # one kv head: four pages per stage
+    (12, 6, [100, 260]),      # head groups of two
+    (32, 16, [300, 40]),      # four head groups per request
 ])
 def test_paged_decode(cuda, oracle, hq, hkv, seq_lens):
     from msgl import ops
