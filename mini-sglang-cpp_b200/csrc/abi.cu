@@ -1,6 +1,7 @@
 // abi.cu -- library-wide C-ABI pieces: status messages, the device error word, version, the
 // counter-based normal generator used for random-init weights, and the TMA descriptor helper.
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -31,6 +32,14 @@ int* device_error_word() {
         ptrs[dev] = static_cast<int*>(p);
     }
     return ptrs[dev];
+}
+
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* v = getenv("MSGL_PDL");
+        return !(v && v[0] == '0');
+    }();
+    return on;
 }
 
 // ------------------------------------------------------------------ TMA descriptors

@@ -177,6 +177,17 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
     const int pps = kDecWarps / hc;   // pages per stage
     const int nq = hc * group;        // query heads of this CTA
     const int qh0 = hg * nq;          // first of them
+    // prologue overlapping the previous kernel: barriers only (the page table and context
+    // lengths are step inputs, but they may be written by a preceding kernel of the caller)
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kDecStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kDecWarps);
+        }
+        fence_barrier_init();
+    }
+    pdl_wait();
+    pdl_trigger();
     int L = seq_lens[b];
     if (L < 0 || L > max_pages * kPage) {  // context longer than the page-table row
         if (threadIdx.x == 0 && chunk == 0 && hg == 0) record_error(err, MSGL_ERR_BOUNDS, 202);
@@ -198,14 +209,6 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
     const int np = min(npages - p0, chunk_pages);
     const int nchunks = (npages + chunk_pages - 1) / chunk_pages;
     const int nsteps = (np + pps - 1) / pps;
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < kDecStages; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kDecWarps);
-        }
-        fence_barrier_init();
-    }
     __syncthreads();
 
     if (warp == kDecWarps) {
@@ -383,6 +386,15 @@ paged_extend_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
     const int b = blockIdx.z, kvh = blockIdx.y;
     const int group = hq / hkv;
     const int tpw = 16 / group;  // query tokens per warp
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kExtendStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        fence_barrier_init();
+    }
+    pdl_wait();
+    pdl_trigger();
     const int qbeg = q_indptr[b];
     const int nq = q_indptr[b + 1] - qbeg;
     const int tile0 = blockIdx.x * kConsumerWarps * tpw;
@@ -397,14 +409,6 @@ paged_extend_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
         npages = max_pages;
     }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < kExtendStages; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kConsumerWarps);
-        }
-        fence_barrier_init();
-    }
     __syncthreads();
 
     if (warp == kConsumerWarps) {
@@ -622,7 +626,7 @@ int msgl_paged_attention_decode(const void* q, const void* k_pool, const void* v
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     dim3 grid(p.max_chunks, n_hg, num_reqs);
     const float sl2e = scale * 1.4426950408889634f;
-    paged_decode_kernel<<<grid, kDecThreads, smem, stream>>>(
+    launch_pdl(paged_decode_kernel, grid, dim3(kDecThreads), smem, stream,
         tk, tv, static_cast<const __nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(out), page_table,
         max_pages, seq_lens, static_cast<int>(num_slots / kPage), num_q_heads, num_kv_heads, hc,
         p.chunk_pages, p.max_chunks, sl2e, p.bytes ? reinterpret_cast<float*>(ws + p.off_o) : nullptr,
@@ -660,7 +664,7 @@ int msgl_paged_attention_extend(const void* q, const void* k_pool, const void* v
     const int tile_tokens = kConsumerWarps * (16 / group);
     dim3 grid((max_q_len + tile_tokens - 1) / tile_tokens, num_kv_heads, num_reqs);
     const float sl2e = scale * 1.4426950408889634f;
-    paged_extend_kernel<<<grid, kThreads, smem, stream>>>(
+    launch_pdl(paged_extend_kernel, grid, dim3(kThreads), smem, stream,
         tk, tv, static_cast<const __nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(out), page_table,
         max_pages, seq_lens, q_indptr, static_cast<int>(num_slots / kPage), num_q_heads,
         num_kv_heads, sl2e, err);

@@ -23,6 +23,11 @@ namespace {
 constexpr int kBM = 128;       // weight rows per tile (UMMA M)
 constexpr int kBK = 64;        // K per stage: one 128-byte swizzle row
 constexpr int kGemmThreads = 192;
+// Stream-K kernel: producer warp, MMA warp, then kSkEpiWarps epilogue warps -- two per TMEM lane
+// quarter, splitting the tile's columns, so each SM sub-partition runs two epilogue warps and
+// hides the latency of the TMEM-load / convert / store chains.
+constexpr int kSkEpiWarps = 8;
+constexpr int kSkThreads = (2 + kSkEpiWarps) * 32;
 constexpr int kTileA = kBM * kBK * 2;  // 16 KB
 constexpr size_t kCounterBytes = 16384;  // split-K arrival counters: up to 4096 tiles
 
@@ -125,6 +130,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum_full + 1);
     int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
+    pdl_wait();
+    pdl_trigger();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m_tile = blockIdx.x, n_tile = blockIdx.y, split = blockIdx.z;
     int m0 = m_tile * BN;
@@ -251,6 +258,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
         }
         tc_fence_before();
     }
+    // Lane 0 of warps 0 and 1 ran the producer / MMA loops alone: reconverge every warp before
+    // the block barrier (bar.sync counts whole warps), so TMEM is freed only after the epilogue.
+    __syncwarp();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
@@ -259,13 +269,20 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
 }
 
 // ============================================================================ stream-K kernel
-// Persistent: one CTA per SM. The (tile, k-block) units of the whole GEMM are cut into G equal
-// contiguous ranges, one per CTA, so every SM streams the same number of weight bytes whatever
-// the tile count. A CTA's range covers one or more tile segments; each segment accumulates into
-// one of two TMEM buffers (the epilogue of segment j overlaps the mainloop of segment j+1).
-// A segment that is a whole tile runs the epilogue directly; a partial segment stores its fp32
-// tile into the CTA's workspace slot, and the last contributor of the tile (arrival counter)
-// sums the contributors' slots in CTA order -- deterministic -- and runs the epilogue.
+// Persistent: one CTA per SM. Hybrid schedule: the T output tiles split into full waves of G
+// whole tiles (data-parallel: CTA c takes tiles c, c + G, ...) and a remainder of T_rem tiles
+// whose (tile, k-block) units are cut into G_sk equal contiguous ranges (stream-K), so every SM
+// streams about the same number of weight bytes whatever the tile count. A CTA's stream-K range
+// is [tail of a tile] [whole tiles] [head of a tile]:
+//  * the tail part (k-blocks [x, KB)) of a tile that an earlier CTA starts: its fp32 part goes to
+//    this CTA's workspace slot and a flag is raised -- done FIRST, at the start of the kernel;
+//  * the head part (k-blocks [0, y)) of a tile: this CTA owns the tile. It runs it LAST, then
+//    waits (bounded) for the flags of the tile's other contributors -- the following CTAs, which
+//    published their parts at their start -- and adds their parts, in CTA order
+//    (deterministic), to its own accumulator before the epilogue.
+// Segment order of a CTA: its stream-K segments but the last, its whole data-parallel tiles, its
+// last stream-K segment. Each segment accumulates into one of two TMEM buffers (the epilogue of
+// segment j overlaps the mainloop of segment j + 1).
 template <int BN>
 struct SkCfg {
     static constexpr int kTileB = BN * kBK * 2;
@@ -275,23 +292,18 @@ struct SkCfg {
     static constexpr size_t kSmem = static_cast<size_t>(kStages) * kStageBytes + 1024 + 256;
 };
 
+constexpr size_t kSkFlagBytes = 4096;  // one flag per CTA (<= 1024 CTAs), then the parts
+constexpr int kSkMaxCtas = static_cast<int>(kSkFlagBytes / sizeof(int));
+
 __device__ __forceinline__ int sk_cta_of(int64_t u, int64_t U, int G) {
     return static_cast<int>(((u + 1) * G + U - 1) / U - 1);
 }
 
-// A CTA's work is a list of tile segments (tile t, k-blocks [kb_s, kb_e)):
-//  * data-parallel mode (tiles >= CTAs): whole tiles c, c + G, c + 2G, ... -- no partials;
-//  * stream-K mode (tiles < CTAs): the CTA's contiguous range of (tile, k-block) units, cut at
-//    tile boundaries.
 struct SkWork {
-    // Hybrid schedule: the T tiles split into full waves of G whole tiles (data-parallel, no
-    // partials) and a remainder of T_rem tiles whose (tile, k-block) units are cut into G_sk
-    // equal contiguous ranges (stream-K). A CTA does its stream-K range first -- so the
-    // reduction of split tiles overlaps its whole tiles -- then its whole tiles c, c + G, ...
     int T, KB, G, c;
     int T_dp, T_rem, G_sk;
     int64_t U_sk, u0, u1;  // this CTA's stream-K units (relative to tile T_dp)
-    int n_sk;              // stream-K segments of this CTA
+    int n_sk, n_dp, lead;  // stream-K segments, whole data-parallel tiles, SK segments run first
     __device__ __forceinline__ void init(int T_, int KB_, int G_, int c_) {
         T = T_; KB = KB_; G = G_; c = c_;
         T_dp = T >= G ? (T / G) * G : 0;
@@ -307,33 +319,46 @@ struct SkWork {
             u0 = u1 = 0;
             n_sk = 0;
         }
+        n_dp = c < T_dp ? (T_dp - c + G - 1) / G : 0;
+        // the last stream-K segment waits for the data-parallel tiles only when it is the head
+        // of a tile this CTA owns (starts at a tile boundary, ends inside the tile)
+        const bool last_is_head = n_sk > 0 && (u1 % KB) != 0 && ((u1 - 1) / KB) * KB >= u0;
+        lead = n_sk - (last_is_head ? 1 : 0);
     }
-    __device__ __forceinline__ int num_segs() const {
-        return n_sk + (c < T_dp ? (T_dp - c + G - 1) / G : 0);
-    }
-    // segment j: tile t, k-blocks [kb_s, kb_e); `partial` when the tile is shared (stream-K)
-    __device__ __forceinline__ void seg(int j, int& t, int& kb_s, int& kb_e) const {
-        if (j < n_sk) {
-            const int tr = static_cast<int>(u0 / KB) + j;
-            const int64_t tb = static_cast<int64_t>(tr) * KB;
-            kb_s = static_cast<int>(max(u0, tb) - tb);
-            kb_e = static_cast<int>(min(u1, tb + KB) - tb);
-            t = T_dp + tr;
+    __device__ __forceinline__ int num_segs() const { return n_sk + n_dp; }
+    // segment j: tile t, k-blocks [kb_s, kb_e); tr = stream-K tile index (relative to T_dp), or
+    // -1 for a data-parallel tile
+    __device__ __forceinline__ void seg(int j, int& t, int& kb_s, int& kb_e, int& tr) const {
+        if (j >= lead && j < lead + n_dp) {
+            t = c + (j - lead) * G;
+            kb_s = 0;
+            kb_e = KB;
+            tr = -1;
             return;
         }
-        t = c + (j - n_sk) * G;
-        kb_s = 0;
-        kb_e = KB;
+        const int js = j < lead ? j : j - n_dp;
+        tr = static_cast<int>(u0 / KB) + js;
+        const int64_t tb = static_cast<int64_t>(tr) * KB;
+        kb_s = static_cast<int>(max(u0, tb) - tb);
+        kb_e = static_cast<int>(min(u1, tb + KB) - tb);
+        t = T_dp + tr;
     }
 };
 
-constexpr int kMaxContrib = 8;  // partial tiles loaded at once by the reducing CTA
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_gpu(int* p, int v) {
+    asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 
 template <int BN, int EPI>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(kSkThreads, 1)
 gemm_sk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                void* __restrict__ y, unsigned long long* __restrict__ amax, int M, int N, int K,
-               int m_tiles, float* __restrict__ ws_part, int* __restrict__ ws_cnt, int id_off,
+               int m_tiles, int* __restrict__ ws_flag, float* __restrict__ ws_part, int id_off,
                int* err) {
     using Cfg = SkCfg<BN>;
     constexpr int ST = Cfg::kStages;
@@ -346,8 +371,8 @@ gemm_sk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     uint64_t* empty = full + ST;
     uint64_t* tfull = empty + ST;   // [2] accumulator ready
     uint64_t* tempty = tfull + 2;   // [2] accumulator drained
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
-    int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
+    uint64_t* pfull = tempty + 2;   // contributors' parts landed in the (drained) ring
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pfull + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     SkWork wk;
@@ -361,8 +386,9 @@ gemm_sk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], 4);
+            mbar_init(&tempty[a], kSkEpiWarps);
         }
+        mbar_init(pfull, 1);
         fence_barrier_init();
     }
     if (warp == 1) {
@@ -380,29 +406,52 @@ gemm_sk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
             tma_prefetch_desc(&tmap_x);
             const uint64_t pol_w = policy_evict_first();
             const uint64_t pol_x = policy_evict_last();
+            // Weight tiles of the first ST k-blocks go out before the dependency wait: weights
+            // are never written by a preceding kernel, so their fetch overlaps its tail.
+            int npre = 0;
+            for (int j = 0; j < nseg && npre < ST; ++j) {
+                int t, kb_s, kb_e, tr;
+                wk.seg(j, t, kb_s, kb_e, tr);
+                const int wrow = (t / m_tiles) * kBM;
+                for (int kb = kb_s; kb < kb_e && npre < ST; ++kb, ++npre) {
+                    mbar_arrive_expect_tx(&full[npre], Cfg::kStageBytes);
+                    tma_load_2d_hint(sA + npre * kTileA, &tmap_w, &full[npre], kb * kBK, wrow, pol_w);
+                }
+            }
+            pdl_wait();
+            pdl_trigger();
             int i = 0;
             bool ok = true;
             for (int j = 0; j < nseg && ok; ++j) {
-                int t, kb_s, kb_e;
-                wk.seg(j, t, kb_s, kb_e);
+                int t, kb_s, kb_e, tr;
+                wk.seg(j, t, kb_s, kb_e, tr);
                 const int wrow = (t / m_tiles) * kBM, xrow = (t % m_tiles) * BN;
                 for (int kb = kb_s; kb < kb_e; ++kb, ++i) {
                     const int s = i % ST;
+                    if (i < npre) {  // stage armed above: activation tile only
+                        tma_load_2d_hint(sB + s * Cfg::kTileB, &tmap_x, &full[s], kb * kBK, xrow, pol_x);
+                        continue;
+                    }
                     if (i >= ST && !mbar_wait(&empty[s], ((i / ST) - 1) & 1, err, 330)) { ok = false; break; }
                     mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
                     tma_load_2d_hint(sA + s * kTileA, &tmap_w, &full[s], kb * kBK, wrow, pol_w);
                     tma_load_2d_hint(sB + s * Cfg::kTileB, &tmap_x, &full[s], kb * kBK, xrow, pol_x);
                 }
             }
+        } else {
+            pdl_wait();
+            pdl_trigger();
         }
     } else if (warp == 1) {
+        pdl_wait();
+        pdl_trigger();
         if (lane == 0) {
             constexpr uint32_t idesc = umma_idesc_bf16(kBM, BN);
             int i = 0;
             bool ok = true;
             for (int j = 0; j < nseg && ok; ++j) {
-                int t, kb_s, kb_e;
-                wk.seg(j, t, kb_s, kb_e);
+                int t, kb_s, kb_e, tr;
+                wk.seg(j, t, kb_s, kb_e, tr);
                 const int a = j & 1;
                 if (j >= 2 && !mbar_wait(&tempty[a], ((j >> 1) - 1) & 1, err, 340)) break;
                 tc_fence_after();
@@ -423,57 +472,114 @@ gemm_sk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
             }
         }
     } else {
-        // ---------------- epilogue warps 2..5
+        // ---------------- epilogue warps 2..9 (named barrier 1 among them): warp w reads TMEM
+        // lane quarter w % 4 (rows) and every other 16-column chunk, starting at chunk eg
+        pdl_wait();
+        pdl_trigger();
         const int warp_q = warp & 3;
+        const int eg = (warp - 2) >> 2;
         const int row = warp_q * 32 + lane;
         const int et = threadIdx.x - 64;
+        constexpr int kEpiThreads = kSkEpiWarps * 32;
+        constexpr int64_t kPart = static_cast<int64_t>(kBM) * BN;  // floats of one part
         for (int j = 0; j < nseg; ++j) {
-            int t, kb_s, kb_e;
-            wk.seg(j, t, kb_s, kb_e);
+            int t, kb_s, kb_e, tr;
+            wk.seg(j, t, kb_s, kb_e, tr);
             const int a = j & 1;
             const bool have = mbar_wait(&tfull[a], (j >> 1) & 1, err, 350);
             tc_fence_after();
             const int n_tile = t / m_tiles, m_tile = t % m_tiles;
             const int n = n_tile * kBM + row, m0 = m_tile * BN;
             const uint32_t taddr = tmem + a * BN + (static_cast<uint32_t>(warp_q * 32) << 16);
-            if (j >= wk.n_sk || (kb_s == 0 && kb_e == wk.KB)) {
+            if (kb_s > 0) {
+                // ---- tail part of a tile owned by an earlier CTA: publish it (column-major
+                // [BN][128], so one warp store covers 32 consecutive rows) and raise the flag
+                float* part = ws_part + wk.c * kPart + row;
 #pragma unroll 1
-                for (int c0 = 0; c0 < BN; c0 += 16) {
+                for (int c0 = eg * 16; c0 < BN; c0 += 32) {
+                    uint32_t r[16];
+                    tmem_ld16(taddr + c0, r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int q = 0; q < 16; ++q)
+                        __stcg(part + (c0 + q) * kBM, have ? __uint_as_float(r[q]) : 0.f);
+                }
+                tc_fence_before();
+                __threadfence();
+                named_bar(1, kEpiThreads);
+                if (et == 0) st_release_gpu(ws_flag + wk.c, 1);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[a]);  // TMEM buffer free for segment j + 2
+                continue;
+            }
+            // ---- whole tile, or the head of a tile this CTA owns (always its last segment, so
+            // the smem ring has drained): pull the contributors' parts -- later CTAs, which
+            // published them at their start -- into the ring with bulk copies, as many per round
+            // trip as fit, and add them in CTA order to the accumulator (kept in TMEM between
+            // rounds), then run the epilogue.
+            const int ncontrib = kb_e < wk.KB
+                ? sk_cta_of(static_cast<int64_t>(tr) * wk.KB + wk.KB - 1, wk.U_sk, wk.G_sk) - wk.c : 0;
+            constexpr uint32_t kPartBytes = static_cast<uint32_t>(kPart * sizeof(float));
+            constexpr int kPerRound = (ST * Cfg::kStageBytes) / kPartBytes;
+            static_assert(kPerRound >= 1, "ring smaller than one part");
+            int done = 0, round = 0;
+            do {
+                const int nb = min(kPerRound, ncontrib - done);
+                if (nb > 0) {
+                    if (et == 0) {
+                        if (round > 0) fence_proxy_async();  // earlier reads before the overwrite
+                        mbar_arrive_expect_tx(pfull, nb * kPartBytes);
+                        for (int k = 0; k < nb; ++k) {
+                            const int cc = wk.c + 1 + done + k;
+                            const uint64_t t0 = globaltimer_ns();
+                            while (ld_acquire_gpu(ws_flag + cc) == 0) {
+                                if (globaltimer_ns() - t0 > 2000000000ull) {
+                                    record_error(err, MSGL_ERR_TIMEOUT, 360);
+                                    break;
+                                }
+                            }
+                            ws_flag[cc] = 0;  // consumed: the workspace is left zero-filled
+                            bulk_load(smem + k * kPartBytes, ws_part + cc * kPart, kPartBytes, pfull);
+                        }
+                    }
+                    if (!mbar_wait(pfull, round & 1, err, 361)) break;
+                }
+                const bool final_round = done + nb >= ncontrib;
+                const float* sp = reinterpret_cast<const float*>(smem) + row;
+#pragma unroll 1
+                for (int c0 = eg * 16; c0 < BN; c0 += 32) {
                     uint32_t r[16];
                     float v[16];
                     tmem_ld16(taddr + c0, r);
                     tmem_ld_wait();
 #pragma unroll
                     for (int q = 0; q < 16; ++q) v[q] = have ? __uint_as_float(r[q]) : 0.f;
-                    epilogue_chunk<EPI>(v, n, N, m0 + c0, M, y, amax, lane, warp_q, n_tile, id_off);
-                }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&tempty[a]);
-                continue;
-            }
-            // ---- stream-K partial tile: publish this CTA's fp32 part (slot 0: its first
-            // segment, slot 1: a later one); sk_fixup_kernel sums the parts of each split tile
-            const int my_slot = (j == 0) ? 0 : 1;
-            float* part = ws_part + ((static_cast<int64_t>(wk.c) * 2 + my_slot) * kBM + row) * BN;
-#pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 16) {
-                uint32_t r[16];
-                tmem_ld16(taddr + c0, r);
-                tmem_ld_wait();
-                float4* dst = reinterpret_cast<float4*>(part + c0);
+                    for (int k = 0; k < nb; ++k)
 #pragma unroll
-                for (int q = 0; q < 4; ++q)
-                    __stcg(dst + q, have ? make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
-                                                       __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]))
-                                         : make_float4(0.f, 0.f, 0.f, 0.f));
-            }
+                        for (int q = 0; q < 16; ++q) v[q] += sp[k * kPart + (c0 + q) * kBM];
+                    if (final_round) {
+                        epilogue_chunk<EPI>(v, n, N, m0 + c0, M, y, amax, lane, warp_q, n_tile, id_off);
+                    } else {
+#pragma unroll
+                        for (int q = 0; q < 16; ++q) r[q] = __float_as_uint(v[q]);
+                        tmem_st16(taddr + c0, r);
+                    }
+                }
+                if (final_round) break;
+                tmem_st_wait();
+                named_bar(1, kEpiThreads);  // every thread has read this round's parts
+                done += nb;
+                ++round;
+            } while (true);
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[a]);  // TMEM buffer free for segment j + 2
+            if (lane == 0) mbar_arrive(&tempty[a]);
         }
         tc_fence_before();
     }
+    // Lane 0 of warps 0 and 1 ran the producer / MMA loops alone: reconverge every warp before
+    // the block barrier (bar.sync counts whole warps), so TMEM is freed only after the epilogue.
+    __syncwarp();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
@@ -481,53 +587,244 @@ gemm_sk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     }
 }
 
-// Sums the contributors' fp32 parts of every split (stream-K) tile in CTA order --
-// deterministic -- and runs the epilogue. grid (split tiles, BN / 16 column chunks), 128
-// threads = the tile's 128 weight rows; every contributor's load of a chunk is in flight at once.
+// ============================================================================ cluster split-K
+// Decode-sized GEMMs (M <= 128 tokens, so one token tile): every output tile is computed by a
+// cluster of C CTAs, CTA rank r accumulating k-blocks [r KB / C, (r + 1) KB / C) in TMEM. The
+// tile's 16-column chunks are owned round-robin by the ranks (chunk ci by rank ci % C). After
+// its mainloop a CTA publishes the chunks it does not own (fp32, column-major [BN][128]) in its
+// own shared memory and arrives on the owners' `pready` mbarriers (remote arrive, release at
+// cluster scope); each owner then adds the peers' chunks -- read over distributed shared memory,
+// in rank order (deterministic) -- to its own TMEM accumulator and runs 1/C of the epilogue, and
+// arrives on the peers' `pfree` mbarriers once it no longer needs their buffers. No fp32
+// partials go to global memory and no second kernel runs. The cluster is persistent over tiles
+// q, q + n_clusters, ...; TMEM is double-buffered, so a tile's reduction and epilogue overlap
+// the next tile's mainloop. Producer warp, MMA warp and 8 epilogue warps as in the stream-K
+// kernel.
+template <int BN>
+struct ClCfg {
+    static constexpr int kTileB = BN * kBK * 2;
+    static constexpr int kStageBytes = kTileA + kTileB;
+    static constexpr int kStages = BN >= 128 ? 4 : (BN >= 64 ? 5 : 6);
+    static constexpr int kPartBytes = kBM * BN * 4;
+    static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+    static constexpr size_t kSmem =
+        static_cast<size_t>(kStages) * kStageBytes + kPartBytes + 1024 + 256;
+};
+constexpr int kClMaxC = 8;
+
 template <int BN, int EPI>
-__global__ void __launch_bounds__(128)
-sk_fixup_kernel(const float* __restrict__ ws_part, void* __restrict__ y,
-                unsigned long long* __restrict__ amax, int M, int N, int K, int m_tiles,
-                int G, int id_off) {
-    SkWork wk;
-    wk.init(m_tiles * ((N + kBM - 1) / kBM), (K + kBK - 1) / kBK, G, 0);
-    const int t_rel = blockIdx.x, c0 = blockIdx.y * 16;
-    const int t = wk.T_dp + t_rel;
-    const int row = threadIdx.x, lane = threadIdx.x & 31, warp_q = threadIdx.x >> 5;
-    const int64_t tb = static_cast<int64_t>(t_rel) * wk.KB;
-    const int first = sk_cta_of(tb, wk.U_sk, wk.G_sk);
-    const int last = sk_cta_of(tb + wk.KB - 1, wk.U_sk, wk.G_sk);
-    float acc[16];
-#pragma unroll
-    for (int q = 0; q < 16; ++q) acc[q] = 0.f;
-    for (int g0 = first; g0 <= last; g0 += kMaxContrib) {
-        float4 buf[kMaxContrib][4];
-#pragma unroll
-        for (int k = 0; k < kMaxContrib; ++k) {
-            const int cc = g0 + k;
-            if (cc <= last) {
-                const int slot = (static_cast<int64_t>(cc) * wk.U_sk / wk.G_sk) / wk.KB == t_rel ? 0 : 1;
-                const float4* src = reinterpret_cast<const float4*>(
-                    ws_part + ((static_cast<int64_t>(cc) * 2 + slot) * kBM + row) * BN + c0);
-#pragma unroll
-                for (int q = 0; q < 4; ++q) buf[k][q] = __ldcg(src + q);
-            }
+__global__ void __launch_bounds__(kSkThreads, 1)
+gemm_cl_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+               void* __restrict__ y, unsigned long long* __restrict__ amax, int M, int N, int K,
+               int id_off, int* err) {
+    using Cfg = ClCfg<BN>;
+    constexpr int ST = Cfg::kStages;
+    constexpr int NCH = BN / 16;  // 16-column chunks per tile
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + ST * kTileA;
+    float* part = reinterpret_cast<float*>(smem + ST * Cfg::kStageBytes);  // [BN][128]
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + ST * Cfg::kStageBytes + Cfg::kPartBytes);
+    uint64_t* empty = full + ST;
+    uint64_t* tfull = empty + ST;   // [2] accumulator ready
+    uint64_t* tempty = tfull + 2;   // [2] accumulator drained
+    uint64_t* pready = tempty + 2;  // peers' chunks for me are published
+    uint64_t* pfree = pready + 1;   // peers are done with my published chunks
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pfree + 1);
+    volatile int* verdict = reinterpret_cast<volatile int*>(tmem_slot + 1);  // epilogue broadcast
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int C = static_cast<int>(cluster_nctarank());
+    const int rank = static_cast<int>(cluster_ctarank());
+    const int n_clusters = static_cast<int>(nclusters_x());
+    const int q = static_cast<int>(cluster_id_x());
+    const int n_tiles = (N + kBM - 1) / kBM;
+    const int KB = (K + kBK - 1) / kBK;
+    const int kb0 = rank * KB / C, kb1 = (rank + 1) * KB / C;
+    const int my_tiles = q < n_tiles ? (n_tiles - q + n_clusters - 1) / n_clusters : 0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < ST; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
         }
-#pragma unroll
-        for (int k = 0; k < kMaxContrib; ++k) {
-            if (g0 + k > last) break;
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                acc[4 * q] += buf[k][q].x;
-                acc[4 * q + 1] += buf[k][q].y;
-                acc[4 * q + 2] += buf[k][q].z;
-                acc[4 * q + 3] += buf[k][q].w;
-            }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], kSkEpiWarps);
         }
+        mbar_init(pready, C > 1 ? C - 1 : 1);
+        mbar_init(pfree, C > 1 ? C - 1 : 1);
+        fence_barrier_init();
     }
-    const int n_tile = t / m_tiles, m_tile = t % m_tiles;
-    epilogue_chunk<EPI>(acc, n_tile * kBM + row, N, m_tile * BN + c0, M, y, amax, lane, warp_q,
-                        n_tile, id_off);
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, Cfg::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    cluster_sync_all();  // barriers of every CTA initialised before any remote arrive
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            tma_prefetch_desc(&tmap_w);
+            tma_prefetch_desc(&tmap_x);
+            const uint64_t pol_w = policy_evict_first();
+            const uint64_t pol_x = policy_evict_last();
+            // weight tiles of the first ST k-blocks before the dependency wait (see gemm_sk_kernel)
+            int npre = 0;
+            for (int i = 0; i < my_tiles && npre < ST; ++i) {
+                const int wrow = (q + i * n_clusters) * kBM;
+                for (int kb = kb0; kb < kb1 && npre < ST; ++kb, ++npre) {
+                    mbar_arrive_expect_tx(&full[npre], Cfg::kStageBytes);
+                    tma_load_2d_hint(sA + npre * kTileA, &tmap_w, &full[npre], kb * kBK, wrow, pol_w);
+                }
+            }
+            pdl_wait();
+            pdl_trigger();
+            int it = 0;
+            bool ok = true;
+            for (int i = 0; i < my_tiles && ok; ++i) {
+                const int wrow = (q + i * n_clusters) * kBM;
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
+                    const int s = it % ST;
+                    if (it < npre) {
+                        tma_load_2d_hint(sB + s * Cfg::kTileB, &tmap_x, &full[s], kb * kBK, 0, pol_x);
+                        continue;
+                    }
+                    if (it >= ST && !mbar_wait(&empty[s], ((it / ST) - 1) & 1, err, 430)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
+                    tma_load_2d_hint(sA + s * kTileA, &tmap_w, &full[s], kb * kBK, wrow, pol_w);
+                    tma_load_2d_hint(sB + s * Cfg::kTileB, &tmap_x, &full[s], kb * kBK, 0, pol_x);
+                }
+            }
+        } else {
+            pdl_wait();
+            pdl_trigger();
+        }
+    } else if (warp == 1) {
+        pdl_wait();
+        pdl_trigger();
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_bf16(kBM, BN);
+            int it = 0;
+            bool ok = true;
+            for (int i = 0; i < my_tiles && ok; ++i) {
+                const int a = i & 1;
+                if (i >= 2 && !mbar_wait(&tempty[a], ((i >> 1) - 1) & 1, err, 440)) break;
+                tc_fence_after();
+                const uint32_t acc = tmem + a * BN;
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
+                    const int s = it % ST;
+                    if (!mbar_wait(&full[s], (it / ST) & 1, err, 441)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(sA + s * kTileA);
+                    const uint32_t b_addr = smem_u32(sB + s * Cfg::kTileB);
+#pragma unroll
+                    for (int k = 0; k < kBK / 16; ++k)
+                        umma_bf16(acc, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32),
+                                  idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+                    umma_commit(&empty[s]);
+                }
+                umma_commit(&tfull[a]);
+            }
+        }
+    } else {
+        // ---------------- epilogue warps 2..9: warp w reads TMEM lane quarter w % 4; the two warp
+        // groups eg = 0, 1 take alternate chunks of the lists below
+        pdl_wait();
+        pdl_trigger();
+        const int warp_q = warp & 3;
+        const int eg = (warp - 2) >> 2;
+        const int row = warp_q * 32 + lane;
+        const int et = threadIdx.x - 64;
+        constexpr int kEpiThreads = kSkEpiWarps * 32;
+        const uint32_t part_u32 = smem_u32(part);
+        for (int i = 0; i < my_tiles; ++i) {
+            const int a = i & 1;
+            const int n_tile = q + i * n_clusters;
+            const int n = n_tile * kBM + row;
+            // One thread waits (bounded) for the accumulator and, from tile 1 on, for the peers to
+            // be done with this CTA's buffer; the verdict is broadcast so that every epilogue warp
+            // takes the same path through the named barriers below.
+            if (et == 0)
+                *verdict = mbar_wait(&tfull[a], (i >> 1) & 1, err, 450) &&
+                           (C == 1 || i == 0 || mbar_wait_cluster(pfree, (i - 1) & 1, err, 451));
+            named_bar(1, kEpiThreads);
+            const bool ok_acc = *verdict != 0;
+            named_bar(1, kEpiThreads);  // verdict read by all before it is rewritten
+            if (!ok_acc) break;
+            tc_fence_after();
+            const uint32_t taddr = tmem + a * BN + (static_cast<uint32_t>(warp_q * 32) << 16);
+            if (C > 1) {
+                // publish the chunks the peers own
+                int j = 0;
+                for (int ci = 0; ci < NCH; ++ci) {
+                    if (ci % C == rank) continue;
+                    if ((j++ & 1) != eg) continue;
+                    uint32_t r[16];
+                    tmem_ld16(taddr + ci * 16, r);
+                    tmem_ld_wait();
+                    float* dst = part + ci * 16 * kBM + row;
+#pragma unroll
+                    for (int qq = 0; qq < 16; ++qq) dst[qq * kBM] = __uint_as_float(r[qq]);
+                }
+                fence_acq_rel_cluster();
+                named_bar(1, kEpiThreads);
+                if (et < C && et != rank)  // one thread per peer
+                    mbar_remote_arrive(mapa_shared(smem_u32(pready), et));
+                if (et == 0) *verdict = mbar_wait_cluster(pready, i & 1, err, 452);
+                named_bar(1, kEpiThreads);
+                const bool ok_peers = *verdict != 0;
+                named_bar(1, kEpiThreads);
+                if (!ok_peers) break;
+            }
+            // my chunks: own accumulator + the peers' published parts, in rank order
+            int j = 0;
+            for (int ci = rank; ci < NCH; ci += C) {
+                if ((j++ & 1) != eg) continue;
+                uint32_t r[16];
+                float v[16];
+                tmem_ld16(taddr + ci * 16, r);
+                tmem_ld_wait();
+#pragma unroll
+                for (int qq = 0; qq < 16; ++qq) v[qq] = 0.f;
+                for (int pr = 0; pr < C; ++pr) {
+                    if (pr == rank) {
+#pragma unroll
+                        for (int qq = 0; qq < 16; ++qq) v[qq] += __uint_as_float(r[qq]);
+                    } else {
+                        const uint32_t src = mapa_shared(part_u32 + (ci * 16 * kBM + row) * 4, pr);
+                        float pv[16];
+#pragma unroll
+                        for (int qq = 0; qq < 16; ++qq) pv[qq] = ld_dsmem_f32(src + qq * kBM * 4);
+#pragma unroll
+                        for (int qq = 0; qq < 16; ++qq) v[qq] += pv[qq];
+                    }
+                }
+                epilogue_chunk<EPI>(v, n, N, ci * 16, M, y, amax, lane, warp_q, n_tile, id_off);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[a]);
+            if (C > 1) {
+                fence_acq_rel_cluster();
+                named_bar(1, kEpiThreads);
+                if (et < C && et != rank)  // done reading peer et's buffer
+                    mbar_remote_arrive(mapa_shared(smem_u32(pfree), et));
+            }
+        }
+        tc_fence_before();
+    }
+    __syncwarp();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, Cfg::kTmemCols);
+    }
+    cluster_sync_all();  // no CTA leaves while a peer may still read its shared memory
 }
 
 int num_sms() {
@@ -543,9 +840,9 @@ int num_sms() {
     return n[dev];
 }
 
-// Stream-K workspace: 2 fp32 tile slots per CTA (no persistent state between calls).
+// Stream-K workspace: one flag per CTA (zero when idle), then one fp32 part slot per CTA.
 size_t sk_workspace_bytes(int bn, int sms) {
-    return static_cast<size_t>(sms) * 2 * kBM * bn * sizeof(float);
+    return kSkFlagBytes + static_cast<size_t>(sms) * kBM * bn * sizeof(float);
 }
 
 struct GemmPlan {
@@ -598,7 +895,7 @@ int launch_bn(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& tx, v
                          static_cast<int>(Cfg::kSmem));
     dim3 grid(p.m_tiles, p.n_tiles, p.splits);
     uint8_t* w8 = static_cast<uint8_t*>(ws);
-    gemm_kernel<BN, EPI, GROUPED><<<grid, kGemmThreads, Cfg::kSmem, stream>>>(
+    launch_pdl(gemm_kernel<BN, EPI, GROUPED>, grid, dim3(kGemmThreads), Cfg::kSmem, stream,
         tw, tx, y, amax, M, N, K, p.kb_per_split, p.splits,
         p.splits > 1 ? reinterpret_cast<float*>(w8 + kCounterBytes) : nullptr,
         p.splits > 1 ? reinterpret_cast<int*>(w8 + p.ws_cnt_off) : nullptr, grp, id_off, err);
@@ -616,19 +913,100 @@ int launch_sk(const CUtensorMap& tw, const CUtensorMap& tx, void* y, unsigned lo
                          static_cast<int>(Cfg::kSmem));
     const int m_tiles = (M + BN - 1) / BN;
     const int64_t units = static_cast<int64_t>(m_tiles) * ((N + kBM - 1) / kBM) * ((K + kBK - 1) / kBK);
-    const int G = static_cast<int>(std::min<int64_t>(sms, units));
-    float* part = static_cast<float*>(ws);
-    gemm_sk_kernel<BN, EPI><<<G, kGemmThreads, Cfg::kSmem, stream>>>(
-        tw, tx, y, amax, M, N, K, m_tiles, part, nullptr, id_off, err);
+    const int G = static_cast<int>(std::min<int64_t>(std::min(sms, kSkMaxCtas), units));
+    uint8_t* w8 = static_cast<uint8_t*>(ws);
+    launch_pdl(gemm_sk_kernel<BN, EPI>, dim3(G), dim3(kSkThreads), Cfg::kSmem, stream,
+        tw, tx, y, amax, M, N, K, m_tiles, reinterpret_cast<int*>(w8),
+        reinterpret_cast<float*>(w8 + kSkFlagBytes), id_off, err);
     MSGL_LAUNCH_CHECK();
-    // split tiles of the stream-K remainder: same schedule arithmetic as SkWork::init
-    const int T = m_tiles * ((N + kBM - 1) / kBM);
-    const int T_rem = T - (T >= G ? (T / G) * G : 0);
-    if (T_rem > 0) {
-        sk_fixup_kernel<BN, EPI><<<dim3(T_rem, BN / 16), 128, 0, stream>>>(
-            part, y, amax, M, N, K, m_tiles, G, id_off);
-        MSGL_LAUNCH_CHECK();
+    return MSGL_OK;
+}
+
+// Cluster split-K launch: grid = n_clusters clusters of C CTAs (cluster dims C x 1 x 1),
+// programmatic stream serialisation as every kernel of the forward path.
+template <int BN, int EPI>
+cudaError_t launch_cl_raw(const CUtensorMap& tw, const CUtensorMap& tx, void* y,
+                          unsigned long long* amax, int M, int N, int K, int C, int n_clusters,
+                          int id_off, int* err, cudaStream_t stream) {
+    using Cfg = ClCfg<BN>;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(n_clusters * C);
+    cfg.blockDim = dim3(kSkThreads);
+    cfg.dynamicSmemBytes = Cfg::kSmem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = C;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, gemm_cl_kernel<BN, EPI>, tw, tx, y, amax, M, N, K, id_off, err);
+}
+
+// Co-resident clusters of C CTAs of gemm_cl_kernel<BN, EPI> on this device (cached).
+template <int BN, int EPI>
+int cl_max_clusters(int C) {
+    static int cache[64][kClMaxC + 1] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    if (cache[dev][C]) return cache[dev][C] > 0 ? cache[dev][C] : 0;
+    using Cfg = ClCfg<BN>;
+    cudaFuncSetAttribute(gemm_cl_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(Cfg::kSmem));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(C * 64);
+    cfg.blockDim = dim3(kSkThreads);
+    cfg.dynamicSmemBytes = Cfg::kSmem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = C;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_cl_kernel<BN, EPI>, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
     }
+    cache[dev][C] = n > 0 ? n : -1;
+    return n;
+}
+
+// Cluster size for a decode GEMM of T tiles x KB k-blocks: the C in 1..8 (C <= KB) with the
+// fewest k-blocks per CTA over all waves, ceil(T / clusters) * ceil(KB / C); ties go to the
+// smaller C (less reduction traffic).
+template <int BN, int EPI>
+void plan_cl(int T, int KB, int& C_best, int& n_clusters) {
+    int64_t best = -1;
+    C_best = 1;
+    n_clusters = 0;
+    for (int C = 1; C <= kClMaxC && C <= KB; ++C) {
+        const int nc = cl_max_clusters<BN, EPI>(C);
+        if (nc <= 0) continue;
+        const int64_t cost = static_cast<int64_t>((T + nc - 1) / nc) * ((KB + C - 1) / C);
+        if (best < 0 || cost < best) {
+            best = cost;
+            C_best = C;
+            n_clusters = std::min(nc, T);
+        }
+    }
+}
+
+template <int BN, int EPI>
+int launch_cl(const CUtensorMap& tw, const CUtensorMap& tx, void* y, unsigned long long* amax,
+              int M, int N, int K, cudaStream_t stream, int id_off) {
+    int* err = device_error_word();
+    if (!err) return set_error(MSGL_ERR_CUDA, "device error word unavailable");
+    const int T = (N + kBM - 1) / kBM, KB = (K + kBK - 1) / kBK;
+    int C = 1, nc = 0;
+    plan_cl<BN, EPI>(T, KB, C, nc);
+    if (nc <= 0) return set_error(MSGL_ERR_CUDA, "gemm: no cluster configuration fits");
+    cudaError_t e = launch_cl_raw<BN, EPI>(tw, tx, y, amax, M, N, K, C, nc, id_off, err, stream);
+    if (e != cudaSuccess) return set_error(MSGL_ERR_CUDA, cudaGetErrorString(e));
     return MSGL_OK;
 }
 
@@ -646,10 +1024,20 @@ int run_gemm(const void* x, const void* w, void* y, unsigned long long* amax, in
     if (rc) return rc;
     rc = make_tmap_2d_bf16(&tx, x, K, M, static_cast<uint64_t>(K) * 2, kBK, bn, true);
     if (rc) return rc;
+    if (bn <= 128) {  // one token tile: cluster split-K, no workspace needed
+        switch (bn) {
+            case 16: return launch_cl<16, EPI>(tw, tx, y, amax, M, N, K, stream, id_off);
+            case 32: return launch_cl<32, EPI>(tw, tx, y, amax, M, N, K, stream, id_off);
+            case 64: return launch_cl<64, EPI>(tw, tx, y, amax, M, N, K, stream, id_off);
+            default: return launch_cl<128, EPI>(tw, tx, y, amax, M, N, K, stream, id_off);
+        }
+    }
     if (tiles <= static_cast<int64_t>(kCounterBytes / sizeof(int))) {
         const int sms = num_sms();
         if (!ws || ws_bytes < sk_workspace_bytes(bn, sms))
             return set_error(MSGL_ERR_WORKSPACE, "gemm: workspace too small");
+        if (reinterpret_cast<uintptr_t>(ws) & 15)
+            return set_error(MSGL_ERR_INVALID_ARG, "gemm: workspace must be 16-byte aligned");
         switch (bn) {
             case 16: return launch_sk<16, EPI>(tw, tx, y, amax, M, N, K, ws, sms, stream, id_off);
             case 32: return launch_sk<32, EPI>(tw, tx, y, amax, M, N, K, ws, sms, stream, id_off);
@@ -675,6 +1063,8 @@ int run_gemm(const void* x, const void* w, void* y, unsigned long long* amax, in
 __global__ void group_tiles_kernel(const int* __restrict__ offsets, int E, int bn,
                                    int2* __restrict__ tiles, int* __restrict__ num_tiles) {
     __shared__ int pre[1025];
+    pdl_wait();
+    pdl_trigger();
     const int e = threadIdx.x;
     int cnt = 0, beg = 0;
     if (e < E) {
@@ -707,7 +1097,7 @@ int run_grouped(const void* x, const void* w, void* y, const int* offsets, int E
     if (max_tiles > 65535 * 8) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "grouped gemm: too many tiles");
     int* num_tiles = static_cast<int*>(ws);
     int2* tiles = reinterpret_cast<int2*>(static_cast<uint8_t*>(ws) + 256);
-    group_tiles_kernel<<<1, E, 0, stream>>>(offsets, E, bn, tiles, num_tiles);
+    launch_pdl(group_tiles_kernel, dim3(1), dim3(E), 0, stream, offsets, E, bn, tiles, num_tiles);
     MSGL_LAUNCH_CHECK();
     CUtensorMap tw, tx;
     int rc = make_tmap_2d_bf16(&tw, w, K, static_cast<uint64_t>(E) * N, static_cast<uint64_t>(K) * 2,
@@ -742,6 +1132,8 @@ __global__ void pack_gate_up_kernel(const uint4* __restrict__ src, uint4* __rest
 
 __global__ void unpack_argmax_kernel(unsigned long long* __restrict__ packed, int* __restrict__ ids,
                                      int M) {
+    pdl_wait();
+    pdl_trigger();
     int m = blockIdx.x * blockDim.x + threadIdx.x;
     if (m < M) ids[m] = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(packed[m] & 0xFFFFFFFFull));
 }
@@ -749,6 +1141,8 @@ __global__ void unpack_argmax_kernel(unsigned long long* __restrict__ packed, in
 template <typename T>
 __global__ void argmax_rows_kernel(const T* __restrict__ logits, int vocab, int* __restrict__ out) {
     __shared__ unsigned long long red[8];
+    pdl_wait();
+    pdl_trigger();
     const T* r = logits + static_cast<int64_t>(blockIdx.x) * vocab;
     unsigned long long best = 0ull;
     for (int v = threadIdx.x; v < vocab; v += blockDim.x) {
@@ -854,7 +1248,7 @@ int msgl_lm_head_argmax(const void* x, const void* w, int M, int vocab, int K,
     int rc = run_gemm<EPI_ARGMAX>(x, w, nullptr, packed, M, vocab, K, workspace, workspace_bytes,
                                   stream);
     if (rc) return rc;
-    unpack_argmax_kernel<<<(M + 255) / 256, 256, 0, stream>>>(packed, ids, M);
+    launch_pdl(unpack_argmax_kernel, dim3((M + 255) / 256), dim3(256), 0, stream, packed, ids, M);
     MSGL_LAUNCH_CHECK();
     return MSGL_OK;
 }
@@ -876,11 +1270,11 @@ int msgl_argmax(const void* logits, int num_rows, int vocab, int dtype, int* out
     if (num_rows < 0 || vocab <= 0) return set_error(MSGL_ERR_INVALID_ARG, "argmax: bad sizes");
     if (num_rows == 0) return MSGL_OK;
     if (dtype == MSGL_F32)
-        argmax_rows_kernel<float><<<num_rows, 256, 0, stream>>>(static_cast<const float*>(logits),
-                                                                vocab, out);
+        launch_pdl(argmax_rows_kernel<float>, dim3(num_rows), dim3(256), 0, stream,
+                   static_cast<const float*>(logits), vocab, out);
     else if (dtype == MSGL_BF16)
-        argmax_rows_kernel<__nv_bfloat16><<<num_rows, 256, 0, stream>>>(
-            static_cast<const __nv_bfloat16*>(logits), vocab, out);
+        launch_pdl(argmax_rows_kernel<__nv_bfloat16>, dim3(num_rows), dim3(256), 0, stream,
+                   static_cast<const __nv_bfloat16*>(logits), vocab, out);
     else
         return set_error(MSGL_ERR_INVALID_ARG, "argmax: unknown dtype");
     MSGL_LAUNCH_CHECK();

@@ -26,6 +26,8 @@ constexpr int kMaxPerLane = 8;
 
 __global__ void route_topk_kernel(const float* __restrict__ logits, int T, int E, int top_k,
                                   int norm_topk, int* __restrict__ ids, float* __restrict__ w) {
+    pdl_wait();
+    pdl_trigger();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (warp >= T) return;
@@ -90,6 +92,8 @@ permute_kernel(const int* __restrict__ ids, int num_pairs, int top_k, int E,
                int* __restrict__ offsets, int* __restrict__ sorted_token,
                int* __restrict__ pair_pos, int* err) {
     extern __shared__ int sm[];
+    pdl_wait();
+    pdl_trigger();
     int* base = sm;                       // [E] running start of each expert
     int* wcnt = sm + E;                   // [kPermWarps][E]
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -151,6 +155,8 @@ permute_kernel(const int* __restrict__ ids, int num_pairs, int top_k, int E,
 __global__ void combine_kernel(const __nv_bfloat16* __restrict__ y, const int* __restrict__ pair_pos,
                                const float* __restrict__ w, int top_k, int hidden,
                                __nv_bfloat16* __restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     const int t = blockIdx.x;
     for (int h8 = threadIdx.x; h8 * 8 < hidden; h8 += blockDim.x) {
         float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
@@ -186,8 +192,8 @@ int msgl_moe_route_topk(const float* router_logits, int num_tokens, int num_expe
     if (num_tokens == 0) return MSGL_OK;
     const int threads = 256;
     const int blocks = (num_tokens * 32 + threads - 1) / threads;
-    route_topk_kernel<<<blocks, threads, 0, stream>>>(router_logits, num_tokens, num_experts, top_k,
-                                                      norm_topk, topk_ids, topk_weights);
+    launch_pdl(route_topk_kernel, dim3(blocks), dim3(threads), 0, stream, router_logits,
+               num_tokens, num_experts, top_k, norm_topk, topk_ids, topk_weights);
     MSGL_LAUNCH_CHECK();
     return MSGL_OK;
 }
@@ -201,9 +207,8 @@ int msgl_moe_permute(const int* topk_ids, int num_tokens, int top_k, int num_exp
     const size_t smem = static_cast<size_t>(num_experts) * (kPermWarps + 1) * sizeof(int);
     cudaFuncSetAttribute(permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(smem));
-    permute_kernel<<<1, kPermThreads, smem, stream>>>(topk_ids, num_tokens * top_k, top_k,
-                                                      num_experts, expert_offsets, sorted_token,
-                                                      pair_pos, err);
+    launch_pdl(permute_kernel, dim3(1), dim3(kPermThreads), smem, stream, topk_ids,
+               num_tokens * top_k, top_k, num_experts, expert_offsets, sorted_token, pair_pos, err);
     MSGL_LAUNCH_CHECK();
     return MSGL_OK;
 }
@@ -213,9 +218,9 @@ int msgl_moe_combine(const void* y_sorted, const int* pair_pos, const float* top
     if (num_tokens < 0 || top_k <= 0 || hidden <= 0 || hidden % 8)
         return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "moe_combine: hidden % 8");
     if (num_tokens == 0) return MSGL_OK;
-    combine_kernel<<<num_tokens, 128, 0, stream>>>(static_cast<const __nv_bfloat16*>(y_sorted),
-                                                    pair_pos, topk_weights, top_k, hidden,
-                                                    static_cast<__nv_bfloat16*>(out));
+    launch_pdl(combine_kernel, dim3(num_tokens), dim3(128), 0, stream,
+               static_cast<const __nv_bfloat16*>(y_sorted), pair_pos, topk_weights, top_k, hidden,
+               static_cast<__nv_bfloat16*>(out));
     MSGL_LAUNCH_CHECK();
     return MSGL_OK;
 }

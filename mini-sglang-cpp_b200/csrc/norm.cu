@@ -55,6 +55,8 @@ rmsnorm_kernel(const T* x_in, T* x_out, float* __restrict__ resid,
                const T* __restrict__ w, const int* __restrict__ ids, int vocab, int hidden,
                float eps) {
     __shared__ float red[4];
+    pdl_wait();
+    pdl_trigger();
     const int row = blockIdx.x;
     const int nvec = hidden >> 3;
     const T* src = x_in + static_cast<int64_t>(row) * hidden;
@@ -115,8 +117,8 @@ int launch_norm(const T* x_in, T* x_out, float* resid, const T* w, const int* id
     dim3 grid(num_tokens), block(kNormThreads);
 #define MSGL_NORM_CASE(N)                                                                   \
     case N:                                                                                 \
-        rmsnorm_kernel<T, MODE, N><<<grid, block, 0, stream>>>(x_in, x_out, resid, w, ids,  \
-                                                               vocab, hidden, eps);         \
+        launch_pdl(rmsnorm_kernel<T, MODE, N>, grid, block, 0, stream, x_in, x_out, resid, w, \
+                   ids, vocab, hidden, eps);                                                \
         break;
     switch (vpt) {
         MSGL_NORM_CASE(1) MSGL_NORM_CASE(2) MSGL_NORM_CASE(3) MSGL_NORM_CASE(4)
@@ -131,6 +133,8 @@ int launch_norm(const T* x_in, T* x_out, float* resid, const T* w, const int* id
 template <typename T>
 __global__ void index_gather_kernel(const T* __restrict__ in, const int* __restrict__ idx,
                                     T* __restrict__ out, int hidden, int num_rows) {
+    pdl_wait();
+    pdl_trigger();
     int i = blockIdx.x;
     int id = idx[i];
     bool valid = id >= 0 && id < num_rows;
@@ -189,13 +193,13 @@ int msgl_launch_index_gather(const void* input, const int* indices, void* output
     if (num_indices < 0 || hidden_size <= 0) return set_error(MSGL_ERR_INVALID_ARG, "index_gather: sizes");
     if (num_indices == 0) return MSGL_OK;
     if (dtype == MSGL_BF16)
-        index_gather_kernel<__nv_bfloat16><<<num_indices, 128, 0, stream>>>(
-            static_cast<const __nv_bfloat16*>(input), indices, static_cast<__nv_bfloat16*>(output),
-            hidden_size, num_rows);
+        launch_pdl(index_gather_kernel<__nv_bfloat16>, dim3(num_indices), dim3(128), 0, stream,
+                   static_cast<const __nv_bfloat16*>(input), indices,
+                   static_cast<__nv_bfloat16*>(output), hidden_size, num_rows);
     else if (dtype == MSGL_F32)
-        index_gather_kernel<float><<<num_indices, 128, 0, stream>>>(
-            static_cast<const float*>(input), indices, static_cast<float*>(output), hidden_size,
-            num_rows);
+        launch_pdl(index_gather_kernel<float>, dim3(num_indices), dim3(128), 0, stream,
+                   static_cast<const float*>(input), indices, static_cast<float*>(output),
+                   hidden_size, num_rows);
     else
         return set_error(MSGL_ERR_INVALID_ARG, "index_gather: unknown dtype");
     MSGL_LAUNCH_CHECK();

@@ -75,6 +75,8 @@ qknorm_rope_store_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* _
                          const int* __restrict__ slots, const float* __restrict__ cs_table,
                          const __nv_bfloat16* __restrict__ qn, const __nv_bfloat16* __restrict__ kn,
                          int num_tokens, int hq, int hkv, float eps, int* err) {
+    pdl_wait();
+    pdl_trigger();
     const int nh = hq + 2 * hkv;
     const int lane = threadIdx.x & 31;
     const int64_t wid = static_cast<int64_t>(blockIdx.x) * kQkvWarps + (threadIdx.x >> 5);
@@ -201,7 +203,7 @@ int msgl_qknorm_rope_store_kv(const void* qkv, void* q_out, void* k_pool, void* 
     if (!err) return set_error(MSGL_ERR_CUDA, "device error word unavailable");
     int64_t warps = static_cast<int64_t>(num_tokens) * (num_q_heads + 2 * num_kv_heads);
     int blocks = static_cast<int>((warps + kQkvWarps - 1) / kQkvWarps);
-    qknorm_rope_store_kernel<<<blocks, kQkvWarps * 32, 0, stream>>>(
+    launch_pdl(qknorm_rope_store_kernel, dim3(blocks), dim3(kQkvWarps * 32), 0, stream,
         static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(q_out),
         static_cast<__nv_bfloat16*>(k_pool), static_cast<__nv_bfloat16*>(v_pool), num_slots,
         positions, slot_mapping, cos_sin_cache, static_cast<const __nv_bfloat16*>(q_norm_w),

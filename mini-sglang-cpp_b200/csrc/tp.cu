@@ -30,6 +30,8 @@ int nccl_err(ncclResult_t r, const char* what) {
 
 __global__ void unpack_keys_kernel(const unsigned long long* __restrict__ packed,
                                    int* __restrict__ ids, int M) {
+    pdl_wait();
+    pdl_trigger();
     int m = blockIdx.x * blockDim.x + threadIdx.x;
     if (m < M) ids[m] = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(packed[m] & 0xFFFFFFFFull));
 }
@@ -107,7 +109,8 @@ int msgl_tp_argmax_combine(msgl_tp* tp, unsigned long long* packed, int* ids, in
                                        ncclMax, tp->comm, stream);
         if (r != ncclSuccess) return nccl_err(r, "ncclAllReduce(max)");
     }
-    unpack_keys_kernel<<<(num_rows + 255) / 256, 256, 0, stream>>>(packed, ids, num_rows);
+    launch_pdl(unpack_keys_kernel, dim3((num_rows + 255) / 256), dim3(256), 0, stream, packed, ids,
+               num_rows);
     MSGL_LAUNCH_CHECK();
     return MSGL_OK;
 }
