@@ -82,6 +82,12 @@ def decode_batch_host(pt, vocab, seed=1):
 
 
 # ------------------------------------------------------------------------------ clocks
+# DRAM bytes (read + write) of one paged_decode_kernel launch at this workload, from the ncu
+# capture summarised in profiles/paged_decode_b128_ctx2048_hkv8.md (548.2 MB read + 13.4 MB
+# written; the algorithmic unique K+V bytes are 541.1 MB).
+PAGED_DECODE_TRAFFIC_BYTES = 561_577_984
+
+
 class ClockSampler:
     """nvidia-smi clock / throttle-reason samples of this rank's GPU during the timed region."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -98,22 +104,29 @@ class ClockSampler:
             pass
 
     def __enter__(self):
+        self.first = ""
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
                                        "--format=csv,noheader,nounits", "-lms", "100"],
                                       stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.p = None
+        if self.p:  # the timed region starts once the sampler is producing samples
+            import select
+            r, _, _ = select.select([self.p.stdout], [], [], 10.0)
+            if r:
+                self.first = self.p.stdout.readline()
         return self
 
     def __exit__(self, *a):
         if self.p:
             self.p.terminate()
             try:
-                self.out, _ = self.p.communicate(timeout=5)
+                rest, _ = self.p.communicate(timeout=5)
+                self.out = self.first + (rest or "")
             except subprocess.TimeoutExpired:
                 self.p.kill()
-                self.out = ""
+                self.out = self.first
 
     def summary(self):
         sm, mx, reasons = [], 0, set()
@@ -389,7 +402,7 @@ def run_ours(args, rank, world, local_rank):
                     "ms_per_step": ms_e2e},
             "roofline": {"kernel": "paged_decode_kernel", "bound": "hbm",
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None,
+                         "frac": achieved / peak, "traffic": PAGED_DECODE_TRAFFIC_BYTES,
                          "algorithmic_bytes_per_launch": unique_bytes,
                          "per_request_bytes_per_launch": per_request_bytes,
                          "launch_ms": attn_ms,
@@ -533,7 +546,7 @@ def run_breakdown(args, dev):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--case", choices=["attention", "gemm", "gemm_qkv", "breakdown"], default=None,

@@ -978,9 +978,9 @@ int cl_max_clusters(int C) {
 
 // Cluster size for a decode GEMM of T tiles x KB k-blocks: the C in 1..8 (C <= KB) with the
 // fewest k-blocks per CTA over all waves, ceil(T / clusters) * ceil(KB / C); ties go to the
-// smaller C (less reduction traffic).
+// smaller C (less reduction traffic). Returns that cost (k-blocks on the busiest CTA).
 template <int BN, int EPI>
-void plan_cl(int T, int KB, int& C_best, int& n_clusters) {
+int64_t plan_cl(int T, int KB, int& C_best, int& n_clusters) {
     int64_t best = -1;
     C_best = 1;
     n_clusters = 0;
@@ -994,8 +994,13 @@ void plan_cl(int T, int KB, int& C_best, int& n_clusters) {
             n_clusters = std::min(nc, T);
         }
     }
+    return best;
 }
 
+// Launches the cluster kernel when its wave-quantised cost is within 20% of a perfect balance
+// of the T * KB k-blocks over the SMs; returns -1 (nothing launched) otherwise, so that the
+// caller runs the stream-K kernel, whose balance is exact but whose cross-CTA reduction goes
+// through global memory.
 template <int BN, int EPI>
 int launch_cl(const CUtensorMap& tw, const CUtensorMap& tx, void* y, unsigned long long* amax,
               int M, int N, int K, cudaStream_t stream, int id_off) {
@@ -1003,8 +1008,10 @@ int launch_cl(const CUtensorMap& tw, const CUtensorMap& tx, void* y, unsigned lo
     if (!err) return set_error(MSGL_ERR_CUDA, "device error word unavailable");
     const int T = (N + kBM - 1) / kBM, KB = (K + kBK - 1) / kBK;
     int C = 1, nc = 0;
-    plan_cl<BN, EPI>(T, KB, C, nc);
-    if (nc <= 0) return set_error(MSGL_ERR_CUDA, "gemm: no cluster configuration fits");
+    const int64_t cost = plan_cl<BN, EPI>(T, KB, C, nc);
+    const int64_t sms = num_sms();
+    const int64_t balanced = (static_cast<int64_t>(T) * KB + sms - 1) / sms;
+    if (nc <= 0 || cost * 5 > balanced * 6) return -1;
     cudaError_t e = launch_cl_raw<BN, EPI>(tw, tx, y, amax, M, N, K, C, nc, id_off, err, stream);
     if (e != cudaSuccess) return set_error(MSGL_ERR_CUDA, cudaGetErrorString(e));
     return MSGL_OK;
@@ -1024,13 +1031,15 @@ int run_gemm(const void* x, const void* w, void* y, unsigned long long* amax, in
     if (rc) return rc;
     rc = make_tmap_2d_bf16(&tx, x, K, M, static_cast<uint64_t>(K) * 2, kBK, bn, true);
     if (rc) return rc;
-    if (bn <= 128) {  // one token tile: cluster split-K, no workspace needed
+    if (bn <= 128) {  // one token tile: cluster split-K when it balances well (no workspace)
+        int r;
         switch (bn) {
-            case 16: return launch_cl<16, EPI>(tw, tx, y, amax, M, N, K, stream, id_off);
-            case 32: return launch_cl<32, EPI>(tw, tx, y, amax, M, N, K, stream, id_off);
-            case 64: return launch_cl<64, EPI>(tw, tx, y, amax, M, N, K, stream, id_off);
-            default: return launch_cl<128, EPI>(tw, tx, y, amax, M, N, K, stream, id_off);
+            case 16: r = launch_cl<16, EPI>(tw, tx, y, amax, M, N, K, stream, id_off); break;
+            case 32: r = launch_cl<32, EPI>(tw, tx, y, amax, M, N, K, stream, id_off); break;
+            case 64: r = launch_cl<64, EPI>(tw, tx, y, amax, M, N, K, stream, id_off); break;
+            default: r = launch_cl<128, EPI>(tw, tx, y, amax, M, N, K, stream, id_off); break;
         }
+        if (r != -1) return r;
     }
     if (tiles <= static_cast<int64_t>(kCounterBytes / sizeof(int))) {
         const int sms = num_sms();
