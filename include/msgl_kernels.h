@@ -131,6 +131,24 @@ MSGL_API int msgl_paged_attention_decode(const void* q, const void* k_pool, cons
                                 float scale, void* out, void* workspace,
                                 size_t workspace_bytes, msgl_stream_t stream);
 
+/* Decode without a caller workspace. No counterpart in the reference (its launchers take no
+ * workspace); this is an addition for callers that cannot hand in device memory. Same arguments
+ * and results as msgl_paged_attention_decode minus the workspace: the scratch is a file-scope
+ * 8 MiB device array of the library. Batches whose msgl_paged_attention_workspace_size exceeds
+ * 8 MiB are rejected with MSGL_ERR_WORKSPACE. No cudaMalloc / cudaFree or other allocating call;
+ * each call clears (cudaMemsetAsync on `stream`) the split-KV arrival counters it uses. The first
+ * call on a device looks up the array's address (cudaGetSymbolAddress) with that device current;
+ * make that first call before any stream capture. Every call on a device shares the one array,
+ * which keeps the last call's partial results; calls that overlap on the GPU (other streams, other
+ * host threads) race on it and must be serialised by the caller. */
+MSGL_API int msgl_paged_attention_decode_noalloc(const void* q, const void* k_pool,
+                                                 const void* v_pool, int64_t num_slots,
+                                                 const int* page_table, int max_pages,
+                                                 const int* seq_lens, int num_reqs,
+                                                 int max_seq_len, int num_q_heads,
+                                                 int num_kv_heads, int head_dim, int page_size,
+                                                 float scale, void* out, msgl_stream_t stream);
+
 /* Extend / prefill: request r owns query rows [q_indptr[r], q_indptr[r+1]) of q/out
  * [total_q, Hq, D]; row i of an n-row request sits at position seq_lens[r] - n + i and attends
  * causally to context tokens 0..that position. max_q_len bounds the per-request row count. */

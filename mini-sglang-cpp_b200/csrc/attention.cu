@@ -19,6 +19,8 @@
 // Bound: HBM. Per (request, kv head, token) the kernel reads 512 B of K/V; the tensor work per
 // byte is ~4 FLOP, far below the MMA rate.
 #include <algorithm>
+#include <cstdio>
+#include <mutex>
 
 #include "common.cuh"
 #include "tmap.h"
@@ -575,6 +577,11 @@ int make_decode_maps(CUtensorMap* tk, CUtensorMap* tv, const void* k_pool, const
     return make_tmap_3d_bf16(tv, v_pool, 64, num_slots, 2 * hkv, row_bytes, 128, 64, kPage, 2 * hc);
 }
 
+// Scratch of msgl_paged_attention_decode_noalloc: one file-scope device array per device (module
+// load zero-fills it), shared by every call of that entry point on the device.
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB
+static __device__ __align__(256) uint8_t g_decode_scratch[kNoAllocScratchBytes];
+
 }  // namespace
 }  // namespace msgl
 
@@ -670,6 +677,57 @@ int msgl_paged_attention_extend(const void* q, const void* k_pool, const void* v
         num_kv_heads, sl2e, err);
     MSGL_LAUNCH_CHECK();
     return MSGL_OK;
+}
+
+// The device address of the static scratch is looked up once per device (on the first call with
+// that device current) and cached; the call then clears the split-KV arrival counters it will
+// use and runs msgl_paged_attention_decode on the scratch.
+int msgl_paged_attention_decode_noalloc(const void* q, const void* k_pool, const void* v_pool,
+                                        int64_t num_slots, const int* page_table, int max_pages,
+                                        const int* seq_lens, int num_reqs, int max_seq_len,
+                                        int num_q_heads, int num_kv_heads, int head_dim,
+                                        int page_size, float scale, void* out,
+                                        msgl_stream_t stream) {
+    if (num_reqs < 0 || num_kv_heads <= 0 || head_dim != kHd)
+        return set_error(MSGL_ERR_INVALID_ARG, "decode_noalloc: bad sizes");
+    const size_t need = msgl_paged_attention_workspace_size(num_reqs, max_seq_len, num_q_heads,
+                                                            num_kv_heads, head_dim);
+    if (need > kNoAllocScratchBytes) {
+        char buf[160];
+        snprintf(buf, sizeof(buf),
+                 "decode_noalloc: this batch needs %zu bytes of scratch; the static scratch holds "
+                 "%zu (8 MiB) -- use msgl_paged_attention_decode with a workspace",
+                 need, kNoAllocScratchBytes);
+        return set_error(MSGL_ERR_WORKSPACE, buf);
+    }
+    static void* ptrs[64] = {nullptr};
+    static std::mutex mu;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return set_error(MSGL_ERR_CUDA, "decode_noalloc: no current device");
+    void* scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!ptrs[dev]) {
+            void* p = nullptr;
+            cudaError_t e = cudaGetSymbolAddress(&p, g_decode_scratch);
+            if (e != cudaSuccess || !p)
+                return set_error(MSGL_ERR_CUDA, e != cudaSuccess ? cudaGetErrorString(e)
+                                                                 : "decode_noalloc: null scratch");
+            ptrs[dev] = p;
+        }
+        scratch = ptrs[dev];
+    }
+    if (need > 0) {  // arrival counters at offset 0 must start at zero
+        const size_t cnt_bytes = static_cast<size_t>(num_reqs) *
+                                 (num_kv_heads / decode_heads_per_cta(num_kv_heads)) * sizeof(int);
+        if (cudaMemsetAsync(scratch, 0, std::min(cnt_bytes, kDecodeCounterBytes), stream) != cudaSuccess)
+            return set_error(MSGL_ERR_CUDA, cudaGetErrorString(cudaGetLastError()));
+    }
+    return msgl_paged_attention_decode(q, k_pool, v_pool, num_slots, page_table, max_pages,
+                                       seq_lens, num_reqs, max_seq_len, num_q_heads, num_kv_heads,
+                                       head_dim, page_size, scale, out, scratch,
+                                       kNoAllocScratchBytes, stream);
 }
 
 }  // extern "C"
