@@ -46,6 +46,19 @@ __device__ __forceinline__ void named_bar(int id, int count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// Named barrier that also ORs a predicate over its `count` threads: every participant gets the
+// same answer, so a decision taken on it is uniform across the warps.
+__device__ __forceinline__ bool named_bar_or(int id, int count, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(count)
+        : "memory");
+    return r != 0;
+}
+
 __device__ __forceinline__ unsigned long long argmax_key(float v, int n) {
     uint32_t u = __float_as_uint(v);
     u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
@@ -542,7 +555,9 @@ gemm_sk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
                             bulk_load(smem + k * kPartBytes, ws_part + cc * kPart, kPartBytes, pfull);
                         }
                     }
-                    if (!mbar_wait(pfull, round & 1, err, 361)) break;
+                    // every thread acquires the copies; a timeout anywhere stops all of them
+                    const bool timed_out = !mbar_wait(pfull, round & 1, err, 361);
+                    if (named_bar_or(1, kEpiThreads, timed_out)) break;
                 }
                 const bool final_round = done + nb >= ncontrib;
                 const float* sp = reinterpret_cast<const float*>(smem) + row;
