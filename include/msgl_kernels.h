@@ -247,6 +247,24 @@ MSGL_API int msgl_tp_allreduce_add_rmsnorm(msgl_tp* tp, void* x, float* residual
                                            float eps, int first, msgl_stream_t stream);
 /* packed [num_rows] uint64 keys (msgl_lm_head_argmax_partial) max-reduced over the ranks and
  * unpacked to ids [num_rows]: greedy sampling over the full vocabulary. */
+/* One-kernel all-reduce + add + RMSNorm over NVLink peer memory (no counterpart in the
+ * reference, whose TPCommunicator is a stub; it replaces NCCL all-reduce + msgl_add_rmsnorm).
+ * msgl_tp_enable_p2p (collective, every rank the same `bytes`) allocates this rank's
+ * peer-mapped region -- two slots of `bytes` for partial rows plus flags -- exchanges cudaIpc
+ * handles with an NCCL all-gather on `stream` and maps every other rank's region (plain peer
+ * loads; no multicast). msgl_tp_p2p_buffer returns slot 0 or 1: the row-parallel GEMM writes its
+ * partial [T, H] bf16 rows there, and CONSECUTIVE fused calls must use alternate slots (checked).
+ * msgl_tp_fused_allreduce_add_rmsnorm (every rank, same calls in the same order) computes, on
+ * every rank, residual (+)= sum over ranks (rank order, fp32) of the partial rows and
+ * x_out = RMSNorm(residual) * weight (bf16; `first` as msgl_add_rmsnorm); all ranks get the same
+ * bits. The ranks meet through per-CTA epoch flags in the regions (bounded waits: a rank that does
+ * not arrive within ~2 s gives MSGL_ERR_TIMEOUT in the error word, site 500). */
+MSGL_API int msgl_tp_enable_p2p(msgl_tp* tp, size_t bytes, msgl_stream_t stream);
+MSGL_API int msgl_tp_p2p_buffer(msgl_tp* tp, int slot, void** ptr, size_t* bytes);
+MSGL_API int msgl_tp_fused_allreduce_add_rmsnorm(msgl_tp* tp, const void* partial, void* x_out,
+                                                 float* residual, const void* weight,
+                                                 int num_tokens, int hidden, float eps, int first,
+                                                 msgl_stream_t stream);
 MSGL_API int msgl_tp_argmax_combine(msgl_tp* tp, unsigned long long* packed, int* ids,
                                     int num_rows, msgl_stream_t stream);
 /* Host only: the shard of `rank` as 8 ints {q_head0, q_heads, kv_head0, kv_heads, inter0,

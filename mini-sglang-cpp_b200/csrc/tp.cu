@@ -8,16 +8,28 @@
 //  * msgl_tp_argmax_combine   vocab-parallel greedy sampling: each rank's packed (logit, id) keys
 //                             reduced with a 64-bit max, then unpacked to token ids
 //  * msgl_tp_shard_plan       which rows / columns of every weight a rank owns (host only)
+//  * msgl_tp_enable_p2p / msgl_tp_p2p_buffer / msgl_tp_fused_allreduce_add_rmsnorm
+//                             the same all-reduce + add + RMSNorm as ONE kernel over NVLink peer
+//                             memory: every rank reads the other ranks' partial rows directly
+//                             (cudaIpc mappings, plain loads, no multicast) -- see below.
 #include <nccl.h>
 
 #include <cstring>
 #include <string>
+#include <vector>
 
 #include "common.cuh"
+
+constexpr int kTpMaxWorld = 8;
 
 struct msgl_tp {
     ncclComm_t comm = nullptr;
     int rank = 0, world = 1;
+    // peer-mapped region (msgl_tp_enable_p2p): [slot 0: data_bytes][slot 1: data_bytes][flags]
+    void* sym = nullptr;
+    size_t data_bytes = 0;
+    void* peer[kTpMaxWorld] = {};  // every rank's region in this process (peer[rank] = sym)
+    int last_slot = -1;            // slot of the previous fused call (calls must alternate)
 };
 
 namespace msgl {
@@ -34,6 +46,150 @@ __global__ void unpack_keys_kernel(const unsigned long long* __restrict__ packed
     pdl_trigger();
     int m = blockIdx.x * blockDim.x + threadIdx.x;
     if (m < M) ids[m] = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(packed[m] & 0xFFFFFFFFull));
+}
+
+// ------------------------------------------------------------------ P2P all-reduce + norm
+// Region of each rank: two slots of partial rows (consecutive calls alternate slots), then
+// flags (4-byte words, zero at setup), one per CTA index b < kTpMaxCtas so that CTA b of every
+// rank pairs with CTA b of the others and no two CTAs write the same word:
+//   ready[q][b]  = e + 1 once CTA b of rank q starts call e (its partial rows are complete)
+//   epoch[b]     calls CTA b has taken part in on this rank (the same on every rank: all ranks
+//                run the same calls with the same row count, hence the same grid)
+// Why two slots and no end-of-call handshake: a slot is rewritten two calls later, after this
+// rank's call in between waited for every peer's ready flag of that call -- raised only once the
+// peer's previous call, the one that read the slot, had completed.
+constexpr int kTpMaxCtas = 148;
+constexpr size_t kFlagBytes = static_cast<size_t>(kTpMaxWorld + 1) * kTpMaxCtas * 4;
+struct TpPeers {
+    const __nv_bfloat16* part[kTpMaxWorld];  // every rank's partial rows (this call's slot)
+    unsigned* flags[kTpMaxWorld];            // every rank's flag area
+};
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint4 ld_volatile_v4(const void* p) {
+    uint4 v;
+    asm volatile("ld.volatile.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// Thread t < world (t != rank) of CTA b: raise slot [rank][b] on rank t, then wait (bounded)
+// until rank t raised this rank's slot [t][b]; the CTA then synchronises.
+__device__ __forceinline__ void ready_exchange(const TpPeers& peers, unsigned* local, int world,
+                                               int rank, unsigned value, int* err) {
+    const int t = threadIdx.x;
+    if (t < world && t != rank) {
+        st_release_sys(peers.flags[t] + rank * kTpMaxCtas + blockIdx.x, value);
+        const unsigned* mine = local + t * kTpMaxCtas + blockIdx.x;
+        const uint64_t t0 = globaltimer_ns();
+        while (ld_acquire_sys(mine) < value) {
+            if (globaltimer_ns() - t0 > 2000000000ull) {
+                record_error(err, MSGL_ERR_TIMEOUT, 500);
+                break;
+            }
+        }
+    }
+    __syncthreads();
+}
+
+// One CTA (128 threads, VPT 8-element vectors per thread) per row, rows strided over the grid.
+// x[row] = RMSNorm(residual[row] (+)= sum over ranks, in rank order, of partial_q[row]) * w.
+// Every rank sums the same values in the same order, so every rank gets the same bits. W is
+// the world size rounded up to 2 / 4 / 8; a thread issues the peer loads of G = 8 / W vectors
+// (8 loads) before it uses any, so their NVLink round trips overlap.
+template <int VPT, int W>
+__global__ void __launch_bounds__(128)
+tp_fused_ar_norm_kernel(TpPeers peers, int world, int rank, __nv_bfloat16* __restrict__ x_out,
+                        float* __restrict__ resid, const __nv_bfloat16* __restrict__ w, int T,
+                        int H, float eps, int first, unsigned* __restrict__ local, int* err) {
+    constexpr int G = W >= 8 ? 1 : 8 / W;
+    __shared__ float red[4];
+    pdl_wait();  // this rank's partial (the previous kernel's output) is complete
+    pdl_trigger();
+    unsigned* epoch_p = local + kTpMaxWorld * kTpMaxCtas + blockIdx.x;
+    const unsigned e = *reinterpret_cast<volatile unsigned*>(epoch_p);
+    ready_exchange(peers, local, world, rank, e + 1, err);  // every rank's partial is complete
+    const int nvec = H >> 3;
+    for (int row = blockIdx.x; row < T; row += gridDim.x) {
+        const int64_t rbase = static_cast<int64_t>(row) * H;
+        float v[VPT][8];
+        float ss = 0.f;
+#pragma unroll
+        for (int i0 = 0; i0 < VPT; i0 += G) {
+            uint4 u[G][W];
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const int vi = threadIdx.x + (i0 + g) * 128;
+                if (i0 + g < VPT && vi < nvec) {
+#pragma unroll
+                    for (int q = 0; q < W; ++q)
+                        if (q < world) u[g][q] = ld_volatile_v4(peers.part[q] + rbase + vi * 8);
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const int i = i0 + g;
+                const int vi = threadIdx.x + i * 128;
+                if (i >= VPT || vi >= nvec) continue;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
+#pragma unroll
+                for (int q = 0; q < W; ++q) {
+                    if (q >= world) break;
+                    v[i][0] += bf16lo(u[g][q].x); v[i][1] += bf16hi(u[g][q].x);
+                    v[i][2] += bf16lo(u[g][q].y); v[i][3] += bf16hi(u[g][q].y);
+                    v[i][4] += bf16lo(u[g][q].z); v[i][5] += bf16hi(u[g][q].z);
+                    v[i][6] += bf16lo(u[g][q].w); v[i][7] += bf16hi(u[g][q].w);
+                }
+                float4* r4 = reinterpret_cast<float4*>(resid + rbase + vi * 8);
+                if (!first) {
+                    const float4 a = r4[0], b = r4[1];
+                    v[i][0] += a.x; v[i][1] += a.y; v[i][2] += a.z; v[i][3] += a.w;
+                    v[i][4] += b.x; v[i][5] += b.y; v[i][6] += b.z; v[i][7] += b.w;
+                }
+                r4[0] = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
+                r4[1] = make_float4(v[i][4], v[i][5], v[i][6], v[i][7]);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+            }
+        }
+        ss = warp_sum(ss);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+        __syncthreads();
+        const float tot = red[0] + red[1] + red[2] + red[3];
+        __syncthreads();
+        const float inv = 1.0f / sqrtf(tot / static_cast<float>(H) + eps);
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) {
+            const int vi = threadIdx.x + i * 128;
+            if (vi >= nvec) continue;
+            const uint4 wu = *reinterpret_cast<const uint4*>(w + vi * 8);
+            uint4 o;
+            o.x = pack_bf16x2(v[i][0] * inv * bf16lo(wu.x), v[i][1] * inv * bf16hi(wu.x));
+            o.y = pack_bf16x2(v[i][2] * inv * bf16lo(wu.y), v[i][3] * inv * bf16hi(wu.y));
+            o.z = pack_bf16x2(v[i][4] * inv * bf16lo(wu.z), v[i][5] * inv * bf16hi(wu.z));
+            o.w = pack_bf16x2(v[i][6] * inv * bf16lo(wu.w), v[i][7] * inv * bf16hi(wu.w));
+            *reinterpret_cast<uint4*>(x_out + rbase + vi * 8) = o;
+        }
+    }
+    if (threadIdx.x == 0) *reinterpret_cast<volatile unsigned*>(epoch_p) = e + 1;
+}
+
+template <int VPT, int W>
+cudaError_t launch_ar(int grid, cudaStream_t stream, const TpPeers& pr, const msgl_tp* tp,
+                      void* x_out, float* residual, const void* weight, int T, int H, float eps,
+                      int first, unsigned* local, int* err) {
+    return launch_pdl(tp_fused_ar_norm_kernel<VPT, W>, dim3(grid), dim3(128), 0, stream, pr,
+                      tp->world, tp->rank, static_cast<__nv_bfloat16*>(x_out), residual,
+                      static_cast<const __nv_bfloat16*>(weight), T, H, eps, first, local, err);
 }
 
 }  // namespace
@@ -76,8 +232,114 @@ int msgl_tp_init(int rank, int world, const void* unique_id, msgl_tp** out) {
 
 int msgl_tp_destroy(msgl_tp* tp) {
     if (!tp) return MSGL_OK;
+    for (int q = 0; q < tp->world && q < kTpMaxWorld; ++q)
+        if (q != tp->rank && tp->peer[q]) cudaIpcCloseMemHandle(tp->peer[q]);
+    if (tp->sym) cudaFree(tp->sym);
     if (tp->comm) ncclCommDestroy(tp->comm);
     delete tp;
+    return MSGL_OK;
+}
+
+// Collective (every rank, same bytes): allocate this rank's peer-mapped region, exchange the
+// cudaIpc handles with an NCCL all-gather, and map every other rank's region.
+int msgl_tp_enable_p2p(msgl_tp* tp, size_t bytes, msgl_stream_t stream) {
+    if (!tp || bytes == 0 || bytes % 16) return set_error(MSGL_ERR_INVALID_ARG, "tp_enable_p2p: bad args");
+    if (tp->world > kTpMaxWorld) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "tp_enable_p2p: world > 8");
+    if (tp->sym) return set_error(MSGL_ERR_INVALID_ARG, "tp_enable_p2p: already enabled");
+    const size_t total = 2 * bytes + kFlagBytes;
+    if (cudaMalloc(&tp->sym, total) != cudaSuccess || cudaMemset(tp->sym, 0, total) != cudaSuccess) {
+        tp->sym = nullptr;
+        return set_error(MSGL_ERR_CUDA, "tp_enable_p2p: region allocation failed");
+    }
+    tp->data_bytes = bytes;
+    tp->peer[tp->rank] = tp->sym;
+    if (tp->world == 1) return MSGL_OK;
+    cudaIpcMemHandle_t mine;
+    if (cudaIpcGetMemHandle(&mine, tp->sym) != cudaSuccess)
+        return set_error(MSGL_ERR_CUDA, cudaGetErrorString(cudaGetLastError()));
+    const size_t hb = sizeof(cudaIpcMemHandle_t);
+    void* dev = nullptr;
+    if (cudaMalloc(&dev, hb * (tp->world + 1)) != cudaSuccess)
+        return set_error(MSGL_ERR_CUDA, "tp_enable_p2p: handle buffer");
+    uint8_t* d8 = static_cast<uint8_t*>(dev);
+    std::vector<uint8_t> all(hb * tp->world);
+    int rc = MSGL_OK;
+    if (cudaMemcpy(d8 + hb * tp->world, &mine, hb, cudaMemcpyHostToDevice) != cudaSuccess) {
+        rc = set_error(MSGL_ERR_CUDA, "tp_enable_p2p: handle copy");
+    } else {
+        ncclResult_t r = ncclAllGather(d8 + hb * tp->world, d8, hb, ncclUint8, tp->comm, stream);
+        if (r != ncclSuccess) rc = nccl_err(r, "ncclAllGather(ipc handles)");
+        else if (cudaStreamSynchronize(stream) != cudaSuccess ||
+                 cudaMemcpy(all.data(), d8, hb * tp->world, cudaMemcpyDeviceToHost) != cudaSuccess)
+            rc = set_error(MSGL_ERR_CUDA, "tp_enable_p2p: handle gather");
+    }
+    cudaFree(dev);
+    if (rc) return rc;
+    for (int q = 0; q < tp->world; ++q) {
+        if (q == tp->rank) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, all.data() + hb * q, hb);
+        if (cudaIpcOpenMemHandle(&tp->peer[q], h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            tp->peer[q] = nullptr;
+            return set_error(MSGL_ERR_CUDA, cudaGetErrorString(cudaGetLastError()));
+        }
+    }
+    return MSGL_OK;
+}
+
+int msgl_tp_p2p_buffer(msgl_tp* tp, int slot, void** ptr, size_t* bytes) {
+    if (!tp || !ptr || slot < 0 || slot > 1) return set_error(MSGL_ERR_INVALID_ARG, "tp_p2p_buffer: bad args");
+    *ptr = tp->sym ? static_cast<uint8_t*>(tp->sym) + slot * tp->data_bytes : nullptr;
+    if (bytes) *bytes = tp->data_bytes;
+    return tp->sym ? MSGL_OK : set_error(MSGL_ERR_INVALID_ARG, "tp_p2p_buffer: msgl_tp_enable_p2p not called");
+}
+
+int msgl_tp_fused_allreduce_add_rmsnorm(msgl_tp* tp, const void* partial, void* x_out,
+                                        float* residual, const void* weight, int num_tokens,
+                                        int hidden, float eps, int first, msgl_stream_t stream) {
+    if (!tp || !x_out || !residual || !weight || num_tokens < 0 || hidden <= 0 || hidden % 8 ||
+        hidden > 8 * 8 * 128)
+        return set_error(MSGL_ERR_INVALID_ARG, "tp_fused_allreduce: bad args");
+    if (!tp->sym) return set_error(MSGL_ERR_INVALID_ARG, "tp_fused_allreduce: msgl_tp_enable_p2p not called");
+    int slot = -1;
+    for (int k = 0; k < 2; ++k)
+        if (partial == static_cast<uint8_t*>(tp->sym) + k * tp->data_bytes) slot = k;
+    if (slot < 0)
+        return set_error(MSGL_ERR_INVALID_ARG, "tp_fused_allreduce: partial must be a msgl_tp_p2p_buffer slot");
+    if (slot == tp->last_slot)
+        return set_error(MSGL_ERR_INVALID_ARG, "tp_fused_allreduce: consecutive calls must alternate slots");
+    if (static_cast<size_t>(num_tokens) * hidden * 2 > tp->data_bytes)
+        return set_error(MSGL_ERR_WORKSPACE, "tp_fused_allreduce: rows exceed the peer-mapped region");
+    if (num_tokens == 0) return MSGL_OK;
+    int* err = device_error_word();
+    if (!err) return set_error(MSGL_ERR_CUDA, "device error word unavailable");
+    TpPeers pr{};
+    for (int q = 0; q < tp->world; ++q) {
+        uint8_t* base = static_cast<uint8_t*>(tp->peer[q]);
+        pr.part[q] = reinterpret_cast<const __nv_bfloat16*>(base + slot * tp->data_bytes);
+        pr.flags[q] = reinterpret_cast<unsigned*>(base + 2 * tp->data_bytes);
+    }
+    unsigned* local = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(tp->sym) + 2 * tp->data_bytes);
+    const int grid = num_tokens < kTpMaxCtas ? num_tokens : kTpMaxCtas;
+    const int vpt = (hidden / 8 + 127) / 128;
+    cudaError_t e;
+#define MSGL_TP_CASE(N)                                                                          \
+    case N:                                                                                      \
+        e = tp->world <= 2 ? launch_ar<N, 2>(grid, stream, pr, tp, x_out, residual, weight,     \
+                                             num_tokens, hidden, eps, first, local, err)        \
+          : tp->world <= 4 ? launch_ar<N, 4>(grid, stream, pr, tp, x_out, residual, weight,     \
+                                             num_tokens, hidden, eps, first, local, err)        \
+                           : launch_ar<N, 8>(grid, stream, pr, tp, x_out, residual, weight,     \
+                                             num_tokens, hidden, eps, first, local, err);       \
+        break;
+    switch (vpt) {
+        MSGL_TP_CASE(1) MSGL_TP_CASE(2) MSGL_TP_CASE(3) MSGL_TP_CASE(4)
+        MSGL_TP_CASE(5) MSGL_TP_CASE(6) MSGL_TP_CASE(7) MSGL_TP_CASE(8)
+        default: return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "tp_fused_allreduce: hidden too large");
+    }
+#undef MSGL_TP_CASE
+    if (e != cudaSuccess) return set_error(MSGL_ERR_CUDA, cudaGetErrorString(e));
+    tp->last_slot = slot;
     return MSGL_OK;
 }
 

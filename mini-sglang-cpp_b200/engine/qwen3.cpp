@@ -47,6 +47,7 @@ struct Model {
     int kv_head0 = 0;                              // first global kv head held by this rank
     int vocab0 = 0;                                // first lm_head row (token id) of this rank
     msgl_tp* tp = nullptr;                         // communicator (tp_size > 1), not owned
+    bf16_t* tp_part[2] = {nullptr, nullptr};       // its peer-mapped slots: row-parallel outputs
     std::vector<Qwen3DecoderLayer> layers;
     DevBuf embed;        // [V, H]
     RMSNorm norm;        // final norm
@@ -72,10 +73,12 @@ struct Model {
     };
     std::vector<GraphEntry> graphs;
 
-    ~Model() {
+    void graphs_reset() {  // captured graphs hold the old communicator / buffers
         for (auto& g : graphs)
             if (g.exec) cudaGraphExecDestroy(g.exec);
+        graphs.clear();
     }
+    ~Model() { graphs_reset(); }
 
     int64_t weight_bytes() const {
         int64_t b = embed.bytes + norm.weight.bytes + lm_head.weight.bytes;
@@ -376,28 +379,39 @@ static void forward(Model& m, const msgl_batch& b, int* next_tokens, float* logi
     ck(msgl_embed_rmsnorm(m.embed.p, b.input_ids, T, c.vocab, H, m.layers[0].input_layernorm.weight.p,
                           c.eps, x, res, s),
        "embed_tokens");
+    // Tensor parallel: the row-parallel outputs (o_proj, down_proj / expert combine) go to the
+    // communicator's peer-mapped rows, and one kernel all-reduces them over NVLink fused with
+    // the residual add and the next RMSNorm (post-attention norm; the next layer's input norm;
+    // after the last layer the final norm).
+    // (o_proj uses slot 0, down_proj slot 1: consecutive all-reduces alternate slots)
+    bf16_t* part_o = m.tp ? m.tp_part[0] : x;
+    bf16_t* part_d = m.tp ? m.tp_part[1] : x;
     for (int l = 0; l < nl; ++l) {
         auto& L = m.layers[l];
-        if (l > 0) L.input_layernorm.forward_fused_add(x, res, T, false, s);  // qwen3.cpp:19
+        if (l > 0 && !m.tp) L.input_layernorm.forward_fused_add(x, res, T, false, s);  // qwen3.cpp:19
         L.qkv_proj.forward(x, m.qkv.as<bf16_t>(), T, m.scratch, s);          // :22
         L.attn.prepare(m.qkv.as<bf16_t>(), m.q.as<bf16_t>(), L.k_pool.p, L.v_pool.p, m.num_slots,
                        b.positions, b.slot_mapping, m.rope, L.q_norm.p, L.k_norm.p, T, s);  // :28-48
         L.attn.forward(m.q.as<bf16_t>(), L.k_pool.p, L.v_pool.p, m.num_slots, b,
                        m.attn_out.as<bf16_t>(), m.scratch, s);                // :51-52
-        L.o_proj.forward(m.attn_out.as<bf16_t>(), x, T, m.scratch, s);       // :55
+        L.o_proj.forward(m.attn_out.as<bf16_t>(), part_o, T, m.scratch, s);  // :55
         if (m.tp)  // row-parallel o_proj: all-reduce fused with the add + norm of :57
-            ck(msgl_tp_allreduce_add_rmsnorm(m.tp, x, res, L.post_attention_layernorm.weight.p, T, H,
-                                             c.eps, 0, s), "o_proj all-reduce");
+            ck(msgl_tp_fused_allreduce_add_rmsnorm(m.tp, part_o, x, res,
+                                                   L.post_attention_layernorm.weight.p, T, H,
+                                                   c.eps, 0, s), "o_proj all-reduce");
         else
             L.post_attention_layernorm.forward_fused_add(x, res, T, false, s);  // :57
         if (c.num_experts > 0) {
-            L.moe.forward(x, x, T, m.moe_scratch, m.scratch, s);              // qwen3_moe.cpp:62-111
+            L.moe.forward(x, part_d, T, m.moe_scratch, m.scratch, s);         // qwen3_moe.cpp:62-111
         } else {
             L.gate_up_proj.forward(x, m.act.as<bf16_t>(), T, m.scratch, s);  // :60-79
-            L.down_proj.forward(m.act.as<bf16_t>(), x, T, m.scratch, s);     // :80
+            L.down_proj.forward(m.act.as<bf16_t>(), part_d, T, m.scratch, s);  // :80
         }
-        if (m.tp)  // row-parallel down_proj / expert combine: partial sums over the ranks
-            ck(msgl_tp_all_reduce_sum(m.tp, x, static_cast<int64_t>(T) * H, s), "mlp all-reduce");
+        if (m.tp) {  // row-parallel down_proj / expert combine: all-reduce + add + next norm
+            const void* next_w = l + 1 < nl ? m.layers[l + 1].input_layernorm.weight.p : m.norm.weight.p;
+            ck(msgl_tp_fused_allreduce_add_rmsnorm(m.tp, part_d, x, res, next_w, T, H, c.eps, 0, s),
+               "mlp all-reduce");
+        }
     }
     // final norm on each request's last row (qwen3.cpp:177, sampling row of D10), lm_head +
     // greedy argmax (scheduler.cpp:117-124)
@@ -406,11 +420,13 @@ static void forward(Model& m, const msgl_batch& b, int* next_tokens, float* logi
     float* rl = res;
     if (!b.is_decode) {
         ck(msgl_launch_index_gather(x, b.last_idx, m.x_last.p, H, B, T, MSGL_BF16, s), "gather x");
-        ck(msgl_launch_index_gather(res, b.last_idx, m.res_last.p, H, B, T, MSGL_F32, s), "gather res");
+        if (!m.tp)
+            ck(msgl_launch_index_gather(res, b.last_idx, m.res_last.p, H, B, T, MSGL_F32, s),
+               "gather res");
         xl = m.x_last.as<bf16_t>();
         rl = m.res_last.as<float>();
     }
-    m.norm.forward_fused_add(xl, rl, B, false, s);
+    if (!m.tp) m.norm.forward_fused_add(xl, rl, B, false, s);  // (TP: done by the last all-reduce)
     if (m.tp) {  // vocab-parallel lm_head: local best (logit, id), max over the ranks
         if (logits) throw Fail(MSGL_ERR_UNSUPPORTED_SHAPE, "forward: logits output needs tp_size 1");
         ck(msgl_lm_head_argmax_partial(xl, m.lm_head.weight.p, B, m.vocab_l, H, m.vocab0,
@@ -600,7 +616,24 @@ int msgl_model_set_tp(msgl_model* m, msgl_tp* tp) {
     const int world = tp ? msgl_tp_world(tp) : 1;
     if (world != m->m.cfg.tp_size || (tp && msgl_tp_rank(tp) != m->m.cfg.tp_rank))
         return msgl::set_error(MSGL_ERR_INVALID_ARG, "set_tp: communicator rank/world differ from the config");
-    m->m.tp = world > 1 ? tp : nullptr;
+    m->m.tp = nullptr;
+    m->m.tp_part[0] = m->m.tp_part[1] = nullptr;
+    if (world > 1) {  // collective: every rank of the communicator calls set_tp
+        const size_t need = static_cast<size_t>(m->m.cfg.max_tokens) * m->m.cfg.hidden * 2;
+        void* buf[2] = {nullptr, nullptr};
+        size_t have = 0;
+        if (msgl_tp_p2p_buffer(tp, 0, &buf[0], &have) != MSGL_OK) {
+            const int rc = msgl_tp_enable_p2p(tp, need, nullptr);
+            if (rc) return rc;
+            msgl_tp_p2p_buffer(tp, 0, &buf[0], &have);
+        }
+        msgl_tp_p2p_buffer(tp, 1, &buf[1], &have);
+        if (have < need) return msgl::set_error(MSGL_ERR_WORKSPACE, "set_tp: peer-mapped region too small");
+        m->m.tp = tp;
+        m->m.tp_part[0] = static_cast<bf16_t*>(buf[0]);
+        m->m.tp_part[1] = static_cast<bf16_t*>(buf[1]);
+        m->m.graphs_reset();
+    }
     return MSGL_OK;
 }
 

@@ -135,3 +135,124 @@ def test_tp2_matches_tp1():
     status, agree, total = res[0]
     assert status == "ok", res
     assert agree >= total - 1, res  # greedy ids equal (one near-tie flip tolerated)
+
+
+# ---------------------------------------------------------------- 2-GPU fused P2P all-reduce
+def _p2p_worker(rank, world, port, mode, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    comm = None
+    try:
+        import ctypes as C
+
+        from msgl import ops
+        from msgl._lib import check, lib
+        from msgl.model import TPComm, device_view
+        from oracle import bf16_round
+        L = lib()
+        uid = [TPComm.new_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = TPComm(rank, world, uid[0])
+        T, H, eps = 96, 4096, 1e-6
+        check(L.msgl_tp_enable_p2p(comm.h, 128 * H * 2, None))
+        slots, nbytes = [C.c_void_p(), C.c_void_p()], C.c_size_t()
+        for k in range(2):
+            check(L.msgl_tp_p2p_buffer(comm.h, k, C.byref(slots[k]), C.byref(nbytes)))
+        parts_dev = [device_view(p.value, (128, H), torch.bfloat16)[:T] for p in slots]
+        ops.device_error(reset=True)
+        if mode == "parity":
+            res = torch.zeros(T, H, dtype=torch.float32, device="cuda")
+            res_ref = np.zeros((T, H), np.float32)
+            x = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+            worst = 0.0
+            for it in range(4):  # consecutive calls: the epoch flags advance
+                rng = np.random.default_rng(100 + it)  # same draws on every rank
+                parts = [bf16_round(rng.standard_normal((T, H)).astype(np.float32)) for _ in range(world)]
+                wt = bf16_round(1.0 + 0.1 * rng.standard_normal(H).astype(np.float32))
+                first = int(it == 0)
+                ptr = slots[it % 2]  # consecutive calls alternate slots
+                parts_dev[it % 2].copy_(torch.from_numpy(parts[rank]).to(torch.bfloat16))
+                torch.cuda.synchronize()
+                dist.barrier()  # not needed by the kernel; keeps the host copies ordered
+                check(L.msgl_tp_fused_allreduce_add_rmsnorm(
+                    comm.h, ptr, x.data_ptr(), res.data_ptr(),
+                    torch.from_numpy(wt).to(torch.bfloat16).cuda().data_ptr(), T, H, eps, first,
+                    torch.cuda.current_stream().cuda_stream))
+                torch.cuda.synchronize()
+                s = np.zeros((T, H), np.float32)
+                for p in parts:  # rank order, fp32
+                    s = s + p
+                res_ref = s if first else res_ref + s
+                inv = 1.0 / np.sqrt((res_ref.astype(np.float64) ** 2).mean(axis=1) + eps)
+                x_ref = res_ref * inv[:, None].astype(np.float32) * wt
+                assert np.array_equal(res.cpu().numpy(), res_ref), it  # same adds, same order
+                got = x.float().cpu().numpy()
+                err = float(np.linalg.norm(got - x_ref) / np.linalg.norm(x_ref))
+                worst = max(worst, err)
+                assert err < 1e-2, (it, err)
+                # every rank holds the same bits
+                allx = [torch.zeros(T * H // 2, dtype=torch.int32) for _ in range(world)]
+                dist.all_gather(allx, x.view(torch.int32).reshape(-1).cpu())
+                assert all(torch.equal(allx[0], a) for a in allx[1:]), it
+            assert ops.device_error() == (0, 0)
+            q.put((rank, ("ok", worst)))
+        else:  # "timeout": rank 1 never arrives; rank 0's bounded wait must report it
+            if rank == 0:
+                x = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+                res = torch.zeros(T, H, dtype=torch.float32, device="cuda")
+                w = torch.ones(H, dtype=torch.bfloat16, device="cuda")
+                check(L.msgl_tp_fused_allreduce_add_rmsnorm(
+                    comm.h, slots[0], x.data_ptr(), res.data_ptr(), w.data_ptr(), T, H, eps, 0,
+                    torch.cuda.current_stream().cuda_stream))
+                torch.cuda.synchronize()
+                err = ops.device_error()
+                # the context stays usable after the timeout
+                y = (torch.ones(4, device="cuda") * 2).sum().item()
+                q.put((rank, ("ok", err, y)))
+            else:
+                q.put((rank, ("ok", None, None)))
+            dist.barrier()  # rank 1 stays alive (its region mapped) until rank 0 is done
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, repr(e)))
+    finally:
+        if comm is not None:
+            comm.close()
+        dist.destroy_process_group()
+
+
+def _run_p2p(mode):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_p2p_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+    return res
+
+
+@pytest.mark.gpu
+def test_fused_p2p_allreduce_add_rmsnorm_2gpu():
+    """One-kernel all-reduce + add + RMSNorm over peer memory vs an fp32 reference (residual
+    bit-exact: same additions in the same order), identical bits on both ranks, 4 calls in a
+    row (epoch flags)."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    res = _run_p2p("parity")
+    assert res[0][0] == "ok" and res[1][0] == "ok", res
+
+
+@pytest.mark.gpu
+def test_fused_p2p_allreduce_timeout_2gpu():
+    """A rank that never arrives: the other rank's bounded wait ends, MSGL_ERR_TIMEOUT (5) is in
+    its error word, and its CUDA context keeps working. No GPU fault, no hang."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    res = _run_p2p("timeout")
+    assert res[0][0] == "ok", res
+    _, err, y = res[0]
+    assert err[0] == 5 and err[1] in (500, 501), err  # MSGL_ERR_TIMEOUT at a flag wait
+    assert y == 8.0
