@@ -402,7 +402,9 @@ def run_ours(args, rank, world, local_rank):
                     "ms_per_step": ms_e2e},
             "roofline": {"kernel": "paged_decode_kernel", "bound": "hbm",
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": PAGED_DECODE_TRAFFIC_BYTES,
+                         "frac": achieved / peak,
+                         # the capture is of 8 kv heads; a TP rank reads its own heads only
+                         "traffic": PAGED_DECODE_TRAFFIC_BYTES * hkv // CFG8B["num_kv_heads"],
                          "algorithmic_bytes_per_launch": unique_bytes,
                          "per_request_bytes_per_launch": per_request_bytes,
                          "launch_ms": attn_ms,
