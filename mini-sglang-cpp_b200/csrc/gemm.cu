@@ -29,6 +29,11 @@ constexpr int kGemmThreads = 192;
 constexpr int kSkEpiWarps = 8;
 constexpr int kSkThreads = (2 + kSkEpiWarps) * 32;
 constexpr int kTileA = kBM * kBK * 2;  // 16 KB
+// K-blocks per ring stage of the persistent kernels (one mbarrier phase carries kKps weight and
+// kKps activation tiles). Measured on B200 with the decode shapes: 2 per stage with half the
+// stages was no faster than 1 per stage with a deeper ring, so the ring keeps single k-blocks.
+constexpr int kKps = 1;
+constexpr int kRingBudget = 192 * 1024;  // shared memory for the ring (and cluster part buffer)
 constexpr size_t kCounterBytes = 16384;  // split-K arrival counters: up to 4096 tiles
 
 enum Epi { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3 };
@@ -299,8 +304,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
 template <int BN>
 struct SkCfg {
     static constexpr int kTileB = BN * kBK * 2;
-    static constexpr int kStageBytes = kTileA + kTileB;
-    static constexpr int kStages = BN >= 256 ? 4 : (BN >= 128 ? 6 : 8);
+    static constexpr int kStageBytes = kKps * (kTileA + kTileB);
+    static constexpr int kStages = kRingBudget / kStageBytes > 8 ? 8 : kRingBudget / kStageBytes;
     static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
     static constexpr size_t kSmem = static_cast<size_t>(kStages) * kStageBytes + 1024 + 256;
 };
@@ -378,8 +383,8 @@ gemm_sk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sA = smem;
-    uint8_t* sB = smem + ST * kTileA;
+    uint8_t* sA = smem;                      // [ST][kKps] weight tiles
+    uint8_t* sB = smem + ST * kKps * kTileA;  // [ST][kKps] activation tiles
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + ST * Cfg::kStageBytes);
     uint64_t* empty = full + ST;
     uint64_t* tfull = empty + ST;   // [2] accumulator ready
@@ -419,16 +424,21 @@ gemm_sk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
             tma_prefetch_desc(&tmap_x);
             const uint64_t pol_w = policy_evict_first();
             const uint64_t pol_x = policy_evict_last();
-            // Weight tiles of the first ST k-blocks go out before the dependency wait: weights
-            // are never written by a preceding kernel, so their fetch overlaps its tail.
+            // Weight tiles of the first ST stages go out before the dependency wait: weights
+            // are never written by a preceding kernel, so their fetch overlaps its tail. A stage
+            // holds up to kKps consecutive k-blocks of one segment.
+            constexpr uint32_t kKbBytes = kTileA + Cfg::kTileB;
             int npre = 0;
             for (int j = 0; j < nseg && npre < ST; ++j) {
                 int t, kb_s, kb_e, tr;
                 wk.seg(j, t, kb_s, kb_e, tr);
                 const int wrow = (t / m_tiles) * kBM;
-                for (int kb = kb_s; kb < kb_e && npre < ST; ++kb, ++npre) {
-                    mbar_arrive_expect_tx(&full[npre], Cfg::kStageBytes);
-                    tma_load_2d_hint(sA + npre * kTileA, &tmap_w, &full[npre], kb * kBK, wrow, pol_w);
+                for (int kb = kb_s; kb < kb_e && npre < ST; kb += kKps, ++npre) {
+                    const int nk = min(kKps, kb_e - kb);
+                    mbar_arrive_expect_tx(&full[npre], nk * kKbBytes);
+                    for (int u = 0; u < nk; ++u)
+                        tma_load_2d_hint(sA + (npre * kKps + u) * kTileA, &tmap_w, &full[npre],
+                                         (kb + u) * kBK, wrow, pol_w);
                 }
             }
             pdl_wait();
@@ -439,16 +449,19 @@ gemm_sk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
                 int t, kb_s, kb_e, tr;
                 wk.seg(j, t, kb_s, kb_e, tr);
                 const int wrow = (t / m_tiles) * kBM, xrow = (t % m_tiles) * BN;
-                for (int kb = kb_s; kb < kb_e; ++kb, ++i) {
+                for (int kb = kb_s; kb < kb_e; kb += kKps, ++i) {
                     const int s = i % ST;
-                    if (i < npre) {  // stage armed above: activation tile only
-                        tma_load_2d_hint(sB + s * Cfg::kTileB, &tmap_x, &full[s], kb * kBK, xrow, pol_x);
-                        continue;
+                    const int nk = min(kKps, kb_e - kb);
+                    if (i >= npre) {
+                        if (i >= ST && !mbar_wait(&empty[s], ((i / ST) - 1) & 1, err, 330)) { ok = false; break; }
+                        mbar_arrive_expect_tx(&full[s], nk * kKbBytes);
+                        for (int u = 0; u < nk; ++u)
+                            tma_load_2d_hint(sA + (s * kKps + u) * kTileA, &tmap_w, &full[s],
+                                             (kb + u) * kBK, wrow, pol_w);
                     }
-                    if (i >= ST && !mbar_wait(&empty[s], ((i / ST) - 1) & 1, err, 330)) { ok = false; break; }
-                    mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
-                    tma_load_2d_hint(sA + s * kTileA, &tmap_w, &full[s], kb * kBK, wrow, pol_w);
-                    tma_load_2d_hint(sB + s * Cfg::kTileB, &tmap_x, &full[s], kb * kBK, xrow, pol_x);
+                    for (int u = 0; u < nk; ++u)  // (stages armed above get their activations here)
+                        tma_load_2d_hint(sB + (s * kKps + u) * Cfg::kTileB, &tmap_x, &full[s],
+                                         (kb + u) * kBK, xrow, pol_x);
                 }
             }
         } else {
@@ -469,16 +482,20 @@ gemm_sk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
                 if (j >= 2 && !mbar_wait(&tempty[a], ((j >> 1) - 1) & 1, err, 340)) break;
                 tc_fence_after();
                 const uint32_t acc = tmem + a * BN;
-                for (int kb = kb_s; kb < kb_e; ++kb, ++i) {
+                for (int kb = kb_s; kb < kb_e; kb += kKps, ++i) {
                     const int s = i % ST;
+                    const int nk = min(kKps, kb_e - kb);
                     if (!mbar_wait(&full[s], (i / ST) & 1, err, 341)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t a_addr = smem_u32(sA + s * kTileA);
-                    const uint32_t b_addr = smem_u32(sB + s * Cfg::kTileB);
+                    for (int u = 0; u < nk; ++u) {
+                        const uint32_t a_addr = smem_u32(sA + (s * kKps + u) * kTileA);
+                        const uint32_t b_addr = smem_u32(sB + (s * kKps + u) * Cfg::kTileB);
 #pragma unroll
-                    for (int k = 0; k < kBK / 16; ++k)
-                        umma_bf16(acc, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32),
-                                  idesc, (kb > kb_s || k > 0) ? 1u : 0u);
+                        for (int k = 0; k < kBK / 16; ++k)
+                            umma_bf16(acc, umma_desc_sw128(a_addr + k * 32),
+                                      umma_desc_sw128(b_addr + k * 32), idesc,
+                                      (kb > kb_s || u > 0 || k > 0) ? 1u : 0u);
+                    }
                     umma_commit(&empty[s]);
                 }
                 umma_commit(&tfull[a]);
@@ -618,9 +635,10 @@ gemm_sk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
 template <int BN>
 struct ClCfg {
     static constexpr int kTileB = BN * kBK * 2;
-    static constexpr int kStageBytes = kTileA + kTileB;
-    static constexpr int kStages = BN >= 128 ? 4 : (BN >= 64 ? 5 : 6);
+    static constexpr int kStageBytes = kKps * (kTileA + kTileB);
     static constexpr int kPartBytes = kBM * BN * 4;
+    static constexpr int kStages = (kRingBudget - kPartBytes) / kStageBytes > 8
+                                       ? 8 : (kRingBudget - kPartBytes) / kStageBytes;
     static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
     static constexpr size_t kSmem =
         static_cast<size_t>(kStages) * kStageBytes + kPartBytes + 1024 + 256;
@@ -638,8 +656,8 @@ gemm_cl_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sA = smem;
-    uint8_t* sB = smem + ST * kTileA;
+    uint8_t* sA = smem;                      // [ST][kKps] weight tiles
+    uint8_t* sB = smem + ST * kKps * kTileA;  // [ST][kKps] activation tiles
     float* part = reinterpret_cast<float*>(smem + ST * Cfg::kStageBytes);  // [BN][128]
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + ST * Cfg::kStageBytes + Cfg::kPartBytes);
     uint64_t* empty = full + ST;
@@ -688,13 +706,17 @@ gemm_cl_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
             tma_prefetch_desc(&tmap_x);
             const uint64_t pol_w = policy_evict_first();
             const uint64_t pol_x = policy_evict_last();
-            // weight tiles of the first ST k-blocks before the dependency wait (see gemm_sk_kernel)
+            // weight tiles of the first ST stages before the dependency wait (see gemm_sk_kernel)
+            constexpr uint32_t kKbBytes = kTileA + Cfg::kTileB;
             int npre = 0;
             for (int i = 0; i < my_tiles && npre < ST; ++i) {
                 const int wrow = (q + i * n_clusters) * kBM;
-                for (int kb = kb0; kb < kb1 && npre < ST; ++kb, ++npre) {
-                    mbar_arrive_expect_tx(&full[npre], Cfg::kStageBytes);
-                    tma_load_2d_hint(sA + npre * kTileA, &tmap_w, &full[npre], kb * kBK, wrow, pol_w);
+                for (int kb = kb0; kb < kb1 && npre < ST; kb += kKps, ++npre) {
+                    const int nk = min(kKps, kb1 - kb);
+                    mbar_arrive_expect_tx(&full[npre], nk * kKbBytes);
+                    for (int u = 0; u < nk; ++u)
+                        tma_load_2d_hint(sA + (npre * kKps + u) * kTileA, &tmap_w, &full[npre],
+                                         (kb + u) * kBK, wrow, pol_w);
                 }
             }
             pdl_wait();
@@ -703,16 +725,19 @@ gemm_cl_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
             bool ok = true;
             for (int i = 0; i < my_tiles && ok; ++i) {
                 const int wrow = (q + i * n_clusters) * kBM;
-                for (int kb = kb0; kb < kb1; ++kb, ++it) {
+                for (int kb = kb0; kb < kb1; kb += kKps, ++it) {
                     const int s = it % ST;
-                    if (it < npre) {
-                        tma_load_2d_hint(sB + s * Cfg::kTileB, &tmap_x, &full[s], kb * kBK, 0, pol_x);
-                        continue;
+                    const int nk = min(kKps, kb1 - kb);
+                    if (it >= npre) {
+                        if (it >= ST && !mbar_wait(&empty[s], ((it / ST) - 1) & 1, err, 430)) { ok = false; break; }
+                        mbar_arrive_expect_tx(&full[s], nk * kKbBytes);
+                        for (int u = 0; u < nk; ++u)
+                            tma_load_2d_hint(sA + (s * kKps + u) * kTileA, &tmap_w, &full[s],
+                                             (kb + u) * kBK, wrow, pol_w);
                     }
-                    if (it >= ST && !mbar_wait(&empty[s], ((it / ST) - 1) & 1, err, 430)) { ok = false; break; }
-                    mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
-                    tma_load_2d_hint(sA + s * kTileA, &tmap_w, &full[s], kb * kBK, wrow, pol_w);
-                    tma_load_2d_hint(sB + s * Cfg::kTileB, &tmap_x, &full[s], kb * kBK, 0, pol_x);
+                    for (int u = 0; u < nk; ++u)
+                        tma_load_2d_hint(sB + (s * kKps + u) * Cfg::kTileB, &tmap_x, &full[s],
+                                         (kb + u) * kBK, 0, pol_x);
                 }
             }
         } else {
@@ -731,16 +756,20 @@ gemm_cl_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
                 if (i >= 2 && !mbar_wait(&tempty[a], ((i >> 1) - 1) & 1, err, 440)) break;
                 tc_fence_after();
                 const uint32_t acc = tmem + a * BN;
-                for (int kb = kb0; kb < kb1; ++kb, ++it) {
+                for (int kb = kb0; kb < kb1; kb += kKps, ++it) {
                     const int s = it % ST;
+                    const int nk = min(kKps, kb1 - kb);
                     if (!mbar_wait(&full[s], (it / ST) & 1, err, 441)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t a_addr = smem_u32(sA + s * kTileA);
-                    const uint32_t b_addr = smem_u32(sB + s * Cfg::kTileB);
+                    for (int u = 0; u < nk; ++u) {
+                        const uint32_t a_addr = smem_u32(sA + (s * kKps + u) * kTileA);
+                        const uint32_t b_addr = smem_u32(sB + (s * kKps + u) * Cfg::kTileB);
 #pragma unroll
-                    for (int k = 0; k < kBK / 16; ++k)
-                        umma_bf16(acc, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32),
-                                  idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+                        for (int k = 0; k < kBK / 16; ++k)
+                            umma_bf16(acc, umma_desc_sw128(a_addr + k * 32),
+                                      umma_desc_sw128(b_addr + k * 32), idesc,
+                                      (kb > kb0 || u > 0 || k > 0) ? 1u : 0u);
+                    }
                     umma_commit(&empty[s]);
                 }
                 umma_commit(&tfull[a]);

@@ -7,7 +7,8 @@ import re
 
 PKG = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 ROOT = os.path.dirname(PKG)
-LIB_PATH = os.path.join(PKG, "libmsgl.so")
+# the in-tree build; MSGL_LIB names another build of the same library (e.g. a debug build)
+LIB_PATH = os.environ.get("MSGL_LIB") or os.path.join(PKG, "libmsgl.so")
 HEADERS = [os.path.join(ROOT, "include", f) for f in ("msgl_kernels.h", "msgl_engine.h")]
 
 P, I, I64, F, SZ, U64 = C.c_void_p, C.c_int, C.c_int64, C.c_float, C.c_size_t, C.c_uint64
