@@ -256,7 +256,8 @@ def run_ours(args, rank, world, local_rank):
 
     import msgl
     from msgl import ops
-    from msgl.model import BatchT, Qwen3Model, TPComm, device_view, make_step, shard_plan
+    from msgl.model import (SHARED_PREFIX_DETECT, BatchT, Qwen3Model, TPComm, device_view,
+                            make_step, shard_plan)
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -326,7 +327,7 @@ def run_ours(args, rank, world, local_rank):
     hb = BatchT(BATCH, BATCH, 1, pt.shape[1], CTX, 1,
                 *[pinned[k].data_ptr() for k in ("input_ids", "positions", "slot_mapping",
                                                   "page_table", "seq_lens", "q_indptr",
-                                                  "last_idx")])
+                                                  "last_idx")], SHARED_PREFIX_DETECT)
     out_host = torch.empty(BATCH, dtype=torch.int32).pin_memory()
     lib = msgl.lib()
     sp = stream.cuda_stream
@@ -346,19 +347,24 @@ def run_ours(args, rank, world, local_rank):
     d2h = BATCH * 4
     assert torch.equal(out_host.to(dev), nxt), "host step and device step disagree"
 
-    # ---- roofline: paged decode attention alone, every layer's pool
+    # ---- roofline: the step's decode attention (cascade over the shared prefix) alone, every
+    # layer's pool
     hq, hkv = hq_l, hkv_l  # this rank's heads
     q = torch.empty(BATCH, hq, 128, dtype=torch.bfloat16, device=dev)
     ops.fill_normal_(q, seed=5, std=1.0)
     aout = torch.empty_like(q)
-    ws = ops.attention_workspace(BATCH, CTX, hq, hkv, dev)
+    shared = int(sb.struct.shared_prefix_pages)
+    assert shared == PREFIX // PAGE, shared
+    wsn = lib.msgl_paged_attention_cascade_workspace_size(BATCH, CTX, shared, hq, hkv, 128)
+    ws = torch.zeros(wsn, dtype=torch.uint8, device=dev)
     pt_d, seq_d = sb.tensors["page_table"], sb.tensors["seq_lens"]
 
     def attn(l):
         k, v, n = pools[l]
-        msgl.check(lib.msgl_paged_attention_decode(
+        msgl.check(lib.msgl_paged_attention_decode_cascade(
             q.data_ptr(), k, v, n, pt_d.data_ptr(), pt_d.shape[1], seq_d.data_ptr(), BATCH, CTX,
-            hq, hkv, 128, PAGE, 1.0 / 128 ** 0.5, aout.data_ptr(), ws.data_ptr(), ws.numel(), sp))
+            shared, hq, hkv, 128, PAGE, 1.0 / 128 ** 0.5, aout.data_ptr(), ws.data_ptr(),
+            ws.numel(), sp))
 
     for l in range(L):
         attn(l)
@@ -400,7 +406,7 @@ def run_ours(args, rank, world, local_rank):
             "e2e": {"value": BATCH / (ms_e2e * 1e-3), "unit": UNIT,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": ms_e2e},
-            "roofline": {"kernel": "paged_decode_kernel", "bound": "hbm",
+            "roofline": {"kernel": "paged_decode_cascade_kernel", "bound": "hbm",
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
                          # the capture is of 8 kv heads; a TP rank reads its own heads only
@@ -425,7 +431,8 @@ def run_ours(args, rank, world, local_rank):
 
 def run_case(args):
     """Small single-kernel cases at the bench's shapes, for profiling (one layer, < 1 GB):
-    `attention`: paged decode attention, 128 requests x 2048 context (shared 1024 prefix);
+    `attention` / `attention_cascade`: paged decode attention (plain / cascade over the shared
+    prefix), 128 requests x 2048 context (shared 1024 prefix);
     `gemm`: the gate_up + SwiGLU projection of one layer at 128 tokens (201 MB of weights)."""
     import torch
 
@@ -436,7 +443,7 @@ def run_case(args):
     hq, hkv, H, I = CFG8B["num_q_heads"], CFG8B["num_kv_heads"], CFG8B["hidden"], CFG8B["inter"]
     if args.case == "breakdown":
         return run_breakdown(args, dev)
-    if args.case == "attention":
+    if args.case in ("attention", "attention_cascade"):
         num_pages, pt = build_pages()
         kp = torch.empty(num_pages * PAGE, hkv * 128, dtype=torch.bfloat16, device=dev)
         vp = torch.empty_like(kp)
@@ -445,8 +452,15 @@ def run_case(args):
         q = ops.fill_normal_(torch.empty(BATCH, hq, 128, dtype=torch.bfloat16, device=dev), seed=5)
         ptd = torch.from_numpy(pt).to(dev)
         seq = torch.full((BATCH,), CTX, dtype=torch.int32, device=dev)
-        ws = ops.attention_workspace(BATCH, CTX, hq, hkv, dev)
-        run = lambda: ops.paged_attention_decode(q, kp, vp, ptd, seq, CTX, hq, hkv, workspace=ws)
+        if args.case == "attention":
+            ws = ops.attention_workspace(BATCH, CTX, hq, hkv, dev)
+            run = lambda: ops.paged_attention_decode(q, kp, vp, ptd, seq, CTX, hq, hkv, workspace=ws)
+        else:  # the step's kernel: cascade over the 1024-token shared prefix
+            n = ops.lib().msgl_paged_attention_cascade_workspace_size(BATCH, CTX, PREFIX // PAGE,
+                                                                      hq, hkv, 128)
+            ws = torch.zeros(n, dtype=torch.uint8, device=dev)
+            run = lambda: ops.paged_attention_decode_cascade(q, kp, vp, ptd, seq, CTX,
+                                                             PREFIX // PAGE, hq, hkv, workspace=ws)
     elif args.case == "gemm":
         x = ops.fill_normal_(torch.empty(BATCH, H, dtype=torch.bfloat16, device=dev), seed=6)
         w = ops.fill_normal_(torch.empty(2 * I, H, dtype=torch.bfloat16, device=dev), seed=7,
@@ -534,6 +548,11 @@ def run_breakdown(args, dev):
     unique = (PREFIX + BATCH * (CTX - PREFIX)) * hkv * 128 * 4
     timed("paged_decode", [lambda: ops.paged_attention_decode(q, kp, vp, ptd, seq, CTX, hq, hkv,
                                                                workspace=aws)], unique)
+    cws = torch.zeros(ops.lib().msgl_paged_attention_cascade_workspace_size(BATCH, CTX, PREFIX // PAGE,
+                                                                            hq, hkv, 128),
+                      dtype=torch.uint8, device=dev)
+    timed("paged_decode_cascade", [lambda: ops.paged_attention_decode_cascade(
+        q, kp, vp, ptd, seq, CTX, PREFIX // PAGE, hq, hkv, workspace=cws)], unique)
     r = torch.zeros(BATCH, H, dtype=torch.float32, device=dev)
     nw = torch.ones(H, dtype=torch.bfloat16, device=dev)
     timed("add_rmsnorm", [lambda: ops.add_rmsnorm_(x, r, nw, 1e-6)], BATCH * H * 12)
@@ -551,7 +570,8 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--case", choices=["attention", "gemm", "gemm_qkv", "breakdown"], default=None,
+    ap.add_argument("--case", choices=["attention", "attention_cascade", "gemm", "gemm_qkv",
+                                       "breakdown"], default=None,
                     help="run one kernel of the step on a small single-layer case (profiling)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))

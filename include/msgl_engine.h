@@ -50,7 +50,13 @@ typedef struct {
     const int* seq_lens;     /* [B] context length including this step's tokens */
     const int* q_indptr;     /* [B+1] */
     const int* last_idx;     /* [B] row of each request's last token (q_indptr[r+1]-1) */
+    int shared_prefix_pages; /* > 0: the first n page-table columns are the same pages in every
+                                row (a prefix shared through the radix cache) and every context
+                                covers them; decode then runs the cascade kernel. 0: none.
+                                MSGL_SHARED_PREFIX_DETECT (msgl_model_step_host only): computed
+                                from the host page table */
 } msgl_batch;
+#define MSGL_SHARED_PREFIX_DETECT (-1)
 
 MSGL_API int msgl_model_create(const msgl_model_config* cfg, msgl_model** out);
 MSGL_API int msgl_model_destroy(msgl_model* m);

@@ -131,6 +131,28 @@ MSGL_API int msgl_paged_attention_decode(const void* q, const void* k_pool, cons
                                 float scale, void* out, void* workspace,
                                 size_t workspace_bytes, msgl_stream_t stream);
 
+/* Cascade decode for a batch whose first `shared_pages` page-table columns hold the same pages
+ * in every row (a prefix shared through the radix cache, RadixCache::match_prefix) and whose
+ * contexts all cover them. Same result as msgl_paged_attention_decode: the shared pages are
+ * attended once per kv head for all requests' query heads together (full MMA rows), each
+ * request's remaining pages as in plain decode, and the partial softmax states merged in a fixed
+ * order. The kernel checks the sharing (a row that differs, or a context shorter than the prefix,
+ * is recorded as MSGL_ERR_BOUNDS in the error word, sites 204 / 205). No counterpart in the
+ * reference; workspace: msgl_paged_attention_cascade_workspace_size, zero-filled once, left
+ * zero-filled. */
+MSGL_API size_t msgl_paged_attention_cascade_workspace_size(int num_reqs, int max_seq_len,
+                                                           int shared_pages, int num_q_heads,
+                                                           int num_kv_heads, int head_dim);
+MSGL_API int msgl_paged_attention_decode_cascade(const void* q, const void* k_pool,
+                                                 const void* v_pool, int64_t num_slots,
+                                                 const int* page_table, int max_pages,
+                                                 const int* seq_lens, int num_reqs,
+                                                 int max_seq_len, int shared_pages,
+                                                 int num_q_heads, int num_kv_heads, int head_dim,
+                                                 int page_size, float scale, void* out,
+                                                 void* workspace, size_t workspace_bytes,
+                                                 msgl_stream_t stream);
+
 /* Decode without a caller workspace. No counterpart in the reference (its launchers take no
  * workspace); this is an addition for callers that cannot hand in device memory. Same arguments
  * and results as msgl_paged_attention_decode minus the workspace: the scratch is a file-scope

@@ -510,6 +510,369 @@ paged_extend_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
     }
 }
 
+// ------------------------------------------------------------------------------ cascade decode
+// Decode when the first S page-table columns are the same pages for every request (a prefix
+// shared through the radix cache). One launch, two kinds of CTA:
+//  * prefix CTAs (first in the grid): (prefix chunk, kv head g, 64-row tile) -- the rows are the
+//    (request, query head of g) pairs of all requests, so one warp's 16 MMA rows are 16 / group
+//    requests x group heads and every row is live; the chunk's shared pages are read once per kv
+//    head (4 pages of one head per 32 KB stage, a 3-D box {64, 16, 2}); no mask (every request
+//    sees the whole prefix);
+//  * suffix CTAs: the decode CTAs of the plain kernel over page columns >= S.
+// Both write unnormalised partials (O, m, l) to the workspace; the last CTA to arrive for a
+// (request, head group) merges its suffix chunks then its prefix chunks, in that fixed order.
+struct CascadePlan {
+    int shared_pages;  // S
+    int pc_pages;      // prefix pages per prefix chunk
+    int n_pchunks;     // prefix chunks
+    int row_tiles;     // 64-row tiles of (request, q head) rows of one kv head
+    int n_pre;         // prefix CTAs = n_pchunks * Hkv * row_tiles
+    int chunk_pages;   // suffix pages per suffix chunk
+    int chunks_sfx;    // suffix chunks per (request, head group) in the grid
+    int n_hg;          // head groups
+    int max_chunks;    // workspace chunk stride = chunks_sfx + n_pchunks
+};
+constexpr int kPrePagesPerStage = 4;
+constexpr int kPreRows = kDecWarps * 16;  // 64 rows per prefix CTA
+
+// The 128 consumer threads merge request b's head group hg: suffix chunks 0..nsfx-1, then prefix
+// chunks chunks_sfx .. chunks_sfx + n_pchunks - 1.
+__device__ __forceinline__ void cascade_merge(int b, int hg, int nsfx, int hq, int nq,
+                                              const CascadePlan& cp, const float* ws_o,
+                                              const float* ws_ml, __nv_bfloat16* out) {
+    const int qh0 = hg * nq;
+    const int total = nsfx + cp.n_pchunks;
+    for (int item = threadIdx.x; item < nq * 16; item += kDecWarps * 32) {
+        const int qh = qh0 + (item >> 4), d0 = (item & 15) * 8;
+        float M = kNegInf;
+        for (int k = 0; k < total; ++k) {
+            const int ch = k < nsfx ? k : cp.chunks_sfx + (k - nsfx);
+            M = fmaxf(M, __ldcg(ws_ml + ((static_cast<int64_t>(b) * cp.max_chunks + ch) * hq + qh) * 2));
+        }
+        float O[8] = {0, 0, 0, 0, 0, 0, 0, 0}, Ls = 0.f;
+        for (int k = 0; k < total; ++k) {
+            const int ch = k < nsfx ? k : cp.chunks_sfx + (k - nsfx);
+            const int64_t pi = (static_cast<int64_t>(b) * cp.max_chunks + ch) * hq + qh;
+            const float mc = __ldcg(ws_ml + pi * 2);
+            const float sc = (mc == kNegInf) ? 0.f : exp2f(mc - M);
+            Ls += __ldcg(ws_ml + pi * 2 + 1) * sc;
+            const float4* src = reinterpret_cast<const float4*>(ws_o + pi * kHd + d0);
+            const float4 x0 = __ldcg(src), x1 = __ldcg(src + 1);
+            O[0] += x0.x * sc; O[1] += x0.y * sc; O[2] += x0.z * sc; O[3] += x0.w * sc;
+            O[4] += x1.x * sc; O[5] += x1.y * sc; O[6] += x1.z * sc; O[7] += x1.w * sc;
+        }
+        const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) O[e] *= inv;
+        store_bf16x8(out + (static_cast<int64_t>(b) * hq + qh) * kHd + d0, O);
+    }
+}
+
+// suffix chunks of request b that have pages (the suffix CTAs that arrive)
+__device__ __forceinline__ int cascade_nsfx(int L, const CascadePlan& cp) {
+    const int npages = (L + kPage - 1) / kPage;
+    const int sp = npages - cp.shared_pages;
+    return sp > 0 ? (sp + cp.chunk_pages - 1) / cp.chunk_pages : 0;
+}
+
+__global__ void __launch_bounds__(kDecThreads, 2)
+paged_decode_cascade_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+                            const __grid_constant__ CUtensorMap tk1, const __grid_constant__ CUtensorMap tv1,
+                            const __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ out,
+                            const int* __restrict__ page_table, int max_pages,
+                            const int* __restrict__ seq_lens, int num_reqs, int pool_pages, int hq,
+                            int hkv, int hc, CascadePlan cp, float sl2e, float* __restrict__ ws_o,
+                            float* __restrict__ ws_ml, int* __restrict__ ws_cnt, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = align1024(smem_raw);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDecStages * kDecStageBytes);
+    uint64_t* empty = full + kDecStages;
+    int* flag = reinterpret_cast<int*>(empty + kDecStages);
+    int* mlist = flag + 4;              // [kPreRows] requests this CTA merges
+    int* pages = mlist + kPreRows;      // [<= kMaxChunkPages] page ids
+    if (threadIdx.x == 0) {
+        for (int st = 0; st < kDecStages; ++st) {
+            mbar_init(&full[st], 1);
+            mbar_init(&empty[st], kDecWarps);
+        }
+        fence_barrier_init();
+    }
+    pdl_wait();
+    pdl_trigger();
+    const int group = hq / hkv;
+    const int nq = hc * group;  // query heads per head group
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g4 = lane >> 2, c = lane & 3;
+    const int S = cp.shared_pages;
+    const int maxL = max_pages * kPage;
+
+    if (blockIdx.x < static_cast<unsigned>(cp.n_pre)) {
+        // ======================================================== prefix CTA
+        const int pc = blockIdx.x % cp.n_pchunks;
+        const int kvh = (blockIdx.x / cp.n_pchunks) % hkv;
+        const int rt = blockIdx.x / (cp.n_pchunks * hkv);
+        const int hg = kvh / hc;
+        const int pbeg = pc * cp.pc_pages;
+        const int np = min(S - pbeg, cp.pc_pages);
+        const int nsteps = (np + kPrePagesPerStage - 1) / kPrePagesPerStage;
+        __syncthreads();
+        if (warp == kDecWarps) {
+            for (int i = lane; i < np; i += 32) {
+                int page = page_table[pbeg + i];  // row 0: the shared columns
+                if (static_cast<unsigned>(page) >= static_cast<unsigned>(pool_pages)) {
+                    record_error(err, MSGL_ERR_BOUNDS, 206);
+                    page = 0;
+                }
+                pages[i] = page;
+            }
+            __syncwarp();
+            if (lane == 0) {
+                tma_prefetch_desc(&tk1);
+                tma_prefetch_desc(&tv1);
+                for (int it = 0; it < nsteps; ++it) {
+                    const int st = it % kDecStages;
+                    if (it >= kDecStages && !mbar_wait(&empty[st], ((it / kDecStages) - 1) & 1, err, 240))
+                        break;
+                    const int cnt = min(kPrePagesPerStage, np - it * kPrePagesPerStage);
+                    mbar_arrive_expect_tx(&full[st], cnt * 8192);
+                    uint8_t* stg = smem + st * kDecStageBytes;
+                    for (int pp = 0; pp < cnt; ++pp) {
+                        const int y = pages[it * kPrePagesPerStage + pp] * kPage;
+                        tma_load_3d(stg + pp * 4096, &tk1, &full[st], 0, y, 2 * kvh);
+                        tma_load_3d(stg + kDecHalfStage + pp * 4096, &tv1, &full[st], 0, y, 2 * kvh);
+                    }
+                }
+            }
+            return;
+        }
+        // rows of this warp: r = rt * 64 + warp * 16 + i -> request r / group, head r % group
+        const int rbase = rt * kPreRows + warp * 16;
+        const int ra = rbase + g4, rb = rbase + g4 + 8;
+        const int ba = ra / group, bb = rb / group;
+        const bool va = ba < num_reqs, vb = bb < num_reqs;
+        const int qa_h = kvh * group + ra % group, qb_h = kvh * group + rb % group;
+        uint32_t qa[8][4];
+        {
+            const __nv_bfloat16* q0 = q + (static_cast<int64_t>(va ? ba : 0) * hq + qa_h) * kHd;
+            const __nv_bfloat16* q1 = q + (static_cast<int64_t>(vb ? bb : 0) * hq + qb_h) * kHd;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+                qa[kk][0] = va ? *reinterpret_cast<const uint32_t*>(q0 + 16 * kk + 2 * c) : 0u;
+                qa[kk][2] = va ? *reinterpret_cast<const uint32_t*>(q0 + 16 * kk + 8 + 2 * c) : 0u;
+                qa[kk][1] = vb ? *reinterpret_cast<const uint32_t*>(q1 + 16 * kk + 2 * c) : 0u;
+                qa[kk][3] = vb ? *reinterpret_cast<const uint32_t*>(q1 + 16 * kk + 8 + 2 * c) : 0u;
+            }
+        }
+        float o[16][4];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+        float m[2] = {kNegInf, kNegInf}, l[2] = {0.f, 0.f};
+        constexpr int kAll = 0x3fffffff;  // no mask: every request sees the whole prefix
+        for (int it = 0; it < nsteps; ++it) {
+            const int st = it % kDecStages;
+            if (!mbar_wait(&full[st], (it / kDecStages) & 1, err, 241)) break;
+            const int cnt = min(kPrePagesPerStage, np - it * kPrePagesPerStage);
+            const uint32_t base = smem_u32(smem + st * kDecStageBytes);
+            for (int pp = 0; pp < cnt; ++pp)
+                attend_page<true>(base + pp * 4096, base + kDecHalfStage + pp * 4096, qa, o, m, l,
+                                  0, kAll, kAll, sl2e, lane);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);
+        }
+        // partials of rows ra, rb -> chunk chunks_sfx + pc
+        const int ch = cp.chunks_sfx + pc;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            float ls = l[r];
+            ls += __shfl_xor_sync(0xffffffffu, ls, 1);
+            ls += __shfl_xor_sync(0xffffffffu, ls, 2);
+            const bool valid = r == 0 ? va : vb;
+            if (!valid) continue;
+            const int bq = r == 0 ? ba : bb, qh = r == 0 ? qa_h : qb_h;
+            const int64_t pi = (static_cast<int64_t>(bq) * cp.max_chunks + ch) * hq + qh;
+            float* dst = ws_o + pi * kHd;
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                *reinterpret_cast<float2*>(dst + 8 * j + 2 * c) = make_float2(o[j][2 * r], o[j][2 * r + 1]);
+            if (c == 0) {
+                ws_ml[pi * 2] = m[r];
+                ws_ml[pi * 2 + 1] = ls;
+            }
+        }
+        // arrive for every request of the tile; merge those this CTA completes
+        __threadfence();
+        named_bar_sync(1, kDecWarps * 32);
+        const int rq0 = rt * kPreRows / group;
+        const int nrq = min(kPreRows / group, num_reqs - rq0);
+        if (threadIdx.x == 0) *flag = 0;
+        named_bar_sync(1, kDecWarps * 32);
+        if (threadIdx.x < nrq) {
+            const int bq = rq0 + threadIdx.x;
+            int L = seq_lens[bq];
+            L = L < 0 ? 0 : (L > maxL ? maxL : L);
+            const int expected = cascade_nsfx(L, cp) + cp.n_pchunks * hc;
+            const int old = atomicAdd(&ws_cnt[static_cast<int64_t>(bq) * cp.n_hg + hg], 1);
+            if (old == expected - 1) mlist[atomicAdd(flag, 1)] = bq;
+        }
+        named_bar_sync(1, kDecWarps * 32);
+        const int nm = *flag;
+        if (nm == 0) return;
+        __threadfence();
+        for (int k = 0; k < nm; ++k) {
+            const int bq = mlist[k];
+            int L = seq_lens[bq];
+            L = L < 0 ? 0 : (L > maxL ? maxL : L);
+            cascade_merge(bq, hg, cascade_nsfx(L, cp), hq, nq, cp, ws_o, ws_ml, out);
+            if (threadIdx.x == 0) ws_cnt[static_cast<int64_t>(bq) * cp.n_hg + hg] = 0;
+        }
+        return;
+    }
+
+    // ============================================================ suffix CTA
+    const int sidx = blockIdx.x - cp.n_pre;
+    const int chunk = sidx % cp.chunks_sfx;
+    const int hg = (sidx / cp.chunks_sfx) % cp.n_hg;
+    const int b = sidx / (cp.chunks_sfx * cp.n_hg);
+    const int pps = kDecWarps / hc;
+    const int qh0 = hg * nq;
+    int L = seq_lens[b];
+    if (L < 0 || L > maxL) {
+        if (threadIdx.x == 0 && chunk == 0 && hg == 0) record_error(err, MSGL_ERR_BOUNDS, 202);
+        L = L < 0 ? 0 : maxL;
+    }
+    const int npages = (L + kPage - 1) / kPage;
+    if (chunk == 0 && hg == 0 && warp == kDecWarps) {  // the batch must really share the prefix
+        if (L < S * kPage && lane == 0) record_error(err, MSGL_ERR_BOUNDS, 204);
+        for (int i = lane; i < S; i += 32)
+            if (page_table[static_cast<int64_t>(b) * max_pages + i] != page_table[i])
+                record_error(err, MSGL_ERR_BOUNDS, 205);
+    }
+    const int p0 = S + chunk * cp.chunk_pages;
+    if (p0 >= npages) return;  // no suffix pages for this chunk: it does not arrive
+    const int np = min(npages - p0, cp.chunk_pages);
+    const int nsteps = (np + pps - 1) / pps;
+    __syncthreads();
+
+    if (warp == kDecWarps) {
+        const int* pt = page_table + static_cast<int64_t>(b) * max_pages + p0;
+        for (int i = lane; i < np; i += 32) {
+            int page = pt[i];
+            if (static_cast<unsigned>(page) >= static_cast<unsigned>(pool_pages)) {
+                record_error(err, MSGL_ERR_BOUNDS, 201);
+                page = 0;
+            }
+            pages[i] = page;
+        }
+        __syncwarp();
+        if (lane == 0) {
+            tma_prefetch_desc(&tk);
+            tma_prefetch_desc(&tv);
+            const int page_half = hc * 4096;
+            for (int it = 0; it < nsteps; ++it) {
+                const int st = it % kDecStages;
+                if (it >= kDecStages && !mbar_wait(&empty[st], ((it / kDecStages) - 1) & 1, err, 200))
+                    break;
+                const int cnt = min(pps, np - it * pps);
+                mbar_arrive_expect_tx(&full[st], cnt * 2 * page_half);
+                uint8_t* stg = smem + st * kDecStageBytes;
+                for (int pp = 0; pp < cnt; ++pp) {
+                    const int y = pages[it * pps + pp] * kPage;
+                    tma_load_3d(stg + pp * page_half, &tk, &full[st], 0, y, 2 * hc * hg);
+                    tma_load_3d(stg + kDecHalfStage + pp * page_half, &tv, &full[st], 0, y, 2 * hc * hg);
+                }
+            }
+        }
+        return;
+    }
+    const int head = warp % hc, psub = warp / hc;
+    uint32_t qa[8][4];
+    {
+        const bool real = g4 < group;
+        const __nv_bfloat16* qr =
+            q + (static_cast<int64_t>(b) * hq + qh0 + head * group + (real ? g4 : 0)) * kHd;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+            qa[kk][0] = real ? *reinterpret_cast<const uint32_t*>(qr + 16 * kk + 2 * c) : 0u;
+            qa[kk][2] = real ? *reinterpret_cast<const uint32_t*>(qr + 16 * kk + 8 + 2 * c) : 0u;
+            qa[kk][1] = 0u;
+            qa[kk][3] = 0u;
+        }
+    }
+    float o[16][4];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    float m[2] = {kNegInf, kNegInf}, l[2] = {0.f, 0.f};
+    const uint32_t my_off = (psub * hc + head) * 4096;
+    for (int it = 0; it < nsteps; ++it) {
+        const int st = it % kDecStages;
+        if (!mbar_wait(&full[st], (it / kDecStages) & 1, err, 210)) break;
+        const int pidx = it * pps + psub;
+        if (pidx < np) {
+            const uint32_t base = smem_u32(smem + st * kDecStageBytes) + my_off;
+            attend_page<false>(base, base + kDecHalfStage, qa, o, m, l, (p0 + pidx) * kPage, L - 1,
+                               -1, sl2e, lane);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+    }
+    // combine the pps warps of each head, write this chunk's partial
+    float lsum = l[0];
+    lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
+    lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);
+    named_bar_sync(1, kDecWarps * 32);
+    float* mo = reinterpret_cast<float*>(smem);
+    float* mm = mo + kDecWarps * 8 * kHd;
+    float* ml = mm + kDecWarps * 8;
+    if (g4 < group) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            mo[(warp * 8 + g4) * kHd + 8 * j + 2 * c] = o[j][0];
+            mo[(warp * 8 + g4) * kHd + 8 * j + 2 * c + 1] = o[j][1];
+        }
+        if (c == 0) {
+            mm[warp * 8 + g4] = m[0];
+            ml[warp * 8 + g4] = lsum;
+        }
+    }
+    named_bar_sync(1, kDecWarps * 32);
+    for (int item = threadIdx.x; item < nq * 16; item += kDecWarps * 32) {
+        const int lq = item >> 4, d0 = (item & 15) * 8;
+        const int h = lq / group, r = lq % group;
+        const int qh = qh0 + lq;
+        float M = kNegInf;
+        for (int ps = 0; ps < pps; ++ps) M = fmaxf(M, mm[(ps * hc + h) * 8 + r]);
+        float O[8] = {0, 0, 0, 0, 0, 0, 0, 0}, Ls = 0.f;
+        for (int ps = 0; ps < pps; ++ps) {
+            const int w = ps * hc + h;
+            const float mw = mm[w * 8 + r];
+            const float sc = (mw == kNegInf) ? 0.f : exp2f(mw - M);
+            Ls += ml[w * 8 + r] * sc;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) O[e] += mo[(w * 8 + r) * kHd + d0 + e] * sc;
+        }
+        const int64_t pi = (static_cast<int64_t>(b) * cp.max_chunks + chunk) * hq + qh;
+        float4* dst = reinterpret_cast<float4*>(ws_o + pi * kHd + d0);
+        dst[0] = make_float4(O[0], O[1], O[2], O[3]);
+        dst[1] = make_float4(O[4], O[5], O[6], O[7]);
+        if ((item & 15) == 0) {
+            ws_ml[pi * 2] = M;
+            ws_ml[pi * 2 + 1] = Ls;
+        }
+    }
+    __threadfence();
+    named_bar_sync(1, kDecWarps * 32);
+    int* cnt = ws_cnt + static_cast<int64_t>(b) * cp.n_hg + hg;
+    if (threadIdx.x == 0) {
+        const int expected = cascade_nsfx(L, cp) + cp.n_pchunks * hc;
+        *flag = (atomicAdd(cnt, 1) == expected - 1);
+    }
+    named_bar_sync(1, kDecWarps * 32);
+    if (!*flag) return;
+    __threadfence();
+    cascade_merge(b, hg, cascade_nsfx(L, cp), hq, nq, cp, ws_o, ws_ml, out);
+    if (threadIdx.x == 0) *cnt = 0;
+}
+
 // ------------------------------------------------------------------------------ host side
 constexpr size_t kDecodeCounterBytes = 262144;  // one int per request: up to 65536
 
@@ -581,6 +944,34 @@ int make_decode_maps(CUtensorMap* tk, CUtensorMap* tv, const void* k_pool, const
 // load zero-fills it), shared by every call of that entry point on the device.
 constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB
 static __device__ __align__(256) uint8_t g_decode_scratch[kNoAllocScratchBytes];
+
+// Cascade plan: suffix chunks from the plain decode plan of the suffix length; prefix chunks of
+// at least the suffix chunk size (so each CTA walks a similar number of pages) and no more
+// prefix chunks than suffix chunks (the workspace is then at most twice the plain one).
+CascadePlan plan_cascade(int B, int max_seq_len, int shared_pages, int hq, int hkv) {
+    CascadePlan cp{};
+    const int max_pages_seq = std::max(1, (max_seq_len + kPage - 1) / kPage);
+    const int sfx_pages = std::max(1, max_pages_seq - shared_pages);
+    const DecodePlan dp = plan_decode(B, sfx_pages * kPage, hq, hkv);
+    const int group = hq / hkv;
+    cp.shared_pages = shared_pages;
+    cp.chunk_pages = dp.chunk_pages;
+    cp.chunks_sfx = dp.max_chunks;
+    cp.pc_pages = std::min(kMaxChunkPages,
+                           std::max(cp.chunk_pages, (shared_pages + cp.chunks_sfx - 1) / cp.chunks_sfx));
+    cp.n_pchunks = (shared_pages + cp.pc_pages - 1) / cp.pc_pages;
+    cp.row_tiles = (B * group + kPreRows - 1) / kPreRows;
+    cp.n_pre = cp.n_pchunks * hkv * cp.row_tiles;
+    cp.n_hg = hkv / decode_heads_per_cta(hkv);
+    cp.max_chunks = cp.chunks_sfx + cp.n_pchunks;
+    return cp;
+}
+
+size_t cascade_workspace_bytes(int B, const CascadePlan& cp, int hq) {
+    auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+    return kDecodeCounterBytes + up(static_cast<size_t>(B) * cp.max_chunks * hq * kHd * sizeof(float)) +
+           up(static_cast<size_t>(B) * cp.max_chunks * hq * 2 * sizeof(float));
+}
 
 }  // namespace
 }  // namespace msgl
@@ -675,6 +1066,67 @@ int msgl_paged_attention_extend(const void* q, const void* k_pool, const void* v
         tk, tv, static_cast<const __nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(out), page_table,
         max_pages, seq_lens, q_indptr, static_cast<int>(num_slots / kPage), num_q_heads,
         num_kv_heads, sl2e, err);
+    MSGL_LAUNCH_CHECK();
+    return MSGL_OK;
+}
+
+size_t msgl_paged_attention_cascade_workspace_size(int num_reqs, int max_seq_len, int shared_pages,
+                                                   int num_q_heads, int num_kv_heads, int head_dim) {
+    if (num_reqs <= 0 || num_kv_heads <= 0 || head_dim != kHd || shared_pages <= 0) return 0;
+    const CascadePlan cp = plan_cascade(num_reqs, max_seq_len, shared_pages, num_q_heads, num_kv_heads);
+    return cascade_workspace_bytes(num_reqs, cp, num_q_heads);
+}
+
+int msgl_paged_attention_decode_cascade(const void* q, const void* k_pool, const void* v_pool,
+                                        int64_t num_slots, const int* page_table, int max_pages,
+                                        const int* seq_lens, int num_reqs, int max_seq_len,
+                                        int shared_pages, int num_q_heads, int num_kv_heads,
+                                        int head_dim, int page_size, float scale, void* out,
+                                        void* workspace, size_t workspace_bytes,
+                                        msgl_stream_t stream) {
+    int rc = check_common(num_q_heads, num_kv_heads, head_dim, page_size, num_slots);
+    if (rc) return rc;
+    if (num_reqs < 0 || max_seq_len < 0 || max_pages <= 0)
+        return set_error(MSGL_ERR_INVALID_ARG, "decode_cascade: bad sizes");
+    if (num_reqs == 0) return MSGL_OK;
+    if ((max_seq_len + kPage - 1) / kPage > max_pages)
+        return set_error(MSGL_ERR_INVALID_ARG, "decode_cascade: max_seq_len exceeds page-table width");
+    if (shared_pages <= 0 || shared_pages > max_pages || shared_pages * kPage > max_seq_len)
+        return set_error(MSGL_ERR_INVALID_ARG, "decode_cascade: shared_pages outside the contexts");
+    if (num_reqs > 65535) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "decode_cascade: num_reqs > 65535");
+    const CascadePlan cp = plan_cascade(num_reqs, max_seq_len, shared_pages, num_q_heads, num_kv_heads);
+    const size_t need = cascade_workspace_bytes(num_reqs, cp, num_q_heads);
+    if (!workspace || workspace_bytes < need)
+        return set_error(MSGL_ERR_WORKSPACE, "decode_cascade: workspace too small");
+    if (static_cast<size_t>(num_reqs) * cp.n_hg * sizeof(int) > kDecodeCounterBytes)
+        return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "decode_cascade: num_reqs * Hkv / 4 > 65536");
+    const int hc = decode_heads_per_cta(num_kv_heads);
+    CUtensorMap tk, tv, tk1, tv1;
+    rc = make_decode_maps(&tk, &tv, k_pool, v_pool, num_slots, num_kv_heads, hc);
+    if (rc) return rc;
+    rc = make_decode_maps(&tk1, &tv1, k_pool, v_pool, num_slots, num_kv_heads, 1);
+    if (rc) return rc;
+    int* err = device_error_word();
+    if (!err) return set_error(MSGL_ERR_CUDA, "device error word unavailable");
+    const size_t smem = kDecStages * kDecStageBytes + 2 * kDecStages * 8 + 16 +
+                        (kPreRows + kMaxChunkPages) * sizeof(int) + 1024;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaFuncSetAttribute(paged_decode_cascade_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem));
+        attr_set = true;
+    }
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const size_t o_bytes = (static_cast<size_t>(num_reqs) * cp.max_chunks * num_q_heads * kHd * sizeof(float) + 255) & ~size_t(255);
+    const int grid = cp.n_pre + cp.chunks_sfx * cp.n_hg * num_reqs;
+    const float sl2e = scale * 1.4426950408889634f;
+    launch_pdl(paged_decode_cascade_kernel, dim3(grid), dim3(kDecThreads), smem, stream, tk, tv, tk1,
+               tv1, static_cast<const __nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(out),
+               page_table, max_pages, seq_lens, num_reqs, static_cast<int>(num_slots / kPage),
+               num_q_heads, num_kv_heads, hc, cp, sl2e,
+               reinterpret_cast<float*>(ws + kDecodeCounterBytes),
+               reinterpret_cast<float*>(ws + kDecodeCounterBytes + o_bytes),
+               reinterpret_cast<int*>(ws), err);
     MSGL_LAUNCH_CHECK();
     return MSGL_OK;
 }

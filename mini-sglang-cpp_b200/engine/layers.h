@@ -163,7 +163,19 @@ class Attention {
     void forward(const bf16_t* q, const void* k_pool, const void* v_pool, int64_t num_slots,
                  const msgl_batch& b, bf16_t* out, const Scratch& ws, cudaStream_t s) const {
         const float scale = 1.0f / sqrtf(static_cast<float>(head_dim_));  // layer.cpp:212
-        if (b.is_decode)
+        // decode over a prefix that every request shares (radix-cache hit): the cascade kernel
+        // attends the shared pages once per kv head for the whole batch
+        const int sp = b.shared_prefix_pages;
+        if (b.is_decode && b.num_reqs >= 2 && sp >= kMinCascadePages && sp <= b.max_pages &&
+            sp * 16 <= b.max_seq_len &&
+            msgl_paged_attention_cascade_workspace_size(b.num_reqs, b.max_seq_len, sp, hq_, hkv_,
+                                                        head_dim_) <= ws.attn_ws_bytes)
+            ck(msgl_paged_attention_decode_cascade(q, k_pool, v_pool, num_slots, b.page_table,
+                                                   b.max_pages, b.seq_lens, b.num_reqs,
+                                                   b.max_seq_len, sp, hq_, hkv_, head_dim_, 16,
+                                                   scale, out, ws.attn_ws, ws.attn_ws_bytes, s),
+               "Attention::forward(cascade decode)");
+        else if (b.is_decode)
             ck(msgl_paged_attention_decode(q, k_pool, v_pool, num_slots, b.page_table, b.max_pages,
                                            b.seq_lens, b.num_reqs, b.max_seq_len, hq_, hkv_,
                                            head_dim_, 16, scale, out, ws.attn_ws, ws.attn_ws_bytes,
@@ -177,6 +189,8 @@ class Attention {
     }
     int hq() const { return hq_; }
     int hkv() const { return hkv_; }
+
+    static constexpr int kMinCascadePages = 2;  // shorter shared prefixes: plain decode
 
   private:
     int hq_ = 0, hkv_ = 0, head_dim_ = 128;

@@ -189,6 +189,8 @@ static void create(Model& m, const msgl_model_config& c) {
     size_t aws = 0;
     for (int b = 1; b <= static_cast<int>(B); ++b)
         aws = std::max(aws, msgl_paged_attention_workspace_size(b, c.max_position, m.hq, m.hkv, D));
+    // the cascade decode (shared prefix) needs at most twice the plain decode's partial storage
+    aws = aws > 0 ? 2 * aws : 0;
     m.attn_ws.alloc(std::max<size_t>(aws, 256));
     ckc(cudaMemset(m.attn_ws.p, 0, m.attn_ws.bytes), "attention workspace");
     m.scratch = Scratch{m.gemm_ws.p, m.gemm_ws.bytes, m.attn_ws.p, m.attn_ws.bytes};
@@ -448,7 +450,7 @@ static void forward(Model& m, const msgl_batch& b, int* next_tokens, float* logi
 
 static std::vector<int64_t> graph_key(const msgl_batch& b, const int* next, const float* logits) {
     return {b.num_tokens, b.num_reqs, b.is_decode, b.max_pages, b.max_seq_len, b.max_q_len,
-            reinterpret_cast<int64_t>(b.input_ids), reinterpret_cast<int64_t>(b.positions),
+            b.shared_prefix_pages, reinterpret_cast<int64_t>(b.input_ids), reinterpret_cast<int64_t>(b.positions),
             reinterpret_cast<int64_t>(b.slot_mapping), reinterpret_cast<int64_t>(b.page_table),
             reinterpret_cast<int64_t>(b.seq_lens), reinterpret_cast<int64_t>(b.q_indptr),
             reinterpret_cast<int64_t>(b.last_idx), reinterpret_cast<int64_t>(next),
@@ -507,6 +509,24 @@ static void step_host(Model& m, const msgl_batch& hb, int* host_next, int flags,
     h2d(m.st_indptr, hb.q_indptr, B + 1);
     h2d(m.st_last, hb.last_idx, B);
     msgl_batch db = hb;
+    if (hb.shared_prefix_pages == MSGL_SHARED_PREFIX_DETECT) {
+        // leading page-table columns that are the same page in every row, covered by every
+        // context (two or more requests)
+        int n = 0;
+        if (B >= 2) {
+            int min_len = hb.seq_lens[0];
+            for (int r = 1; r < B; ++r) min_len = std::min(min_len, hb.seq_lens[r]);
+            const int cap = std::min(hb.max_pages, min_len / 16);
+            for (; n < cap; ++n) {
+                const int p = hb.page_table[n];
+                bool same = true;
+                for (int r = 1; r < B && same; ++r)
+                    same = hb.page_table[static_cast<size_t>(r) * hb.max_pages + n] == p;
+                if (!same) break;
+            }
+        }
+        db.shared_prefix_pages = n;
+    }
     db.input_ids = m.st_ids.as<int>();
     db.positions = m.st_pos.as<int>();
     db.slot_mapping = m.st_slots.as<int>();

@@ -28,6 +28,8 @@ SIGNATURES = {
     "msgl_paged_attention_workspace_size": (SZ, [I, I, I, I, I]),
     "msgl_paged_attention_decode": (I, [P, P, P, I64, P, I, P, I, I, I, I, I, I, F, P, P, SZ, P]),
     "msgl_paged_attention_extend": (I, [P, P, P, I64, P, I, P, P, I, I, I, I, I, I, F, P, P]),
+    "msgl_paged_attention_cascade_workspace_size": (SZ, [I, I, I, I, I, I]),
+    "msgl_paged_attention_decode_cascade": (I, [P, P, P, I64, P, I, P, I, I, I, I, I, I, I, F, P, P, SZ, P]),
     "msgl_paged_attention_decode_noalloc": (I, [P, P, P, I64, P, I, P, I, I, I, I, I, I, F, P, P]),
     "msgl_gemm_workspace_size": (SZ, [I, I, I]),
     "msgl_gemm_bf16": (I, [P, P, P, I, I, I, I, P, SZ, P]),

@@ -31,7 +31,22 @@ class BatchT(C.Structure):
     _fields_ = [(n, C.c_int) for n in ("num_tokens", "num_reqs", "is_decode", "max_pages",
                                         "max_seq_len", "max_q_len")] + \
                [(n, C.c_void_p) for n in ("input_ids", "positions", "slot_mapping", "page_table",
-                                           "seq_lens", "q_indptr", "last_idx")]
+                                           "seq_lens", "q_indptr", "last_idx")] + \
+               [("shared_prefix_pages", C.c_int)]
+
+
+SHARED_PREFIX_DETECT = -1  # msgl_model_step_host computes it from the host page table
+
+
+def shared_prefix_pages(page_table: np.ndarray, seq_lens: np.ndarray, page_size: int = 16) -> int:
+    """Leading page-table columns holding the same page in every row and covered by every
+    context (0 for fewer than two requests): the prefix the cascade decode attends once."""
+    B = page_table.shape[0]
+    if B < 2:
+        return 0
+    cap = min(page_table.shape[1], int(np.min(seq_lens)) // page_size)
+    same = np.all(page_table[:, :cap] == page_table[0:1, :cap], axis=0)
+    return int(cap if same.all() else np.argmin(same))
 
 
 def _engine():
@@ -133,10 +148,11 @@ class BatchBuilder:
 def make_step(host: dict, decode: bool, device, max_seq_len: int, max_q_len: int) -> StepBatch:
     t = {k: torch.from_numpy(np.ascontiguousarray(v)).to(device) for k, v in host.items()}
     B = t["seq_lens"].numel()
+    sp = shared_prefix_pages(np.asarray(host["page_table"]), np.asarray(host["seq_lens"])) if decode else 0
     st = BatchT(t["input_ids"].numel(), B, int(decode), t["page_table"].shape[1], max_seq_len,
                 max_q_len, *[t[k].data_ptr() for k in ("input_ids", "positions", "slot_mapping",
                                                         "page_table", "seq_lens", "q_indptr",
-                                                        "last_idx")])
+                                                        "last_idx")], sp)
     return StepBatch(t, st, B)
 
 

@@ -113,6 +113,29 @@ def paged_attention_decode(q, k_pool, v_pool, page_table, seq_lens, max_seq_len,
     return out
 
 
+def paged_attention_decode_cascade(q, k_pool, v_pool, page_table, seq_lens, max_seq_len,
+                                   shared_pages, hq, hkv, scale=None, page_size=16, workspace=None,
+                                   out=None):
+    """msgl_paged_attention_decode_cascade: decode with the first `shared_pages` page-table
+    columns common to every request."""
+    _c(q, torch.bfloat16), _c(page_table, torch.int32), _c(seq_lens, torch.int32)
+    B = seq_lens.numel()
+    if scale is None:
+        scale = 1.0 / (128 ** 0.5)
+    if workspace is None:
+        n = lib().msgl_paged_attention_cascade_workspace_size(B, max_seq_len, shared_pages, hq, hkv, 128)
+        workspace = torch.zeros(max(n, 256), dtype=torch.uint8, device=q.device)
+    if out is None:
+        out = torch.empty(B, hq, 128, dtype=torch.bfloat16, device=q.device)
+    num_slots = k_pool.numel() // (hkv * 128)
+    check(lib().msgl_paged_attention_decode_cascade(_p(q), _p(k_pool), _p(v_pool), num_slots,
+                                                    _p(page_table), page_table.shape[1],
+                                                    _p(seq_lens), B, max_seq_len, shared_pages, hq,
+                                                    hkv, 128, page_size, scale, _p(out),
+                                                    _p(workspace), workspace.numel(), _s()))
+    return out
+
+
 def paged_attention_decode_noalloc(q, k_pool, v_pool, page_table, seq_lens, max_seq_len, hq, hkv,
                                    scale=None, page_size=16, out=None):
     """msgl_paged_attention_decode_noalloc: decode on the library's static scratch."""

@@ -201,6 +201,68 @@ def test_paged_extend(cuda, oracle, hq, hkv, qlens, ctx):
     assert ops.device_error() == (0, 0)
 
 
+def make_shared_prefix(rng, S, suffix_lens, hkv, extra=4, P=16, D=128):
+    """Page tables whose first S columns are the same pages for every request (a shared prefix),
+    then each request's own pages; contexts S * 16 + suffix_len."""
+    own = [(n + P - 1) // P for n in suffix_lens]
+    num_pages = S + sum(own) + extra
+    perm = rng.permutation(num_pages).astype(np.int32)
+    width = S + max(max(own), 1)
+    pt = np.zeros((len(suffix_lens), width), np.int32)
+    pt[:, :S] = perm[:S]
+    off = S
+    for r, n in enumerate(own):
+        pt[r, S:S + n] = perm[off:off + n]
+        off += n
+    kp = rn(rng, num_pages * P, hkv * D)
+    vp = rn(rng, num_pages * P, hkv * D)
+    seq = np.array([S * P + n for n in suffix_lens], np.int32)
+    return kp, vp, pt, seq
+
+
+@pytest.mark.parametrize("hq,hkv,S,suffix", [
+    (32, 8, 8, [1, 17, 300, 16, 0, 255]),     # empty suffix, partial / full last pages
+    (16, 2, 5, [40, 1, 99]),
+    (8, 1, 3, [5, 70]),                        # one kv head, group 8
+    (32, 16, 4, [33, 2]),                      # four head groups
+    (32, 8, 64, [1024] * 4 + [7, 900]),        # long shared prefix (bench-like)
+    (32, 8, 6, list(range(1, 41))),            # 40 requests: 3 row tiles of 64 (request, head) rows
+])
+def test_paged_decode_cascade(cuda, oracle, hq, hkv, S, suffix):
+    from msgl import ops
+    rng = np.random.default_rng(S * 31 + hq + len(suffix))
+    kp, vp, pt, seq = make_shared_prefix(rng, S, suffix, hkv)
+    B = len(suffix)
+    q = rn(rng, B, hq * 128)
+    ref = oracle.paged_attention(q, kp, vp, pt, seq, np.arange(B + 1, dtype=np.int32), hq, hkv, 128, 16)
+    L = int(seq.max())
+    args = (dev(q), dev(kp), dev(vp), dev(pt, torch.int32), dev(seq, torch.int32), L)
+    n = ops.lib().msgl_paged_attention_cascade_workspace_size(B, L, S, hq, hkv, 128)
+    ws = torch.zeros(n, dtype=torch.uint8, device="cuda")
+    out = host(ops.paged_attention_decode_cascade(*args, S, hq, hkv, workspace=ws)).reshape(B, -1)
+    assert rel_l2(out, ref) < 1e-2, rel_l2(out, ref)
+    plain = host(ops.paged_attention_decode(*args, hq, hkv)).reshape(B, -1)
+    assert rel_l2(out, plain) < 5e-3
+    # counters reset themselves: a second call on the same workspace gives the same bits
+    out2 = host(ops.paged_attention_decode_cascade(*args, S, hq, hkv, workspace=ws)).reshape(B, -1)
+    assert np.array_equal(out, out2)
+    assert ops.device_error() == (0, 0)
+
+
+def test_paged_decode_cascade_detects_unshared_prefix(cuda):
+    """A row whose 'shared' columns differ is reported in the error word (no fault)."""
+    from msgl import ops
+    rng = np.random.default_rng(5)
+    kp, vp, pt, seq = make_shared_prefix(rng, 4, [20, 30], 8)
+    pt[1, 2] = pt[1, 4]  # request 1 does not share column 2
+    q = rn(rng, 2, 32 * 128)
+    ops.device_error(reset=True)
+    ops.paged_attention_decode_cascade(dev(q), dev(kp), dev(vp), dev(pt, torch.int32),
+                                       dev(seq, torch.int32), int(seq.max()), 4, 32, 8)
+    torch.cuda.synchronize()
+    assert ops.device_error() == (6, 205)  # MSGL_ERR_BOUNDS at the sharing check
+
+
 def test_decode_equals_extend_single_token(cuda):
     """Decode and extend agree on one-token-per-request batches."""
     from msgl import ops
