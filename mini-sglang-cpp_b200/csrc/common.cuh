@@ -148,6 +148,16 @@ __device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
     asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
     return v;
 }
+// 16-byte load from another CTA's shared memory (volatile: stays after the barrier that
+// publishes the data; the loads of one thread are still in flight together).
+__device__ __forceinline__ float4 ld_dsmem_v4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
+}
 // Arrive (release, cluster scope) on an mbarrier of another CTA of the cluster.
 __device__ __forceinline__ void mbar_remote_arrive(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)

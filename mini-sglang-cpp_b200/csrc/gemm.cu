@@ -631,7 +631,7 @@ gemm_sk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
 // partials go to global memory and no second kernel runs. The cluster is persistent over tiles
 // q, q + n_clusters, ...; TMEM is double-buffered, so a tile's reduction and epilogue overlap
 // the next tile's mainloop. Producer warp, MMA warp and 8 epilogue warps as in the stream-K
-// kernel.
+// kernel. A CTA exits once its peers are done with its last published chunks.
 template <int BN>
 struct ClCfg {
     static constexpr int kTileB = BN * kBK * 2;
@@ -803,7 +803,8 @@ gemm_cl_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
             tc_fence_after();
             const uint32_t taddr = tmem + a * BN + (static_cast<uint32_t>(warp_q * 32) << 16);
             if (C > 1) {
-                // publish the chunks the peers own
+                // publish the chunks the peers own: chunk ci is [4 quarters][128 rows][4 floats],
+                // so one warp's 16-byte store (or a peer's load) covers 512 contiguous bytes
                 int j = 0;
                 for (int ci = 0; ci < NCH; ++ci) {
                     if (ci % C == rank) continue;
@@ -811,9 +812,12 @@ gemm_cl_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
                     uint32_t r[16];
                     tmem_ld16(taddr + ci * 16, r);
                     tmem_ld_wait();
-                    float* dst = part + ci * 16 * kBM + row;
+                    float4* dst = reinterpret_cast<float4*>(part) + ci * 4 * kBM + row;
 #pragma unroll
-                    for (int qq = 0; qq < 16; ++qq) dst[qq * kBM] = __uint_as_float(r[qq]);
+                    for (int q4 = 0; q4 < 4; ++q4)
+                        dst[q4 * kBM] =
+                            make_float4(__uint_as_float(r[4 * q4]), __uint_as_float(r[4 * q4 + 1]),
+                                        __uint_as_float(r[4 * q4 + 2]), __uint_as_float(r[4 * q4 + 3]));
                 }
                 fence_acq_rel_cluster();
                 named_bar(1, kEpiThreads);
@@ -840,12 +844,17 @@ gemm_cl_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
 #pragma unroll
                         for (int qq = 0; qq < 16; ++qq) v[qq] += __uint_as_float(r[qq]);
                     } else {
-                        const uint32_t src = mapa_shared(part_u32 + (ci * 16 * kBM + row) * 4, pr);
-                        float pv[16];
+                        const uint32_t src = mapa_shared(part_u32 + (ci * 4 * kBM + row) * 16, pr);
+                        float4 pv[4];
 #pragma unroll
-                        for (int qq = 0; qq < 16; ++qq) pv[qq] = ld_dsmem_f32(src + qq * kBM * 4);
+                        for (int q4 = 0; q4 < 4; ++q4) pv[q4] = ld_dsmem_v4(src + q4 * kBM * 16);
 #pragma unroll
-                        for (int qq = 0; qq < 16; ++qq) v[qq] += pv[qq];
+                        for (int q4 = 0; q4 < 4; ++q4) {
+                            v[4 * q4] += pv[q4].x;
+                            v[4 * q4 + 1] += pv[q4].y;
+                            v[4 * q4 + 2] += pv[q4].z;
+                            v[4 * q4 + 3] += pv[q4].w;
+                        }
                     }
                 }
                 epilogue_chunk<EPI>(v, n, N, ci * 16, M, y, amax, lane, warp_q, n_tile, id_off);
@@ -860,6 +869,9 @@ gemm_cl_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
                     mbar_remote_arrive(mapa_shared(smem_u32(pfree), et));
             }
         }
+        // no CTA leaves while a peer may still read its buffer: wait until every peer is done
+        // with the last tile's (every remote access to this CTA's shared memory precedes it)
+        if (C > 1 && my_tiles > 0 && et == 0) mbar_wait_cluster(pfree, (my_tiles - 1) & 1, err, 453);
         tc_fence_before();
     }
     __syncwarp();
@@ -868,7 +880,6 @@ gemm_cl_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         tc_fence_after();
         tmem_dealloc(tmem, Cfg::kTmemCols);
     }
-    cluster_sync_all();  // no CTA leaves while a peer may still read its shared memory
 }
 
 int num_sms() {
