@@ -889,11 +889,13 @@ DecodePlan plan_decode(int B, int max_seq_len, int hq, int hkv) {
     const int max_pages_seq = std::max(1, (max_seq_len + kPage - 1) / kPage);
     const int n_hg = hkv / decode_heads_per_cta(hkv);
     // Two CTAs per SM (96 KB ring each): split each request's pages into chunks so that
-    // (chunk, head group, request) gives about four waves of CTAs, chunks of at least 16 pages
-    // (so the pipeline fill is amortised) and at most kMaxChunkPages.
+    // (chunk, head group, request) gives about one wave of CTAs (measured at batch 128,
+    // context 2048: 1 wave 101.6 us, 2 waves 109, 4 waves 112, 8 waves 115 -- fewer, longer
+    // chunks amortise the pipeline fill and the merge), chunks of at least 16 pages and at most
+    // kMaxChunkPages.
     const int slots = 2 * 148;
     const long long rows = static_cast<long long>(std::max(1, B)) * n_hg;
-    int chunks = static_cast<int>(std::min<long long>((4LL * slots + rows - 1) / rows, 1 << 20));
+    int chunks = static_cast<int>(std::min<long long>((slots + rows - 1) / rows, 1 << 20));
     chunks = std::max(1, std::min(chunks, (max_pages_seq + 15) / 16));
     chunks = std::max(chunks, (max_pages_seq + kMaxChunkPages - 1) / kMaxChunkPages);
     p.chunk_pages = (max_pages_seq + chunks - 1) / chunks;
