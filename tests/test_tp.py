@@ -221,28 +221,29 @@ def _p2p_worker(rank, world, port, mode, q):
         dist.destroy_process_group()
 
 
-def _run_p2p(mode):
+def _run_p2p(mode, world=2):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_p2p_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    procs = [ctx.Process(target=_p2p_worker, args=(r, world, port, mode, q)) for r in range(world)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=300) for _ in range(2))
+    res = dict(q.get(timeout=300) for _ in range(world))
     for p in procs:
         p.join(timeout=120)
     return res
 
 
 @pytest.mark.gpu
-def test_fused_p2p_allreduce_add_rmsnorm_2gpu():
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_fused_p2p_allreduce_add_rmsnorm(world):
     """One-kernel all-reduce + add + RMSNorm over peer memory vs an fp32 reference (residual
-    bit-exact: same additions in the same order), identical bits on both ranks, 4 calls in a
+    bit-exact: same additions in the same order), identical bits on every rank, 4 calls in a
     row (epoch flags)."""
-    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
-    res = _run_p2p("parity")
-    assert res[0][0] == "ok" and res[1][0] == "ok", res
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    res = _run_p2p("parity", world)
+    assert all(res[r][0] == "ok" for r in range(world)), res
 
 
 @pytest.mark.gpu
