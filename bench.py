@@ -82,10 +82,11 @@ def decode_batch_host(pt, vocab, seed=1):
 
 
 # ------------------------------------------------------------------------------ clocks
-# DRAM bytes (read + write) of one paged_decode_kernel launch at this workload, from the ncu
-# capture summarised in profiles/paged_decode_b128_ctx2048_hkv8.md (548.2 MB read + 13.4 MB
-# written; the algorithmic unique K+V bytes are 541.1 MB).
-PAGED_DECODE_TRAFFIC_BYTES = 561_577_984
+# DRAM bytes (read + write) of one paged_decode_cascade_kernel launch at this workload (8 kv
+# heads), from the ncu capture summarised in
+# profiles/paged_decode_cascade_b128_ctx2048_prefix1024_hkv8.md (547 404 544 B read + 11 156 224 B
+# written; the algorithmic unique K+V bytes are 541 065 216 B).
+PAGED_DECODE_TRAFFIC_BYTES = 558_560_768
 
 
 class ClockSampler:
@@ -433,7 +434,8 @@ def run_case(args):
     """Small single-kernel cases at the bench's shapes, for profiling (one layer, < 1 GB):
     `attention` / `attention_cascade`: paged decode attention (plain / cascade over the shared
     prefix), 128 requests x 2048 context (shared 1024 prefix);
-    `gemm`: the gate_up + SwiGLU projection of one layer at 128 tokens (201 MB of weights)."""
+    `gemm`: the gate_up + SwiGLU projection of one layer at 128 tokens (201 MB of weights);
+    `gemm_qkv`: the qkv projection at 128 tokens; `gemm_prefill`: gate_up + SwiGLU at 2048 tokens."""
     import torch
 
     import msgl
@@ -466,6 +468,12 @@ def run_case(args):
         w = ops.fill_normal_(torch.empty(2 * I, H, dtype=torch.bfloat16, device=dev), seed=7,
                              std=0.02)
         ws = ops.gemm_workspace(BATCH, 2 * I, H, dev)
+        run = lambda: ops.gate_up_silu(x, w, workspace=ws)
+    elif args.case == "gemm_prefill":  # gate_up + SwiGLU of one layer at 2048 prefill tokens
+        x = ops.fill_normal_(torch.empty(2048, H, dtype=torch.bfloat16, device=dev), seed=6)
+        w = ops.fill_normal_(torch.empty(2 * I, H, dtype=torch.bfloat16, device=dev), seed=7,
+                             std=0.02)
+        ws = ops.gemm_workspace(2048, 2 * I, H, dev)
         run = lambda: ops.gate_up_silu(x, w, workspace=ws)
     else:  # gemm_qkv: the qkv projection, a small-N (stream-K) GEMM
         n = (hq + 2 * hkv) * 128
@@ -556,10 +564,26 @@ def run_breakdown(args, dev):
     r = torch.zeros(BATCH, H, dtype=torch.float32, device=dev)
     nw = torch.ones(H, dtype=torch.bfloat16, device=dev)
     timed("add_rmsnorm", [lambda: ops.add_rmsnorm_(x, r, nw, 1e-6)], BATCH * H * 12)
-    peak = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))).get("hbm_gbs", 6650.0) \
-        if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else 6650.0
+    peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) \
+        if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+    peak = peaks.get("hbm_gbs", 6650.0)
     for v in res.values():
         v["frac_hbm"] = round(v["GB/s"] / peak, 3)
+    # prefill-sized projections (2048 tokens): tensor-bound, reported against the bf16 peak
+    tpeak = peaks.get("bf16_tflops", 1590.0)
+    mp = 2048
+    xp = ops.fill_normal_(torch.empty(mp, H, dtype=torch.bfloat16, device=dev), seed=30)
+    for name, (n, kind) in {"prefill_qkv_m2048": ((hq + 2 * hkv) * 128, "bf16"),
+                            "prefill_gate_up_silu_m2048": (2 * I, "silu")}.items():
+        w = ops.fill_normal_(torch.empty(n, H, dtype=torch.bfloat16, device=dev), seed=31, std=0.02)
+        gws = ops.gemm_workspace(mp, n, H, dev)
+        f = (lambda: ops.gate_up_silu(xp, w, workspace=gws)) if kind == "silu" else \
+            (lambda: ops.linear(xp, w, workspace=gws))
+        timed(name, [f], n * H * 2 + mp * H * 2)
+        us = res[name]["us"]
+        res[name]["TFLOP/s"] = round(2.0 * mp * n * H / (us * 1e-6) / 1e12, 1)
+        res[name]["frac_tensor"] = round(res[name]["TFLOP/s"] / tpeak, 3)
+        del w
     print(json.dumps({"case": "breakdown", "kernels": res}), flush=True)
     return 0
 
@@ -571,7 +595,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--case", choices=["attention", "attention_cascade", "gemm", "gemm_qkv",
-                                       "breakdown"], default=None,
+                                       "gemm_prefill", "breakdown"], default=None,
                     help="run one kernel of the step on a small single-layer case (profiling)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
