@@ -540,6 +540,38 @@ def run_breakdown(args, dev):
             fns = [lambda w=w: ops.linear(inp, w, workspace=gws) for w in ws]
         timed(name, fns, n * k * 2)
         del ws
+    # the same projections as split-K partials (the decode step's path at tensor parallel size 1)
+    for name, (n, k, inp) in {"qkv_partials": ((hq + 2 * hkv) * 128, H, x),
+                              "o_proj_partials": (H, hq * 128, attn_in),
+                              "down_partials": (H, I, act)}.items():
+        copies = max(1, -(-400_000_000 // (n * k * 2)))
+        ws = [ops.fill_normal_(torch.empty(n, k, dtype=torch.bfloat16, device=dev), seed=10 + i,
+                               std=0.02) for i in range(copies)]
+        S = ops.gemm_partials_splits(BATCH, n, k)
+        pbuf = torch.empty(S, BATCH, n, dtype=torch.float32, device=dev)
+        timed(name, [lambda w=w: ops.linear_partials(inp, w, S, out=pbuf) for w in ws], n * k * 2)
+        res[name]["splits"] = S
+        del ws
+    S = ops.gemm_partials_splits(BATCH, H, H)
+    pn = torch.randn(S * BATCH * H, dtype=torch.float32, device=dev)
+    rr = torch.zeros(BATCH, H, dtype=torch.float32, device=dev)
+    nw = torch.ones(H, dtype=torch.bfloat16, device=dev)
+    timed("add_partials_rmsnorm", [lambda: ops.add_partials_rmsnorm_(pn, x, rr, nw, 1e-6)],
+          BATCH * H * (4 * S + 10))
+    nq = (hq + 2 * hkv) * 128
+    Sq = ops.gemm_partials_splits(BATCH, nq, H)
+    qkv_b = ops.fill_normal_(torch.empty(BATCH, nq, dtype=torch.bfloat16, device=dev), seed=22)
+    qkv_p = torch.randn(Sq * BATCH * nq, dtype=torch.float32, device=dev)
+    kpool = torch.zeros(BATCH * 16, hkv * 128, dtype=torch.bfloat16, device=dev)
+    vpool = torch.zeros_like(kpool)
+    pos = torch.arange(BATCH, dtype=torch.int32, device=dev)
+    cs = torch.randn(BATCH * 128, dtype=torch.float32, device=dev)
+    qnw = torch.ones(128, dtype=torch.bfloat16, device=dev)
+    timed("qknorm_rope", [lambda: ops.qknorm_rope_store_kv(qkv_b, kpool, vpool, pos, pos, cs, qnw,
+                                                           qnw, hq, hkv, 1e-6)], BATCH * nq * 4)
+    timed("qknorm_rope_partials", [lambda: ops.qknorm_rope_store_kv_partials(
+        qkv_p, kpool, vpool, pos, pos, cs, qnw, qnw, hq, hkv, 1e-6)], BATCH * nq * (4 * Sq + 2))
+    del qkv_p, pn
     wl = ops.fill_normal_(torch.empty(V, H, dtype=torch.bfloat16, device=dev), seed=20, std=0.02)
     lws = ops.gemm_workspace(BATCH, V, H, dev)
     timed("lm_head_argmax", [lambda: ops.lm_head_argmax(x, wl, workspace=lws)], V * H * 2)

@@ -93,6 +93,14 @@ MSGL_API int msgl_launch_store_kv_page(const void* k, const void* v, void* k_cac
 MSGL_API int msgl_add_rmsnorm(void* x, float* residual, const void* weight, int num_tokens, int hidden,
                      float eps, int first, msgl_stream_t stream);
 
+/* forward_fused_add (layer.cpp:79-112) whose input is the sum of fp32 split-K partials
+ * parts [nparts][num_tokens][hidden] (msgl_gemm_bf16_partials): residual += sum_p parts[p]
+ * (added in p order); x_out = rmsnorm(residual) * weight (bf16). 1 <= nparts <= 64; parts
+ * 16-byte aligned. */
+MSGL_API int msgl_add_partials_rmsnorm(const float* parts, int nparts, void* x_out, float* residual,
+                                       const void* weight, int num_tokens, int hidden, float eps,
+                                       msgl_stream_t stream);
+
 /* Embedding::forward (layer.cpp:15-42) fused with the first layer's input norm:
  * residual = embed[ids]; x = rmsnorm(residual) * w. Out-of-range ids give zero rows. */
 MSGL_API int msgl_embed_rmsnorm(const void* embed, const int* ids, int num_tokens, int vocab, int hidden,
@@ -112,6 +120,15 @@ MSGL_API int msgl_qknorm_rope_store_kv(const void* qkv, void* q_out, void* k_poo
                               const float* cos_sin_cache, const void* q_norm_w,
                               const void* k_norm_w, int num_tokens, int num_q_heads,
                               int num_kv_heads, int head_dim, float eps, msgl_stream_t stream);
+/* The same, with the QKV row the sum (in p order) of fp32 split-K partials
+ * parts [nparts][T][(Hq + 2 Hkv) D] of the QKV projection (msgl_gemm_bf16_partials). */
+MSGL_API int msgl_qknorm_rope_store_kv_partials(const float* parts, int nparts, void* q_out,
+                                                void* k_pool, void* v_pool, int64_t num_slots,
+                                                const int* positions, const int* slot_mapping,
+                                                const float* cos_sin_cache, const void* q_norm_w,
+                                                const void* k_norm_w, int num_tokens,
+                                                int num_q_heads, int num_kv_heads, int head_dim,
+                                                float eps, msgl_stream_t stream);
 
 /* ---------------------------------------------------------------- paged attention */
 /* Replaces Attention::forward (src/layer/layer.cpp:214-262) with attention over the paged KV
@@ -196,6 +213,16 @@ MSGL_API int msgl_pack_gate_up(const void* w_gate_up, void* w_packed, int inter,
                       msgl_stream_t stream);
 MSGL_API int msgl_gemm_gate_up_silu(const void* x, const void* w_packed, void* y, int M, int inter, int K,
                            void* workspace, size_t workspace_bytes, msgl_stream_t stream);
+
+/* Linear::forward (layer.cpp:122-143) as split-K partials for decode-sized batches whose next
+ * kernel adds them (msgl_add_partials_rmsnorm, msgl_qknorm_rope_store_kv_partials):
+ * parts[s][M][N] (fp32) = x[:, Ks] W[:, Ks]^T over the s-th of `splits` equal k-block ranges, so
+ * that sum_s parts[s] = x W^T. No cross-CTA reduction, no workspace. 1 <= M <= 128,
+ * 1 <= splits <= min(64, ceil(K / 64)); msgl_gemm_partials_splits gives the split count that
+ * fills the GPU in one wave (0 for unsupported sizes). */
+MSGL_API int msgl_gemm_partials_splits(int M, int N, int K);
+MSGL_API int msgl_gemm_bf16_partials(const void* x, const void* w, float* parts, int M, int N, int K,
+                                     int splits, msgl_stream_t stream);
 
 /* lm_head (qwen3.cpp:178) fused with greedy sampling (scheduler.cpp:117-124): ids[m] = argmax_n
  * of the fp32 logits x[m] . W[n]; ties to the lowest id. `packed` is [M] uint64 scratch. */

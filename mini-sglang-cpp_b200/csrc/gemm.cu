@@ -882,6 +882,148 @@ gemm_cl_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     }
 }
 
+// ============================================================================ split-K partials
+// Decode-sized GEMMs (M <= 128 tokens) whose consumer can take the K-split reduction over: CTA
+// blockIdx.x = tile * S + s accumulates k-blocks [s KB / S, (s + 1) KB / S) of weight rows
+// [tile * 128, tile * 128 + 128) in TMEM and stores the fp32 partial tile into
+// parts[s][M][N] (row-major per split: token m, column n). No CTA waits for another: the
+// kernel ends when the slowest CTA has stored its tile, and the next kernel on the stream (fused
+// add + RMSNorm, QK-norm + RoPE) adds the S partials in split order (deterministic). Producer
+// warp, MMA warp and 8 epilogue warps as in the stream-K kernel; one tile per CTA, so the
+// accumulator is single-buffered and the ring is as deep as the shared-memory budget allows.
+template <int BN>
+struct PartCfg {
+    static constexpr int kTileB = BN * kBK * 2;
+    static constexpr int kStageBytes = kTileA + kTileB;
+    static constexpr int kStages = kRingBudget / kStageBytes > 8 ? 8 : kRingBudget / kStageBytes;
+    static constexpr int kTmemCols = BN < 32 ? 32 : BN;
+    static constexpr size_t kSmem = static_cast<size_t>(kStages) * kStageBytes + 1024 + 256;
+};
+
+template <int BN>
+__global__ void __launch_bounds__(kSkThreads, 1)
+gemm_part_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+                 float* __restrict__ parts, int M, int N, int K, int S, int* err) {
+    using Cfg = PartCfg<BN>;
+    constexpr int ST = Cfg::kStages;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;                // [ST] weight tiles
+    uint8_t* sB = smem + ST * kTileA;  // [ST] activation tiles
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + ST * Cfg::kStageBytes);
+    uint64_t* empty = full + ST;
+    uint64_t* tfull = empty + ST;  // accumulator ready
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tile = blockIdx.x / S, sp = blockIdx.x % S;
+    const int KB = (K + kBK - 1) / kBK;
+    const int kb0 = sp * KB / S, kb1 = (sp + 1) * KB / S;  // S <= KB: never empty
+    const int wrow = tile * kBM;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < ST; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(tfull, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, Cfg::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            tma_prefetch_desc(&tmap_w);
+            tma_prefetch_desc(&tmap_x);
+            const uint64_t pol_w = policy_evict_first();
+            const uint64_t pol_x = policy_evict_last();
+            constexpr uint32_t kKbBytes = kTileA + Cfg::kTileB;
+            // weight tiles of the first ST stages before the dependency wait (see gemm_sk_kernel)
+            const int npre = min(ST, kb1 - kb0);
+            for (int i = 0; i < npre; ++i) {
+                mbar_arrive_expect_tx(&full[i], kKbBytes);
+                tma_load_2d_hint(sA + i * kTileA, &tmap_w, &full[i], (kb0 + i) * kBK, wrow, pol_w);
+            }
+            pdl_wait();
+            pdl_trigger();
+            for (int kb = kb0, i = 0; kb < kb1; ++kb, ++i) {
+                const int s = i % ST;
+                if (i >= npre) {
+                    if (!mbar_wait(&empty[s], ((i / ST) - 1) & 1, err, 470)) break;
+                    mbar_arrive_expect_tx(&full[s], kKbBytes);
+                    tma_load_2d_hint(sA + s * kTileA, &tmap_w, &full[s], kb * kBK, wrow, pol_w);
+                }
+                tma_load_2d_hint(sB + s * Cfg::kTileB, &tmap_x, &full[s], kb * kBK, 0, pol_x);
+            }
+        } else {
+            pdl_wait();
+            pdl_trigger();
+        }
+    } else if (warp == 1) {
+        pdl_wait();
+        pdl_trigger();
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_bf16(kBM, BN);
+            bool ok = true;
+            for (int kb = kb0, i = 0; kb < kb1; ++kb, ++i) {
+                const int s = i % ST;
+                if (!mbar_wait(&full[s], (i / ST) & 1, err, 471)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t a_addr = smem_u32(sA + s * kTileA);
+                const uint32_t b_addr = smem_u32(sB + s * Cfg::kTileB);
+#pragma unroll
+                for (int k = 0; k < kBK / 16; ++k)
+                    umma_bf16(tmem, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32),
+                              idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+                umma_commit(&empty[s]);
+            }
+            if (ok) umma_commit(tfull);
+        }
+    } else {
+        // ---------------- epilogue warps 2..9: warp w reads TMEM lane quarter w % 4 (32 weight
+        // rows) and every other 16-column chunk (16 tokens); a warp's store of one token covers
+        // 32 consecutive columns n (128 B)
+        pdl_wait();
+        pdl_trigger();
+        const int warp_q = warp & 3;
+        const int eg = (warp - 2) >> 2;
+        const int row = warp_q * 32 + lane;
+        const int n = wrow + row;
+        const bool have = mbar_wait(tfull, 0, err, 472);
+        tc_fence_after();
+        const uint32_t taddr = tmem + (static_cast<uint32_t>(warp_q * 32) << 16);
+        float* dst = parts + static_cast<int64_t>(sp) * M * N + n;
+#pragma unroll 1
+        for (int c0 = eg * 16; c0 < BN && c0 < M; c0 += 32) {
+            uint32_t r[16];
+            tmem_ld16(taddr + c0, r);
+            tmem_ld_wait();
+            if (n < N) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (c0 + j < M)
+                        dst[static_cast<int64_t>(c0 + j) * N] = have ? __uint_as_float(r[j]) : 0.f;
+            }
+        }
+        tc_fence_before();
+    }
+    // lane 0 of warps 0 and 1 ran their loops alone: reconverge before the block barrier
+    __syncwarp();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, Cfg::kTmemCols);
+    }
+}
+
 int num_sms() {
     static int n[64] = {0};
     int dev = 0;
@@ -1069,6 +1211,29 @@ int launch_cl(const CUtensorMap& tw, const CUtensorMap& tx, void* y, unsigned lo
     if (nc <= 0 || cost * 5 > balanced * 6) return -1;
     cudaError_t e = launch_cl_raw<BN, EPI>(tw, tx, y, amax, M, N, K, C, nc, id_off, err, stream);
     if (e != cudaSuccess) return set_error(MSGL_ERR_CUDA, cudaGetErrorString(e));
+    return MSGL_OK;
+}
+
+// Split count of the partials kernel: as many splits as keep one tile-split per SM in a single
+// wave, at least 4 k-blocks per split, at most 16 partials for the consumer to add.
+int part_splits(int N, int K) {
+    const int T = (N + kBM - 1) / kBM, KB = (K + kBK - 1) / kBK, sms = num_sms();
+    if (T >= sms) return 1;
+    return std::max(1, std::min({sms / T, std::max(1, KB / 4), 16}));
+}
+
+template <int BN>
+int launch_part(const CUtensorMap& tw, const CUtensorMap& tx, float* parts, int M, int N, int K,
+                int S, cudaStream_t stream) {
+    using Cfg = PartCfg<BN>;
+    int* err = device_error_word();
+    if (!err) return set_error(MSGL_ERR_CUDA, "device error word unavailable");
+    cudaFuncSetAttribute(gemm_part_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(Cfg::kSmem));
+    const int T = (N + kBM - 1) / kBM;
+    launch_pdl(gemm_part_kernel<BN>, dim3(T * S), dim3(kSkThreads), Cfg::kSmem, stream, tw, tx,
+               parts, M, N, K, S, err);
+    MSGL_LAUNCH_CHECK();
     return MSGL_OK;
 }
 
@@ -1278,6 +1443,35 @@ int msgl_gemm_gate_up_silu(const void* x, const void* w_packed, void* y, int M, 
     if (inter <= 0 || inter % 16) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "gate_up: inter % 16");
     return run_gemm<EPI_SWIGLU>(x, w_packed, y, nullptr, M, 2 * inter, K, workspace,
                                 workspace_bytes, stream);
+}
+
+int msgl_gemm_partials_splits(int M, int N, int K) {
+    if (M <= 0 || M > 128 || N <= 0 || K <= 0) return 0;
+    return part_splits(N, K);
+}
+
+int msgl_gemm_bf16_partials(const void* x, const void* w, float* parts, int M, int N, int K,
+                            int splits, msgl_stream_t stream) {
+    if (M < 0 || N <= 0 || K <= 0 || !x || !w || !parts)
+        return set_error(MSGL_ERR_INVALID_ARG, "gemm_partials: bad arguments");
+    if (M > 128) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "gemm_partials: M must be <= 128");
+    if (K % 8) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "gemm_partials: K must be a multiple of 8");
+    const int KB = (K + kBK - 1) / kBK;
+    if (splits < 1 || splits > KB || splits > 64)
+        return set_error(MSGL_ERR_INVALID_ARG, "gemm_partials: splits must be in [1, min(64, K / 64)]");
+    if (M == 0) return MSGL_OK;
+    const int bn = pick_bn(M);
+    CUtensorMap tw, tx;
+    int rc = make_tmap_2d_bf16(&tw, w, K, N, static_cast<uint64_t>(K) * 2, kBK, kBM, true);
+    if (rc) return rc;
+    rc = make_tmap_2d_bf16(&tx, x, K, M, static_cast<uint64_t>(K) * 2, kBK, bn, true);
+    if (rc) return rc;
+    switch (bn) {
+        case 16: return launch_part<16>(tw, tx, parts, M, N, K, splits, stream);
+        case 32: return launch_part<32>(tw, tx, parts, M, N, K, splits, stream);
+        case 64: return launch_part<64>(tw, tx, parts, M, N, K, splits, stream);
+        default: return launch_part<128>(tw, tx, parts, M, N, K, splits, stream);
+    }
 }
 
 size_t msgl_grouped_gemm_workspace_size(int max_rows, int num_experts) {

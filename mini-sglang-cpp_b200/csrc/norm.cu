@@ -49,11 +49,13 @@ __device__ __forceinline__ void store8(float* p, const float (&v)[8]) {
 // MODE 1: r += x; x = rmsnorm(r)                (x bf16 in/out, r fp32 in/out)
 // MODE 2: r = x;  x = rmsnorm(x)                (first fused call)
 // MODE 3: r = E[id]; x = rmsnorm(r)             (embedding + first norm; x = E (bf16) rows)
+// MODE 4: r += sum_p P[p]; x = rmsnorm(r)       (P: fp32 split-K partials [nparts][rows][hidden]
+//                                                added in p order, then the residual, as MODE 1)
 template <typename T, int MODE, int VPT>
 __global__ void __launch_bounds__(kNormThreads)
 rmsnorm_kernel(const T* x_in, T* x_out, float* __restrict__ resid,
                const T* __restrict__ w, const int* __restrict__ ids, int vocab, int hidden,
-               float eps) {
+               float eps, const float* __restrict__ parts, int nparts, int64_t part_stride) {
     __shared__ float red[4];
     pdl_wait();
     pdl_trigger();
@@ -72,12 +74,23 @@ rmsnorm_kernel(const T* x_in, T* x_out, float* __restrict__ resid,
     for (int i = 0; i < VPT; ++i) {
         int vi = threadIdx.x + i * kNormThreads;
         if (vi < nvec) {
-            load8(src + vi * 8, v[i]);
+            if (MODE == 4) {
+                const float* pp = parts + static_cast<int64_t>(row) * hidden + vi * 8;
+                load8(pp, v[i]);
+                for (int p = 1; p < nparts; ++p) {
+                    float t[8];
+                    load8(pp + p * part_stride, t);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) v[i][j] += t[j];
+                }
+            } else {
+                load8(src + vi * 8, v[i]);
+            }
             if (MODE == 3 && zero_row) {
 #pragma unroll
                 for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
             }
-            if (MODE == 1) {
+            if (MODE == 1 || MODE == 4) {
                 float r[8];
                 load8(resid + static_cast<int64_t>(row) * hidden + vi * 8, r);
 #pragma unroll
@@ -106,19 +119,22 @@ rmsnorm_kernel(const T* x_in, T* x_out, float* __restrict__ resid,
 
 template <typename T, int MODE>
 int launch_norm(const T* x_in, T* x_out, float* resid, const T* w, const int* ids, int vocab,
-                int num_tokens, int hidden, float eps, cudaStream_t stream) {
+                int num_tokens, int hidden, float eps, cudaStream_t stream,
+                const float* parts = nullptr, int nparts = 0) {
     if (num_tokens < 0 || hidden <= 0 || hidden % 8 != 0 || hidden > 8 * 8 * kNormThreads)
         return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "rmsnorm: hidden must be a multiple of 8, <= 8192");
     if (num_tokens == 0) return MSGL_OK;
     if ((reinterpret_cast<uintptr_t>(x_in) | reinterpret_cast<uintptr_t>(x_out) |
-         reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(resid)) & 15)
+         reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(resid) |
+         reinterpret_cast<uintptr_t>(parts)) & 15)
         return set_error(MSGL_ERR_INVALID_ARG, "rmsnorm: pointers must be 16-byte aligned");
     int vpt = (hidden / 8 + kNormThreads - 1) / kNormThreads;
     dim3 grid(num_tokens), block(kNormThreads);
 #define MSGL_NORM_CASE(N)                                                                   \
     case N:                                                                                 \
         launch_pdl(rmsnorm_kernel<T, MODE, N>, grid, block, 0, stream, x_in, x_out, resid, w, \
-                   ids, vocab, hidden, eps);                                                \
+                   ids, vocab, hidden, eps, parts, nparts,                                  \
+                   static_cast<int64_t>(num_tokens) * hidden);                              \
         break;
     switch (vpt) {
         MSGL_NORM_CASE(1) MSGL_NORM_CASE(2) MSGL_NORM_CASE(3) MSGL_NORM_CASE(4)
@@ -175,6 +191,18 @@ int msgl_add_rmsnorm(void* x, float* residual, const void* weight, int num_token
                                              eps, stream);
     return launch_norm<__nv_bfloat16, 1>(xb, xb, residual, wb, nullptr, 0, num_tokens, hidden, eps,
                                          stream);
+}
+
+int msgl_add_partials_rmsnorm(const float* parts, int nparts, void* x_out, float* residual,
+                              const void* weight, int num_tokens, int hidden, float eps,
+                              msgl_stream_t stream) {
+    if (!parts || !x_out || !residual || !weight)
+        return set_error(MSGL_ERR_INVALID_ARG, "add_partials_rmsnorm: null");
+    if (nparts < 1 || nparts > 64)
+        return set_error(MSGL_ERR_INVALID_ARG, "add_partials_rmsnorm: nparts must be in [1, 64]");
+    auto* xb = static_cast<__nv_bfloat16*>(x_out);
+    return launch_norm<__nv_bfloat16, 4>(xb, xb, residual, static_cast<const __nv_bfloat16*>(weight),
+                                         nullptr, 0, num_tokens, hidden, eps, stream, parts, nparts);
 }
 
 int msgl_embed_rmsnorm(const void* embed, const int* ids, int num_tokens, int vocab, int hidden,

@@ -66,10 +66,14 @@ __global__ void store_kv_page_kernel(const T* __restrict__ k, const T* __restric
 
 // One warp per (token, head) of the fused QKV row; head_dim 128: lane l owns elements
 // {2l, 2l+1} of the first half and {64+2l, 64+2l+1} of the second (the rotate-half partners).
+// PARTS: the row is the sum, in split order, of `nparts` fp32 split-K partials of the QKV
+// projection ([nparts][T][(Hq + 2 Hkv) D]) instead of one bf16 row.
 constexpr int kQkvWarps = 8;
 
+template <bool PARTS>
 __global__ void __launch_bounds__(kQkvWarps * 32)
-qknorm_rope_store_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ q_out,
+qknorm_rope_store_kernel(const __nv_bfloat16* __restrict__ qkv, const float* __restrict__ parts,
+                         int nparts, __nv_bfloat16* __restrict__ q_out,
                          __nv_bfloat16* __restrict__ k_pool, __nv_bfloat16* __restrict__ v_pool,
                          int64_t num_slots, const int* __restrict__ positions,
                          const int* __restrict__ slots, const float* __restrict__ cs_table,
@@ -83,10 +87,24 @@ qknorm_rope_store_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* _
     if (wid >= static_cast<int64_t>(num_tokens) * nh) return;
     const int t = static_cast<int>(wid / nh);
     const int h = static_cast<int>(wid % nh);
-    const __nv_bfloat16* src = qkv + wid * 128;
-    uint32_t ua = *reinterpret_cast<const uint32_t*>(src + 2 * lane);
-    uint32_t ub = *reinterpret_cast<const uint32_t*>(src + 64 + 2 * lane);
-    float a0 = bf16lo(ua), a1 = bf16hi(ua), b0 = bf16lo(ub), b1 = bf16hi(ub);
+    float a0, a1, b0, b1;
+    if (PARTS) {
+        const int64_t stride = static_cast<int64_t>(num_tokens) * nh * 128;
+        const float* src = parts + wid * 128;
+        float2 pa = *reinterpret_cast<const float2*>(src + 2 * lane);
+        float2 pb = *reinterpret_cast<const float2*>(src + 64 + 2 * lane);
+        for (int p = 1; p < nparts; ++p) {
+            const float2 ta = *reinterpret_cast<const float2*>(src + p * stride + 2 * lane);
+            const float2 tb = *reinterpret_cast<const float2*>(src + p * stride + 64 + 2 * lane);
+            pa.x += ta.x; pa.y += ta.y; pb.x += tb.x; pb.y += tb.y;
+        }
+        a0 = pa.x; a1 = pa.y; b0 = pb.x; b1 = pb.y;
+    } else {
+        const __nv_bfloat16* src = qkv + wid * 128;
+        uint32_t ua = *reinterpret_cast<const uint32_t*>(src + 2 * lane);
+        uint32_t ub = *reinterpret_cast<const uint32_t*>(src + 64 + 2 * lane);
+        a0 = bf16lo(ua); a1 = bf16hi(ua); b0 = bf16lo(ub); b1 = bf16hi(ub);
+    }
 
     __nv_bfloat16* dst;
     if (h < hq + hkv) {
@@ -190,11 +208,12 @@ int msgl_launch_store_kv_page(const void* k, const void* v, void* k_cache, void*
     return MSGL_OK;
 }
 
-int msgl_qknorm_rope_store_kv(const void* qkv, void* q_out, void* k_pool, void* v_pool,
-                              int64_t num_slots, const int* positions, const int* slot_mapping,
-                              const float* cos_sin_cache, const void* q_norm_w,
-                              const void* k_norm_w, int num_tokens, int num_q_heads,
-                              int num_kv_heads, int head_dim, float eps, msgl_stream_t stream) {
+static int launch_qknorm_rope(const void* qkv, const float* parts, int nparts, void* q_out,
+                              void* k_pool, void* v_pool, int64_t num_slots, const int* positions,
+                              const int* slot_mapping, const float* cos_sin_cache,
+                              const void* q_norm_w, const void* k_norm_w, int num_tokens,
+                              int num_q_heads, int num_kv_heads, int head_dim, float eps,
+                              msgl_stream_t stream) {
     if (head_dim != 128) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "qknorm_rope: head_dim != 128");
     if (num_tokens < 0 || num_q_heads <= 0 || num_kv_heads <= 0)
         return set_error(MSGL_ERR_INVALID_ARG, "qknorm_rope: bad sizes");
@@ -203,14 +222,41 @@ int msgl_qknorm_rope_store_kv(const void* qkv, void* q_out, void* k_pool, void* 
     if (!err) return set_error(MSGL_ERR_CUDA, "device error word unavailable");
     int64_t warps = static_cast<int64_t>(num_tokens) * (num_q_heads + 2 * num_kv_heads);
     int blocks = static_cast<int>((warps + kQkvWarps - 1) / kQkvWarps);
-    launch_pdl(qknorm_rope_store_kernel, dim3(blocks), dim3(kQkvWarps * 32), 0, stream,
-        static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(q_out),
+    auto kern = parts ? qknorm_rope_store_kernel<true> : qknorm_rope_store_kernel<false>;
+    launch_pdl(kern, dim3(blocks), dim3(kQkvWarps * 32), 0, stream,
+        static_cast<const __nv_bfloat16*>(qkv), parts, nparts, static_cast<__nv_bfloat16*>(q_out),
         static_cast<__nv_bfloat16*>(k_pool), static_cast<__nv_bfloat16*>(v_pool), num_slots,
         positions, slot_mapping, cos_sin_cache, static_cast<const __nv_bfloat16*>(q_norm_w),
         static_cast<const __nv_bfloat16*>(k_norm_w), num_tokens, num_q_heads, num_kv_heads, eps,
         err);
     MSGL_LAUNCH_CHECK();
     return MSGL_OK;
+}
+
+int msgl_qknorm_rope_store_kv(const void* qkv, void* q_out, void* k_pool, void* v_pool,
+                              int64_t num_slots, const int* positions, const int* slot_mapping,
+                              const float* cos_sin_cache, const void* q_norm_w,
+                              const void* k_norm_w, int num_tokens, int num_q_heads,
+                              int num_kv_heads, int head_dim, float eps, msgl_stream_t stream) {
+    return launch_qknorm_rope(qkv, nullptr, 0, q_out, k_pool, v_pool, num_slots, positions,
+                              slot_mapping, cos_sin_cache, q_norm_w, k_norm_w, num_tokens,
+                              num_q_heads, num_kv_heads, head_dim, eps, stream);
+}
+
+int msgl_qknorm_rope_store_kv_partials(const float* parts, int nparts, void* q_out, void* k_pool,
+                                       void* v_pool, int64_t num_slots, const int* positions,
+                                       const int* slot_mapping, const float* cos_sin_cache,
+                                       const void* q_norm_w, const void* k_norm_w, int num_tokens,
+                                       int num_q_heads, int num_kv_heads, int head_dim, float eps,
+                                       msgl_stream_t stream) {
+    if (head_dim != 128) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "qknorm_rope: head_dim != 128");
+    if (!parts || nparts < 1 || nparts > 64)
+        return set_error(MSGL_ERR_INVALID_ARG, "qknorm_rope_partials: parts / nparts in [1, 64]");
+    if (reinterpret_cast<uintptr_t>(parts) & 7)
+        return set_error(MSGL_ERR_INVALID_ARG, "qknorm_rope_partials: parts must be 8-byte aligned");
+    return launch_qknorm_rope(nullptr, parts, nparts, q_out, k_pool, v_pool, num_slots, positions,
+                              slot_mapping, cos_sin_cache, q_norm_w, k_norm_w, num_tokens,
+                              num_q_heads, num_kv_heads, head_dim, eps, stream);
 }
 
 }  // extern "C"

@@ -85,6 +85,12 @@ class RMSNorm {  // layer.h:23-34
         ck(msgl_add_rmsnorm(x, residual, weight.p, num_tokens, size_, eps_, first ? 1 : 0, s),
            "RMSNorm::forward_fused_add");
     }
+    // the same with the added input the sum of fp32 split-K partials [nparts][T][size]
+    void forward_fused_add_partials(const float* parts, int nparts, bf16_t* x, float* residual,
+                                    int num_tokens, cudaStream_t s) const {
+        ck(msgl_add_partials_rmsnorm(parts, nparts, x, residual, weight.p, num_tokens, size_, eps_, s),
+           "RMSNorm::forward_fused_add(partials)");
+    }
     DevBuf weight;  // bf16 [size]
     int size() const { return size_; }
     float eps() const { return eps_; }
@@ -103,6 +109,15 @@ class Linear {  // layer.h:36-48; y = x W^T, W [out, in]
         ck(msgl_gemm_bf16(x, weight.p, y, num_tokens, out_, in_, MSGL_BF16, ws.gemm_ws,
                           ws.gemm_ws_bytes, s),
            "Linear::forward");
+    }
+    // Decode-sized batches whose next kernel adds the K split: fp32 partials [S][T][out];
+    // returns S (0: not available for this size, use forward).
+    int partial_splits(int num_tokens) const { return msgl_gemm_partials_splits(num_tokens, out_, in_); }
+    int forward_partials(const bf16_t* x, float* parts, int num_tokens, cudaStream_t s) const {
+        const int S = partial_splits(num_tokens);
+        ck(msgl_gemm_bf16_partials(x, weight.p, parts, num_tokens, out_, in_, S, s),
+           "Linear::forward(partials)");
+        return S;
     }
     size_t workspace(int max_tokens) const { return msgl_gemm_workspace_size(max_tokens, out_, in_); }
     DevBuf weight;  // bf16 [out, in]
@@ -159,6 +174,17 @@ class Attention {
                                      rope.cos_sin_cache.as<float>(), q_norm_w, k_norm_w,
                                      num_tokens, hq_, hkv_, head_dim_, eps_, s),
            "Attention::prepare");
+    }
+    // the same from the QKV projection's fp32 split-K partials [nparts][T][(hq + 2 hkv) D]
+    void prepare_partials(const float* parts, int nparts, bf16_t* q, void* k_pool, void* v_pool,
+                          int64_t num_slots, const int* positions, const int* slot_mapping,
+                          const RotaryEmbedding& rope, const void* q_norm_w, const void* k_norm_w,
+                          int num_tokens, cudaStream_t s) const {
+        ck(msgl_qknorm_rope_store_kv_partials(parts, nparts, q, k_pool, v_pool, num_slots,
+                                              positions, slot_mapping,
+                                              rope.cos_sin_cache.as<float>(), q_norm_w, k_norm_w,
+                                              num_tokens, hq_, hkv_, head_dim_, eps_, s),
+           "Attention::prepare(partials)");
     }
     void forward(const bf16_t* q, const void* k_pool, const void* v_pool, int64_t num_slots,
                  const msgl_batch& b, bf16_t* out, const Scratch& ws, cudaStream_t s) const {

@@ -1,6 +1,7 @@
 // qwen3.cpp -- the device-side Qwen3 executor (Qwen3DecoderLayer / Qwen3ForCausalLM of
 // src/model/qwen3.cpp:16-83, 85-92, 168-180) and its C ABI (include/msgl_engine.h).
 #include <cmath>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <memory>
@@ -59,6 +60,9 @@ struct Model {
 
     // workspace (allocated once)
     DevBuf x, residual, qkv, q, attn_out, act, x_last, res_last, packed, gemm_ws, attn_ws;
+    // fp32 split-K partials of a decode-sized projection, added by the kernel that follows it
+    // (qkv: QK-norm + RoPE; o_proj / down_proj: the fused add + RMSNorm, tensor parallel size 1)
+    DevBuf parts;
     Scratch scratch;
     DevBuf moe_logits, moe_ids, moe_w, moe_off, moe_tok, moe_pos, moe_xs, moe_act, moe_ys, moe_ws;
     MoEScratch moe_scratch;
@@ -194,6 +198,20 @@ static void create(Model& m, const msgl_model_config& c) {
     m.attn_ws.alloc(std::max<size_t>(aws, 256));
     ckc(cudaMemset(m.attn_ws.p, 0, m.attn_ws.bytes), "attention workspace");
     m.scratch = Scratch{m.gemm_ws.p, m.gemm_ws.bytes, m.attn_ws.p, m.attn_ws.bytes};
+    // split-K partials (steps of <= 128 tokens; MSGL_SPLITK_PARTIALS=0 turns the path off)
+    const char* env_parts = std::getenv("MSGL_SPLITK_PARTIALS");
+    if (!(env_parts && env_parts[0] == '0')) {
+        const int tm = static_cast<int>(std::min<size_t>(T, 128));
+        auto need = [&](const Linear& l) {
+            return static_cast<size_t>(l.partial_splits(tm)) * tm * l.out_features() * sizeof(float);
+        };
+        size_t pb = need(L0.qkv_proj);
+        if (tp == 1) {
+            pb = std::max(pb, need(L0.o_proj));
+            if (c.num_experts == 0) pb = std::max(pb, need(L0.down_proj));
+        }
+        if (pb > 0) m.parts.alloc(pb);
+    }
     if (c.num_experts > 0) {
         const size_t E = c.num_experts, k = c.top_k, R = T * k;
         m.moe_logits.alloc(T * E * 4);
@@ -388,26 +406,55 @@ static void forward(Model& m, const msgl_batch& b, int* next_tokens, float* logi
     // (o_proj uses slot 0, down_proj slot 1: consecutive all-reduces alternate slots)
     bf16_t* part_o = m.tp ? m.tp_part[0] : x;
     bf16_t* part_d = m.tp ? m.tp_part[1] : x;
+    // Steps of <= 128 tokens: qkv, o_proj and (dense, tensor parallel size 1) down_proj write
+    // fp32 split-K partials that the next kernel adds, instead of reducing the K split across
+    // CTAs inside the GEMM. `pend` = splits of down_proj partials the next norm has to add.
+    float* parts = m.parts.as<float>();
+    const bool use_parts = parts != nullptr && T <= 128;
+    int pend = 0;
     for (int l = 0; l < nl; ++l) {
         auto& L = m.layers[l];
-        if (l > 0 && !m.tp) L.input_layernorm.forward_fused_add(x, res, T, false, s);  // qwen3.cpp:19
-        L.qkv_proj.forward(x, m.qkv.as<bf16_t>(), T, m.scratch, s);          // :22
-        L.attn.prepare(m.qkv.as<bf16_t>(), m.q.as<bf16_t>(), L.k_pool.p, L.v_pool.p, m.num_slots,
-                       b.positions, b.slot_mapping, m.rope, L.q_norm.p, L.k_norm.p, T, s);  // :28-48
+        if (l > 0 && !m.tp) {  // qwen3.cpp:19
+            if (pend)
+                L.input_layernorm.forward_fused_add_partials(parts, pend, x, res, T, s);
+            else
+                L.input_layernorm.forward_fused_add(x, res, T, false, s);
+            pend = 0;
+        }
+        if (use_parts) {  // :22, :28-48
+            const int S = L.qkv_proj.forward_partials(x, parts, T, s);
+            L.attn.prepare_partials(parts, S, m.q.as<bf16_t>(), L.k_pool.p, L.v_pool.p,
+                                    m.num_slots, b.positions, b.slot_mapping, m.rope, L.q_norm.p,
+                                    L.k_norm.p, T, s);
+        } else {
+            L.qkv_proj.forward(x, m.qkv.as<bf16_t>(), T, m.scratch, s);
+            L.attn.prepare(m.qkv.as<bf16_t>(), m.q.as<bf16_t>(), L.k_pool.p, L.v_pool.p,
+                           m.num_slots, b.positions, b.slot_mapping, m.rope, L.q_norm.p,
+                           L.k_norm.p, T, s);
+        }
         L.attn.forward(m.q.as<bf16_t>(), L.k_pool.p, L.v_pool.p, m.num_slots, b,
                        m.attn_out.as<bf16_t>(), m.scratch, s);                // :51-52
-        L.o_proj.forward(m.attn_out.as<bf16_t>(), part_o, T, m.scratch, s);  // :55
-        if (m.tp)  // row-parallel o_proj: all-reduce fused with the add + norm of :57
+        if (m.tp) {  // row-parallel o_proj (:55): all-reduce fused with the add + norm of :57
+            L.o_proj.forward(m.attn_out.as<bf16_t>(), part_o, T, m.scratch, s);
             ck(msgl_tp_fused_allreduce_add_rmsnorm(m.tp, part_o, x, res,
                                                    L.post_attention_layernorm.weight.p, T, H,
                                                    c.eps, 0, s), "o_proj all-reduce");
-        else
+        } else if (use_parts) {
+            const int S = L.o_proj.forward_partials(m.attn_out.as<bf16_t>(), parts, T, s);
+            L.post_attention_layernorm.forward_fused_add_partials(parts, S, x, res, T, s);
+        } else {
+            L.o_proj.forward(m.attn_out.as<bf16_t>(), part_o, T, m.scratch, s);
             L.post_attention_layernorm.forward_fused_add(x, res, T, false, s);  // :57
+        }
         if (c.num_experts > 0) {
             L.moe.forward(x, part_d, T, m.moe_scratch, m.scratch, s);         // qwen3_moe.cpp:62-111
         } else {
             L.gate_up_proj.forward(x, m.act.as<bf16_t>(), T, m.scratch, s);  // :60-79
-            L.down_proj.forward(m.act.as<bf16_t>(), part_d, T, m.scratch, s);  // :80
+            // (the last layer's down_proj writes x, the hidden state msgl_model_hidden reads)
+            if (use_parts && !m.tp && l + 1 < nl)                             // :80
+                pend = L.down_proj.forward_partials(m.act.as<bf16_t>(), parts, T, s);
+            else
+                L.down_proj.forward(m.act.as<bf16_t>(), part_d, T, m.scratch, s);
         }
         if (m.tp) {  // row-parallel down_proj / expert combine: all-reduce + add + next norm
             const void* next_w = l + 1 < nl ? m.layers[l + 1].input_layernorm.weight.p : m.norm.weight.p;

@@ -35,6 +35,10 @@ SIGNATURES = {
     "msgl_gemm_bf16": (I, [P, P, P, I, I, I, I, P, SZ, P]),
     "msgl_pack_gate_up": (I, [P, P, I, I, P]),
     "msgl_gemm_gate_up_silu": (I, [P, P, P, I, I, I, P, SZ, P]),
+    "msgl_gemm_partials_splits": (I, [I, I, I]),
+    "msgl_gemm_bf16_partials": (I, [P, P, P, I, I, I, I, P]),
+    "msgl_add_partials_rmsnorm": (I, [P, I, P, P, P, I, I, F, P]),
+    "msgl_qknorm_rope_store_kv_partials": (I, [P, I, P, P, P, I64, P, P, P, P, P, I, I, I, I, F, P]),
     "msgl_lm_head_argmax": (I, [P, P, I, I, I, P, P, P, SZ, P]),
     "msgl_argmax": (I, [P, I, I, I, P, P]),
     "msgl_fill_normal_bf16": (I, [P, I64, U64, U64, F, F, P]),

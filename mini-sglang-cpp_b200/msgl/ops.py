@@ -67,6 +67,16 @@ def add_rmsnorm_(x, residual, w, eps, first=False):
     check(lib().msgl_add_rmsnorm(_p(x), _p(residual), _p(w), x.numel() // H, H, eps, int(first), _s()))
 
 
+def add_partials_rmsnorm_(parts, x, residual, w, eps):
+    """residual += sum_p parts[p] (fp32 split-K partials [P, T, H], added in p order);
+    x = rmsnorm(residual) * w (x written in place)."""
+    _c(parts, torch.float32), _c(x, torch.bfloat16), _c(residual, torch.float32), _c(w, torch.bfloat16)
+    H = w.numel()
+    T = x.numel() // H
+    check(lib().msgl_add_partials_rmsnorm(_p(parts), parts.numel() // (T * H), _p(x), _p(residual),
+                                          _p(w), T, H, eps, _s()))
+
+
 def embed_rmsnorm(embed, ids, w, eps):
     _c(embed, torch.bfloat16), _c(ids, torch.int32), _c(w, torch.bfloat16)
     V, H = embed.shape
@@ -86,6 +96,22 @@ def qknorm_rope_store_kv(qkv, k_pool, v_pool, positions, slot_mapping, cos_sin, 
     check(lib().msgl_qknorm_rope_store_kv(_p(qkv), _p(q), _p(k_pool), _p(v_pool), num_slots,
                                           _p(positions), _p(slot_mapping), _p(cos_sin), _p(q_norm),
                                           _p(k_norm), T, num_q_heads, num_kv_heads, head_dim, eps, _s()))
+    return q
+
+
+def qknorm_rope_store_kv_partials(parts, k_pool, v_pool, positions, slot_mapping, cos_sin, q_norm,
+                                  k_norm, num_q_heads, num_kv_heads, eps, head_dim=128):
+    """As qknorm_rope_store_kv with the QKV rows the sum of fp32 partials [P, T, (Hq+2Hkv) D]."""
+    _c(parts, torch.float32), _c(k_pool, torch.bfloat16), _c(v_pool, torch.bfloat16)
+    _c(positions, torch.int32), _c(slot_mapping, torch.int32), _c(cos_sin, torch.float32)
+    T = positions.numel()
+    nparts = parts.numel() // (T * (num_q_heads + 2 * num_kv_heads) * head_dim)
+    q = torch.empty(T, num_q_heads, head_dim, dtype=torch.bfloat16, device=parts.device)
+    num_slots = k_pool.numel() // (num_kv_heads * head_dim)
+    check(lib().msgl_qknorm_rope_store_kv_partials(
+        _p(parts), nparts, _p(q), _p(k_pool), _p(v_pool), num_slots, _p(positions),
+        _p(slot_mapping), _p(cos_sin), _p(q_norm), _p(k_norm), T, num_q_heads, num_kv_heads,
+        head_dim, eps, _s()))
     return q
 
 
@@ -186,6 +212,23 @@ def linear(x, w, out_dtype=torch.bfloat16, workspace=None):
     check(lib().msgl_gemm_bf16(_p(x), _p(w), _p(y), M, N, K, _DT[out_dtype], _p(workspace),
                                workspace.numel(), _s()))
     return y
+
+
+def gemm_partials_splits(M, N, K):
+    return lib().msgl_gemm_partials_splits(M, N, K)
+
+
+def linear_partials(x, w, splits=None, out=None):
+    """fp32 split-K partials [S, M, N] of x W^T (sum over S = x W^T)."""
+    _c(x, torch.bfloat16), _c(w, torch.bfloat16)
+    N, K = w.shape
+    M = x.numel() // K
+    if splits is None:
+        splits = gemm_partials_splits(M, N, K)
+    if out is None:
+        out = torch.empty(splits, M, N, dtype=torch.float32, device=x.device)
+    check(lib().msgl_gemm_bf16_partials(_p(x), _p(w), _p(out), M, N, K, splits, _s()))
+    return out
 
 
 def pack_gate_up(w_gate_up):
