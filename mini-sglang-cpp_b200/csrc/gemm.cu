@@ -883,35 +883,35 @@ gemm_cl_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
 }
 
 // ============================================================================ split-K partials
-// Decode-sized GEMMs (M <= 128 tokens) whose consumer can take the K-split reduction over: CTA
-// blockIdx.x = tile * S + s accumulates k-blocks [s KB / S, (s + 1) KB / S) of weight rows
-// [tile * 128, tile * 128 + 128) in TMEM and stores the fp32 partial tile into
-// parts[s][M][N] (row-major per split: token m, column n). No CTA waits for another: the
-// kernel ends when the slowest CTA has stored its tile, and the next kernel on the stream (fused
+// Decode-sized GEMMs (M <= 128 tokens) whose consumer can take the K-split reduction over. The
+// operands are swapped relative to the other kernels: the tokens are the UMMA M dimension (128,
+// rows past M zero-filled by TMA) and 256 weight rows the N dimension, so a ring stage holds a
+// 16 KB token tile and a 32 KB weight tile -- 1.5 bytes staged per weight byte instead of 2,
+// which is what bounds a decode GEMM when every SM streams weights (per-SM TMA ingest).
+// CTA blockIdx.x = tile * S + s accumulates k-blocks [s KB / S, (s + 1) KB / S) of weight rows
+// [256 tile, 256 tile + 256) in TMEM (lane = token, column = weight row) and stores the fp32
+// partial into parts[s][M][N]. No CTA waits for another; the next kernel on the stream (fused
 // add + RMSNorm, QK-norm + RoPE) adds the S partials in split order (deterministic). Producer
-// warp, MMA warp and 8 epilogue warps as in the stream-K kernel; one tile per CTA, so the
-// accumulator is single-buffered and the ring is as deep as the shared-memory budget allows.
-template <int BN>
-struct PartCfg {
-    static constexpr int kTileB = BN * kBK * 2;
-    static constexpr int kStageBytes = kTileA + kTileB;
-    static constexpr int kStages = kRingBudget / kStageBytes > 8 ? 8 : kRingBudget / kStageBytes;
-    static constexpr int kTmemCols = BN < 32 ? 32 : BN;
-    static constexpr size_t kSmem = static_cast<size_t>(kStages) * kStageBytes + 1024 + 256;
-};
+// warp, MMA warp, 8 epilogue warps as in the stream-K kernel.
+constexpr int kPartBN = 256;                        // weight rows per tile (UMMA N)
+constexpr int kPartTileX = kBM * kBK * 2;           // 16 KB token tile (UMMA A, M = 128)
+constexpr int kPartTileW = kPartBN * kBK * 2;       // 32 KB weight tile (UMMA B)
+constexpr int kPartStage = kPartTileX + kPartTileW;
+constexpr int kPartStages = kRingBudget / kPartStage;  // 4
+constexpr size_t kPartSmem = static_cast<size_t>(kPartStages) * kPartStage + 1024 + 256;
+constexpr int kPartPitch = kPartBN + 4;  // floats per token row of the epilogue staging tile
+static_assert(kBM * kPartPitch * 4 <= kPartStages * kPartStage, "staging tile exceeds the ring");
 
-template <int BN>
 __global__ void __launch_bounds__(kSkThreads, 1)
 gemm_part_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                  float* __restrict__ parts, int M, int N, int K, int S, int* err) {
-    using Cfg = PartCfg<BN>;
-    constexpr int ST = Cfg::kStages;
+    constexpr int ST = kPartStages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sA = smem;                // [ST] weight tiles
-    uint8_t* sB = smem + ST * kTileA;  // [ST] activation tiles
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + ST * Cfg::kStageBytes);
+    uint8_t* sW = smem;                     // [ST] weight tiles (B)
+    uint8_t* sX = smem + ST * kPartTileW;   // [ST] token tiles (A)
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + ST * kPartStage);
     uint64_t* empty = full + ST;
     uint64_t* tfull = empty + ST;  // accumulator ready
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
@@ -920,7 +920,7 @@ gemm_part_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
     const int tile = blockIdx.x / S, sp = blockIdx.x % S;
     const int KB = (K + kBK - 1) / kBK;
     const int kb0 = sp * KB / S, kb1 = (sp + 1) * KB / S;  // S <= KB: never empty
-    const int wrow = tile * kBM;
+    const int wrow = tile * kPartBN;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < ST; ++s) {
@@ -931,7 +931,7 @@ gemm_part_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
         fence_barrier_init();
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, Cfg::kTmemCols);
+        tmem_alloc(tmem_slot, kPartBN);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -945,12 +945,11 @@ gemm_part_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
             tma_prefetch_desc(&tmap_x);
             const uint64_t pol_w = policy_evict_first();
             const uint64_t pol_x = policy_evict_last();
-            constexpr uint32_t kKbBytes = kTileA + Cfg::kTileB;
             // weight tiles of the first ST stages before the dependency wait (see gemm_sk_kernel)
             const int npre = min(ST, kb1 - kb0);
             for (int i = 0; i < npre; ++i) {
-                mbar_arrive_expect_tx(&full[i], kKbBytes);
-                tma_load_2d_hint(sA + i * kTileA, &tmap_w, &full[i], (kb0 + i) * kBK, wrow, pol_w);
+                mbar_arrive_expect_tx(&full[i], kPartStage);
+                tma_load_2d_hint(sW + i * kPartTileW, &tmap_w, &full[i], (kb0 + i) * kBK, wrow, pol_w);
             }
             pdl_wait();
             pdl_trigger();
@@ -958,10 +957,10 @@ gemm_part_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
                 const int s = i % ST;
                 if (i >= npre) {
                     if (!mbar_wait(&empty[s], ((i / ST) - 1) & 1, err, 470)) break;
-                    mbar_arrive_expect_tx(&full[s], kKbBytes);
-                    tma_load_2d_hint(sA + s * kTileA, &tmap_w, &full[s], kb * kBK, wrow, pol_w);
+                    mbar_arrive_expect_tx(&full[s], kPartStage);
+                    tma_load_2d_hint(sW + s * kPartTileW, &tmap_w, &full[s], kb * kBK, wrow, pol_w);
                 }
-                tma_load_2d_hint(sB + s * Cfg::kTileB, &tmap_x, &full[s], kb * kBK, 0, pol_x);
+                tma_load_2d_hint(sX + s * kPartTileX, &tmap_x, &full[s], kb * kBK, 0, pol_x);
             }
         } else {
             pdl_wait();
@@ -971,14 +970,14 @@ gemm_part_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
         pdl_wait();
         pdl_trigger();
         if (lane == 0) {
-            constexpr uint32_t idesc = umma_idesc_bf16(kBM, BN);
+            constexpr uint32_t idesc = umma_idesc_bf16(kBM, kPartBN);
             bool ok = true;
             for (int kb = kb0, i = 0; kb < kb1; ++kb, ++i) {
                 const int s = i % ST;
                 if (!mbar_wait(&full[s], (i / ST) & 1, err, 471)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t a_addr = smem_u32(sA + s * kTileA);
-                const uint32_t b_addr = smem_u32(sB + s * Cfg::kTileB);
+                const uint32_t a_addr = smem_u32(sX + s * kPartTileX);
+                const uint32_t b_addr = smem_u32(sW + s * kPartTileW);
 #pragma unroll
                 for (int k = 0; k < kBK / 16; ++k)
                     umma_bf16(tmem, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32),
@@ -988,39 +987,64 @@ gemm_part_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
             if (ok) umma_commit(tfull);
         }
     } else {
-        // ---------------- epilogue warps 2..9: warp w reads TMEM lane quarter w % 4 (32 weight
-        // rows) and every other 16-column chunk (16 tokens); a warp's store of one token covers
-        // 32 consecutive columns n (128 B)
+        // ---------------- epilogue warps 2..9: warp w reads TMEM lane quarter w % 4 (32 tokens)
+        // and every other 16-column chunk (16 weight rows) into the drained ring, laid out
+        // [token][kPartPitch] (rows padded by 16 B: a warp's 16-byte stores hit distinct banks);
+        // then each warp writes whole token rows to global memory, 512 contiguous bytes per store
         pdl_wait();
         pdl_trigger();
         const int warp_q = warp & 3;
         const int eg = (warp - 2) >> 2;
-        const int row = warp_q * 32 + lane;
-        const int n = wrow + row;
+        const int ew = warp - 2;
+        constexpr int kEpiThreads = kSkEpiWarps * 32;
         const bool have = mbar_wait(tfull, 0, err, 472);
         tc_fence_after();
-        const uint32_t taddr = tmem + (static_cast<uint32_t>(warp_q * 32) << 16);
-        float* dst = parts + static_cast<int64_t>(sp) * M * N + n;
+        float* stage = reinterpret_cast<float*>(smem);  // the ring is drained once tfull fired
+        if (warp_q * 32 < M) {  // warp-uniform: quarters past the last token load nothing
+            const uint32_t taddr = tmem + (static_cast<uint32_t>(warp_q * 32) << 16);
+            float4* srow = reinterpret_cast<float4*>(stage + (warp_q * 32 + lane) * kPartPitch);
 #pragma unroll 1
-        for (int c0 = eg * 16; c0 < BN && c0 < M; c0 += 32) {
-            uint32_t r[16];
-            tmem_ld16(taddr + c0, r);
-            tmem_ld_wait();
-            if (n < N) {
+            for (int ci = eg; ci < kPartBN / 16; ci += 4) {  // two chunks per TMEM round trip
+                uint32_t r[2][16];
+                tmem_ld16(taddr + ci * 16, r[0]);
+                tmem_ld16(taddr + (ci + 2) * 16, r[1]);
+                tmem_ld_wait();
 #pragma unroll
-                for (int j = 0; j < 16; ++j)
-                    if (c0 + j < M)
-                        dst[static_cast<int64_t>(c0 + j) * N] = have ? __uint_as_float(r[j]) : 0.f;
+                for (int h = 0; h < 2; ++h)
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; ++q4)
+                        srow[(ci + 2 * h) * 4 + q4] =
+                            have ? make_float4(__uint_as_float(r[h][4 * q4]), __uint_as_float(r[h][4 * q4 + 1]),
+                                               __uint_as_float(r[h][4 * q4 + 2]), __uint_as_float(r[h][4 * q4 + 3]))
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
             }
         }
         tc_fence_before();
+        named_bar(1, kEpiThreads);
+        const bool vec = (N & 3) == 0 && wrow + kPartBN <= N;
+        for (int m = ew; m < M; m += kSkEpiWarps) {
+            const float* src = stage + m * kPartPitch;
+            float* dst = parts + (static_cast<int64_t>(sp) * M + m) * N + wrow;
+#pragma unroll
+            for (int c = lane * 4; c < kPartBN; c += 128) {
+                const float4 v = *reinterpret_cast<const float4*>(src + c);
+                if (vec) {
+                    *reinterpret_cast<float4*>(dst + c) = v;
+                } else {
+                    if (wrow + c < N) dst[c] = v.x;
+                    if (wrow + c + 1 < N) dst[c + 1] = v.y;
+                    if (wrow + c + 2 < N) dst[c + 2] = v.z;
+                    if (wrow + c + 3 < N) dst[c + 3] = v.w;
+                }
+            }
+        }
     }
     // lane 0 of warps 0 and 1 ran their loops alone: reconverge before the block barrier
     __syncwarp();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, Cfg::kTmemCols);
+        tmem_dealloc(tmem, kPartBN);
     }
 }
 
@@ -1217,22 +1241,20 @@ int launch_cl(const CUtensorMap& tw, const CUtensorMap& tx, void* y, unsigned lo
 // Split count of the partials kernel: as many splits as keep one tile-split per SM in a single
 // wave, at least 4 k-blocks per split, at most 16 partials for the consumer to add.
 int part_splits(int N, int K) {
-    const int T = (N + kBM - 1) / kBM, KB = (K + kBK - 1) / kBK, sms = num_sms();
+    const int T = (N + kPartBN - 1) / kPartBN, KB = (K + kBK - 1) / kBK, sms = num_sms();
     if (T >= sms) return 1;
     return std::max(1, std::min({sms / T, std::max(1, KB / 4), 16}));
 }
 
-template <int BN>
 int launch_part(const CUtensorMap& tw, const CUtensorMap& tx, float* parts, int M, int N, int K,
                 int S, cudaStream_t stream) {
-    using Cfg = PartCfg<BN>;
     int* err = device_error_word();
     if (!err) return set_error(MSGL_ERR_CUDA, "device error word unavailable");
-    cudaFuncSetAttribute(gemm_part_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(Cfg::kSmem));
-    const int T = (N + kBM - 1) / kBM;
-    launch_pdl(gemm_part_kernel<BN>, dim3(T * S), dim3(kSkThreads), Cfg::kSmem, stream, tw, tx,
-               parts, M, N, K, S, err);
+    cudaFuncSetAttribute(gemm_part_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(kPartSmem));
+    const int T = (N + kPartBN - 1) / kPartBN;
+    launch_pdl(gemm_part_kernel, dim3(T * S), dim3(kSkThreads), kPartSmem, stream, tw, tx, parts,
+               M, N, K, S, err);
     MSGL_LAUNCH_CHECK();
     return MSGL_OK;
 }
@@ -1460,18 +1482,12 @@ int msgl_gemm_bf16_partials(const void* x, const void* w, float* parts, int M, i
     if (splits < 1 || splits > KB || splits > 64)
         return set_error(MSGL_ERR_INVALID_ARG, "gemm_partials: splits must be in [1, min(64, K / 64)]");
     if (M == 0) return MSGL_OK;
-    const int bn = pick_bn(M);
     CUtensorMap tw, tx;
-    int rc = make_tmap_2d_bf16(&tw, w, K, N, static_cast<uint64_t>(K) * 2, kBK, kBM, true);
+    int rc = make_tmap_2d_bf16(&tw, w, K, N, static_cast<uint64_t>(K) * 2, kBK, kPartBN, true);
     if (rc) return rc;
-    rc = make_tmap_2d_bf16(&tx, x, K, M, static_cast<uint64_t>(K) * 2, kBK, bn, true);
+    rc = make_tmap_2d_bf16(&tx, x, K, M, static_cast<uint64_t>(K) * 2, kBK, kBM, true);
     if (rc) return rc;
-    switch (bn) {
-        case 16: return launch_part<16>(tw, tx, parts, M, N, K, splits, stream);
-        case 32: return launch_part<32>(tw, tx, parts, M, N, K, splits, stream);
-        case 64: return launch_part<64>(tw, tx, parts, M, N, K, splits, stream);
-        default: return launch_part<128>(tw, tx, parts, M, N, K, splits, stream);
-    }
+    return launch_part(tw, tx, parts, M, N, K, splits, stream);
 }
 
 size_t msgl_grouped_gemm_workspace_size(int max_rows, int num_experts) {

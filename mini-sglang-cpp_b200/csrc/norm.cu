@@ -49,13 +49,11 @@ __device__ __forceinline__ void store8(float* p, const float (&v)[8]) {
 // MODE 1: r += x; x = rmsnorm(r)                (x bf16 in/out, r fp32 in/out)
 // MODE 2: r = x;  x = rmsnorm(x)                (first fused call)
 // MODE 3: r = E[id]; x = rmsnorm(r)             (embedding + first norm; x = E (bf16) rows)
-// MODE 4: r += sum_p P[p]; x = rmsnorm(r)       (P: fp32 split-K partials [nparts][rows][hidden]
-//                                                added in p order, then the residual, as MODE 1)
 template <typename T, int MODE, int VPT>
 __global__ void __launch_bounds__(kNormThreads)
 rmsnorm_kernel(const T* x_in, T* x_out, float* __restrict__ resid,
                const T* __restrict__ w, const int* __restrict__ ids, int vocab, int hidden,
-               float eps, const float* __restrict__ parts, int nparts, int64_t part_stride) {
+               float eps) {
     __shared__ float red[4];
     pdl_wait();
     pdl_trigger();
@@ -74,23 +72,12 @@ rmsnorm_kernel(const T* x_in, T* x_out, float* __restrict__ resid,
     for (int i = 0; i < VPT; ++i) {
         int vi = threadIdx.x + i * kNormThreads;
         if (vi < nvec) {
-            if (MODE == 4) {
-                const float* pp = parts + static_cast<int64_t>(row) * hidden + vi * 8;
-                load8(pp, v[i]);
-                for (int p = 1; p < nparts; ++p) {
-                    float t[8];
-                    load8(pp + p * part_stride, t);
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) v[i][j] += t[j];
-                }
-            } else {
-                load8(src + vi * 8, v[i]);
-            }
+            load8(src + vi * 8, v[i]);
             if (MODE == 3 && zero_row) {
 #pragma unroll
                 for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
             }
-            if (MODE == 1 || MODE == 4) {
+            if (MODE == 1) {
                 float r[8];
                 load8(resid + static_cast<int64_t>(row) * hidden + vi * 8, r);
 #pragma unroll
@@ -119,22 +106,19 @@ rmsnorm_kernel(const T* x_in, T* x_out, float* __restrict__ resid,
 
 template <typename T, int MODE>
 int launch_norm(const T* x_in, T* x_out, float* resid, const T* w, const int* ids, int vocab,
-                int num_tokens, int hidden, float eps, cudaStream_t stream,
-                const float* parts = nullptr, int nparts = 0) {
+                int num_tokens, int hidden, float eps, cudaStream_t stream) {
     if (num_tokens < 0 || hidden <= 0 || hidden % 8 != 0 || hidden > 8 * 8 * kNormThreads)
         return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "rmsnorm: hidden must be a multiple of 8, <= 8192");
     if (num_tokens == 0) return MSGL_OK;
     if ((reinterpret_cast<uintptr_t>(x_in) | reinterpret_cast<uintptr_t>(x_out) |
-         reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(resid) |
-         reinterpret_cast<uintptr_t>(parts)) & 15)
+         reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(resid)) & 15)
         return set_error(MSGL_ERR_INVALID_ARG, "rmsnorm: pointers must be 16-byte aligned");
     int vpt = (hidden / 8 + kNormThreads - 1) / kNormThreads;
     dim3 grid(num_tokens), block(kNormThreads);
 #define MSGL_NORM_CASE(N)                                                                   \
     case N:                                                                                 \
         launch_pdl(rmsnorm_kernel<T, MODE, N>, grid, block, 0, stream, x_in, x_out, resid, w, \
-                   ids, vocab, hidden, eps, parts, nparts,                                  \
-                   static_cast<int64_t>(num_tokens) * hidden);                              \
+                   ids, vocab, hidden, eps);                                                \
         break;
     switch (vpt) {
         MSGL_NORM_CASE(1) MSGL_NORM_CASE(2) MSGL_NORM_CASE(3) MSGL_NORM_CASE(4)
@@ -144,6 +128,66 @@ int launch_norm(const T* x_in, T* x_out, float* resid, const T* w, const int* id
 #undef MSGL_NORM_CASE
     MSGL_LAUNCH_CHECK();
     return MSGL_OK;
+}
+
+// residual += sum_p P[p]; x = rmsnorm(residual) * w, with P the fp32 split-K partials
+// [nparts][rows][hidden] of the projection before the norm, added in p order, then the residual
+// (as forward_fused_add adds x to the residual). One CTA per row, one thread per 8 elements
+// (hidden / 8 threads), partial loads issued four at a time so that the L2 round trips overlap.
+__global__ void __launch_bounds__(1024)
+add_partials_rmsnorm_kernel(const float* __restrict__ parts, int nparts, __nv_bfloat16* __restrict__ x_out,
+                            float* __restrict__ resid, const __nv_bfloat16* __restrict__ w,
+                            int hidden, float eps) {
+    __shared__ float red[32];
+    pdl_wait();
+    pdl_trigger();
+    const int row = blockIdx.x, vi = threadIdx.x;
+    const bool active = vi * 8 < hidden;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * hidden;
+    const int64_t off = static_cast<int64_t>(row) * hidden + vi * 8;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float ss = 0.f;
+    if (active) {
+        const float* pp = parts + off;
+        int p = 0;
+        for (; p + 4 <= nparts; p += 4) {
+            float t0[8], t1[8], t2[8], t3[8];
+            load8(pp + p * stride, t0);
+            load8(pp + (p + 1) * stride, t1);
+            load8(pp + (p + 2) * stride, t2);
+            load8(pp + (p + 3) * stride, t3);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = ((v[j] + t0[j]) + t1[j] + t2[j]) + t3[j];
+        }
+        for (; p < nparts; ++p) {
+            float t[8];
+            load8(pp + p * stride, t);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] += t[j];
+        }
+        float r[8];
+        load8(resid + off, r);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            v[j] += r[j];
+            ss += v[j] * v[j];
+        }
+        store8(resid + off, v);
+    }
+    ss = warp_sum(ss);
+    const int nw = (blockDim.x + 31) >> 5;
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+    for (int i = 0; i < nw; ++i) tot += red[i];
+    const float inv_rms = 1.0f / sqrtf(tot / static_cast<float>(hidden) + eps);
+    if (active) {
+        float wv[8], o[8];
+        load8(w + vi * 8, wv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = v[j] * inv_rms * wv[j];
+        store8(x_out + off, o);
+    }
 }
 
 template <typename T>
@@ -200,9 +244,18 @@ int msgl_add_partials_rmsnorm(const float* parts, int nparts, void* x_out, float
         return set_error(MSGL_ERR_INVALID_ARG, "add_partials_rmsnorm: null");
     if (nparts < 1 || nparts > 64)
         return set_error(MSGL_ERR_INVALID_ARG, "add_partials_rmsnorm: nparts must be in [1, 64]");
-    auto* xb = static_cast<__nv_bfloat16*>(x_out);
-    return launch_norm<__nv_bfloat16, 4>(xb, xb, residual, static_cast<const __nv_bfloat16*>(weight),
-                                         nullptr, 0, num_tokens, hidden, eps, stream, parts, nparts);
+    if (num_tokens < 0 || hidden <= 0 || hidden % 8 != 0 || hidden > 8 * 1024)
+        return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "add_partials_rmsnorm: hidden must be a multiple of 8, <= 8192");
+    if ((reinterpret_cast<uintptr_t>(parts) | reinterpret_cast<uintptr_t>(x_out) |
+         reinterpret_cast<uintptr_t>(weight) | reinterpret_cast<uintptr_t>(residual)) & 15)
+        return set_error(MSGL_ERR_INVALID_ARG, "add_partials_rmsnorm: pointers must be 16-byte aligned");
+    if (num_tokens == 0) return MSGL_OK;
+    const int threads = ((hidden / 8 + 31) / 32) * 32;
+    launch_pdl(add_partials_rmsnorm_kernel, dim3(num_tokens), dim3(threads), 0, stream, parts, nparts,
+               static_cast<__nv_bfloat16*>(x_out), residual,
+               static_cast<const __nv_bfloat16*>(weight), hidden, eps);
+    MSGL_LAUNCH_CHECK();
+    return MSGL_OK;
 }
 
 int msgl_embed_rmsnorm(const void* embed, const int* ids, int num_tokens, int vocab, int hidden,

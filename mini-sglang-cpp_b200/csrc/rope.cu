@@ -91,9 +91,21 @@ qknorm_rope_store_kernel(const __nv_bfloat16* __restrict__ qkv, const float* __r
     if (PARTS) {
         const int64_t stride = static_cast<int64_t>(num_tokens) * nh * 128;
         const float* src = parts + wid * 128;
-        float2 pa = *reinterpret_cast<const float2*>(src + 2 * lane);
-        float2 pb = *reinterpret_cast<const float2*>(src + 64 + 2 * lane);
-        for (int p = 1; p < nparts; ++p) {
+        float2 pa = make_float2(0.f, 0.f), pb = make_float2(0.f, 0.f);
+        int p = 0;
+        for (; p + 4 <= nparts; p += 4) {  // four partials' loads in flight, added in order
+            float2 ta[4], tb[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                ta[u] = *reinterpret_cast<const float2*>(src + (p + u) * stride + 2 * lane);
+                tb[u] = *reinterpret_cast<const float2*>(src + (p + u) * stride + 64 + 2 * lane);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                pa.x += ta[u].x; pa.y += ta[u].y; pb.x += tb[u].x; pb.y += tb[u].y;
+            }
+        }
+        for (; p < nparts; ++p) {
             const float2 ta = *reinterpret_cast<const float2*>(src + p * stride + 2 * lane);
             const float2 tb = *reinterpret_cast<const float2*>(src + p * stride + 64 + 2 * lane);
             pa.x += ta.x; pa.y += ta.y; pb.x += tb.x; pb.y += tb.y;
