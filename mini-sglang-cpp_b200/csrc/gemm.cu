@@ -13,6 +13,7 @@
 // Epilogues: bf16 store, fp32 store, SwiGLU (gate/up rows interleaved by msgl_pack_gate_up;
 // split of qwen3.cpp:62-77 + SwiGLU of layer.cpp:155-158), argmax (scheduler.cpp:117-124).
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "tmap.h"
@@ -90,14 +91,15 @@ __device__ __forceinline__ void epilogue_chunk(const float (&vals)[16], int n, i
             }
         }
     } else if (EPI == EPI_SWIGLU) {
-        // rows of each 32-row group: 16 gate rows then the 16 matching up rows
+        // rows of each 16-row group: 8 gate rows then the 8 matching up rows; lane l pairs with
+        // lane l ^ 8, the even token going to the gate lane and the odd one to the up lane
         const int inter = N >> 1;
-        const int f = n_tile * (kBM / 2) + warp_q * 16 + (lane & 15);
-        const bool lo = lane < 16;
+        const int f = n_tile * (kBM / 2) + warp_q * 16 + (lane >> 4) * 8 + (lane & 7);
+        const bool lo = (lane & 8) == 0;
 #pragma unroll
         for (int j = 0; j < 16; j += 2) {
             float send = lo ? vals[j + 1] : vals[j];
-            float recv = __shfl_xor_sync(0xffffffffu, send, 16);
+            float recv = __shfl_xor_sync(0xffffffffu, send, 8);
             float g = lo ? vals[j] : recv;
             float u = lo ? recv : vals[j + 1];
             int m = m_base + j + (lo ? 0 : 1);
@@ -1048,6 +1050,237 @@ gemm_part_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
     }
 }
 
+// ============================================================================ row ranges
+// Decode-sized GEMMs with many weight rows (gate_up, lm_head): every CTA owns whole tiles of BR
+// consecutive weight rows (BR = 16 hs, hs <= 16, chosen on the host so that the tiles fill the
+// GPU's CTAs in near-equal rounds) over the full K, so there is no K split and no cross-CTA
+// reduction. Operands as in the partials kernel: tokens are the UMMA M dimension (128) and the
+// tile's weight rows the N dimension (BR), a ring stage holding a 16 KB token tile and a
+// BR x 64 weight tile. The CTA walks its tiles t = blockIdx.x, + gridDim.x, ... with the
+// accumulator double-buffered in TMEM (2 x 256 columns), so a tile's epilogue overlaps the next
+// tile's mainloop. Epilogue thread = token (TMEM lane), 16 consecutive weight rows per chunk:
+//   BF16 / F32  y[m][n .. n + 15]
+//   SWIGLU      packed rows (16-row groups: 8 gate, then the 8 matching up rows) ->
+//               y[m][f .. f + 7] = silu(gate) * up for the group's 8 features
+//   ARGMAX      running best (logit, lowest id) over the thread's rows, one atomicMax per token
+constexpr int kRowsTileX = kBM * kBK * 2;         // 16 KB token tile (UMMA A)
+constexpr int kRowsTileW = 256 * kBK * 2;         // room for a 256-row weight tile (UMMA B)
+constexpr int kRowsStage = kRowsTileX + kRowsTileW;
+constexpr int kRowsStages = kRingBudget / kRowsStage;  // 4
+constexpr size_t kRowsSmem = static_cast<size_t>(kRowsStages) * kRowsStage + 1024 + 256;
+
+__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
+
+template <int EPI>
+__global__ void __launch_bounds__(kSkThreads, 1)
+gemm_rows_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+                 void* __restrict__ y, unsigned long long* __restrict__ amax, int M, int N, int K,
+                 int BR, int id_off, int* err) {
+    constexpr int ST = kRowsStages;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sW = smem;                     // [ST] weight tiles (B)
+    uint8_t* sX = smem + ST * kRowsTileW;   // [ST] token tiles (A)
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + ST * kRowsStage);
+    uint64_t* empty = full + ST;
+    uint64_t* tfull = empty + ST;   // [2] accumulator ready
+    uint64_t* tempty = tfull + 2;   // [2] accumulator drained
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int T = (N + BR - 1) / BR;
+    const int KB = (K + kBK - 1) / kBK;
+    const int G = gridDim.x;
+    const int my_tiles = static_cast<int>(blockIdx.x) < T ? (T - blockIdx.x + G - 1) / G : 0;
+    const uint32_t stage_tx = kRowsTileX + static_cast<uint32_t>(BR) * kBK * 2;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < ST; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], kSkEpiWarps);
+        }
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            tma_prefetch_desc(&tmap_w);
+            tma_prefetch_desc(&tmap_x);
+            const uint64_t pol_w = policy_evict_first();
+            const uint64_t pol_x = policy_evict_last();
+            // weight tiles of the first ST stages before the dependency wait (see gemm_sk_kernel)
+            const int npre = my_tiles > 0 ? min(ST, my_tiles * KB) : 0;
+            for (int i = 0; i < npre; ++i) {
+                const int t = blockIdx.x + (i / KB) * G;
+                mbar_arrive_expect_tx(&full[i], stage_tx);
+                tma_load_2d_hint(sW + i * kRowsTileW, &tmap_w, &full[i], (i % KB) * kBK, t * BR, pol_w);
+            }
+            pdl_wait();
+            pdl_trigger();
+            int i = 0;
+            bool ok = true;
+            for (int it = 0; it < my_tiles && ok; ++it) {
+                const int wrow = (blockIdx.x + it * G) * BR;
+                for (int kb = 0; kb < KB; ++kb, ++i) {
+                    const int s = i % ST;
+                    if (i >= npre) {
+                        if (!mbar_wait(&empty[s], ((i / ST) - 1) & 1, err, 480)) { ok = false; break; }
+                        mbar_arrive_expect_tx(&full[s], stage_tx);
+                        tma_load_2d_hint(sW + s * kRowsTileW, &tmap_w, &full[s], kb * kBK, wrow, pol_w);
+                    }
+                    tma_load_2d_hint(sX + s * kRowsTileX, &tmap_x, &full[s], kb * kBK, 0, pol_x);
+                }
+            }
+        } else {
+            pdl_wait();
+            pdl_trigger();
+        }
+    } else if (warp == 1) {
+        pdl_wait();
+        pdl_trigger();
+        if (lane == 0) {
+            const uint32_t idesc = umma_idesc_bf16(kBM, BR);
+            int i = 0;
+            bool ok = true;
+            for (int it = 0; it < my_tiles && ok; ++it) {
+                const int a = it & 1;
+                if (it >= 2 && !mbar_wait(&tempty[a], ((it >> 1) - 1) & 1, err, 481)) break;
+                tc_fence_after();
+                const uint32_t acc = tmem + a * 256;
+                for (int kb = 0; kb < KB; ++kb, ++i) {
+                    const int s = i % ST;
+                    if (!mbar_wait(&full[s], (i / ST) & 1, err, 482)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(sX + s * kRowsTileX);
+                    const uint32_t b_addr = smem_u32(sW + s * kRowsTileW);
+#pragma unroll
+                    for (int k = 0; k < kBK / 16; ++k)
+                        umma_bf16(acc, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32),
+                                  idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                    umma_commit(&empty[s]);
+                }
+                if (ok) umma_commit(&tfull[a]);
+            }
+        }
+    } else {
+        // ---------------- epilogue warps 2..9: warp w reads TMEM lane quarter w % 4 (32 tokens);
+        // the two warps of a quarter take alternate 16-row chunks
+        pdl_wait();
+        pdl_trigger();
+        const int warp_q = warp & 3;
+        const int eg = (warp - 2) >> 2;
+        const int m = warp_q * 32 + lane;
+        const bool live = warp_q * 32 < M;  // warp-uniform
+        const int nch = BR / 16;
+        unsigned long long best = 0ull;
+        for (int it = 0; it < my_tiles; ++it) {
+            const int a = it & 1;
+            const int wrow = (blockIdx.x + it * G) * BR;
+            const bool have = mbar_wait(&tfull[a], (it >> 1) & 1, err, 483);
+            tc_fence_after();
+            if (live) {
+                const uint32_t taddr = tmem + a * 256 + (static_cast<uint32_t>(warp_q * 32) << 16);
+#pragma unroll 1
+                for (int ci = eg; ci < nch; ci += 2) {
+                    uint32_t r[16];
+                    __syncwarp();  // converged for the warp-collective TMEM load
+                    tmem_ld16(taddr + ci * 16, r);
+                    tmem_ld_wait();
+                    float v[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] = have ? __uint_as_float(r[j]) : 0.f;
+                    const int n0 = wrow + ci * 16;
+                    if (m >= M || n0 >= N) {
+                    } else if (EPI == EPI_ARGMAX) {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const unsigned long long key =
+                                n0 + j < N ? argmax_key(v[j], n0 + j + id_off) : 0ull;
+                            best = key > best ? key : best;
+                        }
+                    } else if (EPI == EPI_SWIGLU) {
+                        const int inter = N >> 1;
+                        const int f0 = n0 >> 1;  // the group's first feature
+                        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(y) + static_cast<int64_t>(m) * inter + f0;
+                        if ((inter & 7) == 0) {
+                            uint4 o;
+                            o.x = pack_bf16x2(silu_mul(v[0], v[8]), silu_mul(v[1], v[9]));
+                            o.y = pack_bf16x2(silu_mul(v[2], v[10]), silu_mul(v[3], v[11]));
+                            o.z = pack_bf16x2(silu_mul(v[4], v[12]), silu_mul(v[5], v[13]));
+                            o.w = pack_bf16x2(silu_mul(v[6], v[14]), silu_mul(v[7], v[15]));
+                            *reinterpret_cast<uint4*>(dst) = o;
+                        } else {
+#pragma unroll
+                            for (int k = 0; k < 8; ++k)
+                                if (f0 + k < inter) dst[k] = __float2bfloat16_rn(silu_mul(v[k], v[k + 8]));
+                        }
+                    } else if (EPI == EPI_BF16) {
+                        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(y) + static_cast<int64_t>(m) * N + n0;
+                        if ((N & 7) == 0 && n0 + 16 <= N) {
+                            uint4 o[2];
+                            uint32_t* ow = reinterpret_cast<uint32_t*>(o);
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) ow[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+                            reinterpret_cast<uint4*>(dst)[0] = o[0];
+                            reinterpret_cast<uint4*>(dst)[1] = o[1];
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 16; ++j)
+                                if (n0 + j < N) dst[j] = __float2bfloat16_rn(v[j]);
+                        }
+                    } else {  // EPI_F32
+                        float* dst = static_cast<float*>(y) + static_cast<int64_t>(m) * N + n0;
+                        if ((N & 3) == 0 && n0 + 16 <= N) {
+#pragma unroll
+                            for (int q4 = 0; q4 < 4; ++q4)
+                                reinterpret_cast<float4*>(dst)[q4] =
+                                    make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 16; ++j)
+                                if (n0 + j < N) dst[j] = v[j];
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[a]);
+        }
+        if (EPI == EPI_ARGMAX && live && m < M && best) atomicMax(amax + m, best);
+        tc_fence_before();
+    }
+    // lane 0 of warps 0 and 1 ran their loops alone: reconverge before the block barrier
+    __syncwarp();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+// MSGL_GEMM_ROWS=0 turns the row-range schedule off (the cluster / stream-K schedules run).
+bool rows_disabled() {
+    static const bool off = [] {
+        const char* e = std::getenv("MSGL_GEMM_ROWS");
+        return e && e[0] == '0';
+    }();
+    return off;
+}
+
 int num_sms() {
     static int n[64] = {0};
     int dev = 0;
@@ -1259,6 +1492,49 @@ int launch_part(const CUtensorMap& tw, const CUtensorMap& tx, float* parts, int 
     return MSGL_OK;
 }
 
+// Tile height (in 16-row groups) of the row-range kernel for N weight rows on `sms` CTAs: the
+// hs in [10, 16] whose tiles spread over the CTAs with the least staged bytes on the busiest
+// CTA (rounds x (16 KB token tile + 2 KB x hs weight tile) per k-block), among those that keep
+// the CTAs at least 85% evenly loaded; 0 when none does (the caller uses another schedule).
+// Below 10 groups the token tile would be most of what a stage brings in.
+int plan_rows(int N, int sms, int& tiles) {
+    const int n = (N + 15) / 16;
+    int best_hs = 0;
+    int64_t best = -1;
+    tiles = 0;
+    for (int hs = 10; hs <= 16; ++hs) {
+        const int T = (n + hs - 1) / hs;
+        const int rounds = (T + sms - 1) / sms;
+        if (static_cast<int64_t>(T) * 100 < static_cast<int64_t>(rounds) * sms * 85) continue;
+        const int64_t cost = static_cast<int64_t>(rounds) * (16 + 2 * hs);
+        if (best < 0 || cost < best) {
+            best = cost;
+            best_hs = hs;
+            tiles = T;
+        }
+    }
+    return best_hs;
+}
+
+template <int EPI>
+int launch_rows(const void* x, const void* w, void* y, unsigned long long* amax, int M, int N,
+                int K, int hs, int tiles, int sms, cudaStream_t stream, int id_off) {
+    int* err = device_error_word();
+    if (!err) return set_error(MSGL_ERR_CUDA, "device error word unavailable");
+    const int BR = hs * 16;
+    CUtensorMap tw, tx;
+    int rc = make_tmap_2d_bf16(&tw, w, K, N, static_cast<uint64_t>(K) * 2, kBK, BR, true);
+    if (rc) return rc;
+    rc = make_tmap_2d_bf16(&tx, x, K, M, static_cast<uint64_t>(K) * 2, kBK, kBM, true);
+    if (rc) return rc;
+    cudaFuncSetAttribute(gemm_rows_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(kRowsSmem));
+    launch_pdl(gemm_rows_kernel<EPI>, dim3(std::min(tiles, sms)), dim3(kSkThreads), kRowsSmem,
+               stream, tw, tx, y, amax, M, N, K, BR, id_off, err);
+    MSGL_LAUNCH_CHECK();
+    return MSGL_OK;
+}
+
 template <int EPI>
 int run_gemm(const void* x, const void* w, void* y, unsigned long long* amax, int M, int N, int K,
              void* ws, size_t ws_bytes, cudaStream_t stream, int id_off = 0) {
@@ -1266,6 +1542,12 @@ int run_gemm(const void* x, const void* w, void* y, unsigned long long* amax, in
     if (K % 8) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "gemm: K must be a multiple of 8");
     if (M == 0) return MSGL_OK;
     if (M > 65535 * 256) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "gemm: M too large");
+    if (M <= 128 && !rows_disabled()) {  // many weight rows: whole row tiles per CTA, no K split
+        const int sms = num_sms();
+        int tiles = 0;
+        const int hs = plan_rows(N, sms, tiles);
+        if (hs) return launch_rows<EPI>(x, w, y, amax, M, N, K, hs, tiles, sms, stream, id_off);
+    }
     const int bn = pick_bn(M);
     const int64_t tiles = static_cast<int64_t>((M + bn - 1) / bn) * ((N + kBM - 1) / kBM);
     CUtensorMap tw, tx;
@@ -1374,9 +1656,9 @@ int run_grouped(const void* x, const void* w, void* y, const int* offsets, int E
 
 __global__ void pack_gate_up_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst,
                                     int inter, int row_vecs) {
-    const int r = blockIdx.x;  // packed row
-    const int grp = r >> 5, within = r & 31;
-    const int srow = within < 16 ? grp * 16 + within : inter + grp * 16 + within - 16;
+    const int r = blockIdx.x;  // packed row: groups of 16 = 8 gate rows, then the 8 up rows
+    const int grp = r >> 4, within = r & 15;
+    const int srow = within < 8 ? grp * 8 + within : inter + grp * 8 + within - 8;
     for (int v = threadIdx.x; v < row_vecs; v += blockDim.x)
         dst[static_cast<int64_t>(r) * row_vecs + v] = src[static_cast<int64_t>(srow) * row_vecs + v];
 }

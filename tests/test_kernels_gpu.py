@@ -281,6 +281,8 @@ def test_decode_equals_extend_single_token(cuda):
 @pytest.mark.parametrize("M,N,K", [
     (1, 128, 64), (7, 256, 128), (16, 384, 1024), (64, 1024, 1024), (128, 6144, 4096),
     (128, 1000, 200), (200, 512, 4096), (300, 640, 576), (96, 4096, 12288),
+    # row-range schedule: 148 tiles of 176 rows; 136 tiles of 192 rows, the last one partial
+    (77, 26048, 320), (128, 26088, 256),
 ])
 def test_gemm_bf16(cuda, M, N, K):
     from msgl import ops
@@ -344,7 +346,10 @@ def test_gemm_matches_oracle_linear(cuda, oracle):
     np.testing.assert_allclose(y, ref, rtol=1e-4, atol=1e-4)
 
 
-@pytest.mark.parametrize("M,I,K", [(4, 3072, 1024), (128, 1536, 4096), (37, 96, 256), (300, 768, 512)])
+# (128, 12288, 1024) and (5, 12288, 256): 24576 weight rows take the row-range schedule (whole
+# 176-row tiles per CTA); the others the cluster / stream-K schedules
+@pytest.mark.parametrize("M,I,K", [(4, 3072, 1024), (128, 1536, 4096), (37, 96, 256), (300, 768, 512),
+                                   (128, 12288, 1024), (5, 12288, 256)])
 def test_gate_up_silu(cuda, oracle, M, I, K):
     from msgl import ops
     rng = np.random.default_rng(M + I)
