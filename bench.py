@@ -435,7 +435,8 @@ def run_case(args):
     `attention` / `attention_cascade`: paged decode attention (plain / cascade over the shared
     prefix), 128 requests x 2048 context (shared 1024 prefix);
     `gemm`: the gate_up + SwiGLU projection of one layer at 128 tokens (201 MB of weights);
-    `gemm_qkv`: the qkv projection at 128 tokens; `gemm_prefill`: gate_up + SwiGLU at 2048 tokens."""
+    `gemm_qkv`: the qkv projection at 128 tokens; `gemm_partials`: o_proj at 128 tokens as
+    split-K partials; `gemm_prefill`: gate_up + SwiGLU at 2048 tokens."""
     import torch
 
     import msgl
@@ -469,6 +470,13 @@ def run_case(args):
                              std=0.02)
         ws = ops.gemm_workspace(BATCH, 2 * I, H, dev)
         run = lambda: ops.gate_up_silu(x, w, workspace=ws)
+    elif args.case == "gemm_partials":  # o_proj of one layer at 128 tokens as split-K partials
+        x = ops.fill_normal_(torch.empty(BATCH, hq * 128, dtype=torch.bfloat16, device=dev), seed=6)
+        w = ops.fill_normal_(torch.empty(H, hq * 128, dtype=torch.bfloat16, device=dev), seed=7,
+                             std=0.02)
+        S = ops.gemm_partials_splits(BATCH, H, hq * 128)
+        pbuf = torch.empty(S, BATCH, H, dtype=torch.float32, device=dev)
+        run = lambda: ops.linear_partials(x, w, S, out=pbuf)
     elif args.case == "gemm_prefill":  # gate_up + SwiGLU of one layer at 2048 prefill tokens
         x = ops.fill_normal_(torch.empty(2048, H, dtype=torch.bfloat16, device=dev), seed=6)
         w = ops.fill_normal_(torch.empty(2 * I, H, dtype=torch.bfloat16, device=dev), seed=7,
@@ -627,7 +635,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--case", choices=["attention", "attention_cascade", "gemm", "gemm_qkv",
-                                       "gemm_prefill", "breakdown"], default=None,
+                                       "gemm_partials", "gemm_prefill", "breakdown"], default=None,
                     help="run one kernel of the step on a small single-layer case (profiling)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))

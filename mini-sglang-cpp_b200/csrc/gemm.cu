@@ -1493,16 +1493,16 @@ int launch_part(const CUtensorMap& tw, const CUtensorMap& tx, float* parts, int 
 }
 
 // Tile height (in 16-row groups) of the row-range kernel for N weight rows on `sms` CTAs: the
-// hs in [10, 16] whose tiles spread over the CTAs with the least staged bytes on the busiest
+// hs in [6, 16] whose tiles spread over the CTAs with the least staged bytes on the busiest
 // CTA (rounds x (16 KB token tile + 2 KB x hs weight tile) per k-block), among those that keep
 // the CTAs at least 85% evenly loaded; 0 when none does (the caller uses another schedule).
-// Below 10 groups the token tile would be most of what a stage brings in.
+// Below 6 groups the token tile would be most of what a stage brings in.
 int plan_rows(int N, int sms, int& tiles) {
     const int n = (N + 15) / 16;
     int best_hs = 0;
     int64_t best = -1;
     tiles = 0;
-    for (int hs = 10; hs <= 16; ++hs) {
+    for (int hs = 6; hs <= 16; ++hs) {
         const int T = (n + hs - 1) / hs;
         const int rounds = (T + sms - 1) / sms;
         if (static_cast<int64_t>(T) * 100 < static_cast<int64_t>(rounds) * sms * 85) continue;

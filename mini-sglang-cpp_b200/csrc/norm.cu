@@ -132,47 +132,65 @@ int launch_norm(const T* x_in, T* x_out, float* resid, const T* w, const int* id
 
 // residual += sum_p P[p]; x = rmsnorm(residual) * w, with P the fp32 split-K partials
 // [nparts][rows][hidden] of the projection before the norm, added in p order, then the residual
-// (as forward_fused_add adds x to the residual). One CTA per row, one thread per 8 elements
-// (hidden / 8 threads), partial loads issued four at a time so that the L2 round trips overlap.
-__global__ void __launch_bounds__(1024)
+// (as forward_fused_add adds x to the residual). One CTA of up to 512 threads per row, VPT
+// vectors of 8 elements per thread. The residual and weight loads go out first, then the
+// partials eight at a time, so that a row costs about two L2 round trips per vector.
+constexpr int kPartNormThreads = 512;
+
+template <int VPT>
+__global__ void __launch_bounds__(kPartNormThreads, 1)
 add_partials_rmsnorm_kernel(const float* __restrict__ parts, int nparts, __nv_bfloat16* __restrict__ x_out,
                             float* __restrict__ resid, const __nv_bfloat16* __restrict__ w,
                             int hidden, float eps) {
     __shared__ float red[32];
     pdl_wait();
     pdl_trigger();
-    const int row = blockIdx.x, vi = threadIdx.x;
-    const bool active = vi * 8 < hidden;
+    const int row = blockIdx.x;
     const int64_t stride = static_cast<int64_t>(gridDim.x) * hidden;
-    const int64_t off = static_cast<int64_t>(row) * hidden + vi * 8;
-    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float v[VPT][8], r[VPT][8], wv[VPT][8];
     float ss = 0.f;
-    if (active) {
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const int vi = threadIdx.x + i * blockDim.x;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
+        if (vi * 8 >= hidden) continue;
+        const int64_t off = static_cast<int64_t>(row) * hidden + vi * 8;
+        load8(resid + off, r[i]);
+        load8(w + vi * 8, wv[i]);
         const float* pp = parts + off;
         int p = 0;
-        for (; p + 4 <= nparts; p += 4) {
-            float t0[8], t1[8], t2[8], t3[8];
-            load8(pp + p * stride, t0);
-            load8(pp + (p + 1) * stride, t1);
-            load8(pp + (p + 2) * stride, t2);
-            load8(pp + (p + 3) * stride, t3);
+        for (; p + 8 <= nparts; p += 8) {
+            float t[8][8];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = ((v[j] + t0[j]) + t1[j] + t2[j]) + t3[j];
+            for (int u = 0; u < 8; ++u) load8(pp + (p + u) * stride, t[u]);
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[i][j] += t[u][j];
+        }
+        if (p + 4 <= nparts) {
+            float t[4][8];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) load8(pp + (p + u) * stride, t[u]);
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[i][j] += t[u][j];
+            p += 4;
         }
         for (; p < nparts; ++p) {
             float t[8];
             load8(pp + p * stride, t);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] += t[j];
+            for (int j = 0; j < 8; ++j) v[i][j] += t[j];
         }
-        float r[8];
-        load8(resid + off, r);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            v[j] += r[j];
-            ss += v[j] * v[j];
+            v[i][j] += r[i][j];
+            ss += v[i][j] * v[i][j];
         }
-        store8(resid + off, v);
+        store8(resid + off, v[i]);
     }
     ss = warp_sum(ss);
     const int nw = (blockDim.x + 31) >> 5;
@@ -181,12 +199,14 @@ add_partials_rmsnorm_kernel(const float* __restrict__ parts, int nparts, __nv_bf
     float tot = 0.f;
     for (int i = 0; i < nw; ++i) tot += red[i];
     const float inv_rms = 1.0f / sqrtf(tot / static_cast<float>(hidden) + eps);
-    if (active) {
-        float wv[8], o[8];
-        load8(w + vi * 8, wv);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] = v[j] * inv_rms * wv[j];
-        store8(x_out + off, o);
+    for (int i = 0; i < VPT; ++i) {
+        const int vi = threadIdx.x + i * blockDim.x;
+        if (vi * 8 >= hidden) continue;
+        float o[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = v[i][j] * inv_rms * wv[i][j];
+        store8(x_out + static_cast<int64_t>(row) * hidden + vi * 8, o);
     }
 }
 
@@ -250,8 +270,11 @@ int msgl_add_partials_rmsnorm(const float* parts, int nparts, void* x_out, float
          reinterpret_cast<uintptr_t>(weight) | reinterpret_cast<uintptr_t>(residual)) & 15)
         return set_error(MSGL_ERR_INVALID_ARG, "add_partials_rmsnorm: pointers must be 16-byte aligned");
     if (num_tokens == 0) return MSGL_OK;
-    const int threads = ((hidden / 8 + 31) / 32) * 32;
-    launch_pdl(add_partials_rmsnorm_kernel, dim3(num_tokens), dim3(threads), 0, stream, parts, nparts,
+    const int vecs = hidden / 8;
+    const int vpt = vecs > kPartNormThreads ? 2 : 1;
+    const int threads = ((vecs / vpt + (vecs % vpt ? 1 : 0) + 31) / 32) * 32;
+    auto kern = vpt == 1 ? add_partials_rmsnorm_kernel<1> : add_partials_rmsnorm_kernel<2>;
+    launch_pdl(kern, dim3(num_tokens), dim3(threads), 0, stream, parts, nparts,
                static_cast<__nv_bfloat16*>(x_out), residual,
                static_cast<const __nv_bfloat16*>(weight), hidden, eps);
     MSGL_LAUNCH_CHECK();

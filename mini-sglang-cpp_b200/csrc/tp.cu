@@ -73,13 +73,6 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
 __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ uint4 ld_volatile_v4(const void* p) {
-    uint4 v;
-    asm volatile("ld.volatile.global.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
-    return v;
-}
 
 // Thread t < world (t != rank) of CTA b: raise slot [rank][b] on rank t, then wait (bounded)
 // until rank t raised this rank's slot [t][b]; the CTA then synchronises.
@@ -102,68 +95,84 @@ __device__ __forceinline__ void ready_exchange(const TpPeers& peers, unsigned* l
 
 // One CTA (128 threads, VPT 8-element vectors per thread) per row, rows strided over the grid.
 // x[row] = RMSNorm(residual[row] (+)= sum over ranks, in rank order, of partial_q[row]) * w.
-// Every rank sums the same values in the same order, so every rank gets the same bits. W is
-// the world size rounded up to 2 / 4 / 8; a thread issues the peer loads of G = 8 / W vectors
-// (8 loads) before it uses any, so their NVLink round trips overlap.
-template <int VPT, int W>
+// Every rank sums the same values in the same order, so every rank gets the same bits. The row
+// of every rank (its own included) comes into shared memory with one bulk copy each
+// (cp.async.bulk from the peer-mapped region, no multicast): a few large NVLink transfers per
+// row instead of one 16-byte request per thread and vector.
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+template <int VPT>
 __global__ void __launch_bounds__(128)
 tp_fused_ar_norm_kernel(TpPeers peers, int world, int rank, __nv_bfloat16* __restrict__ x_out,
                         float* __restrict__ resid, const __nv_bfloat16* __restrict__ w, int T,
                         int H, float eps, int first, unsigned* __restrict__ local, int* err) {
-    constexpr int G = W >= 8 ? 1 : 8 / W;
+    extern __shared__ __align__(16) uint8_t ar_smem[];
+    const __nv_bfloat16* rows = reinterpret_cast<const __nv_bfloat16*>(ar_smem);  // [world][H]
+    uint64_t* bar = reinterpret_cast<uint64_t*>(ar_smem + static_cast<size_t>(world) * H * 2);
     __shared__ float red[4];
     pdl_wait();  // this rank's partial (the previous kernel's output) is complete
     pdl_trigger();
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        fence_barrier_init();
+    }
     unsigned* epoch_p = local + kTpMaxWorld * kTpMaxCtas + blockIdx.x;
     const unsigned e = *reinterpret_cast<volatile unsigned*>(epoch_p);
     ready_exchange(peers, local, world, rank, e + 1, err);  // every rank's partial is complete
     const int nvec = H >> 3;
+    const uint32_t row_bytes = static_cast<uint32_t>(H) * 2;
+    uint32_t phase = 0;
     for (int row = blockIdx.x; row < T; row += gridDim.x) {
         const int64_t rbase = static_cast<int64_t>(row) * H;
+        if (threadIdx.x == 0) {
+            fence_proxy_async_global();  // the acquired peer rows, read through the async proxy
+            fence_proxy_async();         // this CTA's reads of the previous row's copies are done
+            mbar_arrive_expect_tx(bar, row_bytes * world);
+            for (int q = 0; q < world; ++q)
+                bulk_load(ar_smem + static_cast<size_t>(q) * row_bytes, peers.part[q] + rbase, row_bytes, bar);
+        }
         float v[VPT][8];
+        float rr[VPT][8];
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) {  // residual loads overlap the copies
+            const int vi = threadIdx.x + i * 128;
+            if (vi >= nvec || first) continue;
+            const float4* r4 = reinterpret_cast<const float4*>(resid + rbase + vi * 8);
+            const float4 a = r4[0], b = r4[1];
+            rr[i][0] = a.x; rr[i][1] = a.y; rr[i][2] = a.z; rr[i][3] = a.w;
+            rr[i][4] = b.x; rr[i][5] = b.y; rr[i][6] = b.z; rr[i][7] = b.w;
+        }
+        mbar_wait(bar, phase, err, 502);
+        phase ^= 1;
         float ss = 0.f;
 #pragma unroll
-        for (int i0 = 0; i0 < VPT; i0 += G) {
-            uint4 u[G][W];
+        for (int i = 0; i < VPT; ++i) {
+            const int vi = threadIdx.x + i * 128;
+            if (vi >= nvec) continue;
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
-                const int vi = threadIdx.x + (i0 + g) * 128;
-                if (i0 + g < VPT && vi < nvec) {
-#pragma unroll
-                    for (int q = 0; q < W; ++q)
-                        if (q < world) u[g][q] = ld_volatile_v4(peers.part[q] + rbase + vi * 8);
-                }
+            for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
+            for (int q = 0; q < world; ++q) {
+                const uint4 u = *reinterpret_cast<const uint4*>(rows + static_cast<int64_t>(q) * H + vi * 8);
+                v[i][0] += bf16lo(u.x); v[i][1] += bf16hi(u.x);
+                v[i][2] += bf16lo(u.y); v[i][3] += bf16hi(u.y);
+                v[i][4] += bf16lo(u.z); v[i][5] += bf16hi(u.z);
+                v[i][6] += bf16lo(u.w); v[i][7] += bf16hi(u.w);
             }
+            if (!first) {
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
-                const int i = i0 + g;
-                const int vi = threadIdx.x + i * 128;
-                if (i >= VPT || vi >= nvec) continue;
-#pragma unroll
-                for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
-#pragma unroll
-                for (int q = 0; q < W; ++q) {
-                    if (q >= world) break;
-                    v[i][0] += bf16lo(u[g][q].x); v[i][1] += bf16hi(u[g][q].x);
-                    v[i][2] += bf16lo(u[g][q].y); v[i][3] += bf16hi(u[g][q].y);
-                    v[i][4] += bf16lo(u[g][q].z); v[i][5] += bf16hi(u[g][q].z);
-                    v[i][6] += bf16lo(u[g][q].w); v[i][7] += bf16hi(u[g][q].w);
-                }
-                float4* r4 = reinterpret_cast<float4*>(resid + rbase + vi * 8);
-                if (!first) {
-                    const float4 a = r4[0], b = r4[1];
-                    v[i][0] += a.x; v[i][1] += a.y; v[i][2] += a.z; v[i][3] += a.w;
-                    v[i][4] += b.x; v[i][5] += b.y; v[i][6] += b.z; v[i][7] += b.w;
-                }
-                r4[0] = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
-                r4[1] = make_float4(v[i][4], v[i][5], v[i][6], v[i][7]);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+                for (int j = 0; j < 8; ++j) v[i][j] += rr[i][j];
             }
+            float4* r4 = reinterpret_cast<float4*>(resid + rbase + vi * 8);
+            r4[0] = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
+            r4[1] = make_float4(v[i][4], v[i][5], v[i][6], v[i][7]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
         }
         ss = warp_sum(ss);
         if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-        __syncthreads();
+        __syncthreads();  // also: every thread is done reading this row's copies
         const float tot = red[0] + red[1] + red[2] + red[3];
         __syncthreads();
         const float inv = 1.0f / sqrtf(tot / static_cast<float>(H) + eps);
@@ -183,11 +192,14 @@ tp_fused_ar_norm_kernel(TpPeers peers, int world, int rank, __nv_bfloat16* __res
     if (threadIdx.x == 0) *reinterpret_cast<volatile unsigned*>(epoch_p) = e + 1;
 }
 
-template <int VPT, int W>
+template <int VPT>
 cudaError_t launch_ar(int grid, cudaStream_t stream, const TpPeers& pr, const msgl_tp* tp,
                       void* x_out, float* residual, const void* weight, int T, int H, float eps,
                       int first, unsigned* local, int* err) {
-    return launch_pdl(tp_fused_ar_norm_kernel<VPT, W>, dim3(grid), dim3(128), 0, stream, pr,
+    const size_t smem = static_cast<size_t>(tp->world) * H * 2 + 16;
+    cudaFuncSetAttribute(tp_fused_ar_norm_kernel<VPT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+    return launch_pdl(tp_fused_ar_norm_kernel<VPT>, dim3(grid), dim3(128), smem, stream, pr,
                       tp->world, tp->rank, static_cast<__nv_bfloat16*>(x_out), residual,
                       static_cast<const __nv_bfloat16*>(weight), T, H, eps, first, local, err);
 }
@@ -325,12 +337,8 @@ int msgl_tp_fused_allreduce_add_rmsnorm(msgl_tp* tp, const void* partial, void* 
     cudaError_t e;
 #define MSGL_TP_CASE(N)                                                                          \
     case N:                                                                                      \
-        e = tp->world <= 2 ? launch_ar<N, 2>(grid, stream, pr, tp, x_out, residual, weight,     \
-                                             num_tokens, hidden, eps, first, local, err)        \
-          : tp->world <= 4 ? launch_ar<N, 4>(grid, stream, pr, tp, x_out, residual, weight,     \
-                                             num_tokens, hidden, eps, first, local, err)        \
-                           : launch_ar<N, 8>(grid, stream, pr, tp, x_out, residual, weight,     \
-                                             num_tokens, hidden, eps, first, local, err);       \
+        e = launch_ar<N>(grid, stream, pr, tp, x_out, residual, weight, num_tokens, hidden, eps, \
+                         first, local, err);                                                     \
         break;
     switch (vpt) {
         MSGL_TP_CASE(1) MSGL_TP_CASE(2) MSGL_TP_CASE(3) MSGL_TP_CASE(4)

@@ -347,9 +347,10 @@ def test_gemm_matches_oracle_linear(cuda, oracle):
 
 
 # (128, 12288, 1024) and (5, 12288, 256): 24576 weight rows take the row-range schedule (whole
-# 176-row tiles per CTA); the others the cluster / stream-K schedules
+# 176-row tiles per CTA), (96, 6144, 512) with 96-row tiles; the others the cluster / stream-K
+# schedules
 @pytest.mark.parametrize("M,I,K", [(4, 3072, 1024), (128, 1536, 4096), (37, 96, 256), (300, 768, 512),
-                                   (128, 12288, 1024), (5, 12288, 256)])
+                                   (128, 12288, 1024), (5, 12288, 256), (96, 6144, 512)])
 def test_gate_up_silu(cuda, oracle, M, I, K):
     from msgl import ops
     rng = np.random.default_rng(M + I)
@@ -361,7 +362,8 @@ def test_gate_up_silu(cuda, oracle, M, I, K):
     assert rel_l2(y, ref) < 8e-3, rel_l2(y, ref)
 
 
-@pytest.mark.parametrize("M,V,K", [(4, 1024, 256), (64, 151936, 1024), (130, 4096, 512)])
+@pytest.mark.parametrize("M,V,K", [(4, 1024, 256), (64, 151936, 1024), (130, 4096, 512),
+                                   (128, 37984, 512)])
 def test_lm_head_argmax(cuda, oracle, M, V, K):
     from msgl import ops
     rng = np.random.default_rng(M + V)
