@@ -1288,7 +1288,10 @@ int num_sms() {
     if (dev < 0 || dev >= 64) return 148;
     if (!n[dev]) {
         int v = 0;
-        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) {
+            cudaGetLastError();  // no device (host-only query): a 148-SM B200
+            v = 148;
+        }
         n[dev] = v;
     }
     return n[dev];
@@ -1471,6 +1474,94 @@ int launch_cl(const CUtensorMap& tw, const CUtensorMap& tx, void* y, unsigned lo
     return MSGL_OK;
 }
 
+// Sum of the S fp32 split-K partials parts[S][M][N] of a decode GEMM, in split order, in the
+// form the GEMM's caller asked for: BF16 / F32 y[m][n] (4 columns per thread), SWIGLU the packed
+// gate/up rows in 16-column groups (8 gate, then the 8 matching up columns) -> y[m][f] =
+// silu(gate) * up for the group's 8 features (one group per thread). Partial loads go out four
+// splits at a time.
+template <int EPI>
+__global__ void __launch_bounds__(256)
+partials_reduce_kernel(const float* __restrict__ parts, int S, void* __restrict__ y, int M, int N) {
+    pdl_wait();
+    pdl_trigger();
+    const int64_t stride = static_cast<int64_t>(M) * N;
+    const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (EPI == EPI_SWIGLU) {
+        const int groups = N >> 4;
+        if (idx >= static_cast<int64_t>(M) * groups) return;
+        const int m = static_cast<int>(idx / groups), g = static_cast<int>(idx % groups);
+        const float4* src = reinterpret_cast<const float4*>(parts + static_cast<int64_t>(m) * N + g * 16);
+        float4 acc[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+        int sp = 0;
+        for (; sp + 2 <= S; sp += 2) {
+            float4 t[2][4];
+#pragma unroll
+            for (int u = 0; u < 2; ++u)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) t[u][q] = src[(sp + u) * (stride >> 2) + q];
+#pragma unroll
+            for (int u = 0; u < 2; ++u)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    acc[q].x += t[u][q].x; acc[q].y += t[u][q].y;
+                    acc[q].z += t[u][q].z; acc[q].w += t[u][q].w;
+                }
+        }
+        for (; sp < S; ++sp)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float4 t = src[sp * (stride >> 2) + q];
+                acc[q].x += t.x; acc[q].y += t.y; acc[q].z += t.z; acc[q].w += t.w;
+            }
+        const float* v = reinterpret_cast<const float*>(acc);  // 8 gate, then 8 up
+        const int inter = N >> 1;
+        uint4 o;
+        o.x = pack_bf16x2(silu_mul(v[0], v[8]), silu_mul(v[1], v[9]));
+        o.y = pack_bf16x2(silu_mul(v[2], v[10]), silu_mul(v[3], v[11]));
+        o.z = pack_bf16x2(silu_mul(v[4], v[12]), silu_mul(v[5], v[13]));
+        o.w = pack_bf16x2(silu_mul(v[6], v[14]), silu_mul(v[7], v[15]));
+        *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(y) + static_cast<int64_t>(m) * inter + g * 8) = o;
+    } else {
+        // 4 columns per thread when rows are float4-aligned, else one
+        const bool vec = (N & 3) == 0;
+        const int per = vec ? 4 : 1;
+        const int64_t cols = N / per;
+        if (idx >= static_cast<int64_t>(M) * cols) return;
+        const int64_t e0 = (idx / cols) * N + (idx % cols) * per;  // first element
+        float a[4] = {0.f, 0.f, 0.f, 0.f};
+        if (vec) {
+            const float4* src = reinterpret_cast<const float4*>(parts + e0);
+            int sp = 0;
+            for (; sp + 4 <= S; sp += 4) {
+                float4 t[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) t[u] = src[(sp + u) * (stride >> 2)];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) { a[0] += t[u].x; a[1] += t[u].y; a[2] += t[u].z; a[3] += t[u].w; }
+            }
+            for (; sp < S; ++sp) {
+                const float4 t = src[sp * (stride >> 2)];
+                a[0] += t.x; a[1] += t.y; a[2] += t.z; a[3] += t.w;
+            }
+        } else {
+            for (int sp = 0; sp < S; ++sp) a[0] += parts[sp * stride + e0];
+        }
+        for (int j = 0; j < per; ++j) {
+            if (EPI == EPI_BF16) static_cast<__nv_bfloat16*>(y)[e0 + j] = __float2bfloat16_rn(a[j]);
+            else static_cast<float*>(y)[e0 + j] = a[j];
+        }
+    }
+}
+
+// Decode-sized GEMM as split-K partials in the caller's workspace (after the counter region,
+// which must stay zero-filled) plus the reduce kernel above. Returns -1 (nothing launched) when
+// the shape gives fewer than 2 splits or the workspace is too small.
+template <int EPI>
+int launch_part_reduce(const void* x, const void* w, void* y, int M, int N, int K, void* ws,
+                       size_t ws_bytes, cudaStream_t stream);
+
 // Split count of the partials kernel: as many splits as keep one tile-split per SM in a single
 // wave, at least 4 k-blocks per split, at most 16 partials for the consumer to add.
 int part_splits(int N, int K) {
@@ -1535,6 +1626,35 @@ int launch_rows(const void* x, const void* w, void* y, unsigned long long* amax,
     return MSGL_OK;
 }
 
+size_t part_reduce_bytes(int M, int N, int K) {
+    const int S = part_splits(N, K);
+    if (S < 2 || M > 128) return 0;
+    return kCounterBytes + static_cast<size_t>(S) * M * N * sizeof(float);
+}
+
+template <int EPI>
+int launch_part_reduce(const void* x, const void* w, void* y, int M, int N, int K, void* ws,
+                       size_t ws_bytes, cudaStream_t stream) {
+    const int S = part_splits(N, K);
+    if (S < 2 || (EPI == EPI_SWIGLU && N % 16) || !ws || (reinterpret_cast<uintptr_t>(ws) & 15) ||
+        ws_bytes < kCounterBytes + static_cast<size_t>(S) * M * N * sizeof(float))
+        return -1;
+    float* parts = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kCounterBytes);
+    CUtensorMap tw, tx;
+    int rc = make_tmap_2d_bf16(&tw, w, K, N, static_cast<uint64_t>(K) * 2, kBK, kPartBN, true);
+    if (rc) return rc;
+    rc = make_tmap_2d_bf16(&tx, x, K, M, static_cast<uint64_t>(K) * 2, kBK, kBM, true);
+    if (rc) return rc;
+    rc = launch_part(tw, tx, parts, M, N, K, S, stream);
+    if (rc) return rc;
+    const int64_t work = EPI == EPI_SWIGLU ? static_cast<int64_t>(M) * (N / 16)
+                                           : static_cast<int64_t>(M) * ((N & 3) == 0 ? N / 4 : N);
+    launch_pdl(partials_reduce_kernel<EPI>, dim3(static_cast<unsigned>((work + 255) / 256)), dim3(256), 0,
+               stream, static_cast<const float*>(parts), S, y, M, N);
+    MSGL_LAUNCH_CHECK();
+    return MSGL_OK;
+}
+
 template <int EPI>
 int run_gemm(const void* x, const void* w, void* y, unsigned long long* amax, int M, int N, int K,
              void* ws, size_t ws_bytes, cudaStream_t stream, int id_off = 0) {
@@ -1542,10 +1662,18 @@ int run_gemm(const void* x, const void* w, void* y, unsigned long long* amax, in
     if (K % 8) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "gemm: K must be a multiple of 8");
     if (M == 0) return MSGL_OK;
     if (M > 65535 * 256) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "gemm: M too large");
-    if (M <= 128 && !rows_disabled()) {  // many weight rows: whole row tiles per CTA, no K split
+    if (M <= 128 && !rows_disabled()) {
+        // decode-sized: many weight rows -> whole row tiles per CTA (no K split); otherwise
+        // split-K partials summed by a second small kernel (not for argmax, which needs whole
+        // rows); row tiles of 6-9 groups only when the partials do not apply
         const int sms = num_sms();
         int tiles = 0;
         const int hs = plan_rows(N, sms, tiles);
+        if (hs >= 10) return launch_rows<EPI>(x, w, y, amax, M, N, K, hs, tiles, sms, stream, id_off);
+        if (EPI != EPI_ARGMAX) {
+            const int r = launch_part_reduce<EPI>(x, w, y, M, N, K, ws, ws_bytes, stream);
+            if (r != -1) return r;
+        }
         if (hs) return launch_rows<EPI>(x, w, y, amax, M, N, K, hs, tiles, sms, stream, id_off);
     }
     const int bn = pick_bn(M);
@@ -1718,7 +1846,7 @@ size_t msgl_gemm_workspace_size(int M, int N, int K) {
         sms = v;
     else
         cudaGetLastError();  // no device (host-only query): size for a 148-SM B200
-    return sk_workspace_bytes(bn, sms);
+    return std::max(sk_workspace_bytes(bn, sms), part_reduce_bytes(M, N, K));
 }
 
 int msgl_gemm_bf16(const void* x, const void* w, void* y, int M, int N, int K, int out_dtype,

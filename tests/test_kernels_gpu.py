@@ -301,10 +301,12 @@ def test_gemm_bf16(cuda, M, N, K):
 
 def test_gemm_workspace_shared_across_shapes(cuda):
     """One workspace reused, in stream order, by split-K GEMMs of different shapes (as the
-    executor does across a layer): every result stays correct."""
+    executor does across a layer): decode shapes as partials + reduce, (200, 512, 4096) as
+    stream-K, whose flags share the workspace's zero-filled head; every result stays correct."""
     from msgl import ops
     rng = np.random.default_rng(12)
-    shapes = [(128, 6144, 4096), (128, 4096, 4096), (128, 4096, 12288), (4, 1000, 512)]
+    shapes = [(128, 6144, 4096), (128, 4096, 4096), (200, 512, 4096), (128, 4096, 12288),
+              (4, 1000, 512)]
     ws = torch.zeros(max(ops.gemm_workspace(*s).numel() for s in shapes), dtype=torch.uint8,
                      device="cuda")
     data = [(rn(rng, M, K), rn(rng, N, K, std=0.02)) for M, N, K in shapes]
@@ -347,8 +349,8 @@ def test_gemm_matches_oracle_linear(cuda, oracle):
 
 
 # (128, 12288, 1024) and (5, 12288, 256): 24576 weight rows take the row-range schedule (whole
-# 176-row tiles per CTA), (96, 6144, 512) with 96-row tiles; the others the cluster / stream-K
-# schedules
+# 176-row tiles per CTA); (4, 3072, 1024), (128, 1536, 4096) and (96, 6144, 512) split-K partials
+# summed by the SwiGLU reduce kernel; (37, 96, 256) the cluster kernel, (300, 768, 512) stream-K
 @pytest.mark.parametrize("M,I,K", [(4, 3072, 1024), (128, 1536, 4096), (37, 96, 256), (300, 768, 512),
                                    (128, 12288, 1024), (5, 12288, 256), (96, 6144, 512)])
 def test_gate_up_silu(cuda, oracle, M, I, K):
