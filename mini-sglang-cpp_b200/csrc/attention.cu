@@ -1147,7 +1147,7 @@ int msgl_paged_attention_decode_noalloc(const void* q, const void* k_pool, const
     const size_t need = msgl_paged_attention_workspace_size(num_reqs, max_seq_len, num_q_heads,
                                                             num_kv_heads, head_dim);
     if (need > kNoAllocScratchBytes) {
-        char buf[160];
+        char buf[256];
         snprintf(buf, sizeof(buf),
                  "decode_noalloc: this batch needs %zu bytes of scratch; the static scratch holds "
                  "%zu (8 MiB) -- use msgl_paged_attention_decode with a workspace",
