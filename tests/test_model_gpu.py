@@ -202,3 +202,69 @@ def test_cascade_decode_step_matches_plain(cuda):
     clear = (top2[:, 1] - top2[:, 0]) > 4 * np.abs(a - b).max()
     assert np.array_equal(nxt_c.cpu().numpy()[clear], nxt_p.cpu().numpy()[clear])
     assert ops.device_error() == (0, 0)
+
+
+def _run_steps(model, orc, reqs, steps, num_pages, max_pages, forced=None):
+    """Prefill then decode steps through the executor, each step's logits vs the oracle; the
+    next tokens are the executor's greedy ids, or `forced[step]` when given. Returns the
+    per-step logits and tokens."""
+    from msgl.model import BatchBuilder, PagePool
+    bb = BatchBuilder(PagePool(num_pages))
+    logits, tokens = [], []
+    for step in range(steps):
+        sb = bb.build(reqs, decode=step > 0, max_pages=max_pages)
+        nxt, lg = model.forward(sb, logits=True)
+        torch.cuda.synchronize()
+        h = {k: v.cpu().numpy() for k, v in sb.tensors.items()}
+        ref = orc.forward(h["input_ids"], h["positions"], h["slot_mapping"], h["page_table"],
+                          h["seq_lens"], h["q_indptr"])
+        got = lg.cpu().numpy()
+        assert rel_l2(got, ref) < 2e-2, (step, sb.tensors["input_ids"].numel(), rel_l2(got, ref))
+        ids = forced[step] if forced is not None else [int(t) for t in nxt.cpu().numpy()]
+        logits.append(got)
+        tokens.append(ids)
+        for r, t in zip(reqs, ids):
+            r.cached_len = r.device_len
+            r.input_ids.append(int(t))
+    return logits, tokens
+
+
+def test_long_prefill_then_decode(cuda, oracle):
+    """A prefill of 185 tokens (more than 128: the executor's projections run the regular GEMM
+    schedules and the separate add + RMSNorm) then decode steps of 3 tokens (split-K partials
+    summed by the next kernel): every step's logits vs the oracle."""
+    from msgl.model import Qwen3Model, Request
+    w = weights(CFG, 5)
+    model = Qwen3Model(CFG, max_tokens=256, max_reqs=4)
+    model.set_weights(w)
+    model.alloc_kv(48)
+    orc = OracleModel(oracle, CFG, w, num_slots=48 * 16)
+    rng = np.random.default_rng(9)
+    reqs = [Request(list(rng.integers(0, CFG["vocab"], n))) for n in (100, 60, 25)]
+    _run_steps(model, orc, reqs, 3, 48, max_pages=8)
+
+
+def test_partials_path_matches_regular_path(cuda, oracle, monkeypatch):
+    """The same steps (same tokens fed back) on an executor created with MSGL_SPLITK_PARTIALS=0,
+    where every projection runs the regular GEMM schedules with bf16 outputs: both within the
+    bf16 tolerance of the oracle and of each other."""
+    from msgl.model import Qwen3Model, Request
+    w = weights(CFG, 6)
+    runs, forced = [], None
+    for flag in (None, "0"):
+        if flag is None:
+            monkeypatch.delenv("MSGL_SPLITK_PARTIALS", raising=False)
+        else:
+            monkeypatch.setenv("MSGL_SPLITK_PARTIALS", flag)
+        model = Qwen3Model(CFG, max_tokens=64, max_reqs=4)
+        model.set_weights(w)
+        model.alloc_kv(16)
+        orc = OracleModel(oracle, CFG, w, num_slots=16 * 16)
+        rng = np.random.default_rng(10)
+        reqs = [Request(list(rng.integers(0, CFG["vocab"], n))) for n in (9, 21)]
+        lg, toks = _run_steps(model, orc, reqs, 3, 16, max_pages=4, forced=forced)
+        runs.append(lg)
+        forced = toks
+        del model
+    for a, b in zip(*runs):
+        assert rel_l2(a, b) < 2e-2
