@@ -130,6 +130,22 @@ MSGL_API int msgl_qknorm_rope_store_kv_partials(const float* parts, int nparts, 
                                                 int num_q_heads, int num_kv_heads, int head_dim,
                                                 float eps, msgl_stream_t stream);
 
+/* ---------------------------------------------------------------- batch metadata */
+/* Advances a decode batch on the device (the decode branch of Scheduler::step's host flatten,
+ * src/scheduler/scheduler.cpp:83-106, with KVCachePool::allocate, src/cache/kvcache.cpp:21-28,
+ * and the slot formula of kernels/cuda/radix.cu:19-22): for request r with L = seq_lens[r]
+ * (its length in the step just run), input_ids[r] = next_tokens[r], positions[r] = L,
+ * seq_lens[r] = L + 1, and when L % page_size == 0 a page is popped from the free stack
+ * free_pages[0 .. *free_top) (top first, requests in order: the host pool's LIFO order) into
+ * page_table[r][L / page_size]; slot_mapping[r] = page_table[r][L / page_size] * page_size +
+ * L % page_size. All-or-nothing: if the stack runs out (MSGL_ERR_WORKSPACE, site 700) or a page
+ * would land past max_pages (MSGL_ERR_BOUNDS, site 701), nothing is written and the device
+ * error word records it. All arrays are device int32; page_table is [num_reqs, max_pages]. */
+MSGL_API int msgl_decode_advance(const int* next_tokens, int* input_ids, int* positions,
+                                 int* slot_mapping, int* page_table, int max_pages, int* seq_lens,
+                                 const int* free_pages, int* free_top, int num_reqs, int page_size,
+                                 msgl_stream_t stream);
+
 /* ---------------------------------------------------------------- paged attention */
 /* Replaces Attention::forward (src/layer/layer.cpp:214-262) with attention over the paged KV
  * pool. Pools: [num_slots, Hkv * D] bf16, slot = page * page_size + offset (radix.cu:19-22).

@@ -115,6 +115,18 @@ def qknorm_rope_store_kv_partials(parts, k_pool, v_pool, positions, slot_mapping
     return q
 
 
+def decode_advance(next_tokens, input_ids, positions, slot_mapping, page_table, seq_lens,
+                   free_pages, free_top, page_size=16):
+    """msgl_decode_advance on device int32 tensors (in place): the next decode step's metadata."""
+    for t in (next_tokens, input_ids, positions, slot_mapping, page_table, seq_lens, free_pages,
+              free_top):
+        _c(t, torch.int32)
+    B = seq_lens.numel()
+    check(lib().msgl_decode_advance(_p(next_tokens), _p(input_ids), _p(positions),
+                                    _p(slot_mapping), _p(page_table), page_table.shape[1],
+                                    _p(seq_lens), _p(free_pages), _p(free_top), B, page_size, _s()))
+
+
 # ------------------------------------------------------------------ attention
 def attention_workspace(num_reqs, max_seq_len, hq, hkv, device="cuda"):
     n = lib().msgl_paged_attention_workspace_size(num_reqs, max_seq_len, hq, hkv, 128)

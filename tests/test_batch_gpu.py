@@ -1,0 +1,151 @@
+"""Device-side decode batch metadata (msgl_decode_advance) against the host BatchBuilder /
+PagePool, which follow Scheduler::step's flatten (scheduler.cpp:83-106) and KVCachePool's LIFO
+allocation (kvcache.cpp:21-28). Integer outputs: bit-exact, step after step, including page
+boundary crossings; exhaustion and page-table overflow leave every array untouched."""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ERR_BOUNDS, ERR_WORKSPACE = 6, 7
+
+
+def host_decode_meta(reqs, pool, P, width):
+    from msgl.model import BatchBuilder
+    bb = BatchBuilder(pool, P)
+    ids, pos, slots, seq = [], [], [], []
+    for r in reqs:
+        bb._ensure_pages(r, r.device_len)
+        p = r.device_len - 1
+        ids.append(r.input_ids[-1])
+        pos.append(p)
+        slots.append(r.pages[p // P] * P + p % P)
+        seq.append(r.device_len)
+    pt = np.zeros((len(reqs), width), np.int32)
+    for i, r in enumerate(reqs):
+        pt[i, :len(r.pages)] = r.pages
+    return np.array(ids, np.int32), np.array(pos, np.int32), np.array(slots, np.int32), pt, \
+        np.array(seq, np.int32)
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.int32)).cuda()
+
+
+@pytest.mark.parametrize("B,steps", [(37, 40), (1, 20), (1100, 18)])
+def test_decode_advance_matches_host(cuda, B, steps):
+    from msgl import ops
+    from msgl.model import PagePool, Request
+    P, width = 16, 8
+    rng = np.random.default_rng(B)
+    num_pages = B * width + 5
+    pool = PagePool(num_pages)
+    rng.shuffle(pool.free)
+    # lengths on and around page boundaries, then random
+    lens = [int(x) for x in rng.integers(1, 80, B)]
+    lens[0] = 16
+    if B > 3:
+        lens[1], lens[2], lens[3] = 15, 17, 32
+    reqs = [Request([int(t) for t in rng.integers(0, 1000, n)]) for n in lens]
+    ids, pos, slots, pt, seq = host_decode_meta(reqs, pool, P, width)
+    d = dict(ids=dev(ids), pos=dev(pos), slots=dev(slots), pt=dev(pt), seq=dev(seq))
+    free = dev(np.array(pool.free + [0] * 4, np.int32))  # the stack's unused tail is never read
+    top = dev(np.array([len(pool.free)], np.int32))
+    for step in range(steps):
+        nxt = rng.integers(0, 1000, B).astype(np.int32)
+        for r, t in zip(reqs, nxt):  # host: the sampled token joins each request
+            r.input_ids.append(int(t))
+        ids, pos, slots, pt, seq = host_decode_meta(reqs, pool, P, width)
+        ops.decode_advance(dev(nxt), d["ids"], d["pos"], d["slots"], d["pt"], d["seq"], free, top,
+                           page_size=P)
+        torch.cuda.synchronize()
+        for name, want in (("ids", ids), ("pos", pos), ("slots", slots), ("pt", pt), ("seq", seq)):
+            got = d[name].cpu().numpy()
+            assert np.array_equal(got, want), (step, name)
+        assert int(top.item()) == len(pool.free), step
+    assert ops.device_error() == (0, 0)
+
+
+def test_decode_advance_exhaustion_and_overflow(cuda):
+    from msgl import ops
+    P = 16
+    # two requests about to enter a new page, one page left: nothing may change
+    seq = dev([32, 16, 5])
+    pt = dev([[3, 4, 0], [7, 0, 0], [9, 0, 0]])
+    ids, pos, slots = dev([1, 2, 3]), dev([31, 15, 4]), dev([4 * 16 + 15, 7 * 16 + 15, 9 * 16 + 4])
+    free, top = dev([11, 12]), dev([1])
+    snap = [t.clone() for t in (seq, pt, ids, pos, slots, free, top)]
+    ops.decode_advance(dev([5, 6, 7]), ids, pos, slots, pt, seq, free, top, page_size=P)
+    torch.cuda.synchronize()
+    assert ops.device_error() == (ERR_WORKSPACE, 700)
+    for a, b in zip((seq, pt, ids, pos, slots, free, top), snap):
+        assert torch.equal(a, b)
+    # a page past the page-table width
+    seq2, pt2 = dev([48]), dev([[1, 2, 3]])
+    ids2, pos2, slots2 = dev([0]), dev([47]), dev([3 * 16 + 15])
+    free2, top2 = dev([20, 21]), dev([2])
+    snap = [t.clone() for t in (seq2, pt2, ids2, pos2, slots2, top2)]
+    ops.decode_advance(dev([9]), ids2, pos2, slots2, pt2, seq2, free2, top2, page_size=P)
+    torch.cuda.synchronize()
+    assert ops.device_error() == (ERR_BOUNDS, 701)
+    for a, b in zip((seq2, pt2, ids2, pos2, slots2, top2), snap):
+        assert torch.equal(a, b)
+    # enough pages: both new pages come off the top, first request first
+    top[0] = 2
+    ops.decode_advance(dev([5, 6, 7]), ids, pos, slots, pt, seq, free, top, page_size=P)
+    torch.cuda.synchronize()
+    assert ops.device_error() == (0, 0)
+    assert pt.cpu().numpy().tolist() == [[3, 4, 12], [7, 11, 0], [9, 0, 0]]
+    assert slots.cpu().numpy().tolist() == [12 * 16, 11 * 16, 9 * 16 + 5]
+    assert seq.cpu().numpy().tolist() == [33, 17, 6] and int(top.item()) == 0
+
+
+def test_device_driven_decode_loop_matches_host_loop(cuda):
+    """Greedy decode driven on the device (forward, then msgl_decode_advance feeding the next
+    step) against the host-built steps: the same tokens."""
+    from msgl import ops
+    from msgl.model import BatchBuilder, BatchT, PagePool, Qwen3Model, Request, StepBatch
+    from test_model_gpu import CFG, weights
+    w = weights(CFG, 2)
+    model = Qwen3Model(CFG, max_tokens=64, max_reqs=4)
+    model.set_weights(w)
+    num_pages, width, steps = 24, 6, 6
+    rng = np.random.default_rng(3)
+    prompts = [[int(t) for t in rng.integers(0, CFG["vocab"], n)] for n in (14, 31, 7)]
+    runs = []
+    for mode in ("host", "device"):
+        model.alloc_kv(num_pages)
+        pool = PagePool(num_pages)
+        reqs = [Request(list(p)) for p in prompts]
+        bb = BatchBuilder(pool)
+        sb = bb.build(reqs, decode=False, max_pages=width)
+        nxt = model.forward(sb)
+        toks = [nxt.cpu().numpy().tolist()]
+        for r, t in zip(reqs, toks[0]):
+            r.cached_len = r.device_len
+            r.input_ids.append(int(t))
+        if mode == "host":
+            for _ in range(steps):
+                sb = bb.build(reqs, decode=True, max_pages=width)
+                nxt = model.forward(sb)
+                toks.append(nxt.cpu().numpy().tolist())
+                for r, t in zip(reqs, toks[-1]):
+                    r.input_ids.append(int(t))
+        else:
+            sb = bb.build(reqs, decode=True, max_pages=width)  # the first decode step's metadata
+            t = sb.tensors
+            free = torch.tensor(pool.free + [0], dtype=torch.int32, device="cuda")
+            top = torch.tensor([len(pool.free)], dtype=torch.int32, device="cuda")
+            st = sb.struct
+            st.max_seq_len = width * 16  # an upper bound, valid for every step
+            st.shared_prefix_pages = 0
+            for s in range(steps):
+                nxt = model.forward(StepBatch(t, st, len(reqs)))
+                toks.append(nxt.cpu().numpy().tolist())
+                if s + 1 < steps:
+                    ops.decode_advance(nxt, t["input_ids"], t["positions"], t["slot_mapping"],
+                                       t["page_table"], t["seq_lens"], free, top)
+        runs.append(toks)
+    assert runs[0] == runs[1]
+    assert ops.device_error() == (0, 0)
