@@ -1,17 +1,21 @@
 // gemm.cu -- tcgen05 / TMEM bf16 GEMMs for the dense projections.
 //
 // Linear::forward (src/layer/layer.cpp:122-143): y[M,N] = x[M,K] W[N,K]^T with W in the
-// reference's [out, in] layout. Each CTA computes one 128 x BN tile of y^T = W x^T: the 128
-// weight rows are the UMMA M dimension and up to 256 tokens the N dimension, so a decode step
-// (M = batch tokens) is a single weight-streaming pass in which every weight byte crosses HBM
-// once. Roles (192 threads):
-//   warp 0      TMA producer: 128 x 64 weight tile + BN x 64 token tile per k-block (SW128)
-//   warp 1      TMEM allocator and single-thread tcgen05.mma issuer (M=128, N=BN, K=16)
-//   warps 2-5   epilogue: tcgen05.ld of the fp32 accumulator (one TMEM lane = one weight row)
-// Small grids split K across CTAs; partial tiles go to a workspace and the last CTA to arrive
-// (self-resetting counter) sums them in split order (deterministic) and runs the epilogue.
-// Epilogues: bf16 store, fp32 store, SwiGLU (gate/up rows interleaved by msgl_pack_gate_up;
-// split of qwen3.cpp:62-77 + SwiGLU of layer.cpp:155-158), argmax (scheduler.cpp:117-124).
+// reference's [out, in] layout; every weight byte crosses HBM once per call. All kernels share
+// one structure: a TMA producer warp (weight and token tiles, SW128, k-blocks of 64), a warp that
+// allocates TMEM and issues tcgen05.mma from one thread (fp32 accumulator in TMEM), and
+// epilogue warps that read the accumulator with tcgen05.ld. Schedules, chosen per call
+// (run_gemm):
+//   gemm_rows_kernel   M <= 128, many weight rows: whole tiles of 16 hs weight rows per CTA over
+//                      the full K; tokens are the UMMA M dimension, the tile's rows N
+//   gemm_part_kernel   M <= 128: split-K fp32 partials (tokens as M, 256 weight rows as N), summed
+//                      by the next kernel or by partials_reduce_kernel
+//   gemm_cl_kernel     M <= 128 otherwise: cluster split-K, partials exchanged over DSMEM
+//   gemm_sk_kernel     stream-K (prefill-sized M; 128 weight rows as M, up to 256 tokens as N)
+//   gemm_kernel        one CTA per tile (very large grids) and the grouped MoE GEMM
+// Epilogues: bf16 store, fp32 store, SwiGLU (gate/up rows interleaved in 16-row groups by
+// msgl_pack_gate_up; split of qwen3.cpp:62-77 + SwiGLU of layer.cpp:155-158), argmax
+// (scheduler.cpp:117-124).
 #include <algorithm>
 #include <cstdlib>
 
@@ -131,6 +135,9 @@ struct GroupArgs {
     const int* offsets = nullptr;  // [E + 1] row offsets of each expert
 };
 
+// One CTA per 128 x BN tile of y^T = W x^T (192 threads: warp 0 TMA, warp 1 TMEM + MMA, warps
+// 2-5 epilogue, one TMEM lane = one weight row). Split K: partial tiles go to the workspace and
+// the last CTA to arrive (self-resetting counter) sums them in split order and runs the epilogue.
 template <int BN, int EPI, bool GROUPED>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
