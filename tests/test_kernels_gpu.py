@@ -227,6 +227,7 @@ def make_shared_prefix(rng, S, suffix_lens, hkv, extra=4, P=16, D=128):
     (32, 16, 4, [33, 2]),                      # four head groups
     (32, 8, 64, [1024] * 4 + [7, 900]),        # long shared prefix (bench-like)
     (32, 8, 6, list(range(1, 41))),            # 40 requests: 3 row tiles of 64 (request, head) rows
+    (4, 1, 5, [3, 60, 17] * 8),                # one TP8 rank of Qwen3-8B: 4 q heads on 1 kv head
 ])
 def test_paged_decode_cascade(cuda, oracle, hq, hkv, S, suffix):
     from msgl import ops
@@ -365,7 +366,7 @@ def test_gate_up_silu(cuda, oracle, M, I, K):
 
 
 @pytest.mark.parametrize("M,V,K", [(4, 1024, 256), (64, 151936, 1024), (130, 4096, 512),
-                                   (128, 37984, 512)])
+                                   (128, 37984, 512), (128, 18992, 512)])  # TP4 / TP8 shards
 def test_lm_head_argmax(cuda, oracle, M, V, K):
     from msgl import ops
     rng = np.random.default_rng(M + V)
