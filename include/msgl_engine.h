@@ -70,6 +70,19 @@ MSGL_API int msgl_model_destroy(msgl_model* m);
 MSGL_API int msgl_model_random_init(msgl_model* m, uint64_t seed, float std, msgl_stream_t stream);
 MSGL_API int msgl_model_set_weight(msgl_model* m, const char* name, const uint16_t* host_bf16,
                                    int64_t numel, msgl_stream_t stream);
+/* Checkpoint ingest (WeightLoader, src/model/weight.cpp:32-105, with the name maps of
+ * qwen3.cpp:94-166 / qwen3_moe.cpp:123-199): every *.safetensors file of model_dir is indexed
+ * by its JSON header; model.embed_tokens / model.norm / lm_head (the embedding when absent:
+ * tied) and per layer input_layernorm, post_attention_layernorm, self_attn.{qkv_proj | q_proj +
+ * k_proj + v_proj, q_norm, k_norm, o_proj}, mlp.{gate_up_proj | gate_proj + up_proj, down_proj}
+ * (MoE: mlp.gate and mlp.experts.<e>.{gate_up_proj | gate_proj + up_proj, down_proj}) go
+ * through msgl_model_set_weight. BF16 is copied, F16 / F32 rounded to bf16 (nearest even). A
+ * missing tensor or a malformed header is MSGL_ERR_INVALID_ARG with the name in
+ * msgl_last_error(). msgl_safetensors_index only reads the headers (host only, no device). */
+MSGL_API int msgl_model_load_safetensors(msgl_model* m, const char* model_dir, msgl_stream_t stream);
+MSGL_API int msgl_safetensors_index(const char* model_dir, int64_t* num_tensors, int64_t* total_bytes);
+/* The configuration the executor was created with. */
+MSGL_API int msgl_model_get_config(const msgl_model* m, msgl_model_config* out);
 /* Device bytes held by weights / KV pools / workspace. */
 MSGL_API int64_t msgl_model_weight_bytes(const msgl_model* m);
 

@@ -644,6 +644,12 @@ int msgl_model_set_weight(msgl_model* m, const char* name, const uint16_t* host_
 
 int64_t msgl_model_weight_bytes(const msgl_model* m) { return m ? m->m.weight_bytes() : 0; }
 
+int msgl_model_get_config(const msgl_model* m, msgl_model_config* out) {
+    if (!m || !out) return msgl::set_error(MSGL_ERR_INVALID_ARG, "get_config: null");
+    *out = m->m.cfg;
+    return MSGL_OK;
+}
+
 int msgl_model_alloc_kv(msgl_model* m, int num_pages, int page_size, msgl_stream_t stream) {
     if (!m) return msgl::set_error(MSGL_ERR_INVALID_ARG, "null model");
     return guarded([&] { alloc_kv(m->m, num_pages, page_size, stream); });

@@ -69,6 +69,9 @@ SIGNATURES = {
     "msgl_model_random_init": (I, [P, U64, F, P]),
     "msgl_model_set_weight": (I, [P, C.c_char_p, P, I64, P]),
     "msgl_model_weight_bytes": (I64, [P]),
+    "msgl_model_load_safetensors": (I, [P, C.c_char_p, P]),
+    "msgl_safetensors_index": (I, [C.c_char_p, P, P]),
+    "msgl_model_get_config": (I, [P, P]),
     "msgl_model_alloc_kv": (I, [P, I, I, P]),
     "msgl_model_kv_pool": (I, [P, I, P, P, P]),
     "msgl_model_forward": (I, [P, P, P, P, I, P]),

@@ -9,6 +9,7 @@ pages per request (the reference allocates one page per token, D12).
 from __future__ import annotations
 
 import ctypes as C
+import os
 from dataclasses import dataclass, field
 
 import numpy as np
@@ -197,6 +198,10 @@ class Qwen3Model:
 
     def weight_bytes(self) -> int:
         return self.L.msgl_model_weight_bytes(self.h)
+
+    def load_safetensors(self, model_dir: str):
+        """Weights from a Hugging Face safetensors checkpoint directory (msgl_model_load_safetensors)."""
+        check(self.L.msgl_model_load_safetensors(self.h, os.fsencode(model_dir), _s()))
 
     def alloc_kv(self, num_pages: int, page_size: int = 16):
         check(self.L.msgl_model_alloc_kv(self.h, num_pages, page_size, _s()))
