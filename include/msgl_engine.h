@@ -58,6 +58,25 @@ typedef struct {
 } msgl_batch;
 #define MSGL_SHARED_PREFIX_DETECT (-1)
 
+/* ------------------------------------------------------------------ prefix cache (host)
+ * RadixCache (src/cache/kvcache.cpp:40-115) at page granularity, with its insert / split /
+ * eviction defects fixed: match walks the longest cached prefix of whole pages (splitting a
+ * node where it ends inside one), insert adds the uncached pages and reports the caller's
+ * pages for the cached part that differ from the tree's (to return to the free list), lock
+ * (+1 / -1) pins the path of a node for a running request, evict frees up to num_pages pages of
+ * unlocked leaves, least recently used first (ties: the lower page id), one page at a time from
+ * the leaf's end. Node handles: 0 is the root; a handle stays valid until its node is evicted. */
+typedef struct msgl_radix msgl_radix;
+MSGL_API int msgl_radix_create(int page_size, msgl_radix** out);
+MSGL_API int msgl_radix_destroy(msgl_radix* r);
+MSGL_API int msgl_radix_match(msgl_radix* r, const int32_t* tokens, int num_tokens, int32_t* pages_out,
+                              int max_pages, int* matched_tokens, int64_t* node);
+MSGL_API int msgl_radix_insert(msgl_radix* r, const int32_t* tokens, int num_tokens, const int32_t* pages,
+                               int* present_tokens, int32_t* dup_pages_out, int* num_dup, int64_t* node);
+MSGL_API int msgl_radix_lock(msgl_radix* r, int64_t node, int delta);
+MSGL_API int msgl_radix_evict(msgl_radix* r, int num_pages, int32_t* freed_out, int* num_freed);
+MSGL_API int msgl_radix_size(const msgl_radix* r, int* cached_pages, int* evictable_pages);
+
 MSGL_API int msgl_model_create(const msgl_model_config* cfg, msgl_model** out);
 MSGL_API int msgl_model_destroy(msgl_model* m);
 

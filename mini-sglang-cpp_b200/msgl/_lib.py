@@ -72,6 +72,13 @@ SIGNATURES = {
     "msgl_model_load_safetensors": (I, [P, C.c_char_p, P]),
     "msgl_safetensors_index": (I, [C.c_char_p, P, P]),
     "msgl_model_get_config": (I, [P, P]),
+    "msgl_radix_create": (I, [I, P]),
+    "msgl_radix_destroy": (I, [P]),
+    "msgl_radix_match": (I, [P, P, I, P, I, P, P]),
+    "msgl_radix_insert": (I, [P, P, I, P, P, P, P, P]),
+    "msgl_radix_lock": (I, [P, I64, I]),
+    "msgl_radix_evict": (I, [P, I, P, P]),
+    "msgl_radix_size": (I, [P, P, P]),
     "msgl_model_alloc_kv": (I, [P, I, I, P]),
     "msgl_model_kv_pool": (I, [P, I, P, P, P]),
     "msgl_model_forward": (I, [P, P, P, P, I, P]),

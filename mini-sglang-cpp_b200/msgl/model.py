@@ -91,6 +91,56 @@ class PagePool:
         return len(self.free)
 
 
+class RadixCache:
+    """msgl_radix_*: the page-granular prefix cache (host side)."""
+
+    def __init__(self, page_size: int = 16):
+        self.L = lib()
+        self.P = page_size
+        h = C.c_void_p()
+        check(self.L.msgl_radix_create(page_size, C.byref(h)))
+        self.h = h
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            self.L.msgl_radix_destroy(self.h)
+            self.h = None
+
+    def match(self, tokens):
+        t = np.ascontiguousarray(tokens, np.int32)
+        out = np.zeros(max(1, len(t) // self.P), np.int32)
+        m, node = C.c_int(0), C.c_int64(0)
+        check(self.L.msgl_radix_match(self.h, t.ctypes.data, len(t), out.ctypes.data, out.size,
+                                      C.byref(m), C.byref(node)))
+        return m.value, out[: m.value // self.P].tolist(), node.value
+
+    def insert(self, tokens, pages):
+        """Returns (tokens already cached, the caller's pages to free, node)."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        pg = np.ascontiguousarray(pages, np.int32)
+        if pg.size < len(t) // self.P:
+            raise ValueError("insert: fewer pages than full pages of tokens")
+        dup = np.zeros(max(1, pg.size), np.int32)
+        present, nd, node = C.c_int(0), C.c_int(0), C.c_int64(0)
+        check(self.L.msgl_radix_insert(self.h, t.ctypes.data, len(t), pg.ctypes.data,
+                                       C.byref(present), dup.ctypes.data, C.byref(nd), C.byref(node)))
+        return present.value, dup[: nd.value].tolist(), node.value
+
+    def lock(self, node: int, delta: int = 1):
+        check(self.L.msgl_radix_lock(self.h, node, delta))
+
+    def evict(self, num_pages: int):
+        out = np.zeros(max(1, num_pages), np.int32)
+        n = C.c_int(0)
+        check(self.L.msgl_radix_evict(self.h, num_pages, out.ctypes.data, C.byref(n)))
+        return out[: n.value].tolist()
+
+    def size(self):
+        a, b = C.c_int(0), C.c_int(0)
+        check(self.L.msgl_radix_size(self.h, C.byref(a), C.byref(b)))
+        return a.value, b.value
+
+
 @dataclass
 class Request:
     """The Req fields the step needs (include/minisgl/core/types.h:29-60)."""
