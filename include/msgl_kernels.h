@@ -130,6 +130,20 @@ MSGL_API int msgl_qknorm_rope_store_kv_partials(const float* parts, int nparts, 
                                                 int num_q_heads, int num_kv_heads, int head_dim,
                                                 float eps, msgl_stream_t stream);
 
+/* ---------------------------------------------------------------- sampling */
+/* Next-token sampling per row of fp32 logits [num_rows, vocab] with per-row SamplingParams
+ * (include/minisgl/core/types.h:12-20; device arrays temperature, top_k, top_p). Rows with
+ * temperature <= 0 or top_k == 1 take the first index of the maximum (the reference's greedy
+ * scan, scheduler.cpp:110-124). Other rows: candidates = the K largest logits (K = top_k if
+ * 1 < top_k <= 1024, else min(vocab, 1024); ties at the K-th value to the lower ids) ordered by
+ * (logit desc, id asc); weights exp((l - l_max) / temperature) summed in that order into c_i;
+ * top-p keeps the first n candidates with c_{n-1} >= top_p * c_{K-1}; with u the 24-bit
+ * SplitMix64 uniform of (seed, step, row), the token is the first i < n with c_i > u * c_{n-1}.
+ * Deterministic for a given (seed, step). */
+MSGL_API int msgl_sample(const float* logits, int num_rows, int vocab, const float* temperature,
+                         const int* top_k, const float* top_p, uint64_t seed, uint64_t step,
+                         int* out, msgl_stream_t stream);
+
 /* ---------------------------------------------------------------- batch metadata */
 /* Advances a decode batch on the device (the decode branch of Scheduler::step's host flatten,
  * src/scheduler/scheduler.cpp:83-106, with KVCachePool::allocate, src/cache/kvcache.cpp:21-28,

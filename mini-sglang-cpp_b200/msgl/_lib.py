@@ -37,6 +37,7 @@ SIGNATURES = {
     "msgl_gemm_gate_up_silu": (I, [P, P, P, I, I, I, P, SZ, P]),
     "msgl_gemm_partials_splits": (I, [I, I, I]),
     "msgl_decode_advance": (I, [P, P, P, P, P, I, P, P, P, I, I, P]),
+    "msgl_sample": (I, [P, I, I, P, P, P, U64, U64, P, P]),
     "msgl_gemm_bf16_partials": (I, [P, P, P, I, I, I, I, P]),
     "msgl_add_partials_rmsnorm": (I, [P, I, P, P, P, I, I, F, P]),
     "msgl_qknorm_rope_store_kv_partials": (I, [P, I, P, P, P, I64, P, P, P, P, P, I, I, I, I, F, P]),

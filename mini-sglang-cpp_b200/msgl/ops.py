@@ -127,6 +127,18 @@ def decode_advance(next_tokens, input_ids, positions, slot_mapping, page_table, 
                                     _p(seq_lens), _p(free_pages), _p(free_top), B, page_size, _s()))
 
 
+def sample(logits, temperature, top_k, top_p, seed=0, step=0, out=None):
+    """msgl_sample: one token id per row of fp32 logits [B, V] (per-row parameters, device)."""
+    _c(logits, torch.float32), _c(temperature, torch.float32), _c(top_k, torch.int32)
+    _c(top_p, torch.float32)
+    B, V = logits.shape
+    if out is None:
+        out = torch.empty(B, dtype=torch.int32, device=logits.device)
+    check(lib().msgl_sample(_p(logits), B, V, _p(temperature), _p(top_k), _p(top_p), seed, step,
+                            _p(out), _s()))
+    return out
+
+
 # ------------------------------------------------------------------ attention
 def attention_workspace(num_reqs, max_seq_len, hq, hkv, device="cuda"):
     n = lib().msgl_paged_attention_workspace_size(num_reqs, max_seq_len, hq, hkv, 128)
