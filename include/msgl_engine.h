@@ -127,6 +127,17 @@ MSGL_API int msgl_model_forward(msgl_model* m, const msgl_batch* batch, int* nex
  * synchronises the stream. */
 MSGL_API int msgl_model_step_host(msgl_model* m, const msgl_batch* host_batch,
                                   int* host_next_tokens, int flags, msgl_stream_t stream);
+/* Decode steps without the host in between (Scheduler::step's decode loop with the flatten of
+ * scheduler.cpp:83-106 on the device): from one decode step's device arrays (*batch, e.g. built
+ * on the host once), run num_steps greedy steps back to back; step s writes its ids to
+ * token_log[s * num_reqs ...] and, before step s + 1, msgl_decode_advance moves the arrays of
+ * *batch on in place (new pages come off the device free stack free_pages[0 .. *free_top)).
+ * Every step runs with max_seq_len = max_pages * page_size (capped at max_position), so with
+ * MSGL_FWD_GRAPH one captured graph serves every step. Nothing waits on the host: the caller
+ * synchronises the stream before reading token_log. */
+MSGL_API int msgl_model_decode_steps(msgl_model* m, const msgl_batch* batch, int num_steps,
+                                     int* token_log, const int* free_pages, int* free_top,
+                                     int flags, msgl_stream_t stream);
 
 /* Debug: device pointer to the hidden state [max_tokens, hidden] bf16 after the most recent
  * forward (the last layer's output before the final norm) -- used by per-layer parity tests

@@ -1,5 +1,6 @@
 // qwen3.cpp -- the device-side Qwen3 executor (Qwen3DecoderLayer / Qwen3ForCausalLM of
 // src/model/qwen3.cpp:16-83, 85-92, 168-180) and its C ABI (include/msgl_engine.h).
+#include <algorithm>
 #include <cmath>
 #include <cstdlib>
 #include <cstdio>
@@ -675,6 +676,36 @@ int msgl_model_step_host(msgl_model* m, const msgl_batch* host_batch, int* host_
     if (!m || !host_batch || !host_next_tokens)
         return msgl::set_error(MSGL_ERR_INVALID_ARG, "step_host: null");
     return guarded([&] { step_host(m->m, *host_batch, host_next_tokens, flags, stream); });
+}
+
+int msgl_model_decode_steps(msgl_model* m, const msgl_batch* batch, int num_steps, int* token_log,
+                            const int* free_pages, int* free_top, int flags, msgl_stream_t stream) {
+    if (!m || !batch || num_steps < 0 || (num_steps > 0 && (!token_log || !free_pages || !free_top)))
+        return msgl::set_error(MSGL_ERR_INVALID_ARG, "decode_steps: bad args");
+    return guarded([&] {
+        Model& md = m->m;
+        if (!batch->is_decode || batch->num_tokens != batch->num_reqs)
+            throw Fail(MSGL_ERR_INVALID_ARG, "decode_steps: needs a decode batch");
+        // every step runs with the same shape fields, so a captured graph serves them all; the
+        // context bound is the page-table width (the advance kernel refuses to go past it)
+        msgl_batch b = *batch;
+        b.max_seq_len = std::min(b.max_pages * md.page_size, md.cfg.max_position);
+        const int B = b.num_reqs;
+        int* next = md.st_next.as<int>();
+        auto* s = static_cast<cudaStream_t>(stream);
+        for (int st = 0; st < num_steps; ++st) {
+            run(md, b, next, nullptr, flags, s);
+            ckc(cudaMemcpyAsync(token_log + static_cast<int64_t>(st) * B, next, sizeof(int) * B,
+                                cudaMemcpyDeviceToDevice, s),
+                "decode_steps: token log");
+            if (st + 1 < num_steps)  // the arrays of *batch are advanced in place
+                ck(msgl_decode_advance(next, const_cast<int*>(b.input_ids), const_cast<int*>(b.positions),
+                                       const_cast<int*>(b.slot_mapping), const_cast<int*>(b.page_table),
+                                       b.max_pages, const_cast<int*>(b.seq_lens), free_pages, free_top,
+                                       B, md.page_size, stream),
+                   "decode_steps: advance");
+        }
+    });
 }
 
 int msgl_model_debug_hidden(msgl_model* m, void** x, float** residual) {

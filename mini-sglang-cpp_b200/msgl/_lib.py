@@ -73,6 +73,7 @@ SIGNATURES = {
     "msgl_model_load_safetensors": (I, [P, C.c_char_p, P]),
     "msgl_safetensors_index": (I, [C.c_char_p, P, P]),
     "msgl_model_get_config": (I, [P, P]),
+    "msgl_model_decode_steps": (I, [P, P, I, P, P, P, I, P]),
     "msgl_radix_create": (I, [I, P]),
     "msgl_radix_destroy": (I, [P]),
     "msgl_radix_match": (I, [P, P, I, P, I, P, P]),

@@ -270,6 +270,16 @@ class Qwen3Model:
                                         None if lg is None else lg.data_ptr(), int(graph), _s()))
         return (nxt, lg) if logits else nxt
 
+    def decode_steps(self, step: StepBatch, num_steps: int, free_pages, free_top, graph: bool = True):
+        """msgl_model_decode_steps: num_steps greedy decode steps on the device from `step` (its
+        arrays are advanced in place); returns the ids, [num_steps, B] int32 on the device."""
+        B = step.num_reqs
+        log = torch.empty(num_steps, B, dtype=torch.int32, device=step.tensors["input_ids"].device)
+        check(self.L.msgl_model_decode_steps(self.h, C.addressof(step.struct), num_steps,
+                                             log.data_ptr(), free_pages.data_ptr(),
+                                             free_top.data_ptr(), int(graph), _s()))
+        return log
+
     def set_tp(self, comm):
         self.tp = comm
         check(self.L.msgl_model_set_tp(self.h, comm.h if comm is not None else None))

@@ -149,3 +149,50 @@ def test_device_driven_decode_loop_matches_host_loop(cuda):
         runs.append(toks)
     assert runs[0] == runs[1]
     assert ops.device_error() == (0, 0)
+
+
+def test_decode_steps_matches_host_loop(cuda):
+    """msgl_model_decode_steps (a captured graph per step and the device advance between steps,
+    no host in between) gives the tokens of the host-driven loop, over page boundaries."""
+    from msgl.model import BatchBuilder, PagePool, Qwen3Model, Request
+    from test_model_gpu import CFG, weights
+    w = weights(CFG, 4)
+    model = Qwen3Model(CFG, max_tokens=128, max_reqs=4)  # the prefill has 84 tokens
+    model.set_weights(w)
+    num_pages, width, steps = 32, 6, 12
+    rng = np.random.default_rng(6)
+    prompts = [[int(t) for t in rng.integers(0, CFG["vocab"], n)] for n in (12, 29, 3, 40)]
+    runs = []
+    s = torch.cuda.Stream()
+    for mode in ("host", "device"):
+        model.alloc_kv(num_pages)
+        pool = PagePool(num_pages)
+        reqs = [Request(list(p)) for p in prompts]
+        bb = BatchBuilder(pool)
+        with torch.cuda.stream(s):
+            nxt = model.forward(bb.build(reqs, decode=False, max_pages=width))
+        torch.cuda.synchronize()
+        for r, t in zip(reqs, nxt.cpu().numpy().tolist()):
+            r.cached_len = r.device_len
+            r.input_ids.append(int(t))
+        toks = []
+        if mode == "host":
+            for _ in range(steps):
+                with torch.cuda.stream(s):
+                    nxt = model.forward(bb.build(reqs, decode=True, max_pages=width), graph=True)
+                torch.cuda.synchronize()
+                toks.append(nxt.cpu().numpy().tolist())
+                for r, t in zip(reqs, toks[-1]):
+                    r.input_ids.append(int(t))
+        else:
+            with torch.cuda.stream(s):
+                sb = bb.build(reqs, decode=True, max_pages=width)
+                free = torch.tensor(pool.free + [0], dtype=torch.int32, device="cuda")
+                top = torch.tensor([len(pool.free)], dtype=torch.int32, device="cuda")
+                log = model.decode_steps(sb, steps, free, top, graph=True)
+            torch.cuda.synchronize()
+            toks = log.cpu().numpy().tolist()
+        runs.append(toks)
+    assert runs[0] == runs[1]
+    from msgl import ops
+    assert ops.device_error() == (0, 0)
