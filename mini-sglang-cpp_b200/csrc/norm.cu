@@ -130,6 +130,61 @@ int launch_norm(const T* x_in, T* x_out, float* resid, const T* w, const int* id
     return MSGL_OK;
 }
 
+// The same for rows of up to 4096 elements with at most 16 partials: one thread per 4 elements
+// (float4), up to 10 partial loads of a thread issued before the first add, so a row of up to
+// 10 partials costs one L2 round trip.
+constexpr int kPartNormWide = 1024;
+constexpr int kPartNormWideMaxParts = 16;
+constexpr int kPartNormWideBatch = 10;  // loads in flight per thread (64 registers at 1024 threads)
+
+__global__ void __launch_bounds__(kPartNormWide, 1)
+add_partials_rmsnorm_wide_kernel(const float* __restrict__ parts, int nparts,
+                                 __nv_bfloat16* __restrict__ x_out, float* __restrict__ resid,
+                                 const __nv_bfloat16* __restrict__ w, int hidden, float eps) {
+    __shared__ float red[32];
+    pdl_wait();
+    pdl_trigger();
+    const int row = blockIdx.x;
+    const int e0 = threadIdx.x * 4;
+    const bool active = e0 < hidden;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * hidden;
+    const int64_t off = static_cast<int64_t>(row) * hidden + e0;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    float ss = 0.f;
+    uint2 wb = make_uint2(0u, 0u);
+    if (active) {
+        const float4 r = *reinterpret_cast<const float4*>(resid + off);
+        wb = *reinterpret_cast<const uint2*>(w + e0);
+        for (int p0 = 0; p0 < nparts; p0 += kPartNormWideBatch) {
+            float4 t[kPartNormWideBatch];
+#pragma unroll
+            for (int u = 0; u < kPartNormWideBatch; ++u)
+                if (p0 + u < nparts) t[u] = *reinterpret_cast<const float4*>(parts + (p0 + u) * stride + off);
+#pragma unroll
+            for (int u = 0; u < kPartNormWideBatch; ++u)
+                if (p0 + u < nparts) {
+                    v.x += t[u].x; v.y += t[u].y; v.z += t[u].z; v.w += t[u].w;
+                }
+        }
+        v.x += r.x; v.y += r.y; v.z += r.z; v.w += r.w;
+        ss = v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        *reinterpret_cast<float4*>(resid + off) = v;
+    }
+    ss = warp_sum(ss);
+    const int nw = (blockDim.x + 31) >> 5;
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+    for (int i = 0; i < nw; ++i) tot += red[i];
+    const float inv_rms = 1.0f / sqrtf(tot / static_cast<float>(hidden) + eps);
+    if (active) {
+        uint2 o;
+        o.x = pack_bf16x2(v.x * inv_rms * bf16lo(wb.x), v.y * inv_rms * bf16hi(wb.x));
+        o.y = pack_bf16x2(v.z * inv_rms * bf16lo(wb.y), v.w * inv_rms * bf16hi(wb.y));
+        *reinterpret_cast<uint2*>(x_out + off) = o;
+    }
+}
+
 // residual += sum_p P[p]; x = rmsnorm(residual) * w, with P the fp32 split-K partials
 // [nparts][rows][hidden] of the projection before the norm, added in p order, then the residual
 // (as forward_fused_add adds x to the residual). One CTA of up to 512 threads per row, VPT
@@ -270,6 +325,14 @@ int msgl_add_partials_rmsnorm(const float* parts, int nparts, void* x_out, float
          reinterpret_cast<uintptr_t>(weight) | reinterpret_cast<uintptr_t>(residual)) & 15)
         return set_error(MSGL_ERR_INVALID_ARG, "add_partials_rmsnorm: pointers must be 16-byte aligned");
     if (num_tokens == 0) return MSGL_OK;
+    if (hidden <= 4 * kPartNormWide && nparts <= kPartNormWideMaxParts) {
+        const int threads = ((hidden / 4 + 31) / 32) * 32;
+        launch_pdl(add_partials_rmsnorm_wide_kernel, dim3(num_tokens), dim3(threads), 0, stream,
+                   parts, nparts, static_cast<__nv_bfloat16*>(x_out), residual,
+                   static_cast<const __nv_bfloat16*>(weight), hidden, eps);
+        MSGL_LAUNCH_CHECK();
+        return MSGL_OK;
+    }
     const int vecs = hidden / 8;
     const int vpt = vecs > kPartNormThreads ? 2 : 1;
     const int threads = ((vecs / vpt + (vecs % vpt ? 1 : 0) + 31) / 32) * 32;

@@ -87,7 +87,10 @@ def test_gemm_partials_rejects_bad_sizes(cuda):
     assert ops.device_error() == (0, 0)
 
 
-@pytest.mark.parametrize("P,T,H", [(1, 5, 1024), (4, 128, 4096), (3, 17, 2048), (16, 2, 4096)])
+# hidden <= 4096 with <= 16 partials: the one-thread-per-4-elements kernel (one or two load
+# batches); (2, 3, 5120) and (20, 4, 1024): the 8-elements-per-thread kernel
+@pytest.mark.parametrize("P,T,H", [(1, 5, 1024), (4, 128, 4096), (3, 17, 2048), (16, 2, 4096),
+                                   (9, 128, 4096), (2, 3, 5120), (20, 4, 1024)])
 def test_add_partials_rmsnorm(cuda, oracle, P, T, H):
     from msgl import ops
     rng = np.random.default_rng(P * 100 + T)
