@@ -44,6 +44,8 @@ UNIT = "tokens/s"
 CFG8B = dict(num_layers=36, hidden=4096, num_q_heads=32, num_kv_heads=8, head_dim=128,
              inter=12288, vocab=151936, eps=1e-6, rope_base=1e6, max_position=4096)
 BATCH, CTX, PREFIX, PAGE = 128, 2048, 1024, 16
+# host threads of the CPU reference (fixed, so the baseline does not follow the host's core count)
+CPU_THREADS = 16
 
 
 def workload_config(n_gpus):
@@ -83,9 +85,8 @@ def decode_batch_host(pt, vocab, seed=1):
 
 # ------------------------------------------------------------------------------ clocks
 # DRAM bytes (read + write) of one paged_decode_cascade_kernel launch at this workload (8 kv
-# heads), from the ncu capture summarised in
-# profiles/paged_decode_cascade_b128_ctx2048_prefix1024_hkv8.md (547 404 544 B read + 11 156 224 B
-# written; the algorithmic unique K+V bytes are 541 065 216 B).
+# heads), from one ncu capture of `bench.py --case attention_cascade` (547 404 544 B read +
+# 11 156 224 B written; the algorithmic unique K+V bytes are 541 065 216 B).
 PAGED_DECODE_TRAFFIC_BYTES = 558_560_768
 
 
@@ -164,8 +165,8 @@ class CpuReference:
     def __init__(self, threads=None):
         from oracle import Oracle, RefLib
         self.ref, self.orc = RefLib(), Oracle()
-        t = threads or os.cpu_count() or 1
-        self.threads = max(1, min(t, 64))
+        t = threads or min(CPU_THREADS, os.cpu_count() or 1)
+        self.threads = max(1, t)
         H, I, V, D = CFG8B["hidden"], CFG8B["inter"], CFG8B["vocab"], 128
         hq, hkv = CFG8B["num_q_heads"], CFG8B["num_kv_heads"]
         self.dims = (H, V, D, hq, hkv)
@@ -238,14 +239,131 @@ def run_reference_arm(args, rank):
     value = float(np.median(vals))
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1000.0 * BATCH / value, "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": 1000.0 * BATCH / value, "extrapolated": True,
+            "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": workload_config(args.gpus),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "reference",
-                             "sample": sample},
+                             "sample": sample, "extrapolated": True},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
+
+
+# ------------------------------------------------------------------------------ timing
+def timed_blocks(fn, args, world, dev, stream, barrier, max_over_ranks):
+    """`args.blocks` back-to-back blocks of exactly `args.steps` steps, each bracketed by a barrier
+    and a device synchronise; returns each block's ms per step (max over ranks). Before each
+    block the ranks meet on the device (a one-element NCCL all-reduce on the timing stream), so
+    the start event fires on every rank once all ranks have arrived: launch skew between ranks
+    stays outside the timed region."""
+    import torch
+    import torch.distributed as dist
+    out = []
+    for _ in range(args.blocks):
+        barrier()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.all_reduce(torch.zeros(1, device=dev))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        out.append(max_over_ranks(e0.elapsed_time(e1) / args.steps))
+    return out
+
+
+# ------------------------------------------------------------------------------ parity record
+PARITY_CFG = dict(num_layers=3, hidden=512, num_q_heads=8, num_kv_heads=2, head_dim=128, inter=768,
+                  vocab=1000, eps=1e-6, rope_base=1e6, max_position=512, page_size=16)
+
+
+def parity_case(rank, world, dev):
+    """The executor at this run's tensor-parallel size on a small Qwen3 (3 layers, hidden 512,
+    8 q / 2 kv heads, head_dim 128, vocab 1000; weights N(0, 0.05) from the device generator,
+    norm gains 1): prefill of 3 requests (5, 20, 33 tokens) + 3 greedy decode steps, on its own
+    communicator. Rank 0 compares every step's all-gathered logits with the oracle; every rank's
+    logits must be the same bits. Returns the record printed in the bench line."""
+    import hashlib
+
+    import torch
+    import torch.distributed as dist
+
+    from msgl import ops
+    from msgl.model import BatchBuilder, PagePool, Qwen3Model, Request, TPComm
+    cfg = PARITY_CFG
+    H, D, hq, hkv, I, V = 512, 128, 8, 2, 768, 1000
+    names = [("embed", (V, H))]
+    for l in range(cfg["num_layers"]):
+        p = f"layers.{l}."
+        names += [(p + "input_ln", (H,)), (p + "qkv", ((hq + 2 * hkv) * D, H)), (p + "q_norm", (D,)),
+                  (p + "k_norm", (D,)), (p + "o", (H, hq * D)), (p + "post_ln", (H,)),
+                  (p + "gate_up", (2 * I, H)), (p + "down", (H, I))]
+    names += [("norm", (H,)), ("lm_head", (V, H))]
+    comm = None
+    if world > 1:
+        uid = [TPComm.new_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = TPComm(rank, world, uid[0])
+    model = Qwen3Model(cfg, max_tokens=128, max_reqs=4, tp_rank=rank, tp_size=world)
+    wts = {}
+    for i, (n, shape) in enumerate(names):
+        if len(shape) == 1:
+            bits = np.full(shape, 0x3F80, np.uint16)
+        else:
+            t = ops.fill_normal_(torch.empty(shape, dtype=torch.bfloat16, device=dev), seed=11,
+                                 stream_id=i, std=0.05)
+            bits = t.view(torch.int16).cpu().numpy().view(np.uint16)
+        model.set_weight_bits(n, bits)
+        wts[n] = bits
+    if comm is not None:
+        model.set_tp(comm)
+    model.alloc_kv(32)
+    orc = None
+    if rank == 0:
+        from oracle import Oracle, OracleModel, from_bf16_bits
+        orc = OracleModel(Oracle(), cfg, {k: from_bf16_bits(v).reshape(v.shape) for k, v in wts.items()},
+                          num_slots=32 * 16)
+    rng = np.random.default_rng(1)
+    reqs = [Request(list(rng.integers(0, V, n))) for n in (5, 20, 33)]
+    bb = BatchBuilder(PagePool(32))
+    worst, agree, total, clear_ok, digests = 0.0, 0, 0, True, []
+    for step in range(4):
+        sb = bb.build(reqs, decode=step > 0, device=dev, max_pages=4)
+        nxt, lg = model.forward(sb, logits=True)
+        torch.cuda.synchronize()
+        got, ids = lg.cpu().numpy(), nxt.cpu().numpy()
+        digests.append(hashlib.sha1(got.tobytes() + ids.tobytes()).hexdigest())
+        if orc is not None:
+            h = {k: v.cpu().numpy() for k, v in sb.tensors.items()}
+            ref = orc.forward(h["input_ids"], h["positions"], h["slot_mapping"], h["page_table"],
+                              h["seq_lens"], h["q_indptr"])
+            worst = max(worst, float(np.linalg.norm(got - ref) / np.linalg.norm(ref)))
+            top2 = np.sort(ref, axis=1)[:, -2:]
+            clear = (top2[:, 1] - top2[:, 0]) > 4 * float(np.abs(got - ref).max())
+            clear_ok &= bool(np.array_equal(ids[clear], ref.argmax(axis=1)[clear]))
+            agree += int((ids == ref.argmax(axis=1)).sum())
+            total += ids.size
+        for r, t in zip(reqs, ids):
+            r.cached_len = r.device_len
+            r.input_ids.append(int(t))
+    same = True
+    if world > 1:
+        allg = [None] * world
+        dist.all_gather_object(allg, digests)
+        same = all(a == allg[0] for a in allg)
+    err = ops.device_error()
+    del model
+    if comm is not None:
+        comm.close()
+    return {"case": f"qwen3 3 layers h512 8/2 heads vocab 1000, tp{world}, prefill + 3 decode "
+                    "steps vs the fp32 oracle", "max_rel_l2": worst, "tol": 2e-2,
+            "ids_equal": f"{agree}/{total}", "margin_clear_ids_equal": clear_ok,
+            "ranks_identical": same,
+            "pass": bool(worst < 2e-2 and clear_ok and same and err == (0, 0))}
 
 
 # ------------------------------------------------------------------------------ our arm
@@ -265,6 +383,7 @@ def run_ours(args, rank, world, local_rank):
     msgl.lib()
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
+    parity = parity_case(rank, world, dev)
 
     # tensor parallel over the `world` GPUs: every rank runs the same 128-request step on its
     # shard (heads / FFN columns / vocab rows); NCCL id from rank 0 through the process group
@@ -305,21 +424,23 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    # ---- value: device-resident inputs, graph replay
+    lib = msgl.lib()
+    sp = stream.cuda_stream
+    # kernels of ours per step, counted on one eager step (graph replays launch nothing from the
+    # host, so the count is taken outside them)
+    n0 = lib.msgl_kernel_launches()
+    model.forward(sb, out=nxt)
+    launches_per_step = lib.msgl_kernel_launches() - n0
+    torch.cuda.synchronize()
+
+    # ---- value: device-resident inputs, graph replay; several blocks of `steps` steps
     for _ in range(max(args.warmup, 3)):
         model.forward(sb, out=nxt, graph=True)
     torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clk:
-        e0.record(stream)
-        for _ in range(args.steps):
-            model.forward(sb, out=nxt, graph=True)
-        e1.record(stream)
-        torch.cuda.synchronize()
-    barrier()
-    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+        blocks = timed_blocks(lambda: model.forward(sb, out=nxt, graph=True), args, world, dev,
+                              stream, barrier, max_over_ranks)
+    ms = float(np.median(blocks))
     err = ops.device_error()
     assert err == (0, 0), f"device error word {err}"
 
@@ -330,20 +451,12 @@ def run_ours(args, rank, world, local_rank):
                                                   "page_table", "seq_lens", "q_indptr",
                                                   "last_idx")], SHARED_PREFIX_DETECT)
     out_host = torch.empty(BATCH, dtype=torch.int32).pin_memory()
-    lib = msgl.lib()
-    sp = stream.cuda_stream
+    step_host = lambda: msgl.check(lib.msgl_model_step_host(model.h, C.addressof(hb),
+                                                            out_host.data_ptr(), 1, sp))
     for _ in range(max(args.warmup, 3)):
-        msgl.check(lib.msgl_model_step_host(model.h, C.addressof(hb), out_host.data_ptr(), 1, sp))
-    barrier()
-    torch.cuda.synchronize()
-    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e2.record(stream)
-    for _ in range(args.steps):
-        msgl.check(lib.msgl_model_step_host(model.h, C.addressof(hb), out_host.data_ptr(), 1, sp))
-    e3.record(stream)
-    torch.cuda.synchronize()
-    barrier()
-    ms_e2e = max_over_ranks(e2.elapsed_time(e3) / args.steps)
+        step_host()
+    blocks_e2e = timed_blocks(step_host, args, world, dev, stream, barrier, max_over_ranks)
+    ms_e2e = float(np.median(blocks_e2e))
     h2d = sum(v.nbytes for v in host.values())
     d2h = BATCH * 4
     assert torch.equal(out_host.to(dev), nxt), "host step and device step disagree"
@@ -390,7 +503,6 @@ def run_ours(args, rank, world, local_rank):
     peak = peaks.get("hbm_gbs", 6650.0)
     achieved = unique_bytes / (attn_ms * 1e-3) / 1e9
 
-    launches_per_step = 1 + L * 8 - 1 + 1 + 2
     if rank == 0:
         cpu = CpuReference()
         cpu.sample()
@@ -400,13 +512,14 @@ def run_ours(args, rank, world, local_rank):
         line = {
             "metric": METRIC, "value": BATCH / (ms * 1e-3), "unit": UNIT,
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+            "blocks_ms_per_step": [round(b, 4) for b in blocks],
+            "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (random-init weights, N(0,1) KV, random token ids)",
             "config": workload_config(world),
             "e2e": {"value": BATCH / (ms_e2e * 1e-3), "unit": UNIT,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": ms_e2e},
+                    "ms_per_step": ms_e2e, "blocks_ms_per_step": [round(b, 4) for b in blocks_e2e]},
             "roofline": {"kernel": "paged_decode_cascade_kernel", "bound": "hbm",
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
@@ -420,6 +533,8 @@ def run_ours(args, rank, world, local_rank):
                              "sample": sample},
             "clocks": clk.summary(),
             "gpu_launches": launches_per_step * args.steps,
+            "gpu_launches_per_step": launches_per_step,
+            "parity": parity,
             "weights_gb": model.weight_bytes() / 1e9,
         }
         print(json.dumps(line), flush=True)
@@ -633,6 +748,8 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--blocks", type=int, default=3,
+                    help="timed blocks of --steps steps each; the median block is reported")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--case", choices=["attention", "attention_cascade", "gemm", "gemm_qkv",
                                        "gemm_partials", "gemm_prefill", "breakdown"], default=None,

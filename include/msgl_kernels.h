@@ -59,6 +59,10 @@ MSGL_API const char* msgl_last_error(void);
 /* Synchronises `stream`, then reads the device error word of the current device (code and an
  * info word naming the failing site); reset != 0 clears it. */
 MSGL_API int msgl_device_error(int* code, int* info, int reset, msgl_stream_t stream);
+/* Number of kernels this library has launched from the host so far, over all threads and
+ * devices (replays of a captured CUDA graph launch nothing from the host and are not counted;
+ * NCCL's own kernels are not counted). */
+MSGL_API unsigned long long msgl_kernel_launches(void);
 
 /* ---------------------------------------------------------------- reference launchers */
 /* launch_rmsnorm (kernels.h:13-14; kernels/cuda/rmsnorm.cu:37-43; semantics of
@@ -319,6 +323,10 @@ MSGL_API int msgl_tp_rank(const msgl_tp* tp);
 MSGL_API int msgl_tp_world(const msgl_tp* tp);
 /* TPCommunicator::all_reduce_sum (tp.cpp:18-31): in-place sum of bf16 x [n] over the ranks. */
 MSGL_API int msgl_tp_all_reduce_sum(msgl_tp* tp, void* x, int64_t n, msgl_stream_t stream);
+/* TPCommunicator::all_gather (tp.cpp:33-47; a stub in the reference): every rank contributes
+ * `bytes` bytes of `send`; `recv` receives world * bytes, rank q's contribution at q * bytes. */
+MSGL_API int msgl_tp_all_gather(msgl_tp* tp, const void* send, void* recv, size_t bytes,
+                                msgl_stream_t stream);
 /* Row-parallel projection output x [T, H] (this rank's partial sum) all-reduced, then
  * msgl_add_rmsnorm (residual += x; x = rmsnorm(residual) * w; first as in msgl_add_rmsnorm). */
 MSGL_API int msgl_tp_allreduce_add_rmsnorm(msgl_tp* tp, void* x, float* residual,

@@ -34,6 +34,11 @@ int* device_error_word() {
     return ptrs[dev];
 }
 
+std::atomic<unsigned long long>& launch_counter() {
+    static std::atomic<unsigned long long> n{0};
+    return n;
+}
+
 bool pdl_enabled() {
     static const bool on = [] {
         const char* v = getenv("MSGL_PDL");
@@ -169,6 +174,8 @@ extern "C" {
 const char* msgl_version(void) { return "msgl-b200 0.1.0 (sm_100a)"; }
 
 const char* msgl_last_error(void) { return t_last_error.c_str(); }
+
+unsigned long long msgl_kernel_launches(void) { return launch_counter().load(); }
 
 int msgl_device_error(int* code, int* info, int reset, msgl_stream_t stream) {
     if (cudaStreamSynchronize(stream) != cudaSuccess)

@@ -975,6 +975,26 @@ size_t cascade_workspace_bytes(int B, const CascadePlan& cp, int hq) {
            up(static_cast<size_t>(B) * cp.max_chunks * hq * 2 * sizeof(float));
 }
 
+// Argument checks of the plain decode entry points (msgl_paged_attention_decode and the
+// no-allocation variant), done before anything is queued on the stream; fills the plan.
+int check_decode(int64_t num_slots, int max_pages, int num_reqs, int max_seq_len, int hq, int hkv,
+                 int head_dim, int page_size, DecodePlan* plan) {
+    int rc = check_common(hq, hkv, head_dim, page_size, num_slots);
+    if (rc) return rc;
+    if (num_reqs < 0 || max_seq_len < 0 || max_pages <= 0)
+        return set_error(MSGL_ERR_INVALID_ARG, "decode: bad sizes");
+    if (num_reqs == 0) return MSGL_OK;
+    if ((max_seq_len + kPage - 1) / kPage > max_pages)
+        return set_error(MSGL_ERR_INVALID_ARG, "decode: max_seq_len exceeds page-table width");
+    *plan = plan_decode(num_reqs, max_seq_len, hq, hkv);
+    const int n_hg = hkv / decode_heads_per_cta(hkv);
+    if (num_reqs > 65535 || n_hg > 65535)
+        return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "decode: num_reqs or Hkv too large");
+    if (plan->bytes > 0 && static_cast<size_t>(num_reqs) * n_hg * sizeof(int) > kDecodeCounterBytes)
+        return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "decode: num_reqs * Hkv / 4 > 65536");
+    return MSGL_OK;
+}
+
 }  // namespace
 }  // namespace msgl
 
@@ -994,22 +1014,15 @@ int msgl_paged_attention_decode(const void* q, const void* k_pool, const void* v
                                 int num_q_heads, int num_kv_heads, int head_dim, int page_size,
                                 float scale, void* out, void* workspace,
                                 size_t workspace_bytes, msgl_stream_t stream) {
-    int rc = check_common(num_q_heads, num_kv_heads, head_dim, page_size, num_slots);
+    DecodePlan p{};
+    int rc = check_decode(num_slots, max_pages, num_reqs, max_seq_len, num_q_heads, num_kv_heads,
+                          head_dim, page_size, &p);
     if (rc) return rc;
-    if (num_reqs < 0 || max_seq_len < 0 || max_pages <= 0)
-        return set_error(MSGL_ERR_INVALID_ARG, "decode: bad sizes");
     if (num_reqs == 0) return MSGL_OK;
-    if ((max_seq_len + kPage - 1) / kPage > max_pages)
-        return set_error(MSGL_ERR_INVALID_ARG, "decode: max_seq_len exceeds page-table width");
-    DecodePlan p = plan_decode(num_reqs, max_seq_len, num_q_heads, num_kv_heads);
     if (p.bytes > 0 && (!workspace || workspace_bytes < p.bytes))
         return set_error(MSGL_ERR_WORKSPACE, "decode: workspace too small");
     const int hc = decode_heads_per_cta(num_kv_heads);
     const int n_hg = num_kv_heads / hc;
-    if (num_reqs > 65535 || n_hg > 65535)
-        return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "decode: num_reqs or Hkv too large");
-    if (p.bytes > 0 && static_cast<size_t>(num_reqs) * n_hg * sizeof(int) > kDecodeCounterBytes)
-        return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "decode: num_reqs * Hkv / 4 > 65536");
     CUtensorMap tk, tv;
     rc = make_decode_maps(&tk, &tv, k_pool, v_pool, num_slots, num_kv_heads, hc);
     if (rc) return rc;
@@ -1017,12 +1030,9 @@ int msgl_paged_attention_decode(const void* q, const void* k_pool, const void* v
     if (!err) return set_error(MSGL_ERR_CUDA, "device error word unavailable");
     const size_t smem = kDecStages * kDecStageBytes + 2 * kDecStages * 8 + 16 +
                         kMaxChunkPages * sizeof(int) + 1024;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaFuncSetAttribute(paged_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem));
-        attr_set = true;
-    }
+    static std::atomic<int> optin[kMaxDevices];
+    cudaError_t e = smem_optin(paged_decode_kernel, smem, optin);
+    if (e != cudaSuccess) return set_error(MSGL_ERR_CUDA, cudaGetErrorString(e));
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     dim3 grid(p.max_chunks, n_hg, num_reqs);
     const float sl2e = scale * 1.4426950408889634f;
@@ -1054,12 +1064,9 @@ int msgl_paged_attention_extend(const void* q, const void* k_pool, const void* v
     if (!err) return set_error(MSGL_ERR_CUDA, "device error word unavailable");
     const size_t smem = kExtendStages * kPageSlotBytes + 2 * kExtendStages * 8 +
                         kExtendPageBatch * sizeof(int) + 1024;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaFuncSetAttribute(paged_extend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem));
-        attr_set = true;
-    }
+    static std::atomic<int> optin[kMaxDevices];
+    cudaError_t e = smem_optin(paged_extend_kernel, smem, optin);
+    if (e != cudaSuccess) return set_error(MSGL_ERR_CUDA, cudaGetErrorString(e));
     const int group = num_q_heads / num_kv_heads;
     const int tile_tokens = kConsumerWarps * (16 / group);
     dim3 grid((max_q_len + tile_tokens - 1) / tile_tokens, num_kv_heads, num_reqs);
@@ -1112,12 +1119,9 @@ int msgl_paged_attention_decode_cascade(const void* q, const void* k_pool, const
     if (!err) return set_error(MSGL_ERR_CUDA, "device error word unavailable");
     const size_t smem = kDecStages * kDecStageBytes + 2 * kDecStages * 8 + 16 +
                         (kPreRows + kMaxChunkPages) * sizeof(int) + 1024;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaFuncSetAttribute(paged_decode_cascade_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem));
-        attr_set = true;
-    }
+    static std::atomic<int> optin[kMaxDevices];
+    cudaError_t e = smem_optin(paged_decode_cascade_kernel, smem, optin);
+    if (e != cudaSuccess) return set_error(MSGL_ERR_CUDA, cudaGetErrorString(e));
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     const size_t o_bytes = (static_cast<size_t>(num_reqs) * cp.max_chunks * num_q_heads * kHd * sizeof(float) + 255) & ~size_t(255);
     const int grid = cp.n_pre + cp.chunks_sfx * cp.n_hg * num_reqs;
@@ -1142,41 +1146,44 @@ int msgl_paged_attention_decode_noalloc(const void* q, const void* k_pool, const
                                         int num_q_heads, int num_kv_heads, int head_dim,
                                         int page_size, float scale, void* out,
                                         msgl_stream_t stream) {
-    if (num_reqs < 0 || num_kv_heads <= 0 || head_dim != kHd)
-        return set_error(MSGL_ERR_INVALID_ARG, "decode_noalloc: bad sizes");
-    const size_t need = msgl_paged_attention_workspace_size(num_reqs, max_seq_len, num_q_heads,
-                                                            num_kv_heads, head_dim);
-    if (need > kNoAllocScratchBytes) {
+    // every argument check of the workspace entry point runs first: a rejected call queues
+    // nothing on the stream
+    DecodePlan p{};
+    int rc = check_decode(num_slots, max_pages, num_reqs, max_seq_len, num_q_heads, num_kv_heads,
+                          head_dim, page_size, &p);
+    if (rc) return rc;
+    if (num_reqs == 0) return MSGL_OK;
+    if (p.bytes > kNoAllocScratchBytes) {
         char buf[256];
         snprintf(buf, sizeof(buf),
                  "decode_noalloc: this batch needs %zu bytes of scratch; the static scratch holds "
                  "%zu (8 MiB) -- use msgl_paged_attention_decode with a workspace",
-                 need, kNoAllocScratchBytes);
+                 p.bytes, kNoAllocScratchBytes);
         return set_error(MSGL_ERR_WORKSPACE, buf);
     }
-    static void* ptrs[64] = {nullptr};
+    static void* ptrs[kMaxDevices] = {nullptr};
     static std::mutex mu;
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
         return set_error(MSGL_ERR_CUDA, "decode_noalloc: no current device");
     void* scratch = nullptr;
     {
         std::lock_guard<std::mutex> lock(mu);
         if (!ptrs[dev]) {
-            void* p = nullptr;
-            cudaError_t e = cudaGetSymbolAddress(&p, g_decode_scratch);
-            if (e != cudaSuccess || !p)
+            void* ptr = nullptr;
+            cudaError_t e = cudaGetSymbolAddress(&ptr, g_decode_scratch);
+            if (e != cudaSuccess || !ptr)
                 return set_error(MSGL_ERR_CUDA, e != cudaSuccess ? cudaGetErrorString(e)
                                                                  : "decode_noalloc: null scratch");
-            ptrs[dev] = p;
+            ptrs[dev] = ptr;
         }
         scratch = ptrs[dev];
     }
-    if (need > 0) {  // arrival counters at offset 0 must start at zero
+    if (p.bytes > 0) {  // arrival counters at offset 0 must start at zero
         const size_t cnt_bytes = static_cast<size_t>(num_reqs) *
                                  (num_kv_heads / decode_heads_per_cta(num_kv_heads)) * sizeof(int);
-        if (cudaMemsetAsync(scratch, 0, std::min(cnt_bytes, kDecodeCounterBytes), stream) != cudaSuccess)
-            return set_error(MSGL_ERR_CUDA, cudaGetErrorString(cudaGetLastError()));
+        const cudaError_t e = cudaMemsetAsync(scratch, 0, std::min(cnt_bytes, kDecodeCounterBytes), stream);
+        if (e != cudaSuccess) return set_error(MSGL_ERR_CUDA, cudaGetErrorString(e));
     }
     return msgl_paged_attention_decode(q, k_pool, v_pool, num_slots, page_table, max_pages,
                                        seq_lens, num_reqs, max_seq_len, num_q_heads, num_kv_heads,

@@ -12,6 +12,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <utility>
 
 #include "../../include/msgl_kernels.h"
@@ -376,6 +377,8 @@ int* device_error_word();                  // device address of {code, info} on 
 // kernel launch once every CTA of this one has issued it. MSGL_PDL=0 in the environment turns
 // the attribute off (plain stream order; the device instructions are then no-ops).
 bool pdl_enabled();
+// Host-side count of the kernels this library has launched (msgl_kernel_launches).
+std::atomic<unsigned long long>& launch_counter();
 
 template <typename... KArgs, typename... Args>
 cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
@@ -390,6 +393,30 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    launch_counter().fetch_add(1, std::memory_order_relaxed);
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// ------------------------------------------------------------ dynamic shared memory opt-in
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) applies to the CURRENT device only, so a
+// process that drives several GPUs must opt a kernel in on each of them. `done` (one static
+// array per kernel) records per device the largest size already granted; the check is a
+// lock-free load, and two host threads racing on a first call both set the same attribute.
+constexpr int kMaxDevices = 64;
+template <typename... KArgs>
+cudaError_t smem_optin(void (*kernel)(KArgs...), size_t bytes, std::atomic<int> (&done)[kMaxDevices]) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const int want = static_cast<int>(bytes);
+    const bool cached = dev >= 0 && dev < kMaxDevices;
+    if (cached && done[dev].load(std::memory_order_acquire) >= want) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, want);
+    if (e == cudaSuccess && cached) {
+        int prev = done[dev].load(std::memory_order_relaxed);
+        while (prev < want && !done[dev].compare_exchange_weak(prev, want)) {
+        }
+    }
+    return e;
 }
 }  // namespace msgl

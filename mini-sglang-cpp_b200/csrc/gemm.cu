@@ -1407,6 +1407,7 @@ cudaError_t launch_cl_raw(const CUtensorMap& tw, const CUtensorMap& tx, void* y,
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    launch_counter().fetch_add(1, std::memory_order_relaxed);
     return cudaLaunchKernelEx(&cfg, gemm_cl_kernel<BN, EPI>, tw, tx, y, amax, M, N, K, id_off, err);
 }
 

@@ -362,6 +362,20 @@ int msgl_tp_all_reduce_sum(msgl_tp* tp, void* x, int64_t n, msgl_stream_t stream
     return r == ncclSuccess ? MSGL_OK : nccl_err(r, "ncclAllReduce");
 }
 
+int msgl_tp_all_gather(msgl_tp* tp, const void* send, void* recv, size_t bytes,
+                       msgl_stream_t stream) {
+    if (!tp || (bytes && (!send || !recv))) return set_error(MSGL_ERR_INVALID_ARG, "tp_all_gather: bad args");
+    if (bytes == 0) return MSGL_OK;
+    if (tp->world == 1) {
+        if (send != recv &&
+            cudaMemcpyAsync(recv, send, bytes, cudaMemcpyDeviceToDevice, stream) != cudaSuccess)
+            return set_error(MSGL_ERR_CUDA, cudaGetErrorString(cudaGetLastError()));
+        return MSGL_OK;
+    }
+    ncclResult_t r = ncclAllGather(send, recv, bytes, ncclUint8, tp->comm, stream);
+    return r == ncclSuccess ? MSGL_OK : nccl_err(r, "ncclAllGather");
+}
+
 int msgl_tp_allreduce_add_rmsnorm(msgl_tp* tp, void* x, float* residual, const void* weight,
                                   int num_tokens, int hidden, float eps, int first,
                                   msgl_stream_t stream) {

@@ -50,6 +50,8 @@ struct Model {
     int vocab0 = 0;                                // first lm_head row (token id) of this rank
     msgl_tp* tp = nullptr;                         // communicator (tp_size > 1), not owned
     bf16_t* tp_part[2] = {nullptr, nullptr};       // its peer-mapped slots: row-parallel outputs
+    DevBuf tp_logits_local, tp_logits_all;         // logits under TP: this rank's vocab columns,
+                                                   // then every rank's (all-gathered)
     std::vector<Qwen3DecoderLayer> layers;
     DevBuf embed;        // [V, H]
     RMSNorm norm;        // final norm
@@ -365,6 +367,7 @@ static void set_weight(Model& m, const std::string& name, const bf16_t* h, int64
 static void alloc_kv(Model& m, int num_pages, int page_size, cudaStream_t s) {
     if (page_size != 16) throw Fail(MSGL_ERR_UNSUPPORTED_SHAPE, "alloc_kv: page_size must be 16");
     if (num_pages <= 0) throw Fail(MSGL_ERR_INVALID_ARG, "alloc_kv: num_pages");
+    m.graphs_reset();  // captured graphs hold the old pools' addresses
     m.page_size = page_size;
     m.num_slots = static_cast<int64_t>(num_pages) * page_size;
     const size_t bytes = static_cast<size_t>(m.num_slots) * m.hkv * m.cfg.head_dim * 2;
@@ -478,7 +481,23 @@ static void forward(Model& m, const msgl_batch& b, int* next_tokens, float* logi
     }
     if (!m.tp) m.norm.forward_fused_add(xl, rl, B, false, s);  // (TP: done by the last all-reduce)
     if (m.tp) {  // vocab-parallel lm_head: local best (logit, id), max over the ranks
-        if (logits) throw Fail(MSGL_ERR_UNSUPPORTED_SHAPE, "forward: logits output needs tp_size 1");
+        if (logits) {  // this rank's vocab columns in fp32, all-gathered, placed as columns
+            const int world = c.tp_size, vpad = (c.vocab + world - 1) / world;
+            const size_t chunk = static_cast<size_t>(B) * vpad * sizeof(float);
+            ck(msgl_gemm_bf16(xl, m.lm_head.weight.p, m.tp_logits_local.p, B, m.vocab_l, H, MSGL_F32,
+                              m.scratch.gemm_ws, m.scratch.gemm_ws_bytes, s), "lm_head logits shard");
+            ck(msgl_tp_all_gather(m.tp, m.tp_logits_local.p, m.tp_logits_all.p, chunk, s),
+               "logits all-gather");
+            for (int q = 0; q < world; ++q) {  // rank q's [B, rows_q] block -> columns [q vpad, ...)
+                const int rows_q = std::min(vpad, c.vocab - q * vpad);
+                if (rows_q <= 0) continue;
+                ckc(cudaMemcpy2DAsync(logits + static_cast<size_t>(q) * vpad, static_cast<size_t>(c.vocab) * 4,
+                                      static_cast<const char*>(m.tp_logits_all.p) + q * chunk,
+                                      static_cast<size_t>(rows_q) * 4, static_cast<size_t>(rows_q) * 4, B,
+                                      cudaMemcpyDeviceToDevice, s),
+                    "logits placement");
+            }
+        }
         ck(msgl_lm_head_argmax_partial(xl, m.lm_head.weight.p, B, m.vocab_l, H, m.vocab0,
                                        m.packed.as<unsigned long long>(), m.scratch.gemm_ws,
                                        m.scratch.gemm_ws_bytes, s), "lm_head");
@@ -733,6 +752,13 @@ int msgl_model_set_tp(msgl_model* m, msgl_tp* tp) {
         }
         msgl_tp_p2p_buffer(tp, 1, &buf[1], &have);
         if (have < need) return msgl::set_error(MSGL_ERR_WORKSPACE, "set_tp: peer-mapped region too small");
+        const int vpad = (m->m.cfg.vocab + world - 1) / world;
+        const size_t chunk = static_cast<size_t>(m->m.cfg.max_reqs) * vpad * sizeof(float);
+        const int rc = guarded([&] {
+            m->m.tp_logits_local.alloc(chunk);
+            m->m.tp_logits_all.alloc(chunk * world);
+        });
+        if (rc) return rc;
         m->m.tp = tp;
         m->m.tp_part[0] = static_cast<bf16_t*>(buf[0]);
         m->m.tp_part[1] = static_cast<bf16_t*>(buf[1]);

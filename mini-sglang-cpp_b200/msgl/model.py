@@ -242,6 +242,11 @@ class Qwen3Model:
         bits = to_bf16_bits(arr)
         check(self.L.msgl_model_set_weight(self.h, name.encode(), bits.ctypes.data, bits.size, _s()))
 
+    def set_weight_bits(self, name: str, bits: np.ndarray):
+        """The same from bf16 bit patterns (uint16) of the full tensor."""
+        bits = np.ascontiguousarray(bits, dtype=np.uint16)
+        check(self.L.msgl_model_set_weight(self.h, name.encode(), bits.ctypes.data, bits.size, _s()))
+
     def set_weights(self, named: dict):
         for k, v in named.items():
             self.set_weight(k, v)

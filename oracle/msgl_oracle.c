@@ -158,7 +158,9 @@ void oracle_store_kv_slots(const float* k, const float* v, float* k_pool, float*
     }
 }
 
-/* layer.cpp:226-257 per request over the paged pool (see header) */
+/* layer.cpp:226-257 per request over the paged pool (see header). Requests are independent and
+ * run in parallel; the value sum keeps the reference's order (j ascending for every output d),
+ * with the j loop outside so that each V row is read once, contiguously. */
 void oracle_paged_attention(const float* q, const float* k_pool, const float* v_pool,
                             const int32_t* page_table, int max_pages, const int32_t* seq_lens,
                             const int32_t* q_indptr, int num_reqs, int num_q_heads,
@@ -166,12 +168,14 @@ void oracle_paged_attention(const float* q, const float* k_pool, const float* v_
                             float* out) {
     int group = num_q_heads / num_kv_heads;
     int64_t kv_stride = (int64_t)num_kv_heads * head_dim;
+#pragma omp parallel for schedule(dynamic, 1)
     for (int r = 0; r < num_reqs; ++r) {
         int ctx = seq_lens[r];
         int n = q_indptr[r + 1] - q_indptr[r];
         const int32_t* pt = page_table + (int64_t)r * max_pages;
         float* scores = (float*)malloc(sizeof(float) * (size_t)(ctx > 0 ? ctx : 1));
         int64_t* slots = (int64_t*)malloc(sizeof(int64_t) * (size_t)(ctx > 0 ? ctx : 1));
+        float* val = (float*)malloc(sizeof(float) * (size_t)head_dim);
         for (int j = 0; j < ctx; ++j)
             slots[j] = (int64_t)pt[j / page_size] * page_size + j % page_size;
         for (int i = 0; i < n; ++i) {
@@ -193,17 +197,17 @@ void oracle_paged_attention(const float* q, const float* k_pool, const float* v_
                     scores[j] = expf(scores[j] - max_score);
                     sum_exp += scores[j];
                 }
-                float* o = out + (t * num_q_heads + h) * head_dim;
-                for (int d = 0; d < head_dim; ++d) {
-                    float val = 0.0f;
-                    for (int j = 0; j <= qpos; ++j) {
-                        float prob = scores[j] / sum_exp;
-                        val += prob * v_pool[slots[j] * kv_stride + (int64_t)kvh * head_dim + d];
-                    }
-                    o[d] = val;
+                for (int d = 0; d < head_dim; ++d) val[d] = 0.0f;
+                for (int j = 0; j <= qpos; ++j) {
+                    float prob = scores[j] / sum_exp;
+                    const float* vv = v_pool + slots[j] * kv_stride + (int64_t)kvh * head_dim;
+                    for (int d = 0; d < head_dim; ++d) val[d] += prob * vv[d];
                 }
+                float* o = out + (t * num_q_heads + h) * head_dim;
+                for (int d = 0; d < head_dim; ++d) o[d] = val[d];
             }
         }
+        free(val);
         free(scores);
         free(slots);
     }

@@ -17,21 +17,31 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libref_harness.so")
-REFERENCE_SRC = "/root/reference"
+# The reference source tree (read-only, only needed to build _ref): MSGL_REFERENCE_SRC.
+REFERENCE_SRC = os.environ.get("MSGL_REFERENCE_SRC", "")
 
 f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
 I64, I32, F32, VP = C.c_int64, C.c_int, C.c_float, C.c_void_p
 
 
-def build(with_ref: bool | None = None) -> None:
-    """Compile liboracle.so (and _ref when the reference sources are present)."""
-    targets = ["oracle"]
+def json_include_dir() -> str:
+    """The nlohmann_json v3.11.3 headers vendored in this interpreter's site-packages."""
+    import sysconfig
+    return os.path.join(sysconfig.get_paths()["purelib"], "include", "cudnn_frontend", "thirdparty")
+
+
+def build(with_ref: bool | None = None, reference_src: str | None = None) -> None:
+    """Compile liboracle.so, and _ref when the reference sources are given (argument or
+    MSGL_REFERENCE_SRC) and present."""
+    src = reference_src if reference_src is not None else REFERENCE_SRC
+    targets, extra = ["oracle"], []
     if with_ref is None:
-        with_ref = os.path.isdir(REFERENCE_SRC)
+        with_ref = bool(src) and os.path.isdir(src)
     if with_ref:
         targets.append("ref")
-    subprocess.run(["make", "-s", "-C", HERE, *targets], check=True)
+        extra = [f"REF={src}", f"JSON_INC={json_include_dir()}"]
+    subprocess.run(["make", "-s", "-C", HERE, *extra, *targets], check=True)
 
 
 def _f(a):
@@ -346,7 +356,10 @@ class OracleModel:
             self.layers.append(lt)
 
     def forward(self, ids, positions, slot_mapping, page_table, seq_lens, q_indptr,
-                return_hidden=False):
+                return_hidden=False, return_state=False):
+        """One step; `return_hidden`: also each layer's output x (the MLP output);
+        `return_state`: also each layer's (x, residual) pair, whose fp32 sum residual + x is
+        the hidden state after the layer."""
         c = self.cfg
         ids, positions, slots = _i(ids), _i(positions), _i(slot_mapping)
         pt, seq_lens, q_indptr = _i(page_table), _i(seq_lens), _i(q_indptr)
@@ -359,10 +372,12 @@ class OracleModel:
         for l, lt in enumerate(self.layers):
             self.lib.oracle_decoder_layer(C.byref(self.ct), C.byref(lt), C.byref(bt), self.table,
                                           x, res, int(l == 0))
-            if return_hidden:
+            if return_state:
+                hidden.append((x.copy(), res.copy()))
+            elif return_hidden:
                 hidden.append(x.copy())
         last = q_indptr[1:] - 1
         xl, rl = x[last].copy(), res[last].copy()
         self.lib.oracle_add_rmsnorm(xl, rl, self.w["norm"], xl.shape[0], c["hidden"], c["eps"], 0)
         logits = self.o.linear(xl, self.w["lm_head"])
-        return (logits, hidden) if return_hidden else logits
+        return (logits, hidden) if (return_hidden or return_state) else logits

@@ -1,0 +1,242 @@
+"""Whole-model parity at the benchmark's model shapes, through the executor, against the oracle.
+
+* Qwen3-0.6B (28 layers, hidden 1024, 16 q / 8 kv heads, head_dim 128, intermediate 3072, vocab
+  151936, RMSNorm eps 1e-6, RoPE theta 1e6): weights N(0, 0.02) from the library's counter-based
+  generator with seed 0 (tensor index = position in name order), norm gains 1; 4 requests x 128
+  prompt ids uniform in [0, 151936) (numpy seed 1); page size 16. The prefill emits token 1, then
+  31 greedy decode steps (32 tokens per request; the scheduler's order, scheduler.cpp:83-124).
+  Teacher-forced on the oracle's tokens, every step checks the last-token logits (relative L2
+  <= 2e-2, the bf16-vs-fp32 tolerance) and that the greedy ids equal the oracle's wherever the
+  oracle's top-1 / top-2 margin exceeds 4x the observed logit error; the prefill also checks the
+  hidden state after every one of the 28 layers. A free-running run through
+  msgl_model_decode_steps (device-advanced metadata, CUDA graphs) must then produce the oracle's
+  greedy tokens.
+* Qwen3-8B (hidden 4096, 32 q / 8 kv heads, intermediate 12288, vocab 151936), 2 layers: the decode
+  step the benchmark times -- 128 requests at context 2048 whose first 1024 tokens are 64 pages
+  shared by every page table -- so the executor runs split-K partials with fused consumers and
+  the cascade attention. KV contents N(0, 1) bf16. Checked: hidden state after each layer and
+  the final logits (relative L2 <= 2e-2), greedy ids where the margin is clear.
+
+The fp32 oracle is fed the bf16 weight values widened to fp32, so weight rounding is not error.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import OracleModel, from_bf16_bits
+
+pytestmark = pytest.mark.gpu
+
+ONE_BF16 = 0x3F80  # 1.0
+
+
+def rel_l2(a, b):
+    return float(np.linalg.norm(a - b) / np.linalg.norm(b))
+
+
+def weight_shapes(cfg):
+    H, D, hq, hkv, I, V = (cfg[k] for k in ("hidden", "head_dim", "num_q_heads", "num_kv_heads",
+                                            "inter", "vocab"))
+    names = [("embed", (V, H))]
+    for l in range(cfg["num_layers"]):
+        p = f"layers.{l}."
+        names += [(p + "input_ln", (H,)), (p + "qkv", ((hq + 2 * hkv) * D, H)),
+                  (p + "q_norm", (D,)), (p + "k_norm", (D,)), (p + "o", (H, hq * D)),
+                  (p + "post_ln", (H,)), (p + "gate_up", (2 * I, H)), (p + "down", (H, I))]
+    return names + [("norm", (H,)), ("lm_head", (V, H))]
+
+
+def load_generated_weights(model, cfg, seed=0, std=0.02, keep_embed=True):
+    """Draw every matrix with the device generator, set it on the executor (bf16 bits) and return
+    the oracle's fp32 copies (the same values). Norm gains are 1.0. With keep_embed False the
+    embedding is returned as bits only (the caller keeps the rows it needs)."""
+    from msgl import ops
+    w = {}
+    for i, (name, shape) in enumerate(weight_shapes(cfg)):
+        if len(shape) == 1:
+            bits = np.full(shape, ONE_BF16, np.uint16)
+        else:
+            t = torch.empty(shape, dtype=torch.bfloat16, device="cuda")
+            ops.fill_normal_(t, seed=seed, stream_id=i, std=std)
+            bits = t.view(torch.int16).cpu().numpy().view(np.uint16)
+            del t
+        model.set_weight_bits(name, bits)
+        if name == "embed" and not keep_embed:
+            w[name] = bits
+        else:
+            w[name] = from_bf16_bits(bits).reshape(shape)
+    return w
+
+
+# ------------------------------------------------------------------ Qwen3-0.6B, 32 greedy tokens
+C1 = dict(num_layers=28, hidden=1024, num_q_heads=16, num_kv_heads=8, head_dim=128, inter=3072,
+          vocab=151936, eps=1e-6, rope_base=1e6, max_position=512, page_size=16)
+PROMPT, NREQ, NEW, WIDTH = 128, 4, 32, 12
+
+
+def test_qwen3_0_6b_prefill_and_32_greedy_tokens(cuda, oracle):
+    from msgl.model import BatchBuilder, PagePool, Qwen3Model, Request, device_view
+    model = Qwen3Model(C1, max_tokens=NREQ * PROMPT, max_reqs=NREQ)
+    w = load_generated_weights(model, C1)
+    num_pages = 64
+    model.alloc_kv(num_pages)
+    orc = OracleModel(oracle, C1, w, num_slots=num_pages * 16)
+    prompts = np.random.default_rng(1).integers(0, C1["vocab"], (NREQ, PROMPT)).tolist()
+    reqs = [Request(list(p)) for p in prompts]
+    bb = BatchBuilder(PagePool(num_pages))
+
+    # ---- prefill: the hidden state after every layer, then the logits
+    sb = bb.build(reqs, decode=False, max_pages=WIDTH)
+    h = {k: v.cpu().numpy() for k, v in sb.tensors.items()}
+    ref, state = orc.forward(h["input_ids"], h["positions"], h["slot_mapping"], h["page_table"],
+                             h["seq_lens"], h["q_indptr"], return_state=True)
+    T, H = NREQ * PROMPT, C1["hidden"]
+    hidden_err = []
+    for n in range(1, C1["num_layers"] + 1):
+        model.set_num_layers_run(n)
+        model.forward(sb)
+        torch.cuda.synchronize()
+        xp, rp = model.hidden(T)
+        got = (device_view(rp, (T, H), torch.float32) +
+               device_view(xp, (T, H), torch.bfloat16).float()).cpu().numpy()
+        x_o, r_o = state[n - 1]
+        hidden_err.append(rel_l2(got, r_o + x_o))
+    model.set_num_layers_run(-1)
+    assert max(hidden_err) < 2e-2, hidden_err
+
+    rows, oracle_tokens, agree = [], [], 0
+    unclear_at = [NEW] * NREQ  # first step at which request r's oracle margin is not clear
+    for step in range(NEW):
+        if step > 0:
+            sb = bb.build(reqs, decode=True, max_pages=WIDTH)
+            h = {k: v.cpu().numpy() for k, v in sb.tensors.items()}
+            ref = orc.forward(h["input_ids"], h["positions"], h["slot_mapping"], h["page_table"],
+                              h["seq_lens"], h["q_indptr"])
+        nxt, lg = model.forward(sb, logits=True)
+        torch.cuda.synchronize()
+        got = lg.cpu().numpy()
+        ids = nxt.cpu().numpy()
+        err = rel_l2(got, ref)
+        ref_ids = ref.argmax(axis=1)
+        top2 = np.sort(ref, axis=1)[:, -2:]
+        margin = top2[:, 1] - top2[:, 0]
+        tol = 4 * float(np.abs(got - ref).max())
+        clear = margin > tol
+        rows.append((step, err, float(margin.min()), tol, int((ids == ref_ids).sum()), int(clear.sum())))
+        assert err < 2e-2, rows[-1]
+        assert np.array_equal(ids, got.argmax(axis=1))  # fused lm_head argmax = argmax of logits
+        assert np.array_equal(ids[clear], ref_ids[clear]), rows[-1]
+        agree += int((ids == ref_ids).sum())
+        for r in range(NREQ):
+            if not clear[r]:
+                unclear_at[r] = min(unclear_at[r], step)
+        oracle_tokens.append(ref_ids.tolist())
+        for r, t in zip(reqs, ref_ids):  # teacher-forced on the oracle's tokens
+            r.cached_len = r.device_len
+            r.input_ids.append(int(t))
+    print("\nstep  rel_l2   min_margin  4x|err|  ids==oracle  margin-clear")
+    for r in rows:
+        print(f"{r[0]:4d}  {r[1]:.2e}  {r[2]:9.4f}  {r[3]:7.4f}  {r[4]:6d}/{NREQ}  {r[5]:6d}/{NREQ}")
+    print(f"prefill hidden rel_l2 per layer: max {max(hidden_err):.2e}")
+    print(f"greedy ids equal to the oracle's: {agree}/{NREQ * NEW}")
+
+    # ---- free-running: prefill again on fresh pages, then 31 device-driven decode steps. Each
+    # request must produce the oracle's greedy tokens up to its first step whose oracle margin
+    # is within the bf16 error (a near-tie either way is a legitimate choice; after it the two
+    # sequences may continue differently)
+    model.alloc_kv(num_pages)
+    pool = PagePool(num_pages)
+    reqs = [Request(list(p)) for p in prompts]
+    bb = BatchBuilder(pool)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        first = model.forward(bb.build(reqs, decode=False, max_pages=WIDTH))
+    torch.cuda.synchronize()
+    for r, t in zip(reqs, first.cpu().numpy().tolist()):
+        r.cached_len = r.device_len
+        r.input_ids.append(int(t))
+    with torch.cuda.stream(s):
+        sb = bb.build(reqs, decode=True, max_pages=WIDTH)
+        free = torch.tensor(pool.free + [0], dtype=torch.int32, device="cuda")
+        top = torch.tensor([len(pool.free)], dtype=torch.int32, device="cuda")
+        log = model.decode_steps(sb, NEW - 1, free, top, graph=True)
+    torch.cuda.synchronize()
+    tokens = [first.cpu().numpy().tolist()] + log.cpu().numpy().tolist()
+    full = 0
+    for r in range(NREQ):
+        seq_gpu = [tokens[s][r] for s in range(NEW)]
+        seq_orc = [oracle_tokens[s][r] for s in range(NEW)]
+        k = unclear_at[r]
+        assert seq_gpu[:k] == seq_orc[:k], (r, k, seq_gpu, seq_orc)
+        full += int(seq_gpu == seq_orc)
+    print(f"free-running: {full}/{NREQ} requests give the oracle's {NEW} greedy tokens; "
+          f"steps before the first near-tie per request: {unclear_at}")
+    from msgl import ops
+    assert ops.device_error() == (0, 0)
+
+
+# ------------------------------------------------------------------ Qwen3-8B, the timed decode step
+C8 = dict(num_layers=2, hidden=4096, num_q_heads=32, num_kv_heads=8, head_dim=128, inter=12288,
+          vocab=151936, eps=1e-6, rope_base=1e6, max_position=2064, page_size=16)
+B8, CTX8, PREFIX8 = 128, 2048, 1024
+
+
+def test_qwen3_8b_decode_step_cascade_partials(cuda, oracle):
+    from msgl import ops
+    from msgl.model import PagePool, Qwen3Model, device_view, make_step
+    model = Qwen3Model(C8, max_tokens=B8, max_reqs=B8)
+    w = load_generated_weights(model, C8, keep_embed=False)
+    n_prefix, n_own = PREFIX8 // 16, (CTX8 - PREFIX8) // 16
+    num_pages = n_prefix + B8 * n_own + 16
+    model.alloc_kv(num_pages)
+    pool = PagePool(num_pages)  # LIFO free list, shuffled: pages scattered over the pool
+    np.random.default_rng(3).shuffle(pool.free)
+    prefix = [pool.allocate() for _ in range(n_prefix)]
+    pt = np.array([prefix + [pool.allocate() for _ in range(n_own)] for _ in range(B8)], np.int32)
+    rng = np.random.default_rng(1)
+    ids = rng.integers(0, C8["vocab"], B8).astype(np.int32)
+    pos = np.full(B8, CTX8 - 1, np.int32)
+    host = dict(input_ids=ids, positions=pos,
+                slot_mapping=(pt[:, (CTX8 - 1) // 16] * 16 + (CTX8 - 1) % 16).astype(np.int32),
+                page_table=pt, seq_lens=np.full(B8, CTX8, np.int32),
+                q_indptr=np.arange(B8 + 1, dtype=np.int32), last_idx=np.arange(B8, dtype=np.int32))
+    sb = make_step(host, True, "cuda", CTX8, 1)
+    assert sb.struct.shared_prefix_pages == n_prefix  # the executor takes the cascade path
+
+    width = C8["num_kv_heads"] * 128
+    # the oracle embeds through the 128 rows it needs (ids remapped to 0..127)
+    emb = from_bf16_bits(w["embed"].reshape(C8["vocab"], -1)[ids]).reshape(B8, -1)
+    w["embed"] = emb
+    orc = OracleModel(oracle, C8, w, num_slots=num_pages * 16)
+    for l in range(C8["num_layers"]):  # synthetic KV cache contents, the same on both sides
+        kp, vp, n = model.kv_pool(l)
+        for j, (ptr, dst) in enumerate(((kp, orc.k_pools[l]), (vp, orc.v_pools[l]))):
+            t = device_view(ptr, (n, width), torch.bfloat16)
+            ops.fill_normal_(t, seed=4, stream_id=2 * l + j, std=1.0)
+            dst[:] = t.float().cpu().numpy()
+    ref, state = orc.forward(np.arange(B8, dtype=np.int32), pos, host["slot_mapping"], pt,
+                             host["seq_lens"], host["q_indptr"], return_state=True)
+    # layer by layer: the decode step's final norm adds x into the residual in place, so after a
+    # forward of n layers the residual holds the hidden state after layer n
+    hidden_err = []
+    for n in range(1, C8["num_layers"] + 1):
+        model.set_num_layers_run(n)
+        nxt, lg = model.forward(sb, logits=True)
+        torch.cuda.synchronize()
+        _, rp = model.hidden(B8)
+        got = device_view(rp, (B8, C8["hidden"]), torch.float32).cpu().numpy()
+        x_o, r_o = state[n - 1]
+        hidden_err.append(rel_l2(got, r_o + x_o))
+    assert max(hidden_err) < 2e-2, hidden_err
+    got = lg.cpu().numpy()
+    err = rel_l2(got, ref)
+    assert err < 2e-2, err
+    top2 = np.sort(ref, axis=1)[:, -2:]
+    clear = (top2[:, 1] - top2[:, 0]) > 4 * float(np.abs(got - ref).max())
+    out = nxt.cpu().numpy()
+    assert np.array_equal(out, got.argmax(axis=1))
+    assert np.array_equal(out[clear], ref.argmax(axis=1)[clear])
+    print(f"\n8B decode step: hidden rel_l2 per layer {[f'{e:.2e}' for e in hidden_err]}, "
+          f"logits rel_l2 {err:.2e}, ids equal {int((out == ref.argmax(axis=1)).sum())}/{B8} "
+          f"(margin-clear {int(clear.sum())})")
+    assert ops.device_error() == (0, 0)

@@ -59,6 +59,34 @@ def test_noalloc_matches_workspace_entry_point(cuda, seq_lens, hq, hkv):
     assert ops.device_error() == (0, 0)
 
 
+def test_noalloc_allocates_nothing_and_matches_oracle(cuda, oracle):
+    """After a first call (which looks up the scratch address on this device), further calls with
+    a preallocated output leave the device's free memory unchanged, and their output equals the
+    oracle's fp32 paged attention within the per-op bf16 tolerance."""
+    from msgl import ops
+    seq_lens, hq, hkv = [300, 2048, 17, 777, 1], 32, 8
+    q, kp, vp, pt, seq = _case(11, seq_lens, hq, hkv)
+    L = max(seq_lens)
+    out = torch.empty(len(seq_lens), hq, D, dtype=torch.bfloat16, device="cuda")
+    ops.paged_attention_decode_noalloc(q, kp, vp, pt, seq, L, hq, hkv, out=out)
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        ops.paged_attention_decode_noalloc(q, kp, vp, pt, seq, L, hq, hkv, out=out)
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0, (free0, free1)
+    B = len(seq_lens)
+    ref = oracle.paged_attention(q.float().cpu().numpy().reshape(B, hq * D),
+                                 kp.float().cpu().numpy(), vp.float().cpu().numpy(),
+                                 pt.cpu().numpy(), seq.cpu().numpy(), np.arange(B + 1), hq, hkv,
+                                 D, P)
+    got = out.float().cpu().numpy().reshape(B, hq * D)
+    err = float(np.linalg.norm(got - ref) / np.linalg.norm(ref))
+    assert err < 1e-2, err
+    assert ops.device_error() == (0, 0)
+
+
 def test_noalloc_rejects_oversized_batch(cuda):
     from msgl import ops
     from msgl._lib import MsglError, lib
