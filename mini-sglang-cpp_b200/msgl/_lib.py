@@ -18,6 +18,7 @@ SIGNATURES = {
     "msgl_version": (C.c_char_p, []),
     "msgl_last_error": (C.c_char_p, []),
     "msgl_device_error": (I, [P, P, I, P]),
+    "msgl_kernel_launches": (C.c_ulonglong, []),
     "msgl_launch_rmsnorm": (I, [P, P, P, I, I, F, I, P]),
     "msgl_launch_rope": (I, [P, P, P, P, I, I, I, I, I, P]),
     "msgl_launch_index_gather": (I, [P, P, P, I, I, I, I, P]),
@@ -58,6 +59,7 @@ SIGNATURES = {
     "msgl_tp_rank": (I, [P]),
     "msgl_tp_world": (I, [P]),
     "msgl_tp_all_reduce_sum": (I, [P, P, I64, P]),
+    "msgl_tp_all_gather": (I, [P, P, C.c_size_t, P]),
     "msgl_tp_allreduce_add_rmsnorm": (I, [P, P, P, P, I, I, F, I, P]),
     "msgl_tp_argmax_combine": (I, [P, P, P, I, P]),
     "msgl_tp_enable_p2p": (I, [P, SZ, P]),
