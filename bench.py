@@ -615,11 +615,18 @@ def run_case(args):
 def run_breakdown(args, dev):
     """Each kernel of the decode step timed alone with CUDA events at the bench's shapes (one
     layer; weight copies rotated so every launch streams its weights from HBM, as in the step).
-    Prints one JSON line: per kernel the mean launch time and achieved GB/s."""
+    With --tp-shape N the shapes are those of one rank of N-way tensor parallelism (q heads,
+    kv heads, intermediate columns and vocab rows divided by N; kv heads at least 1), without the
+    all-reduce. Prints one JSON line: per kernel the mean launch time and achieved GB/s."""
     import torch
 
     from msgl import ops
-    hq, hkv, H, I, V = (CFG8B[k] for k in ("num_q_heads", "num_kv_heads", "hidden", "inter", "vocab"))
+    tp = max(1, args.tp_shape)
+    H = CFG8B["hidden"]
+    hq = CFG8B["num_q_heads"] // tp
+    hkv = max(1, CFG8B["num_kv_heads"] // tp)
+    I = CFG8B["inter"] // tp
+    V = -(-CFG8B["vocab"] // tp)
     res = {}
 
     def timed(name, fns, nbytes, reps=None):
@@ -724,6 +731,9 @@ def run_breakdown(args, dev):
     peak = peaks.get("hbm_gbs", 6650.0)
     for v in res.values():
         v["frac_hbm"] = round(v["GB/s"] / peak, 3)
+    if tp > 1:
+        print(json.dumps({"case": "breakdown", "tp_shape": tp, "kernels": res}), flush=True)
+        return 0
     # prefill-sized projections (2048 tokens): tensor-bound, reported against the bf16 peak
     tpeak = peaks.get("bf16_tflops", 1590.0)
     mp = 2048
@@ -748,6 +758,8 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--tp-shape", type=int, default=1,
+                    help="--case breakdown: the shapes of one rank of this tensor-parallel size")
     ap.add_argument("--blocks", type=int, default=3,
                     help="timed blocks of --steps steps each; the median block is reported")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")

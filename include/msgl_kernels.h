@@ -337,7 +337,8 @@ MSGL_API int msgl_tp_allreduce_add_rmsnorm(msgl_tp* tp, void* x, float* residual
 /* One-kernel all-reduce + add + RMSNorm over NVLink peer memory (no counterpart in the
  * reference, whose TPCommunicator is a stub; it replaces NCCL all-reduce + msgl_add_rmsnorm).
  * msgl_tp_enable_p2p (collective, every rank the same `bytes`) allocates this rank's
- * peer-mapped region -- two slots of `bytes` for partial rows plus flags -- exchanges cudaIpc
+ * peer-mapped region -- three slots of `bytes` (two for partial rows, one for the two-shot
+ * form's output rows) plus flags -- exchanges cudaIpc
  * handles with an NCCL all-gather on `stream` and maps every other rank's region (plain peer
  * loads; no multicast). msgl_tp_p2p_buffer returns slot 0 or 1: the row-parallel GEMM writes its
  * partial [T, H] bf16 rows there, and CONSECUTIVE fused calls must use alternate slots (checked).
@@ -346,12 +347,30 @@ MSGL_API int msgl_tp_allreduce_add_rmsnorm(msgl_tp* tp, void* x, float* residual
  * x_out = RMSNorm(residual) * weight (bf16; `first` as msgl_add_rmsnorm); all ranks get the same
  * bits. The ranks meet through per-CTA epoch flags in the regions (bounded waits: a rank that does
  * not arrive within ~2 s gives MSGL_ERR_TIMEOUT in the error word, site 500). */
+/* After MSGL_ERR_TIMEOUT from any of the fused calls (site 500 / 503) the ranks' call pairing is
+ * undefined: destroy the communicator and create a new one (msgl_tp_destroy, msgl_tp_init,
+ * msgl_tp_enable_p2p) before the next collective call. A CTA whose wait ran out does not advance
+ * its epoch, so a late peer never reads rows that a later call is rewriting.
+ *
+ * msgl_tp_fused_allreduce_add_rmsnorm_2shot: the same result, computed two-shot. With
+ * per = ceil(num_tokens / world), rank r reduces only rows [r per, min(T, (r + 1) per)): it
+ * reads those rows of every rank's partial, adds its residual rows, normalises, and stores the
+ * bf16 rows into slot 2 of EVERY rank; x_out must be this rank's slot 2 (msgl_tp_p2p_buffer),
+ * which afterwards holds all T rows on every rank. The residual is row-partitioned: this call
+ * reads and writes only the rows rank r owns, so a caller that uses only the two-shot form keeps
+ * each residual row on its owning rank. NVLink bytes per rank: (W-1)/W of the rows read and
+ * written once (the one-shot form reads W-1 full copies). */
 MSGL_API int msgl_tp_enable_p2p(msgl_tp* tp, size_t bytes, msgl_stream_t stream);
 MSGL_API int msgl_tp_p2p_buffer(msgl_tp* tp, int slot, void** ptr, size_t* bytes);
 MSGL_API int msgl_tp_fused_allreduce_add_rmsnorm(msgl_tp* tp, const void* partial, void* x_out,
                                                  float* residual, const void* weight,
                                                  int num_tokens, int hidden, float eps, int first,
                                                  msgl_stream_t stream);
+MSGL_API int msgl_tp_fused_allreduce_add_rmsnorm_2shot(msgl_tp* tp, const void* partial,
+                                                       void* x_out, float* residual,
+                                                       const void* weight, int num_tokens,
+                                                       int hidden, float eps, int first,
+                                                       msgl_stream_t stream);
 MSGL_API int msgl_tp_argmax_combine(msgl_tp* tp, unsigned long long* packed, int* ids,
                                     int num_rows, msgl_stream_t stream);
 /* Host only: the shard of `rank` as 8 ints {q_head0, q_heads, kv_head0, kv_heads, inter0,

@@ -50,6 +50,7 @@ struct Model {
     int vocab0 = 0;                                // first lm_head row (token id) of this rank
     msgl_tp* tp = nullptr;                         // communicator (tp_size > 1), not owned
     bf16_t* tp_part[2] = {nullptr, nullptr};       // its peer-mapped slots: row-parallel outputs
+    bf16_t* tp_x = nullptr;                        // two-shot all-reduce: x lives in slot 2
     DevBuf tp_logits_local, tp_logits_all;         // logits under TP: this rank's vocab columns,
                                                    // then every rank's (all-gathered)
     std::vector<Qwen3DecoderLayer> layers;
@@ -395,8 +396,16 @@ static void forward(Model& m, const msgl_batch& b, int* next_tokens, float* logi
     if (m.num_slots == 0) throw Fail(MSGL_ERR_INVALID_ARG, "forward: KV pools not allocated");
     if (c.tp_size > 1 && !m.tp) throw Fail(MSGL_ERR_INVALID_ARG, "forward: tp_size > 1 needs msgl_model_set_tp");
     const int T = b.num_tokens, H = c.hidden;
-    auto* x = m.x.as<bf16_t>();
+    // tensor parallel with the two-shot all-reduce: x is the peer-mapped slot every rank's
+    // all-reduce stores its normed rows into (the residual then stays row-partitioned)
+    auto* x = m.tp_x ? m.tp_x : m.x.as<bf16_t>();
     float* res = m.residual.as<float>();
+    auto allreduce_norm = [&](bf16_t* part, const void* w, const char* what) {
+        if (m.tp_x)
+            ck(msgl_tp_fused_allreduce_add_rmsnorm_2shot(m.tp, part, x, res, w, T, H, c.eps, 0, s), what);
+        else
+            ck(msgl_tp_fused_allreduce_add_rmsnorm(m.tp, part, x, res, w, T, H, c.eps, 0, s), what);
+    };
     const int nl = m.layers_run >= 0 ? std::min(m.layers_run, c.num_layers) : c.num_layers;
 
     // embed_tokens + layer 0's input_layernorm (residual aliasing first call, layer.cpp:80-84)
@@ -440,9 +449,7 @@ static void forward(Model& m, const msgl_batch& b, int* next_tokens, float* logi
                        m.attn_out.as<bf16_t>(), m.scratch, s);                // :51-52
         if (m.tp) {  // row-parallel o_proj (:55): all-reduce fused with the add + norm of :57
             L.o_proj.forward(m.attn_out.as<bf16_t>(), part_o, T, m.scratch, s);
-            ck(msgl_tp_fused_allreduce_add_rmsnorm(m.tp, part_o, x, res,
-                                                   L.post_attention_layernorm.weight.p, T, H,
-                                                   c.eps, 0, s), "o_proj all-reduce");
+            allreduce_norm(part_o, L.post_attention_layernorm.weight.p, "o_proj all-reduce");
         } else if (use_parts) {
             const int S = L.o_proj.forward_partials(m.attn_out.as<bf16_t>(), parts, T, s);
             L.post_attention_layernorm.forward_fused_add_partials(parts, S, x, res, T, s);
@@ -462,8 +469,7 @@ static void forward(Model& m, const msgl_batch& b, int* next_tokens, float* logi
         }
         if (m.tp) {  // row-parallel down_proj / expert combine: all-reduce + add + next norm
             const void* next_w = l + 1 < nl ? m.layers[l + 1].input_layernorm.weight.p : m.norm.weight.p;
-            ck(msgl_tp_fused_allreduce_add_rmsnorm(m.tp, part_d, x, res, next_w, T, H, c.eps, 0, s),
-               "mlp all-reduce");
+            allreduce_norm(part_d, next_w, "mlp all-reduce");
         }
     }
     // final norm on each request's last row (qwen3.cpp:177, sampling row of D10), lm_head +
@@ -741,6 +747,7 @@ int msgl_model_set_tp(msgl_model* m, msgl_tp* tp) {
         return msgl::set_error(MSGL_ERR_INVALID_ARG, "set_tp: communicator rank/world differ from the config");
     m->m.tp = nullptr;
     m->m.tp_part[0] = m->m.tp_part[1] = nullptr;
+    m->m.tp_x = nullptr;
     if (world > 1) {  // collective: every rank of the communicator calls set_tp
         const size_t need = static_cast<size_t>(m->m.cfg.max_tokens) * m->m.cfg.hidden * 2;
         void* buf[2] = {nullptr, nullptr};
@@ -762,6 +769,15 @@ int msgl_model_set_tp(msgl_model* m, msgl_tp* tp) {
         m->m.tp = tp;
         m->m.tp_part[0] = static_cast<bf16_t*>(buf[0]);
         m->m.tp_part[1] = static_cast<bf16_t*>(buf[1]);
+        // all-reduce form: two-shot from 4 ranks on (each rank reduces T / world rows), one-shot
+        // below; MSGL_TP_ALLREDUCE=1 or 2 forces one
+        const char* env = std::getenv("MSGL_TP_ALLREDUCE");
+        const bool two = env && (env[0] == '1' || env[0] == '2') ? env[0] == '2' : world >= 4;
+        if (two) {
+            void* xs = nullptr;
+            msgl_tp_p2p_buffer(tp, 2, &xs, &have);
+            m->m.tp_x = static_cast<bf16_t*>(xs);
+        }
         m->m.graphs_reset();
     }
     return MSGL_OK;

@@ -65,6 +65,7 @@ SIGNATURES = {
     "msgl_tp_enable_p2p": (I, [P, SZ, P]),
     "msgl_tp_p2p_buffer": (I, [P, I, P, P]),
     "msgl_tp_fused_allreduce_add_rmsnorm": (I, [P, P, P, P, P, I, I, F, I, P]),
+    "msgl_tp_fused_allreduce_add_rmsnorm_2shot": (I, [P, P, P, P, P, I, I, F, I, P]),
     "msgl_tp_shard_plan": (I, [I, I, I, I, I, I, P]),
     # executor (msgl_engine.h)
     "msgl_model_create": (I, [P, P]),

@@ -158,7 +158,58 @@ def test_tp_executor_matches_oracle(world):
           f"(margin-clear {clear_n})")
 
 
-# ---------------------------------------------------------------- 2-GPU fused P2P all-reduce
+# ---------------------------------------------------------------- fused P2P all-reduce
+def _p2p_parity(L, comm, rank, world, T, H, eps, two_shot, calls=4):
+    """`calls` consecutive fused calls (alternating slots) on the same draws on every rank,
+    checked against an fp32 reference: residual bit-exact (the same additions in the same order;
+    two-shot: on the rows this rank owns), x within bf16 rounding and the same bits on every rank.
+    Returns the worst relative L2 error of x."""
+    import ctypes as C
+
+    from msgl._lib import check
+    from msgl.model import device_view
+    from oracle import bf16_round
+    slots, nbytes = [C.c_void_p() for _ in range(3)], C.c_size_t()
+    for k in range(3):
+        check(L.msgl_tp_p2p_buffer(comm.h, k, C.byref(slots[k]), C.byref(nbytes)))
+    parts_dev = [device_view(p.value, (128, H), torch.bfloat16)[:T] for p in slots[:2]]
+    res = torch.zeros(T, H, dtype=torch.float32, device="cuda")
+    res_ref = np.zeros((T, H), np.float32)
+    x = device_view(slots[2].value, (128, H), torch.bfloat16)[:T] if two_shot else \
+        torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    per = -(-T // world)
+    own = slice(rank * per, min(T, (rank + 1) * per)) if two_shot else slice(0, T)
+    fn = L.msgl_tp_fused_allreduce_add_rmsnorm_2shot if two_shot else L.msgl_tp_fused_allreduce_add_rmsnorm
+    worst = 0.0
+    for it in range(calls):  # consecutive calls: the epoch flags advance
+        rng = np.random.default_rng(100 + it)  # same draws on every rank
+        parts = [bf16_round(rng.standard_normal((T, H)).astype(np.float32)) for _ in range(world)]
+        wt = bf16_round(1.0 + 0.1 * rng.standard_normal(H).astype(np.float32))
+        first = int(it == 0)
+        parts_dev[it % 2].copy_(torch.from_numpy(parts[rank]).to(torch.bfloat16))
+        wd = torch.from_numpy(wt).to(torch.bfloat16).cuda()
+        torch.cuda.synchronize()
+        dist.barrier()  # not needed by the kernel; keeps the host copies ordered
+        check(fn(comm.h, slots[it % 2], x.data_ptr(), res.data_ptr(), wd.data_ptr(), T, H, eps,
+                 first, torch.cuda.current_stream().cuda_stream))
+        torch.cuda.synchronize()
+        sm = np.zeros((T, H), np.float32)
+        for p in parts:  # rank order, fp32
+            sm = sm + p
+        res_ref = sm if first else res_ref + sm
+        inv = 1.0 / np.sqrt((res_ref.astype(np.float64) ** 2).mean(axis=1) + eps)
+        x_ref = res_ref * inv[:, None].astype(np.float32) * wt
+        assert np.array_equal(res.cpu().numpy()[own], res_ref[own]), it
+        got = x.float().cpu().numpy()
+        err = float(np.linalg.norm(got - x_ref) / np.linalg.norm(x_ref))
+        worst = max(worst, err)
+        assert err < 1e-2, (it, err)
+        allx = [torch.zeros(T * H // 2, dtype=torch.int32) for _ in range(world)]
+        dist.all_gather(allx, x.contiguous().view(torch.int32).reshape(-1).cpu())
+        assert all(torch.equal(allx[0], a) for a in allx[1:]), it
+    return worst
+
+
 def _p2p_worker(rank, world, port, mode, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -169,71 +220,49 @@ def _p2p_worker(rank, world, port, mode, q):
 
         from msgl import ops
         from msgl._lib import check, lib
-        from msgl.model import TPComm, device_view
-        from oracle import bf16_round
+        from msgl.model import TPComm
         L = lib()
-        uid = [TPComm.new_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(uid, src=0)
-        comm = TPComm(rank, world, uid[0])
+
+        def new_comm():
+            uid = [TPComm.new_unique_id() if rank == 0 else None]
+            dist.broadcast_object_list(uid, src=0)
+            c = TPComm(rank, world, uid[0])
+            check(L.msgl_tp_enable_p2p(c.h, 128 * H * 2, None))
+            return c
+
         T, H, eps = 96, 4096, 1e-6
-        check(L.msgl_tp_enable_p2p(comm.h, 128 * H * 2, None))
-        slots, nbytes = [C.c_void_p(), C.c_void_p()], C.c_size_t()
-        for k in range(2):
-            check(L.msgl_tp_p2p_buffer(comm.h, k, C.byref(slots[k]), C.byref(nbytes)))
-        parts_dev = [device_view(p.value, (128, H), torch.bfloat16)[:T] for p in slots]
+        comm = new_comm()
         ops.device_error(reset=True)
-        if mode == "parity":
-            res = torch.zeros(T, H, dtype=torch.float32, device="cuda")
-            res_ref = np.zeros((T, H), np.float32)
-            x = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
-            worst = 0.0
-            for it in range(4):  # consecutive calls: the epoch flags advance
-                rng = np.random.default_rng(100 + it)  # same draws on every rank
-                parts = [bf16_round(rng.standard_normal((T, H)).astype(np.float32)) for _ in range(world)]
-                wt = bf16_round(1.0 + 0.1 * rng.standard_normal(H).astype(np.float32))
-                first = int(it == 0)
-                ptr = slots[it % 2]  # consecutive calls alternate slots
-                parts_dev[it % 2].copy_(torch.from_numpy(parts[rank]).to(torch.bfloat16))
-                torch.cuda.synchronize()
-                dist.barrier()  # not needed by the kernel; keeps the host copies ordered
-                check(L.msgl_tp_fused_allreduce_add_rmsnorm(
-                    comm.h, ptr, x.data_ptr(), res.data_ptr(),
-                    torch.from_numpy(wt).to(torch.bfloat16).cuda().data_ptr(), T, H, eps, first,
-                    torch.cuda.current_stream().cuda_stream))
-                torch.cuda.synchronize()
-                s = np.zeros((T, H), np.float32)
-                for p in parts:  # rank order, fp32
-                    s = s + p
-                res_ref = s if first else res_ref + s
-                inv = 1.0 / np.sqrt((res_ref.astype(np.float64) ** 2).mean(axis=1) + eps)
-                x_ref = res_ref * inv[:, None].astype(np.float32) * wt
-                assert np.array_equal(res.cpu().numpy(), res_ref), it  # same adds, same order
-                got = x.float().cpu().numpy()
-                err = float(np.linalg.norm(got - x_ref) / np.linalg.norm(x_ref))
-                worst = max(worst, err)
-                assert err < 1e-2, (it, err)
-                # every rank holds the same bits
-                allx = [torch.zeros(T * H // 2, dtype=torch.int32) for _ in range(world)]
-                dist.all_gather(allx, x.view(torch.int32).reshape(-1).cpu())
-                assert all(torch.equal(allx[0], a) for a in allx[1:]), it
+        if mode in ("parity", "parity2"):
+            worst = _p2p_parity(L, comm, rank, world, T, H, eps, mode == "parity2")
+            # an odd row count: the last rank owns fewer rows (or none) in the two-shot form
+            worst = max(worst, _p2p_parity(L, comm, rank, world, 2 * world + 3, H, eps,
+                                           mode == "parity2", calls=2))
             assert ops.device_error() == (0, 0)
             q.put((rank, ("ok", worst)))
         else:  # "timeout": rank 1 never arrives; rank 0's bounded wait must report it
+            report = (None, None)
             if rank == 0:
+                slot0, nb = C.c_void_p(), C.c_size_t()
+                check(L.msgl_tp_p2p_buffer(comm.h, 0, C.byref(slot0), C.byref(nb)))
                 x = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
                 res = torch.zeros(T, H, dtype=torch.float32, device="cuda")
                 w = torch.ones(H, dtype=torch.bfloat16, device="cuda")
                 check(L.msgl_tp_fused_allreduce_add_rmsnorm(
-                    comm.h, slots[0], x.data_ptr(), res.data_ptr(), w.data_ptr(), T, H, eps, 0,
+                    comm.h, slot0, x.data_ptr(), res.data_ptr(), w.data_ptr(), T, H, eps, 0,
                     torch.cuda.current_stream().cuda_stream))
                 torch.cuda.synchronize()
                 err = ops.device_error()
                 # the context stays usable after the timeout
                 y = (torch.ones(4, device="cuda") * 2).sum().item()
-                q.put((rank, ("ok", err, y)))
-            else:
-                q.put((rank, ("ok", None, None)))
+                report = (err, y)
             dist.barrier()  # rank 1 stays alive (its region mapped) until rank 0 is done
+            # the documented recovery: a new communicator on every rank, then calls work again
+            comm.close()
+            comm = new_comm()
+            worst = _p2p_parity(L, comm, rank, world, T, H, eps, False, calls=2)
+            assert ops.device_error() == (0, 0)
+            q.put((rank, ("ok", report[0], report[1], worst)))
     except Exception as e:  # noqa: BLE001
         q.put((rank, repr(e)))
     finally:
@@ -256,25 +285,30 @@ def _run_p2p(mode, world=2):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("two_shot", [False, True])
 @pytest.mark.parametrize("world", [2, 4, 8])
-def test_fused_p2p_allreduce_add_rmsnorm(world):
-    """One-kernel all-reduce + add + RMSNorm over peer memory vs an fp32 reference (residual
-    bit-exact: same additions in the same order), identical bits on every rank, 4 calls in a
-    row (epoch flags)."""
+def test_fused_p2p_allreduce_add_rmsnorm(world, two_shot):
+    """All-reduce + add + RMSNorm in one kernel over peer memory, one-shot (every rank reduces
+    every row) and two-shot (each rank reduces its row block and stores the normed rows into
+    every rank's slot 2), vs an fp32 reference: residual bit-exact (same additions in the same
+    order), identical bits on every rank, 4 calls in a row (epoch flags), then an odd row count."""
     if not torch.cuda.is_available() or torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
-    res = _run_p2p("parity", world)
+    res = _run_p2p("parity2" if two_shot else "parity", world)
     assert all(res[r][0] == "ok" for r in range(world)), res
 
 
 @pytest.mark.gpu
 def test_fused_p2p_allreduce_timeout_2gpu():
     """A rank that never arrives: the other rank's bounded wait ends, MSGL_ERR_TIMEOUT (5) is in
-    its error word, and its CUDA context keeps working. No GPU fault, no hang."""
+    its error word, and its CUDA context keeps working. No GPU fault, no hang. Then the
+    documented recovery: both ranks rebuild the communicator and fused calls give correct
+    results again."""
     if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     res = _run_p2p("timeout")
-    assert res[0][0] == "ok", res
-    _, err, y = res[0]
+    assert res[0][0] == "ok" and res[1][0] == "ok", res
+    _, err, y, worst = res[0]
     assert err[0] == 5 and err[1] in (500, 501), err  # MSGL_ERR_TIMEOUT at a flag wait
     assert y == 8.0
+    assert worst < 1e-2
