@@ -152,32 +152,39 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------------ CPU reference
-class CpuReference:
-    """The decode step on the reference CPU code, timed on a bounded sample.
+class CpuModelRef:
+    """A step of the model on the reference CPU code, timed on a bounded sample.
 
-    Each worker thread carries one token through one layer's four projections (the reference's
-    Linear::forward, weights held in persistent Linear objects as in a loaded model) and one
-    request's attention over the 2048-token context (the C restatement: the reference has no
-    paged / GQA attention), then one token through lm_head. `threads` tokens therefore advance
-    one layer per sample; the full step (128 tokens x 36 layers + lm_head) extrapolates
-    linearly."""
+    Each worker thread carries one token through one decoder layer: the layer's projections by
+    the reference's Linear::forward on persistent weights (as in a loaded model) -- qkv, o_proj,
+    and gate_up + down (dense) or the router and top_k experts' gate_up + down (MoE, the expert
+    loop of qwen3_moe.cpp:62-111) -- plus one request's attention over `ctx` tokens (the C
+    restatement: the reference has no paged / GQA attention). Another sample carries one token
+    through lm_head. `threads` tokens therefore advance one layer per sample and a step of
+    `tokens` tokens through `layers` layers (+ `lm_rows` lm_head rows) extrapolates linearly."""
 
-    def __init__(self, threads=None):
+    def __init__(self, cfg, ctx, threads=None):
         from oracle import Oracle, RefLib
         self.ref, self.orc = RefLib(), Oracle()
         t = threads or min(CPU_THREADS, os.cpu_count() or 1)
         self.threads = max(1, t)
-        H, I, V, D = CFG8B["hidden"], CFG8B["inter"], CFG8B["vocab"], 128
-        hq, hkv = CFG8B["num_q_heads"], CFG8B["num_kv_heads"]
-        self.dims = (H, V, D, hq, hkv)
+        self.cfg, self.ctx = cfg, int(ctx)
+        H, V, D = cfg["hidden"], cfg["vocab"], 128
+        hq, hkv = cfg["num_q_heads"], cfg["num_kv_heads"]
+        E, k, Im = cfg.get("num_experts", 0), cfg.get("top_k", 0), cfg.get("moe_inter", 0)
         L = self.ref.lib
+        shapes = [((hq + 2 * hkv) * D, H), (H, hq * D)]
+        if E:  # router, then top_k distinct experts (a token's route)
+            shapes += [(E, H)] + [(2 * Im, H), (H, Im)] * k
+        else:
+            shapes += [(2 * cfg["inter"], H), (H, cfg["inter"])]
         self.handles = []
-        for n, k in [((hq + 2 * hkv) * D, H), (H, hq * D), (2 * I, H), (H, I)]:
-            w = np.full((n, k), 0.01, np.float32)  # values do not change fp32 loop timing
-            self.handles.append((L.ref_linear_create(w.ctypes.data, k, n), n, k))
+        for n, kk in shapes:
+            w = np.full((n, kk), 0.01, np.float32)  # values do not change fp32 loop timing
+            self.handles.append((L.ref_linear_create(w.ctypes.data, kk, n), n, kk))
         wl = np.full((V, H), 0.01, np.float32)
         self.lm = L.ref_linear_create(wl.ctypes.data, H, V)
-        ctx_pages = CTX // PAGE
+        ctx_pages = -(-self.ctx // PAGE)
         rng = np.random.default_rng(0)
         self.kp = rng.standard_normal((ctx_pages * PAGE, hkv * D)).astype(np.float32)
         self.vp = rng.standard_normal((ctx_pages * PAGE, hkv * D)).astype(np.float32)
@@ -199,8 +206,15 @@ class CpuReference:
             t.join()
         return time.perf_counter() - t0
 
-    def sample(self, layers=36):
-        H, V, D, hq, hkv = self.dims
+    def _timed_pair(self):
+        """Wall seconds of one layer sample and of one lm_head sample (threads tokens each)."""
+        return self._last
+
+    def sample(self, tokens, lm_rows, layers):
+        """(tokens per second of the full step, description of the sample)."""
+        cfg = self.cfg
+        H, V, D = cfg["hidden"], cfg["vocab"], 128
+        hq, hkv = cfg["num_q_heads"], cfg["num_kv_heads"]
         L = self.ref.lib
 
         def layer_worker():
@@ -209,7 +223,8 @@ class CpuReference:
                 out = np.empty((1, n), np.float32)
                 L.ref_linear_run(h, xin.ctypes.data, 1, out.ctypes.data)
             q = np.full((1, hq * D), 0.01, np.float32)
-            self.orc.paged_attention(q, self.kp, self.vp, self.pt, [CTX], [0, 1], hq, hkv, D, PAGE)
+            self.orc.paged_attention(q, self.kp, self.vp, self.pt, [self.ctx], [0, 1], hq, hkv, D,
+                                     PAGE)
 
         def lm_worker():
             xin = np.full((1, H), 0.1, np.float32)
@@ -218,15 +233,77 @@ class CpuReference:
 
         w_layer = self._timed(layer_worker)
         w_lm = self._timed(lm_worker)
-        step_s = BATCH / self.threads * (layers * w_layer + w_lm)
-        desc = (f"{self.threads} tokens x 1 of 36 layers (4 projections, reference "
-                f"Linear::forward; attention over 2048 tokens, C restatement) + {self.threads} "
-                f"tokens x lm_head, extrapolated to 128 tokens x 36 layers; fp32")
-        return BATCH / step_s, desc
+        self._last = (w_layer, w_lm)
+        step_s = (tokens * layers * w_layer + lm_rows * w_lm) / self.threads
+        desc = (f"{self.threads} tokens x 1 of {layers} layers (projections by the reference "
+                f"Linear::forward{', MoE expert loop' if cfg.get('num_experts') else ''}; "
+                f"attention over {self.ctx} tokens, C restatement) + {self.threads} tokens x "
+                f"lm_head, extrapolated to {tokens} tokens x {layers} layers + {lm_rows} lm_head "
+                f"rows; fp32")
+        return tokens / step_s, desc
+
+
+class CpuReference(CpuModelRef):
+    """The Qwen3-8B decode step (128 tokens, context 2048) on the reference CPU code."""
+
+    def __init__(self, threads=None):
+        super().__init__(CFG8B, CTX, threads)
+
+    def sample(self, layers=36):
+        return super().sample(BATCH, BATCH, layers)
+
+
+def reference_workload(name):
+    """(metric, value, sample, config) of a non-default workload on the reference CPU code: the
+    same sample as that workload's cpu_baseline."""
+    if name == "qwen3-0.6b-greedy":
+        cpu = CpuModelRef(dict(CFG06B, max_position=512), 144)
+        _, sample = cpu.sample(1, 1, 1)
+        w_layer, w_lm = cpu._timed_pair()
+        run_s = ((4 * 128 + 4 * 31) * 28 * w_layer + 4 * 32 * w_lm) / cpu.threads
+        cpu.close()
+        return ("Qwen3-0.6B greedy generation tok/s (4 x 128-token prompts, 32 new tokens each)",
+                128 / run_s, sample, cpu.threads, {"workload": name, "model_arch": "Qwen3-0.6B"})
+    if name == "qwen3-0.6b-decode-ragged":
+        ctx = np.random.default_rng(2).integers(512, 4097, 64)
+        cpu = CpuModelRef(CFG06B, int(ctx.mean()))
+        v, sample = cpu.sample(64, 64, 28)
+        cpu.close()
+        return ("Qwen3-0.6B decode tok/s (batch 64, ctx U[512,4096], permuted pages)", v, sample,
+                cpu.threads, {"workload": name, "model_arch": "Qwen3-0.6B", "global_batch": 64})
+    if name == "qwen3-32b-mixed":
+        dctx = np.random.default_rng(2).integers(1024, 8193, 96)
+        cpu = CpuModelRef(CFG32B, int(dctx.mean()))
+        v, sample = cpu.sample(2144, 97, 64)
+        cpu.close()
+        return ("Qwen3-32B mixed chunked-prefill tok/s (2048-token chunk + 96 decodes per step)",
+                v, sample, cpu.threads, {"workload": name, "model_arch": "Qwen3-32B"})
+    cpu = CpuModelRef(CFG30BA3B, 1024)
+    v, sample = cpu.sample(256, 256, 48)
+    cpu.close()
+    return ("Qwen3-30B-A3B decode tok/s (batch 256, ctx 1024)", v, sample, cpu.threads,
+            {"workload": name, "model_arch": "Qwen3-30B-A3B", "global_batch": 256})
 
 
 def run_reference_arm(args, rank):
     if rank != 0:
+        return 0
+    if args.workload != "qwen3-8b-decode":
+        vals = []
+        for i in range(args.warmup + args.steps):
+            metric, v, sample, cores, cfg = reference_workload(args.workload)
+            if i >= args.warmup:
+                vals.append(v)
+        value = float(np.median(vals))
+        print(json.dumps({"impl": "reference", "metric": metric, "value": value, "unit": UNIT,
+                          "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                          "extrapolated": True, "higher_is_better": True, "scaling": "strong",
+                          "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
+                          "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores,
+                                           "kind": "reference", "sample": sample,
+                                           "extrapolated": True},
+                          "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}), flush=True)
         return 0
     cpu = CpuReference()
     vals = []
@@ -753,6 +830,660 @@ def run_breakdown(args, dev):
     return 0
 
 
+# ============================================================================== other workloads
+# The model shapes of the other benchmark configurations (random-init weights, synthetic inputs
+# of each configuration's shape: no dataset is involved).
+CFG06B = dict(num_layers=28, hidden=1024, num_q_heads=16, num_kv_heads=8, head_dim=128, inter=3072,
+              vocab=151936, eps=1e-6, rope_base=1e6)
+CFG32B = dict(num_layers=64, hidden=5120, num_q_heads=64, num_kv_heads=8, head_dim=128, inter=25600,
+              vocab=151936, eps=1e-6, rope_base=1e6)
+CFG30BA3B = dict(num_layers=48, hidden=2048, num_q_heads=32, num_kv_heads=4, head_dim=128, inter=0,
+                 vocab=151936, eps=1e-6, rope_base=1e6, num_experts=128, top_k=8, moe_inter=768,
+                 norm_topk=True)
+
+
+def load_peaks():
+    try:
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        return {}
+
+
+def scattered_pages(ctx_lens, seed, extra=16):
+    """Page tables for requests of the given context lengths, their pages a random permutation
+    of the pool (Fisher-Yates with `seed`). Returns (num_pages, page_table [B, width])."""
+    per = [-(-int(c) // PAGE) for c in ctx_lens]
+    num_pages = sum(per) + extra
+    perm = np.random.default_rng(seed).permutation(num_pages).astype(np.int32)
+    pt = np.zeros((len(per), max(per)), np.int32)
+    off = 0
+    for r, n in enumerate(per):
+        pt[r, :n] = perm[off:off + n]
+        off += n
+    return num_pages, pt
+
+
+def decode_host(pt, ctx, vocab, seed=1):
+    """Host arrays of one decode step at contexts `ctx` (each request's last token)."""
+    B = len(ctx)
+    ctx = np.asarray(ctx, np.int32)
+    pos = (ctx - 1).astype(np.int32)
+    slots = (pt[np.arange(B), pos // PAGE] * PAGE + pos % PAGE).astype(np.int32)
+    return dict(input_ids=np.random.default_rng(seed).integers(0, vocab, B).astype(np.int32),
+                positions=pos, slot_mapping=slots, page_table=np.ascontiguousarray(pt),
+                seq_lens=ctx.copy(), q_indptr=np.arange(B + 1, dtype=np.int32),
+                last_idx=np.arange(B, dtype=np.int32))
+
+
+def fill_kv(model, layers, hkv_l, dev):
+    """Synthetic KV cache contents: every pool N(0, 1) bf16 (seed 4)."""
+    import torch
+
+    from msgl import ops
+    from msgl.model import device_view
+    for l in range(layers):
+        k, v, n = model.kv_pool(l)
+        for j, ptr in enumerate((k, v)):
+            ops.fill_normal_(device_view(ptr, (n * hkv_l * 128,), torch.bfloat16), seed=4,
+                             stream_id=2 * l + j, std=1.0)
+
+
+def time_kernel(fn, reps, stream):
+    """Mean device time (ms) of `fn` over `reps` launches on `stream` (CUDA events, after one
+    warm-up launch)."""
+    import torch
+    fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+class Rig:
+    """Per-process setup shared by the workloads: device, stream, rank helpers."""
+
+    def __init__(self, args, rank, world, local_rank):
+        import torch
+        import torch.distributed as dist
+
+        import msgl
+        self.args, self.rank, self.world = args, rank, world
+        torch.cuda.set_device(local_rank)
+        self.dev = torch.device("cuda", local_rank)
+        self.local_rank = local_rank
+        self.lib = msgl.lib()
+        self.stream = torch.cuda.Stream()
+        torch.cuda.set_stream(self.stream)
+        self.sp = self.stream.cuda_stream
+        self.dist = dist
+        self.comm = None
+        if world > 1:
+            from msgl.model import TPComm
+            uid = [TPComm.new_unique_id() if rank == 0 else None]
+            dist.broadcast_object_list(uid, src=0)
+            self.comm = TPComm(rank, world, uid[0])
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+
+    def max_over_ranks(self, x):
+        if self.world == 1:
+            return x
+        import torch
+        t = torch.tensor([x], dtype=torch.float64, device=self.dev)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def blocks(self, fn):
+        return timed_blocks(fn, self.args, self.world, self.dev, self.stream, self.barrier,
+                            self.max_over_ranks)
+
+    def model(self, cfg, max_tokens, max_reqs):
+        from msgl.model import Qwen3Model
+        m = Qwen3Model(cfg, max_tokens=max_tokens, max_reqs=max_reqs, tp_rank=self.rank,
+                       tp_size=self.world)
+        if self.comm is not None:
+            m.set_tp(self.comm)
+        m.random_init(seed=0, std=0.02)
+        return m
+
+    def launches(self, fn):
+        """Kernels of ours launched by one eager call of fn."""
+        import torch
+        n0 = self.lib.msgl_kernel_launches()
+        fn()
+        n = self.lib.msgl_kernel_launches() - n0
+        torch.cuda.synchronize()
+        return int(n)
+
+    def close(self):
+        if self.comm is not None:
+            self.comm.close()
+
+
+def contract_line(rig, metric, value, unit, ms, blocks, config, dtype="bf16", **extra):
+    line = {"metric": metric, "value": value, "unit": unit, "n_gpus": rig.world,
+            "steps": rig.args.steps, "warmup": rig.args.warmup, "ms_per_step": ms,
+            "blocks_ms_per_step": [round(b, 4) for b in blocks], "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": dtype,
+            "data": "synthetic (random-init weights, N(0,1) KV, random token ids)",
+            "config": config}
+    line.update(extra)
+    return line
+
+
+def e2e_host_batch(host, is_decode, max_seq_len, max_q_len, shared=None, tail=None):
+    """Pinned host copies of a step's arrays and the msgl_batch (host pointers) for
+    msgl_model_step_host."""
+    import ctypes as C
+
+    import torch
+
+    from msgl.model import DECODE_TAIL_DETECT, SHARED_PREFIX_DETECT, BatchT
+    pinned = {k: torch.from_numpy(np.ascontiguousarray(v)).pin_memory() for k, v in host.items()}
+    B = host["seq_lens"].size
+    hb = BatchT(int(host["input_ids"].size), B, int(is_decode), host["page_table"].shape[1],
+                max_seq_len, max_q_len,
+                *[pinned[k].data_ptr() for k in ("input_ids", "positions", "slot_mapping",
+                                                  "page_table", "seq_lens", "q_indptr", "last_idx")],
+                SHARED_PREFIX_DETECT if shared is None else shared,
+                DECODE_TAIL_DETECT if tail is None else tail)
+    out = torch.empty(B, dtype=torch.int32).pin_memory()
+    return pinned, hb, out, C.addressof(hb)
+
+
+# ---------------------------------------------------------------- C2: 0.6B ragged decode
+def run_c2(rig):
+    """Qwen3-0.6B decode step at batch 64, contexts U[512, 4096] (seed 2), every request's pages a
+    random permutation of the pool (seed 3), KV N(0, 1). value: 64 tokens / step (graph replay);
+    roofline: the plain paged decode kernel (no shared prefix here) over the 28 layers' pools,
+    KV bytes = sum(ctx) x Hkv x 128 x 2 B x 2 per launch."""
+    import torch
+
+    import msgl
+    from msgl import ops
+    from msgl.model import make_step, shard_plan
+    B = 64
+    cfg = dict(CFG06B, max_position=4096 + PAGE)
+    ctx = np.random.default_rng(2).integers(512, 4097, B).astype(np.int32)
+    num_pages, pt = scattered_pages(ctx, seed=3)
+    plan = shard_plan(cfg["num_q_heads"], cfg["num_kv_heads"], cfg["inter"], cfg["vocab"], rig.rank, rig.world)
+    hq, hkv = plan["q_heads"], plan["kv_heads"]
+    model = rig.model(cfg, B, B)
+    model.alloc_kv(num_pages)
+    fill_kv(model, cfg["num_layers"], hkv, rig.dev)
+    host = decode_host(pt, ctx, cfg["vocab"])
+    sb = make_step(host, True, rig.dev, int(ctx.max()), 1)
+    assert sb.struct.shared_prefix_pages == 0
+    nxt = torch.empty(B, dtype=torch.int32, device=rig.dev)
+    per_step = rig.launches(lambda: model.forward(sb, out=nxt))
+    for _ in range(max(rig.args.warmup, 3)):
+        model.forward(sb, out=nxt, graph=True)
+    with ClockSampler(rig.local_rank) as clk:
+        blocks = rig.blocks(lambda: model.forward(sb, out=nxt, graph=True))
+    ms = float(np.median(blocks))
+    assert ops.device_error() == (0, 0)
+    pinned, hb, out_host, hbp = e2e_host_batch(host, True, int(ctx.max()), 1)
+    step_host = lambda: msgl.check(rig.lib.msgl_model_step_host(model.h, hbp, out_host.data_ptr(), 1, rig.sp))
+    for _ in range(max(rig.args.warmup, 3)):
+        step_host()
+    blocks_e2e = rig.blocks(step_host)
+    assert torch.equal(out_host.to(rig.dev), nxt)
+    # roofline: the plain decode kernel alone on every layer's pool
+    q = ops.fill_normal_(torch.empty(B, hq, 128, dtype=torch.bfloat16, device=rig.dev), seed=5)
+    aout = torch.empty_like(q)
+    ws = ops.attention_workspace(B, int(ctx.max()), hq, hkv, rig.dev)
+    pt_d, seq_d = sb.tensors["page_table"], sb.tensors["seq_lens"]
+    pools = [model.kv_pool(l) for l in range(cfg["num_layers"])]
+    li = [0]
+
+    def attn():
+        k, v, n = pools[li[0] % len(pools)]
+        li[0] += 1
+        msgl.check(rig.lib.msgl_paged_attention_decode(
+            q.data_ptr(), k, v, n, pt_d.data_ptr(), pt_d.shape[1], seq_d.data_ptr(), B,
+            int(ctx.max()), hq, hkv, 128, PAGE, 1.0 / 128 ** 0.5, aout.data_ptr(), ws.data_ptr(),
+            ws.numel(), rig.sp))
+
+    attn_ms = time_kernel(attn, 3 * cfg["num_layers"], rig.stream)
+    kv_bytes = int(ctx.astype(np.int64).sum()) * hkv * 128 * 2 * 2
+    peaks = load_peaks()
+    peak = peaks.get("hbm_gbs", 6650.0)
+    achieved = kv_bytes / (attn_ms * 1e-3) / 1e9
+    if rig.rank != 0:
+        return 0
+    cpu = CpuModelRef(cfg, int(ctx.mean()))
+    cpu_val, sample = cpu.sample(B, B, cfg["num_layers"])
+    cpu.close()
+    line = contract_line(
+        rig, "Qwen3-0.6B decode tok/s (batch 64, ctx U[512,4096], permuted pages)", B / (ms * 1e-3),
+        UNIT, ms, blocks,
+        {"workload": "qwen3-0.6b-decode-ragged", "model_arch": "Qwen3-0.6B", "global_batch": B,
+         "seq_len": "U[512,4096] (seed 2), mean %d" % int(ctx.mean()), "page_size": PAGE,
+         "pages": "random permutation of the pool (seed 3)", "parallelism": f"tp{rig.world}",
+         "l2": "inputs larger than L2 (%.1f GB of KV + 1.2 GB of weights per step)"
+               % (kv_bytes * cfg["num_layers"] / 1e9 * rig.world)},
+        e2e={"value": B / (float(np.median(blocks_e2e)) * 1e-3), "unit": UNIT,
+             "h2d_bytes_per_step": sum(v.nbytes for v in host.values()), "d2h_bytes_per_step": B * 4,
+             "ms_per_step": float(np.median(blocks_e2e)),
+             "blocks_ms_per_step": [round(b, 4) for b in blocks_e2e]},
+        roofline={"kernel": "paged_decode_kernel", "bound": "hbm", "achieved": achieved,
+                  "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": None,
+                  "algorithmic_bytes_per_launch": kv_bytes, "launch_ms": attn_ms,
+                  "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback"},
+        cpu_baseline={"value": cpu_val, "unit": UNIT, "cores": cpu.threads, "kind": "reference",
+                      "sample": sample, "extrapolated": True},
+        clocks=clk.summary(), gpu_launches=per_step * rig.args.steps,
+        gpu_launches_per_step=per_step)
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------- C5: 30B-A3B MoE
+def run_c5(rig):
+    """Qwen3-30B-A3B (48 layers, 128 experts, top-8, moe_intermediate 768): decode step at batch
+    256, context 1024 (value, graph replay), and one 4096-token prefill chunk (reported beside
+    it). roofline: the grouped expert gate_up + SwiGLU GEMM on a decode step's routing (256
+    tokens x top-8 over 128 experts) -- algorithmic bytes = the gate_up weights of the experts
+    the routing touches."""
+    import torch
+
+    import msgl
+    from msgl import ops
+    from msgl.model import BatchBuilder, PagePool, Request, make_step, shard_plan
+    B, CTXD, PRE = 256, 1024, 4096
+    cfg = dict(CFG30BA3B, max_position=PRE + PAGE)
+    E, K, H = cfg["num_experts"], cfg["top_k"], cfg["hidden"]
+    plan = shard_plan(cfg["num_q_heads"], cfg["num_kv_heads"], cfg["moe_inter"], cfg["vocab"],
+                      rig.rank, rig.world)
+    hkv = plan["kv_heads"]
+    Im = cfg["moe_inter"] // rig.world
+    ctx = np.full(B, CTXD, np.int32)
+    num_pages, pt = scattered_pages(ctx, seed=3, extra=PRE // PAGE + 16)
+    model = rig.model(cfg, PRE, B)
+    model.alloc_kv(num_pages)
+    fill_kv(model, cfg["num_layers"], hkv, rig.dev)
+    host = decode_host(pt, ctx, cfg["vocab"])
+    sb = make_step(host, True, rig.dev, CTXD, 1)
+    nxt = torch.empty(B, dtype=torch.int32, device=rig.dev)
+    per_step = rig.launches(lambda: model.forward(sb, out=nxt))
+    for _ in range(max(rig.args.warmup, 3)):
+        model.forward(sb, out=nxt, graph=True)
+    with ClockSampler(rig.local_rank) as clk:
+        blocks = rig.blocks(lambda: model.forward(sb, out=nxt, graph=True))
+    ms = float(np.median(blocks))
+    pinned, hb, out_host, hbp = e2e_host_batch(host, True, CTXD, 1)
+    step_host = lambda: msgl.check(rig.lib.msgl_model_step_host(model.h, hbp, out_host.data_ptr(), 1, rig.sp))
+    for _ in range(max(rig.args.warmup, 3)):
+        step_host()
+    blocks_e2e = rig.blocks(step_host)
+    # the 4096-token prefill chunk: one request on the pages no decode request holds
+    pool = PagePool(0)
+    pool.free = sorted(set(range(num_pages)) - set(pt.ravel().tolist()))
+    req = Request(list(np.random.default_rng(7).integers(0, cfg["vocab"], PRE)))
+    sbp = BatchBuilder(pool).build([req], decode=False, device=rig.dev)
+    nxp = torch.empty(1, dtype=torch.int32, device=rig.dev)
+    for _ in range(2):
+        model.forward(sbp, out=nxp, graph=True)
+    blocks_pre = rig.blocks(lambda: model.forward(sbp, out=nxp, graph=True))
+    ms_pre = float(np.median(blocks_pre))
+    assert ops.device_error() == (0, 0)
+    # roofline: grouped gate_up + SwiGLU alone on a decode step's routing
+    rng = np.random.default_rng(8)
+    ids = np.stack([rng.choice(E, K, replace=False) for _ in range(B)]).astype(np.int32)
+    ids_d = torch.from_numpy(ids).to(rig.dev)
+    off = torch.zeros(E + 1, dtype=torch.int32, device=rig.dev)
+    tok = torch.empty(B * K, dtype=torch.int32, device=rig.dev)
+    pos = torch.empty(B * K, dtype=torch.int32, device=rig.dev)
+    msgl.check(rig.lib.msgl_moe_permute(ids_d.data_ptr(), B, K, E, off.data_ptr(), tok.data_ptr(),
+                                        pos.data_ptr(), rig.sp))
+    xs = ops.fill_normal_(torch.empty(B * K, H, dtype=torch.bfloat16, device=rig.dev), seed=9)
+    wgu = ops.fill_normal_(torch.empty(E, 2 * Im, H, dtype=torch.bfloat16, device=rig.dev), seed=10,
+                           std=0.02)
+    act = torch.empty(B * K, Im, dtype=torch.bfloat16, device=rig.dev)
+    gws = torch.zeros(rig.lib.msgl_grouped_gemm_workspace_size(B * K, E), dtype=torch.uint8,
+                      device=rig.dev)
+    gu = lambda: msgl.check(rig.lib.msgl_grouped_gemm_gate_up_silu(
+        xs.data_ptr(), wgu.data_ptr(), act.data_ptr(), off.data_ptr(), E, Im, H, B * K,
+        gws.data_ptr(), gws.numel(), rig.sp))
+    gu_ms = time_kernel(gu, 20, rig.stream)
+    touched = len(np.unique(ids))
+    gu_bytes = touched * 2 * Im * H * 2
+    peaks = load_peaks()
+    peak = peaks.get("hbm_gbs", 6650.0)
+    achieved = gu_bytes / (gu_ms * 1e-3) / 1e9
+    if rig.rank != 0:
+        return 0
+    cpu = CpuModelRef(cfg, CTXD)
+    cpu_val, sample = cpu.sample(B, B, cfg["num_layers"])
+    cpu.close()
+    line = contract_line(
+        rig, "Qwen3-30B-A3B decode tok/s (batch 256, ctx 1024)", B / (ms * 1e-3), UNIT, ms, blocks,
+        {"workload": "qwen3-30b-a3b", "model_arch": "Qwen3-30B-A3B", "global_batch": B,
+         "seq_len": CTXD, "page_size": PAGE, "experts": E, "top_k": K,
+         "parallelism": f"tp{rig.world}",
+         "prefill_chunk": {"tokens": PRE, "ms": ms_pre, "tok_s": PRE / (ms_pre * 1e-3),
+                           "blocks_ms": [round(b, 3) for b in blocks_pre]},
+         "l2": "inputs larger than L2 (expert weights ~58 GB + KV 25.8 GB per decode step)"},
+        e2e={"value": B / (float(np.median(blocks_e2e)) * 1e-3), "unit": UNIT,
+             "h2d_bytes_per_step": sum(v.nbytes for v in host.values()), "d2h_bytes_per_step": B * 4,
+             "ms_per_step": float(np.median(blocks_e2e)),
+             "blocks_ms_per_step": [round(b, 4) for b in blocks_e2e]},
+        roofline={"kernel": "gemm_kernel<grouped, SWIGLU> (experts gate_up)", "bound": "hbm",
+                  "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                  "traffic": None, "algorithmic_bytes_per_launch": gu_bytes,
+                  "experts_touched": touched, "launch_ms": gu_ms,
+                  "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback"},
+        cpu_baseline={"value": cpu_val, "unit": UNIT, "cores": cpu.threads, "kind": "reference",
+                      "sample": sample, "extrapolated": True},
+        clocks=clk.summary(), gpu_launches=per_step * rig.args.steps,
+        gpu_launches_per_step=per_step)
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------- C4: 32B mixed chunked prefill
+def run_c4(rig):
+    """Qwen3-32B mixed chunked prefill: each step = one 2048-token chunk of one of 4 prompts of
+    8192 tokens (chunks in order, 16 distinct steps cycled) + 96 decode requests at contexts
+    U[1024, 8192] (seed 2): 2144 tokens per step. The decode requests are the batch's tail
+    (decode_tail = 96: split-KV decode kernel for them, extend kernel for the chunk). On N GPUs:
+    tensor parallel over the N ranks. On 1 GPU the full model does not fit (64 GB of weights +
+    ~125 GB of KV), so the run is ONE RANK OF TP8: the shapes of a TP8 shard (8 q heads, 1 kv
+    head, 3200 intermediate columns, 18992 vocab rows) as a standalone model, without the 128
+    all-reduces per step. roofline: the chunk's gate_up + SwiGLU GEMM (M = 2144) against the
+    sustained bf16 peak; the extend attention of the chunk is reported beside it."""
+    import torch
+
+    from msgl import ops
+    from msgl.model import make_step, shard_plan
+    NDEC, CH, NPROMPT, PLEN = 96, 2048, 4, 8192
+    if rig.world == 1:
+        cfg = dict(CFG32B, num_q_heads=8, num_kv_heads=1, inter=3200, vocab=-(-151936 // 8))
+        par = "tp8 rank shard on 1 GPU (no all-reduce)"
+    else:
+        cfg = dict(CFG32B)
+        par = f"tp{rig.world}"
+    cfg["max_position"] = PLEN + PAGE
+    plan = shard_plan(cfg["num_q_heads"], cfg["num_kv_heads"], cfg["inter"], cfg["vocab"], rig.rank, rig.world)
+    hq, hkv, I_l = plan["q_heads"], plan["kv_heads"], plan["inter_cols"]
+    H = cfg["hidden"]
+    dctx = np.random.default_rng(2).integers(1024, 8193, NDEC).astype(np.int32)
+    # prompts first (4 x 512 pages), then the decode requests' pages, all scattered
+    lens = [PLEN] * NPROMPT + list(dctx)
+    num_pages, pt_all = scattered_pages(lens, seed=3)
+    ppt, dpt = pt_all[:NPROMPT], pt_all[NPROMPT:]
+    model = rig.model(cfg, CH + NDEC, NDEC + 1)
+    model.alloc_kv(num_pages)
+    fill_kv(model, cfg["num_layers"], hkv, rig.dev)
+    width = pt_all.shape[1]
+    rng = np.random.default_rng(1)
+    steps = []
+    for k in range(NPROMPT * (PLEN // CH)):
+        p, c = k // (PLEN // CH), k % (PLEN // CH)
+        pos_c = np.arange(c * CH, (c + 1) * CH, dtype=np.int32)
+        dpos = dctx - 1
+        positions = np.concatenate([pos_c, dpos]).astype(np.int32)
+        slots = np.concatenate([ppt[p, pos_c // PAGE] * PAGE + pos_c % PAGE,
+                                dpt[np.arange(NDEC), dpos // PAGE] * PAGE + dpos % PAGE]).astype(np.int32)
+        host = dict(input_ids=rng.integers(0, cfg["vocab"], CH + NDEC).astype(np.int32),
+                    positions=positions, slot_mapping=slots,
+                    page_table=np.ascontiguousarray(np.concatenate([ppt[p:p + 1], dpt])[:, :width]),
+                    seq_lens=np.concatenate([[(c + 1) * CH], dctx]).astype(np.int32),
+                    q_indptr=np.concatenate([[0], CH + np.arange(NDEC + 1)]).astype(np.int32),
+                    last_idx=np.concatenate([[CH - 1], CH + np.arange(NDEC)]).astype(np.int32))
+        steps.append((host, make_step(host, False, rig.dev, int(max(PLEN, dctx.max())), CH)))
+    assert steps[0][1].struct.decode_tail == NDEC
+    nxt = torch.empty(NDEC + 1, dtype=torch.int32, device=rig.dev)
+    per_step = rig.launches(lambda: model.forward(steps[0][1], out=nxt))
+    it = [0]
+
+    def step():
+        model.forward(steps[it[0] % len(steps)][1], out=nxt)
+        it[0] += 1
+
+    for _ in range(max(rig.args.warmup, 3)):
+        step()
+    with ClockSampler(rig.local_rank) as clk:
+        blocks = rig.blocks(step)
+    ms = float(np.median(blocks))
+    # e2e: host arrays through msgl_model_step_host (no graph for a prefill step)
+    import ctypes as C
+
+    import msgl
+    hbs = [e2e_host_batch(h, False, int(max(PLEN, dctx.max())), CH, shared=0) for h, _ in steps]
+    ie = [0]
+
+    def step_host():
+        _, _, out_h, hbp = hbs[ie[0] % len(hbs)]
+        ie[0] += 1
+        msgl.check(rig.lib.msgl_model_step_host(model.h, hbp, out_h.data_ptr(), 0, rig.sp))
+
+    for _ in range(max(rig.args.warmup, 3)):
+        step_host()
+    blocks_e2e = rig.blocks(step_host)
+    assert ops.device_error() == (0, 0)
+    # roofline: the chunk step's gate_up + SwiGLU at M = 2144 (tensor-bound)
+    M = CH + NDEC
+    x = ops.fill_normal_(torch.empty(M, H, dtype=torch.bfloat16, device=rig.dev), seed=6)
+    w = ops.fill_normal_(torch.empty(2 * I_l, H, dtype=torch.bfloat16, device=rig.dev), seed=7, std=0.02)
+    gws = ops.gemm_workspace(M, 2 * I_l, H, rig.dev)
+    g_ms = time_kernel(lambda: ops.gate_up_silu(x, w, workspace=gws), 20, rig.stream)
+    flops = 2.0 * M * 2 * I_l * H
+    peaks = load_peaks()
+    tpeak = peaks.get("bf16_tflops_sustained", 1400.0)
+    achieved = flops / (g_ms * 1e-3) / 1e12
+    # extend attention of the last chunk (2048 queries over 8192 keys, causal) alone
+    kp, vp, nsl = model.kv_pool(0)
+    q = ops.fill_normal_(torch.empty(CH, hq, 128, dtype=torch.bfloat16, device=rig.dev), seed=8)
+    ao = torch.empty_like(q)
+    ptc = torch.from_numpy(np.ascontiguousarray(ppt[:1])).to(rig.dev)
+    seqc = torch.tensor([PLEN], dtype=torch.int32, device=rig.dev)
+    qip = torch.tensor([0, CH], dtype=torch.int32, device=rig.dev)
+    ext = lambda: msgl.check(rig.lib.msgl_paged_attention_extend(
+        q.data_ptr(), kp, vp, nsl, ptc.data_ptr(), ptc.shape[1], seqc.data_ptr(), qip.data_ptr(), 1,
+        CH, hq, hkv, 128, PAGE, 1.0 / 128 ** 0.5, ao.data_ptr(), rig.sp))
+    e_ms = time_kernel(ext, 10, rig.stream)
+    # causal FLOPs of the chunk: query i sees 6144 + i + 1 keys; QK^T and PV: 4 x 128 per pair
+    pairs = sum(PLEN - CH + i + 1 for i in range(CH))
+    e_flops = 4.0 * 128 * pairs * hq
+    if rig.rank != 0:
+        return 0
+    cpu = CpuModelRef(CFG32B, int(dctx.mean()))
+    cpu_val, sample = cpu.sample(M, NDEC + 1, CFG32B["num_layers"])
+    cpu.close()
+    line = contract_line(
+        rig, "Qwen3-32B mixed chunked-prefill tok/s (2048-token chunk + 96 decodes per step)",
+        M / (ms * 1e-3), UNIT, ms, blocks,
+        {"workload": "qwen3-32b-mixed", "model_arch": "Qwen3-32B", "tokens_per_step": M,
+         "chunk": CH, "prompts": f"{NPROMPT} x {PLEN}", "decodes": NDEC,
+         "decode_ctx": "U[1024,8192] (seed 2)", "page_size": PAGE, "parallelism": par,
+         "shard": {"q_heads": hq, "kv_heads": hkv, "inter_cols": I_l, "vocab_rows": plan["vocab_rows"]},
+         "l2": "inputs larger than L2 (weights %.1f GB per rank per step)" % (model.weight_bytes() / 1e9)},
+        e2e={"value": M / (float(np.median(blocks_e2e)) * 1e-3), "unit": UNIT,
+             "h2d_bytes_per_step": sum(v.nbytes for v in steps[0][0].values()),
+             "d2h_bytes_per_step": (NDEC + 1) * 4, "ms_per_step": float(np.median(blocks_e2e)),
+             "blocks_ms_per_step": [round(b, 4) for b in blocks_e2e]},
+        roofline={"kernel": "gemm_sk_kernel<SWIGLU> (chunk gate_up, M 2144)", "bound": "tensor",
+                  "achieved": achieved, "peak": tpeak, "unit": "TFLOP/s", "frac": achieved / tpeak,
+                  "traffic": None, "algorithmic_flops_per_launch": flops, "launch_ms": g_ms,
+                  "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained"
+                                 if "bf16_tflops_sustained" in peaks else "fallback",
+                  "extend_attention": {"kernel": "paged_extend_kernel", "launch_ms": e_ms,
+                                       "tflops": e_flops / (e_ms * 1e-3) / 1e12,
+                                       "frac_of_sustained": e_flops / (e_ms * 1e-3) / 1e12 / tpeak}},
+        cpu_baseline={"value": cpu_val, "unit": UNIT, "cores": cpu.threads, "kind": "reference",
+                      "sample": sample + " (full 32B model, one process)", "extrapolated": True},
+        clocks=clk.summary(), gpu_launches=per_step * rig.args.steps,
+        gpu_launches_per_step=per_step)
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------- C1: 0.6B greedy run
+def run_c1(rig):
+    """Qwen3-0.6B, 4 requests x 128 prompt tokens (seed 1), page size 16: one step = the whole
+    greedy run, prefill + 31 decode steps (32 new tokens per request); the decode steps go
+    through msgl_model_decode_steps (device-advanced metadata, one CUDA graph). value: new tokens
+    per second (128 per run). e2e: the same run through msgl_model_step_host, one call per
+    step with host arrays. roofline: the fused lm_head + argmax (the largest single launch:
+    151936 x 1024 bf16 = 311 MB)."""
+    import torch
+
+    import msgl
+    from msgl import ops
+    from msgl.model import BatchBuilder, PagePool, Request, make_step
+    NREQ, PROMPT, NEW, WIDTH = 4, 128, 32, 12
+    cfg = dict(CFG06B, max_position=512)
+    num_pages = 64
+    model = rig.model(cfg, NREQ * PROMPT, NREQ)
+    model.alloc_kv(num_pages)
+    prompts = np.random.default_rng(1).integers(0, cfg["vocab"], (NREQ, PROMPT)).tolist()
+    reqs = [Request(list(p)) for p in prompts]
+    pool = PagePool(num_pages)
+    bb = BatchBuilder(pool)
+    sbp = bb.build(reqs, decode=False, device=rig.dev, max_pages=WIDTH)
+    first = torch.empty(NREQ, dtype=torch.int32, device=rig.dev)
+    model.forward(sbp, out=first)
+    torch.cuda.synchronize()
+    for r, t in zip(reqs, first.cpu().numpy().tolist()):
+        r.cached_len = r.device_len
+        r.input_ids.append(int(t))
+    sbd = bb.build(reqs, decode=True, device=rig.dev, max_pages=WIDTH)
+    pristine = {k: v.clone() for k, v in sbd.tensors.items()}
+    free0 = torch.tensor(pool.free + [0], dtype=torch.int32, device=rig.dev)
+    top0 = torch.tensor([len(pool.free)], dtype=torch.int32, device=rig.dev)
+    free, top = free0.clone(), top0.clone()
+    log = torch.empty(NEW - 1, NREQ, dtype=torch.int32, device=rig.dev)
+
+    import ctypes as C
+
+    def run(graph=True):
+        # prefill (writes the prompt KV, emits token 1), then the metadata of the first decode
+        # step restored on the device and 31 device-driven decode steps
+        model.forward(sbp, out=first, graph=graph)
+        for k, v in pristine.items():
+            sbd.tensors[k].copy_(v, non_blocking=True)
+        free.copy_(free0, non_blocking=True)
+        top.copy_(top0, non_blocking=True)
+        msgl.check(rig.lib.msgl_model_decode_steps(model.h, C.addressof(sbd.struct), NEW - 1,
+                                                   log.data_ptr(), free.data_ptr(), top.data_ptr(),
+                                                   int(graph), rig.sp))
+
+    per_run = rig.launches(lambda: run(graph=False))
+    for _ in range(max(rig.args.warmup, 3)):
+        run()
+    with ClockSampler(rig.local_rank) as clk:
+        blocks = rig.blocks(run)
+    ms = float(np.median(blocks))
+    tokens_dev = [first.cpu().numpy().tolist()] + log.cpu().numpy().tolist()
+    # e2e: the scheduler-facing call per step with host arrays. The step metadata (positions,
+    # slots, page tables; the page allocation of the reference's LIFO pool) is staged once in
+    # persistent pinned buffers, one set per step; each step the host writes the previous step's
+    # tokens into its input ids and calls msgl_model_step_host (H2D, step, D2H, sync).
+    reqs2 = [Request(list(p)) for p in prompts]
+    bb2 = BatchBuilder(PagePool(num_pages))
+    staged = []
+    for st in range(NEW):
+        sbh = bb2.build(reqs2, decode=st > 0, device="cpu", max_pages=WIDTH)
+        h = {k: v.numpy() for k, v in sbh.tensors.items()}
+        staged.append(e2e_host_batch(h, st > 0, int(h["seq_lens"].max()), 1 if st > 0 else PROMPT,
+                                     shared=0, tail=0))
+        for r, t in zip(reqs2, tokens_dev[st]):  # lengths only: the ids are rewritten per run
+            r.cached_len = r.device_len
+            r.input_ids.append(int(t))
+    h2d_per_run = sum(sum(v.nbytes for v in pin.values()) for pin, _, _, _ in staged)
+
+    def e2e_run():
+        toks = []
+        for st, (pin, _, out_h, hbp) in enumerate(staged):
+            if st > 0:
+                pin["input_ids"].copy_(torch.tensor(toks[-1], dtype=torch.int32))
+            msgl.check(rig.lib.msgl_model_step_host(model.h, hbp, out_h.data_ptr(), 1, rig.sp))
+            toks.append(out_h.numpy().tolist())
+        return toks
+
+    for _ in range(2):
+        e2e_run()
+    tokens_host = None
+    blocks_e2e = []
+    for _ in range(rig.args.blocks):
+        rig.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(rig.args.steps):
+            tokens_host = e2e_run()
+        torch.cuda.synchronize()
+        blocks_e2e.append(rig.max_over_ranks((time.perf_counter() - t0) * 1e3 / rig.args.steps))
+    assert tokens_host == tokens_dev, "device-driven run and host-driven run disagree"
+    # roofline: lm_head + argmax alone
+    x = ops.fill_normal_(torch.empty(NREQ, cfg["hidden"], dtype=torch.bfloat16, device=rig.dev), seed=3)
+    wl = ops.fill_normal_(torch.empty(-(-cfg["vocab"] // rig.world), cfg["hidden"], dtype=torch.bfloat16,
+                                      device=rig.dev), seed=4, std=0.02)
+    lws = ops.gemm_workspace(NREQ, wl.shape[0], cfg["hidden"], rig.dev)
+    lm_ms = time_kernel(lambda: ops.lm_head_argmax(x, wl, workspace=lws), 50, rig.stream)
+    lm_bytes = wl.numel() * 2
+    peaks = load_peaks()
+    peak = peaks.get("hbm_gbs", 6650.0)
+    achieved = lm_bytes / (lm_ms * 1e-3) / 1e9
+    assert ops.device_error() == (0, 0)
+    if rig.rank != 0:
+        return 0
+    cpu = CpuModelRef(cfg, PROMPT + NEW // 2)
+    _, sample = cpu.sample(1, 1, 1)
+    H, V = cfg["hidden"], cfg["vocab"]
+    # tokens through the layers per run: the prompts, then one per request per decode step
+    tok_layers = NREQ * PROMPT + NREQ * (NEW - 1)
+    w_layer, w_lm = cpu._timed_pair()
+    run_s = (tok_layers * cfg["num_layers"] * w_layer + NREQ * NEW * w_lm) / cpu.threads
+    cpu.close()
+    line = contract_line(
+        rig, "Qwen3-0.6B greedy generation tok/s (4 x 128-token prompts, 32 new tokens each)",
+        NREQ * NEW / (ms * 1e-3), UNIT, ms, blocks,
+        {"workload": "qwen3-0.6b-greedy", "model_arch": "Qwen3-0.6B", "requests": NREQ,
+         "prompt": PROMPT, "new_tokens": NEW, "page_size": PAGE, "parallelism": f"tp{rig.world}",
+         "step": "one whole run: prefill + 31 decode steps",
+         "l2": "weights 1.2 GB read per decode step (> L2)"},
+        e2e={"value": NREQ * NEW / (float(np.median(blocks_e2e)) * 1e-3), "unit": UNIT,
+             "h2d_bytes_per_step": h2d_per_run, "d2h_bytes_per_step": NEW * NREQ * 4,
+             "ms_per_step": float(np.median(blocks_e2e)),
+             "blocks_ms_per_step": [round(b, 4) for b in blocks_e2e],
+             "timing": "host wall clock around 32 msgl_model_step_host calls per run"},
+        roofline={"kernel": "gemm_rows_kernel<ARGMAX> (lm_head + greedy)", "bound": "hbm",
+                  "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                  "traffic": None, "algorithmic_bytes_per_launch": lm_bytes, "launch_ms": lm_ms,
+                  "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback"},
+        cpu_baseline={"value": NREQ * NEW / run_s, "unit": UNIT, "cores": cpu.threads,
+                      "kind": "reference", "extrapolated": True,
+                      "sample": f"{cpu.threads} tokens x 1 of 28 layers + {cpu.threads} tokens x "
+                                f"lm_head (reference Linear::forward; attention over {PROMPT + NEW // 2} "
+                                f"tokens, C restatement), extrapolated to {tok_layers} tokens x 28 "
+                                f"layers + {NREQ * NEW} lm_head rows per run; fp32"},
+        clocks=clk.summary(), gpu_launches=per_run * rig.args.steps, gpu_launches_per_step=per_run,
+        greedy_tokens_device_equal_host=True)
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+WORKLOADS = {"qwen3-0.6b-greedy": run_c1, "qwen3-0.6b-decode-ragged": run_c2,
+             "qwen3-32b-mixed": run_c4, "qwen3-30b-a3b": run_c5}
+
+
+def run_workload(args, rank, world, local_rank):
+    rig = Rig(args, rank, world, local_rank)
+    try:
+        return WORKLOADS[args.workload](rig)
+    finally:
+        import gc
+        gc.collect()  # models (and their graphs) go before the communicator
+        rig.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -763,6 +1494,10 @@ def main():
     ap.add_argument("--blocks", type=int, default=3,
                     help="timed blocks of --steps steps each; the median block is reported")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="qwen3-8b-decode",
+                    choices=["qwen3-8b-decode", *WORKLOADS],
+                    help="qwen3-8b-decode: the headline (default); the others: the remaining "
+                         "benchmark configurations")
     ap.add_argument("--case", choices=["attention", "attention_cascade", "gemm", "gemm_qkv",
                                        "gemm_partials", "gemm_prefill", "breakdown"], default=None,
                     help="run one kernel of the step on a small single-layer case (profiling)")
@@ -782,6 +1517,8 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     try:
+        if args.workload != "qwen3-8b-decode":
+            return run_workload(args, rank, world, local_rank)
         return run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:

@@ -55,7 +55,15 @@ typedef struct {
                                 covers them; decode then runs the cascade kernel. 0: none.
                                 MSGL_SHARED_PREFIX_DETECT (msgl_model_step_host only): computed
                                 from the host page table */
+    int decode_tail;         /* mixed (chunked-prefill) batches, is_decode == 0: the last n
+                                requests each contribute exactly one query row, the last n rows
+                                of the step; attention then runs the split-KV decode kernel on
+                                them and the extend kernel on the requests before. 0: no such
+                                claim (every request through the extend kernel).
+                                MSGL_DECODE_TAIL_DETECT (msgl_model_step_host only): computed
+                                from the host q_indptr */
 } msgl_batch;
+#define MSGL_DECODE_TAIL_DETECT (-1)
 #define MSGL_SHARED_PREFIX_DETECT (-1)
 
 /* ------------------------------------------------------------------ prefix cache (host)
@@ -112,7 +120,8 @@ MSGL_API int msgl_model_kv_pool(msgl_model* m, int layer, void** k_pool, void** 
 
 /* One forward step: next_tokens [B] (device) = greedy tokens of each request's last row
  * (scheduler.cpp:117-124 on the last token, fixing D10); logits (optional, device fp32
- * [B, vocab]) receives the final logits of those rows.
+ * [B, vocab]) receives the final logits of those rows (under tensor parallelism every rank
+ * computes its vocab rows and the shards are all-gathered, so every rank gets all of them).
  * flags & MSGL_FWD_GRAPH: run the step as a CUDA graph, captured on first use and replayed
  * while the batch's pointers and shape fields are unchanged (stream must not be the legacy
  * default stream). */

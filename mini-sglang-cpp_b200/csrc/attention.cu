@@ -947,20 +947,27 @@ int make_decode_maps(CUtensorMap* tk, CUtensorMap* tv, const void* k_pool, const
 constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB
 static __device__ __align__(256) uint8_t g_decode_scratch[kNoAllocScratchBytes];
 
-// Cascade plan: suffix chunks from the plain decode plan of the suffix length; prefix chunks of
-// at least the suffix chunk size (so each CTA walks a similar number of pages) and no more
-// prefix chunks than suffix chunks (the workspace is then at most twice the plain one).
+// Cascade plan: suffix chunks from the plain decode plan of the suffix length. A suffix warp
+// attends chunk_pages * hc / 4 (page, head) pairs (its CTA's hc heads over the chunk, split over
+// 4 warps); a prefix warp attends every page of its prefix chunk for its 16 rows. Prefix chunks
+// therefore get chunk_pages * hc / 4 pages, so both kinds of CTA take about as long (with one
+// kv head per CTA, chunks as long as the suffix's made the prefix CTAs 4x longer than the rest
+// of the grid) -- but no more than 4 prefix chunks per suffix chunk, which bounds the workspace
+// at 5x the plain decode's.
+constexpr int kMaxPreChunksPerSfx = 4;
 CascadePlan plan_cascade(int B, int max_seq_len, int shared_pages, int hq, int hkv) {
     CascadePlan cp{};
     const int max_pages_seq = std::max(1, (max_seq_len + kPage - 1) / kPage);
     const int sfx_pages = std::max(1, max_pages_seq - shared_pages);
     const DecodePlan dp = plan_decode(B, sfx_pages * kPage, hq, hkv);
     const int group = hq / hkv;
+    const int hc = decode_heads_per_cta(hkv);
     cp.shared_pages = shared_pages;
     cp.chunk_pages = dp.chunk_pages;
     cp.chunks_sfx = dp.max_chunks;
-    cp.pc_pages = std::min(kMaxChunkPages,
-                           std::max(cp.chunk_pages, (shared_pages + cp.chunks_sfx - 1) / cp.chunks_sfx));
+    const int balanced = std::max(1, (cp.chunk_pages * hc + kDecWarps - 1) / kDecWarps);
+    const int cap = kMaxPreChunksPerSfx * cp.chunks_sfx;
+    cp.pc_pages = std::min(kMaxChunkPages, std::max(balanced, (shared_pages + cap - 1) / cap));
     cp.n_pchunks = (shared_pages + cp.pc_pages - 1) / cp.pc_pages;
     cp.row_tiles = (B * group + kPreRows - 1) / kPreRows;
     cp.n_pre = cp.n_pchunks * hkv * cp.row_tiles;

@@ -207,11 +207,29 @@ class Attention {
                                            head_dim_, 16, scale, out, ws.attn_ws, ws.attn_ws_bytes,
                                            s),
                "Attention::forward(decode)");
-        else
+        else if (b.decode_tail > 0 && b.decode_tail < b.num_reqs && b.decode_tail < b.num_tokens &&
+                 msgl_paged_attention_workspace_size(b.decode_tail, b.max_seq_len, hq_, hkv_,
+                                                     head_dim_) <= ws.attn_ws_bytes) {
+            // chunked prefill mixed with decodes: the prefill requests through extend, the decode
+            // tail (one row each, the last rows of the step) through the split-KV decode kernel
+            const int nd = b.decode_tail, np_ = b.num_reqs - nd, t0 = b.num_tokens - nd;
+            const size_t row = static_cast<size_t>(hq_) * head_dim_;
+            ck(msgl_paged_attention_extend(q, k_pool, v_pool, num_slots, b.page_table, b.max_pages,
+                                           b.seq_lens, b.q_indptr, np_, b.max_q_len, hq_, hkv_,
+                                           head_dim_, 16, scale, out, s),
+               "Attention::forward(extend part)");
+            ck(msgl_paged_attention_decode(q + t0 * row, k_pool, v_pool, num_slots,
+                                           b.page_table + static_cast<size_t>(np_) * b.max_pages,
+                                           b.max_pages, b.seq_lens + np_, nd, b.max_seq_len, hq_,
+                                           hkv_, head_dim_, 16, scale, out + t0 * row, ws.attn_ws,
+                                           ws.attn_ws_bytes, s),
+               "Attention::forward(decode tail)");
+        } else {
             ck(msgl_paged_attention_extend(q, k_pool, v_pool, num_slots, b.page_table, b.max_pages,
                                            b.seq_lens, b.q_indptr, b.num_reqs, b.max_q_len, hq_,
                                            hkv_, head_dim_, 16, scale, out, s),
                "Attention::forward(extend)");
+        }
     }
     int hq() const { return hq_; }
     int hkv() const { return hkv_; }

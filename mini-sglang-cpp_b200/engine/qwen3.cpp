@@ -197,8 +197,9 @@ static void create(Model& m, const msgl_model_config& c) {
     size_t aws = 0;
     for (int b = 1; b <= static_cast<int>(B); ++b)
         aws = std::max(aws, msgl_paged_attention_workspace_size(b, c.max_position, m.hq, m.hkv, D));
-    // the cascade decode (shared prefix) needs at most twice the plain decode's partial storage
-    aws = aws > 0 ? 2 * aws : 0;
+    // the cascade decode (shared prefix) needs at most 5x the plain decode's partial storage
+    // (at most 4 prefix chunks per suffix chunk)
+    aws = aws > 0 ? 5 * aws : 0;
     m.attn_ws.alloc(std::max<size_t>(aws, 256));
     ckc(cudaMemset(m.attn_ws.p, 0, m.attn_ws.bytes), "attention workspace");
     m.scratch = Scratch{m.gemm_ws.p, m.gemm_ws.bytes, m.attn_ws.p, m.attn_ws.bytes};
@@ -523,7 +524,7 @@ static void forward(Model& m, const msgl_batch& b, int* next_tokens, float* logi
 
 static std::vector<int64_t> graph_key(const msgl_batch& b, const int* next, const float* logits) {
     return {b.num_tokens, b.num_reqs, b.is_decode, b.max_pages, b.max_seq_len, b.max_q_len,
-            b.shared_prefix_pages, reinterpret_cast<int64_t>(b.input_ids), reinterpret_cast<int64_t>(b.positions),
+            b.shared_prefix_pages, b.decode_tail, reinterpret_cast<int64_t>(b.input_ids), reinterpret_cast<int64_t>(b.positions),
             reinterpret_cast<int64_t>(b.slot_mapping), reinterpret_cast<int64_t>(b.page_table),
             reinterpret_cast<int64_t>(b.seq_lens), reinterpret_cast<int64_t>(b.q_indptr),
             reinterpret_cast<int64_t>(b.last_idx), reinterpret_cast<int64_t>(next),
@@ -600,6 +601,13 @@ static void step_host(Model& m, const msgl_batch& hb, int* host_next, int flags,
         }
         db.shared_prefix_pages = n;
     }
+    if (hb.decode_tail == MSGL_DECODE_TAIL_DETECT) {  // trailing requests with one query row
+        int n = 0;
+        if (!hb.is_decode)
+            while (n < B - 1 && hb.q_indptr[B - n] - hb.q_indptr[B - n - 1] == 1) ++n;
+        db.decode_tail = n;
+    }
+    if (db.decode_tail < 0 || db.decode_tail >= B) db.decode_tail = 0;
     db.input_ids = m.st_ids.as<int>();
     db.positions = m.st_pos.as<int>();
     db.slot_mapping = m.st_slots.as<int>();

@@ -33,10 +33,21 @@ class BatchT(C.Structure):
                                         "max_seq_len", "max_q_len")] + \
                [(n, C.c_void_p) for n in ("input_ids", "positions", "slot_mapping", "page_table",
                                            "seq_lens", "q_indptr", "last_idx")] + \
-               [("shared_prefix_pages", C.c_int)]
+               [("shared_prefix_pages", C.c_int), ("decode_tail", C.c_int)]
 
 
 SHARED_PREFIX_DETECT = -1  # msgl_model_step_host computes it from the host page table
+DECODE_TAIL_DETECT = -1    # msgl_model_step_host computes it from the host q_indptr
+
+
+def decode_tail(q_indptr: np.ndarray) -> int:
+    """Trailing requests with exactly one query row (a mixed batch's decode requests), fewer
+    than the batch."""
+    ql = np.diff(np.asarray(q_indptr))
+    n = 0
+    while n < ql.size - 1 and ql[ql.size - 1 - n] == 1:
+        n += 1
+    return n
 
 
 def shared_prefix_pages(page_table: np.ndarray, seq_lens: np.ndarray, page_size: int = 16) -> int:
@@ -200,10 +211,11 @@ def make_step(host: dict, decode: bool, device, max_seq_len: int, max_q_len: int
     t = {k: torch.from_numpy(np.ascontiguousarray(v)).to(device) for k, v in host.items()}
     B = t["seq_lens"].numel()
     sp = shared_prefix_pages(np.asarray(host["page_table"]), np.asarray(host["seq_lens"])) if decode else 0
+    tail = 0 if decode else decode_tail(host["q_indptr"])
     st = BatchT(t["input_ids"].numel(), B, int(decode), t["page_table"].shape[1], max_seq_len,
                 max_q_len, *[t[k].data_ptr() for k in ("input_ids", "positions", "slot_mapping",
                                                         "page_table", "seq_lens", "q_indptr",
-                                                        "last_idx")], sp)
+                                                        "last_idx")], sp, tail)
     return StepBatch(t, st, B)
 
 

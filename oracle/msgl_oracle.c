@@ -168,7 +168,7 @@ void oracle_paged_attention(const float* q, const float* k_pool, const float* v_
                             float* out) {
     int group = num_q_heads / num_kv_heads;
     int64_t kv_stride = (int64_t)num_kv_heads * head_dim;
-#pragma omp parallel for schedule(dynamic, 1)
+#pragma omp parallel for schedule(dynamic, 1) if (num_reqs > 1)
     for (int r = 0; r < num_reqs; ++r) {
         int ctx = seq_lens[r];
         int n = q_indptr[r + 1] - q_indptr[r];

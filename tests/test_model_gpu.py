@@ -268,3 +268,50 @@ def test_partials_path_matches_regular_path(cuda, oracle, monkeypatch):
         del model
     for a, b in zip(*runs):
         assert rel_l2(a, b) < 2e-2
+
+
+def test_mixed_batch_decode_tail(cuda, oracle):
+    """A chunked-prefill step mixed with decodes (request 0 appends a 40-token chunk, requests
+    1-3 decode one token each): with decode_tail = 3 (detected by make_step) the executor runs
+    the extend kernel on request 0 and the split-KV decode kernel on the tail; forced to 0,
+    every request goes through the extend kernel. Both within the whole-model tolerance of the
+    oracle; greedy ids equal where the oracle's margin is clear."""
+    from msgl.model import BatchBuilder, PagePool, Qwen3Model, Request
+    w = weights(CFG, 8)
+    model = Qwen3Model(CFG, max_tokens=256, max_reqs=8)
+    model.set_weights(w)
+    num_pages = 64
+    model.alloc_kv(num_pages)
+    orc = OracleModel(oracle, CFG, w, num_slots=num_pages * 16)
+    rng = np.random.default_rng(11)
+    reqs = [Request(list(rng.integers(0, CFG["vocab"], n))) for n in (30, 300, 17, 90)]
+    bb = BatchBuilder(PagePool(num_pages))
+    sb = bb.build(reqs, decode=False, max_pages=24)
+    model.forward(sb)
+    h = {k: v.cpu().numpy() for k, v in sb.tensors.items()}
+    orc.forward(h["input_ids"], h["positions"], h["slot_mapping"], h["page_table"],
+                h["seq_lens"], h["q_indptr"])
+    for r in reqs:
+        r.cached_len = r.device_len
+    reqs[0].input_ids += list(rng.integers(0, CFG["vocab"], 40))
+    for r in reqs[1:]:
+        r.input_ids.append(int(rng.integers(0, CFG["vocab"])))
+    sb = bb.build(reqs, decode=False, max_pages=24)
+    assert sb.struct.decode_tail == 3
+    h = {k: v.cpu().numpy() for k, v in sb.tensors.items()}
+    ref = orc.forward(h["input_ids"], h["positions"], h["slot_mapping"], h["page_table"],
+                      h["seq_lens"], h["q_indptr"])
+    outs = []
+    for tail in (3, 0):
+        sb.struct.decode_tail = tail
+        nxt, lg = model.forward(sb, logits=True)
+        torch.cuda.synchronize()
+        got = lg.cpu().numpy()
+        assert rel_l2(got, ref) < 2e-2, (tail, rel_l2(got, ref))
+        top2 = np.sort(ref, axis=1)[:, -2:]
+        clear = (top2[:, 1] - top2[:, 0]) > 4 * np.abs(got - ref).max()
+        assert np.array_equal(nxt.cpu().numpy()[clear], ref.argmax(axis=1)[clear])
+        outs.append(got)
+    assert rel_l2(outs[0], outs[1]) < 2e-2
+    from msgl import ops
+    assert ops.device_error() == (0, 0)
