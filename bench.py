@@ -538,8 +538,8 @@ def run_ours(args, rank, world, local_rank):
     d2h = BATCH * 4
     assert torch.equal(out_host.to(dev), nxt), "host step and device step disagree"
 
-    # ---- roofline: the step's decode attention (cascade over the shared prefix) alone, every
-    # layer's pool
+    # ---- roofline: the step's decode attention alone, every layer's pool (the cascade over the
+    # shared prefix; with one kv head per rank the executor runs the plain kernel instead)
     hq, hkv = hq_l, hkv_l  # this rank's heads
     q = torch.empty(BATCH, hq, 128, dtype=torch.bfloat16, device=dev)
     ops.fill_normal_(q, seed=5, std=1.0)
@@ -550,12 +550,22 @@ def run_ours(args, rank, world, local_rank):
     ws = torch.zeros(wsn, dtype=torch.uint8, device=dev)
     pt_d, seq_d = sb.tensors["page_table"], sb.tensors["seq_lens"]
 
+    cascade = hkv >= 2  # the executor's rule (engine/layers.h, Attention::forward)
+    if not cascade:
+        ws = ops.attention_workspace(BATCH, CTX, hq, hkv, dev)
+
     def attn(l):
         k, v, n = pools[l]
-        msgl.check(lib.msgl_paged_attention_decode_cascade(
-            q.data_ptr(), k, v, n, pt_d.data_ptr(), pt_d.shape[1], seq_d.data_ptr(), BATCH, CTX,
-            shared, hq, hkv, 128, PAGE, 1.0 / 128 ** 0.5, aout.data_ptr(), ws.data_ptr(),
-            ws.numel(), sp))
+        if cascade:
+            msgl.check(lib.msgl_paged_attention_decode_cascade(
+                q.data_ptr(), k, v, n, pt_d.data_ptr(), pt_d.shape[1], seq_d.data_ptr(), BATCH,
+                CTX, shared, hq, hkv, 128, PAGE, 1.0 / 128 ** 0.5, aout.data_ptr(), ws.data_ptr(),
+                ws.numel(), sp))
+        else:
+            msgl.check(lib.msgl_paged_attention_decode(
+                q.data_ptr(), k, v, n, pt_d.data_ptr(), pt_d.shape[1], seq_d.data_ptr(), BATCH,
+                CTX, hq, hkv, 128, PAGE, 1.0 / 128 ** 0.5, aout.data_ptr(), ws.data_ptr(),
+                ws.numel(), sp))
 
     for l in range(L):
         attn(l)
@@ -597,11 +607,13 @@ def run_ours(args, rank, world, local_rank):
             "e2e": {"value": BATCH / (ms_e2e * 1e-3), "unit": UNIT,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": ms_e2e, "blocks_ms_per_step": [round(b, 4) for b in blocks_e2e]},
-            "roofline": {"kernel": "paged_decode_cascade_kernel", "bound": "hbm",
+            "roofline": {"kernel": "paged_decode_cascade_kernel" if cascade else "paged_decode_kernel",
+                         "bound": "hbm",
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
                          # the capture is of 8 kv heads; a TP rank reads its own heads only
-                         "traffic": PAGED_DECODE_TRAFFIC_BYTES * hkv // CFG8B["num_kv_heads"],
+                         "traffic": (PAGED_DECODE_TRAFFIC_BYTES * hkv // CFG8B["num_kv_heads"])
+                                    if cascade else None,
                          "algorithmic_bytes_per_launch": unique_bytes,
                          "per_request_bytes_per_launch": per_request_bytes,
                          "launch_ms": attn_ms,

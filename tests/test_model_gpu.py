@@ -278,7 +278,7 @@ def test_mixed_batch_decode_tail(cuda, oracle):
     oracle; greedy ids equal where the oracle's margin is clear."""
     from msgl.model import BatchBuilder, PagePool, Qwen3Model, Request
     w = weights(CFG, 8)
-    model = Qwen3Model(CFG, max_tokens=256, max_reqs=8)
+    model = Qwen3Model(CFG, max_tokens=512, max_reqs=8)
     model.set_weights(w)
     num_pages = 64
     model.alloc_kv(num_pages)
