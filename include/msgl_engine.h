@@ -136,6 +136,22 @@ MSGL_API int msgl_model_forward(msgl_model* m, const msgl_batch* batch, int* nex
  * synchronises the stream. */
 MSGL_API int msgl_model_step_host(msgl_model* m, const msgl_batch* host_batch,
                                   int* host_next_tokens, int flags, msgl_stream_t stream);
+/* Overlap scheduling (SchedulerConfig::overlap_scheduling, include/minisgl/scheduler/
+ * scheduler.h:23, which the reference never acts on): msgl_model_step_host without the wait.
+ * The copies, the step and the D2H of the greedy tokens are queued on `stream` and the call
+ * returns with a ticket; msgl_model_step_wait(ticket) waits for that step (one of the last two
+ * submitted). Consecutive submissions use the executor's two staging sets in turn, so the host
+ * can build and submit step N+1 while step N runs; the host arrays of a step (pinned for
+ * asynchronous copies) and its host_next_tokens must stay untouched until its wait returns.
+ * flags & MSGL_STEP_TOKENS_FROM_PREV (a decode step after a submitted step): input_ids is not
+ * read from the host -- row r takes the greedy token of row r of the previous submitted step,
+ * on the device -- so a decode step can be submitted before the previous step's tokens reach
+ * the host. */
+#define MSGL_STEP_TOKENS_FROM_PREV 2
+MSGL_API int msgl_model_step_host_async(msgl_model* m, const msgl_batch* host_batch,
+                                        int* host_next_tokens, int flags, msgl_stream_t stream,
+                                        uint64_t* ticket);
+MSGL_API int msgl_model_step_wait(msgl_model* m, uint64_t ticket);
 /* Decode steps without the host in between (Scheduler::step's decode loop with the flatten of
  * scheduler.cpp:83-106 on the device): from one decode step's device arrays (*batch, e.g. built
  * on the host once), run num_steps greedy steps back to back; step s writes its ids to
@@ -147,6 +163,25 @@ MSGL_API int msgl_model_step_host(msgl_model* m, const msgl_batch* host_batch,
 MSGL_API int msgl_model_decode_steps(msgl_model* m, const msgl_batch* batch, int num_steps,
                                      int* token_log, const int* free_pages, int* free_top,
                                      int flags, msgl_stream_t stream);
+/* The same with the finish rules of Scheduler::step (scheduler.cpp:126-131) and SamplingParams
+ * (include/minisgl/core/types.h:12-20) applied on the device after every step
+ * (msgl_decode_finish): a request finishes after max_new_tokens[r] tokens or, unless
+ * ignore_eos[r], on a stop id. From then on its token_log entries are -1 and the advance holds it
+ * in place (msgl_decode_advance_masked: no new page, its last step recomputed), so the batch keeps
+ * its shape (and its captured graph) until the host retires the request. finished [B] and
+ * generated [B] are read and written (zero-fill them for fresh requests); all device int32. */
+typedef struct {
+    const int* max_new_tokens; /* [B] tokens each request may generate (the reference's max_tokens) */
+    const int* ignore_eos;     /* [B] nonzero: stop ids do not finish the request; NULL: none set */
+    const int* stop_ids;       /* [num_stop_ids] end-of-sequence token ids */
+    int num_stop_ids;
+    int* finished;             /* [B] in / out */
+    int* generated;            /* [B] in / out */
+} msgl_stop_rules;
+MSGL_API int msgl_model_decode_steps_stop(msgl_model* m, const msgl_batch* batch, int num_steps,
+                                          int* token_log, const int* free_pages, int* free_top,
+                                          const msgl_stop_rules* stop, int flags,
+                                          msgl_stream_t stream);
 
 /* Debug: device pointer to the hidden state [max_tokens, hidden] bf16 after the most recent
  * forward (the last layer's output before the final norm) -- used by per-layer parity tests

@@ -163,6 +163,25 @@ MSGL_API int msgl_decode_advance(const int* next_tokens, int* input_ids, int* po
                                  int* slot_mapping, int* page_table, int max_pages, int* seq_lens,
                                  const int* free_pages, int* free_top, int num_reqs, int page_size,
                                  msgl_stream_t stream);
+/* msgl_decode_advance with finished [num_reqs] (device, may be NULL): requests whose entry is
+ * nonzero are held -- no page is popped for them and their input id, position, slot and length
+ * stay -- so a fixed-shape (graph-replayed) batch keeps running them, recomputing their last step
+ * (the same K/V into the same slot) until the host retires them. */
+MSGL_API int msgl_decode_advance_masked(const int* next_tokens, int* input_ids, int* positions,
+                                        int* slot_mapping, int* page_table, int max_pages,
+                                        int* seq_lens, const int* free_pages, int* free_top,
+                                        const int* finished, int num_reqs, int page_size,
+                                        msgl_stream_t stream);
+/* The finish rule of Scheduler::step (scheduler.cpp:126-131) with the SamplingParams of
+ * include/minisgl/core/types.h:12-20, on the device, for one decode step: for every request not
+ * yet finished, token_out[r] = next_tokens[r], generated[r] += 1, and finished[r] = 1 once
+ * generated[r] >= max_new_tokens[r] (the reference's max_tokens) or, unless ignore_eos[r] (NULL:
+ * all zero), next_tokens[r] is one of stop_ids[0 .. num_stop_ids) (the model's end-of-sequence
+ * ids; the reference never checks them, D17). Finished requests get token_out[r] = -1. All
+ * arrays device int32 [num_reqs]; finished / generated are read and written. */
+MSGL_API int msgl_decode_finish(const int* next_tokens, int* token_out, const int* max_new_tokens,
+                                const int* ignore_eos, const int* stop_ids, int num_stop_ids,
+                                int* finished, int* generated, int num_reqs, msgl_stream_t stream);
 
 /* ---------------------------------------------------------------- paged attention */
 /* Replaces Attention::forward (src/layer/layer.cpp:214-262) with attention over the paged KV

@@ -72,7 +72,16 @@ struct Model {
     MoEScratch moe_scratch;
     int moe_inter = 0;  // this rank's expert intermediate size
     // device copies of a host batch (msgl_model_step_host)
-    DevBuf st_ids, st_pos, st_slots, st_pt, st_seq, st_indptr, st_last, st_next;
+    // (two sets, used in turn: an asynchronous host step may be submitted while the previous
+    // one runs; `done` marks the completion of the step that last used the set)
+    struct Staging {
+        DevBuf ids, pos, slots, pt, seq, indptr, last, next;
+        cudaEvent_t done = nullptr;
+        int num_reqs = 0;
+    };
+    Staging st[2];
+    DevBuf dec_next;            // greedy tokens of msgl_model_decode_steps
+    uint64_t st_submitted = 0;  // host steps submitted so far (the next one uses st[n % 2])
     int st_max_pages = 0;
     // captured decode graphs, keyed by every pointer and shape field of the step
     struct GraphEntry {
@@ -86,7 +95,11 @@ struct Model {
             if (g.exec) cudaGraphExecDestroy(g.exec);
         graphs.clear();
     }
-    ~Model() { graphs_reset(); }
+    ~Model() {
+        graphs_reset();
+        for (auto& x : st)
+            if (x.done) cudaEventDestroy(x.done);
+    }
 
     int64_t weight_bytes() const {
         int64_t b = embed.bytes + norm.weight.bytes + lm_head.weight.bytes;
@@ -238,14 +251,18 @@ static void create(Model& m, const msgl_model_config& c) {
                                    m.moe_ws.p, m.moe_ws.bytes};
     }
     m.st_max_pages = (c.max_position + 15) / 16;
-    m.st_ids.alloc(T * 4);
-    m.st_pos.alloc(T * 4);
-    m.st_slots.alloc(T * 4);
-    m.st_pt.alloc(B * m.st_max_pages * 4);
-    m.st_seq.alloc(B * 4);
-    m.st_indptr.alloc((B + 1) * 4);
-    m.st_last.alloc(B * 4);
-    m.st_next.alloc(B * 4);
+    for (auto& x : m.st) {
+        x.ids.alloc(T * 4);
+        x.pos.alloc(T * 4);
+        x.slots.alloc(T * 4);
+        x.pt.alloc(B * m.st_max_pages * 4);
+        x.seq.alloc(B * 4);
+        x.indptr.alloc((B + 1) * 4);
+        x.last.alloc(B * 4);
+        x.next.alloc(B * 4);
+        ckc(cudaEventCreateWithFlags(&x.done, cudaEventDisableTiming), "staging event");
+    }
+    m.dec_next.alloc(B * 4);
 }
 
 // ----------------------------------------------------------------------------- weights
@@ -565,23 +582,43 @@ static void run(Model& m, const msgl_batch& b, int* next, float* logits, int fla
     ckc(cudaGraphLaunch(exec, s), "cudaGraphLaunch");
 }
 
-static void step_host(Model& m, const msgl_batch& hb, int* host_next, int flags, cudaStream_t s) {
+// The scheduler-facing step (Scheduler::step -> forward, scheduler.cpp:83-124) on host arrays:
+// H2D into one staging set, the step, D2H of the greedy tokens; with `wait` the host waits for
+// it (msgl_model_step_host), otherwise it returns at once (msgl_model_step_host_async: overlap
+// scheduling -- the host builds the next batch while this one runs). Returns the step's ticket.
+static uint64_t step_host(Model& m, const msgl_batch& hb, int* host_next, int flags,
+                          cudaStream_t s, bool wait) {
     const int T = hb.num_tokens, B = hb.num_reqs;
     if (T <= 0 || T > m.cfg.max_tokens || B <= 0 || B > m.cfg.max_reqs)
         throw Fail(MSGL_ERR_INVALID_ARG, "step_host: batch exceeds the executor's capacity");
     if (hb.max_pages <= 0 || hb.max_pages > m.st_max_pages)
         throw Fail(MSGL_ERR_INVALID_ARG, "step_host: page-table width exceeds max_position / 16");
+    const bool prev_ids = (flags & MSGL_STEP_TOKENS_FROM_PREV) != 0;
+    const uint64_t ticket = m.st_submitted;
+    Model::Staging& x = m.st[ticket % 2];
+    if (prev_ids) {
+        const Model::Staging& p = m.st[(ticket + 1) % 2];
+        if (ticket == 0 || !hb.is_decode || T != B || B > p.num_reqs)
+            throw Fail(MSGL_ERR_INVALID_ARG,
+                       "step_host: tokens from the previous step need a decode step of at most "
+                       "its requests, after one");
+    }
     auto h2d = [&](DevBuf& d, const int* h, size_t n) {
         if (!h) throw Fail(MSGL_ERR_INVALID_ARG, "step_host: null host array");
         ckc(cudaMemcpyAsync(d.p, h, n * 4, cudaMemcpyHostToDevice, s), "step_host H2D");
     };
-    h2d(m.st_ids, hb.input_ids, T);
-    h2d(m.st_pos, hb.positions, T);
-    h2d(m.st_slots, hb.slot_mapping, T);
-    h2d(m.st_pt, hb.page_table, static_cast<size_t>(B) * hb.max_pages);
-    h2d(m.st_seq, hb.seq_lens, B);
-    h2d(m.st_indptr, hb.q_indptr, B + 1);
-    h2d(m.st_last, hb.last_idx, B);
+    if (prev_ids)  // row r continues request r of the previous step: its greedy token, on device
+        ckc(cudaMemcpyAsync(x.ids.p, m.st[(ticket + 1) % 2].next.p, static_cast<size_t>(B) * 4,
+                            cudaMemcpyDeviceToDevice, s),
+            "step_host tokens from the previous step");
+    else
+        h2d(x.ids, hb.input_ids, T);
+    h2d(x.pos, hb.positions, T);
+    h2d(x.slots, hb.slot_mapping, T);
+    h2d(x.pt, hb.page_table, static_cast<size_t>(B) * hb.max_pages);
+    h2d(x.seq, hb.seq_lens, B);
+    h2d(x.indptr, hb.q_indptr, B + 1);
+    h2d(x.last, hb.last_idx, B);
     msgl_batch db = hb;
     if (hb.shared_prefix_pages == MSGL_SHARED_PREFIX_DETECT) {
         // leading page-table columns that are the same page in every row, covered by every
@@ -608,16 +645,26 @@ static void step_host(Model& m, const msgl_batch& hb, int* host_next, int flags,
         db.decode_tail = n;
     }
     if (db.decode_tail < 0 || db.decode_tail >= B) db.decode_tail = 0;
-    db.input_ids = m.st_ids.as<int>();
-    db.positions = m.st_pos.as<int>();
-    db.slot_mapping = m.st_slots.as<int>();
-    db.page_table = m.st_pt.as<int>();
-    db.seq_lens = m.st_seq.as<int>();
-    db.q_indptr = m.st_indptr.as<int>();
-    db.last_idx = m.st_last.as<int>();
-    run(m, db, m.st_next.as<int>(), nullptr, hb.is_decode ? flags : 0, s);
-    ckc(cudaMemcpyAsync(host_next, m.st_next.p, B * 4, cudaMemcpyDeviceToHost, s), "step_host D2H");
-    ckc(cudaStreamSynchronize(s), "step_host sync");
+    db.input_ids = x.ids.as<int>();
+    db.positions = x.pos.as<int>();
+    db.slot_mapping = x.slots.as<int>();
+    db.page_table = x.pt.as<int>();
+    db.seq_lens = x.seq.as<int>();
+    db.q_indptr = x.indptr.as<int>();
+    db.last_idx = x.last.as<int>();
+    run(m, db, x.next.as<int>(), nullptr, hb.is_decode ? (flags & MSGL_FWD_GRAPH) : 0, s);
+    ckc(cudaMemcpyAsync(host_next, x.next.p, B * 4, cudaMemcpyDeviceToHost, s), "step_host D2H");
+    ckc(cudaEventRecord(x.done, s), "step_host event");
+    x.num_reqs = B;
+    m.st_submitted = ticket + 1;
+    if (wait) ckc(cudaEventSynchronize(x.done), "step_host sync");
+    return ticket;
+}
+
+static void step_wait(Model& m, uint64_t ticket) {
+    if (ticket >= m.st_submitted || ticket + 2 < m.st_submitted)
+        throw Fail(MSGL_ERR_INVALID_ARG, "step_wait: not one of the last two submitted steps");
+    ckc(cudaEventSynchronize(m.st[ticket % 2].done), "step_wait");
 }
 
 }  // namespace engine
@@ -708,13 +755,40 @@ int msgl_model_step_host(msgl_model* m, const msgl_batch* host_batch, int* host_
                          int flags, msgl_stream_t stream) {
     if (!m || !host_batch || !host_next_tokens)
         return msgl::set_error(MSGL_ERR_INVALID_ARG, "step_host: null");
-    return guarded([&] { step_host(m->m, *host_batch, host_next_tokens, flags, stream); });
+    return guarded([&] { step_host(m->m, *host_batch, host_next_tokens, flags & ~MSGL_STEP_TOKENS_FROM_PREV,
+                                   static_cast<cudaStream_t>(stream), true); });
+}
+
+int msgl_model_step_host_async(msgl_model* m, const msgl_batch* host_batch, int* host_next_tokens,
+                               int flags, msgl_stream_t stream, uint64_t* ticket) {
+    if (!m || !host_batch || !host_next_tokens)
+        return msgl::set_error(MSGL_ERR_INVALID_ARG, "step_host_async: null");
+    return guarded([&] {
+        const uint64_t t = step_host(m->m, *host_batch, host_next_tokens, flags,
+                                     static_cast<cudaStream_t>(stream), false);
+        if (ticket) *ticket = t;
+    });
+}
+
+int msgl_model_step_wait(msgl_model* m, uint64_t ticket) {
+    if (!m) return msgl::set_error(MSGL_ERR_INVALID_ARG, "step_wait: null");
+    return guarded([&] { step_wait(m->m, ticket); });
 }
 
 int msgl_model_decode_steps(msgl_model* m, const msgl_batch* batch, int num_steps, int* token_log,
                             const int* free_pages, int* free_top, int flags, msgl_stream_t stream) {
+    return msgl_model_decode_steps_stop(m, batch, num_steps, token_log, free_pages, free_top,
+                                        nullptr, flags, stream);
+}
+
+int msgl_model_decode_steps_stop(msgl_model* m, const msgl_batch* batch, int num_steps,
+                                 int* token_log, const int* free_pages, int* free_top,
+                                 const msgl_stop_rules* stop, int flags, msgl_stream_t stream) {
     if (!m || !batch || num_steps < 0 || (num_steps > 0 && (!token_log || !free_pages || !free_top)))
         return msgl::set_error(MSGL_ERR_INVALID_ARG, "decode_steps: bad args");
+    if (stop && (!stop->max_new_tokens || !stop->finished || !stop->generated ||
+                 stop->num_stop_ids < 0 || (stop->num_stop_ids > 0 && !stop->stop_ids)))
+        return msgl::set_error(MSGL_ERR_INVALID_ARG, "decode_steps: bad stop rules");
     return guarded([&] {
         Model& md = m->m;
         if (!batch->is_decode || batch->num_tokens != batch->num_reqs)
@@ -724,18 +798,25 @@ int msgl_model_decode_steps(msgl_model* m, const msgl_batch* batch, int num_step
         msgl_batch b = *batch;
         b.max_seq_len = std::min(b.max_pages * md.page_size, md.cfg.max_position);
         const int B = b.num_reqs;
-        int* next = md.st_next.as<int>();
+        int* next = md.dec_next.as<int>();
         auto* s = static_cast<cudaStream_t>(stream);
         for (int st = 0; st < num_steps; ++st) {
-            run(md, b, next, nullptr, flags, s);
-            ckc(cudaMemcpyAsync(token_log + static_cast<int64_t>(st) * B, next, sizeof(int) * B,
-                                cudaMemcpyDeviceToDevice, s),
-                "decode_steps: token log");
+            run(md, b, next, nullptr, flags & MSGL_FWD_GRAPH, s);
+            int* row = token_log + static_cast<int64_t>(st) * B;
+            if (stop)  // finish rules: the log gets the token, or -1 once a request finished
+                ck(msgl_decode_finish(next, row, stop->max_new_tokens, stop->ignore_eos,
+                                      stop->stop_ids, stop->num_stop_ids, stop->finished,
+                                      stop->generated, B, stream),
+                   "decode_steps: finish");
+            else
+                ckc(cudaMemcpyAsync(row, next, sizeof(int) * B, cudaMemcpyDeviceToDevice, s),
+                    "decode_steps: token log");
             if (st + 1 < num_steps)  // the arrays of *batch are advanced in place
-                ck(msgl_decode_advance(next, const_cast<int*>(b.input_ids), const_cast<int*>(b.positions),
-                                       const_cast<int*>(b.slot_mapping), const_cast<int*>(b.page_table),
-                                       b.max_pages, const_cast<int*>(b.seq_lens), free_pages, free_top,
-                                       B, md.page_size, stream),
+                ck(msgl_decode_advance_masked(next, const_cast<int*>(b.input_ids), const_cast<int*>(b.positions),
+                                              const_cast<int*>(b.slot_mapping), const_cast<int*>(b.page_table),
+                                              b.max_pages, const_cast<int*>(b.seq_lens), free_pages,
+                                              free_top, stop ? stop->finished : nullptr, B,
+                                              md.page_size, stream),
                    "decode_steps: advance");
         }
     });

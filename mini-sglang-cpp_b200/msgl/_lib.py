@@ -88,6 +88,11 @@ SIGNATURES = {
     "msgl_model_kv_pool": (I, [P, I, P, P, P]),
     "msgl_model_forward": (I, [P, P, P, P, I, P]),
     "msgl_model_step_host": (I, [P, P, P, I, P]),
+    "msgl_model_step_host_async": (I, [P, P, P, I, P, P]),
+    "msgl_model_step_wait": (I, [P, U64]),
+    "msgl_model_decode_steps_stop": (I, [P, P, I, P, P, P, P, I, P]),
+    "msgl_decode_advance_masked": (I, [P, P, P, P, P, I, P, P, P, P, I, I, P]),
+    "msgl_decode_finish": (I, [P, P, P, P, P, I, P, P, I, P]),
     "msgl_model_debug_hidden": (I, [P, P, P]),
     "msgl_model_set_num_layers_run": (I, [P, I]),
     "msgl_model_set_tp": (I, [P, P]),

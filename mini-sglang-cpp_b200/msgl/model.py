@@ -36,6 +36,12 @@ class BatchT(C.Structure):
                [("shared_prefix_pages", C.c_int), ("decode_tail", C.c_int)]
 
 
+class StopRules(C.Structure):
+    _fields_ = [("max_new_tokens", C.c_void_p), ("ignore_eos", C.c_void_p), ("stop_ids", C.c_void_p),
+                ("num_stop_ids", C.c_int), ("finished", C.c_void_p), ("generated", C.c_void_p)]
+
+
+STEP_TOKENS_FROM_PREV = 2  # msgl_model_step_host_async: decode input ids from the previous step
 SHARED_PREFIX_DETECT = -1  # msgl_model_step_host computes it from the host page table
 DECODE_TAIL_DETECT = -1    # msgl_model_step_host computes it from the host q_indptr
 
@@ -296,6 +302,28 @@ class Qwen3Model:
                                              log.data_ptr(), free_pages.data_ptr(),
                                              free_top.data_ptr(), int(graph), _s()))
         return log
+
+    def decode_steps_stop(self, step: StepBatch, num_steps: int, free_pages, free_top,
+                          max_new_tokens, stop_ids, ignore_eos=None, finished=None,
+                          generated=None, graph: bool = True):
+        """msgl_model_decode_steps_stop: decode steps with the finish rules applied on the device.
+        Returns (token log [num_steps, B] with -1 after a request finished, finished, generated)."""
+        dev = step.tensors["input_ids"].device
+        B = step.num_reqs
+        i32 = lambda a: torch.as_tensor(np.asarray(a, np.int32), device=dev)
+        mx, sid = i32(max_new_tokens), i32(stop_ids)
+        ign = i32(ignore_eos) if ignore_eos is not None else None
+        fin = finished if finished is not None else torch.zeros(B, dtype=torch.int32, device=dev)
+        gen = generated if generated is not None else torch.zeros(B, dtype=torch.int32, device=dev)
+        rules = StopRules(mx.data_ptr(), None if ign is None else ign.data_ptr(), sid.data_ptr(),
+                          sid.numel(), fin.data_ptr(), gen.data_ptr())
+        log = torch.empty(num_steps, B, dtype=torch.int32, device=dev)
+        check(self.L.msgl_model_decode_steps_stop(self.h, C.addressof(step.struct), num_steps,
+                                                  log.data_ptr(), free_pages.data_ptr(),
+                                                  free_top.data_ptr(), C.addressof(rules),
+                                                  int(graph), _s()))
+        torch.cuda.current_stream().synchronize()  # the rule arrays above are local
+        return log, fin, gen
 
     def set_tp(self, comm):
         self.tp = comm

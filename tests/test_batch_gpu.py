@@ -196,3 +196,145 @@ def test_decode_steps_matches_host_loop(cuda):
     assert runs[0] == runs[1]
     from msgl import ops
     assert ops.device_error() == (0, 0)
+
+
+def _prefilled(model, prompts, num_pages, width):
+    from msgl.model import BatchBuilder, PagePool, Request
+    model.alloc_kv(num_pages)
+    pool = PagePool(num_pages)
+    reqs = [Request(list(p)) for p in prompts]
+    bb = BatchBuilder(pool)
+    nxt = model.forward(bb.build(reqs, decode=False, max_pages=width))
+    torch.cuda.synchronize()
+    for r, t in zip(reqs, nxt.cpu().numpy().tolist()):
+        r.cached_len = r.device_len
+        r.input_ids.append(int(t))
+    return pool, reqs, bb
+
+
+def test_decode_steps_stop_rules(cuda):
+    """msgl_model_decode_steps_stop against the reference's finish rule replayed on the host:
+    per request max_tokens (3 / 20 / 5 / 20 new tokens), a stop id that request 0 emits at
+    step 2 (request 2 ignores it), -1 in the log once a request finished; the active requests'
+    tokens equal those of the run without rules (held requests do not disturb them), and no page
+    is taken for a request after it finished."""
+    from msgl.model import Qwen3Model
+    from test_model_gpu import CFG, weights
+    w = weights(CFG, 12)
+    model = Qwen3Model(CFG, max_tokens=128, max_reqs=4)
+    model.set_weights(w)
+    num_pages, width, steps = 40, 8, 16
+    rng = np.random.default_rng(13)
+    prompts = [[int(t) for t in rng.integers(0, CFG["vocab"], n)] for n in (10, 31, 17, 5)]
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        pool, reqs, bb = _prefilled(model, prompts, num_pages, width)
+        sb = bb.build(reqs, decode=True, max_pages=width)
+        free = torch.tensor(pool.free + [0], dtype=torch.int32, device="cuda")
+        top = torch.tensor([len(pool.free)], dtype=torch.int32, device="cuda")
+        free_log = model.decode_steps(sb, steps, free, top, graph=True)
+    torch.cuda.synchronize()
+    free_run = free_log.cpu().numpy()
+    stop_id = int(free_run[2, 0])
+    max_new = [20, 3, 20, 5]
+    ignore = [0, 0, 1, 0]
+    with torch.cuda.stream(s):
+        pool, reqs, bb = _prefilled(model, prompts, num_pages, width)
+        sb = bb.build(reqs, decode=True, max_pages=width)
+        free = torch.tensor(pool.free + [0], dtype=torch.int32, device="cuda")
+        top = torch.tensor([len(pool.free)], dtype=torch.int32, device="cuda")
+        log, fin, gen = model.decode_steps_stop(sb, steps, free, top, max_new, [stop_id],
+                                                ignore_eos=ignore, graph=True)
+    torch.cuda.synchronize()
+    got = log.cpu().numpy()
+    # the finish rule on the host, over the unrestricted run's tokens
+    exp = np.full_like(free_run, -1)
+    done, n = [False] * 4, [0] * 4
+    for st in range(steps):
+        for r in range(4):
+            if done[r]:
+                continue
+            t = int(free_run[st, r])
+            exp[st, r] = t
+            n[r] += 1
+            if n[r] >= max_new[r] or (not ignore[r] and t == stop_id):
+                done[r] = True
+    assert np.array_equal(got, exp), (got, exp)
+    assert fin.cpu().numpy().tolist() == [int(d) for d in done]
+    assert gen.cpu().numpy().tolist() == n
+    # pages: a finished request's page-table row and length stop moving
+    seq = sb.tensors["seq_lens"].cpu().numpy()
+    for r in range(4):
+        last = max(st for st in range(steps) if exp[st, r] >= 0)
+        assert seq[r] == len(prompts[r]) + 1 + (last if done[r] else steps - 1), (r, seq[r], last)
+    from msgl import ops
+    assert ops.device_error() == (0, 0)
+
+
+def test_step_host_async_overlap(cuda):
+    """Overlap scheduling: decode step s + 1 is submitted (msgl_model_step_host_async, input ids
+    taken on the device from step s) before the host waits for step s; the tokens equal those of
+    the synchronous msgl_model_step_host loop."""
+    import ctypes as C
+
+    import msgl
+    from msgl.model import (DECODE_TAIL_DETECT, SHARED_PREFIX_DETECT, STEP_TOKENS_FROM_PREV, BatchT,
+                            Qwen3Model)
+    from test_model_gpu import CFG, weights
+    w = weights(CFG, 14)
+    model = Qwen3Model(CFG, max_tokens=128, max_reqs=4)
+    model.set_weights(w)
+    L = msgl.lib()
+    num_pages, width, steps = 40, 8, 10
+    rng = np.random.default_rng(15)
+    prompts = [[int(t) for t in rng.integers(0, CFG["vocab"], n)] for n in (12, 3, 40, 22)]
+    s = torch.cuda.Stream()
+    sp = s.cuda_stream
+
+    def host_batch(sb):
+        h = {k: torch.from_numpy(np.ascontiguousarray(v.cpu().numpy())).pin_memory()
+             for k, v in sb.tensors.items()}
+        st = sb.struct
+        hb = BatchT(st.num_tokens, st.num_reqs, st.is_decode, st.max_pages, st.max_seq_len,
+                    st.max_q_len, *[h[k].data_ptr() for k in ("input_ids", "positions",
+                                                              "slot_mapping", "page_table",
+                                                              "seq_lens", "q_indptr", "last_idx")],
+                    SHARED_PREFIX_DETECT, DECODE_TAIL_DETECT)
+        return h, hb
+
+    runs = []
+    for mode in ("sync", "async"):
+        with torch.cuda.stream(s):
+            pool, reqs, bb = _prefilled(model, prompts, num_pages, width)
+        toks, keep, pending = [], [], []
+        outs = [torch.empty(4, dtype=torch.int32).pin_memory() for _ in range(steps)]
+        for st in range(steps):
+            sb = bb.build(reqs, decode=True, device="cpu", max_pages=width)
+            h, hb = host_batch(sb)
+            keep.append((h, hb))
+            if mode == "sync":
+                msgl.check(L.msgl_model_step_host(model.h, C.addressof(hb), outs[st].data_ptr(), 1, sp))
+                ids = outs[st].numpy().tolist()
+            else:
+                tk = C.c_uint64()
+                flags = 1 | (STEP_TOKENS_FROM_PREV if st > 0 else 0)
+                msgl.check(L.msgl_model_step_host_async(model.h, C.addressof(hb), outs[st].data_ptr(),
+                                                        flags, sp, C.byref(tk)))
+                pending.append(tk.value)
+                if st > 0:  # the previous step's tokens reach the host while this one runs
+                    msgl.check(L.msgl_model_step_wait(model.h, pending[st - 1]))
+                    toks.append(outs[st - 1].numpy().tolist())
+                ids = None
+            if mode == "sync":
+                toks.append(ids)
+            # lengths advance on the host; the ids are only needed by the sync loop's next batch
+            for r, t in zip(reqs, ids if ids is not None else [0] * 4):
+                r.cached_len = r.device_len
+                r.input_ids.append(int(t))
+        if mode == "async":
+            msgl.check(L.msgl_model_step_wait(model.h, pending[-1]))
+            toks.append(outs[steps - 1].numpy().tolist())
+        runs.append(toks)
+    assert runs[0] == runs[1]
+    from msgl import ops
+    assert ops.device_error() == (0, 0)
