@@ -650,6 +650,23 @@ def run_case(args):
     hq, hkv, H, I = CFG8B["num_q_heads"], CFG8B["num_kv_heads"], CFG8B["hidden"], CFG8B["inter"]
     if args.case == "breakdown":
         return run_breakdown(args, dev)
+    if args.case == "extend":  # the 32B chunked prefill's attention at a TP8 rank: 2048 queries
+        # (8 q heads, 1 kv head) over the last chunk of an 8192-token prompt, causal
+        CH, PL, hq8, hkv8 = 2048, 8192, 8, 1
+        num_pages, ptp = scattered_pages([PL], seed=3)
+        kp = ops.fill_normal_(torch.empty(num_pages * PAGE, hkv8 * 128, dtype=torch.bfloat16, device=dev), seed=4)
+        vp = ops.fill_normal_(torch.empty_like(kp), seed=4, stream_id=1)
+        q = ops.fill_normal_(torch.empty(CH, hq8, 128, dtype=torch.bfloat16, device=dev), seed=5)
+        ptd = torch.from_numpy(ptp).to(dev)
+        seq = torch.tensor([PL], dtype=torch.int32, device=dev)
+        qip = torch.tensor([0, CH], dtype=torch.int32, device=dev)
+        run = lambda: ops.paged_attention_extend(q, kp, vp, ptd, seq, qip, CH, hq8, hkv8)
+        for _ in range(args.steps):
+            run()
+        torch.cuda.synchronize()
+        assert ops.device_error() == (0, 0)
+        print(f"case {args.case}: {args.steps} launches ok", flush=True)
+        return 0
     if args.case in ("attention", "attention_cascade"):
         num_pages, pt = build_pages()
         kp = torch.empty(num_pages * PAGE, hkv * 128, dtype=torch.bfloat16, device=dev)
@@ -1511,7 +1528,8 @@ def main():
                     help="qwen3-8b-decode: the headline (default); the others: the remaining "
                          "benchmark configurations")
     ap.add_argument("--case", choices=["attention", "attention_cascade", "gemm", "gemm_qkv",
-                                       "gemm_partials", "gemm_prefill", "breakdown"], default=None,
+                                       "gemm_partials", "gemm_prefill", "breakdown", "extend"],
+                    default=None,
                     help="run one kernel of the step on a small single-layer case (profiling)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))

@@ -19,6 +19,8 @@
 #include <algorithm>
 #include <cstdlib>
 
+#include <string>
+
 #include "common.cuh"
 #include "tmap.h"
 
@@ -1280,6 +1282,19 @@ gemm_rows_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
 }
 
 // MSGL_GEMM_ROWS=0 turns the row-range schedule off (the cluster / stream-K schedules run).
+// MSGL_GEMM_DECODE (tuning override, default automatic): the schedule of decode-sized GEMMs
+// (M <= 128): "rows", "parts" (split-K partials + reduce), "cl" (cluster split-K) or "sk"
+// (stream-K); a schedule that does not apply to the shape falls through to the automatic choice.
+int decode_schedule() {
+    static const int v = [] {
+        const char* e = std::getenv("MSGL_GEMM_DECODE");
+        if (!e) return 0;
+        const std::string x(e);
+        return x == "rows" ? 1 : x == "parts" ? 2 : x == "cl" ? 3 : x == "sk" ? 4 : 0;
+    }();
+    return v;
+}
+
 bool rows_disabled() {
     static const bool off = [] {
         const char* e = std::getenv("MSGL_GEMM_ROWS");
@@ -1476,7 +1491,7 @@ int launch_cl(const CUtensorMap& tw, const CUtensorMap& tx, void* y, unsigned lo
     const int64_t cost = plan_cl<BN, EPI>(T, KB, C, nc);
     const int64_t sms = num_sms();
     const int64_t balanced = (static_cast<int64_t>(T) * KB + sms - 1) / sms;
-    if (nc <= 0 || cost * 5 > balanced * 6) return -1;
+    if (nc <= 0 || (decode_schedule() != 3 && cost * 5 > balanced * 6)) return -1;
     cudaError_t e = launch_cl_raw<BN, EPI>(tw, tx, y, amax, M, N, K, C, nc, id_off, err, stream);
     if (e != cudaSuccess) return set_error(MSGL_ERR_CUDA, cudaGetErrorString(e));
     return MSGL_OK;
@@ -1670,15 +1685,17 @@ int run_gemm(const void* x, const void* w, void* y, unsigned long long* amax, in
     if (K % 8) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "gemm: K must be a multiple of 8");
     if (M == 0) return MSGL_OK;
     if (M > 65535 * 256) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "gemm: M too large");
-    if (M <= 128 && !rows_disabled()) {
+    const int force = M <= 128 ? decode_schedule() : 0;
+    if (M <= 128 && !rows_disabled() && force <= 2) {
         // decode-sized: many weight rows -> whole row tiles per CTA (no K split); otherwise
         // split-K partials summed by a second small kernel (not for argmax, which needs whole
         // rows); row tiles of 6-9 groups only when the partials do not apply
         const int sms = num_sms();
         int tiles = 0;
         const int hs = plan_rows(N, sms, tiles);
-        if (hs >= 10) return launch_rows<EPI>(x, w, y, amax, M, N, K, hs, tiles, sms, stream, id_off);
-        if (EPI != EPI_ARGMAX) {
+        if (hs >= 10 && force != 2)
+            return launch_rows<EPI>(x, w, y, amax, M, N, K, hs, tiles, sms, stream, id_off);
+        if (EPI != EPI_ARGMAX && force != 1) {
             const int r = launch_part_reduce<EPI>(x, w, y, M, N, K, ws, ws_bytes, stream);
             if (r != -1) return r;
         }
@@ -1691,7 +1708,7 @@ int run_gemm(const void* x, const void* w, void* y, unsigned long long* amax, in
     if (rc) return rc;
     rc = make_tmap_2d_bf16(&tx, x, K, M, static_cast<uint64_t>(K) * 2, kBK, bn, true);
     if (rc) return rc;
-    if (bn <= 128) {  // one token tile: cluster split-K when it balances well (no workspace)
+    if (bn <= 128 && force != 4) {  // one token tile: cluster split-K when it balances well (no workspace)
         int r;
         switch (bn) {
             case 16: r = launch_cl<16, EPI>(tw, tx, y, amax, M, N, K, stream, id_off); break;
