@@ -1686,7 +1686,13 @@ int run_gemm(const void* x, const void* w, void* y, unsigned long long* amax, in
     if (M == 0) return MSGL_OK;
     if (M > 65535 * 256) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "gemm: M too large");
     const int force = M <= 128 ? decode_schedule() : 0;
-    if (M <= 128 && !rows_disabled() && force <= 2) {
+    // Small gate_up + SwiGLU (a wide tensor-parallel rank's shard, e.g. 3072 x 4096): the
+    // cluster schedule reduces in shared memory and needs no second kernel; measured at M 128,
+    // 3072 x 4096: 14.0 us cluster vs 19.8 us partials + reduce (at 6144 x 4096 partials win,
+    // 20.8 vs 23.5 us).
+    const bool small_swiglu = EPI == EPI_SWIGLU && M <= 128 && force == 0 &&
+                              static_cast<int64_t>(N) * K <= (int64_t(16) << 20);
+    if (M <= 128 && !rows_disabled() && force <= 2 && !small_swiglu) {
         // decode-sized: many weight rows -> whole row tiles per CTA (no K split); otherwise
         // split-K partials summed by a second small kernel (not for argmax, which needs whole
         // rows); row tiles of 6-9 groups only when the partials do not apply
@@ -1717,6 +1723,10 @@ int run_gemm(const void* x, const void* w, void* y, unsigned long long* amax, in
             default: r = launch_cl<128, EPI>(tw, tx, y, amax, M, N, K, stream, id_off); break;
         }
         if (r != -1) return r;
+        if (small_swiglu) {  // the cluster plan did not balance: partials + reduce after all
+            r = launch_part_reduce<EPI>(x, w, y, M, N, K, ws, ws_bytes, stream);
+            if (r != -1) return r;
+        }
     }
     if (tiles <= static_cast<int64_t>(kCounterBytes / sizeof(int))) {
         const int sms = num_sms();
