@@ -661,11 +661,12 @@ def run_case(args):
         seq = torch.tensor([PL], dtype=torch.int32, device=dev)
         qip = torch.tensor([0, CH], dtype=torch.int32, device=dev)
         run = lambda: ops.paged_attention_extend(q, kp, vp, ptd, seq, qip, CH, hq8, hkv8)
-        for _ in range(args.steps):
-            run()
-        torch.cuda.synchronize()
+        ms = time_kernel(run, args.steps, torch.cuda.current_stream())
         assert ops.device_error() == (0, 0)
-        print(f"case {args.case}: {args.steps} launches ok", flush=True)
+        pairs = sum(PL - CH + i + 1 for i in range(CH))
+        tf = 4.0 * 128 * pairs * hq8 / (ms * 1e-3) / 1e12
+        print(f"case {args.case}: {args.steps} launches ok, {ms * 1e3:.1f} us per launch, "
+              f"{tf:.1f} TFLOP/s", flush=True)
         return 0
     if args.case in ("attention", "attention_cascade"):
         num_pages, pt = build_pages()

@@ -20,6 +20,7 @@
 // byte is ~4 FLOP, far below the MMA rate.
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -510,6 +511,299 @@ paged_extend_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
     }
 }
 
+// ------------------------------------------------------------------------------ extend, tcgen05
+// Prefill / chunked-prefill attention on the 5th-generation tensor cores. One CTA per (128-row
+// query tile, kv head, request); the rows are (128 / group) query tokens x the group's heads,
+// token-major, so one UMMA of M = 128 covers every query head of the kv head. Keys go in blocks
+// of 128 (8 pages):
+//   warp 0   TMA producer: per block 8 pages x 2 dim halves x {K, V} (2-D boxes of 16 rows x 64
+//            dims, SWIZZLE_128B) into a 2-stage ring; a block's K and V tiles are [128 keys][64]
+//            halves, the canonical K-major layout for S = Q K^T and MN-major for O += P V;
+//   warp 1   MMA issuer (one lane): S = Q K^T into TMEM columns [0, 128) (8 UMMAs, K = 16),
+//            then, once the softmax has written P, O += P V into TMEM columns [128, 256) with P
+//            from shared memory (K-major) and V as an MN-major B operand;
+//   warps 2-5 softmax / epilogue, one TMEM lane (= query row) per thread: the row's Q into shared
+//            memory once; per block the row max (pass 1 over S), p = exp2(s - m) in bf16 into the
+//            P tile (pass 2), the running sum, and O *= exp2(m_old - m_new) in TMEM before the
+//            next P V; at the end O / l to global memory.
+// The online softmax is the reference's (layer.cpp:226-257: scale 1/sqrt(D), max subtraction,
+// fp32 accumulation) evaluated per block; causal masking by position L - q_len + i.
+constexpr int kTcRows = 128;
+constexpr int kTcKeys = 128;
+constexpr int kTcPages = kTcKeys / kPage;  // 8
+constexpr int kTcHalf = kTcRows * 128;     // 16 KB: 128 rows x 64 bf16
+constexpr int kTcTile = 2 * kTcHalf;       // 32 KB: 128 x 128 bf16
+constexpr int kTcStages = 2;
+constexpr int kTcThreads = 6 * 32;
+constexpr size_t kTcSmem = 1024 + 2 * kTcTile + kTcStages * 2 * kTcTile + 128;
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+                       const __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ out,
+                       const int* __restrict__ page_table, int max_pages,
+                       const int* __restrict__ seq_lens, const int* __restrict__ q_indptr,
+                       int pool_pages, int hq, int hkv, float sl2e, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = align1024(smem_raw);
+    uint8_t* sQ = smem;                 // [2 halves][128 rows][64], SW128
+    uint8_t* sP = smem + kTcTile;       // [2 halves][128 rows][64 keys], SW128
+    uint8_t* sKV = smem + 2 * kTcTile;  // stage s: K at s * 2 kTcTile, V at + kTcTile
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * kTcTile + kTcStages * 2 * kTcTile);
+    uint64_t* q_full = bars;
+    uint64_t* kv_full = bars + 1;   // [kTcStages]
+    uint64_t* kv_empty = bars + 3;  // [kTcStages]
+    uint64_t* s_full = bars + 5;
+    uint64_t* p_full = bars + 6;
+    uint64_t* o_ready = bars + 7;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+
+    const int b = blockIdx.z, kvh = blockIdx.y;
+    const int group = hq / hkv;
+    const int tpt = kTcRows / group;  // query tokens per tile
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 4);
+        for (int st = 0; st < kTcStages; ++st) {
+            mbar_init(&kv_full[st], 1);
+            mbar_init(&kv_empty[st], 1);
+        }
+        mbar_init(s_full, 1);
+        mbar_init(p_full, 4);
+        mbar_init(o_ready, 1);
+        fence_barrier_init();
+    }
+    pdl_wait();
+    pdl_trigger();
+    const int qbeg = q_indptr[b];
+    const int nq = q_indptr[b + 1] - qbeg;
+    const int tile0 = blockIdx.x * tpt;
+    if (tile0 >= nq) return;
+    const int L = seq_lens[b];
+    const int last_pos = L - nq + min(nq, tile0 + tpt) - 1;  // last key any row of the tile sees
+    if (last_pos < 0) {
+        if (threadIdx.x == 0) record_error(err, MSGL_ERR_INVALID_ARG, 250);
+        return;
+    }
+    int npages = (L + kPage - 1) / kPage;
+    if (npages > max_pages) {  // context longer than the page-table row
+        if (threadIdx.x == 0) record_error(err, MSGL_ERR_BOUNDS, 252);
+        npages = max_pages;
+    }
+    const int nblk = min(last_pos / kTcKeys + 1, (npages + kTcPages - 1) / kTcPages);
+    if (warp == 1) {  // TMEM: S in columns [0, 128), O in [128, 256)
+        tmem_alloc(tmem_slot, 256);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer
+        const int* pt = page_table + static_cast<int64_t>(b) * max_pages;
+        if (lane == 0) {
+            tma_prefetch_desc(&tk);
+            tma_prefetch_desc(&tv);
+        }
+        bool ok = true;
+        int page_reg = 0;
+        for (int j = 0; j < nblk; ++j) {
+            if ((j & 3) == 0) {  // page ids of blocks j .. j + 3, one per lane
+                const int pi = j * kTcPages + lane;
+                int page = 0;  // past the request's pages: page 0, every key there is masked
+                if (pi < npages) {
+                    page = pt[pi];
+                    if (static_cast<unsigned>(page) >= static_cast<unsigned>(pool_pages)) {
+                        record_error(err, MSGL_ERR_BOUNDS, 251);
+                        page = 0;
+                    }
+                }
+                page_reg = page;
+            }
+            int pg[kTcPages];
+#pragma unroll
+            for (int p = 0; p < kTcPages; ++p) pg[p] = __shfl_sync(0xffffffffu, page_reg, (j & 3) * kTcPages + p);
+            if (lane == 0) {
+                const int st = j % kTcStages;
+                if (j >= kTcStages && !mbar_wait(&kv_empty[st], ((j / kTcStages) - 1) & 1, err, 253)) {
+                    ok = false;
+                } else {
+                    mbar_arrive_expect_tx(&kv_full[st], 2 * kTcTile);
+                    uint8_t* kd = sKV + st * 2 * kTcTile;
+                    uint8_t* vd = kd + kTcTile;
+#pragma unroll
+                    for (int p = 0; p < kTcPages; ++p) {
+                        const int y = pg[p] * kPage;
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            tma_load_2d(kd + h * kTcHalf + p * 2048, &tk, &kv_full[st], kvh * kHd + h * 64, y);
+                            tma_load_2d(vd + h * kTcHalf + p * 2048, &tv, &kv_full[st], kvh * kHd + h * 64, y);
+                        }
+                    }
+                }
+            }
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer (one lane)
+        if (lane == 0) {
+            constexpr uint32_t idS = umma_idesc_bf16(kTcRows, kTcKeys);
+            constexpr uint32_t idO = umma_idesc_bf16_bmn(kTcRows, kHd);
+            const uint32_t tS = tmem, tO = tmem + 128;
+            const uint32_t aQ = smem_u32(sQ), aP = smem_u32(sP);
+            bool ok = mbar_wait(q_full, 0, err, 254);
+            for (int j = 0; ok && j < nblk; ++j) {
+                const int st = j % kTcStages;
+                if (!mbar_wait(&kv_full[st], (j / kTcStages) & 1, err, 255)) break;
+                tc_fence_after();
+                const uint32_t aK = smem_u32(sKV + st * 2 * kTcTile), aV = aK + kTcTile;
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    umma_bf16(tS, umma_desc_sw128(aQ + (k >> 2) * kTcHalf + (k & 3) * 32),
+                              umma_desc_sw128(aK + (k >> 2) * kTcHalf + (k & 3) * 32), idS,
+                              k > 0 ? 1u : 0u);
+                umma_commit(s_full);
+                if (!mbar_wait(p_full, j & 1, err, 256)) break;
+                tc_fence_after();
+#pragma unroll
+                for (int k = 0; k < 8; ++k)  // 16 keys per UMMA: P K-major, V MN-major
+                    umma_bf16(tO, umma_desc_sw128(aP + (k >> 2) * kTcHalf + (k & 3) * 32),
+                              umma_desc_sw128_mn(aV + k * 2048, kTcHalf, 1024), idO,
+                              (j > 0 || k > 0) ? 1u : 0u);
+                umma_commit(o_ready);
+                umma_commit(&kv_empty[st]);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ---------------- softmax / epilogue: thread = TMEM lane = query row
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;
+        const int t = r / group, hl = r % group;
+        const bool valid = tile0 + t < nq;
+        const int qpos = L - nq + tile0 + t;  // the row sees keys 0 .. qpos
+        const uint32_t row_t = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+        // the row's Q into the SW128 tile
+        {
+            const uint4* src = reinterpret_cast<const uint4*>(
+                q + (static_cast<int64_t>(qbeg + tile0 + (valid ? t : 0)) * hq + kvh * group + hl) * kHd);
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+                const uint4 v = valid ? src[c] : make_uint4(0, 0, 0, 0);
+                *reinterpret_cast<uint4*>(sQ + (c >> 3) * kTcHalf + r * 128 + (((c & 7) ^ (r & 7)) << 4)) = v;
+            }
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(q_full);
+        float m = kNegInf, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nblk; ++j) {
+            ok = __all_sync(0xffffffffu, mbar_wait(s_full, j & 1, err, 257));
+            if (!ok) break;
+            tc_fence_after();
+            const int kb = j * kTcKeys;
+            float mx = kNegInf;
+#pragma unroll
+            for (int c = 0; c < 8; c += 2) {  // pass 1: the row maximum of the scaled scores
+                uint32_t v0[16], v1[16];
+                tmem_ld16(row_t + c * 16, v0);
+                tmem_ld16(row_t + (c + 1) * 16, v1);
+                tmem_ld_wait();
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    if (kb + c * 16 + e <= qpos) mx = fmaxf(mx, __uint_as_float(v0[e]) * sl2e);
+                    if (kb + c * 16 + 16 + e <= qpos) mx = fmaxf(mx, __uint_as_float(v1[e]) * sl2e);
+                }
+            }
+            const float m_new = fmaxf(m, mx);
+            const float base = m_new == kNegInf ? 0.f : m_new;
+            const float alpha = m == kNegInf ? 0.f : exp2f(m - m_new);
+            float sum = 0.f;
+#pragma unroll
+            for (int c = 0; c < 8; c += 2) {  // pass 2: p (bf16 into P), the row sum
+                uint32_t v[32];
+                tmem_ld16(row_t + c * 16, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+                tmem_ld16(row_t + (c + 1) * 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
+                tmem_ld_wait();
+                uint32_t pk[16];
+#pragma unroll
+                for (int e = 0; e < 32; e += 2) {
+                    const int key = kb + c * 16 + e;
+                    const float p0 = key <= qpos ? exp2f(__uint_as_float(v[e]) * sl2e - base) : 0.f;
+                    const float p1 = key + 1 <= qpos ? exp2f(__uint_as_float(v[e + 1]) * sl2e - base) : 0.f;
+                    sum += p0 + p1;
+                    pk[e >> 1] = pack_bf16x2(p0, p1);
+                }
+                // keys c*16 .. c*16 + 31: half c / 4, 16-byte chunks (c % 4) * 2 .. + 3
+                uint8_t* prow = sP + (c >> 2) * kTcHalf + r * 128;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int chunk = (c & 3) * 2 + i;
+                    *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) << 4)) =
+                        make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+                }
+            }
+            l = l * alpha + sum;
+            m = m_new;
+            fence_proxy_async();  // the P tile, read by the tensor cores
+            if (j > 0) {          // O *= alpha, after the previous block's P V has landed
+                ok = __all_sync(0xffffffffu, mbar_wait(o_ready, (j - 1) & 1, err, 258));
+                if (!ok) break;
+                tc_fence_after();
+                if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        uint32_t o[16];
+                        tmem_ld16(row_t + 128 + c * 16, o);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+                        tmem_st16(row_t + 128 + c * 16, o);
+                    }
+                    tmem_st_wait();
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(p_full);
+        }
+        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(o_ready, (nblk - 1) & 1, err, 259));
+        if (ok) {
+            tc_fence_after();
+            const float inv = l > 0.f ? 1.f / l : 0.f;
+            __nv_bfloat16* dst = out + (static_cast<int64_t>(qbeg + tile0 + t) * hq + kvh * group + hl) * kHd;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                uint32_t o[16];
+                tmem_ld16(row_t + 128 + c * 16, o);
+                tmem_ld_wait();
+                if (valid) {
+                    uint4 w0, w1;
+                    w0.x = pack_bf16x2(__uint_as_float(o[0]) * inv, __uint_as_float(o[1]) * inv);
+                    w0.y = pack_bf16x2(__uint_as_float(o[2]) * inv, __uint_as_float(o[3]) * inv);
+                    w0.z = pack_bf16x2(__uint_as_float(o[4]) * inv, __uint_as_float(o[5]) * inv);
+                    w0.w = pack_bf16x2(__uint_as_float(o[6]) * inv, __uint_as_float(o[7]) * inv);
+                    w1.x = pack_bf16x2(__uint_as_float(o[8]) * inv, __uint_as_float(o[9]) * inv);
+                    w1.y = pack_bf16x2(__uint_as_float(o[10]) * inv, __uint_as_float(o[11]) * inv);
+                    w1.z = pack_bf16x2(__uint_as_float(o[12]) * inv, __uint_as_float(o[13]) * inv);
+                    w1.w = pack_bf16x2(__uint_as_float(o[14]) * inv, __uint_as_float(o[15]) * inv);
+                    reinterpret_cast<uint4*>(dst + c * 16)[0] = w0;
+                    reinterpret_cast<uint4*>(dst + c * 16)[1] = w1;
+                }
+            }
+        }
+        tc_fence_before();
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 256);
+    }
+}
+
 // ------------------------------------------------------------------------------ cascade decode
 // Decode when the first S page-table columns are the same pages for every request (a prefix
 // shared through the radix cache). One launch, two kinds of CTA:
@@ -982,6 +1276,15 @@ size_t cascade_workspace_bytes(int B, const CascadePlan& cp, int hq) {
            up(static_cast<size_t>(B) * cp.max_chunks * hq * 2 * sizeof(float));
 }
 
+// Extend kernel choice: the tcgen05 kernel when a request can fill at least half a 128-row tile
+// (max_q_len x group >= 64); the warp-level MMA kernel for short extends. MSGL_EXTEND_TC=0 forces
+// the warp-level kernel (read on every call).
+bool use_extend_tc(int max_q_len, int group) {
+    const char* e = std::getenv("MSGL_EXTEND_TC");
+    if (e && e[0] == '0') return false;
+    return static_cast<int64_t>(max_q_len) * group >= 64;
+}
+
 // Argument checks of the plain decode entry points (msgl_paged_attention_decode and the
 // no-allocation variant), done before anything is queued on the stream; fills the plan.
 int check_decode(int64_t num_slots, int max_pages, int num_reqs, int max_seq_len, int hq, int hkv,
@@ -1075,9 +1378,22 @@ int msgl_paged_attention_extend(const void* q, const void* k_pool, const void* v
     cudaError_t e = smem_optin(paged_extend_kernel, smem, optin);
     if (e != cudaSuccess) return set_error(MSGL_ERR_CUDA, cudaGetErrorString(e));
     const int group = num_q_heads / num_kv_heads;
+    const float sl2e = scale * 1.4426950408889634f;
+    if (use_extend_tc(max_q_len, group)) {  // tcgen05 tiles of 128 query rows
+        static std::atomic<int> optin_tc[kMaxDevices];
+        cudaError_t e2 = smem_optin(paged_extend_tc_kernel, kTcSmem, optin_tc);
+        if (e2 != cudaSuccess) return set_error(MSGL_ERR_CUDA, cudaGetErrorString(e2));
+        const int tpt = kTcRows / group;
+        dim3 grid_tc((max_q_len + tpt - 1) / tpt, num_kv_heads, num_reqs);
+        launch_pdl(paged_extend_tc_kernel, grid_tc, dim3(kTcThreads), kTcSmem, stream, tk, tv,
+                   static_cast<const __nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(out),
+                   page_table, max_pages, seq_lens, q_indptr, static_cast<int>(num_slots / kPage),
+                   num_q_heads, num_kv_heads, sl2e, err);
+        MSGL_LAUNCH_CHECK();
+        return MSGL_OK;
+    }
     const int tile_tokens = kConsumerWarps * (16 / group);
     dim3 grid((max_q_len + tile_tokens - 1) / tile_tokens, num_kv_heads, num_reqs);
-    const float sl2e = scale * 1.4426950408889634f;
     launch_pdl(paged_extend_kernel, grid, dim3(kThreads), smem, stream,
         tk, tv, static_cast<const __nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(out), page_table,
         max_pages, seq_lens, q_indptr, static_cast<int>(num_slots / kPage), num_q_heads,

@@ -265,6 +265,20 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
     return d;
 }
 
+// Shared-memory matrix descriptor, MN-major operand in the canonical SWIZZLE_128B layout: the
+// contiguous (M or N) dimension in rows of 128 B (64 bf16), 8 rows along K per 1024 B atom;
+// lbo = bytes between consecutive 64-element blocks along M / N, sbo = bytes between
+// consecutive 8-row groups along K.
+__device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);   // start address  [0,14)
+    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;     // LBO            [16,30)
+    d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;     // SBO            [32,46)
+    d |= static_cast<uint64_t>(1) << 46;                        // descriptor version (sm100)
+    d |= static_cast<uint64_t>(2) << 61;                        // SWIZZLE_128B
+    return d;
+}
+
 // Instruction descriptor: kind::f16, A/B bf16, D fp32, both K-major, shape M x N.
 __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
     return (1u << 4)                                   // D format f32
@@ -272,6 +286,11 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
            | (1u << 10)                                // B format bf16
            | (static_cast<uint32_t>(N >> 3) << 17)     // N / 8
            | (static_cast<uint32_t>(M >> 4) << 24);    // M / 16
+}
+
+// The same with B MN-major (the "transpose B" bit of the instruction descriptor).
+__host__ __device__ constexpr uint32_t umma_idesc_bf16_bmn(int M, int N) {
+    return umma_idesc_bf16(M, N) | (1u << 16);
 }
 
 __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,

@@ -201,6 +201,54 @@ def test_paged_extend(cuda, oracle, hq, hkv, qlens, ctx):
     assert ops.device_error() == (0, 0)
 
 
+@pytest.mark.parametrize("hq,hkv,qlens,ctx", [
+    (16, 2, [300, 512], [1500, 512]),        # group 8: 16 tokens per tile, cached prefix
+    (32, 8, [257, 64, 1], [900, 64, 700]),   # group 4, ragged, a one-token request
+    (8, 4, [200], [1000]),                   # group 2
+    (4, 4, [129, 128], [129, 640]),          # group 1: 128 tokens per tile
+])
+def test_paged_extend_tc(cuda, oracle, monkeypatch, hq, hkv, qlens, ctx):
+    """The tcgen05 extend kernel (128-row tiles, S and O in TMEM) against the oracle over longer
+    prefills, every group size; the warp-MMA kernel (MSGL_EXTEND_TC=0) on the same inputs too."""
+    from msgl import ops
+    rng = np.random.default_rng(sum(ctx) + 7 * hq)
+    num_pages = sum((c + 15) // 16 for c in ctx) + 3
+    kp, vp, pt = make_paged(rng, ctx, hkv, num_pages)
+    indptr = np.concatenate([[0], np.cumsum(qlens)]).astype(np.int32)
+    q = rn(rng, int(indptr[-1]), hq * 128)
+    seq = np.array(ctx, np.int32)
+    ref = oracle.paged_attention(q, kp, vp, pt, seq, indptr, hq, hkv, 128, 16)
+    args = (dev(q), dev(kp), dev(vp), dev(pt, torch.int32), dev(seq, torch.int32),
+            dev(indptr, torch.int32), max(qlens), hq, hkv)
+    out = host(ops.paged_attention_extend(*args)).reshape(q.shape[0], -1)
+    assert rel_l2(out, ref) < 1e-2, rel_l2(out, ref)
+    monkeypatch.setenv("MSGL_EXTEND_TC", "0")
+    legacy = host(ops.paged_attention_extend(*args)).reshape(q.shape[0], -1)
+    assert rel_l2(legacy, ref) < 1e-2
+    assert ops.device_error() == (0, 0)
+
+
+def test_paged_extend_tc_chunk_shape(cuda, monkeypatch):
+    """The 32B chunked prefill at a TP8 rank (8 q heads, 1 kv head): the last 2048-token chunk of
+    an 8192-token prompt, causal, pages scattered; tcgen05 kernel vs warp-MMA kernel (the fp32
+    oracle would take minutes at this size), and run-to-run bit equality."""
+    from msgl import ops
+    rng = np.random.default_rng(21)
+    CH, PL = 2048, 8192
+    kp, vp, pt = make_paged(rng, [PL], 1, PL // 16 + 5)
+    q = rn(rng, CH, 8 * 128)
+    args = (dev(q), dev(kp), dev(vp), dev(pt, torch.int32),
+            dev(np.array([PL], np.int32), torch.int32), dev(np.array([0, CH], np.int32), torch.int32),
+            CH, 8, 1)
+    a = host(ops.paged_attention_extend(*args))
+    b = host(ops.paged_attention_extend(*args))
+    assert np.array_equal(a, b)
+    monkeypatch.setenv("MSGL_EXTEND_TC", "0")
+    c = host(ops.paged_attention_extend(*args))
+    assert rel_l2(a.reshape(CH, -1), c.reshape(CH, -1)) < 1e-2
+    assert ops.device_error() == (0, 0)
+
+
 def make_shared_prefix(rng, S, suffix_lens, hkv, extra=4, P=16, D=128):
     """Page tables whose first S columns are the same pages for every request (a shared prefix),
     then each request's own pages; contexts S * 16 + suffix_len."""
