@@ -516,16 +516,19 @@ paged_extend_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
 // query tile, kv head, request); the rows are (128 / group) query tokens x the group's heads,
 // token-major, so one UMMA of M = 128 covers every query head of the kv head. Keys go in blocks
 // of 128 (8 pages):
-//   warp 0   TMA producer: per block 8 pages x 2 dim halves x {K, V} (2-D boxes of 16 rows x 64
-//            dims, SWIZZLE_128B) into a 2-stage ring; a block's K and V tiles are [128 keys][64]
-//            halves, the canonical K-major layout for S = Q K^T and MN-major for O += P V;
-//   warp 1   MMA issuer (one lane): S = Q K^T into TMEM columns [0, 128) (8 UMMAs, K = 16),
-//            then, once the softmax has written P, O += P V into TMEM columns [128, 256) with P
-//            from shared memory (K-major) and V as an MN-major B operand;
+//   warp 0   TMA producer: per block 8 pages x 2 dim halves of K into a 2-stage K ring and of V
+//            into a 2-stage V ring (2-D boxes of 16 rows x 64 dims, SWIZZLE_128B): a block's tiles
+//            are [128 keys][64] halves, the canonical K-major layout for S = Q K^T and MN-major
+//            for O += P V. A K stage is released when its S MMA completes, a V stage when its
+//            P V MMA completes, so the next block's K lands while the softmax still works;
+//   warp 1   MMA issuer (one lane): S(j+1) = Q K^T into the other of two TMEM S buffers while
+//            the softmax works on S(j), then O += P(j) V(j) into TMEM with P from shared memory
+//            (K-major) and V as an MN-major B operand;
 //   warps 2-5 softmax / epilogue, one TMEM lane (= query row) per thread: the row's Q into shared
-//            memory once; per block the row max (pass 1 over S), p = exp2(s - m) in bf16 into the
-//            P tile (pass 2), the running sum, and O *= exp2(m_old - m_new) in TMEM before the
-//            next P V; at the end O / l to global memory.
+//            memory once; per block S(j) into registers (two 64-column TMEM loads, one wait; the
+//            S buffer is released at once), the row max, p = exp2(s - m) as bf16 into the P
+//            tile, the running sum, O *= exp2(m_old - m_new) in TMEM; at the end O / l to global.
+// TMEM: S buffers at columns [0, 128) and [128, 256), O at [256, 384) (512 allocated).
 // The online softmax is the reference's (layer.cpp:226-257: scale 1/sqrt(D), max subtraction,
 // fp32 accumulation) evaluated per block; causal masking by position L - q_len + i.
 constexpr int kTcRows = 128;
@@ -535,7 +538,7 @@ constexpr int kTcHalf = kTcRows * 128;     // 16 KB: 128 rows x 64 bf16
 constexpr int kTcTile = 2 * kTcHalf;       // 32 KB: 128 x 128 bf16
 constexpr int kTcStages = 2;
 constexpr int kTcThreads = 6 * 32;
-constexpr size_t kTcSmem = 1024 + 2 * kTcTile + kTcStages * 2 * kTcTile + 128;
+constexpr size_t kTcSmem = 1024 + (2 + 2 * kTcStages) * kTcTile + 256;
 
 __global__ void __launch_bounds__(kTcThreads, 1)
 paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
@@ -545,17 +548,21 @@ paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
                        int pool_pages, int hq, int hkv, float sl2e, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = align1024(smem_raw);
-    uint8_t* sQ = smem;                 // [2 halves][128 rows][64], SW128
-    uint8_t* sP = smem + kTcTile;       // [2 halves][128 rows][64 keys], SW128
-    uint8_t* sKV = smem + 2 * kTcTile;  // stage s: K at s * 2 kTcTile, V at + kTcTile
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * kTcTile + kTcStages * 2 * kTcTile);
+    uint8_t* sQ = smem;                                // [2 halves][128 rows][64], SW128
+    uint8_t* sP = smem + kTcTile;                      // [2 halves][128 rows][64 keys], SW128
+    uint8_t* sK = smem + 2 * kTcTile;                  // [kTcStages] tiles
+    uint8_t* sV = sK + kTcStages * kTcTile;            // [kTcStages] tiles
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kTcStages * kTcTile);
     uint64_t* q_full = bars;
-    uint64_t* kv_full = bars + 1;   // [kTcStages]
-    uint64_t* kv_empty = bars + 3;  // [kTcStages]
-    uint64_t* s_full = bars + 5;
-    uint64_t* p_full = bars + 6;
-    uint64_t* o_ready = bars + 7;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+    uint64_t* k_full = bars + 1;    // [2]
+    uint64_t* k_empty = bars + 3;   // [2]
+    uint64_t* v_full = bars + 5;    // [2]
+    uint64_t* v_empty = bars + 7;   // [2]
+    uint64_t* s_full = bars + 9;    // [2]
+    uint64_t* s_free = bars + 11;   // [2]
+    uint64_t* p_full = bars + 13;
+    uint64_t* o_ready = bars + 14;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
 
     const int b = blockIdx.z, kvh = blockIdx.y;
     const int group = hq / hkv;
@@ -564,10 +571,13 @@ paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
     if (threadIdx.x == 0) {
         mbar_init(q_full, 4);
         for (int st = 0; st < kTcStages; ++st) {
-            mbar_init(&kv_full[st], 1);
-            mbar_init(&kv_empty[st], 1);
+            mbar_init(&k_full[st], 1);
+            mbar_init(&k_empty[st], 1);
+            mbar_init(&v_full[st], 1);
+            mbar_init(&v_empty[st], 1);
+            mbar_init(&s_full[st], 1);
+            mbar_init(&s_free[st], 4);
         }
-        mbar_init(s_full, 1);
         mbar_init(p_full, 4);
         mbar_init(o_ready, 1);
         fence_barrier_init();
@@ -590,8 +600,8 @@ paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
         npages = max_pages;
     }
     const int nblk = min(last_pos / kTcKeys + 1, (npages + kTcPages - 1) / kTcPages);
-    if (warp == 1) {  // TMEM: S in columns [0, 128), O in [128, 256)
-        tmem_alloc(tmem_slot, 256);
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, 512);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -626,20 +636,27 @@ paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
             for (int p = 0; p < kTcPages; ++p) pg[p] = __shfl_sync(0xffffffffu, page_reg, (j & 3) * kTcPages + p);
             if (lane == 0) {
                 const int st = j % kTcStages;
-                if (j >= kTcStages && !mbar_wait(&kv_empty[st], ((j / kTcStages) - 1) & 1, err, 253)) {
+                const uint32_t par = ((j / kTcStages) - 1) & 1;
+                if (j >= kTcStages && !mbar_wait(&k_empty[st], par, err, 253)) {
                     ok = false;
                 } else {
-                    mbar_arrive_expect_tx(&kv_full[st], 2 * kTcTile);
-                    uint8_t* kd = sKV + st * 2 * kTcTile;
-                    uint8_t* vd = kd + kTcTile;
+                    mbar_arrive_expect_tx(&k_full[st], kTcTile);
+                    uint8_t* kd = sK + st * kTcTile;
 #pragma unroll
-                    for (int p = 0; p < kTcPages; ++p) {
-                        const int y = pg[p] * kPage;
+                    for (int p = 0; p < kTcPages; ++p)
 #pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            tma_load_2d(kd + h * kTcHalf + p * 2048, &tk, &kv_full[st], kvh * kHd + h * 64, y);
-                            tma_load_2d(vd + h * kTcHalf + p * 2048, &tv, &kv_full[st], kvh * kHd + h * 64, y);
-                        }
+                        for (int h = 0; h < 2; ++h)
+                            tma_load_2d(kd + h * kTcHalf + p * 2048, &tk, &k_full[st], kvh * kHd + h * 64, pg[p] * kPage);
+                    if (j >= kTcStages && !mbar_wait(&v_empty[st], par, err, 253)) {
+                        ok = false;
+                    } else {
+                        mbar_arrive_expect_tx(&v_full[st], kTcTile);
+                        uint8_t* vd = sV + st * kTcTile;
+#pragma unroll
+                        for (int p = 0; p < kTcPages; ++p)
+#pragma unroll
+                            for (int h = 0; h < 2; ++h)
+                                tma_load_2d(vd + h * kTcHalf + p * 2048, &tv, &v_full[st], kvh * kHd + h * 64, pg[p] * kPage);
                     }
                 }
             }
@@ -651,29 +668,41 @@ paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
         if (lane == 0) {
             constexpr uint32_t idS = umma_idesc_bf16(kTcRows, kTcKeys);
             constexpr uint32_t idO = umma_idesc_bf16_bmn(kTcRows, kHd);
-            const uint32_t tS = tmem, tO = tmem + 128;
+            const uint32_t tO = tmem + 256;
             const uint32_t aQ = smem_u32(sQ), aP = smem_u32(sP);
-            bool ok = mbar_wait(q_full, 0, err, 254);
-            for (int j = 0; ok && j < nblk; ++j) {
+            // S(j) = Q K(j)^T into S buffer j % 2 (the caller checked that the buffer is free)
+            auto issue_s = [&](int j) -> bool {
                 const int st = j % kTcStages;
-                if (!mbar_wait(&kv_full[st], (j / kTcStages) & 1, err, 255)) break;
+                if (!mbar_wait(&k_full[st], (j / kTcStages) & 1, err, 255)) return false;
                 tc_fence_after();
-                const uint32_t aK = smem_u32(sKV + st * 2 * kTcTile), aV = aK + kTcTile;
+                const uint32_t aK = smem_u32(sK + st * kTcTile);
 #pragma unroll
                 for (int k = 0; k < 8; ++k)
-                    umma_bf16(tS, umma_desc_sw128(aQ + (k >> 2) * kTcHalf + (k & 3) * 32),
+                    umma_bf16(tmem + (j & 1) * 128, umma_desc_sw128(aQ + (k >> 2) * kTcHalf + (k & 3) * 32),
                               umma_desc_sw128(aK + (k >> 2) * kTcHalf + (k & 3) * 32), idS,
                               k > 0 ? 1u : 0u);
-                umma_commit(s_full);
+                umma_commit(&s_full[j & 1]);
+                umma_commit(&k_empty[st]);
+                return true;
+            };
+            bool ok = mbar_wait(q_full, 0, err, 254) && issue_s(0);
+            for (int j = 0; ok && j < nblk; ++j) {
+                if (j + 1 < nblk) {  // the next block's S, overlapping the softmax of this one
+                    if (j + 1 >= 2 && !mbar_wait(&s_free[(j + 1) & 1], (((j + 1) >> 1) - 1) & 1, err, 256)) break;
+                    if (!issue_s(j + 1)) break;
+                }
+                const int st = j % kTcStages;
+                if (!mbar_wait(&v_full[st], (j / kTcStages) & 1, err, 255)) break;
                 if (!mbar_wait(p_full, j & 1, err, 256)) break;
                 tc_fence_after();
+                const uint32_t aV = smem_u32(sV + st * kTcTile);
 #pragma unroll
                 for (int k = 0; k < 8; ++k)  // 16 keys per UMMA: P K-major, V MN-major
                     umma_bf16(tO, umma_desc_sw128(aP + (k >> 2) * kTcHalf + (k & 3) * 32),
                               umma_desc_sw128_mn(aV + k * 2048, kTcHalf, 1024), idO,
                               (j > 0 || k > 0) ? 1u : 0u);
                 umma_commit(o_ready);
-                umma_commit(&kv_empty[st]);
+                umma_commit(&v_empty[st]);
             }
         }
         __syncwarp();
@@ -685,8 +714,7 @@ paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
         const bool valid = tile0 + t < nq;
         const int qpos = L - nq + tile0 + t;  // the row sees keys 0 .. qpos
         const uint32_t row_t = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-        // the row's Q into the SW128 tile
-        {
+        {   // the row's Q into the SW128 tile
             const uint4* src = reinterpret_cast<const uint4*>(
                 q + (static_cast<int64_t>(qbeg + tile0 + (valid ? t : 0)) * hq + kvh * group + hl) * kHd);
 #pragma unroll
@@ -701,70 +729,60 @@ paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
         float m = kNegInf, l = 0.f;
         bool ok = true;
         for (int j = 0; j < nblk; ++j) {
-            ok = __all_sync(0xffffffffu, mbar_wait(s_full, j & 1, err, 257));
+            ok = __all_sync(0xffffffffu, mbar_wait(&s_full[j & 1], (j >> 1) & 1, err, 257));
             if (!ok) break;
             tc_fence_after();
+            uint32_t sv[128];
+            tmem_ld64(row_t + (j & 1) * 128, *reinterpret_cast<uint32_t(*)[64]>(&sv[0]));
+            tmem_ld64(row_t + (j & 1) * 128 + 64, *reinterpret_cast<uint32_t(*)[64]>(&sv[64]));
+            tmem_ld_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s_free[j & 1]);  // S(j) is in registers
             const int kb = j * kTcKeys;
             float mx = kNegInf;
 #pragma unroll
-            for (int c = 0; c < 8; c += 2) {  // pass 1: the row maximum of the scaled scores
-                uint32_t v0[16], v1[16];
-                tmem_ld16(row_t + c * 16, v0);
-                tmem_ld16(row_t + (c + 1) * 16, v1);
-                tmem_ld_wait();
-#pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    if (kb + c * 16 + e <= qpos) mx = fmaxf(mx, __uint_as_float(v0[e]) * sl2e);
-                    if (kb + c * 16 + 16 + e <= qpos) mx = fmaxf(mx, __uint_as_float(v1[e]) * sl2e);
-                }
+            for (int e = 0; e < 128; ++e) {
+                const float x = kb + e <= qpos ? __uint_as_float(sv[e]) * sl2e : kNegInf;
+                sv[e] = __float_as_uint(x);
+                mx = fmaxf(mx, x);
             }
             const float m_new = fmaxf(m, mx);
             const float base = m_new == kNegInf ? 0.f : m_new;
             const float alpha = m == kNegInf ? 0.f : exp2f(m - m_new);
+            if (j > 0) {  // P(j - 1) V(j - 1) has landed: the P tile is free and O is stable
+                ok = __all_sync(0xffffffffu, mbar_wait(o_ready, (j - 1) & 1, err, 258));
+                if (!ok) break;
+                tc_fence_after();
+            }
             float sum = 0.f;
 #pragma unroll
-            for (int c = 0; c < 8; c += 2) {  // pass 2: p (bf16 into P), the row sum
-                uint32_t v[32];
-                tmem_ld16(row_t + c * 16, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
-                tmem_ld16(row_t + (c + 1) * 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
-                tmem_ld_wait();
-                uint32_t pk[16];
+            for (int c = 0; c < 16; ++c) {  // 8 keys per 16-byte chunk of the P row
+                uint32_t pk[4];
 #pragma unroll
-                for (int e = 0; e < 32; e += 2) {
-                    const int key = kb + c * 16 + e;
-                    const float p0 = key <= qpos ? exp2f(__uint_as_float(v[e]) * sl2e - base) : 0.f;
-                    const float p1 = key + 1 <= qpos ? exp2f(__uint_as_float(v[e + 1]) * sl2e - base) : 0.f;
+                for (int e = 0; e < 4; ++e) {
+                    const float p0 = exp2f(__uint_as_float(sv[8 * c + 2 * e]) - base);
+                    const float p1 = exp2f(__uint_as_float(sv[8 * c + 2 * e + 1]) - base);
                     sum += p0 + p1;
-                    pk[e >> 1] = pack_bf16x2(p0, p1);
+                    pk[e] = pack_bf16x2(p0, p1);
                 }
-                // keys c*16 .. c*16 + 31: half c / 4, 16-byte chunks (c % 4) * 2 .. + 3
-                uint8_t* prow = sP + (c >> 2) * kTcHalf + r * 128;
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int chunk = (c & 3) * 2 + i;
-                    *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) << 4)) =
-                        make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
-                }
+                *reinterpret_cast<uint4*>(sP + (c >> 3) * kTcHalf + r * 128 + (((c & 7) ^ (r & 7)) << 4)) =
+                    make_uint4(pk[0], pk[1], pk[2], pk[3]);
             }
             l = l * alpha + sum;
             m = m_new;
             fence_proxy_async();  // the P tile, read by the tensor cores
-            if (j > 0) {          // O *= alpha, after the previous block's P V has landed
-                ok = __all_sync(0xffffffffu, mbar_wait(o_ready, (j - 1) & 1, err, 258));
-                if (!ok) break;
-                tc_fence_after();
-                if (__any_sync(0xffffffffu, alpha != 1.f)) {
+            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {  // O *= alpha
 #pragma unroll
-                    for (int c = 0; c < 8; ++c) {
-                        uint32_t o[16];
-                        tmem_ld16(row_t + 128 + c * 16, o);
-                        tmem_ld_wait();
+                for (int h = 0; h < 2; ++h) {
+                    uint32_t o[64];
+                    tmem_ld64(row_t + 256 + h * 64, o);
+                    tmem_ld_wait();
 #pragma unroll
-                        for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-                        tmem_st16(row_t + 128 + c * 16, o);
-                    }
-                    tmem_st_wait();
+                    for (int e = 0; e < 64; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+                    tmem_st64(row_t + 256 + h * 64, o);
                 }
+                tmem_st_wait();
             }
             tc_fence_before();
             __syncwarp();
@@ -776,22 +794,20 @@ paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
             const float inv = l > 0.f ? 1.f / l : 0.f;
             __nv_bfloat16* dst = out + (static_cast<int64_t>(qbeg + tile0 + t) * hq + kvh * group + hl) * kHd;
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                uint32_t o[16];
-                tmem_ld16(row_t + 128 + c * 16, o);
+            for (int h = 0; h < 2; ++h) {
+                uint32_t o[64];
+                tmem_ld64(row_t + 256 + h * 64, o);
                 tmem_ld_wait();
                 if (valid) {
-                    uint4 w0, w1;
-                    w0.x = pack_bf16x2(__uint_as_float(o[0]) * inv, __uint_as_float(o[1]) * inv);
-                    w0.y = pack_bf16x2(__uint_as_float(o[2]) * inv, __uint_as_float(o[3]) * inv);
-                    w0.z = pack_bf16x2(__uint_as_float(o[4]) * inv, __uint_as_float(o[5]) * inv);
-                    w0.w = pack_bf16x2(__uint_as_float(o[6]) * inv, __uint_as_float(o[7]) * inv);
-                    w1.x = pack_bf16x2(__uint_as_float(o[8]) * inv, __uint_as_float(o[9]) * inv);
-                    w1.y = pack_bf16x2(__uint_as_float(o[10]) * inv, __uint_as_float(o[11]) * inv);
-                    w1.z = pack_bf16x2(__uint_as_float(o[12]) * inv, __uint_as_float(o[13]) * inv);
-                    w1.w = pack_bf16x2(__uint_as_float(o[14]) * inv, __uint_as_float(o[15]) * inv);
-                    reinterpret_cast<uint4*>(dst + c * 16)[0] = w0;
-                    reinterpret_cast<uint4*>(dst + c * 16)[1] = w1;
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        uint4 w;
+                        w.x = pack_bf16x2(__uint_as_float(o[8 * c]) * inv, __uint_as_float(o[8 * c + 1]) * inv);
+                        w.y = pack_bf16x2(__uint_as_float(o[8 * c + 2]) * inv, __uint_as_float(o[8 * c + 3]) * inv);
+                        w.z = pack_bf16x2(__uint_as_float(o[8 * c + 4]) * inv, __uint_as_float(o[8 * c + 5]) * inv);
+                        w.w = pack_bf16x2(__uint_as_float(o[8 * c + 6]) * inv, __uint_as_float(o[8 * c + 7]) * inv);
+                        reinterpret_cast<uint4*>(dst + h * 64)[c] = w;
+                    }
                 }
             }
         }
@@ -800,7 +816,7 @@ paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, 256);
+        tmem_dealloc(tmem, 512);
     }
 }
 
