@@ -523,7 +523,8 @@ paged_extend_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
 //            P V MMA completes, so the next block's K lands while the softmax still works;
 //   warp 1   MMA issuer (one lane): S(j+1) = Q K^T into the other of two TMEM S buffers while
 //            the softmax works on S(j), then O += P(j) V(j) into TMEM with P from shared memory
-//            (K-major) and V as an MN-major B operand;
+//            (K-major, two P buffers: the softmax writes P(j+1) while P(j) V(j) runs) and V as
+//            an MN-major B operand;
 //   warps 2-5 softmax / epilogue, one TMEM lane (= query row) per thread: the row's Q into shared
 //            memory once; per block S(j) into registers (two 64-column TMEM loads, one wait; the
 //            S buffer is released at once), the row max, p = exp2(s - m) as bf16 into the P
@@ -538,7 +539,7 @@ constexpr int kTcHalf = kTcRows * 128;     // 16 KB: 128 rows x 64 bf16
 constexpr int kTcTile = 2 * kTcHalf;       // 32 KB: 128 x 128 bf16
 constexpr int kTcStages = 2;
 constexpr int kTcThreads = 6 * 32;
-constexpr size_t kTcSmem = 1024 + (2 + 2 * kTcStages) * kTcTile + 256;
+constexpr size_t kTcSmem = 1024 + (3 + 2 * kTcStages) * kTcTile + 256;  // Q, P x 2, K x 2, V x 2
 
 __global__ void __launch_bounds__(kTcThreads, 1)
 paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
@@ -549,8 +550,8 @@ paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = align1024(smem_raw);
     uint8_t* sQ = smem;                                // [2 halves][128 rows][64], SW128
-    uint8_t* sP = smem + kTcTile;                      // [2 halves][128 rows][64 keys], SW128
-    uint8_t* sK = smem + 2 * kTcTile;                  // [kTcStages] tiles
+    uint8_t* sP = smem + kTcTile;                      // [2 blocks][2 halves][128 rows][64 keys]
+    uint8_t* sK = smem + 3 * kTcTile;                  // [kTcStages] tiles
     uint8_t* sV = sK + kTcStages * kTcTile;            // [kTcStages] tiles
     uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kTcStages * kTcTile);
     uint64_t* q_full = bars;
@@ -560,9 +561,11 @@ paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
     uint64_t* v_empty = bars + 7;   // [2]
     uint64_t* s_full = bars + 9;    // [2]
     uint64_t* s_free = bars + 11;   // [2]
-    uint64_t* p_full = bars + 13;
-    uint64_t* o_ready = bars + 14;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+    // one barrier per block parity for every hand-off, so that no waiter can find its barrier
+    // two phases ahead of the phase it waits for
+    uint64_t* p_full = bars + 13;   // [2]
+    uint64_t* o_ready = bars + 15;  // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
 
     const int b = blockIdx.z, kvh = blockIdx.y;
     const int group = hq / hkv;
@@ -578,8 +581,10 @@ paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
             mbar_init(&s_full[st], 1);
             mbar_init(&s_free[st], 4);
         }
-        mbar_init(p_full, 4);
-        mbar_init(o_ready, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&p_full[i], 4);
+            mbar_init(&o_ready[i], 1);
+        }
         fence_barrier_init();
     }
     pdl_wait();
@@ -693,15 +698,15 @@ paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
                 }
                 const int st = j % kTcStages;
                 if (!mbar_wait(&v_full[st], (j / kTcStages) & 1, err, 255)) break;
-                if (!mbar_wait(p_full, j & 1, err, 256)) break;
+                if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, err, 256)) break;
                 tc_fence_after();
-                const uint32_t aV = smem_u32(sV + st * kTcTile);
+                const uint32_t aV = smem_u32(sV + st * kTcTile), aPj = aP + (j & 1) * kTcTile;
 #pragma unroll
                 for (int k = 0; k < 8; ++k)  // 16 keys per UMMA: P K-major, V MN-major
-                    umma_bf16(tO, umma_desc_sw128(aP + (k >> 2) * kTcHalf + (k & 3) * 32),
+                    umma_bf16(tO, umma_desc_sw128(aPj + (k >> 2) * kTcHalf + (k & 3) * 32),
                               umma_desc_sw128_mn(aV + k * 2048, kTcHalf, 1024), idO,
                               (j > 0 || k > 0) ? 1u : 0u);
-                umma_commit(o_ready);
+                umma_commit(&o_ready[j & 1]);
                 umma_commit(&v_empty[st]);
             }
         }
@@ -740,22 +745,30 @@ paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
             __syncwarp();
             if (lane == 0) mbar_arrive(&s_free[j & 1]);  // S(j) is in registers
             const int kb = j * kTcKeys;
-            float mx = kNegInf;
+            float mx8[8];
 #pragma unroll
-            for (int e = 0; e < 128; ++e) {
+            for (int i = 0; i < 8; ++i) mx8[i] = kNegInf;
+#pragma unroll
+            for (int e = 0; e < 128; ++e) {  // eight independent max chains
                 const float x = kb + e <= qpos ? __uint_as_float(sv[e]) * sl2e : kNegInf;
                 sv[e] = __float_as_uint(x);
-                mx = fmaxf(mx, x);
+                mx8[e & 7] = fmaxf(mx8[e & 7], x);
             }
-            const float m_new = fmaxf(m, mx);
+            const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                   fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+            // The running max moves only when the block's max exceeds it by more than 2^8 in p:
+            // p = exp2(s - m) then stays <= 256 (exact enough in bf16, and O / l uses the same m),
+            // and O is rescaled in TMEM only on those (rare, after the first blocks) steps.
+            const float m_new = (m == kNegInf || mx > m + 8.f) ? fmaxf(m, mx) : m;
             const float base = m_new == kNegInf ? 0.f : m_new;
             const float alpha = m == kNegInf ? 0.f : exp2f(m - m_new);
-            if (j > 0) {  // P(j - 1) V(j - 1) has landed: the P tile is free and O is stable
-                ok = __all_sync(0xffffffffu, mbar_wait(o_ready, (j - 1) & 1, err, 258));
+            if (j >= 2) {  // P(j - 2) V(j - 2) has landed: this block's P buffer is free
+                ok = __all_sync(0xffffffffu, mbar_wait(&o_ready[j & 1], ((j - 2) >> 1) & 1, err, 258));
                 if (!ok) break;
                 tc_fence_after();
             }
-            float sum = 0.f;
+            uint8_t* sPj = sP + (j & 1) * kTcTile;
+            float sum4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int c = 0; c < 16; ++c) {  // 8 keys per 16-byte chunk of the P row
                 uint32_t pk[4];
@@ -763,16 +776,20 @@ paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
                 for (int e = 0; e < 4; ++e) {
                     const float p0 = exp2f(__uint_as_float(sv[8 * c + 2 * e]) - base);
                     const float p1 = exp2f(__uint_as_float(sv[8 * c + 2 * e + 1]) - base);
-                    sum += p0 + p1;
+                    sum4[e] += p0 + p1;
                     pk[e] = pack_bf16x2(p0, p1);
                 }
-                *reinterpret_cast<uint4*>(sP + (c >> 3) * kTcHalf + r * 128 + (((c & 7) ^ (r & 7)) << 4)) =
+                *reinterpret_cast<uint4*>(sPj + (c >> 3) * kTcHalf + r * 128 + (((c & 7) ^ (r & 7)) << 4)) =
                     make_uint4(pk[0], pk[1], pk[2], pk[3]);
             }
-            l = l * alpha + sum;
+            l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
             m = m_new;
             fence_proxy_async();  // the P tile, read by the tensor cores
-            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {  // O *= alpha
+            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+                // O *= alpha once P(j - 1) V(j - 1) has landed (and before P(j) V(j) is issued)
+                ok = __all_sync(0xffffffffu, mbar_wait(&o_ready[(j - 1) & 1], ((j - 1) >> 1) & 1, err, 258));
+                if (!ok) break;
+                tc_fence_after();
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     uint32_t o[64];
@@ -786,9 +803,10 @@ paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
+            if (lane == 0) mbar_arrive(&p_full[j & 1]);
         }
-        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(o_ready, (nblk - 1) & 1, err, 259));
+        if (ok)
+            ok = __all_sync(0xffffffffu, mbar_wait(&o_ready[(nblk - 1) & 1], ((nblk - 1) >> 1) & 1, err, 259));
         if (ok) {
             tc_fence_after();
             const float inv = l > 0.f ? 1.f / l : 0.f;
