@@ -525,10 +525,13 @@ paged_extend_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
 //            the softmax works on S(j), then O += P(j) V(j) into TMEM with P from shared memory
 //            (K-major, two P buffers: the softmax writes P(j+1) while P(j) V(j) runs) and V as
 //            an MN-major B operand;
-//   warps 2-5 softmax / epilogue, one TMEM lane (= query row) per thread: the row's Q into shared
-//            memory once; per block S(j) into registers (two 64-column TMEM loads, one wait; the
-//            S buffer is released at once), the row max, p = exp2(s - m) as bf16 into the P
-//            tile, the running sum, O *= exp2(m_old - m_new) in TMEM; at the end O / l to global.
+//   warps 2-9 softmax / epilogue: a pair of warps per TMEM lane quarter (warp % 4), each thread of
+//            the pair one query row and one half of the 128 keys (and of O's 128 columns): the
+//            row's Q half into shared memory once; per block its 64 S columns into registers
+//            (one TMEM load; the S buffer is released once both halves are out), the row max
+//            (the two halves meet through shared memory and a named barrier per pair),
+//            p = exp2(s - m) as bf16 into its half of the P tile, its part of the running sum,
+//            and O *= exp2(m_old - m_new) on its 64 columns; at the end O / l to global.
 // TMEM: S buffers at columns [0, 128) and [128, 256), O at [256, 384) (512 allocated).
 // The online softmax is the reference's (layer.cpp:226-257: scale 1/sqrt(D), max subtraction,
 // fp32 accumulation) evaluated per block; causal masking by position L - q_len + i.
@@ -538,8 +541,8 @@ constexpr int kTcPages = kTcKeys / kPage;  // 8
 constexpr int kTcHalf = kTcRows * 128;     // 16 KB: 128 rows x 64 bf16
 constexpr int kTcTile = 2 * kTcHalf;       // 32 KB: 128 x 128 bf16
 constexpr int kTcStages = 2;
-constexpr int kTcThreads = 6 * 32;
-constexpr size_t kTcSmem = 1024 + (3 + 2 * kTcStages) * kTcTile + 256;  // Q, P x 2, K x 2, V x 2
+constexpr int kTcThreads = 10 * 32;  // producer, MMA, 8 softmax warps
+constexpr size_t kTcSmem = 1024 + (3 + 2 * kTcStages) * kTcTile + 256 + 1024;  // Q, P x 2, K x 2, V x 2, barriers, max exchange
 
 __global__ void __launch_bounds__(kTcThreads, 1)
 paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
@@ -566,23 +569,24 @@ paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
     uint64_t* p_full = bars + 13;   // [2]
     uint64_t* o_ready = bars + 15;  // [2]
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+    float* red = reinterpret_cast<float*>(bars + 18);  // [2 halves][128 rows]
 
     const int b = blockIdx.z, kvh = blockIdx.y;
     const int group = hq / hkv;
     const int tpt = kTcRows / group;  // query tokens per tile
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
-        mbar_init(q_full, 4);
+        mbar_init(q_full, 8);
         for (int st = 0; st < kTcStages; ++st) {
             mbar_init(&k_full[st], 1);
             mbar_init(&k_empty[st], 1);
             mbar_init(&v_full[st], 1);
             mbar_init(&v_empty[st], 1);
             mbar_init(&s_full[st], 1);
-            mbar_init(&s_free[st], 4);
+            mbar_init(&s_free[st], 8);
         }
         for (int i = 0; i < 2; ++i) {
-            mbar_init(&p_full[i], 4);
+            mbar_init(&p_full[i], 8);
             mbar_init(&o_ready[i], 1);
         }
         fence_barrier_init();
@@ -712,20 +716,22 @@ paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
         }
         __syncwarp();
     } else {
-        // ---------------- softmax / epilogue: thread = TMEM lane = query row
+        // ---------------- softmax / epilogue: thread = (TMEM lane = query row, half of the keys)
         const int quarter = warp & 3;
+        const int ch = (warp - 2) >> 2;  // key / O-column half of this warp
         const int r = quarter * 32 + lane;
         const int t = r / group, hl = r % group;
         const bool valid = tile0 + t < nq;
         const int qpos = L - nq + tile0 + t;  // the row sees keys 0 .. qpos
         const uint32_t row_t = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-        {   // the row's Q into the SW128 tile
+        const int pair_bar = 1 + quarter;    // named barrier of the two warps of this quarter
+        {   // this half of the row's Q into the SW128 tile
             const uint4* src = reinterpret_cast<const uint4*>(
-                q + (static_cast<int64_t>(qbeg + tile0 + (valid ? t : 0)) * hq + kvh * group + hl) * kHd);
+                q + (static_cast<int64_t>(qbeg + tile0 + (valid ? t : 0)) * hq + kvh * group + hl) * kHd + ch * 64);
 #pragma unroll
-            for (int c = 0; c < 16; ++c) {
+            for (int c = 0; c < 8; ++c) {
                 const uint4 v = valid ? src[c] : make_uint4(0, 0, 0, 0);
-                *reinterpret_cast<uint4*>(sQ + (c >> 3) * kTcHalf + r * 128 + (((c & 7) ^ (r & 7)) << 4)) = v;
+                *reinterpret_cast<uint4*>(sQ + ch * kTcHalf + r * 128 + ((c ^ (r & 7)) << 4)) = v;
             }
         }
         fence_proxy_async();
@@ -733,29 +739,38 @@ paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
         if (lane == 0) mbar_arrive(q_full);
         float m = kNegInf, l = 0.f;
         bool ok = true;
+        // Every iteration runs the same two pair barriers on both warps of a pair: after a wait
+        // that ran out (recorded in the error word) a warp skips the work and the waits but
+        // keeps the barrier sequence, so the pair never meets at different barriers.
         for (int j = 0; j < nblk; ++j) {
-            ok = __all_sync(0xffffffffu, mbar_wait(&s_full[j & 1], (j >> 1) & 1, err, 257));
-            if (!ok) break;
-            tc_fence_after();
-            uint32_t sv[128];
-            tmem_ld64(row_t + (j & 1) * 128, *reinterpret_cast<uint32_t(*)[64]>(&sv[0]));
-            tmem_ld64(row_t + (j & 1) * 128 + 64, *reinterpret_cast<uint32_t(*)[64]>(&sv[64]));
-            tmem_ld_wait();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s_free[j & 1]);  // S(j) is in registers
-            const int kb = j * kTcKeys;
-            float mx8[8];
+            ok = ok && __all_sync(0xffffffffu, mbar_wait(&s_full[j & 1], (j >> 1) & 1, err, 257));
+            uint32_t sv[64];
+            float mx = kNegInf;
+            const int kb = j * kTcKeys + ch * 64;
+            if (ok) {
+                tc_fence_after();
+                tmem_ld64(row_t + (j & 1) * 128 + ch * 64, sv);
+                tmem_ld_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s_free[j & 1]);  // this half of S(j) is in registers
+                float mx8[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) mx8[i] = kNegInf;
+                for (int i = 0; i < 8; ++i) mx8[i] = kNegInf;
 #pragma unroll
-            for (int e = 0; e < 128; ++e) {  // eight independent max chains
-                const float x = kb + e <= qpos ? __uint_as_float(sv[e]) * sl2e : kNegInf;
-                sv[e] = __float_as_uint(x);
-                mx8[e & 7] = fmaxf(mx8[e & 7], x);
+                for (int e = 0; e < 64; ++e) {  // eight independent max chains
+                    const float x = kb + e <= qpos ? __uint_as_float(sv[e]) * sl2e : kNegInf;
+                    sv[e] = __float_as_uint(x);
+                    mx8[e & 7] = fmaxf(mx8[e & 7], x);
+                }
+                mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                           fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
             }
-            const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                                   fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+            red[ch * 128 + r] = mx;
+            named_bar_sync(pair_bar, 64);
+            mx = fmaxf(mx, red[(1 - ch) * 128 + r]);
+            named_bar_sync(pair_bar, 64);  // both read before either writes the next value
+            if (!ok) continue;
             // The running max moves only when the block's max exceeds it by more than 2^8 in p:
             // p = exp2(s - m) then stays <= 256 (exact enough in bf16, and O / l uses the same m),
             // and O is rescaled in TMEM only on those (rare, after the first blocks) steps.
@@ -764,13 +779,13 @@ paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
             const float alpha = m == kNegInf ? 0.f : exp2f(m - m_new);
             if (j >= 2) {  // P(j - 2) V(j - 2) has landed: this block's P buffer is free
                 ok = __all_sync(0xffffffffu, mbar_wait(&o_ready[j & 1], ((j - 2) >> 1) & 1, err, 258));
-                if (!ok) break;
+                if (!ok) continue;
                 tc_fence_after();
             }
-            uint8_t* sPj = sP + (j & 1) * kTcTile;
+            uint8_t* sPj = sP + (j & 1) * kTcTile + ch * kTcHalf + r * 128;
             float sum4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int c = 0; c < 16; ++c) {  // 8 keys per 16-byte chunk of the P row
+            for (int c = 0; c < 8; ++c) {  // 8 keys per 16-byte chunk of this half of the P row
                 uint32_t pk[4];
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
@@ -779,8 +794,7 @@ paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
                     sum4[e] += p0 + p1;
                     pk[e] = pack_bf16x2(p0, p1);
                 }
-                *reinterpret_cast<uint4*>(sPj + (c >> 3) * kTcHalf + r * 128 + (((c & 7) ^ (r & 7)) << 4)) =
-                    make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                *reinterpret_cast<uint4*>(sPj + ((c ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
             }
             l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
             m = m_new;
@@ -788,17 +802,14 @@ paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
             if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
                 // O *= alpha once P(j - 1) V(j - 1) has landed (and before P(j) V(j) is issued)
                 ok = __all_sync(0xffffffffu, mbar_wait(&o_ready[(j - 1) & 1], ((j - 1) >> 1) & 1, err, 258));
-                if (!ok) break;
+                if (!ok) continue;
                 tc_fence_after();
+                uint32_t o[64];
+                tmem_ld64(row_t + 256 + ch * 64, o);
+                tmem_ld_wait();
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    uint32_t o[64];
-                    tmem_ld64(row_t + 256 + h * 64, o);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int e = 0; e < 64; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-                    tmem_st64(row_t + 256 + h * 64, o);
-                }
+                for (int e = 0; e < 64; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+                tmem_st64(row_t + 256 + ch * 64, o);
                 tmem_st_wait();
             }
             tc_fence_before();
@@ -807,25 +818,26 @@ paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
         }
         if (ok)
             ok = __all_sync(0xffffffffu, mbar_wait(&o_ready[(nblk - 1) & 1], ((nblk - 1) >> 1) & 1, err, 259));
+        // the row sum: this half's part plus the partner's (both halves use the same m)
+        red[ch * 128 + r] = l;
+        named_bar_sync(pair_bar, 64);
+        l += red[(1 - ch) * 128 + r];
         if (ok) {
             tc_fence_after();
             const float inv = l > 0.f ? 1.f / l : 0.f;
-            __nv_bfloat16* dst = out + (static_cast<int64_t>(qbeg + tile0 + t) * hq + kvh * group + hl) * kHd;
+            __nv_bfloat16* dst = out + (static_cast<int64_t>(qbeg + tile0 + t) * hq + kvh * group + hl) * kHd + ch * 64;
+            uint32_t o[64];
+            tmem_ld64(row_t + 256 + ch * 64, o);
+            tmem_ld_wait();
+            if (valid) {
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                uint32_t o[64];
-                tmem_ld64(row_t + 256 + h * 64, o);
-                tmem_ld_wait();
-                if (valid) {
-#pragma unroll
-                    for (int c = 0; c < 8; ++c) {
-                        uint4 w;
-                        w.x = pack_bf16x2(__uint_as_float(o[8 * c]) * inv, __uint_as_float(o[8 * c + 1]) * inv);
-                        w.y = pack_bf16x2(__uint_as_float(o[8 * c + 2]) * inv, __uint_as_float(o[8 * c + 3]) * inv);
-                        w.z = pack_bf16x2(__uint_as_float(o[8 * c + 4]) * inv, __uint_as_float(o[8 * c + 5]) * inv);
-                        w.w = pack_bf16x2(__uint_as_float(o[8 * c + 6]) * inv, __uint_as_float(o[8 * c + 7]) * inv);
-                        reinterpret_cast<uint4*>(dst + h * 64)[c] = w;
-                    }
+                for (int c = 0; c < 8; ++c) {
+                    uint4 w;
+                    w.x = pack_bf16x2(__uint_as_float(o[8 * c]) * inv, __uint_as_float(o[8 * c + 1]) * inv);
+                    w.y = pack_bf16x2(__uint_as_float(o[8 * c + 2]) * inv, __uint_as_float(o[8 * c + 3]) * inv);
+                    w.z = pack_bf16x2(__uint_as_float(o[8 * c + 4]) * inv, __uint_as_float(o[8 * c + 5]) * inv);
+                    w.w = pack_bf16x2(__uint_as_float(o[8 * c + 6]) * inv, __uint_as_float(o[8 * c + 7]) * inv);
+                    reinterpret_cast<uint4*>(dst)[c] = w;
                 }
             }
         }
