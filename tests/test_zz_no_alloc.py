@@ -101,3 +101,36 @@ def test_noalloc_rejects_oversized_batch(cuda):
         ops.paged_attention_decode_noalloc(q, kp, kp, pt, seq, L, hq, hkv)
     assert e.value.code == 7  # MSGL_ERR_WORKSPACE
     assert ops.device_error() == (0, 0)
+
+
+def test_attention_entry_points_on_two_devices_in_one_process(cuda):
+    """One process drives two GPUs: decode, cascade decode, extend (tcgen05) and the no-allocation
+    decode run on device 0 and then on device 1 (each device gets its own shared-memory opt-in and
+    its own static scratch address); every output on device 1 equals device 0's bit for bit."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from msgl import ops
+    seq_lens, hq, hkv = [300, 2048, 17, 777, 1], 32, 8
+    outs = []
+    for d in (0, 1):
+        with torch.cuda.device(d):
+            q, kp, vp, pt, seq = _case(31, seq_lens, hq, hkv)
+            L = max(seq_lens)
+            r = [ops.paged_attention_decode(q, kp, vp, pt, seq, L, hq, hkv),
+                 ops.paged_attention_decode_noalloc(q, kp, vp, pt, seq, L, hq, hkv)]
+            # cascade: every request shares the first two pages of request 1's table
+            shared = pt.clone()
+            shared[:, :2] = pt[1, :2]
+            seq_c = torch.clamp(seq, min=2 * P + 1)
+            r.append(ops.paged_attention_decode_cascade(q, kp, vp, shared, seq_c, L, 2, hq, hkv))
+            # extend: request 1 as a 256-token chunk at the end of its context
+            qe = q.new_zeros(256, hq * D)
+            qe.copy_(torch.randn(256, hq * D, generator=torch.Generator().manual_seed(5)).to(qe.dtype))
+            ind = torch.tensor([0, 256], dtype=torch.int32, device=q.device)
+            r.append(ops.paged_attention_extend(qe, kp, vp, pt[1:2].contiguous(), seq[1:2].contiguous(),
+                                                ind, 256, hq, hkv))
+            torch.cuda.synchronize()
+            assert ops.device_error() == (0, 0)
+            outs.append([x.cpu() for x in r])
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
