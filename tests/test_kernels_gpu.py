@@ -398,8 +398,10 @@ def test_gemm_matches_oracle_linear(cuda, oracle):
 
 
 # (128, 12288, 1024) and (5, 12288, 256): 24576 weight rows take the row-range schedule (whole
-# 176-row tiles per CTA); (4, 3072, 1024), (128, 1536, 4096) and (96, 6144, 512) split-K partials
-# summed by the SwiGLU reduce kernel; (37, 96, 256) the cluster kernel, (300, 768, 512) stream-K
+# 176-row tiles per CTA); (4, 3072, 1024), (128, 1536, 4096) (a TP8 rank of Qwen3-8B) and
+# (96, 6144, 512): small gate_up (2I x K <= 16M elements) on the cluster kernel, or split-K
+# partials summed by the SwiGLU reduce kernel where the cluster plan does not balance;
+# (37, 96, 256) the cluster kernel, (300, 768, 512) stream-K
 @pytest.mark.parametrize("M,I,K", [(4, 3072, 1024), (128, 1536, 4096), (37, 96, 256), (300, 768, 512),
                                    (128, 12288, 1024), (5, 12288, 256), (96, 6144, 512)])
 def test_gate_up_silu(cuda, oracle, M, I, K):
