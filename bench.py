@@ -550,7 +550,7 @@ def run_ours(args, rank, world, local_rank):
     ws = torch.zeros(wsn, dtype=torch.uint8, device=dev)
     pt_d, seq_d = sb.tensors["page_table"], sb.tensors["seq_lens"]
 
-    cascade = hkv >= 2  # the executor's rule (engine/layers.h, Attention::forward)
+    cascade = hkv % 4 == 0  # the executor's rule (engine/layers.h, Attention::forward)
     if not cascade:
         ws = ops.attention_workspace(BATCH, CTX, hq, hkv, dev)
 

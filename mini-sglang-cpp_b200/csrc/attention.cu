@@ -1237,10 +1237,11 @@ DecodePlan plan_decode(int B, int max_seq_len, int hq, int hkv) {
     const long long rows = static_cast<long long>(std::max(1, B)) * n_hg;
     int chunks = static_cast<int>(std::min<long long>((slots + rows - 1) / rows, 1 << 20));
     chunks = std::max(1, std::min(chunks, (max_pages_seq + 15) / 16));
-    // One kv head per CTA: CTAs are short and their own rate (not HBM) bounds them, so a last wave
-    // filled below half costs a whole CTA's time for little work; one chunk fewer keeps one wave
-    // (measured at a TP8 rank of the 8B decode, 128 requests: 3 chunks = 1.3 waves).
-    if (decode_heads_per_cta(hkv) == 1 && chunks > 1) {
+    // One or two kv heads per CTA: CTAs are short and their own rate (not HBM) bounds them, so a
+    // last wave filled below half costs a whole CTA's time for little work; one chunk fewer keeps
+    // one wave (128 requests x 2048 at a TP8 / TP4 rank of the 8B decode: 3 chunks = 1.3 waves;
+    // 25.3 -> 18.0 us at one kv head, 39.0 -> 30.0 us at two).
+    if (decode_heads_per_cta(hkv) <= 2 && chunks > 1) {
         const long long tail = (rows * chunks) % slots;
         if (tail != 0 && tail * 2 < slots && rows * (chunks - 1) * 2 >= slots) --chunks;
     }

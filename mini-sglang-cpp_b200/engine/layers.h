@@ -190,11 +190,12 @@ class Attention {
                  const msgl_batch& b, bf16_t* out, const Scratch& ws, cudaStream_t s) const {
         const float scale = 1.0f / sqrtf(static_cast<float>(head_dim_));  // layer.cpp:212
         // decode over a prefix that every request shares (radix-cache hit): the cascade kernel
-        // attends the shared pages once per kv head for the whole batch. With one kv head (a
-        // rank of wide tensor parallelism) the plain kernel is faster (measured at 128 x 2048
-        // with a 1024-token prefix: 25 us plain, 42 us cascade), so it is used there.
+        // attends the shared pages once per kv head for the whole batch -- when a CTA holds four
+        // kv heads. With one or two (ranks of wide tensor parallelism) the plain kernel is faster
+        // (128 x 2048 with a 1024-token prefix: 18.0 vs 21.9 us at one kv head, 30.0 vs 32.9 us
+        // at two).
         const int sp = b.shared_prefix_pages;
-        if (b.is_decode && b.num_reqs >= 2 && hkv_ >= 2 && sp >= kMinCascadePages && sp <= b.max_pages &&
+        if (b.is_decode && b.num_reqs >= 2 && hkv_ % 4 == 0 && sp >= kMinCascadePages && sp <= b.max_pages &&
             sp * 16 <= b.max_seq_len &&
             msgl_paged_attention_cascade_workspace_size(b.num_reqs, b.max_seq_len, sp, hq_, hkv_,
                                                         head_dim_) <= ws.attn_ws_bytes)
