@@ -161,14 +161,15 @@ def test_cascade_decode_step_matches_plain(cuda):
     whole-model bf16 tolerance, same greedy tokens where the margin is clear."""
     from msgl import ops
     from msgl.model import Qwen3Model, device_view, make_step, shared_prefix_pages
-    w = weights(CFG, 3)
-    model = Qwen3Model(CFG, max_tokens=64, max_reqs=8)
+    cfg = dict(CFG, num_kv_heads=4)  # the executor takes the cascade with 4 kv heads per CTA
+    w = weights(cfg, 3)
+    model = Qwen3Model(cfg, max_tokens=64, max_reqs=8)
     model.set_weights(w)
     num_pages = 40
     model.alloc_kv(num_pages)
-    for l in range(CFG["num_layers"]):  # a KV cache with content in every slot
+    for l in range(cfg["num_layers"]):  # a KV cache with content in every slot
         kp, vp, n = model.kv_pool(l)
-        width = CFG["num_kv_heads"] * CFG["head_dim"]
+        width = cfg["num_kv_heads"] * cfg["head_dim"]
         ops.fill_normal_(device_view(kp, (n, width), torch.bfloat16), seed=100 + l)
         ops.fill_normal_(device_view(vp, (n, width), torch.bfloat16), seed=200 + l)
     rng = np.random.default_rng(7)
@@ -184,7 +185,7 @@ def test_cascade_decode_step_matches_plain(cuda):
     seq = np.array([(S + n - 1) * 16 + int(rng.integers(1, 17)) for n in own], np.int32)
     pos = seq - 1
     slots = np.array([pt[r, p // 16] * 16 + p % 16 for r, p in enumerate(pos)], np.int32)
-    host = dict(input_ids=rng.integers(0, CFG["vocab"], B).astype(np.int32), positions=pos,
+    host = dict(input_ids=rng.integers(0, cfg["vocab"], B).astype(np.int32), positions=pos,
                 slot_mapping=slots, page_table=pt, seq_lens=seq,
                 q_indptr=np.arange(B + 1, dtype=np.int32), last_idx=np.arange(B, dtype=np.int32))
     assert shared_prefix_pages(pt, seq) == S
