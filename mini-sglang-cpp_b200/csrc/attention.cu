@@ -516,23 +516,24 @@ paged_extend_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
 // query tile, kv head, request); the rows are (128 / group) query tokens x the group's heads,
 // token-major, so one UMMA of M = 128 covers every query head of the kv head. Keys go in blocks
 // of 128 (8 pages):
-//   warp 0   TMA producer: per block 8 pages x 2 dim halves of K into a 2-stage K ring and of V
-//            into a 2-stage V ring (2-D boxes of 16 rows x 64 dims, SWIZZLE_128B): a block's tiles
+//   warp 0   TMA producer: per block 8 pages x 2 dim halves of K into a 3-stage K ring and of V
+//            into a 3-stage V ring (2-D boxes of 16 rows x 64 dims, SWIZZLE_128B): a block's tiles
 //            are [128 keys][64] halves, the canonical K-major layout for S = Q K^T and MN-major
 //            for O += P V. A K stage is released when its S MMA completes, a V stage when its
 //            P V MMA completes, so the next block's K lands while the softmax still works;
 //   warp 1   MMA issuer (one lane): S(j+1) = Q K^T into the other of two TMEM S buffers while
-//            the softmax works on S(j), then O += P(j) V(j) into TMEM with P from shared memory
-//            (K-major, two P buffers: the softmax writes P(j+1) while P(j) V(j) runs) and V as
-//            an MN-major B operand;
+//            the softmax works on S(j), then O += P(j) V(j) into TMEM with P read from tensor
+//            memory (bf16 pairs written over S(j)'s first 64 columns) and V as an MN-major B
+//            operand; a K stage is released after its S MMA, a V stage and the S buffer after
+//            the P V MMA;
 //   warps 2-9 softmax / epilogue: a pair of warps per TMEM lane quarter (warp % 4), each thread of
 //            the pair one query row and one half of the 128 keys (and of O's 128 columns): the
 //            row's Q half into shared memory once; per block its 64 S columns into registers
-//            (one TMEM load; the S buffer is released once both halves are out), the row max
-//            (the two halves meet through shared memory and a named barrier per pair),
-//            p = exp2(s - m) as bf16 into its half of the P tile, its part of the running sum,
+//            (one TMEM load), the row max (the two halves meet through shared memory and a named
+//            barrier per pair), p = exp2(s - m) as bf16 pairs into TMEM over its S buffer, its part
+//            of the running sum,
 //            and O *= exp2(m_old - m_new) on its 64 columns; at the end O / l to global.
-// TMEM: S buffers at columns [0, 128) and [128, 256), O at [256, 384) (512 allocated).
+// TMEM: S / P buffers at columns [0, 128) and [128, 256), O at [256, 384) (512 allocated).
 // The online softmax is the reference's (layer.cpp:226-257: scale 1/sqrt(D), max subtraction,
 // fp32 accumulation) evaluated per block; causal masking by position L - q_len + i.
 constexpr int kTcRows = 128;
@@ -540,9 +541,9 @@ constexpr int kTcKeys = 128;
 constexpr int kTcPages = kTcKeys / kPage;  // 8
 constexpr int kTcHalf = kTcRows * 128;     // 16 KB: 128 rows x 64 bf16
 constexpr int kTcTile = 2 * kTcHalf;       // 32 KB: 128 x 128 bf16
-constexpr int kTcStages = 2;
+constexpr int kTcStages = 3;
 constexpr int kTcThreads = 10 * 32;  // producer, MMA, 8 softmax warps
-constexpr size_t kTcSmem = 1024 + (3 + 2 * kTcStages) * kTcTile + 256 + 1024;  // Q, P x 2, K x 2, V x 2, barriers, max exchange
+constexpr size_t kTcSmem = 1024 + (1 + 2 * kTcStages) * kTcTile + 256 + 1024;  // Q, K x 3, V x 3, barriers, max exchange
 
 __global__ void __launch_bounds__(kTcThreads, 1)
 paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
@@ -553,23 +554,22 @@ paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = align1024(smem_raw);
     uint8_t* sQ = smem;                                // [2 halves][128 rows][64], SW128
-    uint8_t* sP = smem + kTcTile;                      // [2 blocks][2 halves][128 rows][64 keys]
-    uint8_t* sK = smem + 3 * kTcTile;                  // [kTcStages] tiles
+    uint8_t* sK = smem + kTcTile;                      // [kTcStages] tiles
     uint8_t* sV = sK + kTcStages * kTcTile;            // [kTcStages] tiles
     uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kTcStages * kTcTile);
     uint64_t* q_full = bars;
-    uint64_t* k_full = bars + 1;    // [2]
-    uint64_t* k_empty = bars + 3;   // [2]
-    uint64_t* v_full = bars + 5;    // [2]
-    uint64_t* v_empty = bars + 7;   // [2]
-    uint64_t* s_full = bars + 9;    // [2]
-    uint64_t* s_free = bars + 11;   // [2]
+    uint64_t* k_full = bars + 1;                     // [kTcStages]
+    uint64_t* k_empty = k_full + kTcStages;          // [kTcStages]
+    uint64_t* v_full = k_empty + kTcStages;          // [kTcStages]
+    uint64_t* v_empty = v_full + kTcStages;          // [kTcStages]
     // one barrier per block parity for every hand-off, so that no waiter can find its barrier
     // two phases ahead of the phase it waits for
-    uint64_t* p_full = bars + 13;   // [2]
-    uint64_t* o_ready = bars + 15;  // [2]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
-    float* red = reinterpret_cast<float*>(bars + 18);  // [2 halves][128 rows]
+    uint64_t* s_full = v_empty + kTcStages;          // [2]
+    uint64_t* s_free = s_full + 2;                   // [2]
+    uint64_t* p_full = s_free + 2;                   // [2]
+    uint64_t* o_ready = p_full + 2;                  // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_ready + 2);
+    float* red = reinterpret_cast<float*>(o_ready + 3);  // [2 halves][128 rows]
 
     const int b = blockIdx.z, kvh = blockIdx.y;
     const int group = hq / hkv;
@@ -582,10 +582,10 @@ paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
             mbar_init(&k_empty[st], 1);
             mbar_init(&v_full[st], 1);
             mbar_init(&v_empty[st], 1);
-            mbar_init(&s_full[st], 1);
-            mbar_init(&s_free[st], 8);
         }
         for (int i = 0; i < 2; ++i) {
+            mbar_init(&s_full[i], 1);
+            mbar_init(&s_free[i], 1);
             mbar_init(&p_full[i], 8);
             mbar_init(&o_ready[i], 1);
         }
@@ -678,7 +678,7 @@ paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
             constexpr uint32_t idS = umma_idesc_bf16(kTcRows, kTcKeys);
             constexpr uint32_t idO = umma_idesc_bf16_bmn(kTcRows, kHd);
             const uint32_t tO = tmem + 256;
-            const uint32_t aQ = smem_u32(sQ), aP = smem_u32(sP);
+            const uint32_t aQ = smem_u32(sQ);
             // S(j) = Q K(j)^T into S buffer j % 2 (the caller checked that the buffer is free)
             auto issue_s = [&](int j) -> bool {
                 const int st = j % kTcStages;
@@ -704,14 +704,14 @@ paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
                 if (!mbar_wait(&v_full[st], (j / kTcStages) & 1, err, 255)) break;
                 if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, err, 256)) break;
                 tc_fence_after();
-                const uint32_t aV = smem_u32(sV + st * kTcTile), aPj = aP + (j & 1) * kTcTile;
+                const uint32_t aV = smem_u32(sV + st * kTcTile), tP = tmem + (j & 1) * 128;
 #pragma unroll
-                for (int k = 0; k < 8; ++k)  // 16 keys per UMMA: P K-major, V MN-major
-                    umma_bf16(tO, umma_desc_sw128(aPj + (k >> 2) * kTcHalf + (k & 3) * 32),
-                              umma_desc_sw128_mn(aV + k * 2048, kTcHalf, 1024), idO,
-                              (j > 0 || k > 0) ? 1u : 0u);
+                for (int k = 0; k < 8; ++k)  // 16 keys per UMMA: P from TMEM (8 columns), V MN-major
+                    umma_bf16_ta(tO, tP + k * 8, umma_desc_sw128_mn(aV + k * 2048, kTcHalf, 1024), idO,
+                                 (j > 0 || k > 0) ? 1u : 0u);
                 umma_commit(&o_ready[j & 1]);
                 umma_commit(&v_empty[st]);
+                umma_commit(&s_free[j & 1]);  // P(j) read: its S buffer may take S(j + 2)
             }
         }
         __syncwarp();
@@ -751,9 +751,6 @@ paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
                 tc_fence_after();
                 tmem_ld64(row_t + (j & 1) * 128 + ch * 64, sv);
                 tmem_ld_wait();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&s_free[j & 1]);  // this half of S(j) is in registers
                 float mx8[8];
 #pragma unroll
                 for (int i = 0; i < 8; ++i) mx8[i] = kNegInf;
@@ -777,28 +774,21 @@ paged_extend_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
             const float m_new = (m == kNegInf || mx > m + 8.f) ? fmaxf(m, mx) : m;
             const float base = m_new == kNegInf ? 0.f : m_new;
             const float alpha = m == kNegInf ? 0.f : exp2f(m - m_new);
-            if (j >= 2) {  // P(j - 2) V(j - 2) has landed: this block's P buffer is free
-                ok = __all_sync(0xffffffffu, mbar_wait(&o_ready[j & 1], ((j - 2) >> 1) & 1, err, 258));
-                if (!ok) continue;
-                tc_fence_after();
-            }
-            uint8_t* sPj = sP + (j & 1) * kTcTile + ch * kTcHalf + r * 128;
+            // P(j) as bf16 pairs into the first 64 columns of S(j)'s TMEM buffer (both halves of
+            // S(j) are in registers: the pair barriers above came after both loads)
             float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+            uint32_t pk[32];
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {  // 8 keys per 16-byte chunk of this half of the P row
-                uint32_t pk[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float p0 = exp2f(__uint_as_float(sv[8 * c + 2 * e]) - base);
-                    const float p1 = exp2f(__uint_as_float(sv[8 * c + 2 * e + 1]) - base);
-                    sum4[e] += p0 + p1;
-                    pk[e] = pack_bf16x2(p0, p1);
-                }
-                *reinterpret_cast<uint4*>(sPj + ((c ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            for (int e = 0; e < 32; ++e) {
+                const float p0 = exp2f(__uint_as_float(sv[2 * e]) - base);
+                const float p1 = exp2f(__uint_as_float(sv[2 * e + 1]) - base);
+                sum4[e & 3] += p0 + p1;
+                pk[e] = pack_bf16x2(p0, p1);
             }
+            tmem_st32(row_t + (j & 1) * 128 + ch * 32, pk);
+            tmem_st_wait();
             l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
             m = m_new;
-            fence_proxy_async();  // the P tile, read by the tensor cores
             if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
                 // O *= alpha once P(j - 1) V(j - 1) has landed (and before P(j) V(j) is issued)
                 ok = __all_sync(0xffffffffu, mbar_wait(&o_ready[(j - 1) & 1], ((j - 1) >> 1) & 1, err, 258));
