@@ -1344,7 +1344,9 @@ def run_c4(rig):
                   "traffic": None, "algorithmic_flops_per_launch": flops, "launch_ms": g_ms,
                   "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained"
                                  if "bf16_tflops_sustained" in peaks else "fallback",
-                  "extend_attention": {"kernel": "paged_extend_kernel", "launch_ms": e_ms,
+                  "extend_attention": {"kernel": "paged_extend_kernel"
+                                       if os.environ.get("MSGL_EXTEND_TC", "1")[:1] == "0"
+                                       else "paged_extend_tc_kernel", "launch_ms": e_ms,
                                        "tflops": e_flops / (e_ms * 1e-3) / 1e12,
                                        "frac_of_sustained": e_flops / (e_ms * 1e-3) / 1e12 / tpeak}},
         cpu_baseline={"value": cpu_val, "unit": UNIT, "cores": cpu.threads, "kind": "reference",

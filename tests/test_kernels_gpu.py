@@ -332,6 +332,8 @@ def test_decode_equals_extend_single_token(cuda):
     (128, 1000, 200), (200, 512, 4096), (300, 640, 576), (96, 4096, 12288),
     # row-range schedule: 148 tiles of 176 rows; 136 tiles of 192 rows, the last one partial
     (77, 26048, 320), (128, 26088, 256),
+    # 129..256 tokens: two passes of the decode schedules (Qwen3-30B-A3B qkv / router at b256)
+    (256, 5120, 2048), (256, 128, 2048), (129, 4096, 4096),
 ])
 def test_gemm_bf16(cuda, M, N, K):
     from msgl import ops
@@ -354,8 +356,8 @@ def test_gemm_workspace_shared_across_shapes(cuda):
     stream-K, whose flags share the workspace's zero-filled head; every result stays correct."""
     from msgl import ops
     rng = np.random.default_rng(12)
-    shapes = [(128, 6144, 4096), (128, 4096, 4096), (200, 512, 4096), (128, 4096, 12288),
-              (4, 1000, 512)]
+    shapes = [(128, 6144, 4096), (128, 4096, 4096), (200, 512, 4096), (300, 512, 4096),
+              (128, 4096, 12288), (4, 1000, 512)]
     ws = torch.zeros(max(ops.gemm_workspace(*s).numel() for s in shapes), dtype=torch.uint8,
                      device="cuda")
     data = [(rn(rng, M, K), rn(rng, N, K, std=0.02)) for M, N, K in shapes]
@@ -401,9 +403,11 @@ def test_gemm_matches_oracle_linear(cuda, oracle):
 # 176-row tiles per CTA); (4, 3072, 1024), (128, 1536, 4096) (a TP8 rank of Qwen3-8B) and
 # (96, 6144, 512): small gate_up (2I x K <= 16M elements) on the cluster kernel, or split-K
 # partials summed by the SwiGLU reduce kernel where the cluster plan does not balance;
-# (37, 96, 256) the cluster kernel, (300, 768, 512) stream-K
+# (37, 96, 256) the cluster kernel, (300, 768, 512) stream-K, (256, 768, 2048) two passes of
+# 128 tokens
 @pytest.mark.parametrize("M,I,K", [(4, 3072, 1024), (128, 1536, 4096), (37, 96, 256), (300, 768, 512),
-                                   (128, 12288, 1024), (5, 12288, 256), (96, 6144, 512)])
+                                   (128, 12288, 1024), (5, 12288, 256), (96, 6144, 512),
+                                   (256, 768, 2048)])
 def test_gate_up_silu(cuda, oracle, M, I, K):
     from msgl import ops
     rng = np.random.default_rng(M + I)
@@ -416,7 +420,8 @@ def test_gate_up_silu(cuda, oracle, M, I, K):
 
 
 @pytest.mark.parametrize("M,V,K", [(4, 1024, 256), (64, 151936, 1024), (130, 4096, 512),
-                                   (128, 37984, 512), (128, 18992, 512)])  # TP4 / TP8 shards
+                                   (128, 37984, 512), (128, 18992, 512),  # TP4 / TP8 shards
+                                   (256, 37984, 1024)])
 def test_lm_head_argmax(cuda, oracle, M, V, K):
     from msgl import ops
     rng = np.random.default_rng(M + V)
