@@ -270,7 +270,8 @@ MSGL_API int msgl_gemm_gate_up_silu(const void* x, const void* w_packed, void* y
 /* Linear::forward (layer.cpp:122-143) as split-K partials for decode-sized batches whose next
  * kernel adds them (msgl_add_partials_rmsnorm, msgl_qknorm_rope_store_kv_partials):
  * parts[s][M][N] (fp32) = x[:, Ks] W[:, Ks]^T over the s-th of `splits` equal k-block ranges, so
- * that sum_s parts[s] = x W^T. No cross-CTA reduction, no workspace. 1 <= M <= 128,
+ * that sum_s parts[s] = x W^T. No cross-CTA reduction, no workspace. 1 <= M <= 256 (tokens
+ * in tiles of 128),
  * 1 <= splits <= min(64, ceil(K / 64)); msgl_gemm_partials_splits gives the split count that
  * fills the GPU in one wave (0 for unsupported sizes). */
 MSGL_API int msgl_gemm_partials_splits(int M, int N, int K);
@@ -291,6 +292,11 @@ MSGL_API int msgl_lm_head_argmax(const void* x, const void* w, int M, int vocab,
 MSGL_API int msgl_moe_route_topk(const float* router_logits, int num_tokens, int num_experts,
                                  int top_k, int norm_topk, int* topk_ids, float* topk_weights,
                                  msgl_stream_t stream);
+/* The same on the router GEMM's split-K partials (msgl_gemm_bf16_partials, [nparts][T][E] fp32),
+ * summed in part order before the selection; 1 <= nparts <= 64. */
+MSGL_API int msgl_moe_route_topk_partials(const float* router_parts, int nparts, int num_tokens,
+                                          int num_experts, int top_k, int norm_topk,
+                                          int* topk_ids, float* topk_weights, msgl_stream_t stream);
 
 /* Counting sort of the num_tokens * top_k (token, k) pairs by expert, stable in pair order:
  * expert_offsets [E+1] (rows of each expert in the sorted matrix), sorted_token [T*k] (token of

@@ -11,7 +11,8 @@
 //   gemm_part_kernel   M <= 128: split-K fp32 partials (tokens as M, 256 weight rows as N), summed
 //                      by the next kernel or by partials_reduce_kernel
 //   gemm_cl_kernel     M <= 128 otherwise: cluster split-K, partials exchanged over DSMEM
-//   (129..256 tokens run as two passes of the schedules above, 128 tokens and the rest)
+//   (129..256 tokens: the partials + reduce over both token tiles; else two passes of the
+//   schedules above, 128 tokens and the rest)
 //   gemm_sk_kernel     stream-K (prefill-sized M; 128 weight rows as M, up to 256 tokens as N)
 //   gemm_kernel        one CTA per tile (very large grids) and the grouped MoE GEMM
 // Epilogues: bf16 store, fp32 store, SwiGLU (gate/up rows interleaved in 16-row groups by
@@ -895,14 +896,16 @@ gemm_cl_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
 }
 
 // ============================================================================ split-K partials
-// Decode-sized GEMMs (M <= 128 tokens) whose consumer can take the K-split reduction over. The
+// Decode-sized GEMMs (M <= 256 tokens) whose consumer can take the K-split reduction over. The
 // operands are swapped relative to the other kernels: the tokens are the UMMA M dimension (128,
 // rows past M zero-filled by TMA) and 256 weight rows the N dimension, so a ring stage holds a
 // 16 KB token tile and a 32 KB weight tile -- 1.5 bytes staged per weight byte instead of 2,
 // which is what bounds a decode GEMM when every SM streams weights (per-SM TMA ingest).
-// CTA blockIdx.x = tile * S + s accumulates k-blocks [s KB / S, (s + 1) KB / S) of weight rows
-// [256 tile, 256 tile + 256) in TMEM (lane = token, column = weight row) and stores the fp32
-// partial into parts[s][M][N]. No CTA waits for another; the next kernel on the stream (fused
+// CTA (blockIdx.x = tile * S + s, blockIdx.y = token tile) accumulates k-blocks
+// [s KB / S, (s + 1) KB / S) of weight rows [256 tile, 256 tile + 256) for tokens
+// [128 y, 128 y + 128) in TMEM (lane = token, column = weight row) and stores the fp32 partial
+// into parts[s][M][N]; the two token tiles of a 256-token step read each weight tile at about the
+// same time, the second mostly from L2. No CTA waits for another; the next kernel on the stream (fused
 // add + RMSNorm, QK-norm + RoPE) adds the S partials in split order (deterministic). Producer
 // warp, MMA warp, 8 epilogue warps as in the stream-K kernel.
 constexpr int kPartBN = 256;                        // weight rows per tile (UMMA N)
@@ -933,6 +936,8 @@ gemm_part_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
     const int KB = (K + kBK - 1) / kBK;
     const int kb0 = sp * KB / S, kb1 = (sp + 1) * KB / S;  // S <= KB: never empty
     const int wrow = tile * kPartBN;
+    const int m0 = blockIdx.y * kBM;          // this CTA's 128-token tile
+    const int Mt = min(kBM, M - m0);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < ST; ++s) {
@@ -972,7 +977,7 @@ gemm_part_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
                     mbar_arrive_expect_tx(&full[s], kPartStage);
                     tma_load_2d_hint(sW + s * kPartTileW, &tmap_w, &full[s], kb * kBK, wrow, pol_w);
                 }
-                tma_load_2d_hint(sX + s * kPartTileX, &tmap_x, &full[s], kb * kBK, 0, pol_x);
+                tma_load_2d_hint(sX + s * kPartTileX, &tmap_x, &full[s], kb * kBK, m0, pol_x);
             }
         } else {
             pdl_wait();
@@ -1012,7 +1017,7 @@ gemm_part_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
         const bool have = mbar_wait(tfull, 0, err, 472);
         tc_fence_after();
         float* stage = reinterpret_cast<float*>(smem);  // the ring is drained once tfull fired
-        if (warp_q * 32 < M) {  // warp-uniform: quarters past the last token load nothing
+        if (warp_q * 32 < Mt) {  // warp-uniform: quarters past the last token load nothing
             const uint32_t taddr = tmem + (static_cast<uint32_t>(warp_q * 32) << 16);
             float4* srow = reinterpret_cast<float4*>(stage + (warp_q * 32 + lane) * kPartPitch);
 #pragma unroll 1
@@ -1034,9 +1039,9 @@ gemm_part_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
         tc_fence_before();
         named_bar(1, kEpiThreads);
         const bool vec = (N & 3) == 0 && wrow + kPartBN <= N;
-        for (int m = ew; m < M; m += kSkEpiWarps) {
+        for (int m = ew; m < Mt; m += kSkEpiWarps) {
             const float* src = stage + m * kPartPitch;
-            float* dst = parts + (static_cast<int64_t>(sp) * M + m) * N + wrow;
+            float* dst = parts + (static_cast<int64_t>(sp) * M + m0 + m) * N + wrow;
 #pragma unroll
             for (int c = lane * 4; c < kPartBN; c += 128) {
                 const float4 v = *reinterpret_cast<const float4*>(src + c);
@@ -1588,8 +1593,9 @@ int launch_part_reduce(const void* x, const void* w, void* y, int M, int N, int 
 
 // Split count of the partials kernel: as many splits as keep one tile-split per SM in a single
 // wave, at least 4 k-blocks per split, at most 16 partials for the consumer to add.
-int part_splits(int N, int K) {
-    const int T = (N + kPartBN - 1) / kPartBN, KB = (K + kBK - 1) / kBK, sms = num_sms();
+int part_splits(int M, int N, int K) {
+    const int MT = std::max(1, (M + kBM - 1) / kBM);
+    const int T = (N + kPartBN - 1) / kPartBN * MT, KB = (K + kBK - 1) / kBK, sms = num_sms();
     if (T >= sms) return 1;
     return std::max(1, std::min({sms / T, std::max(1, KB / 4), 16}));
 }
@@ -1601,8 +1607,8 @@ int launch_part(const CUtensorMap& tw, const CUtensorMap& tx, float* parts, int 
     cudaFuncSetAttribute(gemm_part_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(kPartSmem));
     const int T = (N + kPartBN - 1) / kPartBN;
-    launch_pdl(gemm_part_kernel, dim3(T * S), dim3(kSkThreads), kPartSmem, stream, tw, tx, parts,
-               M, N, K, S, err);
+    launch_pdl(gemm_part_kernel, dim3(T * S, (M + kBM - 1) / kBM), dim3(kSkThreads), kPartSmem,
+               stream, tw, tx, parts, M, N, K, S, err);
     MSGL_LAUNCH_CHECK();
     return MSGL_OK;
 }
@@ -1651,16 +1657,19 @@ int launch_rows(const void* x, const void* w, void* y, unsigned long long* amax,
 }
 
 size_t part_reduce_bytes(int M, int N, int K) {
-    const int S = part_splits(N, K);
-    if (S < 2 || M > 256) return 0;
-    M = std::min(M, 128);  // 129..256 tokens run as two passes of at most 128
-    return kCounterBytes + static_cast<size_t>(S) * M * N * sizeof(float);
+    if (M > 256) return 0;
+    // 129..256 tokens: one pass over both token tiles, or (fewer than 2 splits) two passes of 128
+    const int S = part_splits(M, N, K), S1 = part_splits(std::min(M, 128), N, K);
+    size_t b = 0;
+    if (S >= 2) b = static_cast<size_t>(S) * M * N * sizeof(float);
+    if (S1 >= 2) b = std::max(b, static_cast<size_t>(S1) * std::min(M, 128) * N * sizeof(float));
+    return b ? kCounterBytes + b : 0;
 }
 
 template <int EPI>
 int launch_part_reduce(const void* x, const void* w, void* y, int M, int N, int K, void* ws,
                        size_t ws_bytes, cudaStream_t stream) {
-    const int S = part_splits(N, K);
+    const int S = part_splits(M, N, K);
     if (S < 2 || (EPI == EPI_SWIGLU && N % 16) || !ws || (reinterpret_cast<uintptr_t>(ws) & 15) ||
         ws_bytes < kCounterBytes + static_cast<size_t>(S) * M * N * sizeof(float))
         return -1;
@@ -1687,13 +1696,22 @@ int run_gemm(const void* x, const void* w, void* y, unsigned long long* amax, in
     if (K % 8) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "gemm: K must be a multiple of 8");
     if (M == 0) return MSGL_OK;
     if (M > 65535 * 256) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "gemm: M too large");
+    if (M > 128 && M <= 256 && decode_schedule() == 0 && !rows_disabled()) {
+        // 129..256 tokens (a large decode batch): split-K partials over both 128-token tiles in
+        // one grid, summed by the reduce kernel (the partials kernel alone, measured on B200 at
+        // 256 tokens, against stream-K: 5120 x 2048 10.0 vs 25.1 us, 6144 x 4096 15.3 vs 27.7,
+        // 4096 x 12288 26.3 vs 41.3)
+        if (EPI != EPI_ARGMAX) {
+            const int r = launch_part_reduce<EPI>(x, w, y, M, N, K, ws, ws_bytes, stream);
+            if (r != -1) return r;
+        }
+    }
     if (M > 128 && M <= 256 && decode_schedule() == 0 && !rows_disabled() &&
         (EPI == EPI_ARGMAX || static_cast<int64_t>(N) * K * 2 < (int64_t(40) << 20))) {
-        // 129..256 tokens (a large decode batch): two passes of the decode-sized schedules over
-        // tokens [0, 128) and [128, M); the second pass reads weights under 40 MB from L2.
-        // Measured on B200 at 256 tokens against stream-K: 5120 x 2048 23.9 vs 25.1 us,
-        // 2048 x 4096 21.6 vs 32.9, 128 x 2048 (fp32) 15.6 vs 28.8, lm_head + argmax
-        // 151936 x 2048 199 vs 338; from 6144 x 4096 (50 MB) on stream-K is faster (27.8 vs 30.8).
+        // otherwise (argmax, which needs whole rows, or fewer than 2 splits): two passes of the
+        // decode-sized schedules over tokens [0, 128) and [128, M), the second reading weights
+        // under 40 MB from L2 (lm_head + argmax 151936 x 2048 at 256 tokens: 199 us vs 338 on
+        // stream-K; from 50 MB up stream-K is faster for the other epilogues)
         int rc = run_gemm<EPI>(x, w, y, amax, 128, N, K, ws, ws_bytes, stream, id_off);
         if (rc) return rc;
         const auto* x2 = static_cast<const __nv_bfloat16*>(x) + static_cast<int64_t>(128) * K;
@@ -1932,15 +1950,15 @@ int msgl_gemm_gate_up_silu(const void* x, const void* w_packed, void* y, int M, 
 }
 
 int msgl_gemm_partials_splits(int M, int N, int K) {
-    if (M <= 0 || M > 128 || N <= 0 || K <= 0) return 0;
-    return part_splits(N, K);
+    if (M <= 0 || M > 256 || N <= 0 || K <= 0) return 0;
+    return part_splits(M, N, K);
 }
 
 int msgl_gemm_bf16_partials(const void* x, const void* w, float* parts, int M, int N, int K,
                             int splits, msgl_stream_t stream) {
     if (M < 0 || N <= 0 || K <= 0 || !x || !w || !parts)
         return set_error(MSGL_ERR_INVALID_ARG, "gemm_partials: bad arguments");
-    if (M > 128) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "gemm_partials: M must be <= 128");
+    if (M > 256) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "gemm_partials: M must be <= 256");
     if (K % 8) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "gemm_partials: K must be a multiple of 8");
     const int KB = (K + kBK - 1) / kBK;
     if (splits < 1 || splits > KB || splits > 64)

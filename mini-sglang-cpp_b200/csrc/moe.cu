@@ -2,7 +2,7 @@
 //
 //  * msgl_moe_route_topk   MoERouter::route top-k and weights (src/layer/layer.cpp:283-305)
 //                          on fp32 router logits (the logits GEMM is msgl_gemm_bf16 with an
-//                          fp32 output): descending logit, equal logits -> larger expert id
+//                          fp32 output, or its split-K partials summed here in part order): descending logit, equal logits -> larger expert id
 //                          first (std::greater on pair<float,int>), w = exp(l), divided by the
 //                          top-k sum when norm_topk.
 //  * msgl_moe_permute      counting sort of the (token, k) pairs by expert, stable in pair
@@ -24,20 +24,29 @@ __device__ __forceinline__ bool key_greater(float va, int ia, float vb, int ib) 
 // One warp per token; E <= 32 * kMaxPerLane experts, top_k <= 32.
 constexpr int kMaxPerLane = 8;
 
-__global__ void route_topk_kernel(const float* __restrict__ logits, int T, int E, int top_k,
-                                  int norm_topk, int* __restrict__ ids, float* __restrict__ w) {
+// The logits are the sum of `nparts` fp32 split-K partials [nparts][T][E], added in part order
+// (nparts = 1: plain logits).
+__global__ void route_topk_kernel(const float* __restrict__ logits, int nparts, int T, int E,
+                                  int top_k, int norm_topk, int* __restrict__ ids,
+                                  float* __restrict__ w) {
     pdl_wait();
     pdl_trigger();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (warp >= T) return;
     const float* row = logits + static_cast<int64_t>(warp) * E;
+    const int64_t pstride = static_cast<int64_t>(T) * E;
     float v[kMaxPerLane];
     bool taken[kMaxPerLane];
 #pragma unroll
     for (int i = 0; i < kMaxPerLane; ++i) {
         int e = lane + 32 * i;
-        v[i] = e < E ? row[e] : -__builtin_huge_valf();
+        float x = -__builtin_huge_valf();
+        if (e < E) {
+            x = row[e];
+            for (int pp = 1; pp < nparts; ++pp) x += row[pp * pstride + e];
+        }
+        v[i] = x;
         taken[i] = e >= E;
     }
     float sel_v = 0.f, first_v = 0.f;
@@ -184,18 +193,26 @@ using namespace msgl;
 
 extern "C" {
 
-int msgl_moe_route_topk(const float* router_logits, int num_tokens, int num_experts, int top_k,
-                        int norm_topk, int* topk_ids, float* topk_weights, msgl_stream_t stream) {
+int msgl_moe_route_topk_partials(const float* router_parts, int nparts, int num_tokens,
+                                 int num_experts, int top_k, int norm_topk, int* topk_ids,
+                                 float* topk_weights, msgl_stream_t stream) {
     if (num_tokens < 0 || num_experts <= 0 || num_experts > 32 * kMaxPerLane || top_k <= 0 ||
         top_k > 32 || top_k > num_experts)
         return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "moe_route_topk: E <= 256, top_k <= min(32, E)");
+    if (nparts < 1 || nparts > 64) return set_error(MSGL_ERR_INVALID_ARG, "moe_route_topk: nparts in [1, 64]");
     if (num_tokens == 0) return MSGL_OK;
     const int threads = 256;
     const int blocks = (num_tokens * 32 + threads - 1) / threads;
-    launch_pdl(route_topk_kernel, dim3(blocks), dim3(threads), 0, stream, router_logits,
+    launch_pdl(route_topk_kernel, dim3(blocks), dim3(threads), 0, stream, router_parts, nparts,
                num_tokens, num_experts, top_k, norm_topk, topk_ids, topk_weights);
     MSGL_LAUNCH_CHECK();
     return MSGL_OK;
+}
+
+int msgl_moe_route_topk(const float* router_logits, int num_tokens, int num_experts, int top_k,
+                        int norm_topk, int* topk_ids, float* topk_weights, msgl_stream_t stream) {
+    return msgl_moe_route_topk_partials(router_logits, 1, num_tokens, num_experts, top_k,
+                                        norm_topk, topk_ids, topk_weights, stream);
 }
 
 int msgl_moe_permute(const int* topk_ids, int num_tokens, int top_k, int num_experts,

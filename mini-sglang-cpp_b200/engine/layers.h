@@ -113,6 +113,8 @@ class Linear {  // layer.h:36-48; y = x W^T, W [out, in]
     // Decode-sized batches whose next kernel adds the K split: fp32 partials [S][T][out];
     // returns S (0: not available for this size, use forward).
     int partial_splits(int num_tokens) const { return msgl_gemm_partials_splits(num_tokens, out_, in_); }
+    // partials apply at this step size (up to 256 tokens: two 128-token tiles)
+    bool partials_fit(int num_tokens) const { return num_tokens <= 256; }
     int forward_partials(const bf16_t* x, float* parts, int num_tokens, cudaStream_t s) const {
         const int S = partial_splits(num_tokens);
         ck(msgl_gemm_bf16_partials(x, weight.p, parts, num_tokens, out_, in_, S, s),
@@ -248,7 +250,7 @@ class Attention {
 // (src/model/qwen3_moe.cpp:62-111): router logits GEMM (fp32 out) -> top-k -> stable
 // permutation by expert -> gather -> grouped gate_up+SwiGLU -> grouped down -> weighted combine.
 struct MoEScratch {
-    float* logits = nullptr;      // [T, E]
+    float* logits = nullptr;      // [T, E], or the router's split-K partials [S, T, E]
     int* topk_ids = nullptr;      // [T, k]
     float* topk_w = nullptr;      // [T, k]
     int* offsets = nullptr;       // [E + 1]
@@ -259,6 +261,7 @@ struct MoEScratch {
     bf16_t* ys = nullptr;         // [T k, H]
     void* grouped_ws = nullptr;
     size_t grouped_ws_bytes = 0;
+    size_t logits_floats = 0;     // capacity of `logits`
 };
 
 class MoEExperts {
@@ -269,10 +272,22 @@ class MoEExperts {
     // x [T, H] (post-attention normed) -> out [T, H] (may alias x: x is consumed first)
     void forward(const bf16_t* x, bf16_t* out, int T, const MoEScratch& ms, const Scratch& ws,
                  cudaStream_t s) const {
-        ck(msgl_gemm_bf16(x, router.p, ms.logits, T, E_, hidden_, MSGL_F32, ws.gemm_ws,
-                          ws.gemm_ws_bytes, s), "MoERouter logits");
-        ck(msgl_moe_route_topk(ms.logits, T, E_, k_, norm_topk_ ? 1 : 0, ms.topk_ids, ms.topk_w, s),
-           "MoERouter::route");
+        // router logits (layer.cpp:273-280): as split-K partials summed by the top-k kernel when
+        // the step has <= 256 tokens and the scratch holds them, else one fp32 GEMM
+        const int S = router_splits(T);
+        if (S >= 2 && static_cast<size_t>(S) * T * E_ <= ms.logits_floats) {
+            ck(msgl_gemm_bf16_partials(x, router.p, ms.logits, T, E_, hidden_, S, s),
+               "MoERouter logits (partials)");
+            ck(msgl_moe_route_topk_partials(ms.logits, S, T, E_, k_, norm_topk_ ? 1 : 0,
+                                            ms.topk_ids, ms.topk_w, s),
+               "MoERouter::route");
+        } else {
+            ck(msgl_gemm_bf16(x, router.p, ms.logits, T, E_, hidden_, MSGL_F32, ws.gemm_ws,
+                              ws.gemm_ws_bytes, s), "MoERouter logits");
+            ck(msgl_moe_route_topk(ms.logits, T, E_, k_, norm_topk_ ? 1 : 0, ms.topk_ids,
+                                   ms.topk_w, s),
+               "MoERouter::route");
+        }
         ck(msgl_moe_permute(ms.topk_ids, T, k_, E_, ms.offsets, ms.sorted_token, ms.pair_pos, s),
            "moe permute");
         ck(msgl_launch_index_gather(x, ms.sorted_token, ms.xs, hidden_, T * k_, T, MSGL_BF16, s),
@@ -288,6 +303,8 @@ class MoEExperts {
     DevBuf router;          // bf16 [E, H]
     DevBuf gate_up_packed;  // bf16 [E, 2 inter, H], each expert packed by msgl_pack_gate_up
     DevBuf down;            // bf16 [E, H, inter]
+    // split-K partials of the router logits GEMM for a T-token step (0: one fp32 GEMM instead)
+    int router_splits(int T) const { return msgl_gemm_partials_splits(T, E_, hidden_); }
     int num_experts() const { return E_; }
     int top_k() const { return k_; }
     int inter() const { return inter_; }

@@ -216,12 +216,15 @@ static void create(Model& m, const msgl_model_config& c) {
     m.attn_ws.alloc(std::max<size_t>(aws, 256));
     ckc(cudaMemset(m.attn_ws.p, 0, m.attn_ws.bytes), "attention workspace");
     m.scratch = Scratch{m.gemm_ws.p, m.gemm_ws.bytes, m.attn_ws.p, m.attn_ws.bytes};
-    // split-K partials (steps of <= 128 tokens; MSGL_SPLITK_PARTIALS=0 turns the path off)
+    // split-K partials (steps of <= 256 tokens; MSGL_SPLITK_PARTIALS=0 turns the path off)
     const char* env_parts = std::getenv("MSGL_SPLITK_PARTIALS");
     if (!(env_parts && env_parts[0] == '0')) {
-        const int tm = static_cast<int>(std::min<size_t>(T, 128));
         auto need = [&](const Linear& l) {
-            return static_cast<size_t>(l.partial_splits(tm)) * tm * l.out_features() * sizeof(float);
+            size_t n = 0;
+            for (int tm : {static_cast<int>(std::min<size_t>(T, 128)), static_cast<int>(std::min<size_t>(T, 256))})
+                if (l.partials_fit(tm))
+                    n = std::max(n, static_cast<size_t>(l.partial_splits(tm)) * tm * l.out_features() * sizeof(float));
+            return n;
         };
         size_t pb = need(L0.qkv_proj);
         if (tp == 1) {
@@ -232,7 +235,11 @@ static void create(Model& m, const msgl_model_config& c) {
     }
     if (c.num_experts > 0) {
         const size_t E = c.num_experts, k = c.top_k, R = T * k;
-        m.moe_logits.alloc(T * E * 4);
+        // router logits, or their split-K partials for steps of <= 256 tokens
+        size_t lf = T * E;
+        for (int t = 1; t <= static_cast<int>(std::min<size_t>(T, 256)); ++t)
+            lf = std::max(lf, static_cast<size_t>(std::max(0, m.layers[0].moe.router_splits(t))) * t * E);
+        m.moe_logits.alloc(lf * 4);
         m.moe_ids.alloc(T * k * 4);
         m.moe_w.alloc(T * k * 4);
         m.moe_off.alloc((E + 1) * 4);
@@ -248,7 +255,7 @@ static void create(Model& m, const msgl_model_config& c) {
         m.moe_scratch = MoEScratch{m.moe_logits.as<float>(), m.moe_ids.as<int>(), m.moe_w.as<float>(),
                                    m.moe_off.as<int>(), m.moe_tok.as<int>(), m.moe_pos.as<int>(),
                                    m.moe_xs.as<bf16_t>(), m.moe_act.as<bf16_t>(), m.moe_ys.as<bf16_t>(),
-                                   m.moe_ws.p, m.moe_ws.bytes};
+                                   m.moe_ws.p, m.moe_ws.bytes, lf};
     }
     m.st_max_pages = (c.max_position + 15) / 16;
     for (auto& x : m.st) {
@@ -437,11 +444,12 @@ static void forward(Model& m, const msgl_batch& b, int* next_tokens, float* logi
     // (o_proj uses slot 0, down_proj slot 1: consecutive all-reduces alternate slots)
     bf16_t* part_o = m.tp ? m.tp_part[0] : x;
     bf16_t* part_d = m.tp ? m.tp_part[1] : x;
-    // Steps of <= 128 tokens: qkv, o_proj and (dense, tensor parallel size 1) down_proj write
+    // Steps of <= 256 tokens: qkv, o_proj and (dense, tensor parallel size 1) down_proj write
     // fp32 split-K partials that the next kernel adds, instead of reducing the K split across
-    // CTAs inside the GEMM. `pend` = splits of down_proj partials the next norm has to add.
+    // CTAs inside the GEMM. `pend` = splits of down_proj partials
+    // the next norm has to add.
     float* parts = m.parts.as<float>();
-    const bool use_parts = parts != nullptr && T <= 128;
+    auto use_parts = [&](const Linear& l) { return parts != nullptr && l.partials_fit(T); };
     int pend = 0;
     for (int l = 0; l < nl; ++l) {
         auto& L = m.layers[l];
@@ -452,7 +460,7 @@ static void forward(Model& m, const msgl_batch& b, int* next_tokens, float* logi
                 L.input_layernorm.forward_fused_add(x, res, T, false, s);
             pend = 0;
         }
-        if (use_parts) {  // :22, :28-48
+        if (use_parts(L.qkv_proj)) {  // :22, :28-48
             const int S = L.qkv_proj.forward_partials(x, parts, T, s);
             L.attn.prepare_partials(parts, S, m.q.as<bf16_t>(), L.k_pool.p, L.v_pool.p,
                                     m.num_slots, b.positions, b.slot_mapping, m.rope, L.q_norm.p,
@@ -468,7 +476,7 @@ static void forward(Model& m, const msgl_batch& b, int* next_tokens, float* logi
         if (m.tp) {  // row-parallel o_proj (:55): all-reduce fused with the add + norm of :57
             L.o_proj.forward(m.attn_out.as<bf16_t>(), part_o, T, m.scratch, s);
             allreduce_norm(part_o, L.post_attention_layernorm.weight.p, "o_proj all-reduce");
-        } else if (use_parts) {
+        } else if (use_parts(L.o_proj)) {
             const int S = L.o_proj.forward_partials(m.attn_out.as<bf16_t>(), parts, T, s);
             L.post_attention_layernorm.forward_fused_add_partials(parts, S, x, res, T, s);
         } else {
@@ -480,7 +488,7 @@ static void forward(Model& m, const msgl_batch& b, int* next_tokens, float* logi
         } else {
             L.gate_up_proj.forward(x, m.act.as<bf16_t>(), T, m.scratch, s);  // :60-79
             // (the last layer's down_proj writes x, the hidden state msgl_model_hidden reads)
-            if (use_parts && !m.tp && l + 1 < nl)                             // :80
+            if (use_parts(L.down_proj) && !m.tp && l + 1 < nl)               // :80
                 pend = L.down_proj.forward_partials(m.act.as<bf16_t>(), parts, T, s);
             else
                 L.down_proj.forward(m.act.as<bf16_t>(), part_d, T, m.scratch, s);

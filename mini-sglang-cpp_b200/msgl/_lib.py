@@ -46,6 +46,7 @@ SIGNATURES = {
     "msgl_argmax": (I, [P, I, I, I, P, P]),
     "msgl_fill_normal_bf16": (I, [P, I64, U64, U64, F, F, P]),
     "msgl_moe_route_topk": (I, [P, I, I, I, I, P, P, P]),
+    "msgl_moe_route_topk_partials": (I, [P, I, I, I, I, I, P, P, P]),
     "msgl_moe_permute": (I, [P, I, I, I, P, P, P, P]),
     "msgl_grouped_gemm_workspace_size": (SZ, [I, I]),
     "msgl_grouped_gemm_bf16": (I, [P, P, P, P, I, I, I, I, P, SZ, P]),

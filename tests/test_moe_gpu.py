@@ -81,6 +81,38 @@ def test_router_logits_gemm_then_topk(cuda, oracle):
     assert np.array_equal(host(ids)[clear], eid[clear])
 
 
+@pytest.mark.parametrize("T,H,E,k", [(256, 2048, 128, 8), (200, 2048, 128, 8), (64, 512, 60, 4)])
+def test_route_topk_partials(cuda, oracle, T, H, E, k):
+    """Router logits as split-K partials summed by the top-k kernel in part order: the same ids
+    and weights as the top-k of the partials' in-order fp32 sum (bit-exact), and the oracle's ids
+    where the logit margin is clear."""
+    import msgl
+    from msgl import ops
+    rng = np.random.default_rng(T + E)
+    x, wr = rn(rng, T, H), rn(rng, E, H, std=0.02)
+    S = ops.gemm_partials_splits(T, E, H)
+    assert S >= 2
+    parts = ops.linear_partials(dev(x), dev(wr), S)
+    summed = parts[0].clone()
+    for p in range(1, S):
+        summed += parts[p]
+    ids_ref, w_ref = route(summed, k)
+    ids = torch.empty(T, k, dtype=torch.int32, device="cuda")
+    w = torch.empty(T, k, dtype=torch.float32, device="cuda")
+    msgl.check(msgl.lib().msgl_moe_route_topk_partials(
+        parts.data_ptr(), S, T, E, k, 1, ids.data_ptr(), w.data_ptr(),
+        torch.cuda.current_stream().cuda_stream))
+    assert np.array_equal(host(ids), host(ids_ref))
+    assert np.array_equal(host(w), host(w_ref))
+    ref = oracle.linear(x, wr)
+    eid, _ = oracle.router_topk(ref, k)
+    srt = -np.sort(-ref, axis=1)
+    margin = np.minimum(srt[:, k - 1] - srt[:, k], np.min(-np.diff(srt[:, :k], axis=1), axis=1))
+    clear = margin > 4 * np.abs(host(summed) - ref).max()
+    assert clear.mean() > 0.5
+    assert np.array_equal(host(ids)[clear], eid[clear])
+
+
 @pytest.mark.parametrize("T,E,k", [(3, 8, 2), (256, 128, 8), (4096, 128, 8)])
 def test_permute(cuda, T, E, k):
     rng = np.random.default_rng(T)

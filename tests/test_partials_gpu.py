@@ -49,6 +49,8 @@ def split_sum(parts):
     (1, 128, 64, 1), (7, 256, 128, 2), (16, 384, 1024, None), (100, 1000, 200, 3),
     (128, 6144, 4096, None), (128, 4096, 12288, None), (64, 4096, 4096, 5), (128, 768, 4096, 16),
     (33, 200, 1000, 16),
+    # 129..256 tokens: a second 128-token tile in the grid (the last one partly filled)
+    (256, 5120, 2048, None), (200, 2048, 4096, None), (129, 128, 2048, 4), (256, 1000, 200, 3),
 ])
 def test_gemm_partials(cuda, M, N, K, S):
     from msgl import ops
@@ -73,16 +75,16 @@ def test_gemm_partials(cuda, M, N, K, S):
 
 def test_gemm_partials_rejects_bad_sizes(cuda):
     from msgl import lib, ops
-    x = torch.zeros(200, 256, dtype=torch.bfloat16, device="cuda")
+    x = torch.zeros(300, 256, dtype=torch.bfloat16, device="cuda")
     w = torch.zeros(128, 256, dtype=torch.bfloat16, device="cuda")
-    out = torch.zeros(8, 200, 128, dtype=torch.float32, device="cuda")
+    out = torch.zeros(8, 300, 128, dtype=torch.float32, device="cuda")
     L = lib()
     p = lambda t: t.data_ptr()
-    assert L.msgl_gemm_bf16_partials(p(x), p(w), p(out), 200, 128, 256, 1, None) == ERR_UNSUPPORTED_SHAPE
+    assert L.msgl_gemm_bf16_partials(p(x), p(w), p(out), 300, 128, 256, 1, None) == ERR_UNSUPPORTED_SHAPE
     assert L.msgl_gemm_bf16_partials(p(x), p(w), p(out), 16, 128, 256, 5, None) == ERR_INVALID_ARG
     assert L.msgl_gemm_bf16_partials(p(x), p(w), p(out), 16, 128, 256, 0, None) == ERR_INVALID_ARG
     assert L.msgl_gemm_bf16_partials(p(x), p(w), p(out), 0, 128, 256, 2, None) == 0
-    assert L.msgl_gemm_partials_splits(200, 128, 256) == 0
+    assert L.msgl_gemm_partials_splits(300, 128, 256) == 0
     torch.cuda.synchronize()
     assert ops.device_error() == (0, 0)
 
