@@ -322,7 +322,7 @@ MSGL_API int msgl_grouped_gemm_gate_up_silu(const void* x_sorted, const void* w_
                                             size_t workspace_bytes, msgl_stream_t stream);
 
 /* out[t] = sum_j topk_weights[t,j] * y_sorted[pair_pos[t*k+j]], j in order, fp32 accumulation
- * (qwen3_moe.cpp:102-106). out [T, hidden] bf16. */
+ * (qwen3_moe.cpp:102-106). out [T, hidden] bf16; hidden % 8 == 0, top_k <= 32. */
 MSGL_API int msgl_moe_combine(const void* y_sorted, const int* pair_pos, const float* topk_weights,
                               int num_tokens, int top_k, int hidden, void* out,
                               msgl_stream_t stream);

@@ -41,13 +41,24 @@ __global__ void route_topk_kernel(const float* __restrict__ logits, int nparts, 
 #pragma unroll
     for (int i = 0; i < kMaxPerLane; ++i) {
         int e = lane + 32 * i;
-        float x = -__builtin_huge_valf();
-        if (e < E) {
-            x = row[e];
-            for (int pp = 1; pp < nparts; ++pp) x += row[pp * pstride + e];
-        }
-        v[i] = x;
+        v[i] = e < E ? row[e] : -__builtin_huge_valf();
         taken[i] = e >= E;
+    }
+    // further partials, added in part order; four parts' loads in flight at a time
+    for (int pp = 1; pp < nparts; pp += 4) {
+        float t[4][kMaxPerLane];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int i = 0; i < kMaxPerLane; ++i) {
+                const int e = lane + 32 * i;
+                t[u][i] = (pp + u < nparts && e < E) ? row[(pp + u) * pstride + e] : 0.f;
+            }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int i = 0; i < kMaxPerLane; ++i)
+                if (pp + u < nparts && lane + 32 * i < E) v[i] += t[u][i];
     }
     float sel_v = 0.f, first_v = 0.f;
     int sel_i = 0;
@@ -160,19 +171,29 @@ permute_kernel(const int* __restrict__ ids, int num_pairs, int top_k, int E,
     }
 }
 
-// One CTA per token: out[t, h] = sum_k w[t, k] * y[pair_pos[t k + k], h] (k in order).
+// One CTA per token: out[t, h] = sum_k w[t, k] * y[pair_pos[t k + k], h] (k in order). The
+// token's k (row, weight) pairs are staged in shared memory first, so each thread's k row loads
+// are independent and go out together.
 __global__ void combine_kernel(const __nv_bfloat16* __restrict__ y, const int* __restrict__ pair_pos,
                                const float* __restrict__ w, int top_k, int hidden,
                                __nv_bfloat16* __restrict__ out) {
+    __shared__ int s_pos[32];
+    __shared__ float s_w[32];
     pdl_wait();
     pdl_trigger();
     const int t = blockIdx.x;
+    if (threadIdx.x < top_k) {
+        s_pos[threadIdx.x] = pair_pos[static_cast<int64_t>(t) * top_k + threadIdx.x];
+        s_w[threadIdx.x] = w[static_cast<int64_t>(t) * top_k + threadIdx.x];
+    }
+    __syncthreads();
     for (int h8 = threadIdx.x; h8 * 8 < hidden; h8 += blockDim.x) {
         float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll 8
         for (int k = 0; k < top_k; ++k) {
-            int pos = pair_pos[static_cast<int64_t>(t) * top_k + k];
+            const int pos = s_pos[k];
             if (pos < 0) continue;
-            float wk = w[static_cast<int64_t>(t) * top_k + k];
+            const float wk = s_w[k];
             uint4 u = *reinterpret_cast<const uint4*>(y + static_cast<int64_t>(pos) * hidden + h8 * 8);
             acc[0] += wk * bf16lo(u.x); acc[1] += wk * bf16hi(u.x);
             acc[2] += wk * bf16lo(u.y); acc[3] += wk * bf16hi(u.y);
@@ -232,8 +253,8 @@ int msgl_moe_permute(const int* topk_ids, int num_tokens, int top_k, int num_exp
 
 int msgl_moe_combine(const void* y_sorted, const int* pair_pos, const float* topk_weights,
                      int num_tokens, int top_k, int hidden, void* out, msgl_stream_t stream) {
-    if (num_tokens < 0 || top_k <= 0 || hidden <= 0 || hidden % 8)
-        return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "moe_combine: hidden % 8");
+    if (num_tokens < 0 || top_k <= 0 || top_k > 32 || hidden <= 0 || hidden % 8)
+        return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "moe_combine: hidden % 8, top_k <= 32");
     if (num_tokens == 0) return MSGL_OK;
     launch_pdl(combine_kernel, dim3(num_tokens), dim3(128), 0, stream,
                static_cast<const __nv_bfloat16*>(y_sorted), pair_pos, topk_weights, top_k, hidden,

@@ -275,6 +275,15 @@ __global__ void index_gather_kernel(const T* __restrict__ in, const int* __restr
     bool valid = id >= 0 && id < num_rows;
     const T* src = in + static_cast<int64_t>(valid ? id : 0) * hidden;
     T* dst = out + static_cast<int64_t>(i) * hidden;
+    if ((hidden * sizeof(T)) % 16 == 0 && (reinterpret_cast<uintptr_t>(in) & 15) == 0 &&
+        (reinterpret_cast<uintptr_t>(out) & 15) == 0) {  // 16-byte rows: one uint4 per thread
+        const int n16 = static_cast<int>(hidden * sizeof(T) / 16);
+        const uint4* s4 = reinterpret_cast<const uint4*>(src);
+        uint4* d4 = reinterpret_cast<uint4*>(dst);
+        for (int h = threadIdx.x; h < n16; h += blockDim.x)
+            d4[h] = valid ? s4[h] : make_uint4(0u, 0u, 0u, 0u);
+        return;
+    }
     for (int h = threadIdx.x; h < hidden; h += blockDim.x) dst[h] = valid ? src[h] : T(0.0f);
 }
 
