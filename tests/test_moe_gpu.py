@@ -128,7 +128,8 @@ def test_permute(cuda, T, E, k):
     assert np.array_equal(host(pos), inv)
 
 
-@pytest.mark.parametrize("T,E,k,H,I", [(16, 8, 2, 256, 96), (256, 128, 8, 2048, 768), (2048, 32, 4, 512, 256)])
+@pytest.mark.parametrize("T,E,k,H,I", [(16, 8, 2, 256, 96), (256, 128, 8, 2048, 768), (2048, 32, 4, 512, 256),
+                                       (2048, 64, 8, 512, 256)])  # the last: 256-row tiles
 def test_expert_block(cuda, oracle, T, E, k, H, I):
     """permute -> gather -> grouped gate_up+SwiGLU -> grouped down -> combine, vs the reference
     expert loop (qwen3_moe.cpp:74-108) restated in the oracle."""
