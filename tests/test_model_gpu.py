@@ -316,3 +316,21 @@ def test_mixed_batch_decode_tail(cuda, oracle):
     assert rel_l2(outs[0], outs[1]) < 2e-2
     from msgl import ops
     assert ops.device_error() == (0, 0)
+
+
+@pytest.mark.parametrize("moe", [False, True])
+def test_decode_batch_over_128_requests(cuda, oracle, moe):
+    """200 decode requests in one step: qkv / o_proj / down (dense) and the MoE router run as
+    split-K partials over two 128-token tiles, added by the following kernel; prefill and three
+    decode steps vs the oracle."""
+    from msgl.model import Qwen3Model, Request
+    cfg = MOE_CFG if moe else CFG
+    w = moe_weights(cfg, 8) if moe else weights(cfg, 8)
+    B, pages = 200, 200 * 2 + 8
+    model = Qwen3Model(cfg, max_tokens=4096, max_reqs=B)
+    model.set_weights(w)
+    model.alloc_kv(pages)
+    orc = OracleModel(oracle, cfg, w, num_slots=pages * 16)
+    rng = np.random.default_rng(12)
+    reqs = [Request(list(rng.integers(0, cfg["vocab"], int(n)))) for n in rng.integers(1, 14, B)]
+    _run_steps(model, orc, reqs, 4, pages, max_pages=2)
