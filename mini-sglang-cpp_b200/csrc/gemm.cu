@@ -1301,6 +1301,16 @@ int decode_schedule() {
     return v;
 }
 
+// K up to which decode GEMMs take narrow row tiles (no K split); MSGL_GEMM_SHORTK_ROWS=0 turns
+// that off (read on every call). Measured on B200 at 128 tokens against split-K partials +
+// reduce: 4096 x 512 4.9 vs 8.8 us, 4096 x 1024 7.2 vs 9.4, 4096 x 1536 9.6 vs 10.2; at
+// 4096 x 2048 the partials win (10.9 vs 11.8).
+constexpr int kRowsShortK = 1536;
+bool small_k_rows() {
+    const char* e = std::getenv("MSGL_GEMM_SHORTK_ROWS");
+    return !(e && e[0] == '0');
+}
+
 bool rows_disabled() {
     static const bool off = [] {
         const char* e = std::getenv("MSGL_GEMM_ROWS");
@@ -1618,12 +1628,12 @@ int launch_part(const CUtensorMap& tw, const CUtensorMap& tx, float* parts, int 
 // CTA (rounds x (16 KB token tile + 2 KB x hs weight tile) per k-block), among those that keep
 // the CTAs at least 85% evenly loaded; 0 when none does (the caller uses another schedule).
 // Below 6 groups the token tile would be most of what a stage brings in.
-int plan_rows(int N, int sms, int& tiles) {
+int plan_rows(int N, int sms, int& tiles, int min_hs = 6) {
     const int n = (N + 15) / 16;
     int best_hs = 0;
     int64_t best = -1;
     tiles = 0;
-    for (int hs = 6; hs <= 16; ++hs) {
+    for (int hs = min_hs; hs <= 16; ++hs) {
         const int T = (n + hs - 1) / hs;
         const int rounds = (T + sms - 1) / sms;
         if (static_cast<int64_t>(T) * 100 < static_cast<int64_t>(rounds) * sms * 85) continue;
@@ -1735,8 +1745,11 @@ int run_gemm(const void* x, const void* w, void* y, unsigned long long* amax, in
         // rows); row tiles of 6-9 groups only when the partials do not apply
         const int sms = num_sms();
         int tiles = 0;
-        const int hs = plan_rows(N, sms, tiles);
-        if (hs >= 10 && force != 2)
+        // short K (a wide tensor-parallel rank's row-parallel projection): narrow row tiles over
+        // the whole K in one launch beat split-K partials + reduce (two launches)
+        const bool short_k = K <= kRowsShortK && small_k_rows();
+        const int hs = plan_rows(N, sms, tiles, short_k ? 2 : 6);
+        if ((hs >= 10 || (short_k && hs > 0)) && force != 2)
             return launch_rows<EPI>(x, w, y, amax, M, N, K, hs, tiles, sms, stream, id_off);
         if (EPI != EPI_ARGMAX && force != 1) {
             const int r = launch_part_reduce<EPI>(x, w, y, M, N, K, ws, ws_bytes, stream);
