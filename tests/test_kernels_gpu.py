@@ -332,8 +332,11 @@ def test_decode_equals_extend_single_token(cuda):
     (128, 1000, 200), (200, 512, 4096), (300, 640, 576), (96, 4096, 12288),
     # row-range schedule: 148 tiles of 176 rows; 136 tiles of 192 rows, the last one partial
     (77, 26048, 320), (128, 26088, 256),
-    # 129..256 tokens: two passes of the decode schedules (Qwen3-30B-A3B qkv / router at b256)
+    # 129..256 tokens: split-K partials over both token tiles (Qwen3-30B-A3B qkv / router at
+    # b256), or two passes of 128
     (256, 5120, 2048), (256, 128, 2048), (129, 4096, 4096),
+    # short K (a TP8 / TP4 rank's o_proj, a TP8 rank's down): narrow row tiles over the whole K
+    (128, 4096, 512), (100, 4096, 1024), (128, 4096, 1536), (5, 4096, 512),
 ])
 def test_gemm_bf16(cuda, M, N, K):
     from msgl import ops
