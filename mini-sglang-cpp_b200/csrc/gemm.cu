@@ -919,7 +919,7 @@ static_assert(kBM * kPartPitch * 4 <= kPartStages * kPartStage, "staging tile ex
 
 __global__ void __launch_bounds__(kSkThreads, 1)
 gemm_part_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
-                 float* __restrict__ parts, int M, int N, int K, int S, int* err) {
+                 float* __restrict__ parts, int M, int N, int K, int S, int xbox, int* err) {
     constexpr int ST = kPartStages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -938,6 +938,9 @@ gemm_part_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
     const int wrow = tile * kPartBN;
     const int m0 = blockIdx.y * kBM;          // this CTA's 128-token tile
     const int Mt = min(kBM, M - m0);
+    // the token box holds xbox rows (M rounded up to 8 when M < 128): the tile's other rows are
+    // stale shared memory, whose MMA rows are never stored
+    const uint32_t stage_tx = kPartTileW + static_cast<uint32_t>(xbox) * kBK * 2;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < ST; ++s) {
@@ -965,7 +968,7 @@ gemm_part_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
             // weight tiles of the first ST stages before the dependency wait (see gemm_sk_kernel)
             const int npre = min(ST, kb1 - kb0);
             for (int i = 0; i < npre; ++i) {
-                mbar_arrive_expect_tx(&full[i], kPartStage);
+                mbar_arrive_expect_tx(&full[i], stage_tx);
                 tma_load_2d_hint(sW + i * kPartTileW, &tmap_w, &full[i], (kb0 + i) * kBK, wrow, pol_w);
             }
             pdl_wait();
@@ -974,7 +977,7 @@ gemm_part_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
                 const int s = i % ST;
                 if (i >= npre) {
                     if (!mbar_wait(&empty[s], ((i / ST) - 1) & 1, err, 470)) break;
-                    mbar_arrive_expect_tx(&full[s], kPartStage);
+                    mbar_arrive_expect_tx(&full[s], stage_tx);
                     tma_load_2d_hint(sW + s * kPartTileW, &tmap_w, &full[s], kb * kBK, wrow, pol_w);
                 }
                 tma_load_2d_hint(sX + s * kPartTileX, &tmap_x, &full[s], kb * kBK, m0, pol_x);
@@ -1090,7 +1093,7 @@ template <int EPI>
 __global__ void __launch_bounds__(kSkThreads, 1)
 gemm_rows_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                  void* __restrict__ y, unsigned long long* __restrict__ amax, int M, int N, int K,
-                 int BR, int id_off, int* err) {
+                 int BR, int xbox, int id_off, int* err) {
     constexpr int ST = kRowsStages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -1108,7 +1111,8 @@ gemm_rows_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
     const int KB = (K + kBK - 1) / kBK;
     const int G = gridDim.x;
     const int my_tiles = static_cast<int>(blockIdx.x) < T ? (T - blockIdx.x + G - 1) / G : 0;
-    const uint32_t stage_tx = kRowsTileX + static_cast<uint32_t>(BR) * kBK * 2;
+    // token box of xbox rows (M rounded up to 8): the tile's other rows are never stored
+    const uint32_t stage_tx = static_cast<uint32_t>(xbox + BR) * kBK * 2;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < ST; ++s) {
@@ -1603,6 +1607,12 @@ int launch_part_reduce(const void* x, const void* w, void* y, int M, int N, int 
 
 // Split count of the partials kernel: as many splits as keep one tile-split per SM in a single
 // wave, at least 4 k-blocks per split, at most 16 partials for the consumer to add.
+// Rows of the token box of the kernels that take tokens as the UMMA M dimension: M rounded up to
+// 8 below 128 tokens. The TMA then brings only those rows (out-of-range rows of a 128-row box
+// cost as much as real ones: lm_head + argmax over 151936 x 1024 took 80 us at 4 tokens against
+// 58 us at 64).
+int token_box(int M) { return M >= kBM ? kBM : std::max(8, (M + 7) & ~7); }
+
 int part_splits(int M, int N, int K) {
     const int MT = std::max(1, (M + kBM - 1) / kBM);
     const int T = (N + kPartBN - 1) / kPartBN * MT, KB = (K + kBK - 1) / kBK, sms = num_sms();
@@ -1610,6 +1620,7 @@ int part_splits(int M, int N, int K) {
     return std::max(1, std::min({sms / T, std::max(1, KB / 4), 16}));
 }
 
+// tx: the token tensor map with a box of token_box(M) rows (the kernel expects those bytes)
 int launch_part(const CUtensorMap& tw, const CUtensorMap& tx, float* parts, int M, int N, int K,
                 int S, cudaStream_t stream) {
     int* err = device_error_word();
@@ -1618,7 +1629,7 @@ int launch_part(const CUtensorMap& tw, const CUtensorMap& tx, float* parts, int 
                          static_cast<int>(kPartSmem));
     const int T = (N + kPartBN - 1) / kPartBN;
     launch_pdl(gemm_part_kernel, dim3(T * S, (M + kBM - 1) / kBM), dim3(kSkThreads), kPartSmem,
-               stream, tw, tx, parts, M, N, K, S, err);
+               stream, tw, tx, parts, M, N, K, S, token_box(M), err);
     MSGL_LAUNCH_CHECK();
     return MSGL_OK;
 }
@@ -1656,12 +1667,12 @@ int launch_rows(const void* x, const void* w, void* y, unsigned long long* amax,
     CUtensorMap tw, tx;
     int rc = make_tmap_2d_bf16(&tw, w, K, N, static_cast<uint64_t>(K) * 2, kBK, BR, true);
     if (rc) return rc;
-    rc = make_tmap_2d_bf16(&tx, x, K, M, static_cast<uint64_t>(K) * 2, kBK, kBM, true);
+    rc = make_tmap_2d_bf16(&tx, x, K, M, static_cast<uint64_t>(K) * 2, kBK, token_box(M), true);
     if (rc) return rc;
     cudaFuncSetAttribute(gemm_rows_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(kRowsSmem));
     launch_pdl(gemm_rows_kernel<EPI>, dim3(std::min(tiles, sms)), dim3(kSkThreads), kRowsSmem,
-               stream, tw, tx, y, amax, M, N, K, BR, id_off, err);
+               stream, tw, tx, y, amax, M, N, K, BR, token_box(M), id_off, err);
     MSGL_LAUNCH_CHECK();
     return MSGL_OK;
 }
@@ -1687,7 +1698,7 @@ int launch_part_reduce(const void* x, const void* w, void* y, int M, int N, int 
     CUtensorMap tw, tx;
     int rc = make_tmap_2d_bf16(&tw, w, K, N, static_cast<uint64_t>(K) * 2, kBK, kPartBN, true);
     if (rc) return rc;
-    rc = make_tmap_2d_bf16(&tx, x, K, M, static_cast<uint64_t>(K) * 2, kBK, kBM, true);
+    rc = make_tmap_2d_bf16(&tx, x, K, M, static_cast<uint64_t>(K) * 2, kBK, token_box(M), true);
     if (rc) return rc;
     rc = launch_part(tw, tx, parts, M, N, K, S, stream);
     if (rc) return rc;
@@ -1980,7 +1991,7 @@ int msgl_gemm_bf16_partials(const void* x, const void* w, float* parts, int M, i
     CUtensorMap tw, tx;
     int rc = make_tmap_2d_bf16(&tw, w, K, N, static_cast<uint64_t>(K) * 2, kBK, kPartBN, true);
     if (rc) return rc;
-    rc = make_tmap_2d_bf16(&tx, x, K, M, static_cast<uint64_t>(K) * 2, kBK, kBM, true);
+    rc = make_tmap_2d_bf16(&tx, x, K, M, static_cast<uint64_t>(K) * 2, kBK, token_box(M), true);
     if (rc) return rc;
     return launch_part(tw, tx, parts, M, N, K, splits, stream);
 }
