@@ -161,6 +161,87 @@ constexpr int kDecHalfStage = kDecHeads * 2 * 2048;          // 16 KB of K (or o
 constexpr int kDecStageBytes = 2 * kDecHalfStage;            // 32 KB: K then V
 constexpr int kDecStages = 3;                                // 96 KB ring: 2 CTAs per SM
 
+// Merge of split-KV partials by the 128 consumer threads of the last CTA to arrive: for each
+// (query head, 8-wide slice) item, O = sum_k exp2(m_k - M) O_k / sum_k exp2(m_k - M) l_k over the
+// `total` chunks k in order (M = max_k m_k; a chunk with m = -inf adds nothing). Partial k of
+// query head qh sits at index chunk_of(k) * hq + qh of ws_ml (pairs m, l) / ws_o (rows of 128).
+// Each thread takes two items at a time and issues a batch's loads (8 maxima, then 4 chunks of
+// l and O) before using any of them, so a merge costs a few L2 round trips, not one per chunk
+// and item; the sums keep the chunk order (same bits as a chunk-by-chunk loop).
+template <class ChunkBase>
+__device__ __forceinline__ void merge_partials(int total, int nq, int qh0, int hq,
+                                               ChunkBase chunk_base, const float* ws_o,
+                                               const float* ws_ml, __nv_bfloat16* out_row0) {
+    constexpr int kT = kDecWarps * 32;
+    const int nitems = nq * 16;
+    for (int base = threadIdx.x; base < nitems; base += 2 * kT) {
+        const int it[2] = {base, base + kT};
+        const bool live[2] = {it[0] < nitems, it[1] < nitems};
+        int64_t qoff[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) qoff[u] = qh0 + (live[u] ? (it[u] >> 4) : 0);
+        float M[2] = {kNegInf, kNegInf};
+        for (int k0 = 0; k0 < total; k0 += 8) {
+            float mv[2][8];
+#pragma unroll
+            for (int u = 0; u < 2; ++u)
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    mv[u][j] = (live[u] && k0 + j < total)
+                                   ? __ldcg(ws_ml + (chunk_base(k0 + j) * hq + qoff[u]) * 2)
+                                   : kNegInf;
+#pragma unroll
+            for (int u = 0; u < 2; ++u)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) M[u] = fmaxf(M[u], mv[u][j]);
+        }
+        float O[2][8], Ls[2] = {0.f, 0.f};
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) O[u][e] = 0.f;
+        for (int k0 = 0; k0 < total; k0 += 4) {
+            float mc[2][4], lc[2][4];
+            float4 x0[2][4], x1[2][4];
+#pragma unroll
+            for (int u = 0; u < 2; ++u)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const bool ok = live[u] && k0 + j < total;
+                    const int64_t pi = ok ? chunk_base(k0 + j) * hq + qoff[u] : 0;
+                    const int d0 = (it[u] & 15) * 8;
+                    mc[u][j] = ok ? __ldcg(ws_ml + pi * 2) : kNegInf;
+                    lc[u][j] = ok ? __ldcg(ws_ml + pi * 2 + 1) : 0.f;
+                    const float4* src = reinterpret_cast<const float4*>(ws_o + pi * kHd + d0);
+                    x0[u][j] = ok ? __ldcg(src) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    x1[u][j] = ok ? __ldcg(src + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+            for (int u = 0; u < 2; ++u)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    if (!(live[u] && k0 + j < total)) continue;
+                    const float sc = (mc[u][j] == kNegInf) ? 0.f : exp2f(mc[u][j] - M[u]);
+                    Ls[u] += lc[u][j] * sc;
+                    O[u][0] += x0[u][j].x * sc; O[u][1] += x0[u][j].y * sc;
+                    O[u][2] += x0[u][j].z * sc; O[u][3] += x0[u][j].w * sc;
+                    O[u][4] += x1[u][j].x * sc; O[u][5] += x1[u][j].y * sc;
+                    O[u][6] += x1[u][j].z * sc; O[u][7] += x1[u][j].w * sc;
+                }
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            if (!live[u]) continue;
+            const float inv = Ls[u] > 0.f ? 1.f / Ls[u] : 0.f;
+            float r[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) r[e] = O[u][e] * inv;
+            store_bf16x8(out_row0 + qoff[u] * kHd + (it[u] & 15) * 8, r);
+        }
+    }
+}
+
+
 __global__ void __launch_bounds__(kDecThreads, 2)
 paged_decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                     const __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ out,
@@ -348,27 +429,9 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
     named_bar_sync(1, kDecWarps * 32);
     if (!*flag) return;
     __threadfence();
-    for (int item = threadIdx.x; item < nq * 16; item += kDecWarps * 32) {
-        const int qh = qh0 + (item >> 4), d0 = (item & 15) * 8;
-        float M = kNegInf;
-        for (int ch = 0; ch < nchunks; ++ch)
-            M = fmaxf(M, __ldcg(ws_ml + ((static_cast<int64_t>(b) * max_chunks + ch) * hq + qh) * 2));
-        float O[8] = {0, 0, 0, 0, 0, 0, 0, 0}, Ls = 0.f;
-        for (int ch = 0; ch < nchunks; ++ch) {
-            const int64_t pi = (static_cast<int64_t>(b) * max_chunks + ch) * hq + qh;
-            const float mc = __ldcg(ws_ml + pi * 2);
-            const float sc = (mc == kNegInf) ? 0.f : exp2f(mc - M);
-            Ls += __ldcg(ws_ml + pi * 2 + 1) * sc;
-            const float4* src = reinterpret_cast<const float4*>(ws_o + pi * kHd + d0);
-            const float4 x0 = __ldcg(src), x1 = __ldcg(src + 1);
-            O[0] += x0.x * sc; O[1] += x0.y * sc; O[2] += x0.z * sc; O[3] += x0.w * sc;
-            O[4] += x1.x * sc; O[5] += x1.y * sc; O[6] += x1.z * sc; O[7] += x1.w * sc;
-        }
-        const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) O[e] *= inv;
-        store_bf16x8(out + (static_cast<int64_t>(b) * hq + qh) * kHd + d0, O);
-    }
+    const int64_t cbase = static_cast<int64_t>(b) * max_chunks;
+    merge_partials(nchunks, nq, qh0, hq, [cbase](int k) { return cbase + k; }, ws_o, ws_ml,
+                   out + static_cast<int64_t>(b) * hq * kHd);
     if (threadIdx.x == 0) *cnt = 0;
 }
 
@@ -870,32 +933,11 @@ constexpr int kPreRows = kDecWarps * 16;  // 64 rows per prefix CTA
 __device__ __forceinline__ void cascade_merge(int b, int hg, int nsfx, int hq, int nq,
                                               const CascadePlan& cp, const float* ws_o,
                                               const float* ws_ml, __nv_bfloat16* out) {
-    const int qh0 = hg * nq;
-    const int total = nsfx + cp.n_pchunks;
-    for (int item = threadIdx.x; item < nq * 16; item += kDecWarps * 32) {
-        const int qh = qh0 + (item >> 4), d0 = (item & 15) * 8;
-        float M = kNegInf;
-        for (int k = 0; k < total; ++k) {
-            const int ch = k < nsfx ? k : cp.chunks_sfx + (k - nsfx);
-            M = fmaxf(M, __ldcg(ws_ml + ((static_cast<int64_t>(b) * cp.max_chunks + ch) * hq + qh) * 2));
-        }
-        float O[8] = {0, 0, 0, 0, 0, 0, 0, 0}, Ls = 0.f;
-        for (int k = 0; k < total; ++k) {
-            const int ch = k < nsfx ? k : cp.chunks_sfx + (k - nsfx);
-            const int64_t pi = (static_cast<int64_t>(b) * cp.max_chunks + ch) * hq + qh;
-            const float mc = __ldcg(ws_ml + pi * 2);
-            const float sc = (mc == kNegInf) ? 0.f : exp2f(mc - M);
-            Ls += __ldcg(ws_ml + pi * 2 + 1) * sc;
-            const float4* src = reinterpret_cast<const float4*>(ws_o + pi * kHd + d0);
-            const float4 x0 = __ldcg(src), x1 = __ldcg(src + 1);
-            O[0] += x0.x * sc; O[1] += x0.y * sc; O[2] += x0.z * sc; O[3] += x0.w * sc;
-            O[4] += x1.x * sc; O[5] += x1.y * sc; O[6] += x1.z * sc; O[7] += x1.w * sc;
-        }
-        const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) O[e] *= inv;
-        store_bf16x8(out + (static_cast<int64_t>(b) * hq + qh) * kHd + d0, O);
-    }
+    const int64_t cbase = static_cast<int64_t>(b) * cp.max_chunks;
+    const int csfx = cp.chunks_sfx;
+    merge_partials(nsfx + cp.n_pchunks, nq, hg * nq, hq,
+                   [cbase, nsfx, csfx](int k) { return cbase + (k < nsfx ? k : csfx + (k - nsfx)); },
+                   ws_o, ws_ml, out + static_cast<int64_t>(b) * hq * kHd);
 }
 
 // suffix chunks of request b that have pages (the suffix CTAs that arrive)
