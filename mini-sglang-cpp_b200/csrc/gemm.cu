@@ -919,7 +919,8 @@ static_assert(kBM * kPartPitch * 4 <= kPartStages * kPartStage, "staging tile ex
 
 __global__ void __launch_bounds__(kSkThreads, 1)
 gemm_part_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
-                 float* __restrict__ parts, int M, int N, int K, int S, int xbox, int* err) {
+                 const __grid_constant__ CUtensorMap tmap_x2, float* __restrict__ parts, int M,
+                 int N, int K, int S, int xbox, int xbox2, int* err) {
     constexpr int ST = kPartStages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -938,9 +939,11 @@ gemm_part_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
     const int wrow = tile * kPartBN;
     const int m0 = blockIdx.y * kBM;          // this CTA's 128-token tile
     const int Mt = min(kBM, M - m0);
-    // the token box holds xbox rows (M rounded up to 8 when M < 128): the tile's other rows are
-    // stale shared memory, whose MMA rows are never stored
-    const uint32_t stage_tx = kPartTileW + static_cast<uint32_t>(xbox) * kBK * 2;
+    // the token box holds xbox rows (M rounded up to 8 when M < 128; the second token tile has
+    // its own map, xbox2 rows): the tile's other rows are stale shared memory, whose MMA rows
+    // are never stored
+    const CUtensorMap* tmx = blockIdx.y ? &tmap_x2 : &tmap_x;
+    const uint32_t stage_tx = kPartTileW + static_cast<uint32_t>(blockIdx.y ? xbox2 : xbox) * kBK * 2;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < ST; ++s) {
@@ -962,7 +965,7 @@ gemm_part_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
     if (warp == 0) {
         if (lane == 0) {
             tma_prefetch_desc(&tmap_w);
-            tma_prefetch_desc(&tmap_x);
+            tma_prefetch_desc(tmx);
             const uint64_t pol_w = policy_evict_first();
             const uint64_t pol_x = policy_evict_last();
             // weight tiles of the first ST stages before the dependency wait (see gemm_sk_kernel)
@@ -980,7 +983,7 @@ gemm_part_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
                     mbar_arrive_expect_tx(&full[s], stage_tx);
                     tma_load_2d_hint(sW + s * kPartTileW, &tmap_w, &full[s], kb * kBK, wrow, pol_w);
                 }
-                tma_load_2d_hint(sX + s * kPartTileX, &tmap_x, &full[s], kb * kBK, m0, pol_x);
+                tma_load_2d_hint(sX + s * kPartTileX, tmx, &full[s], kb * kBK, m0, pol_x);
             }
         } else {
             pdl_wait();
@@ -1620,16 +1623,24 @@ int part_splits(int M, int N, int K) {
     return std::max(1, std::min({sms / T, std::max(1, KB / 4), 16}));
 }
 
-// tx: the token tensor map with a box of token_box(M) rows (the kernel expects those bytes)
-int launch_part(const CUtensorMap& tw, const CUtensorMap& tx, float* parts, int M, int N, int K,
-                int S, cudaStream_t stream) {
+// Token maps: tokens [0, 128) with a box of token_box(M) rows, and (M > 128) tokens [128, M)
+// with a box of token_box(M - 128) rows -- the byte counts the kernel expects.
+int launch_part(const void* x, const CUtensorMap& tw, float* parts, int M, int N, int K, int S,
+                cudaStream_t stream) {
     int* err = device_error_word();
     if (!err) return set_error(MSGL_ERR_CUDA, "device error word unavailable");
+    CUtensorMap tx, tx2;
+    const int xbox = token_box(std::min(M, kBM));
+    const int xbox2 = M > kBM ? token_box(M - kBM) : xbox;
+    int rc = make_tmap_2d_bf16(&tx, x, K, M, static_cast<uint64_t>(K) * 2, kBK, xbox, true);
+    if (rc) return rc;
+    rc = make_tmap_2d_bf16(&tx2, x, K, M, static_cast<uint64_t>(K) * 2, kBK, xbox2, true);
+    if (rc) return rc;
     cudaFuncSetAttribute(gemm_part_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(kPartSmem));
     const int T = (N + kPartBN - 1) / kPartBN;
     launch_pdl(gemm_part_kernel, dim3(T * S, (M + kBM - 1) / kBM), dim3(kSkThreads), kPartSmem,
-               stream, tw, tx, parts, M, N, K, S, token_box(M), err);
+               stream, tw, tx, tx2, parts, M, N, K, S, xbox, xbox2, err);
     MSGL_LAUNCH_CHECK();
     return MSGL_OK;
 }
@@ -1695,12 +1706,10 @@ int launch_part_reduce(const void* x, const void* w, void* y, int M, int N, int 
         ws_bytes < kCounterBytes + static_cast<size_t>(S) * M * N * sizeof(float))
         return -1;
     float* parts = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kCounterBytes);
-    CUtensorMap tw, tx;
+    CUtensorMap tw;
     int rc = make_tmap_2d_bf16(&tw, w, K, N, static_cast<uint64_t>(K) * 2, kBK, kPartBN, true);
     if (rc) return rc;
-    rc = make_tmap_2d_bf16(&tx, x, K, M, static_cast<uint64_t>(K) * 2, kBK, token_box(M), true);
-    if (rc) return rc;
-    rc = launch_part(tw, tx, parts, M, N, K, S, stream);
+    rc = launch_part(x, tw, parts, M, N, K, S, stream);
     if (rc) return rc;
     const int64_t work = EPI == EPI_SWIGLU ? static_cast<int64_t>(M) * (N / 16)
                                            : static_cast<int64_t>(M) * ((N & 3) == 0 ? N / 4 : N);
@@ -1988,12 +1997,10 @@ int msgl_gemm_bf16_partials(const void* x, const void* w, float* parts, int M, i
     if (splits < 1 || splits > KB || splits > 64)
         return set_error(MSGL_ERR_INVALID_ARG, "gemm_partials: splits must be in [1, min(64, K / 64)]");
     if (M == 0) return MSGL_OK;
-    CUtensorMap tw, tx;
+    CUtensorMap tw;
     int rc = make_tmap_2d_bf16(&tw, w, K, N, static_cast<uint64_t>(K) * 2, kBK, kPartBN, true);
     if (rc) return rc;
-    rc = make_tmap_2d_bf16(&tx, x, K, M, static_cast<uint64_t>(K) * 2, kBK, token_box(M), true);
-    if (rc) return rc;
-    return launch_part(tw, tx, parts, M, N, K, splits, stream);
+    return launch_part(x, tw, parts, M, N, K, splits, stream);
 }
 
 size_t msgl_grouped_gemm_workspace_size(int max_rows, int num_experts) {
