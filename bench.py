@@ -640,7 +640,10 @@ def run_case(args):
     prefix), 128 requests x 2048 context (shared 1024 prefix);
     `gemm`: the gate_up + SwiGLU projection of one layer at 128 tokens (201 MB of weights);
     `gemm_qkv`: the qkv projection at 128 tokens; `gemm_partials`: o_proj at 128 tokens as
-    split-K partials; `gemm_prefill`: gate_up + SwiGLU at 2048 tokens."""
+    split-K partials; `gemm_prefill`: gate_up + SwiGLU at 2048 tokens; `attention_ragged`: the
+    plain decode of the Qwen3-0.6B ragged step (64 requests, contexts U[512, 4096], permuted
+    pages, 16 q / 8 kv heads, ~0.6 GB of KV); `moe_gate_up`: the Qwen3-30B-A3B experts' grouped
+    gate_up + SwiGLU at 256 decode tokens x top-8 (128 experts x 1536 x 2048, 0.8 GB)."""
     import torch
 
     import msgl
@@ -668,7 +671,39 @@ def run_case(args):
         print(f"case {args.case}: {args.steps} launches ok, {ms * 1e3:.1f} us per launch, "
               f"{tf:.1f} TFLOP/s", flush=True)
         return 0
-    if args.case in ("attention", "attention_cascade"):
+    if args.case == "attention_ragged":
+        B, hq6, hkv6 = 64, CFG06B["num_q_heads"], CFG06B["num_kv_heads"]
+        ctx = np.random.default_rng(2).integers(512, 4097, B).astype(np.int32)
+        num_pages, ptr = scattered_pages(ctx, seed=3)
+        kp = ops.fill_normal_(torch.empty(num_pages * PAGE, hkv6 * 128, dtype=torch.bfloat16, device=dev), seed=4)
+        vp = ops.fill_normal_(torch.empty_like(kp), seed=4, stream_id=1)
+        q = ops.fill_normal_(torch.empty(B, hq6, 128, dtype=torch.bfloat16, device=dev), seed=5)
+        ptd = torch.from_numpy(ptr).to(dev)
+        seq = torch.from_numpy(ctx).to(dev)
+        ws = ops.attention_workspace(B, int(ctx.max()), hq6, hkv6, dev)
+        run = lambda: ops.paged_attention_decode(q, kp, vp, ptd, seq, int(ctx.max()), hq6, hkv6,
+                                                 workspace=ws)
+    elif args.case == "moe_gate_up":
+        T, E, K, Hm, Im = 256, 128, 8, 2048, 768
+        lib = msgl.lib()
+        s_ = torch.cuda.current_stream().cuda_stream
+        rng = np.random.default_rng(7)
+        ids = np.stack([rng.choice(E, K, replace=False) for _ in range(T)]).astype(np.int32)
+        idd = torch.from_numpy(ids).to(dev)
+        off = torch.empty(E + 1, dtype=torch.int32, device=dev)
+        tok = torch.empty(T * K, dtype=torch.int32, device=dev)
+        pos = torch.empty(T * K, dtype=torch.int32, device=dev)
+        msgl.check(lib.msgl_moe_permute(idd.data_ptr(), T, K, E, off.data_ptr(), tok.data_ptr(),
+                                        pos.data_ptr(), s_))
+        xs = ops.fill_normal_(torch.empty(T * K, Hm, dtype=torch.bfloat16, device=dev), seed=6)
+        w = ops.fill_normal_(torch.empty(E, 2 * Im, Hm, dtype=torch.bfloat16, device=dev), seed=7,
+                             std=0.02)
+        act = torch.empty(T * K, Im, dtype=torch.bfloat16, device=dev)
+        gws = torch.zeros(lib.msgl_grouped_gemm_workspace_size(T * K, E), dtype=torch.uint8, device=dev)
+        run = lambda: msgl.check(lib.msgl_grouped_gemm_gate_up_silu(
+            xs.data_ptr(), w.data_ptr(), act.data_ptr(), off.data_ptr(), E, Im, Hm, T * K,
+            gws.data_ptr(), gws.numel(), torch.cuda.current_stream().cuda_stream))
+    elif args.case in ("attention", "attention_cascade"):
         num_pages, pt = build_pages()
         kp = torch.empty(num_pages * PAGE, hkv * 128, dtype=torch.bfloat16, device=dev)
         vp = torch.empty_like(kp)
@@ -1531,7 +1566,8 @@ def main():
                     help="qwen3-8b-decode: the headline (default); the others: the remaining "
                          "benchmark configurations")
     ap.add_argument("--case", choices=["attention", "attention_cascade", "gemm", "gemm_qkv",
-                                       "gemm_partials", "gemm_prefill", "breakdown", "extend"],
+                                       "gemm_partials", "gemm_prefill", "breakdown", "extend",
+                                       "attention_ragged", "moe_gate_up"],
                     default=None,
                     help="run one kernel of the step on a small single-layer case (profiling)")
     args = ap.parse_args()
