@@ -51,3 +51,20 @@ def test_workspace_sizes():
     assert L.msgl_gemm_workspace_size(2048, 151936, 4096) == 0
     # 128 requests x 8 kv heads x 2048 tokens: split-KV workspace present
     assert L.msgl_paged_attention_workspace_size(128, 2048, 32, 8, 128) > 0
+
+
+def test_partials_split_plan_host():
+    """Split-K partials plan (host only, 148 SMs without a device): one 128-token tile up to 128
+    tokens, two tiles up to 256 (the split count then fills the GPU with both tiles), none above;
+    the workspace of msgl_gemm_bf16 covers its 129..256-token partials."""
+    L = msgl.lib()
+    # Qwen3-30B-A3B qkv 5120 x 2048: 20 tiles of 256 rows -> 7 splits at one token tile, 3 at two
+    assert L.msgl_gemm_partials_splits(128, 5120, 2048) == 7
+    assert L.msgl_gemm_partials_splits(256, 5120, 2048) == 3
+    assert L.msgl_gemm_partials_splits(200, 5120, 2048) == 3
+    assert L.msgl_gemm_partials_splits(257, 5120, 2048) == 0
+    # router 128 x 2048: one tile, split count capped by K / (4 x 64)
+    assert L.msgl_gemm_partials_splits(256, 128, 2048) == 8
+    for M, N, K in [(256, 5120, 2048), (200, 2048, 4096), (256, 128, 2048)]:
+        S = L.msgl_gemm_partials_splits(M, N, K)
+        assert L.msgl_gemm_workspace_size(M, N, K) >= S * M * N * 4
