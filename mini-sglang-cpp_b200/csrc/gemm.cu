@@ -1318,6 +1318,7 @@ bool small_k_rows() {
     return !(e && e[0] == '0');
 }
 
+
 bool rows_disabled() {
     static const bool off = [] {
         const char* e = std::getenv("MSGL_GEMM_ROWS");
@@ -1756,9 +1757,12 @@ int run_gemm(const void* x, const void* w, void* y, unsigned long long* amax, in
     // Small gate_up + SwiGLU (a wide tensor-parallel rank's shard, e.g. 3072 x 4096): the
     // cluster schedule reduces in shared memory and needs no second kernel; measured at M 128,
     // 3072 x 4096: 14.0 us cluster vs 19.8 us partials + reduce (at 6144 x 4096 partials win,
-    // 20.8 vs 23.5 us).
+    // 20.8 vs 23.5 us). With a short K and at least 32 tokens narrow row tiles beat both
+    // (Qwen3-0.6B's 6144 x 1024: 8.2 vs 9.4 us at 64 tokens, 8.3 vs 11.3 at 128; at 4 tokens
+    // the cluster / partials path stays faster, 7.0 vs 8.2).
     const bool small_swiglu = EPI == EPI_SWIGLU && M <= 128 && force == 0 &&
-                              static_cast<int64_t>(N) * K <= (int64_t(16) << 20);
+                              static_cast<int64_t>(N) * K <= (int64_t(16) << 20) &&
+                              !(K <= kRowsShortK && M >= 32 && small_k_rows());
     if (M <= 128 && !rows_disabled() && force <= 2 && !small_swiglu) {
         // decode-sized: many weight rows -> whole row tiles per CTA (no K split); otherwise
         // split-K partials summed by a second small kernel (not for argmax, which needs whole

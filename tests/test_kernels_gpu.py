@@ -410,7 +410,9 @@ def test_gemm_matches_oracle_linear(cuda, oracle):
 # 128 tokens
 @pytest.mark.parametrize("M,I,K", [(4, 3072, 1024), (128, 1536, 4096), (37, 96, 256), (300, 768, 512),
                                    (128, 12288, 1024), (5, 12288, 256), (96, 6144, 512),
-                                   (256, 768, 2048)])
+                                   (256, 768, 2048),
+                                   # short K at 64 / 128 tokens: narrow row tiles (Qwen3-0.6B)
+                                   (64, 3072, 1024), (128, 3072, 1024)])
 def test_gate_up_silu(cuda, oracle, M, I, K):
     from msgl import ops
     rng = np.random.default_rng(M + I)
