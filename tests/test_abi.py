@@ -40,6 +40,14 @@ def test_host_side_validation():
                                          1.0, None, None, 0, None) == 1
     # GEMM: K not a multiple of 8
     assert L.msgl_gemm_bf16(None, None, None, 4, 128, 100, 1, None, 0, None) == 2
+    # MoE: router partials count outside [1, 64]; combine with top_k above 32
+    assert L.msgl_moe_route_topk_partials(None, 0, 4, 128, 8, 1, None, None, None) == 1
+    assert L.msgl_moe_route_topk_partials(None, 65, 4, 128, 8, 1, None, None, None) == 1
+    assert L.msgl_moe_combine(None, None, None, 4, 33, 2048, None, None) == 2
+    # split-K partials: more than 256 tokens (rejected before any pointer is used)
+    fake = 256  # an address that is never dereferenced
+    assert L.msgl_gemm_bf16_partials(fake, fake, fake, 300, 128, 256, 1, None) == 2
+    assert L.msgl_gemm_bf16_partials(None, None, None, 16, 128, 256, 1, None) == 1
     # zero-size work is a no-op
     assert L.msgl_launch_rmsnorm(None, None, None, 0, 64, 1e-6, 1, None) == 0
 
