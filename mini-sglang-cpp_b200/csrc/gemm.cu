@@ -1114,6 +1114,7 @@ gemm_rows_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
     const int KB = (K + kBK - 1) / kBK;
     const int G = gridDim.x;
     const int my_tiles = static_cast<int>(blockIdx.x) < T ? (T - blockIdx.x + G - 1) / G : 0;
+    const int m0 = blockIdx.y * kBM;  // token tile (129..256 tokens: two, each with its own CTAs)
     // token box of xbox rows (M rounded up to 8): the tile's other rows are never stored
     const uint32_t stage_tx = static_cast<uint32_t>(xbox + BR) * kBK * 2;
 
@@ -1163,7 +1164,7 @@ gemm_rows_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
                         mbar_arrive_expect_tx(&full[s], stage_tx);
                         tma_load_2d_hint(sW + s * kRowsTileW, &tmap_w, &full[s], kb * kBK, wrow, pol_w);
                     }
-                    tma_load_2d_hint(sX + s * kRowsTileX, &tmap_x, &full[s], kb * kBK, 0, pol_x);
+                    tma_load_2d_hint(sX + s * kRowsTileX, &tmap_x, &full[s], kb * kBK, m0, pol_x);
                 }
             }
         } else {
@@ -1204,8 +1205,8 @@ gemm_rows_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
         pdl_trigger();
         const int warp_q = warp & 3;
         const int eg = (warp - 2) >> 2;
-        const int m = warp_q * 32 + lane;
-        const bool live = warp_q * 32 < M;  // warp-uniform
+        const int m = m0 + warp_q * 32 + lane;
+        const bool live = m0 + warp_q * 32 < M;  // warp-uniform
         const int nch = BR / 16;
         unsigned long long best = 0ull;
         for (int it = 0; it < my_tiles; ++it) {
@@ -1683,8 +1684,10 @@ int launch_rows(const void* x, const void* w, void* y, unsigned long long* amax,
     if (rc) return rc;
     cudaFuncSetAttribute(gemm_rows_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(kRowsSmem));
-    launch_pdl(gemm_rows_kernel<EPI>, dim3(std::min(tiles, sms)), dim3(kSkThreads), kRowsSmem,
-               stream, tw, tx, y, amax, M, N, K, BR, token_box(M), id_off, err);
+    // grid.y = token tiles of 128 (two at 129..256 tokens; `sms` is then the CTAs per tile)
+    launch_pdl(gemm_rows_kernel<EPI>, dim3(std::min(tiles, sms), (M + kBM - 1) / kBM),
+               dim3(kSkThreads), kRowsSmem, stream, tw, tx, y, amax, M, N, K, BR, token_box(M),
+               id_off, err);
     MSGL_LAUNCH_CHECK();
     return MSGL_OK;
 }
@@ -1735,6 +1738,13 @@ int run_gemm(const void* x, const void* w, void* y, unsigned long long* amax, in
         if (EPI != EPI_ARGMAX) {
             const int r = launch_part_reduce<EPI>(x, w, y, M, N, K, ws, ws_bytes, stream);
             if (r != -1) return r;
+        } else {
+            // argmax needs whole rows: row tiles for both token tiles in one launch, half of
+            // the SMs on each, so the two CTAs of a weight tile read it at about the same time
+            const int half = std::max(1, num_sms() / 2);
+            int tiles = 0;
+            const int hs = plan_rows(N, half, tiles);
+            if (hs > 0) return launch_rows<EPI>(x, w, y, amax, M, N, K, hs, tiles, half, stream, id_off);
         }
     }
     if (M > 128 && M <= 256 && decode_schedule() == 0 && !rows_disabled() &&
