@@ -6,12 +6,13 @@
 // allocates TMEM and issues tcgen05.mma from one thread (fp32 accumulator in TMEM), and
 // epilogue warps that read the accumulator with tcgen05.ld. Schedules, chosen per call
 // (run_gemm):
-//   gemm_rows_kernel   M <= 128, many weight rows: whole tiles of 16 hs weight rows per CTA over
-//                      the full K; tokens are the UMMA M dimension, the tile's rows N
-//   gemm_part_kernel   M <= 128: split-K fp32 partials (tokens as M, 256 weight rows as N), summed
-//                      by the next kernel or by partials_reduce_kernel
+//   gemm_rows_kernel   M <= 128, many weight rows (or a short K): whole tiles of 16 hs weight
+//                      rows per CTA over the full K; tokens are the UMMA M dimension, the tile's
+//                      rows N; at 129..256 tokens (argmax) one token tile per grid row
+//   gemm_part_kernel   M <= 256: split-K fp32 partials (tokens as M in tiles of 128, 256 weight
+//                      rows as N), summed by the next kernel or by partials_reduce_kernel
 //   gemm_cl_kernel     M <= 128 otherwise: cluster split-K, partials exchanged over DSMEM
-//   (129..256 tokens: the partials + reduce over both token tiles; else two passes of the
+//   (129..256 tokens: the partials + reduce; argmax on the row kernel; else two passes of the
 //   schedules above, 128 tokens and the rest)
 //   gemm_sk_kernel     stream-K (prefill-sized M; 128 weight rows as M, up to 256 tokens as N)
 //   gemm_kernel        one CTA per tile (very large grids) and the grouped MoE GEMM
