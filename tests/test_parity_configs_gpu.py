@@ -240,3 +240,96 @@ def test_qwen3_8b_decode_step_cascade_partials(cuda, oracle):
           f"logits rel_l2 {err:.2e}, ids equal {int((out == ref.argmax(axis=1)).sum())}/{B8} "
           f"(margin-clear {int(clear.sum())})")
     assert ops.device_error() == (0, 0)
+
+
+# ------------------------------------------------------------------ Qwen3-30B-A3B decode, batch 256
+C5 = dict(num_layers=1, hidden=2048, num_q_heads=32, num_kv_heads=4, head_dim=128, inter=0,
+          vocab=151936, eps=1e-6, rope_base=1e6, max_position=1040, page_size=16,
+          num_experts=128, top_k=8, moe_inter=768, norm_topk=True)
+B5, CTX5 = 256, 1024
+
+
+def moe_weight_shapes(cfg):
+    H, D, hq, hkv, V = (cfg[k] for k in ("hidden", "head_dim", "num_q_heads", "num_kv_heads", "vocab"))
+    E, Im = cfg["num_experts"], cfg["moe_inter"]
+    names = [("embed", (V, H))]
+    for l in range(cfg["num_layers"]):
+        p = f"layers.{l}."
+        names += [(p + "input_ln", (H,)), (p + "qkv", ((hq + 2 * hkv) * D, H)),
+                  (p + "q_norm", (D,)), (p + "k_norm", (D,)), (p + "o", (H, hq * D)),
+                  (p + "post_ln", (H,)), (p + "router", (E, H))]
+        for e in range(E):
+            names += [(p + f"experts.{e}.gate_up", (2 * Im, H)), (p + f"experts.{e}.down", (H, Im))]
+    return names + [("norm", (H,)), ("lm_head", (V, H))]
+
+
+def test_qwen3_30b_a3b_decode_step_b256(cuda, oracle):
+    """One Qwen3-30B-A3B layer (128 experts, top-8, expert intermediate 768) in the benchmark's
+    decode step: 256 requests at context 1024, so the projections and the router run as split-K
+    partials over two 128-token tiles and the experts as grouped GEMMs. Routing is discrete: a
+    token whose 8th / 9th router logits are closer than the bf16 error may pick another expert
+    than the oracle, which changes that token's output. Checked over the tokens whose gap
+    between the 8th and 9th router logit (the oracle's) is clear of that error: the final logits
+    within the bf16 tolerance, together and token by token."""
+    from msgl import ops
+    from msgl.model import PagePool, Qwen3Model, device_view, make_step
+    model = Qwen3Model(C5, max_tokens=B5, max_reqs=B5)
+    w = {}
+    for i, (name, shape) in enumerate(moe_weight_shapes(C5)):
+        if len(shape) == 1:
+            bits = np.full(shape, ONE_BF16, np.uint16)
+        else:
+            t = torch.empty(shape, dtype=torch.bfloat16, device="cuda")
+            ops.fill_normal_(t, seed=0, stream_id=i, std=0.02)
+            bits = t.view(torch.int16).cpu().numpy().view(np.uint16)
+            del t
+        model.set_weight_bits(name, bits)
+        w[name] = bits if name == "embed" else from_bf16_bits(bits).reshape(shape)
+    n_own = CTX5 // 16
+    num_pages = B5 * n_own + 16
+    model.alloc_kv(num_pages)
+    pool = PagePool(num_pages)
+    np.random.default_rng(3).shuffle(pool.free)
+    pt = np.array([[pool.allocate() for _ in range(n_own)] for _ in range(B5)], np.int32)
+    rng = np.random.default_rng(2)
+    ids = rng.integers(0, C5["vocab"], B5).astype(np.int32)
+    pos = np.full(B5, CTX5 - 1, np.int32)
+    host = dict(input_ids=ids, positions=pos,
+                slot_mapping=(pt[:, (CTX5 - 1) // 16] * 16 + (CTX5 - 1) % 16).astype(np.int32),
+                page_table=pt, seq_lens=np.full(B5, CTX5, np.int32),
+                q_indptr=np.arange(B5 + 1, dtype=np.int32), last_idx=np.arange(B5, dtype=np.int32))
+    sb = make_step(host, True, "cuda", CTX5, 1)
+    width = C5["num_kv_heads"] * 128
+    w["embed"] = from_bf16_bits(w["embed"].reshape(C5["vocab"], -1)[ids]).reshape(B5, -1)
+    orc = OracleModel(oracle, C5, w, num_slots=num_pages * 16)
+    for l in range(C5["num_layers"]):
+        kp, vp, n = model.kv_pool(l)
+        for j, (ptr, dst) in enumerate(((kp, orc.k_pools[l]), (vp, orc.v_pools[l]))):
+            t = device_view(ptr, (n, width), torch.bfloat16)
+            ops.fill_normal_(t, seed=4, stream_id=2 * l + j, std=1.0)
+            dst[:] = t.float().cpu().numpy()
+    ref, state = orc.forward(np.arange(B5, dtype=np.int32), pos, host["slot_mapping"], pt,
+                             host["seq_lens"], host["q_indptr"], return_state=True)
+    nxt, lg = model.forward(sb, logits=True)
+    torch.cuda.synchronize()
+    got = lg.cpu().numpy()
+    # the oracle's router input (the residual after attention, RMS-normed; gains are 1) and the
+    # gap between each token's 8th and 9th router logits
+    _, r0 = state[0]
+    xin = r0 / np.sqrt((r0.astype(np.float64) ** 2).mean(axis=1, keepdims=True) + C5["eps"])
+    rl = xin @ w["layers.0.router"].astype(np.float64).T
+    srt = -np.sort(-rl, axis=1)
+    k = C5["top_k"]
+    clear = (srt[:, k - 1] - srt[:, k]) > 1e-2  # ~5x the logit error of a bf16 router input
+    per_tok = np.linalg.norm(got - ref, axis=1) / np.linalg.norm(ref, axis=1)
+    err_clear = rel_l2(got[clear], ref[clear])
+    print(f"\n30B-A3B decode step (1 layer, 256 requests): logits rel_l2 {rel_l2(got, ref):.2e} "
+          f"(all), {err_clear:.2e} over the {int(clear.sum())} tokens with a clear routing "
+          f"margin; per-token median {np.median(per_tok):.2e}, max {per_tok[clear].max():.2e} "
+          f"(clear), {per_tok[~clear].max() if (~clear).any() else 0:.2e} (near ties)")
+    assert clear.mean() > 0.8
+    assert err_clear < 2e-2, err_clear
+    assert (per_tok[clear] < 2e-2).all(), per_tok[clear].max()
+    out = nxt.cpu().numpy()
+    assert np.array_equal(out, got.argmax(axis=1))
+    assert ops.device_error() == (0, 0)
