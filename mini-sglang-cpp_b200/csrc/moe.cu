@@ -2,9 +2,10 @@
 //
 //  * msgl_moe_route_topk   MoERouter::route top-k and weights (src/layer/layer.cpp:283-305)
 //                          on fp32 router logits (the logits GEMM is msgl_gemm_bf16 with an
-//                          fp32 output, or its split-K partials summed here in part order): descending logit, equal logits -> larger expert id
-//                          first (std::greater on pair<float,int>), w = exp(l), divided by the
-//                          top-k sum when norm_topk.
+//                          fp32 output, or its split-K partials, summed here in part order):
+//                          descending logit, equal logits -> larger expert id first
+//                          (std::greater on pair<float,int>), w = exp(l), divided by the top-k
+//                          sum when norm_topk.
 //  * msgl_moe_permute      counting sort of the (token, k) pairs by expert, stable in pair
 //                          order: expert row offsets, the token of each sorted row, and the
 //                          sorted position of each pair (deterministic, no atomics on output).

@@ -219,11 +219,16 @@ static void create(Model& m, const msgl_model_config& c) {
     // split-K partials (steps of <= 256 tokens; MSGL_SPLITK_PARTIALS=0 turns the path off)
     const char* env_parts = std::getenv("MSGL_SPLITK_PARTIALS");
     if (!(env_parts && env_parts[0] == '0')) {
+        // the split count depends on the number of 128-token tiles: the largest buffer is at
+        // 128 tokens or at the largest step size up to 256
         auto need = [&](const Linear& l) {
             size_t n = 0;
-            for (int tm : {static_cast<int>(std::min<size_t>(T, 128)), static_cast<int>(std::min<size_t>(T, 256))})
+            for (size_t cap : {size_t(128), size_t(256)}) {
+                const int tm = static_cast<int>(std::min<size_t>(T, cap));
                 if (l.partials_fit(tm))
-                    n = std::max(n, static_cast<size_t>(l.partial_splits(tm)) * tm * l.out_features() * sizeof(float));
+                    n = std::max(n, static_cast<size_t>(l.partial_splits(tm)) * tm *
+                                        l.out_features() * sizeof(float));
+            }
             return n;
         };
         size_t pb = need(L0.qkv_proj);
@@ -238,7 +243,8 @@ static void create(Model& m, const msgl_model_config& c) {
         // router logits, or their split-K partials for steps of <= 256 tokens
         size_t lf = T * E;
         for (int t = 1; t <= static_cast<int>(std::min<size_t>(T, 256)); ++t)
-            lf = std::max(lf, static_cast<size_t>(std::max(0, m.layers[0].moe.router_splits(t))) * t * E);
+            lf = std::max(lf, static_cast<size_t>(std::max(0, m.layers[0].moe.router_splits(t))) *
+                                  t * E);
         m.moe_logits.alloc(lf * 4);
         m.moe_ids.alloc(T * k * 4);
         m.moe_w.alloc(T * k * 4);
@@ -446,8 +452,7 @@ static void forward(Model& m, const msgl_batch& b, int* next_tokens, float* logi
     bf16_t* part_d = m.tp ? m.tp_part[1] : x;
     // Steps of <= 256 tokens: qkv, o_proj and (dense, tensor parallel size 1) down_proj write
     // fp32 split-K partials that the next kernel adds, instead of reducing the K split across
-    // CTAs inside the GEMM. `pend` = splits of down_proj partials
-    // the next norm has to add.
+    // CTAs inside the GEMM. `pend` = splits of down_proj partials the next norm has to add.
     float* parts = m.parts.as<float>();
     auto use_parts = [&](const Linear& l) { return parts != nullptr && l.partials_fit(T); };
     int pend = 0;
