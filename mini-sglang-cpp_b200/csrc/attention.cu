@@ -936,7 +936,9 @@ __device__ __forceinline__ void cascade_merge(int b, int hg, int nsfx, int hq, i
     const int64_t cbase = static_cast<int64_t>(b) * cp.max_chunks;
     const int csfx = cp.chunks_sfx;
     merge_partials(nsfx + cp.n_pchunks, nq, hg * nq, hq,
-                   [cbase, nsfx, csfx](int k) { return cbase + (k < nsfx ? k : csfx + (k - nsfx)); },
+                   [cbase, nsfx, csfx](int k) {
+                       return cbase + (k < nsfx ? k : csfx + (k - nsfx));
+                   },
                    ws_o, ws_ml, out + static_cast<int64_t>(b) * hq * kHd);
 }
 

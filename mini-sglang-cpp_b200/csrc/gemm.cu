@@ -906,9 +906,9 @@ gemm_cl_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
 // [s KB / S, (s + 1) KB / S) of weight rows [256 tile, 256 tile + 256) for tokens
 // [128 y, 128 y + 128) in TMEM (lane = token, column = weight row) and stores the fp32 partial
 // into parts[s][M][N]; the two token tiles of a 256-token step read each weight tile at about the
-// same time, the second mostly from L2. No CTA waits for another; the next kernel on the stream (fused
-// add + RMSNorm, QK-norm + RoPE) adds the S partials in split order (deterministic). Producer
-// warp, MMA warp, 8 epilogue warps as in the stream-K kernel.
+// same time, the second mostly from L2. No CTA waits for another; the next kernel on the stream
+// (fused add + RMSNorm, QK-norm + RoPE) adds the S partials in split order (deterministic).
+// Producer warp, MMA warp, 8 epilogue warps as in the stream-K kernel.
 constexpr int kPartBN = 256;                        // weight rows per tile (UMMA N)
 constexpr int kPartTileX = kBM * kBK * 2;           // 16 KB token tile (UMMA A, M = 128)
 constexpr int kPartTileW = kPartBN * kBK * 2;       // 32 KB weight tile (UMMA B)
@@ -944,7 +944,8 @@ gemm_part_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
     // its own map, xbox2 rows): the tile's other rows are stale shared memory, whose MMA rows
     // are never stored
     const CUtensorMap* tmx = blockIdx.y ? &tmap_x2 : &tmap_x;
-    const uint32_t stage_tx = kPartTileW + static_cast<uint32_t>(blockIdx.y ? xbox2 : xbox) * kBK * 2;
+    const uint32_t stage_tx =
+        kPartTileW + static_cast<uint32_t>(blockIdx.y ? xbox2 : xbox) * kBK * 2;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < ST; ++s) {
@@ -1745,7 +1746,8 @@ int run_gemm(const void* x, const void* w, void* y, unsigned long long* amax, in
             const int half = std::max(1, num_sms() / 2);
             int tiles = 0;
             const int hs = plan_rows(N, half, tiles);
-            if (hs > 0) return launch_rows<EPI>(x, w, y, amax, M, N, K, hs, tiles, half, stream, id_off);
+            if (hs > 0)
+                return launch_rows<EPI>(x, w, y, amax, M, N, K, hs, tiles, half, stream, id_off);
         }
     }
     if (M > 128 && M <= 256 && decode_schedule() == 0 && !rows_disabled() &&
@@ -1759,8 +1761,10 @@ int run_gemm(const void* x, const void* w, void* y, unsigned long long* amax, in
         const auto* x2 = static_cast<const __nv_bfloat16*>(x) + static_cast<int64_t>(128) * K;
         void* y2 = y;
         if (EPI == EPI_F32) y2 = static_cast<float*>(y) + static_cast<int64_t>(128) * N;
-        else if (EPI == EPI_SWIGLU) y2 = static_cast<__nv_bfloat16*>(y) + static_cast<int64_t>(128) * (N / 2);
-        else if (EPI == EPI_BF16) y2 = static_cast<__nv_bfloat16*>(y) + static_cast<int64_t>(128) * N;
+        else if (EPI == EPI_SWIGLU)
+            y2 = static_cast<__nv_bfloat16*>(y) + static_cast<int64_t>(128) * (N / 2);
+        else if (EPI == EPI_BF16)
+            y2 = static_cast<__nv_bfloat16*>(y) + static_cast<int64_t>(128) * N;
         return run_gemm<EPI>(x2, w, y2, amax ? amax + 128 : nullptr, M - 128, N, K, ws, ws_bytes,
                              stream, id_off);
     }
