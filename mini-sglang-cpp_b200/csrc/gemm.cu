@@ -1578,16 +1578,20 @@ int launch_bn(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& tx, v
     return MSGL_OK;
 }
 
-// Grouped GEMM schedule: the persistent kernel with dynamic work for prefill-sized tiles (bn >=
-// 128 rows per tile), one CTA per tile for decode-sized ones. Measured on B200, Qwen3-30B-A3B
-// experts (128 x 1536 x 2048 gate_up, 128 x 2048 x 768 down), persistent vs per-tile: 4096
-// tokens x top-8 (bn 256) gate_up 408 vs 480 us, down 200 vs 309; 256 tokens x top-8 (bn 16)
-// gate_up 151 vs 130, down 83 vs 76. MSGL_GROUPED_PERSISTENT=0 / 1 forces either (read on every
-// call).
-bool grouped_persistent(int bn) {
+// Grouped GEMM schedule: the persistent kernel with dynamic work for prefill-sized tiles, one
+// CTA per tile for decode-sized ones. Measured on B200, Qwen3-30B-A3B experts (128 x 1536 x 2048
+// gate_up + SwiGLU, 128 x 2048 x 768 down), persistent vs per-tile, in us:
+//   tokens x top-8  rows/tile  gate_up       down
+//   4096            256        408 vs 480    200 vs 309
+//   2048            128        249 vs 233    130 vs 138
+//   1024 / 512      64 / 32    176 vs 156    99 vs 100  (and 166 vs 138, 92 vs 86)
+//   256             16         151 vs 130    83 vs 76
+// so: 256-row tiles, and the plain (non-SwiGLU) epilogue from 128-row tiles.
+// MSGL_GROUPED_PERSISTENT=0 / 1 forces either (read on every call).
+bool grouped_persistent(int bn, bool swiglu) {
     const char* e = std::getenv("MSGL_GROUPED_PERSISTENT");
     if (e && (e[0] == '0' || e[0] == '1')) return e[0] == '1';
-    return bn >= 128;
+    return bn >= 256 || (bn >= 128 && !swiglu);
 }
 
 template <int BN, int EPI>
@@ -2102,7 +2106,7 @@ int run_grouped(const void* x, const void* w, void* y, const int* offsets, int E
     p.splits = 1;
     p.kb_per_split = (K + kBK - 1) / kBK;
     GroupArgs g{tiles, num_tiles, offsets};
-    if (grouped_persistent(bn)) {
+    if (grouped_persistent(bn, EPI == EPI_SWIGLU)) {
         const int64_t max_items = static_cast<int64_t>(max_tiles) * p.n_tiles;
         switch (bn) {
             case 16: return launch_grouped_dyn<16, EPI>(tw, tx, y, N, K, g, num_tiles + 1, max_items, stream);

@@ -128,7 +128,7 @@ def test_permute(cuda, T, E, k):
     assert np.array_equal(host(pos), inv)
 
 
-# the last two cases have tiles of 128 / 256 rows: the persistent grouped kernel (dynamic work)
+# the last two cases have tiles of 128 / 256 rows (the persistent grouped kernel's sizes)
 @pytest.mark.parametrize("T,E,k,H,I", [(16, 8, 2, 256, 96), (256, 128, 8, 2048, 768), (2048, 32, 4, 512, 256),
                                        (2048, 64, 8, 512, 256)])
 def test_expert_block(cuda, oracle, monkeypatch, T, E, k, H, I):
@@ -164,14 +164,14 @@ def test_expert_block(cuda, oracle, monkeypatch, T, E, k, H, I):
                                   T, k, H, out.data_ptr(), s))
     assert rel_l2(host(out), ref) < 1e-2, rel_l2(host(out), ref)
     assert ops.device_error() == (0, 0)
-    # the other grouped schedule (persistent <-> one CTA per tile) gives the same bits: the same
-    # k order in both
-    bn_persistent = L.msgl_grouped_gemm_workspace_size(R, E) > 0 and (R + E - 1) // E > 64
-    monkeypatch.setenv("MSGL_GROUPED_PERSISTENT", "0" if bn_persistent else "1")
-    act2, ys2 = torch.empty_like(act), torch.empty_like(ys)
-    msgl.check(L.msgl_grouped_gemm_gate_up_silu(xs.data_ptr(), gu_packed.data_ptr(), act2.data_ptr(),
-                                                off.data_ptr(), E, I, H, R, ws.data_ptr(), ws.numel(), s))
-    msgl.check(L.msgl_grouped_gemm_bf16(act2.data_ptr(), dn_d.data_ptr(), ys2.data_ptr(), off.data_ptr(),
-                                        E, H, I, R, ws.data_ptr(), ws.numel(), s))
-    assert torch.equal(act, act2) and torch.equal(ys, ys2)
+    # both grouped schedules forced (persistent, one CTA per tile) give the default's bits: the
+    # same k order in all of them
+    for force in ("0", "1"):
+        monkeypatch.setenv("MSGL_GROUPED_PERSISTENT", force)
+        act2, ys2 = torch.empty_like(act), torch.empty_like(ys)
+        msgl.check(L.msgl_grouped_gemm_gate_up_silu(xs.data_ptr(), gu_packed.data_ptr(), act2.data_ptr(),
+                                                    off.data_ptr(), E, I, H, R, ws.data_ptr(), ws.numel(), s))
+        msgl.check(L.msgl_grouped_gemm_bf16(act2.data_ptr(), dn_d.data_ptr(), ys2.data_ptr(),
+                                            off.data_ptr(), E, H, I, R, ws.data_ptr(), ws.numel(), s))
+        assert torch.equal(act, act2) and torch.equal(ys, ys2), force
     assert ops.device_error() == (0, 0)
