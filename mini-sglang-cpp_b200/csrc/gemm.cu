@@ -52,7 +52,7 @@ template <int BN>
 struct GemmCfg {
     static constexpr int kTileB = BN * kBK * 2;
     static constexpr int kStageBytes = kTileA + kTileB;
-    static constexpr int kStages = BN >= 256 ? 4 : (96 * 1024) / kStageBytes;
+    static constexpr int kStages = BN >= 256 ? 4 : (BN == 16 ? 3 : (96 * 1024) / kStageBytes);
     static constexpr int kTmemCols = BN < 32 ? 32 : BN;
     static constexpr size_t kSmem = static_cast<size_t>(kStages) * kStageBytes + 1024 + 256;
 };
