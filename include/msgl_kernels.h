@@ -320,12 +320,31 @@ MSGL_API int msgl_grouped_gemm_gate_up_silu(const void* x_sorted, const void* w_
                                             const int* expert_offsets, int num_experts, int inter,
                                             int K, int max_rows, void* workspace,
                                             size_t workspace_bytes, msgl_stream_t stream);
+/* msgl_grouped_gemm_bf16 over the tile list that the previous grouped call on this stream left in
+ * the same workspace for the same expert_offsets, num_experts and max_rows (the expert down
+ * projection after msgl_grouped_gemm_gate_up_silu): the per-call tile-list kernel is not launched
+ * again where the schedule needs nothing else from it. A workspace filled for other offsets or
+ * sizes gives wrong rows. */
+MSGL_API int msgl_grouped_gemm_bf16_reuse_tiles(const void* x_sorted, const void* w, void* y,
+                                                const int* expert_offsets, int num_experts, int N,
+                                                int K, int max_rows, void* workspace,
+                                                size_t workspace_bytes, msgl_stream_t stream);
 
 /* out[t] = sum_j topk_weights[t,j] * y_sorted[pair_pos[t*k+j]], j in order, fp32 accumulation
  * (qwen3_moe.cpp:102-106). out [T, hidden] bf16; hidden % 8 == 0, top_k <= 32. */
 MSGL_API int msgl_moe_combine(const void* y_sorted, const int* pair_pos, const float* topk_weights,
                               int num_tokens, int top_k, int hidden, void* out,
                               msgl_stream_t stream);
+
+/* msgl_moe_combine fused with the residual add and the RMSNorm that follow it (the next decoder
+ * layer's input_layernorm, src/layer/layer.cpp:79-112): m = combine row rounded to bf16,
+ * residual += m (fp32 [T, hidden]), x_out = rmsnorm(residual) * norm_weight (bf16). Equal bit for
+ * bit to msgl_moe_combine into x followed by msgl_add_rmsnorm(x, residual, ..., first = 0).
+ * hidden % 8 == 0, hidden <= 8192, top_k <= 32; 16-byte aligned rows. */
+MSGL_API int msgl_moe_combine_add_rmsnorm(const void* y_sorted, const int* pair_pos,
+                                          const float* topk_weights, int num_tokens, int top_k,
+                                          int hidden, float* residual, const void* norm_weight,
+                                          float eps, void* x_out, msgl_stream_t stream);
 
 /* Vocab-parallel lm_head: this rank's rows W [vocab_local, K] cover token ids
  * [vocab_offset, vocab_offset + vocab_local). packed[m] receives the rank's best

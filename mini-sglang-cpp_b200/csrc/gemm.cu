@@ -2076,9 +2076,13 @@ __global__ void group_tiles_kernel(const int* __restrict__ offsets, int E, int b
     for (int i = 0; i < cnt; ++i) tiles[pre[e] + i] = make_int2(e, beg + i * bn);
 }
 
+// reuse_tiles: the workspace already holds the tile list of an earlier grouped call with the same
+// offsets, max_rows and E (so the same bn); the tile kernel is skipped unless the persistent
+// schedule runs, which needs the work counter that kernel zeroes.
 template <int EPI>
 int run_grouped(const void* x, const void* w, void* y, const int* offsets, int E, int N, int K,
-                int max_rows, void* ws, size_t ws_bytes, cudaStream_t stream) {
+                int max_rows, void* ws, size_t ws_bytes, cudaStream_t stream,
+                bool reuse_tiles = false) {
     if (E <= 0 || E > 1024 || N <= 0 || K <= 0 || max_rows < 0)
         return set_error(MSGL_ERR_INVALID_ARG, "grouped gemm: bad sizes");
     if (K % 8) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "grouped gemm: K % 8");
@@ -2091,8 +2095,11 @@ int run_grouped(const void* x, const void* w, void* y, const int* offsets, int E
     if (max_tiles > 65535 * 8) return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "grouped gemm: too many tiles");
     int* num_tiles = static_cast<int*>(ws);
     int2* tiles = reinterpret_cast<int2*>(static_cast<uint8_t*>(ws) + 256);
-    launch_pdl(group_tiles_kernel, dim3(1), dim3(E), 0, stream, offsets, E, bn, tiles, num_tiles);
-    MSGL_LAUNCH_CHECK();
+    const bool persistent = grouped_persistent(bn, EPI == EPI_SWIGLU);
+    if (!reuse_tiles || persistent) {
+        launch_pdl(group_tiles_kernel, dim3(1), dim3(E), 0, stream, offsets, E, bn, tiles, num_tiles);
+        MSGL_LAUNCH_CHECK();
+    }
     CUtensorMap tw, tx;
     int rc = make_tmap_2d_bf16(&tw, w, K, static_cast<uint64_t>(E) * N, static_cast<uint64_t>(K) * 2,
                                kBK, kBM, true);
@@ -2106,7 +2113,7 @@ int run_grouped(const void* x, const void* w, void* y, const int* offsets, int E
     p.splits = 1;
     p.kb_per_split = (K + kBK - 1) / kBK;
     GroupArgs g{tiles, num_tiles, offsets};
-    if (grouped_persistent(bn, EPI == EPI_SWIGLU)) {
+    if (persistent) {
         const int64_t max_items = static_cast<int64_t>(max_tiles) * p.n_tiles;
         switch (bn) {
             case 16: return launch_grouped_dyn<16, EPI>(tw, tx, y, N, K, g, num_tiles + 1, max_items, stream);
@@ -2252,6 +2259,14 @@ int msgl_grouped_gemm_bf16(const void* x_sorted, const void* w, void* y,
                            void* workspace, size_t workspace_bytes, msgl_stream_t stream) {
     return run_grouped<EPI_BF16>(x_sorted, w, y, expert_offsets, num_experts, N, K, max_rows,
                                  workspace, workspace_bytes, stream);
+}
+
+int msgl_grouped_gemm_bf16_reuse_tiles(const void* x_sorted, const void* w, void* y,
+                                       const int* expert_offsets, int num_experts, int N, int K,
+                                       int max_rows, void* workspace, size_t workspace_bytes,
+                                       msgl_stream_t stream) {
+    return run_grouped<EPI_BF16>(x_sorted, w, y, expert_offsets, num_experts, N, K, max_rows,
+                                 workspace, workspace_bytes, stream, true);
 }
 
 int msgl_grouped_gemm_gate_up_silu(const void* x_sorted, const void* w_packed, void* y,

@@ -11,6 +11,10 @@
 //                          sorted position of each pair (deterministic, no atomics on output).
 //  * msgl_moe_combine      out[t] = sum_k w[t,k] * y_sorted[pos(t,k)], k in order, fp32
 //                          accumulation (the expert loop of src/model/qwen3_moe.cpp:74-108).
+//  * msgl_moe_combine_add_rmsnorm  the combine, then the decoder layer's residual add and the
+//                          next RMSNorm of the same row in the same CTA (qwen3.cpp:19 on the
+//                          MoE output, layer.cpp:79-112): equal bit for bit to msgl_moe_combine
+//                          followed by msgl_add_rmsnorm.
 #include "common.cuh"
 
 namespace msgl {
@@ -208,6 +212,90 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ y, const int* _
     }
 }
 
+// combine_kernel fused with the residual add and the RMSNorm that follow it: one 128-thread CTA
+// per token row, thread t owning the row vectors t + 128 i (i < VPT), as the add + RMSNorm kernel
+// does. Per vector: m = bf16(sum_k w_k y[pos_k]) (rounded as combine_kernel stores it),
+// r += m, and r's squares go into the row sum in the same order; the block reduction and the
+// scaling x = bf16(r * inv_rms * g) are that kernel's too, so the output equals the two kernels
+// run back to back.
+constexpr int kCombNormThreads = 128;
+
+template <int VPT>
+__global__ void __launch_bounds__(kCombNormThreads)
+combine_add_rmsnorm_kernel(const __nv_bfloat16* __restrict__ y, const int* __restrict__ pair_pos,
+                           const float* __restrict__ w, int top_k, int hidden,
+                           float* __restrict__ resid, const __nv_bfloat16* __restrict__ g,
+                           float eps, __nv_bfloat16* __restrict__ x_out) {
+    __shared__ int s_pos[32];
+    __shared__ float s_w[32];
+    __shared__ float red[kCombNormThreads / 32];
+    pdl_wait();
+    pdl_trigger();
+    const int t = blockIdx.x;
+    if (threadIdx.x < top_k) {
+        s_pos[threadIdx.x] = pair_pos[static_cast<int64_t>(t) * top_k + threadIdx.x];
+        s_w[threadIdx.x] = w[static_cast<int64_t>(t) * top_k + threadIdx.x];
+    }
+    __syncthreads();
+    const int nvec = hidden >> 3;
+    float* rrow = resid + static_cast<int64_t>(t) * hidden;
+    float v[VPT][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const int vi = threadIdx.x + i * kCombNormThreads;
+        if (vi < nvec) {
+            float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll 8
+            for (int k = 0; k < top_k; ++k) {
+                const int pos = s_pos[k];
+                if (pos < 0) continue;
+                const float wk = s_w[k];
+                uint4 u = *reinterpret_cast<const uint4*>(y + static_cast<int64_t>(pos) * hidden + vi * 8);
+                acc[0] += wk * bf16lo(u.x); acc[1] += wk * bf16hi(u.x);
+                acc[2] += wk * bf16lo(u.y); acc[3] += wk * bf16hi(u.y);
+                acc[4] += wk * bf16lo(u.z); acc[5] += wk * bf16hi(u.z);
+                acc[6] += wk * bf16lo(u.w); acc[7] += wk * bf16hi(u.w);
+            }
+            const float4 r0 = reinterpret_cast<const float4*>(rrow + vi * 8)[0];
+            const float4 r1 = reinterpret_cast<const float4*>(rrow + vi * 8)[1];
+            const float r[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+#pragma unroll
+            for (int j = 0; j < 8; j += 2) {
+                const uint32_t m = pack_bf16x2(acc[j], acc[j + 1]);
+                v[i][j] = bf16lo(m) + r[j];
+                v[i][j + 1] = bf16hi(m) + r[j + 1];
+            }
+            reinterpret_cast<float4*>(rrow + vi * 8)[0] = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
+            reinterpret_cast<float4*>(rrow + vi * 8)[1] = make_float4(v[i][4], v[i][5], v[i][6], v[i][7]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+        }
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    ss = red[0] + red[1] + red[2] + red[3];
+    const float inv_rms = 1.0f / sqrtf(ss / static_cast<float>(hidden) + eps);
+    __nv_bfloat16* dst = x_out + static_cast<int64_t>(t) * hidden;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const int vi = threadIdx.x + i * kCombNormThreads;
+        if (vi < nvec) {
+            const uint4 gu = *reinterpret_cast<const uint4*>(g + vi * 8);
+            const float gv[8] = {bf16lo(gu.x), bf16hi(gu.x), bf16lo(gu.y), bf16hi(gu.y),
+                                 bf16lo(gu.z), bf16hi(gu.z), bf16lo(gu.w), bf16hi(gu.w)};
+            float o[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o[j] = v[i][j] * inv_rms * gv[j];
+            uint4 u;
+            u.x = pack_bf16x2(o[0], o[1]); u.y = pack_bf16x2(o[2], o[3]);
+            u.z = pack_bf16x2(o[4], o[5]); u.w = pack_bf16x2(o[6], o[7]);
+            *reinterpret_cast<uint4*>(dst + vi * 8) = u;
+        }
+    }
+}
+
 }  // namespace
 }  // namespace msgl
 
@@ -260,6 +348,40 @@ int msgl_moe_combine(const void* y_sorted, const int* pair_pos, const float* top
     launch_pdl(combine_kernel, dim3(num_tokens), dim3(128), 0, stream,
                static_cast<const __nv_bfloat16*>(y_sorted), pair_pos, topk_weights, top_k, hidden,
                static_cast<__nv_bfloat16*>(out));
+    MSGL_LAUNCH_CHECK();
+    return MSGL_OK;
+}
+
+int msgl_moe_combine_add_rmsnorm(const void* y_sorted, const int* pair_pos,
+                                 const float* topk_weights, int num_tokens, int top_k, int hidden,
+                                 float* residual, const void* norm_weight, float eps, void* x_out,
+                                 msgl_stream_t stream) {
+    if (!y_sorted || !pair_pos || !topk_weights || !residual || !norm_weight || !x_out)
+        return set_error(MSGL_ERR_INVALID_ARG, "moe_combine_add_rmsnorm: null");
+    if (num_tokens < 0 || top_k <= 0 || top_k > 32 || hidden <= 0 || hidden % 8 ||
+        hidden > 8 * 8 * kCombNormThreads)
+        return set_error(MSGL_ERR_UNSUPPORTED_SHAPE,
+                         "moe_combine_add_rmsnorm: hidden % 8, hidden <= 8192, top_k <= 32");
+    if ((reinterpret_cast<uintptr_t>(y_sorted) | reinterpret_cast<uintptr_t>(residual) |
+         reinterpret_cast<uintptr_t>(norm_weight) | reinterpret_cast<uintptr_t>(x_out)) & 15)
+        return set_error(MSGL_ERR_INVALID_ARG, "moe_combine_add_rmsnorm: pointers must be 16-byte aligned");
+    if (num_tokens == 0) return MSGL_OK;
+    const int vpt = (hidden / 8 + kCombNormThreads - 1) / kCombNormThreads;
+    const auto* y = static_cast<const __nv_bfloat16*>(y_sorted);
+    const auto* g = static_cast<const __nv_bfloat16*>(norm_weight);
+    auto* xo = static_cast<__nv_bfloat16*>(x_out);
+    const dim3 grid(num_tokens), block(kCombNormThreads);
+#define MSGL_COMB_CASE(N)                                                                      \
+    case N:                                                                                    \
+        launch_pdl(combine_add_rmsnorm_kernel<N>, grid, block, 0, stream, y, pair_pos,          \
+                   topk_weights, top_k, hidden, residual, g, eps, xo);                          \
+        break;
+    switch (vpt) {
+        MSGL_COMB_CASE(1) MSGL_COMB_CASE(2) MSGL_COMB_CASE(3) MSGL_COMB_CASE(4)
+        MSGL_COMB_CASE(5) MSGL_COMB_CASE(6) MSGL_COMB_CASE(7) MSGL_COMB_CASE(8)
+        default: return set_error(MSGL_ERR_UNSUPPORTED_SHAPE, "moe_combine_add_rmsnorm: hidden");
+    }
+#undef MSGL_COMB_CASE
     MSGL_LAUNCH_CHECK();
     return MSGL_OK;
 }

@@ -269,9 +269,12 @@ class MoEExperts {
     MoEExperts() = default;
     MoEExperts(int hidden, int num_experts, int top_k, int inter, bool norm_topk)
         : hidden_(hidden), E_(num_experts), k_(top_k), inter_(inter), norm_topk_(norm_topk) {}
-    // x [T, H] (post-attention normed) -> out [T, H] (may alias x: x is consumed first)
+    // x [T, H] (post-attention normed) -> out [T, H] (may alias x: x is consumed first).
+    // With next_norm: residual += the expert output and out = next_norm(residual), the residual
+    // add and RMSNorm that follow the layer (qwen3.cpp:19), in the combine kernel.
     void forward(const bf16_t* x, bf16_t* out, int T, const MoEScratch& ms, const Scratch& ws,
-                 cudaStream_t s) const {
+                 cudaStream_t s, const RMSNorm* next_norm = nullptr,
+                 float* residual = nullptr) const {
         // router logits (layer.cpp:273-280): as split-K partials summed by the top-k kernel when
         // the step has <= 256 tokens and the scratch holds them, else one fp32 GEMM
         const int S = router_splits(T);
@@ -295,10 +298,17 @@ class MoEExperts {
         ck(msgl_grouped_gemm_gate_up_silu(ms.xs, gate_up_packed.p, ms.act, ms.offsets, E_, inter_,
                                           hidden_, T * k_, ms.grouped_ws, ms.grouped_ws_bytes, s),
            "experts gate_up");
-        ck(msgl_grouped_gemm_bf16(ms.act, down.p, ms.ys, ms.offsets, E_, hidden_, inter_, T * k_,
-                                  ms.grouped_ws, ms.grouped_ws_bytes, s),
+        // (same offsets, rows and experts as gate_up: its tile list is still in the workspace)
+        ck(msgl_grouped_gemm_bf16_reuse_tiles(ms.act, down.p, ms.ys, ms.offsets, E_, hidden_,
+                                              inter_, T * k_, ms.grouped_ws, ms.grouped_ws_bytes,
+                                              s),
            "experts down");
-        ck(msgl_moe_combine(ms.ys, ms.pair_pos, ms.topk_w, T, k_, hidden_, out, s), "moe combine");
+        if (next_norm)
+            ck(msgl_moe_combine_add_rmsnorm(ms.ys, ms.pair_pos, ms.topk_w, T, k_, hidden_, residual,
+                                            next_norm->weight.p, next_norm->eps(), out, s),
+               "moe combine + add + RMSNorm");
+        else
+            ck(msgl_moe_combine(ms.ys, ms.pair_pos, ms.topk_w, T, k_, hidden_, out, s), "moe combine");
     }
     DevBuf router;          // bf16 [E, H]
     DevBuf gate_up_packed;  // bf16 [E, 2 inter, H], each expert packed by msgl_pack_gate_up

@@ -456,15 +456,17 @@ static void forward(Model& m, const msgl_batch& b, int* next_tokens, float* logi
     float* parts = m.parts.as<float>();
     auto use_parts = [&](const Linear& l) { return parts != nullptr && l.partials_fit(T); };
     int pend = 0;
+    bool normed = false;  // the previous layer's MoE combine already ran this layer's input norm
     for (int l = 0; l < nl; ++l) {
         auto& L = m.layers[l];
-        if (l > 0 && !m.tp) {  // qwen3.cpp:19
+        if (l > 0 && !m.tp && !normed) {  // qwen3.cpp:19
             if (pend)
                 L.input_layernorm.forward_fused_add_partials(parts, pend, x, res, T, s);
             else
                 L.input_layernorm.forward_fused_add(x, res, T, false, s);
             pend = 0;
         }
+        normed = false;
         if (use_parts(L.qkv_proj)) {  // :22, :28-48
             const int S = L.qkv_proj.forward_partials(x, parts, T, s);
             L.attn.prepare_partials(parts, S, m.q.as<bf16_t>(), L.k_pool.p, L.v_pool.p,
@@ -488,8 +490,14 @@ static void forward(Model& m, const msgl_batch& b, int* next_tokens, float* logi
             L.o_proj.forward(m.attn_out.as<bf16_t>(), part_o, T, m.scratch, s);
             L.post_attention_layernorm.forward_fused_add(x, res, T, false, s);  // :57
         }
-        if (c.num_experts > 0) {
-            L.moe.forward(x, part_d, T, m.moe_scratch, m.scratch, s);         // qwen3_moe.cpp:62-111
+        if (c.num_experts > 0) {  // qwen3_moe.cpp:62-111
+            if (!m.tp && l + 1 < nl) {  // + the residual add and the next layer's input norm
+                L.moe.forward(x, x, T, m.moe_scratch, m.scratch, s, &m.layers[l + 1].input_layernorm,
+                              res);
+                normed = true;
+            } else {
+                L.moe.forward(x, part_d, T, m.moe_scratch, m.scratch, s);
+            }
         } else {
             L.gate_up_proj.forward(x, m.act.as<bf16_t>(), T, m.scratch, s);  // :60-79
             // (the last layer's down_proj writes x, the hidden state msgl_model_hidden reads)

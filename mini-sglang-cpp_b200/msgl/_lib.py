@@ -50,8 +50,10 @@ SIGNATURES = {
     "msgl_moe_permute": (I, [P, I, I, I, P, P, P, P]),
     "msgl_grouped_gemm_workspace_size": (SZ, [I, I]),
     "msgl_grouped_gemm_bf16": (I, [P, P, P, P, I, I, I, I, P, SZ, P]),
+    "msgl_grouped_gemm_bf16_reuse_tiles": (I, [P, P, P, P, I, I, I, I, P, SZ, P]),
     "msgl_grouped_gemm_gate_up_silu": (I, [P, P, P, P, I, I, I, I, P, SZ, P]),
     "msgl_moe_combine": (I, [P, P, P, I, I, I, P, P]),
+    "msgl_moe_combine_add_rmsnorm": (I, [P, P, P, I, I, I, P, P, F, P, P]),
     "msgl_lm_head_argmax_partial": (I, [P, P, I, I, I, I, P, P, SZ, P]),
     "msgl_tp_unique_id_size": (SZ, []),
     "msgl_tp_get_unique_id": (I, [P]),

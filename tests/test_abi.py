@@ -48,8 +48,15 @@ def test_host_side_validation():
     fake = 256  # an address that is never dereferenced
     assert L.msgl_gemm_bf16_partials(fake, fake, fake, 300, 128, 256, 1, None) == 2
     assert L.msgl_gemm_bf16_partials(None, None, None, 16, 128, 256, 1, None) == 1
+    # combine + add + RMSNorm: null pointers, top_k above 32, hidden above 8192, rows not
+    # 16-byte aligned (all rejected before any pointer is used)
+    assert L.msgl_moe_combine_add_rmsnorm(None, None, None, 4, 8, 2048, None, None, 1e-6, None, None) == 1
+    assert L.msgl_moe_combine_add_rmsnorm(fake, fake, fake, 4, 33, 2048, fake, fake, 1e-6, fake, None) == 2
+    assert L.msgl_moe_combine_add_rmsnorm(fake, fake, fake, 4, 8, 8200, fake, fake, 1e-6, fake, None) == 2
+    assert L.msgl_moe_combine_add_rmsnorm(fake, fake, fake, 4, 8, 2048, fake, fake, 1e-6, fake + 8, None) == 1
     # zero-size work is a no-op
     assert L.msgl_launch_rmsnorm(None, None, None, 0, 64, 1e-6, 1, None) == 0
+    assert L.msgl_moe_combine_add_rmsnorm(fake, fake, fake, 0, 8, 2048, fake, fake, 1e-6, fake, None) == 0
 
 
 def test_workspace_sizes():

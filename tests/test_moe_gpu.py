@@ -175,3 +175,65 @@ def test_expert_block(cuda, oracle, monkeypatch, T, E, k, H, I):
                                             off.data_ptr(), E, H, I, R, ws.data_ptr(), ws.numel(), s))
         assert torch.equal(act, act2) and torch.equal(ys, ys2), force
     assert ops.device_error() == (0, 0)
+    # the down projection over the tile list that gate_up left in the workspace (the engine's
+    # sequence): the same bits under the default schedule and both forced ones
+    for force in (None, "0", "1"):
+        if force is None:
+            monkeypatch.delenv("MSGL_GROUPED_PERSISTENT", raising=False)
+        else:
+            monkeypatch.setenv("MSGL_GROUPED_PERSISTENT", force)
+        ws.zero_()
+        act2, ys2 = torch.empty_like(act), torch.empty_like(ys)
+        msgl.check(L.msgl_grouped_gemm_gate_up_silu(xs.data_ptr(), gu_packed.data_ptr(), act2.data_ptr(),
+                                                    off.data_ptr(), E, I, H, R, ws.data_ptr(), ws.numel(), s))
+        msgl.check(L.msgl_grouped_gemm_bf16_reuse_tiles(act2.data_ptr(), dn_d.data_ptr(), ys2.data_ptr(),
+                                                        off.data_ptr(), E, H, I, R, ws.data_ptr(),
+                                                        ws.numel(), s))
+        assert torch.equal(act, act2) and torch.equal(ys, ys2), force
+    assert ops.device_error() == (0, 0)
+
+
+@pytest.mark.parametrize("T,k,H", [(1, 8, 2048), (256, 8, 2048), (37, 4, 1032), (64, 2, 4096), (3, 32, 8192)])
+def test_combine_add_rmsnorm(cuda, T, k, H):
+    """The combine fused with the residual add and the next RMSNorm equals msgl_moe_combine
+    followed by msgl_add_rmsnorm bit for bit (dropped pairs, pos = -1, included), and both match
+    an fp32 torch restatement."""
+    import msgl
+    from msgl import ops
+    rng = np.random.default_rng(T * 31 + H)
+    R = T * k
+    ys = dev(rn(rng, R, H))
+    pos = rng.permutation(R).astype(np.int32)
+    pos[rng.random(R) < 0.05] = -1
+    wts = rng.random((T, k)).astype(np.float32)
+    resid0 = rn(rng, T, H).astype(np.float32)
+    g = dev(1.0 + 0.1 * rn(rng, H))
+    eps = 1e-6
+    s = torch.cuda.current_stream().cuda_stream
+    L = msgl.lib()
+    pos_d, w_d = dev(pos, torch.int32), dev(wts, torch.float32)
+
+    x1 = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    r1 = dev(resid0, torch.float32)
+    msgl.check(L.msgl_moe_combine(ys.data_ptr(), pos_d.data_ptr(), w_d.data_ptr(), T, k, H, x1.data_ptr(), s))
+    msgl.check(L.msgl_add_rmsnorm(x1.data_ptr(), r1.data_ptr(), g.data_ptr(), T, H, eps, 0, s))
+
+    x2 = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    r2 = dev(resid0, torch.float32)
+    msgl.check(L.msgl_moe_combine_add_rmsnorm(ys.data_ptr(), pos_d.data_ptr(), w_d.data_ptr(), T, k, H,
+                                              r2.data_ptr(), g.data_ptr(), eps, x2.data_ptr(), s))
+    torch.cuda.synchronize()
+    assert torch.equal(r1, r2) and torch.equal(x1, x2)
+    assert ops.device_error() == (0, 0)
+
+    # fp32 restatement: m = bf16(sum_j w y[pos]); r += m; x = r * rsqrt(mean(r^2) + eps) * g
+    yf = ys.float()
+    pt = torch.from_numpy(pos).long().cuda().view(T, k)
+    gathered = yf[pt.clamp(min=0)] * (pt >= 0).unsqueeze(-1)
+    m = (gathered * w_d.view(T, k, 1)).sum(1).bfloat16().float()
+    r = torch.from_numpy(resid0).cuda() + m
+    xr = r * torch.rsqrt(r.pow(2).mean(-1, keepdim=True) + eps) * g.float()
+    # (torch sums the k products in another order, so its bf16 rounding of m may land one bf16
+    # ulp, 2^-8 relative, away from the kernel's)
+    assert bool(((r2 - r).abs() <= m.abs() * 2.0 ** -7 + 1e-5).all())
+    assert rel_l2(host(x2), xr.cpu().numpy()) < 1e-2
