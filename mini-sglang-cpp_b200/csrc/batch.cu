@@ -23,34 +23,6 @@ namespace {
 
 constexpr int kAdvThreads = 1024;
 
-__device__ __forceinline__ int block_excl_scan(int v, int* sh, int& total) {
-    // inclusive warp scan, then the warp totals
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    int x = v;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, x, o);
-        if (lane >= o) x += y;
-    }
-    if (lane == 31) sh[w] = x;
-    __syncthreads();
-    if (w == 0) {
-        const int nw = (blockDim.x + 31) >> 5;
-        int t = lane < nw ? sh[lane] : 0;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, t, o);
-            if (lane >= o) t += y;
-        }
-        if (lane < nw) sh[lane] = t;  // inclusive prefix of the warp totals
-    }
-    __syncthreads();
-    const int before = (w > 0 ? sh[w - 1] : 0) + x - v;
-    total = sh[((blockDim.x + 31) >> 5) - 1];
-    __syncthreads();  // sh is reused by the next block of requests
-    return before;
-}
-
 // finished (optional, [B]): requests with a nonzero entry are held where they are -- no page,
 // no new position, same input id -- so the next step recomputes their last step (writing the
 // same K/V to the same slot) and their output is ignored.

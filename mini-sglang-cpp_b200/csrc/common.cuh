@@ -60,6 +60,37 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
+// Exclusive scan of one int per thread over the whole block (blockDim.x a multiple of 32, every
+// thread calls it): returns the sum of v over the threads before this one and sets `total` to
+// the block's sum. Inclusive warp scans by shuffles, then a scan of the warp totals by warp 0.
+// sh: 32 ints of shared memory, free again when it returns.
+__device__ __forceinline__ int block_excl_scan(int v, int* sh, int& total) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int nw = (blockDim.x + 31) >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) sh[w] = x;
+    __syncthreads();
+    if (w == 0) {
+        int t = lane < nw ? sh[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, t, o);
+            if (lane >= o) t += y;
+        }
+        if (lane < nw) sh[lane] = t;  // inclusive prefix of the warp totals
+    }
+    __syncthreads();
+    const int before = (w > 0 ? sh[w - 1] : 0) + x - v;
+    total = sh[nw - 1];
+    __syncthreads();
+    return before;
+}
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));

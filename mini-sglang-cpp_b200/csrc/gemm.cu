@@ -2055,7 +2055,9 @@ int run_gemm(const void* x, const void* w, void* y, unsigned long long* amax, in
 // One thread per expert: the expert's row tiles of height bn, as (expert, first row) pairs.
 __global__ void group_tiles_kernel(const int* __restrict__ offsets, int E, int bn,
                                    int2* __restrict__ tiles, int* __restrict__ num_tiles) {
-    __shared__ int pre[1025];
+    // one thread per expert (the block is E rounded up to whole warps): its tile count, the
+    // block's exclusive scan of the counts, then its tiles at that position
+    __shared__ int sh[32];
     pdl_wait();
     pdl_trigger();
     const int e = threadIdx.x;
@@ -2064,16 +2066,13 @@ __global__ void group_tiles_kernel(const int* __restrict__ offsets, int E, int b
         beg = offsets[e];
         cnt = (offsets[e + 1] - beg + bn - 1) / bn;
     }
-    pre[e + 1] = cnt;
-    if (e == 0) pre[0] = 0;
-    __syncthreads();
+    int total;
+    const int first = block_excl_scan(cnt, sh, total);
     if (e == 0) {
-        for (int i = 1; i <= static_cast<int>(blockDim.x); ++i) pre[i] += pre[i - 1];
-        num_tiles[0] = pre[blockDim.x];
+        num_tiles[0] = total;
         num_tiles[1] = 0;  // the persistent grouped kernel's work counter
     }
-    __syncthreads();
-    for (int i = 0; i < cnt; ++i) tiles[pre[e] + i] = make_int2(e, beg + i * bn);
+    for (int i = 0; i < cnt; ++i) tiles[first + i] = make_int2(e, beg + i * bn);
 }
 
 // reuse_tiles: the workspace already holds the tile list of an earlier grouped call with the same
@@ -2097,7 +2096,8 @@ int run_grouped(const void* x, const void* w, void* y, const int* offsets, int E
     int2* tiles = reinterpret_cast<int2*>(static_cast<uint8_t*>(ws) + 256);
     const bool persistent = grouped_persistent(bn, EPI == EPI_SWIGLU);
     if (!reuse_tiles || persistent) {
-        launch_pdl(group_tiles_kernel, dim3(1), dim3(E), 0, stream, offsets, E, bn, tiles, num_tiles);
+        launch_pdl(group_tiles_kernel, dim3(1), dim3((E + 31) & ~31), 0, stream, offsets, E, bn, tiles,
+                   num_tiles);
         MSGL_LAUNCH_CHECK();
     }
     CUtensorMap tw, tx;

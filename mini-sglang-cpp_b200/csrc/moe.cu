@@ -106,7 +106,7 @@ __global__ void route_topk_kernel(const float* __restrict__ logits, int nparts, 
     }
 }
 
-// Single CTA, 1024 threads: histogram, scan, then stable placement chunk by chunk
+// Single CTA, 1024 threads: histogram, block scan, then stable placement chunk by chunk
 // (per-warp expert counts in shared memory, prefix over warps, rank inside the warp by
 // __match_any_sync).
 constexpr int kPermThreads = 1024;
@@ -117,6 +117,7 @@ permute_kernel(const int* __restrict__ ids, int num_pairs, int top_k, int E,
                int* __restrict__ offsets, int* __restrict__ sorted_token,
                int* __restrict__ pair_pos, int* err) {
     extern __shared__ int sm[];
+    __shared__ int scan_sh[32];
     pdl_wait();
     pdl_trigger();
     int* base = sm;                       // [E] running start of each expert
@@ -133,15 +134,15 @@ permute_kernel(const int* __restrict__ ids, int num_pairs, int top_k, int E,
         atomicAdd(&base[e], 1);
     }
     __syncthreads();
-    if (tid == 0) {  // exclusive scan -> offsets
-        int run = 0;
-        for (int e = 0; e < E; ++e) {
-            int c = base[e];
-            offsets[e] = run;
-            base[e] = run;
-            run += c;
+    {  // exclusive scan of the expert counts -> offsets (E <= 256 < kPermThreads)
+        const int c = tid < E ? base[tid] : 0;
+        int total;
+        const int before = block_excl_scan(c, scan_sh, total);
+        if (tid < E) {
+            offsets[tid] = before;
+            base[tid] = before;
         }
-        offsets[E] = run;
+        if (tid == 0) offsets[E] = total;
     }
     __syncthreads();
     for (int c0 = 0; c0 < num_pairs; c0 += kPermThreads) {

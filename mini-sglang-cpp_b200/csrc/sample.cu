@@ -35,33 +35,6 @@ __device__ __forceinline__ float uniform24(uint64_t seed, uint64_t step, uint64_
     return static_cast<float>(z >> 40) * (1.0f / 16777216.0f);
 }
 
-// exclusive block scan of one int per thread (1024 threads)
-__device__ __forceinline__ int block_scan_excl(int v, int* sh, int& total) {
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    int x = v;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, x, o);
-        if (lane >= o) x += y;
-    }
-    if (lane == 31) sh[w] = x;
-    __syncthreads();
-    if (w == 0) {
-        int t = sh[lane];
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, t, o);
-            if (lane >= o) t += y;
-        }
-        sh[lane] = t;
-    }
-    __syncthreads();
-    const int r = (w > 0 ? sh[w - 1] : 0) + x - v;
-    total = sh[31];
-    __syncthreads();
-    return r;
-}
-
 __global__ void __launch_bounds__(kSampThreads)
 sample_kernel(const float* __restrict__ logits, int V, const float* __restrict__ temperature,
               const int* __restrict__ top_k, const float* __restrict__ top_p, uint64_t seed,
@@ -144,8 +117,8 @@ sample_kernel(const float* __restrict__ logits, int V, const float* __restrict__
         eq += key == t;
     }
     int gt_total, eq_total;
-    int gt_off = block_scan_excl(gt, sh, gt_total);
-    int eq_off = block_scan_excl(eq, sh, eq_total);
+    int gt_off = block_excl_scan(gt, sh, gt_total);
+    int eq_off = block_excl_scan(eq, sh, eq_total);
     for (int i = beg; i < end; ++i) {
         const uint32_t key = ord_key(l[i]);
         const unsigned long long e =
